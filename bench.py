@@ -1,0 +1,360 @@
+"""
+Benchmark of the routed-expert MoE layer (router + forward + manual backward with LoRA) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = route T tokens (KimiK3MoERouter), run the routed-expert forward (gate/up with
+SiTU-GLU, down, weighted combine, LoRA fused) and the full backward (grad_h, grad_w and the
+six LoRA gradients) of one 896-expert MXFP4 layer, d=7168, f=2048, top-8 (BASELINE configs[1]
+at N=1: T=1024). Expert weights (~21 GB) are resident in HBM, far larger than the 126 MB L2,
+so every step streams them from DRAM. Inputs are seeded synthetic tensors with the
+distributions of BASELINE.json (the Kimi K3 checkpoint is not available).
+
+Under torchrun (N>1) each rank runs the same layer on its own 1024 tokens and its own copy
+of the experts (replicas; expert-parallel dispatch is a separate path), so per-GPU work is
+fixed: "scaling": "weak". Timing is device time (CUDA events on the launching stream),
+barrier + synchronize on both sides, max over ranks.
+
+--impl reference times the reference's own CPU implementation of the path on this box's
+host cores: the reference's C kernel (lazy_lora/native/mxfp4_gemm.c, compiled from source into
+oracle/_ref) driven by the restated expert loop of oracle/moe_oracle.py, on a bounded sample
+of the same layer (a subset of experts with all their routed tokens), scaled to the full layer.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "MoE-layer fwd+bwd tokens/s (d=7168, f=2048, E=896, top-8, LoRA r=16)"
+UNIT = "tokens/s"
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            p = json.load(fh)
+        return float(p["hbm_gbs"]), float(p.get("bf16_tflops", 1639.8)), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(args):
+    if args.gpus > 1 or int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        import datetime
+        import torch.distributed as dist
+        rank = int(os.environ.get("RANK", "0"))
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+        return rank, local, world, dist
+    if torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return 0, 0, 1, None
+
+
+def expert_bytes(cfg):
+    return 3 * cfg.f * cfg.d // 2 + 3 * cfg.f * cfg.d // 32
+
+
+# --------------------------------------------------------------------- reference arm
+def cpu_reference_sample(cfg, inp_dev, idx, w, n_experts: int, kind: str = "ref"):
+    """Time the reference CPU path (fwd + bwd sweep) over a subset of experts; returns
+    (seconds for the sample, fraction of the layer's expert work it covers, threads)."""
+    from oracle import moe_oracle as O
+    nthreads = os.cpu_count() or 1
+    torch.set_num_threads(nthreads)
+    os.environ.setdefault("OMP_NUM_THREADS", str(nthreads))
+    kern = O.MXFP4Checker(kind)
+    active = torch.unique(idx).tolist()
+    g = torch.Generator().manual_seed(123)
+    pick = sorted(active[i] for i in torch.randperm(len(active), generator=g)[:n_experts].tolist())
+    ev = torch.tensor(pick, device=idx.device)
+    cpu = {key: inp_dev[key][ev].cpu() for key in ("w1p", "w1s", "w3p", "w3s", "w2p", "w2s")}
+    cpu.update({key: inp_dev[key].float().cpu() for key in ("A_g", "B_g", "A_u", "B_u", "A_d", "B_d")})
+    remap = torch.full((cfg.E,), -1, dtype=torch.int64)
+    remap[torch.tensor(pick)] = torch.arange(len(pick))
+    idx_c = idx.cpu()
+    idx_r = torch.where(idx_c >= 0, remap[idx_c.clamp(min=0)], idx_c)
+    layer = O.Layer.from_inputs(cpu, cfg.scaling)
+    x = inp_dev["x"].float().cpu()
+    gr = inp_dev["g"].float().cpu()
+    wc = w.cpu()
+    experts = list(range(len(pick)))
+    t0 = time.perf_counter()
+    O.experts_forward(kern, layer, x, idx_r, wc, experts)
+    O.experts_backward(kern, layer, x, idx_r, wc, gr, experts)
+    dt = time.perf_counter() - t0
+    return dt, len(pick) / max(1, len(active)), kern.threads()
+
+
+def run_reference(args, cfg, rank, world, dist):
+    from lazylora_b200.synthetic import make_layer_device
+    if rank != 0:
+        return
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    if dev == "cpu":
+        print(json.dumps({"impl": "reference", "unavailable": "no CUDA device to generate the layer inputs on"}))
+        return
+    inp = make_layer_device(cfg, device=dev)
+    from oracle import moe_oracle as O
+    x = inp["x"].float()
+    # routing with the reference's router arithmetic on CPU (fp32 logits, torch.topk)
+    idx, w = O.route(x.cpu(), inp["router_w"].cpu(), inp["router_b"].cpu(), cfg.k)
+    kind = "ref" if os.path.exists(O.REF_SO) else "oracle"
+    n_exp = args.ref_experts
+    times = []
+    for i in range(args.warmup + args.steps):
+        dt, frac, threads = cpu_reference_sample(cfg, inp, idx.to(dev), w.to(dev), n_exp, kind)
+        if i >= args.warmup:
+            times.append(dt / frac)            # seconds for the whole layer
+    step_s = statistics.median(times)
+    value = cfg.T / step_s
+    sample = (f"fwd+bwd over {n_exp} of the layer's active experts with all their routed tokens "
+              f"(expert-sampled, scaled by active/{n_exp}); router on CPU not included")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "configs[1]: 896-expert MXFP4 MoE layer fwd+bwd", "d": cfg.d, "f": cfg.f,
+                       "E": cfg.E, "k": cfg.k, "T": cfg.T, "r": cfg.r},
+            "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads,
+                             "kind": "reference" if kind == "ref" else "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------- our arm
+def run_ours(args, cfg, rank, local, world, dist):
+    from lazylora_b200 import _lib as L
+    from lazylora_b200.core.moe_router import KimiK3MoERouter
+    from lazylora_b200.synthetic import make_layer_device
+    from lazylora_b200.trainer.routed_experts import RoutedExpertsLayer
+
+    dev = torch.device("cuda", local)
+    lib = L.load()
+    inp = make_layer_device(cfg, device=dev)
+    layer = RoutedExpertsLayer.from_inputs(inp, cfg.scaling, device=dev)
+    router = KimiK3MoERouter(hidden_size=cfg.d, num_experts=cfg.E, top_k=cfg.k, device=dev)
+    x = inp["x"].to(torch.bfloat16).contiguous()
+    g = inp["g"].to(torch.bfloat16).contiguous()
+    Wr, br = inp["router_w"], inp["router_b"]
+    del inp["w1p"], inp["w3p"], inp["w2p"]   # the layer holds the weights
+
+    launches = [0]
+
+    def step(xx, gg):
+        idx, w = router.forward(xx, weight=Wr, bias=br)
+        n = 2                                   # router: logits + select
+        out = layer.forward(xx, idx, w)
+        n += lib.ll_last_launch_count()
+        gh, gw, grads = layer.backward(xx, idx, w, gg)
+        n += lib.ll_last_launch_count()
+        launches[0] += n
+        return out, gh, gw, grads, idx, w
+
+    # ---- warm-up + correctness status
+    for _ in range(args.warmup):
+        res = step(x, g)
+    layer.check_status(cfg.T, cfg.k)
+    idx = res[4]
+    U = int(torch.unique(idx).numel())
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- timed region (device time), with per-GEMM events for the roofline
+    stream = torch.cuda.current_stream()
+    n_gemm_ev = 8
+    gemm_events = [[torch.cuda.Event(enable_timing=True) for _ in range(n_gemm_ev)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches[0] = 0
+    barrier()
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            ev = gemm_events[i]
+            arr = (L.c_void_p * n_gemm_ev)(*[e.cuda_event for e in ev])
+            lib.ll_profile_gemm_events(arr, n_gemm_ev)
+            step(x, g)
+        end.record(stream)
+        barrier()
+    lib.ll_profile_gemm_events(None, 0)
+    layer.check_status(cfg.T, cfg.k)
+    total_ms = start.elapsed_time(end)
+    gemm_ms = [[gemm_events[i][2 * j].elapsed_time(gemm_events[i][2 * j + 1]) for j in range(4)]
+               for i in range(args.steps)]
+    clocks = clk.summary()
+
+    # ---- end to end through the public API, host buffers, copies inside the timed region
+    x_h = x.cpu().pin_memory()
+    g_h = g.cpu().pin_memory()
+    out_h = torch.empty((cfg.T, cfg.d), dtype=torch.float32).pin_memory()
+    gh_h = torch.empty((cfg.T, cfg.d), dtype=torch.float32).pin_memory()
+    gw_h = torch.empty((cfg.T, cfg.k), dtype=torch.float32).pin_memory()
+    e_steps = max(1, min(args.steps, 10))
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e_steps):
+        xd = x_h.to(dev, non_blocking=True)
+        gd = g_h.to(dev, non_blocking=True)
+        out, gh, gw, grads, _, _ = step(xd, gd)
+        out_h.copy_(out, non_blocking=True)
+        gh_h.copy_(gh, non_blocking=True)
+        gw_h.copy_(gw, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e_steps
+    h2d = x_h.numel() * 2 + g_h.numel() * 2
+    d2h = (out_h.numel() + gh_h.numel() + gw_h.numel()) * 4
+
+    # ---- max over ranks
+    ms_step = total_ms / args.steps
+    vals = torch.tensor([ms_step, e2e_ms], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms_step, e2e_ms = float(vals[0]), float(vals[1])
+    if rank != 0:
+        return
+
+    hbm_peak, tf_peak, peak_kind = _peaks()
+    eb = expert_bytes(cfg)
+    names = ["F1 gate/up (W1,W3 . x)", "F2 down (W2 . h)", "B1 (g . W2)", "B2 dX (dg . W1 + du . W3)"]
+    per_kernel_bytes = [U * 2 * cfg.f * cfg.d * 17 // 32, U * cfg.f * cfg.d * 17 // 32,
+                        U * cfg.f * cfg.d * 17 // 32, U * 2 * cfg.f * cfg.d * 17 // 32]
+    avg_ms = [statistics.mean(s[j] for s in gemm_ms) for j in range(4)]
+    shares = [a / ms_step for a in avg_ms]
+    dom = max(range(4), key=lambda j: avg_ms[j])
+    achieved = per_kernel_bytes[dom] / (avg_ms[dom] * 1e-3) / 1e9
+    weight_tbs = 2 * U * eb / (ms_step * 1e-3) / 1e12
+    value = world * cfg.T / (ms_step * 1e-3)
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 operands / fp32 accumulate (MXFP4 weights decoded exactly)",
+        "data": "synthetic",
+        "config": {"workload": "configs[1]: 896-expert MXFP4 MoE layer, route + fwd + full LoRA bwd",
+                   "d": cfg.d, "f": cfg.f, "E": cfg.E, "k": cfg.k, "T_per_gpu": cfg.T, "r": cfg.r,
+                   "active_experts": U, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "weights 21 GB >> 126 MB L2: every step streams them from HBM"},
+        "weight_TBps": weight_tbs,
+        "hbm_roofline_ms": 2 * U * eb / (hbm_peak * 1e9) * 1e3,
+        "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "peak_kind": peak_kind,
+                     "traffic": None,
+                     "algorithmic_bytes_per_launch": per_kernel_bytes[dom], "avg_launch_ms": avg_ms[dom]},
+        "kernel_ms": {n: round(a, 4) for n, a in zip(names, avg_ms)},
+        "kernel_share": {n: round(s, 4) for n, s in zip(names, shares)},
+        "e2e": {"value": world * cfg.T / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches[0],
+        "clocks": clocks,
+    }
+    if args.cpu_baseline and world == 1:
+        weights = {"w1p": layer.w1p, "w3p": layer.w3p, "w2p": layer.w2p, "w1s": layer.w1s[..., :cfg.d // 32],
+                   "w3s": layer.w3s[..., :cfg.d // 32], "w2s": layer.w2s[..., :cfg.f // 32]}
+        dt, frac, threads = cpu_reference_sample(cfg, {**inp, **weights}, idx, res[5], args.ref_experts)
+        full = dt / frac
+        line["cpu_baseline"] = {"value": cfg.T / full, "unit": UNIT, "cores": threads, "kind": "reference",
+                                "sample": f"reference C kernel (oracle/_ref) + restated expert loop, fwd+bwd over "
+                                          f"{args.ref_experts} of {U} active experts, scaled to the layer"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c1")
+    ap.add_argument("--ref-experts", type=int, default=48)
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    from lazylora_b200.synthetic import CONFIGS
+    cfg = CONFIGS[args.config]
+    rank, local, world, dist = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, cfg, rank, world, dist)
+        else:
+            run_ours(args, cfg, rank, local, world, dist)
+    finally:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

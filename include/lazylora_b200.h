@@ -1,0 +1,161 @@
+/*
+ * lazylora_b200 — C ABI of the B200 (sm_100a) routed-expert MXFP4 path.
+ *
+ * Plain pointers, sizes and a cudaStream_t passed as void*; no torch types. Every buffer is
+ * device memory owned by the caller (the library never allocates or frees); scratch space
+ * is a caller-sized workspace whose size the *_workspace_bytes functions return.
+ * Every call returns an ll_status; kernels never trap: a bounded wait that runs out is
+ * reported as LL_ERR_TIMEOUT through the status word read back after the launch.
+ *
+ * Weight format (the reference's, lazy_lora/native/mxfp4_gemm.c:12-18): W is [R, K] with K a
+ * multiple of 32; packed [R, K/2] bytes, element 2j in the low nibble of byte j; scales
+ * [R, K/32] E8M0 bytes, 2^(b-127), bytes >= 253 contribute zero. Here the scale rows may be
+ * padded: `scale_stride` is the byte distance between scale rows and must be a multiple of
+ * 16 (it equals K/32 whenever K is a multiple of 512, e.g. 7168, 3584, 2048).
+ */
+#ifndef LAZYLORA_B200_H
+#define LAZYLORA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  LL_OK = 0,
+  LL_ERR_ARG = 1,        /* bad shape, stride, alignment or pointer */
+  LL_ERR_CUDA = 2,       /* a CUDA runtime call failed (launch, memcpy, attribute) */
+  LL_ERR_TIMEOUT = 3,    /* a device-side bounded wait ran out; the kernel wound down */
+  LL_ERR_WORKSPACE = 4,  /* workspace smaller than *_workspace_bytes asked for */
+  LL_ERR_RANGE = 5,      /* value outside what the kernel represents exactly */
+  LL_ERR_ARCH = 6        /* device is not sm_100 */
+} ll_status;
+
+/* Human-readable text for a status code (static storage). */
+const char* ll_status_string(int status);
+
+/* Last CUDA error text seen by the library on this thread ("" if none). */
+const char* ll_last_cuda_error(void);
+
+/* ------------------------------------------------------------------ drop-in kernels
+ * Device-pointer versions of the four symbols of lazy_lora/native/mxfp4_gemm.c, with the
+ * same argument meaning; `ws` is scratch of ll_mxfp4_workspace_bytes(M, K, R) bytes.
+ */
+
+/* Replaces mxfp4_threads (lazy_lora/native/mxfp4_gemm.c:131-138): the parallel width the
+ * kernels use (streaming multiprocessors of the current device). */
+int ll_mxfp4_threads(void);
+
+size_t ll_mxfp4_workspace_bytes(int M, int K, int R);
+
+/* Replaces mxfp4_gemm (lazy_lora/native/mxfp4_gemm.c:64-94): y[M,R] = x[M,K] . W^T. */
+int ll_mxfp4_gemm(float* y, const float* x, const uint8_t* packed, const uint8_t* scales,
+                  int M, int K, int R, int64_t scale_stride, void* ws, size_t ws_bytes,
+                  void* stream);
+
+/* Replaces mxfp4_gemm_t (lazy_lora/native/mxfp4_gemm.c:96-129): y[M,K] += dy[M,R] . W
+ * (accumulates into y, as the reference does). */
+int ll_mxfp4_gemm_t(float* y, const float* dy, const uint8_t* packed, const uint8_t* scales,
+                    int M, int K, int R, int64_t scale_stride, void* ws, size_t ws_bytes,
+                    void* stream);
+
+/* Replaces mxfp4_dequant (lazy_lora/native/mxfp4_gemm.c:142-150): out[R,K] = W, exact.
+ * out_dtype: 0 = fp32 (the reference's), 1 = bf16, 2 = fp16 (exact when the scale bytes
+ * lie in 104..140). Note the reference's (K, R) argument order. */
+int ll_mxfp4_dequant(void* out, const uint8_t* packed, const uint8_t* scales, int K, int R,
+                     int64_t scale_stride, int out_dtype, void* stream);
+
+/* ------------------------------------------------------------------------- router
+ * KimiK3MoERouter.forward (lazy_lora/core/moe_router.py:80-100): logits = x . Wr^T (fp32),
+ * scores = sigmoid(logits), selection on scores + bias (bias may be NULL), top-k in
+ * descending order (ties: lower expert id first), weights gathered from the unbiased
+ * scores, renormalised by (sum + 1e-20) when renormalize != 0 and k > 1, times scale.
+ * x_dtype: 0 = fp32, 1 = bf16. idx is int64 [T,k] like torch.topk's indices.
+ */
+size_t ll_route_workspace_bytes(int T, int E);
+int ll_route_topk(const void* x, int x_dtype, const float* router_w, const float* bias,
+                  int T, int d, int E, int k, int renormalize, float routed_scaling_factor,
+                  int64_t* idx, float* w, float* scores_out /* optional [T,E] */,
+                  void* ws, size_t ws_bytes, void* stream);
+
+/* The selection half alone (moe_router.py:92-99) from given fp32 scores / scores_for_choice:
+ * bit-exact indices and weights for identical inputs. */
+int ll_route_select(const float* scores, const float* scores_for_choice, int T, int E, int k,
+                    int renormalize, float routed_scaling_factor, int64_t* idx, float* w,
+                    void* stream);
+
+/* ------------------------------------------------------------ routed-expert layer
+ * One MoE layer's routed experts: the forward sum of LazyLoRATrainer._routed_experts_forward
+ * (lazy_lora/trainer/lazy_trainer.py:806-834) and the manual backward of
+ * _routed_experts_backward (lazy_trainer.py:836-880), with the layer's shared rank-r LoRA
+ * adapters (lazy_lora/core/lora_layer.py) on gate, up and down and the SiTU-GLU activation
+ * (lazy_lora/core/situ_activation.py).
+ */
+typedef struct {
+  int d;          /* expert input width (K of gate/up), multiple of 128 */
+  int f;          /* expert intermediate width, multiple of 128 */
+  int E;          /* experts resident in these arrays (local experts under expert parallelism) */
+  int r;          /* LoRA rank, 1..32 */
+  float lora_scaling;          /* alpha / r */
+  const uint8_t* w1p;  const uint8_t* w1s;   /* gate  [E,f,d/2], scales [E,f,*] */
+  const uint8_t* w3p;  const uint8_t* w3s;   /* up    [E,f,d/2], scales [E,f,*] */
+  const uint8_t* w2p;  const uint8_t* w2s;   /* down  [E,d,f/2], scales [E,d,*] */
+  int64_t s13_stride;          /* scale row stride of gate/up, bytes (>= d/32, %16 == 0) */
+  int64_t s2_stride;           /* scale row stride of down, bytes (>= f/32, %16 == 0) */
+  const int32_t* beta;         /* [E][2] power-of-two decode bias from ll_moe_prepare */
+  const float* A_g; const float* B_g;   /* gate LoRA A [r,d], B [f,r] */
+  const float* A_u; const float* B_u;   /* up   LoRA A [r,d], B [f,r] */
+  const float* A_d; const float* B_d;   /* down LoRA A [r,f], B [d,r] */
+} ll_moe_layer;
+
+/* Per-expert decode bias (beta[e][0] for gate+up, beta[e][1] for down) so that every scale
+ * byte within 36 of the matrix maximum decodes exactly to fp16. Run once per weight load. */
+int ll_moe_prepare(const ll_moe_layer* L, int32_t* beta_out, void* stream);
+
+/* Workspace for a forward + backward of T tokens with top-k routing. The forward leaves
+ * the activations the backward needs in it (the role of ctx.save_for_backward). */
+size_t ll_moe_workspace_bytes(const ll_moe_layer* L, int T, int k);
+
+/* out[T,d] fp32 = sum over the k selected experts of w * expert(x) (experts ascending).
+ * idx int64 [T,k] (values < E, distinct per row; -1 = slot not routed here), w fp32 [T,k].
+ * x_dtype: 0 = fp32, 1 = bf16. */
+int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dtype,
+                   const int64_t* idx, const float* w, float* out, void* ws, size_t ws_bytes,
+                   void* stream);
+
+/* Backward of the forward that last ran in `ws` for upstream gradient g [T,d] (g_dtype as
+ * x_dtype): grad_h [T,d], grad_w [T,k] (fp32, overwritten) and the LoRA gradients
+ * dA_g [r,d], dB_g [f,r], dA_u [r,d], dB_u [f,r], dA_d [r,f], dB_d [d,r] (fp32, overwritten;
+ * the caller adds them into .grad as accumulate_grad does). */
+int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dtype,
+                    const int64_t* idx, const float* w, const void* g, int g_dtype,
+                    float* grad_h, float* grad_w, float* dA_g, float* dB_g, float* dA_u,
+                    float* dB_u, float* dA_d, float* dB_d, void* ws, size_t ws_bytes,
+                    void* stream);
+
+/* Reads and clears the device status word the layer kernels write into `ws` (a bounded
+ * wait that ran out, see LL_ERR_TIMEOUT). Synchronises `stream`. */
+int ll_moe_status(const ll_moe_layer* L, int T, int k, void* ws, void* stream);
+
+/* The stable permutation the last ll_moe_forward built in `ws` (device buffers): offsets
+ * [E+1] of each expert's rows, then token and slot of each sorted row (expert ascending,
+ * tokens ascending within an expert: the row order of lazy_trainer.py:823-827). Rows past
+ * offsets[E] are -1. */
+int ll_moe_permutation(const ll_moe_layer* L, int T, int k, void* ws, int* offsets,
+                       int* perm_token, int* perm_slot, void* stream);
+
+/* Profiling hook: record events[2i] / events[2i+1] (cudaEvent_t handles) on the launching
+ * stream around the i-th grouped-GEMM launch that follows on this thread, for the first n/2
+ * launches; n = 0 turns it off. Calling it again restarts at i = 0. */
+int ll_profile_gemm_events(void* const* events, int n);
+
+/* Number of kernel launches the last ll_moe_forward / ll_moe_backward on this thread made. */
+int ll_last_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LAZYLORA_B200_H */

@@ -1,0 +1,264 @@
+// Shared device helpers for the sm_100a kernels: status reporting, mbarriers with bounded
+// waits, TMA tiled loads, tcgen05 (TMEM alloc, MMA, commit, loads), UMMA descriptors and the
+// exact MXFP4 (E2M1 codes + E8M0 block-32 scales) decode into fp16.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "lazylora_b200.h"
+
+#define LL_DEV __device__ __forceinline__
+
+namespace ll {
+
+// ------------------------------------------------------------------------------ status
+// Kernels never trap. A wait that runs out records LL_ERR_TIMEOUT (and where) in a
+// caller-visible status word and the kernel winds down; the host reads the word back.
+struct DevStatus {
+  int code;
+  int where;
+  int info;
+  int pad;
+};
+
+LL_DEV void report(DevStatus* st, int code, int where, int info) {
+  if (st && atomicCAS(&st->code, 0, code) == 0) {
+    st->where = where;
+    st->info = info;
+  }
+}
+
+// ---------------------------------------------------------------------------- mbarrier
+LL_DEV uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+LL_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+LL_DEV void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+LL_DEV void fence_async_smem() {  // generic-proxy smem writes -> visible to the async proxy
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+LL_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+LL_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+LL_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// ~1 s at the B200's clocks: a healthy pipeline waits microseconds.
+constexpr long long kWaitLimitCycles = 2000000000LL;
+
+// Bounded wait. Returns false (after recording the timeout and raising the CTA abort flag)
+// when the phase does not complete in time, or when another role already aborted.
+LL_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, DevStatus* st,
+                      int where) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      *abort_flag = 1;
+      report(st, LL_ERR_TIMEOUT, where, 0);
+      return false;
+    }
+  }
+}
+
+// --------------------------------------------------------------------------------- TMA
+LL_DEV void tma_prefetch_desc(const CUtensorMap* m) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+
+LL_DEV void tma_load_2d(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// ----------------------------------------------------------------------------- tcgen05
+LL_DEV void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {  // whole warp
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+LL_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // whole warp
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+LL_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+LL_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16 (fp16 or bf16 in, fp32 accumulate)
+LL_DEV void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05.mma issued so far by this thread has completed.
+LL_DEV void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+LL_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 16 consecutive 32-bit columns; thread i of the warp gets lane (base lane + i).
+LL_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// UMMA shared-memory descriptor (tcgen05 format): start address, leading / stride byte
+// offsets (all >> 4), version 1 at bits 46-47, layout type at bits 61-63.
+enum : uint32_t { kSwizzleNone = 0, kSwizzle128B = 2, kSwizzle64B = 4, kSwizzle32B = 6 };
+
+LL_DEV uint64_t umma_desc(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)(layout & 0x7) << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16: fp16 A and B, fp32 D, M = 128, N = n (multiple of 16).
+LL_DEV uint32_t idesc_f16_m128(uint32_t n, bool a_mn_major, bool b_mn_major) {
+  uint32_t d = 0;
+  d |= 1u << 4;                  // D format F32
+  d |= 0u << 7;                  // A format F16
+  d |= 0u << 10;                 // B format F16
+  d |= (a_mn_major ? 1u : 0u) << 15;
+  d |= (b_mn_major ? 1u : 0u) << 16;
+  d |= (n >> 3) << 17;
+  d |= (128u >> 4) << 24;
+  return d;
+}
+
+// ------------------------------------------------------------------------ MXFP4 decode
+// fp16 bit pattern of 2^(b - 127 + bias) for an E8M0 scale byte b; 0 for b >= 253 (an
+// unrepresentable / damaged group contributes nothing) and for exponents below fp16's
+// smallest subnormal 2^-24. The caller picks `bias` so that 6 * 2^(b-127+bias) <= 2^15.
+LL_DEV uint32_t e8m0_to_half_bits(uint32_t b, int bias) {
+  if (b >= 253u) return 0u;
+  const int e = (int)b - 127 + bias;
+  if (e >= -14) return (uint32_t)(e + 15) << 10;     // normal (e <= 15 guaranteed by bias)
+  if (e >= -24) return 1u << (e + 24);                // subnormal power of two
+  return 0u;
+}
+
+// Two E2M1 codes (low nibble = even element) -> fp16x2 (even element in the low half),
+// exact. One hardware conversion per byte.
+LL_DEV uint32_t e2m1x2_to_half2(uint32_t byte) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t}"
+      : "=r"(out)
+      : "r"(byte));
+  return out;
+}
+
+// Four bytes (8 codes) -> 4 x fp16x2, scaled by an fp16x2 splat of the group scale.
+LL_DEV void decode8(uint32_t w, uint32_t scale2, uint32_t (&o)[4]) {
+  uint32_t h0, h1, h2, h3;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(h0), "=r"(h1), "=r"(h2), "=r"(h3)
+      : "r"(w));
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[0]) : "r"(h0), "r"(scale2));
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[1]) : "r"(h1), "r"(scale2));
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[2]) : "r"(h2), "r"(scale2));
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[3]) : "r"(h3), "r"(scale2));
+}
+
+LL_DEV void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+LL_DEV uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+LL_DEV void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// -------------------------------------------------------------------------- SiTU-GLU
+// situ(g) = 4 tanh(g/4) sigmoid(g);  u' = 25 tanh(u/25)   (beta 4, linear beta 25)
+constexpr float kSituBeta = 4.0f;
+constexpr float kSituLinBeta = 25.0f;
+
+LL_DEV float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+LL_DEV float situ_glu_fwd(float g, float u) {
+  const float a = kSituBeta * tanhf(g / kSituBeta) * sigmoidf_(g);
+  return a * (kSituLinBeta * tanhf(u / kSituLinBeta));
+}
+
+LL_DEV void situ_glu_bwd(float go, float g, float u, float& dg, float& du) {
+  const float t = tanhf(g / kSituBeta);
+  const float s = sigmoidf_(g);
+  const float a = kSituBeta * t * s;
+  const float da = (1.0f - t * t) * s + kSituBeta * t * s * (1.0f - s);
+  const float tu = tanhf(u / kSituLinBeta);
+  dg = go * (kSituLinBeta * tu) * da;
+  du = go * a * (1.0f - tu * tu);
+}
+
+// power-of-two exponent that brings max|row| into [2^14, 2^15): fp16 keeps full precision
+// for the large entries and has headroom below 65504.
+LL_DEV int row_scale_exp(float maxabs) {
+  if (!(maxabs > 0.f) || !isfinite(maxabs)) return 0;
+  int e;
+  frexpf(maxabs, &e);   // maxabs = m * 2^e, m in [0.5, 1)
+  return 15 - e;        // maxabs * 2^(15-e) in [2^14, 2^15)
+}
+
+}  // namespace ll

@@ -1,0 +1,115 @@
+// Host-side helpers shared by the entry points: CUDA error capture, device properties,
+// TMA tensor-map encoding (through the driver entry point, so the library does not link
+// libcuda directly), workspace carving and the grouped-GEMM launcher.
+#pragma once
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "grouped_gemm.cuh"
+
+namespace ll {
+
+extern thread_local char g_last_cuda_error[256];
+extern thread_local int g_launch_count;
+// Optional CUDA events recorded around each grouped-GEMM launch (profiling hook).
+extern thread_local cudaEvent_t* g_prof_events;
+extern thread_local int g_prof_n;
+extern thread_local int g_prof_i;
+
+inline int cuda_fail(cudaError_t e, const char* what) {
+  snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s", what, cudaGetErrorString(e));
+  return LL_ERR_CUDA;
+}
+
+#define LL_CUDA(call)                                      \
+  do {                                                     \
+    cudaError_t e_ = (call);                               \
+    if (e_ != cudaSuccess) return ::ll::cuda_fail(e_, #call); \
+  } while (0)
+
+#define LL_TRY(call)             \
+  do {                           \
+    int s_ = (call);             \
+    if (s_ != LL_OK) return s_;  \
+  } while (0)
+
+inline int check_launch(const char* what) {
+  g_launch_count++;
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return LL_OK;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+  int minor = 0;
+};
+
+DeviceInfo device_info();   // of the current device, cached
+
+// ------------------------------------------------------------------------ tensor maps
+int make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t dim0, uint64_t dim1,
+                uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle sw);
+
+// Packed weight bytes [rows_total][cols/2] and scale bytes [rows_total][*] for the two
+// orientations of the grouped GEMM.
+inline int make_weight_maps(CUtensorMap* pk, CUtensorMap* sc, const uint8_t* packed, const uint8_t* scales,
+                            int64_t rows_total, int cols, int64_t scale_stride, bool trans) {
+  const uint32_t box_rows = trans ? 64 : 128;
+  LL_TRY(make_map_2d(pk, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, (uint64_t)cols / 2, (uint64_t)rows_total,
+                     (uint64_t)cols / 2, 64, box_rows, trans ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_64B));
+  LL_TRY(make_map_2d(sc, CU_TENSOR_MAP_DATA_TYPE_UINT8, scales, (uint64_t)cols / 32, (uint64_t)rows_total,
+                     (uint64_t)scale_stride, 16, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE));
+  return LL_OK;
+}
+
+// fp16 activation rows [rows][K], K-major 128-byte-swizzled boxes of 16 rows x 64 columns.
+inline int make_act_map(CUtensorMap* m, const __half* base, int64_t rows, int K) {
+  return make_map_2d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base, (uint64_t)K, (uint64_t)rows, (uint64_t)K * 2, 64, 16,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int set_smem_attr(const void* func, int bytes);
+
+template <int EPI, int NMAT, int NB, int ND, bool TRANS, int N_MAX>
+int launch_gemm(const CUtensorMap* pk, const CUtensorMap* sc, const CUtensorMap* act, const GemmArgs& a,
+                cudaStream_t stream) {
+  using Cfg = GemmCfg<NMAT, NB, ND, TRANS, N_MAX>;
+  TmaSet<NMAT, NB, ND, TRANS, N_MAX> tm;
+  for (int i = 0; i < NMAT; i++) { tm.pk[i] = pk[i]; tm.sc[i] = sc[i]; }
+  for (int i = 0; i < NB; i++) tm.act[i] = act[i];
+  auto kern = grouped_mxfp4_gemm<EPI, NMAT, NB, ND, TRANS, N_MAX>;
+  LL_TRY(set_smem_attr(reinterpret_cast<const void*>(kern), Cfg::SMEM));
+  const DeviceInfo di = device_info();
+  const bool prof = g_prof_events && g_prof_i + 2 <= g_prof_n;
+  if (prof) LL_CUDA(cudaEventRecord(g_prof_events[g_prof_i], stream));
+  kern<<<di.sms, Cfg::kThreads, Cfg::SMEM, stream>>>(tm, a);
+  const int rc = check_launch("grouped_mxfp4_gemm");
+  if (prof) {
+    LL_CUDA(cudaEventRecord(g_prof_events[g_prof_i + 1], stream));
+    g_prof_i += 2;
+  }
+  return rc;
+}
+
+// ----------------------------------------------------------------------- workspace
+struct Carver {
+  uint8_t* base;
+  size_t off = 0;
+  explicit Carver(void* b) : base(static_cast<uint8_t*>(b)) {}
+  template <class T>
+  T* take(size_t n) {
+    off = (off + 255) & ~size_t(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += n * sizeof(T);
+    return p;
+  }
+};
+
+// Status word + reset, read back after a sequence of launches.
+int reset_status(DevStatus* st, cudaStream_t s);
+int read_status(DevStatus* st, cudaStream_t s);
+
+}  // namespace ll

@@ -1,0 +1,375 @@
+// Drop-in MXFP4 kernels (device-pointer versions of lazy_lora/native/mxfp4_gemm.c) and the
+// host plumbing every entry point shares.
+#include <cuda_runtime.h>
+
+#include "host_common.cuh"
+#include "ops.cuh"
+
+namespace ll {
+
+thread_local char g_last_cuda_error[256] = "";
+thread_local int g_launch_count = 0;
+thread_local cudaEvent_t* g_prof_events = nullptr;
+thread_local int g_prof_n = 0;
+thread_local int g_prof_i = 0;
+static thread_local cudaEvent_t g_prof_store[64];
+
+DeviceInfo device_info() {
+  static DeviceInfo cache[64];
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  DeviceInfo& d = cache[dev & 63];
+  if (d.sms == 0) {
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
+  }
+  return d;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t dim0, uint64_t dim1,
+                uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "cuTensorMapEncodeTiled unavailable");
+    return LL_ERR_CUDA;
+  }
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (stride1_bytes & 15)) return LL_ERR_ARG;
+  cuuint64_t dims[2] = {dim0, dim1};
+  cuuint64_t strides[1] = {stride1_bytes};
+  cuuint32_t box[2] = {box0, box1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return LL_ERR_ARG;
+  }
+  return LL_OK;
+}
+
+int set_smem_attr(const void* func, int bytes) {
+  LL_CUDA(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  return LL_OK;
+}
+
+int reset_status(DevStatus* st, cudaStream_t s) {
+  LL_CUDA(cudaMemsetAsync(st, 0, sizeof(DevStatus), s));
+  return LL_OK;
+}
+
+int read_status(DevStatus* st, cudaStream_t s) {
+  DevStatus h;
+  LL_CUDA(cudaMemcpyAsync(&h, st, sizeof(DevStatus), cudaMemcpyDeviceToHost, s));
+  LL_CUDA(cudaStreamSynchronize(s));
+  if (h.code != 0) {
+    snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "device status %d at site %d (info %d)", h.code,
+             h.where, h.info);
+    return h.code;
+  }
+  return LL_OK;
+}
+
+int check_arch() {
+  const DeviceInfo d = device_info();
+  if (d.major != 10) return LL_ERR_ARCH;
+  return LL_OK;
+}
+
+// ------------------------------------------------------------------------- kernels
+
+// out[R,K] = W (exact). One thread per packed byte pair of elements; 16 bytes per thread.
+template <int OUT>  // 0 fp32, 1 bf16, 2 fp16
+__global__ void k_dequant(void* out, const uint8_t* __restrict__ packed, const uint8_t* __restrict__ scales,
+                          int K, int R, int64_t sstride) {
+  const int64_t groups = (int64_t)R * (K / 32);
+  for (int64_t gi = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; gi < groups; gi += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = gi / (K / 32);
+    const int g = (int)(gi % (K / 32));
+    const uint4 raw = *reinterpret_cast<const uint4*>(packed + r * (K / 2) + g * 16);
+    const uint32_t b = scales[r * sstride + g];
+    const float s = b >= 253u ? 0.f : ldexpf(1.f, (int)b - 127);
+    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+    const int64_t o = r * K + (int64_t)g * 32;
+#pragma unroll
+    for (int wi = 0; wi < 4; wi++) {
+      uint32_t h[4];
+      decode8(words[wi], 0x3C003C00u /* fp16 1.0 splat */, h);
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&h[j]));
+        const float v0 = v.x * s, v1 = v.y * s;   // exact: a 2-significant-bit value times 2^e
+        const int64_t idx = o + wi * 8 + j * 2;
+        if (OUT == 0) {
+          reinterpret_cast<float*>(out)[idx] = v0;
+          reinterpret_cast<float*>(out)[idx + 1] = v1;
+        } else if (OUT == 1) {
+          reinterpret_cast<__nv_bfloat16*>(out)[idx] = __float2bfloat16_rn(v0);
+          reinterpret_cast<__nv_bfloat16*>(out)[idx + 1] = __float2bfloat16_rn(v1);
+        } else {
+          reinterpret_cast<__half*>(out)[idx] = __float2half_rn(v0);
+          reinterpret_cast<__half*>(out)[idx + 1] = __float2half_rn(v1);
+        }
+      }
+    }
+  }
+}
+
+// beta[e*2 + col] = 140 - (largest scale byte < 253 of the expert's matrices), so that
+// 6 * 2^(b - 127 + beta) <= 2^15 for every byte: fp16 holds each decoded weight exactly for
+// bytes within 36 of that maximum. Matrices with no usable byte get beta 0.
+__global__ void k_prepare_beta(const uint8_t* __restrict__ s_a, const uint8_t* __restrict__ s_b, int rows, int ngroups,
+                               int64_t sstride, int32_t* beta, int col) {
+  const int e = blockIdx.x;
+  int mx = -1;
+  for (const uint8_t* s : {s_a, s_b}) {
+    if (!s) continue;
+    const uint8_t* base = s + (int64_t)e * rows * sstride;
+    for (int64_t i = threadIdx.x; i < (int64_t)rows * ngroups; i += blockDim.x) {
+      const int v = base[(i / ngroups) * sstride + (i % ngroups)];
+      if (v < 253 && v > mx) mx = v;
+    }
+  }
+  __shared__ int red[32];
+  for (int off = 16; off > 0; off >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int m = -1;
+    for (int i = 0; i < (int)(blockDim.x / 32); i++) m = max(m, red[i]);
+    beta[e * 2 + col] = m < 0 ? 0 : 140 - m;
+  }
+}
+
+// Row scaling into fp16: for each of `rows` output rows, src row = index ? index[row] : row,
+// sigma = row_scale_exp(max|src row|); dst = fp16(src * 2^sigma); inv[row] = 2^-sigma.
+// A row index < 0 yields a zero row. SRC: 0 fp32, 1 bf16.
+template <int SRC>
+__global__ void k_rows_to_half(const void* __restrict__ src, const int* __restrict__ index, int rows, int K,
+                               __half* __restrict__ dst, float* __restrict__ inv) {
+  const int row = blockIdx.x;
+  if (row >= rows) return;
+  const int sr = index ? index[row] : row;
+  __shared__ float red[32];
+  __shared__ float sh_scale;
+  float mx = 0.f;
+  if (sr >= 0) {
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+      const float v = SRC == 0 ? reinterpret_cast<const float*>(src)[(int64_t)sr * K + k]
+                               : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(src)[(int64_t)sr * K + k]);
+      mx = fmaxf(mx, fabsf(v));
+    }
+  }
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = 0.f;
+    for (int i = 0; i < (int)(blockDim.x / 32); i++) m = fmaxf(m, red[i]);
+    const int e = row_scale_exp(m);
+    sh_scale = ldexpf(1.f, e);
+    if (inv) inv[row] = ldexpf(1.f, -e);
+  }
+  __syncthreads();
+  const float sc = sh_scale;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    float v = 0.f;
+    if (sr >= 0)
+      v = SRC == 0 ? reinterpret_cast<const float*>(src)[(int64_t)sr * K + k]
+                   : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(src)[(int64_t)sr * K + k]);
+    dst[(int64_t)row * K + k] = __float2half_rn(v * sc);
+  }
+}
+
+__global__ void k_single_expert_chunks(Chunk* chunks, int* n_chunks, int M, int nmax) {
+  const int n = (M + nmax - 1) / nmax;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) chunks[i] = Chunk{0, i * nmax, min(nmax, M - i * nmax), 0};
+  if (threadIdx.x == 0) *n_chunks = n;
+}
+
+// --------------------------------------------------------------------- launchers
+
+int launch_prepare_beta(const uint8_t* s_a, const uint8_t* s_b, int E, int rows, int cols, int64_t sstride,
+                        int32_t* beta, int col, cudaStream_t s) {
+  k_prepare_beta<<<E, 256, 0, s>>>(s_a, s_b, rows, cols / 32, sstride, beta, col);
+  return check_launch("k_prepare_beta");
+}
+
+int launch_rows_to_half(const void* src, int src_dtype, const int* index, int rows, int K, __half* dst, float* inv,
+                        cudaStream_t s) {
+  if (rows <= 0) return LL_OK;
+  if (src_dtype == 0)
+    k_rows_to_half<0><<<rows, 256, 0, s>>>(src, index, rows, K, dst, inv);
+  else
+    k_rows_to_half<1><<<rows, 256, 0, s>>>(src, index, rows, K, dst, inv);
+  return check_launch("k_rows_to_half");
+}
+
+}  // namespace ll
+
+using namespace ll;
+
+static constexpr int kDropInNmax = 128;
+
+struct DropInWs {
+  DevStatus* st;
+  Chunk* chunks;
+  int* n_chunks;
+  int32_t* beta;
+  float* inv;
+  __half* act;
+};
+
+static size_t dropin_layout(void* base, int rows, int K, DropInWs* w) {
+  Carver c(base);
+  DropInWs t;
+  t.st = c.take<DevStatus>(1);
+  t.chunks = c.take<Chunk>((rows + kDropInNmax - 1) / kDropInNmax + 1);
+  t.n_chunks = c.take<int>(1);
+  t.beta = c.take<int32_t>(2);
+  t.inv = c.take<float>(rows);
+  t.act = c.take<__half>((size_t)rows * K);
+  if (w) *w = t;
+  return c.off + 256;
+}
+
+extern "C" {
+
+const char* ll_status_string(int status) {
+  switch (status) {
+    case LL_OK: return "ok";
+    case LL_ERR_ARG: return "invalid argument (shape, stride, alignment or pointer)";
+    case LL_ERR_CUDA: return "CUDA runtime error";
+    case LL_ERR_TIMEOUT: return "device-side wait timed out";
+    case LL_ERR_WORKSPACE: return "workspace too small";
+    case LL_ERR_RANGE: return "value outside the exactly representable range";
+    case LL_ERR_ARCH: return "device is not sm_100 (B200)";
+    default: return "unknown status";
+  }
+}
+
+const char* ll_last_cuda_error(void) { return g_last_cuda_error; }
+
+int ll_last_launch_count(void) { return g_launch_count; }
+
+int ll_mxfp4_threads(void) { return device_info().sms; }
+
+int ll_profile_gemm_events(void* const* events, int n) {
+  if (n < 0 || n > 64 || (n > 0 && !events)) return LL_ERR_ARG;
+  for (int i = 0; i < n; i++) g_prof_store[i] = static_cast<cudaEvent_t>(events[i]);
+  g_prof_events = n > 0 ? g_prof_store : nullptr;
+  g_prof_n = n;
+  g_prof_i = 0;
+  return LL_OK;
+}
+
+size_t ll_mxfp4_workspace_bytes(int M, int K, int R) {
+  const int rows = M;
+  const int width = K > R ? K : R;
+  return dropin_layout(nullptr, rows, width, nullptr);
+}
+
+int ll_mxfp4_dequant(void* out, const uint8_t* packed, const uint8_t* scales, int K, int R, int64_t scale_stride,
+                     int out_dtype, void* stream) {
+  if (K <= 0 || R <= 0 || K % 32 || !out || !packed || !scales || scale_stride < K / 32) return LL_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(packed) & 15)) return LL_ERR_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t groups = (int64_t)R * (K / 32);
+  const int grid = (int)std::min<int64_t>((groups + 255) / 256, 148 * 16);
+  if (out_dtype == 0) k_dequant<0><<<grid, 256, 0, s>>>(out, packed, scales, K, R, scale_stride);
+  else if (out_dtype == 1) k_dequant<1><<<grid, 256, 0, s>>>(out, packed, scales, K, R, scale_stride);
+  else if (out_dtype == 2) k_dequant<2><<<grid, 256, 0, s>>>(out, packed, scales, K, R, scale_stride);
+  else return LL_ERR_ARG;
+  return check_launch("k_dequant");
+}
+
+int ll_mxfp4_gemm(float* y, const float* x, const uint8_t* packed, const uint8_t* scales, int M, int K, int R,
+                  int64_t scale_stride, void* ws, size_t ws_bytes, void* stream) {
+  if (M <= 0 || K <= 0 || R <= 0 || K % 32 || scale_stride < K / 32 || scale_stride % 16) return LL_ERR_ARG;
+  if (!y || !x || !packed || !scales || !ws) return LL_ERR_ARG;
+  LL_TRY(check_arch());
+  if (ws_bytes < ll_mxfp4_workspace_bytes(M, K, R)) return LL_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DropInWs w;
+  dropin_layout(ws, M, K, &w);
+  g_launch_count = 0;
+  LL_TRY(reset_status(w.st, s));
+  k_single_expert_chunks<<<1, 128, 0, s>>>(w.chunks, w.n_chunks, M, kDropInNmax);
+  LL_TRY(check_launch("k_single_expert_chunks"));
+  LL_TRY(launch_prepare_beta(scales, nullptr, 1, R, K, scale_stride, w.beta, 0, s));
+  LL_TRY(launch_rows_to_half(x, 0, nullptr, M, K, w.act, w.inv, s));
+  CUtensorMap pk, sc, act;
+  LL_TRY(make_weight_maps(&pk, &sc, packed, scales, R, K, scale_stride, false));
+  LL_TRY(make_act_map(&act, w.act, M, K));
+  GemmArgs a{};
+  a.chunks = w.chunks;
+  a.n_chunks = w.n_chunks;
+  a.mtiles = (R + 127) / 128;
+  a.K = K;
+  a.e_rows = R;
+  a.status = w.st;
+  a.epi.row_scale_inv = w.inv;
+  a.epi.beta = w.beta;
+  a.epi.beta_col = 0;
+  a.epi.P = M;
+  a.epi.M = R;
+  a.epi.Y = y;
+  LL_TRY((launch_gemm<EPI_STORE, 1, 1, 1, false, kDropInNmax>(&pk, &sc, &act, a, s)));
+  return read_status(w.st, s);
+}
+
+int ll_mxfp4_gemm_t(float* y, const float* dy, const uint8_t* packed, const uint8_t* scales, int M, int K, int R,
+                    int64_t scale_stride, void* ws, size_t ws_bytes, void* stream) {
+  if (M <= 0 || K <= 0 || R <= 0 || K % 32 || R % 8 || scale_stride < K / 32 || scale_stride % 16) return LL_ERR_ARG;
+  if (!y || !dy || !packed || !scales || !ws) return LL_ERR_ARG;
+  LL_TRY(check_arch());
+  if (ws_bytes < ll_mxfp4_workspace_bytes(M, K, R)) return LL_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DropInWs w;
+  dropin_layout(ws, M, R, &w);
+  g_launch_count = 0;
+  LL_TRY(reset_status(w.st, s));
+  k_single_expert_chunks<<<1, 128, 0, s>>>(w.chunks, w.n_chunks, M, kDropInNmax);
+  LL_TRY(check_launch("k_single_expert_chunks"));
+  LL_TRY(launch_prepare_beta(scales, nullptr, 1, R, K, scale_stride, w.beta, 0, s));
+  LL_TRY(launch_rows_to_half(dy, 0, nullptr, M, R, w.act, w.inv, s));
+  CUtensorMap pk, sc, act;
+  LL_TRY(make_weight_maps(&pk, &sc, packed, scales, R, K, scale_stride, true));
+  LL_TRY(make_act_map(&act, w.act, M, R));
+  GemmArgs a{};
+  a.chunks = w.chunks;
+  a.n_chunks = w.n_chunks;
+  a.mtiles = (K + 127) / 128;
+  a.K = R;
+  a.e_rows = R;
+  a.status = w.st;
+  a.epi.row_scale_inv = w.inv;
+  a.epi.beta = w.beta;
+  a.epi.beta_col = 0;
+  a.epi.P = M;
+  a.epi.M = K;
+  a.epi.Y = y;
+  LL_TRY((launch_gemm<EPI_ACCUM, 1, 1, 1, true, kDropInNmax>(&pk, &sc, &act, a, s)));
+  return read_status(w.st, s);
+}
+
+}  // extern "C"
