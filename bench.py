@@ -235,6 +235,9 @@ def run_ours(args, cfg, rank, local, world, dist):
     stream = torch.cuda.current_stream()
     n_gemm_ev = 8
     gemm_events = [[torch.cuda.Event(enable_timing=True) for _ in range(n_gemm_ev)] for _ in range(args.steps)]
+    for evs in gemm_events:          # torch creates the CUDA event on first record
+        for e in evs:
+            e.record(stream)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches[0] = 0
     barrier()

@@ -133,9 +133,15 @@ __global__ void k_route_select(const float* __restrict__ a, const float* __restr
     }
   }
   if (lane == 0) {
+    // Sum in the order torch's CPU reduction uses for a short row (moe_router.py:97): eight
+    // lane accumulators (element i into lane i % 8, in order), then the lanes in order.
+    // For k <= 8 that is the plain left-to-right sum; for k = 16 it is sum_i (v_i + v_{i+8}).
     float denom = 0.f;
     if (k > 1 && renorm) {
-      for (int kk = 0; kk < k; kk++) denom += wsel[kk];
+      float lanes[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int kk = 0; kk < k; kk++) lanes[kk & 7] += wsel[kk];
+      denom = lanes[0];
+      for (int i = 1; i < 8; i++) denom += lanes[i];
       denom += 1e-20f;
     }
     for (int kk = 0; kk < k; kk++) {

@@ -60,6 +60,9 @@ CONFIGS: Dict[str, LayerConfig] = {
     "c3_t4": LayerConfig(d=7168, f=2048, E=896, k=8, T=4, zipf_s=1.1),
     "c3_t16": LayerConfig(d=7168, f=2048, E=896, k=8, T=16, zipf_s=1.1),
     "c4": LayerConfig(d=7168, f=2048, E=896, k=8, T=2048, r=64),
+    # configs[1]'s per-expert load (9 tokens per expert) on 64 experts: 1.5 GB of weights,
+    # larger than L2 but small enough for multi-pass ncu captures
+    "prof": LayerConfig(d=7168, f=2048, E=64, k=8, T=72),
     # small parity cases (K <= 4096 so the reference C kernel runs unchunked)
     "tiny": LayerConfig(d=256, f=128, E=8, k=2, T=16, r=4, alpha=8, x_dtype="f32"),
     "small": LayerConfig(d=1024, f=512, E=16, k=4, T=48, r=16, x_dtype="bf16"),
