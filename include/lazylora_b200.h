@@ -108,11 +108,22 @@ typedef struct {
   const float* A_g; const float* B_g;   /* gate LoRA A [r,d], B [f,r] */
   const float* A_u; const float* B_u;   /* up   LoRA A [r,d], B [f,r] */
   const float* A_d; const float* B_d;   /* down LoRA A [r,f], B [d,r] */
+  /* Transposed copies for the backward, built by ll_moe_prepare into caller buffers:
+   * codes of W^T ([E,d,f/2] for gate/up, [E,f,d/2] for down) and the per-element scales as
+   * fp16 multipliers with the decode bias folded in ([E,d/32,f] gate/up, [E,f/32,d] down). */
+  const uint8_t* w1t; const uint8_t* w3t; const uint8_t* w2t;
+  const uint16_t* s1t; const uint16_t* s3t; const uint16_t* s2t;
 } ll_moe_layer;
 
-/* Per-expert decode bias (beta[e][0] for gate+up, beta[e][1] for down) so that every scale
- * byte within 36 of the matrix maximum decodes exactly to fp16. Run once per weight load. */
+/* One-time preparation per weight load (the base weights are frozen): the per-expert
+ * decode bias beta (beta[e][0] gate+up, beta[e][1] down, so that every scale byte within 36
+ * of the matrix maximum decodes exactly to fp16), then the transposed copies w1t..s2t that
+ * L points at (beta_out must be L->beta). */
 int ll_moe_prepare(const ll_moe_layer* L, int32_t* beta_out, void* stream);
+
+/* Bytes of each transposed copy ll_moe_prepare fills: codes (same as the packed stack) and
+ * fp16 scale tables, for a stack of E matrices of R rows and C columns. */
+size_t ll_mxfp4_transposed_bytes(int E, int R, int C, int which /* 0 codes, 1 scales */);
 
 /* Workspace for a forward + backward of T tokens with top-k routing. The forward leaves
  * the activations the backward needs in it (the role of ctx.save_for_backward). */

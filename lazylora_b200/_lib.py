@@ -38,6 +38,8 @@ class MoELayerDesc(ctypes.Structure):
         ("beta", c_void_p),
         ("A_g", c_void_p), ("B_g", c_void_p), ("A_u", c_void_p), ("B_u", c_void_p),
         ("A_d", c_void_p), ("B_d", c_void_p),
+        ("w1t", c_void_p), ("w3t", c_void_p), ("w2t", c_void_p),
+        ("s1t", c_void_p), ("s3t", c_void_p), ("s2t", c_void_p),
     ]
 
 
@@ -58,6 +60,7 @@ _SIGS = {
     "ll_route_select": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_void_p, c_void_p,
                                 c_void_p]),
     "ll_moe_prepare": (c_int, [ctypes.POINTER(MoELayerDesc), c_void_p, c_void_p]),
+    "ll_mxfp4_transposed_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "ll_moe_workspace_bytes": (c_size_t, [ctypes.POINTER(MoELayerDesc), c_int, c_int]),
     "ll_moe_forward": (c_int, [ctypes.POINTER(MoELayerDesc), c_int, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                c_void_p, c_void_p, c_size_t, c_void_p]),

@@ -127,6 +127,29 @@ LL_DEV void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16. A occupies 128 lanes (lane = row m); a
+// 32-bit column c holds k = 2c (low half) and k = 2c + 1 (high half), 8 columns per K = 16.
+LL_DEV void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns from registers; thread i writes lane (base + i).
+LL_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+LL_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Arrive on `bar` once every tcgen05.mma issued so far by this thread has completed.
 LL_DEV void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -213,6 +236,23 @@ LL_DEV void decode8(uint32_t w, uint32_t scale2, uint32_t (&o)[4]) {
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[1]) : "r"(h1), "r"(scale2));
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[2]) : "r"(h2), "r"(scale2));
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[3]) : "r"(h3), "r"(scale2));
+}
+
+// Four bytes (8 codes) -> 4 x fp16x2, output pair j scaled by its own fp16x2 scale sc[j].
+LL_DEV void decode8v(uint32_t w, const uint32_t* sc, uint32_t* o) {
+  uint32_t h0, h1, h2, h3;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(h0), "=r"(h1), "=r"(h2), "=r"(h3)
+      : "r"(w));
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[0]) : "r"(h0), "r"(sc[0]));
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[1]) : "r"(h1), "r"(sc[1]));
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[2]) : "r"(h2), "r"(sc[2]));
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[3]) : "r"(h3), "r"(sc[3]));
 }
 
 LL_DEV void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {

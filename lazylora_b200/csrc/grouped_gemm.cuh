@@ -9,17 +9,24 @@
 // weight rows), tokens the B operand (N = 16..N_MAX), so the few tokens an expert gets do
 // not waste a 128-wide MMA dimension.
 //
-// Two orientations of the stored weight W[rows][cols]:
-//   K-major (TRANS = false): M = rows, K = cols  (forward: gate/up from W1/W3, down from W2)
-//   TRANS   (TRANS = true) : M = cols, K = rows  (backward: x W2 and the dX through W1/W3)
-// The packed bytes and the scale bytes are TMA-staged into shared memory as stored; the
-// dequant warps decode them (one cvt.e2m1x2 and one fp16x2 multiply per byte) and write
-// the A tile in the UMMA canonical 128-byte-swizzled layout, K-major or MN-major, so the
-// transposed use needs no transposed copy of the weights.
+// Data path per 128-element K stage: TMA brings the packed E2M1 bytes (and the scales) of
+// the weight tile into shared memory; each dequant thread owns one weight row (one TMEM
+// lane), decodes 32 consecutive K elements of it (one cvt.e2m1x2 and one fp16x2 multiply
+// per byte) and writes them into tensor memory with a single tcgen05.st; the MMA reads A
+// from tensor memory and the activations from shared memory (TMA, 128-byte swizzle). The
+// decoded weights never touch shared memory, which keeps the per-element shared-memory
+// traffic to the packed bytes.
+//
+// Scales. ROWSCALE (COLSCALE = false): the reference layout, one E8M0 byte per (row, 32
+// K elements), used for W as stored (forward: gate/up rows = f, down rows = d).
+// COLSCALE: the transposed copy of W that the backward reads (ll_moe_prepare builds it
+// once per weight load): codes [cols][rows/2], and one fp16 multiplier per (32-row group,
+// k) with the decode bias folded in, so the dequant thread multiplies each element pair by
+// its own pair of scales.
 //
 // Warp roles (15 warps): 0 packed/scale TMA, 1 activation TMA, 2 MMA issue + TMEM owner,
-// 3..10 dequant, 11..14 epilogue (double-buffered accumulators, so the epilogue of one unit
-// overlaps the main loop of the next).
+// 3..10 dequant (two warps per TMEM lane quarter, one per 32-element half of a 64-K
+// sub-chunk), 11..14 epilogue.
 #pragma once
 #include "common.cuh"
 
@@ -74,54 +81,58 @@ struct GemmArgs {
   const int* n_chunks;
   int mtiles;        // ceil(M / 128)
   int K;             // reduction length
-  int e_rows;        // stored rows per expert (K-major: M, TRANS: K)
+  int e_rows;        // stored weight rows per expert (= M)
   DevStatus* status;
   EpiParams epi;
 };
 
-template <int NMAT, int NB, int ND, bool TRANS, int N_MAX>
+template <int NMAT, int NB, int ND, bool COLSCALE, int N_MAX>
 struct GemmCfg {
   static constexpr int kThreads = 15 * 32;
-  static constexpr int kDqWarp0 = 3, kDqWarps = 8, kDqThreads = kDqWarps * 32;
+  static constexpr int kDqWarp0 = 3, kDqWarps = 8;
   static constexpr int kEpWarp0 = 11, kEpWarps = 4;
-  static constexpr int BK = TRANS ? 64 : 128;           // K per packed stage
-  static constexpr int SUBS = BK / 64;                   // A sub-chunks (K = 64) per stage
-  static constexpr int PK_BYTES = TRANS ? 64 * 64 : 128 * 64;
-  static constexpr int SC_BYTES = TRANS ? 64 * 16 : 128 * 16;
+  static constexpr int BK = 128;                          // K per packed stage
+  static constexpr int SUBS = 2;                          // 64-K A sub-chunks per stage
+  static constexpr int PK_BYTES = 128 * 64;               // 128 rows x 64 packed bytes
+  static constexpr int SC_BYTES = COLSCALE ? 4 * 128 * 2  // 4 row groups x 128 k x fp16
+                                           : 128 * 16;    // 128 rows x 16 scale bytes
   static constexpr int P_STAGE = NMAT * (PK_BYTES + SC_BYTES);
-  static constexpr int A_SLOT = NMAT * 16384;
-  static constexpr int S_A = 2;
   static constexpr int B_SLOT = NB * N_MAX * 128;
-  static constexpr int AVAIL = 227 * 1024 - 2048 - S_A * A_SLOT;
+  // tensor memory: accumulators first, then the A stages (32 columns per matrix and stage)
+  static constexpr int S_A = NMAT == 2 ? 3 : 4;
+  static constexpr int A_COLS = S_A * NMAT * 32;
+  static constexpr int NACC = (2 * ND * N_MAX + A_COLS <= 512) ? 2 : 1;
+  static constexpr int A_BASE = NACC * ND * N_MAX;
+  static constexpr int TMEM_COLS0 = A_BASE + A_COLS;
+  static constexpr int TMEM_COLS = TMEM_COLS0 <= 32 ? 32 : TMEM_COLS0 <= 64 ? 64 : TMEM_COLS0 <= 128 ? 128
+                                   : TMEM_COLS0 <= 256 ? 256 : 512;
+  static_assert(TMEM_COLS0 <= 512, "tensor memory budget");
+  // shared memory: B ring and packed ring
+  static constexpr int AVAIL = 227 * 1024 - 2048;
   static constexpr int S_B0 = (AVAIL * 2 / 5) / B_SLOT;
-  static constexpr int S_B = S_B0 < 2 ? 2 : (S_B0 > 8 ? 8 : S_B0);
+  static constexpr int S_B = S_B0 < 3 ? 3 : (S_B0 > 8 ? 8 : S_B0);
   static constexpr int S_P0 = (AVAIL - S_B * B_SLOT) / P_STAGE;
-  static constexpr int S_P = S_P0 < 2 ? 2 : (S_P0 > 16 ? 16 : S_P0);
-  static constexpr int OFF_A = 0;
-  static constexpr int OFF_B = OFF_A + S_A * A_SLOT;
+  static constexpr int S_P = S_P0 < 2 ? 2 : (S_P0 > 12 ? 12 : S_P0);
+  static constexpr int OFF_B = 0;
   static constexpr int OFF_P = OFF_B + S_B * B_SLOT;
   static constexpr int OFF_BAR = OFF_P + S_P * P_STAGE;
   static constexpr int N_BARS = 2 * S_P + 2 * S_A + 2 * S_B + 4 + 1;
   static constexpr int SMEM = OFF_BAR + N_BARS * 8 + 64 + 1024;  // + alignment slack
-  static constexpr int TMEM_COLS0 = 2 * ND * N_MAX;
-  static constexpr int TMEM_COLS = TMEM_COLS0 <= 32 ? 32 : TMEM_COLS0 <= 64 ? 64 : TMEM_COLS0 <= 128 ? 128
-                                   : TMEM_COLS0 <= 256 ? 256 : 512;
-  static_assert(TMEM_COLS0 <= 512, "accumulators exceed tensor memory");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
   static_assert(N_MAX % 16 == 0 && N_MAX <= 256, "N_MAX");
 };
 
-template <int NMAT, int NB, int ND, bool TRANS, int N_MAX>
+template <int NMAT, int NB>
 struct TmaSet {
   CUtensorMap pk[NMAT];
   CUtensorMap sc[NMAT];
   CUtensorMap act[NB];
 };
 
-template <int EPI, int NMAT, int NB, int ND, bool TRANS, int N_MAX>
+template <int EPI, int NMAT, int NB, int ND, bool COLSCALE, int N_MAX>
 __global__ void __launch_bounds__(15 * 32, 1)
-grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB, ND, TRANS, N_MAX> tm, const GemmArgs args) {
-  using C = GemmCfg<NMAT, NB, ND, TRANS, N_MAX>;
+grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs args) {
+  using C = GemmCfg<NMAT, NB, ND, COLSCALE, N_MAX>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -174,27 +185,25 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB, ND, TRANS, N_MAX> tm
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const Chunk ch = args.chunks[u / args.mtiles];
         const int mt = u % args.mtiles;
+        const int row = ch.e * args.e_rows + mt * 128;
+        const int grp = (ch.e * args.e_rows) / 32 + mt * 4;
         for (int ks = 0; ks < n_stage && ok; ks++) {
           if (!(ok = mbar_wait(&pempty[s], ph ^ 1, abort_flag, st, 1))) break;
           uint8_t* stage = smem + C::OFF_P + s * C::P_STAGE;
           mbar_arrive_expect_tx(&pfull[s], C::P_STAGE);
           for (int i = 0; i < NMAT; i++) {
             uint8_t* pk = stage + i * (C::PK_BYTES + C::SC_BYTES);
-            if (!TRANS) {
-              const int row = ch.e * args.e_rows + mt * 128;
-              tma_load_2d(pk, &tm.pk[i], &pfull[s], ks * (C::BK / 2), row);
+            tma_load_2d(pk, &tm.pk[i], &pfull[s], ks * (C::BK / 2), row);
+            if (COLSCALE)
+              tma_load_2d(pk + C::PK_BYTES, &tm.sc[i], &pfull[s], ks * C::BK, grp);
+            else
               tma_load_2d(pk + C::PK_BYTES, &tm.sc[i], &pfull[s], ((ks * C::BK) / 32) & ~15, row);
-            } else {
-              const int row = ch.e * args.e_rows + ks * C::BK;
-              tma_load_2d(pk, &tm.pk[i], &pfull[s], mt * 64, row);
-              tma_load_2d(pk + C::PK_BYTES, &tm.sc[i], &pfull[s], (mt * 4) & ~15, row);
-            }
           }
           issued++;
           if (++s == C::S_P) { s = 0; ph ^= 1; }
         }
       }
-      // drain: the last min(issued, S_P) stages were issued; wait for their bytes to land
+      // drain: wait for the bytes of the last issued stages to land before exiting
       for (int i = 0; i < C::S_P && i < issued; i++) {
         if (--s < 0) { s = C::S_P - 1; ph ^= 1; }
         mbar_wait(&pfull[s], ph, abort_flag, st, 11);
@@ -236,7 +245,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB, ND, TRANS, N_MAX> tm
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const Chunk ch = args.chunks[u / args.mtiles];
         const int npad = (ch.n + 15) & ~15;
-        const uint32_t idesc = idesc_f16_m128(npad, TRANS, false);
+        const uint32_t idesc = idesc_f16_m128(npad, false, false);
         if (!(ok = mbar_wait(&accempty[ab], abph ^ 1, abort_flag, st, 3))) break;
         tc_fence_after();
         const uint32_t d0 = tmem + ab * ND * N_MAX;
@@ -244,20 +253,17 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB, ND, TRANS, N_MAX> tm
           if (!(ok = mbar_wait(&afull[as], aph, abort_flag, st, 4))) break;
           if (!(ok = mbar_wait(&bfull[bs], bph, abort_flag, st, 5))) break;
           tc_fence_after();
-          const uint32_t a_base = smem_u32(smem + C::OFF_A + as * C::A_SLOT);
           const uint32_t b_base = smem_u32(smem + C::OFF_B + bs * C::B_SLOT);
 #pragma unroll
           for (int i = 0; i < NMAT; i++) {
             const uint32_t d = d0 + (ND == 2 ? i : 0) * N_MAX;
-            const uint32_t a_addr = a_base + i * 16384;
+            const uint32_t a_tmem = tmem + C::A_BASE + (as * NMAT + i) * 32;
             const uint32_t b_addr = b_base + (NB == 2 ? i : 0) * N_MAX * 128;
 #pragma unroll
             for (int kk = 0; kk < 4; kk++) {
-              const uint64_t adesc = TRANS ? umma_desc(a_addr + kk * 4096, 1024, 2048, kSwizzle128B)
-                                           : umma_desc(a_addr + kk * 32, 16, 1024, kSwizzle128B);
               const uint64_t bdesc = umma_desc(b_addr + kk * 32, 16, 1024, kSwizzle128B);
               const uint32_t acc = (sb > 0 || kk > 0 || (ND == 1 && i > 0)) ? 1u : 0u;
-              mma_f16_ss(d, adesc, bdesc, idesc, acc);
+              mma_f16_ts(d, a_tmem + kk * 8, bdesc, idesc, acc);
             }
           }
           mma_commit(&aempty[as]);
@@ -266,14 +272,19 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB, ND, TRANS, N_MAX> tm
           if (++bs == C::S_B) { bs = 0; bph ^= 1; }
         }
         mma_commit(&accfull[ab]);
-        if (++ab == 2) { ab = 0; abph ^= 1; }
+        if (++ab == C::NACC) { ab = 0; abph ^= 1; }
       }
       mma_commit(drain);            // completes once every MMA issued above has finished
       mbar_wait(drain, 0, abort_flag, st, 13);
     }
   } else if (warp < C::kEpWarp0) {
     // ---------------------------------------------------------------- dequant warps
-    const int dt = threadIdx.x - C::kDqWarp0 * 32;   // 0..255
+    // warp -> (TMEM lane quarter q, 32-element half h of each 64-K sub-chunk); thread -> row
+    const int dw = warp - C::kDqWarp0;           // 0..7
+    const int q = warp & 3;
+    const int h = dw >> 2;
+    const int m = q * 32 + lane;                 // weight row within the 128-row tile
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const int32_t* beta = args.epi.beta;
     const int bcol = args.epi.beta_col;
     int ps = 0, as = 0;
@@ -281,68 +292,45 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB, ND, TRANS, N_MAX> tm
     bool ok = true;
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
       const Chunk ch = args.chunks[u / args.mtiles];
-      const int mt = u % args.mtiles;
-      const int bias = beta ? beta[ch.e * 2 + bcol] : 0;
+      const int bias = (!COLSCALE && beta) ? beta[ch.e * 2 + bcol] : 0;
       for (int ks = 0; ks < n_stage && ok; ks++) {
         if (!(ok = mbar_wait(&pfull[ps], pph, abort_flag, st, 6))) break;
         const uint8_t* stage = smem + C::OFF_P + ps * C::P_STAGE;
         for (int sub = 0; sub < C::SUBS; sub++) {
           if (ks * C::SUBS + sub >= n_sub) break;
           if (!(ok = mbar_wait(&aempty[as], aph ^ 1, abort_flag, st, 7))) break;
-          uint8_t* aslot = smem + C::OFF_A + as * C::A_SLOT;
+          tc_fence_after();
+          const int c = sub * 2 + h;                   // 16-byte chunk (32 K) in the 64-byte row
 #pragma unroll
-          for (int it = 0; it < 2 * NMAT; it++) {
-            const int q = dt + it * C::kDqThreads;      // 0 .. 256*NMAT*... items
-            const int mat = q / 256;
-            const int qi = q % 256;
-            if (mat >= NMAT) break;
-            const uint8_t* pk = stage + mat * (C::PK_BYTES + C::SC_BYTES);
+          for (int i = 0; i < NMAT; i++) {
+            const uint8_t* pk = stage + i * (C::PK_BYTES + C::SC_BYTES);
             const uint8_t* sc = pk + C::PK_BYTES;
-            const uint32_t abase = smem_u32(aslot + mat * 16384);
-            if (!TRANS) {
-              // item = (row m, 32-K group h of this 64-K sub-chunk)
-              const int m = qi % 128;
-              const int h = qi / 128;
-              const int c = sub * 2 + h;                                   // 16-B chunk in the 64-B row
-              const uint4 raw = ld_shared_v4(smem_u32(pk + m * 64 + ((c ^ ((m >> 1) & 3)) << 4)));
+            const uint4 raw = ld_shared_v4(smem_u32(pk + m * 64 + ((c ^ ((m >> 1) & 3)) << 4)));
+            uint32_t o[16];
+            if (COLSCALE) {
+              // fp16 multipliers of k = 32c .. 32c+31 for this warp's 32-row group q
+              const uint32_t sa = smem_u32(sc + (q * 128 + c * 32) * 2);
+              const uint4 s0 = ld_shared_v4(sa), s1 = ld_shared_v4(sa + 16);
+              const uint4 s2 = ld_shared_v4(sa + 32), s3 = ld_shared_v4(sa + 48);
+              const uint32_t sv[16] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w,
+                                       s2.x, s2.y, s2.z, s2.w, s3.x, s3.y, s3.z, s3.w};
+              decode8v(raw.x, &sv[0], &o[0]);
+              decode8v(raw.y, &sv[4], &o[4]);
+              decode8v(raw.z, &sv[8], &o[8]);
+              decode8v(raw.w, &sv[12], &o[12]);
+            } else {
               const uint32_t sbyte = sc[m * 16 + (((ks * C::BK) / 32) & 15) + c];
               const uint32_t s1 = e8m0_to_half_bits(sbyte, bias);
               const uint32_t s2 = s1 | (s1 << 16);
-              uint32_t o[16];
               decode8(raw.x, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[0]));
               decode8(raw.y, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[4]));
               decode8(raw.z, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[8]));
               decode8(raw.w, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[12]));
-              const uint32_t rowaddr = abase + m * 128;
-#pragma unroll
-              for (int j = 0; j < 4; j++) {
-                const int kc = h * 4 + j;                                  // 8-element K chunk
-                st_shared_v4(rowaddr + ((kc ^ (m & 7)) << 4), o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-              }
-            } else {
-              // item = (K row k of this 64-row stage, 32-wide M block c)
-              const int k = qi / 4;
-              const int c = qi % 4;
-              const uint4 raw = ld_shared_v4(smem_u32(pk + k * 64 + c * 16));
-              const uint32_t sbyte = sc[k * 16 + ((mt * 4) & 15) + c];
-              const uint32_t s1 = e8m0_to_half_bits(sbyte, bias);
-              const uint32_t s2 = s1 | (s1 << 16);
-              uint32_t o[16];
-              decode8(raw.x, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[0]));
-              decode8(raw.y, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[4]));
-              decode8(raw.z, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[8]));
-              decode8(raw.w, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[12]));
-              const int r = k & 7;
-              const uint32_t base = abase + (k >> 3) * 2048 + (c >> 1) * 1024 + r * 128;
-#pragma unroll
-              for (int j0 = 0; j0 < 4; j0++) {
-                const int j = (j0 + (c >> 1) * 2) & 3;                   // staggers the two atoms' banks
-                const int chunk16 = (c & 1) * 4 + j;
-                st_shared_v4(base + ((chunk16 ^ r) << 4), o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-              }
             }
+            tmem_st16(tmem + lane_base + C::A_BASE + (as * NMAT + i) * 32 + h * 16, o);
           }
-          fence_async_smem();
+          tmem_st_wait();
+          tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&afull[as]);
           if (++as == C::S_A) { as = 0; aph ^= 1; }
@@ -438,7 +426,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB, ND, TRANS, N_MAX> tm
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&accempty[ab]);
-      if (++ab == 2) { ab = 0; abph ^= 1; }
+      if (++ab == C::NACC) { ab = 0; abph ^= 1; }
     }
   }
 

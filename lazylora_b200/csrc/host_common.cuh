@@ -53,15 +53,25 @@ DeviceInfo device_info();   // of the current device, cached
 int make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t dim0, uint64_t dim1,
                 uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle sw);
 
-// Packed weight bytes [rows_total][cols/2] and scale bytes [rows_total][*] for the two
-// orientations of the grouped GEMM.
-inline int make_weight_maps(CUtensorMap* pk, CUtensorMap* sc, const uint8_t* packed, const uint8_t* scales,
-                            int64_t rows_total, int cols, int64_t scale_stride, bool trans) {
-  const uint32_t box_rows = trans ? 64 : 128;
+// Packed weight bytes [rows_total][cols/2] (boxes of 128 rows x 64 bytes, 64-byte swizzle)
+// with the reference's E8M0 scale bytes [rows_total][scale_stride] (boxes of 128 x 16 bytes).
+inline int make_rowscale_maps(CUtensorMap* pk, CUtensorMap* sc, const uint8_t* packed, const uint8_t* scales,
+                              int64_t rows_total, int cols, int64_t scale_stride) {
   LL_TRY(make_map_2d(pk, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, (uint64_t)cols / 2, (uint64_t)rows_total,
-                     (uint64_t)cols / 2, 64, box_rows, trans ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_64B));
+                     (uint64_t)cols / 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_64B));
   LL_TRY(make_map_2d(sc, CU_TENSOR_MAP_DATA_TYPE_UINT8, scales, (uint64_t)cols / 32, (uint64_t)rows_total,
-                     (uint64_t)scale_stride, 16, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE));
+                     (uint64_t)scale_stride, 16, 128, CU_TENSOR_MAP_SWIZZLE_NONE));
+  return LL_OK;
+}
+
+// Transposed codes [rows_total][K/2] with the fp16 column-scale table [rows_total/32][K]
+// (boxes of 4 row groups x 128 k).
+inline int make_colscale_maps(CUtensorMap* pk, CUtensorMap* sc, const uint8_t* codes, const __half* cscales,
+                              int64_t rows_total, int K) {
+  LL_TRY(make_map_2d(pk, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, (uint64_t)K / 2, (uint64_t)rows_total, (uint64_t)K / 2,
+                     64, 128, CU_TENSOR_MAP_SWIZZLE_64B));
+  LL_TRY(make_map_2d(sc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, cscales, (uint64_t)K, (uint64_t)rows_total / 32,
+                     (uint64_t)K * 2, 128, 4, CU_TENSOR_MAP_SWIZZLE_NONE));
   return LL_OK;
 }
 
@@ -73,14 +83,14 @@ inline int make_act_map(CUtensorMap* m, const __half* base, int64_t rows, int K)
 
 int set_smem_attr(const void* func, int bytes);
 
-template <int EPI, int NMAT, int NB, int ND, bool TRANS, int N_MAX>
+template <int EPI, int NMAT, int NB, int ND, bool COLSCALE, int N_MAX>
 int launch_gemm(const CUtensorMap* pk, const CUtensorMap* sc, const CUtensorMap* act, const GemmArgs& a,
                 cudaStream_t stream) {
-  using Cfg = GemmCfg<NMAT, NB, ND, TRANS, N_MAX>;
-  TmaSet<NMAT, NB, ND, TRANS, N_MAX> tm;
+  using Cfg = GemmCfg<NMAT, NB, ND, COLSCALE, N_MAX>;
+  TmaSet<NMAT, NB> tm;
   for (int i = 0; i < NMAT; i++) { tm.pk[i] = pk[i]; tm.sc[i] = sc[i]; }
   for (int i = 0; i < NB; i++) tm.act[i] = act[i];
-  auto kern = grouped_mxfp4_gemm<EPI, NMAT, NB, ND, TRANS, N_MAX>;
+  auto kern = grouped_mxfp4_gemm<EPI, NMAT, NB, ND, COLSCALE, N_MAX>;
   LL_TRY(set_smem_attr(reinterpret_cast<const void*>(kern), Cfg::SMEM));
   const DeviceInfo di = device_info();
   const bool prof = g_prof_events && g_prof_i + 2 <= g_prof_n;

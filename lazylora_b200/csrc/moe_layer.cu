@@ -486,14 +486,15 @@ static int validate(const ll_moe_layer* L, int T, int k) {
   if (L->s13_stride < L->d / 32 || L->s13_stride % 16 || L->s2_stride < L->f / 32 || L->s2_stride % 16) return LL_ERR_ARG;
   if (!L->w1p || !L->w1s || !L->w3p || !L->w3s || !L->w2p || !L->w2s || !L->beta) return LL_ERR_ARG;
   if (!L->A_g || !L->B_g || !L->A_u || !L->B_u || !L->A_d || !L->B_d) return LL_ERR_ARG;
+  if (!L->w1t || !L->w3t || !L->w2t || !L->s1t || !L->s3t || !L->s2t) return LL_ERR_ARG;
   return LL_OK;
 }
 
-template <int EPI, int NMAT, int NB, int ND, bool TRANS>
+template <int EPI, int NMAT, int NB, int ND, bool COLSCALE>
 static int gemm_nmax(int nmax, const CUtensorMap* pk, const CUtensorMap* sc, const CUtensorMap* act, const GemmArgs& a,
                      cudaStream_t s) {
-  if (nmax == 32) return launch_gemm<EPI, NMAT, NB, ND, TRANS, 32>(pk, sc, act, a, s);
-  return launch_gemm<EPI, NMAT, NB, ND, TRANS, 128>(pk, sc, act, a, s);
+  if (nmax == 32) return launch_gemm<EPI, NMAT, NB, ND, COLSCALE, 32>(pk, sc, act, a, s);
+  return launch_gemm<EPI, NMAT, NB, ND, COLSCALE, 128>(pk, sc, act, a, s);
 }
 
 template <int QK, bool PG>
@@ -517,11 +518,23 @@ using namespace ll;
 
 extern "C" {
 
+size_t ll_mxfp4_transposed_bytes(int E, int R, int C, int which) {
+  if (E <= 0 || R <= 0 || C <= 0) return 0;
+  return which == 0 ? (size_t)E * R * C / 2 : (size_t)E * (C / 32) * R * 2;
+}
+
 int ll_moe_prepare(const ll_moe_layer* L, int32_t* beta_out, void* stream) {
-  if (!L || !beta_out || L->E <= 0 || L->d <= 0 || L->f <= 0) return LL_ERR_ARG;
+  if (!L || !beta_out || L->E <= 0 || L->d <= 0 || L->f <= 0 || L->d % 128 || L->f % 128) return LL_ERR_ARG;
+  if (!L->w1t || !L->w3t || !L->w2t || !L->s1t || !L->s3t || !L->s2t) return LL_ERR_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  LL_TRY(launch_prepare_beta(L->w1s, L->w3s, L->E, L->f, L->d, L->s13_stride, beta_out, 0, s));
-  LL_TRY(launch_prepare_beta(L->w2s, nullptr, L->E, L->d, L->f, L->s2_stride, beta_out, 1, s));
+  const int E = L->E, d = L->d, f = L->f;
+  LL_TRY(launch_prepare_beta(L->w1s, L->w3s, E, f, d, L->s13_stride, beta_out, 0, s));
+  LL_TRY(launch_prepare_beta(L->w2s, nullptr, E, d, f, L->s2_stride, beta_out, 1, s));
+  auto cw = [](const uint8_t* p) { return const_cast<uint8_t*>(p); };
+  auto ch = [](const uint16_t* p) { return reinterpret_cast<__half*>(const_cast<uint16_t*>(p)); };
+  LL_TRY(launch_transpose_mxfp4(L->w1p, L->w1s, L->s13_stride, E, f, d, beta_out, 0, cw(L->w1t), ch(L->s1t), s));
+  LL_TRY(launch_transpose_mxfp4(L->w3p, L->w3s, L->s13_stride, E, f, d, beta_out, 0, cw(L->w3t), ch(L->s3t), s));
+  LL_TRY(launch_transpose_mxfp4(L->w2p, L->w2s, L->s2_stride, E, d, f, beta_out, 1, cw(L->w2t), ch(L->s2t), s));
   return LL_OK;
 }
 
@@ -568,8 +581,8 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   // F1: gate / up
   {
     CUtensorMap pk[2], sc[2], act[1];
-    LL_TRY(make_weight_maps(&pk[0], &sc[0], L->w1p, L->w1s, (int64_t)E * f, d, L->s13_stride, false));
-    LL_TRY(make_weight_maps(&pk[1], &sc[1], L->w3p, L->w3s, (int64_t)E * f, d, L->s13_stride, false));
+    LL_TRY(make_rowscale_maps(&pk[0], &sc[0], L->w1p, L->w1s, (int64_t)E * f, d, L->s13_stride));
+    LL_TRY(make_rowscale_maps(&pk[1], &sc[1], L->w3p, L->w3s, (int64_t)E * f, d, L->s13_stride));
     LL_TRY(make_act_map(&act[0], W.xh, P, d));
     GemmArgs a{};
     a.chunks = W.chunks;
@@ -602,7 +615,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   // F2: down
   {
     CUtensorMap pk[1], sc[1], act[1];
-    LL_TRY(make_weight_maps(&pk[0], &sc[0], L->w2p, L->w2s, (int64_t)E * d, f, L->s2_stride, false));
+    LL_TRY(make_rowscale_maps(&pk[0], &sc[0], L->w2p, L->w2s, (int64_t)E * d, f, L->s2_stride));
     LL_TRY(make_act_map(&act[0], W.H, P, f));
     GemmArgs a{};
     a.chunks = W.chunks;
@@ -652,14 +665,14 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
   // B1: v = g . W2 (+ LoRA down), SiTU-GLU backward
   {
     CUtensorMap pk[1], sc[1], act[1];
-    LL_TRY(make_weight_maps(&pk[0], &sc[0], L->w2p, L->w2s, (int64_t)E * d, f, L->s2_stride, true));
+    LL_TRY(make_colscale_maps(&pk[0], &sc[0], L->w2t, reinterpret_cast<const __half*>(L->s2t), (int64_t)E * f, d));
     LL_TRY(make_act_map(&act[0], W.gh, P, d));
     GemmArgs a{};
     a.chunks = W.chunks;
     a.n_chunks = W.n_chunks;
     a.mtiles = f / 128;
     a.K = d;
-    a.e_rows = d;
+    a.e_rows = f;
     a.status = W.st;
     a.epi.perm_token = W.perm_token;
     a.epi.row_scale_inv = W.ginv;
@@ -684,8 +697,8 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
   // B2: dX = dg . W1 + du . W3
   {
     CUtensorMap pk[2], sc[2], act[2];
-    LL_TRY(make_weight_maps(&pk[0], &sc[0], L->w1p, L->w1s, (int64_t)E * f, d, L->s13_stride, true));
-    LL_TRY(make_weight_maps(&pk[1], &sc[1], L->w3p, L->w3s, (int64_t)E * f, d, L->s13_stride, true));
+    LL_TRY(make_colscale_maps(&pk[0], &sc[0], L->w1t, reinterpret_cast<const __half*>(L->s1t), (int64_t)E * d, f));
+    LL_TRY(make_colscale_maps(&pk[1], &sc[1], L->w3t, reinterpret_cast<const __half*>(L->s3t), (int64_t)E * d, f));
     LL_TRY(make_act_map(&act[0], W.DGh, P, f));
     LL_TRY(make_act_map(&act[1], W.DUh, P, f));
     GemmArgs a{};
@@ -693,7 +706,7 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
     a.n_chunks = W.n_chunks;
     a.mtiles = d / 128;
     a.K = f;
-    a.e_rows = f;
+    a.e_rows = d;
     a.status = W.st;
     a.epi.perm_token = W.perm_token;
     a.epi.row_scale_inv = W.rinv;

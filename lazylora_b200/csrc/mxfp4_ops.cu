@@ -200,6 +200,47 @@ __global__ void k_rows_to_half(const void* __restrict__ src, const int* __restri
   }
 }
 
+// Transposed copy of an MXFP4 stack for the backward GEMMs. For every expert:
+//   codes_t[c][r/2]  = the E2M1 codes of W[r][c], transposed (element 2j of a row still in
+//                      the low nibble of byte j), and
+//   scales_t[c/32][r] = fp16 of 2^(b - 127 + beta) for the scale byte b of (r, c/32): the
+//                      multiplier of every element of that group, decode bias included
+//                      (0 for bytes >= 253).
+// One 64 x 64 element tile per block.
+__global__ void k_transpose_mxfp4(const uint8_t* __restrict__ packed, const uint8_t* __restrict__ scales,
+                                  int64_t sstride, int R, int C, const int32_t* __restrict__ beta, int col,
+                                  uint8_t* __restrict__ codes_t, __half* __restrict__ scales_t) {
+  __shared__ uint8_t tile[64][65];
+  const int e = blockIdx.z;
+  const int r0 = blockIdx.y * 64, c0 = blockIdx.x * 64;
+  const uint8_t* pe = packed + (int64_t)e * R * (C / 2);
+  for (int i = threadIdx.x; i < 64 * 32; i += blockDim.x) {
+    const int r = i / 32, b = i % 32;
+    uint8_t v = 0;
+    if (r0 + r < R && c0 + 2 * b < C) v = pe[(int64_t)(r0 + r) * (C / 2) + c0 / 2 + b];
+    tile[r][2 * b] = v & 0x0F;
+    tile[r][2 * b + 1] = v >> 4;
+  }
+  __syncthreads();
+  uint8_t* te = codes_t + (int64_t)e * C * (R / 2);
+  for (int i = threadIdx.x; i < 64 * 32; i += blockDim.x) {
+    const int c = i / 32, j = i % 32;
+    if (c0 + c < C && r0 + 2 * j < R)
+      te[(int64_t)(c0 + c) * (R / 2) + r0 / 2 + j] = (uint8_t)(tile[2 * j][c] | (tile[2 * j + 1][c] << 4));
+  }
+  const int bias = beta ? beta[e * 2 + col] : 0;
+  const uint8_t* se = scales + (int64_t)e * R * sstride;
+  __half* ste = scales_t + (int64_t)e * (C / 32) * R;
+  for (int i = threadIdx.x; i < 2 * 64; i += blockDim.x) {
+    const int g = i / 64, r = i % 64;
+    const int cg = c0 / 32 + g;
+    if (r0 + r < R && cg * 32 < C) {
+      const uint32_t bits = e8m0_to_half_bits(se[(int64_t)(r0 + r) * sstride + cg], bias);
+      ste[(int64_t)cg * R + r0 + r] = __ushort_as_half((unsigned short)bits);
+    }
+  }
+}
+
 __global__ void k_single_expert_chunks(Chunk* chunks, int* n_chunks, int M, int nmax) {
   const int n = (M + nmax - 1) / nmax;
   for (int i = threadIdx.x; i < n; i += blockDim.x) chunks[i] = Chunk{0, i * nmax, min(nmax, M - i * nmax), 0};
@@ -212,6 +253,13 @@ int launch_prepare_beta(const uint8_t* s_a, const uint8_t* s_b, int E, int rows,
                         int32_t* beta, int col, cudaStream_t s) {
   k_prepare_beta<<<E, 256, 0, s>>>(s_a, s_b, rows, cols / 32, sstride, beta, col);
   return check_launch("k_prepare_beta");
+}
+
+int launch_transpose_mxfp4(const uint8_t* packed, const uint8_t* scales, int64_t sstride, int E, int R, int C,
+                           const int32_t* beta, int col, uint8_t* codes_t, __half* scales_t, cudaStream_t s) {
+  dim3 grid((C + 63) / 64, (R + 63) / 64, E);
+  k_transpose_mxfp4<<<grid, 256, 0, s>>>(packed, scales, sstride, R, C, beta, col, codes_t, scales_t);
+  return check_launch("k_transpose_mxfp4");
 }
 
 int launch_rows_to_half(const void* src, int src_dtype, const int* index, int rows, int K, __half* dst, float* inv,
@@ -237,9 +285,12 @@ struct DropInWs {
   int32_t* beta;
   float* inv;
   __half* act;
+  uint8_t* codes_t;    // gemm_t: transposed codes [K][R/2]
+  __half* scales_t;    // gemm_t: fp16 column multipliers [K/32][R]
 };
 
-static size_t dropin_layout(void* base, int rows, int K, DropInWs* w) {
+// rows: activation rows (M); width: activation row length; R, K: the weight's shape
+static size_t dropin_layout(void* base, int rows, int width, int R, int K, DropInWs* w) {
   Carver c(base);
   DropInWs t;
   t.st = c.take<DevStatus>(1);
@@ -247,7 +298,9 @@ static size_t dropin_layout(void* base, int rows, int K, DropInWs* w) {
   t.n_chunks = c.take<int>(1);
   t.beta = c.take<int32_t>(2);
   t.inv = c.take<float>(rows);
-  t.act = c.take<__half>((size_t)rows * K);
+  t.act = c.take<__half>((size_t)rows * width);
+  t.codes_t = c.take<uint8_t>((size_t)R * K / 2);
+  t.scales_t = c.take<__half>((size_t)(K / 32) * R);
   if (w) *w = t;
   return c.off + 256;
 }
@@ -283,9 +336,7 @@ int ll_profile_gemm_events(void* const* events, int n) {
 }
 
 size_t ll_mxfp4_workspace_bytes(int M, int K, int R) {
-  const int rows = M;
-  const int width = K > R ? K : R;
-  return dropin_layout(nullptr, rows, width, nullptr);
+  return dropin_layout(nullptr, M, K > R ? K : R, R, K, nullptr);
 }
 
 int ll_mxfp4_dequant(void* out, const uint8_t* packed, const uint8_t* scales, int K, int R, int64_t scale_stride,
@@ -310,7 +361,7 @@ int ll_mxfp4_gemm(float* y, const float* x, const uint8_t* packed, const uint8_t
   if (ws_bytes < ll_mxfp4_workspace_bytes(M, K, R)) return LL_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   DropInWs w;
-  dropin_layout(ws, M, K, &w);
+  dropin_layout(ws, M, K > R ? K : R, R, K, &w);
   g_launch_count = 0;
   LL_TRY(reset_status(w.st, s));
   k_single_expert_chunks<<<1, 128, 0, s>>>(w.chunks, w.n_chunks, M, kDropInNmax);
@@ -318,7 +369,7 @@ int ll_mxfp4_gemm(float* y, const float* x, const uint8_t* packed, const uint8_t
   LL_TRY(launch_prepare_beta(scales, nullptr, 1, R, K, scale_stride, w.beta, 0, s));
   LL_TRY(launch_rows_to_half(x, 0, nullptr, M, K, w.act, w.inv, s));
   CUtensorMap pk, sc, act;
-  LL_TRY(make_weight_maps(&pk, &sc, packed, scales, R, K, scale_stride, false));
+  LL_TRY(make_rowscale_maps(&pk, &sc, packed, scales, R, K, scale_stride));
   LL_TRY(make_act_map(&act, w.act, M, K));
   GemmArgs a{};
   a.chunks = w.chunks;
@@ -339,28 +390,30 @@ int ll_mxfp4_gemm(float* y, const float* x, const uint8_t* packed, const uint8_t
 
 int ll_mxfp4_gemm_t(float* y, const float* dy, const uint8_t* packed, const uint8_t* scales, int M, int K, int R,
                     int64_t scale_stride, void* ws, size_t ws_bytes, void* stream) {
-  if (M <= 0 || K <= 0 || R <= 0 || K % 32 || R % 8 || scale_stride < K / 32 || scale_stride % 16) return LL_ERR_ARG;
+  if (M <= 0 || K <= 0 || R <= 0 || K % 32 || R % 32 || scale_stride < K / 32 || scale_stride % 16) return LL_ERR_ARG;
   if (!y || !dy || !packed || !scales || !ws) return LL_ERR_ARG;
   LL_TRY(check_arch());
   if (ws_bytes < ll_mxfp4_workspace_bytes(M, K, R)) return LL_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   DropInWs w;
-  dropin_layout(ws, M, R, &w);
+  dropin_layout(ws, M, K > R ? K : R, R, K, &w);
   g_launch_count = 0;
   LL_TRY(reset_status(w.st, s));
   k_single_expert_chunks<<<1, 128, 0, s>>>(w.chunks, w.n_chunks, M, kDropInNmax);
   LL_TRY(check_launch("k_single_expert_chunks"));
   LL_TRY(launch_prepare_beta(scales, nullptr, 1, R, K, scale_stride, w.beta, 0, s));
   LL_TRY(launch_rows_to_half(dy, 0, nullptr, M, R, w.act, w.inv, s));
+  // the backward orientation reads a transposed copy: codes [K][R/2], fp16 multipliers [K/32][R]
+  LL_TRY(launch_transpose_mxfp4(packed, scales, scale_stride, 1, R, K, w.beta, 0, w.codes_t, w.scales_t, s));
   CUtensorMap pk, sc, act;
-  LL_TRY(make_weight_maps(&pk, &sc, packed, scales, R, K, scale_stride, true));
+  LL_TRY(make_colscale_maps(&pk, &sc, w.codes_t, w.scales_t, K, R));
   LL_TRY(make_act_map(&act, w.act, M, R));
   GemmArgs a{};
   a.chunks = w.chunks;
   a.n_chunks = w.n_chunks;
   a.mtiles = (K + 127) / 128;
   a.K = R;
-  a.e_rows = R;
+  a.e_rows = K;
   a.status = w.st;
   a.epi.row_scale_inv = w.inv;
   a.epi.beta = w.beta;

@@ -63,8 +63,8 @@ class MXFP4Kernel:
         assert packed.shape[0] == R and scales.shape == (R, K // 32)
         packed = packed.contiguous()
         sc, stride = _pad_scales(scales)
-        if R % 8:
-            pad = (R + 7) // 8 * 8
+        if R % 32:
+            pad = (R + 31) // 32 * 32
             dy = torch.nn.functional.pad(dy, (0, pad - R))
             packed = torch.nn.functional.pad(packed, (0, 0, 0, pad - R))
             sc = torch.nn.functional.pad(sc, (0, 0, 0, pad - R))

@@ -52,6 +52,14 @@ class RoutedExpertsLayer:
         self.A_u, self.B_u = A_u.float().contiguous(), B_u.float().contiguous()
         self.A_d, self.B_d = A_d.float().contiguous(), B_d.float().contiguous()
         self.beta = torch.zeros((E, 2), dtype=torch.int32, device=w1p.device)
+        # transposed copies the backward GEMMs read (built once by ll_moe_prepare)
+        dev = w1p.device
+        self.w1t = torch.empty((E, d, f // 2), dtype=torch.uint8, device=dev)
+        self.w3t = torch.empty((E, d, f // 2), dtype=torch.uint8, device=dev)
+        self.w2t = torch.empty((E, f, d // 2), dtype=torch.uint8, device=dev)
+        self.s1t = torch.empty((E, d // 32, f), dtype=torch.float16, device=dev)
+        self.s3t = torch.empty((E, d // 32, f), dtype=torch.float16, device=dev)
+        self.s2t = torch.empty((E, f // 32, d), dtype=torch.float16, device=dev)
         self.desc = L.MoELayerDesc()
         self._fill_desc()
         L.check(self.lib.ll_moe_prepare(ctypes.byref(self.desc), self.beta.data_ptr(), L.stream_ptr()), "ll_moe_prepare")
@@ -74,6 +82,8 @@ class RoutedExpertsLayer:
         D.beta = self.beta.data_ptr()
         D.A_g, D.B_g, D.A_u, D.B_u = self.A_g.data_ptr(), self.B_g.data_ptr(), self.A_u.data_ptr(), self.B_u.data_ptr()
         D.A_d, D.B_d = self.A_d.data_ptr(), self.B_d.data_ptr()
+        D.w1t, D.w3t, D.w2t = self.w1t.data_ptr(), self.w3t.data_ptr(), self.w2t.data_ptr()
+        D.s1t, D.s3t, D.s2t = self.s1t.data_ptr(), self.s3t.data_ptr(), self.s2t.data_ptr()
 
     def set_lora(self, A_g, B_g, A_u, B_u, A_d, B_d):
         """Point the layer at (updated) adapter tensors, e.g. after an optimizer step."""
