@@ -24,9 +24,13 @@
 // k) with the decode bias folded in, so the dequant thread multiplies each element pair by
 // its own pair of scales.
 //
-// Warp roles (15 warps): 0 packed/scale TMA, 1 activation TMA, 2 MMA issue + TMEM owner,
-// 3..10 dequant (two warps per TMEM lane quarter, one per 32-element half of a 64-K
-// sub-chunk), 11..14 epilogue.
+// Warp roles (24 warps): 0 packed/scale TMA, 1 activation TMA, 2 and 3 MMA issuers (warp 2
+// owns the TMEM allocation), 4..19 dequant (four warps per TMEM lane quarter, one per 32-K
+// segment of a 128-K stage), 20..23 epilogue. The two issuers accumulate into separate
+// accumulators (gate / up, W1 / W3, or even / odd K stages), so neither waits on the other
+// and the sums stay deterministic; the epilogue adds them where they are one product.
+// Per 128-K stage there is one "full" barrier (16 dequant warps + the activation TMA) and
+// one "empty" commit, which keeps the MMA issuers' synchronisation off the critical path.
 #pragma once
 #include "common.cuh"
 
@@ -86,40 +90,42 @@ struct GemmArgs {
   EpiParams epi;
 };
 
-template <int NMAT, int NB, int ND, bool COLSCALE, int N_MAX>
+
+template <int NMAT, int NB, bool COLSCALE, int N_MAX>
 struct GemmCfg {
-  static constexpr int kThreads = 15 * 32;
-  static constexpr int kDqWarp0 = 3, kDqWarps = 8;
-  static constexpr int kEpWarp0 = 11, kEpWarps = 4;
-  static constexpr int BK = 128;                          // K per packed stage
-  static constexpr int SUBS = 2;                          // 64-K A sub-chunks per stage
+  static constexpr int kThreads = 24 * 32;
+  static constexpr int kIssuerWarp0 = 2;
+  static constexpr int kDqWarp0 = 4, kDqWarps = 16;
+  static constexpr int kEpWarp0 = 20, kEpWarps = 4;
+  static constexpr int BK = 128;                          // K per stage
   static constexpr int PK_BYTES = 128 * 64;               // 128 rows x 64 packed bytes
   static constexpr int SC_BYTES = COLSCALE ? 4 * 128 * 2  // 4 row groups x 128 k x fp16
                                            : 128 * 16;    // 128 rows x 16 scale bytes
   static constexpr int P_STAGE = NMAT * (PK_BYTES + SC_BYTES);
-  static constexpr int B_SLOT = NB * N_MAX * 128;
-  // tensor memory: accumulators first, then the A stages (32 columns per matrix and stage)
-  static constexpr int S_A = NMAT == 2 ? 3 : 4;
-  static constexpr int A_COLS = S_A * NMAT * 32;
-  static constexpr int NACC = (2 * ND * N_MAX + A_COLS <= 512) ? 2 : 1;
-  static constexpr int A_BASE = NACC * ND * N_MAX;
-  static constexpr int TMEM_COLS0 = A_BASE + A_COLS;
+  static constexpr int B_HALF = N_MAX * 128;              // one 64-K half of one operand
+  static constexpr int B_SLOT = NB * 2 * B_HALF;
+  // tensor memory: two accumulators per buffer (one per issuer), then the A stages
+  static constexpr int ACC_COLS = 2 * N_MAX;
+  static constexpr int NACC = (2 * ACC_COLS + 2 * NMAT * 64 <= 512) ? 2 : 1;
+  static constexpr int A_BASE = NACC * ACC_COLS;
+  static constexpr int S_AB0 = (512 - A_BASE) / (NMAT * 64);
+  static constexpr int S_AB = S_AB0 > 6 ? 6 : S_AB0;
+  static_assert(S_AB >= 2, "tensor memory budget");
+  static constexpr int TMEM_COLS0 = A_BASE + S_AB * NMAT * 64;
   static constexpr int TMEM_COLS = TMEM_COLS0 <= 32 ? 32 : TMEM_COLS0 <= 64 ? 64 : TMEM_COLS0 <= 128 ? 128
                                    : TMEM_COLS0 <= 256 ? 256 : 512;
-  static_assert(TMEM_COLS0 <= 512, "tensor memory budget");
-  // shared memory: B ring and packed ring
+  // shared memory: activation ring (S_AB slots) and the deeper packed-weight ring
   static constexpr int AVAIL = 227 * 1024 - 2048;
-  static constexpr int S_B0 = (AVAIL * 2 / 5) / B_SLOT;
-  static constexpr int S_B = S_B0 < 3 ? 3 : (S_B0 > 8 ? 8 : S_B0);
-  static constexpr int S_P0 = (AVAIL - S_B * B_SLOT) / P_STAGE;
-  static constexpr int S_P = S_P0 < 2 ? 2 : (S_P0 > 12 ? 12 : S_P0);
+  static constexpr int S_P0 = (AVAIL - S_AB * B_SLOT) / P_STAGE;
+  static constexpr int S_P = S_P0 > 10 ? 10 : S_P0;
+  static_assert(S_P >= S_AB, "shared memory budget");
   static constexpr int OFF_B = 0;
-  static constexpr int OFF_P = OFF_B + S_B * B_SLOT;
+  static constexpr int OFF_P = OFF_B + S_AB * B_SLOT;
   static constexpr int OFF_BAR = OFF_P + S_P * P_STAGE;
-  static constexpr int N_BARS = 2 * S_P + 2 * S_A + 2 * S_B + 4 + 1;
+  static constexpr int N_BARS = 2 * S_P + 2 * S_AB + 4 + 1;
   static constexpr int SMEM = OFF_BAR + N_BARS * 8 + 64 + 1024;  // + alignment slack
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
-  static_assert(N_MAX % 16 == 0 && N_MAX <= 256, "N_MAX");
+  static_assert(N_MAX % 16 == 0 && N_MAX <= 128, "N_MAX");
 };
 
 template <int NMAT, int NB>
@@ -129,20 +135,18 @@ struct TmaSet {
   CUtensorMap act[NB];
 };
 
-template <int EPI, int NMAT, int NB, int ND, bool COLSCALE, int N_MAX>
-__global__ void __launch_bounds__(15 * 32, 1)
+template <int EPI, int NMAT, int NB, bool COLSCALE, int N_MAX>
+__global__ void __launch_bounds__(24 * 32, 1)
 grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs args) {
-  using C = GemmCfg<NMAT, NB, ND, COLSCALE, N_MAX>;
+  using C = GemmCfg<NMAT, NB, COLSCALE, N_MAX>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* pfull = bars;
   uint64_t* pempty = pfull + C::S_P;
-  uint64_t* afull = pempty + C::S_P;
-  uint64_t* aempty = afull + C::S_A;
-  uint64_t* bfull = aempty + C::S_A;
-  uint64_t* bempty = bfull + C::S_B;
-  uint64_t* accfull = bempty + C::S_B;
+  uint64_t* full = pempty + C::S_P;
+  uint64_t* empty = full + C::S_AB;
+  uint64_t* accfull = empty + C::S_AB;
   uint64_t* accempty = accfull + 2;
   uint64_t* drain = accempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -153,25 +157,25 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
   const int n_units = (*args.n_chunks) * args.mtiles;
   if ((int)blockIdx.x >= n_units) return;   // uniform over the CTA: nothing allocated yet
 
+  const int K = args.K;
+  const int n_stage = (K + C::BK - 1) / C::BK;
+  // with one weight matrix the two issuers take alternate stages; a 1-stage K leaves one idle
+  const bool two_acc_sum = NMAT == 1 ? n_stage > 1 : EPI != EPI_F1;
+
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::S_P; i++) { mbar_init(&pfull[i], 1); mbar_init(&pempty[i], C::kDqWarps); }
-    for (int i = 0; i < C::S_A; i++) { mbar_init(&afull[i], C::kDqWarps); mbar_init(&aempty[i], 1); }
-    for (int i = 0; i < C::S_B; i++) { mbar_init(&bfull[i], 1); mbar_init(&bempty[i], 1); }
-    for (int i = 0; i < 2; i++) { mbar_init(&accfull[i], 1); mbar_init(&accempty[i], C::kEpWarps); }
-    mbar_init(drain, 1);
+    for (int i = 0; i < C::S_AB; i++) { mbar_init(&full[i], C::kDqWarps + 1); mbar_init(&empty[i], NMAT == 2 ? 2 : 1); }
+    for (int i = 0; i < 2; i++) { mbar_init(&accfull[i], 2); mbar_init(&accempty[i], C::kEpWarps); }
+    mbar_init(drain, 2);
     *abort_flag = 0;
     fence_barrier_init();
     fence_async_smem();
   }
-  if (warp == 2) tmem_alloc(tmem_slot, C::TMEM_COLS);
+  if (warp == C::kIssuerWarp0) tmem_alloc(tmem_slot, C::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  const int K = args.K;
-  const int n_sub = (K + 63) / 64;
-  const int n_stage = (K + C::BK - 1) / C::BK;
   DevStatus* st = args.status;
 
   if (warp == 0) {
@@ -203,8 +207,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
           if (++s == C::S_P) { s = 0; ph ^= 1; }
         }
       }
-      // drain: wait for the bytes of the last issued stages to land before exiting
-      for (int i = 0; i < C::S_P && i < issued; i++) {
+      for (int i = 0; i < C::S_P && i < issued; i++) {   // drain: bytes of the last stages landed
         if (--s < 0) { s = C::S_P - 1; ph ^= 1; }
         mbar_wait(&pfull[s], ph, abort_flag, st, 11);
       }
@@ -220,27 +223,30 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const Chunk ch = args.chunks[u / args.mtiles];
         const int npad = (ch.n + 15) & ~15;
-        for (int sb = 0; sb < n_sub && ok; sb++) {
-          if (!(ok = mbar_wait(&bempty[s], ph ^ 1, abort_flag, st, 2))) break;
+        for (int ks = 0; ks < n_stage && ok; ks++) {
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1, abort_flag, st, 2))) break;
           uint8_t* slot = smem + C::OFF_B + s * C::B_SLOT;
-          mbar_arrive_expect_tx(&bfull[s], NB * npad * 128);
+          mbar_arrive_expect_tx(&full[s], NB * 2 * npad * 128);
           for (int b = 0; b < NB; b++)
-            for (int rb = 0; rb < npad; rb += 16)
-              tma_load_2d(slot + b * N_MAX * 128 + rb * 128, &tm.act[b], &bfull[s], sb * 64, ch.p0 + rb);
+            for (int h = 0; h < 2; h++)
+              for (int rb = 0; rb < npad; rb += 16)
+                tma_load_2d(slot + (b * 2 + h) * C::B_HALF + rb * 128, &tm.act[b], &full[s], ks * C::BK + h * 64,
+                            ch.p0 + rb);
           issued++;
-          if (++s == C::S_B) { s = 0; ph ^= 1; }
+          if (++s == C::S_AB) { s = 0; ph ^= 1; }
         }
       }
-      for (int i = 0; i < C::S_B && i < issued; i++) {
-        if (--s < 0) { s = C::S_B - 1; ph ^= 1; }
-        mbar_wait(&bfull[s], ph, abort_flag, st, 12);
+      for (int i = 0; i < C::S_AB && i < issued; i++) {
+        if (--s < 0) { s = C::S_AB - 1; ph ^= 1; }
+        mbar_wait(&full[s], ph, abort_flag, st, 12);
       }
     }
-  } else if (warp == 2) {
-    // ------------------------------------------------------------------ MMA issuer
+  } else if (warp < C::kDqWarp0) {
+    // ---------------------------------------------------------------- MMA issuers
+    const int issuer = warp - C::kIssuerWarp0;   // 0 or 1
     if (lane == 0) {
-      int as = 0, bs = 0, ab = 0;
-      uint32_t aph = 0, bph = 0, abph = 0;
+      int s = 0, ab = 0;
+      uint32_t ph = 0, abph = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const Chunk ch = args.chunks[u / args.mtiles];
@@ -248,28 +254,24 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
         const uint32_t idesc = idesc_f16_m128(npad, false, false);
         if (!(ok = mbar_wait(&accempty[ab], abph ^ 1, abort_flag, st, 3))) break;
         tc_fence_after();
-        const uint32_t d0 = tmem + ab * ND * N_MAX;
-        for (int sb = 0; sb < n_sub && ok; sb++) {
-          if (!(ok = mbar_wait(&afull[as], aph, abort_flag, st, 4))) break;
-          if (!(ok = mbar_wait(&bfull[bs], bph, abort_flag, st, 5))) break;
-          tc_fence_after();
-          const uint32_t b_base = smem_u32(smem + C::OFF_B + bs * C::B_SLOT);
+        const uint32_t d = tmem + (ab * 2 + issuer) * N_MAX;
+        bool first = true;
+        for (int ks = 0; ks < n_stage && ok; ks++) {
+          const bool mine = NMAT == 2 || (ks & 1) == issuer;
+          if (mine) {
+            if (!(ok = mbar_wait(&full[s], ph, abort_flag, st, 4))) break;
+            tc_fence_after();
+            const uint32_t a_tmem = tmem + C::A_BASE + (s * NMAT + (NMAT == 2 ? issuer : 0)) * 64;
+            const uint32_t b_addr = smem_u32(smem + C::OFF_B + s * C::B_SLOT) + (NB == 2 ? issuer : 0) * 2 * C::B_HALF;
 #pragma unroll
-          for (int i = 0; i < NMAT; i++) {
-            const uint32_t d = d0 + (ND == 2 ? i : 0) * N_MAX;
-            const uint32_t a_tmem = tmem + C::A_BASE + (as * NMAT + i) * 32;
-            const uint32_t b_addr = b_base + (NB == 2 ? i : 0) * N_MAX * 128;
-#pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-              const uint64_t bdesc = umma_desc(b_addr + kk * 32, 16, 1024, kSwizzle128B);
-              const uint32_t acc = (sb > 0 || kk > 0 || (ND == 1 && i > 0)) ? 1u : 0u;
-              mma_f16_ts(d, a_tmem + kk * 8, bdesc, idesc, acc);
+            for (int kk = 0; kk < 8; kk++) {
+              const uint64_t bdesc = umma_desc(b_addr + (kk >> 2) * C::B_HALF + (kk & 3) * 32, 16, 1024, kSwizzle128B);
+              mma_f16_ts(d, a_tmem + kk * 8, bdesc, idesc, first ? 0u : 1u);
+              first = false;
             }
+            mma_commit(&empty[s]);
           }
-          mma_commit(&aempty[as]);
-          mma_commit(&bempty[bs]);
-          if (++as == C::S_A) { as = 0; aph ^= 1; }
-          if (++bs == C::S_B) { bs = 0; bph ^= 1; }
+          if (++s == C::S_AB) { s = 0; ph ^= 1; }
         }
         mma_commit(&accfull[ab]);
         if (++ab == C::NACC) { ab = 0; abph ^= 1; }
@@ -279,10 +281,10 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
     }
   } else if (warp < C::kEpWarp0) {
     // ---------------------------------------------------------------- dequant warps
-    // warp -> (TMEM lane quarter q, 32-element half h of each 64-K sub-chunk); thread -> row
-    const int dw = warp - C::kDqWarp0;           // 0..7
+    // warp -> (TMEM lane quarter q, 32-element K segment seg of each 128-K stage); thread -> row
+    const int dw = warp - C::kDqWarp0;           // 0..15
     const int q = warp & 3;
-    const int h = dw >> 2;
+    const int seg = dw >> 2;                     // 0..3 = 16-byte chunk of the 64-byte packed row
     const int m = q * 32 + lane;                 // weight row within the 128-row tile
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const int32_t* beta = args.epi.beta;
@@ -296,48 +298,45 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
       for (int ks = 0; ks < n_stage && ok; ks++) {
         if (!(ok = mbar_wait(&pfull[ps], pph, abort_flag, st, 6))) break;
         const uint8_t* stage = smem + C::OFF_P + ps * C::P_STAGE;
-        for (int sub = 0; sub < C::SUBS; sub++) {
-          if (ks * C::SUBS + sub >= n_sub) break;
-          if (!(ok = mbar_wait(&aempty[as], aph ^ 1, abort_flag, st, 7))) break;
-          tc_fence_after();
-          const int c = sub * 2 + h;                   // 16-byte chunk (32 K) in the 64-byte row
+        uint32_t o[NMAT][16];
 #pragma unroll
-          for (int i = 0; i < NMAT; i++) {
-            const uint8_t* pk = stage + i * (C::PK_BYTES + C::SC_BYTES);
-            const uint8_t* sc = pk + C::PK_BYTES;
-            const uint4 raw = ld_shared_v4(smem_u32(pk + m * 64 + ((c ^ ((m >> 1) & 3)) << 4)));
-            uint32_t o[16];
-            if (COLSCALE) {
-              // fp16 multipliers of k = 32c .. 32c+31 for this warp's 32-row group q
-              const uint32_t sa = smem_u32(sc + (q * 128 + c * 32) * 2);
-              const uint4 s0 = ld_shared_v4(sa), s1 = ld_shared_v4(sa + 16);
-              const uint4 s2 = ld_shared_v4(sa + 32), s3 = ld_shared_v4(sa + 48);
-              const uint32_t sv[16] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w,
-                                       s2.x, s2.y, s2.z, s2.w, s3.x, s3.y, s3.z, s3.w};
-              decode8v(raw.x, &sv[0], &o[0]);
-              decode8v(raw.y, &sv[4], &o[4]);
-              decode8v(raw.z, &sv[8], &o[8]);
-              decode8v(raw.w, &sv[12], &o[12]);
-            } else {
-              const uint32_t sbyte = sc[m * 16 + (((ks * C::BK) / 32) & 15) + c];
-              const uint32_t s1 = e8m0_to_half_bits(sbyte, bias);
-              const uint32_t s2 = s1 | (s1 << 16);
-              decode8(raw.x, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[0]));
-              decode8(raw.y, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[4]));
-              decode8(raw.z, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[8]));
-              decode8(raw.w, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[12]));
-            }
-            tmem_st16(tmem + lane_base + C::A_BASE + (as * NMAT + i) * 32 + h * 16, o);
+        for (int i = 0; i < NMAT; i++) {
+          const uint8_t* pk = stage + i * (C::PK_BYTES + C::SC_BYTES);
+          const uint8_t* sc = pk + C::PK_BYTES;
+          const uint4 raw = ld_shared_v4(smem_u32(pk + m * 64 + ((seg ^ ((m >> 1) & 3)) << 4)));
+          if (COLSCALE) {
+            // fp16 multipliers of k = 32 seg .. 32 seg + 31 for this warp's 32-row group q
+            const uint32_t sa = smem_u32(sc + (q * 128 + seg * 32) * 2);
+            const uint4 s0 = ld_shared_v4(sa), s1 = ld_shared_v4(sa + 16);
+            const uint4 s2 = ld_shared_v4(sa + 32), s3 = ld_shared_v4(sa + 48);
+            const uint32_t sv[16] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w,
+                                     s2.x, s2.y, s2.z, s2.w, s3.x, s3.y, s3.z, s3.w};
+            decode8v(raw.x, &sv[0], &o[i][0]);
+            decode8v(raw.y, &sv[4], &o[i][4]);
+            decode8v(raw.z, &sv[8], &o[i][8]);
+            decode8v(raw.w, &sv[12], &o[i][12]);
+          } else {
+            const uint32_t sbyte = sc[m * 16 + (((ks * C::BK) / 32) & 15) + seg];
+            const uint32_t s1 = e8m0_to_half_bits(sbyte, bias);
+            const uint32_t s2 = s1 | (s1 << 16);
+            decode8(raw.x, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[i][0]));
+            decode8(raw.y, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[i][4]));
+            decode8(raw.z, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[i][8]));
+            decode8(raw.w, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[i][12]));
           }
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&afull[as]);
-          if (++as == C::S_A) { as = 0; aph ^= 1; }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&pempty[ps]);
+        if (lane == 0) mbar_arrive(&pempty[ps]);      // packed bytes consumed (in registers now)
         if (++ps == C::S_P) { ps = 0; pph ^= 1; }
+        if (!(ok = mbar_wait(&empty[as], aph ^ 1, abort_flag, st, 7))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int i = 0; i < NMAT; i++) tmem_st16(tmem + lane_base + C::A_BASE + (as * NMAT + i) * 64 + seg * 16, o[i]);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[as]);
+        if (++as == C::S_AB) { as = 0; aph ^= 1; }
       }
     }
   } else {
@@ -358,17 +357,16 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
       const float wunscale = exp2f((float)(-bias));
       if (!(ok = mbar_wait(&accfull[ab], abph, abort_flag, st, 8))) break;
       tc_fence_after();
-      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * ND * N_MAX;
-      float ad[32];
-      if (EPI == EPI_B1) {
-#pragma unroll
-        for (int rr = 0; rr < 32; rr++) ad[rr] = (rr < ep.r && mvalid) ? ep.A_d[rr * ep.M + m] : 0.f;
-      }
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * 2 * N_MAX;
       for (int j0 = 0; j0 < npad; j0 += 16) {
         float v0[16], v1[16];
         tmem_ld16(tbase + j0, v0);
-        if (ND == 2) tmem_ld16(tbase + N_MAX + j0, v1);
+        tmem_ld16(tbase + N_MAX + j0, v1);
         tmem_ld_wait();
+        if (EPI != EPI_F1) {
+#pragma unroll
+          for (int jj = 0; jj < 16; jj++) v0[jj] = two_acc_sum ? v0[jj] + v1[jj] : v0[jj];
+        }
         float gwp[16];
 #pragma unroll
         for (int jj = 0; jj < 16; jj++) {
@@ -390,9 +388,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
           } else if (EPI == EPI_B1) {
             const float ys = v0[jj] * ep.row_scale_inv[p] * wunscale;
             float lorad = 0.f;
-#pragma unroll
-            for (int rr = 0; rr < 32; rr++)
-              if (rr < ep.r) lorad += ep.gB[(size_t)t * ep.r + rr] * ad[rr];
+            for (int rr = 0; rr < ep.r; rr++) lorad += ep.gB[(size_t)t * ep.r + rr] * ep.A_d[(size_t)rr * ep.M + m];
             const float v = ys + ep.lora_scaling * lorad;
             const float g = ep.Gs[o], uu = ep.Us[o];
             gwp[jj] = situ_glu_fwd(g, uu) * v;
@@ -433,7 +429,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 2) tmem_dealloc(tmem, C::TMEM_COLS);
+  if (warp == C::kIssuerWarp0) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
 }  // namespace ll

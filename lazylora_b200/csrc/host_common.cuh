@@ -83,14 +83,14 @@ inline int make_act_map(CUtensorMap* m, const __half* base, int64_t rows, int K)
 
 int set_smem_attr(const void* func, int bytes);
 
-template <int EPI, int NMAT, int NB, int ND, bool COLSCALE, int N_MAX>
+template <int EPI, int NMAT, int NB, bool COLSCALE, int N_MAX>
 int launch_gemm(const CUtensorMap* pk, const CUtensorMap* sc, const CUtensorMap* act, const GemmArgs& a,
                 cudaStream_t stream) {
-  using Cfg = GemmCfg<NMAT, NB, ND, COLSCALE, N_MAX>;
+  using Cfg = GemmCfg<NMAT, NB, COLSCALE, N_MAX>;
   TmaSet<NMAT, NB> tm;
   for (int i = 0; i < NMAT; i++) { tm.pk[i] = pk[i]; tm.sc[i] = sc[i]; }
   for (int i = 0; i < NB; i++) tm.act[i] = act[i];
-  auto kern = grouped_mxfp4_gemm<EPI, NMAT, NB, ND, COLSCALE, N_MAX>;
+  auto kern = grouped_mxfp4_gemm<EPI, NMAT, NB, COLSCALE, N_MAX>;
   LL_TRY(set_smem_attr(reinterpret_cast<const void*>(kern), Cfg::SMEM));
   const DeviceInfo di = device_info();
   const bool prof = g_prof_events && g_prof_i + 2 <= g_prof_n;

@@ -490,11 +490,11 @@ static int validate(const ll_moe_layer* L, int T, int k) {
   return LL_OK;
 }
 
-template <int EPI, int NMAT, int NB, int ND, bool COLSCALE>
+template <int EPI, int NMAT, int NB, bool COLSCALE>
 static int gemm_nmax(int nmax, const CUtensorMap* pk, const CUtensorMap* sc, const CUtensorMap* act, const GemmArgs& a,
                      cudaStream_t s) {
-  if (nmax == 32) return launch_gemm<EPI, NMAT, NB, ND, COLSCALE, 32>(pk, sc, act, a, s);
-  return launch_gemm<EPI, NMAT, NB, ND, COLSCALE, 128>(pk, sc, act, a, s);
+  if (nmax == 32) return launch_gemm<EPI, NMAT, NB, COLSCALE, 32>(pk, sc, act, a, s);
+  return launch_gemm<EPI, NMAT, NB, COLSCALE, 128>(pk, sc, act, a, s);
 }
 
 template <int QK, bool PG>
@@ -602,7 +602,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
     a.epi.G = W.G;
     a.epi.U = W.U;
     a.epi.H = W.H;
-    LL_TRY((gemm_nmax<EPI_F1, 2, 1, 2, false>(W.nmax, pk, sc, act, a, s)));
+    LL_TRY((gemm_nmax<EPI_F1, 2, 1, false>(W.nmax, pk, sc, act, a, s)));
   }
   const int* n_valid = W.offsets + E;
   k_z<<<P, 256, 0, s>>>(W.G, W.U, L->A_d, f, r, n_valid, W.z);
@@ -631,7 +631,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
     a.epi.P = P;
     a.epi.M = d;
     a.epi.Y = W.Y;
-    LL_TRY((gemm_nmax<EPI_F2, 1, 1, 1, false>(W.nmax, pk, sc, act, a, s)));
+    LL_TRY((gemm_nmax<EPI_F2, 1, 1, false>(W.nmax, pk, sc, act, a, s)));
   }
   k_combine<true><<<dim3((d + 255) / 256, T), 256, 0, s>>>(W.tok_pos, W.Y, k, d, r, L->lora_scaling, W.q, L->B_d,
                                                           nullptr, nullptr, out);
@@ -690,7 +690,7 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
     a.epi.DG = W.DG;
     a.epi.DU = W.DU;
     a.epi.gw_part = W.gw_part;
-    LL_TRY((gemm_nmax<EPI_B1, 1, 1, 1, true>(W.nmax, pk, sc, act, a, s)));
+    LL_TRY((gemm_nmax<EPI_B1, 1, 1, true>(W.nmax, pk, sc, act, a, s)));
   }
   k_pair_rows_half<<<P, 256, 0, s>>>(W.DG, W.DU, f, n_valid, W.DGh, W.DUh, W.rinv);
   LL_TRY(check_launch("k_pair_rows_half"));
@@ -715,7 +715,7 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
     a.epi.P = P;
     a.epi.M = d;
     a.epi.Y = W.Y;
-    LL_TRY((gemm_nmax<EPI_B2, 2, 2, 1, true>(W.nmax, pk, sc, act, a, s)));
+    LL_TRY((gemm_nmax<EPI_B2, 2, 2, true>(W.nmax, pk, sc, act, a, s)));
   }
   k_token_sum<<<dim3((f + 255) / 256, T), 256, 0, s>>>(W.tok_pos, W.DG, W.DU, T, k, f, W.Dg, W.Du);
   LL_TRY(check_launch("k_token_sum"));

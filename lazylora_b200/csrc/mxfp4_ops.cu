@@ -384,7 +384,7 @@ int ll_mxfp4_gemm(float* y, const float* x, const uint8_t* packed, const uint8_t
   a.epi.P = M;
   a.epi.M = R;
   a.epi.Y = y;
-  LL_TRY((launch_gemm<EPI_STORE, 1, 1, 1, false, kDropInNmax>(&pk, &sc, &act, a, s)));
+  LL_TRY((launch_gemm<EPI_STORE, 1, 1, false, kDropInNmax>(&pk, &sc, &act, a, s)));
   return read_status(w.st, s);
 }
 
@@ -421,7 +421,7 @@ int ll_mxfp4_gemm_t(float* y, const float* dy, const uint8_t* packed, const uint
   a.epi.P = M;
   a.epi.M = K;
   a.epi.Y = y;
-  LL_TRY((launch_gemm<EPI_ACCUM, 1, 1, 1, true, kDropInNmax>(&pk, &sc, &act, a, s)));
+  LL_TRY((launch_gemm<EPI_ACCUM, 1, 1, true, kDropInNmax>(&pk, &sc, &act, a, s)));
   return read_status(w.st, s);
 }
 
