@@ -24,6 +24,7 @@
 
 #include "host_common.cuh"
 #include "ops.cuh"
+#include "lora_aux.cuh"
 
 namespace ll {
 
@@ -132,96 +133,6 @@ __global__ void k_scatter(const int64_t* __restrict__ idx, const float* __restri
   }
 }
 
-// ----------------------------------------------------------------- LoRA helpers
-// out{0,1}[t][rr] = sum_k X[t][k] * W{0,1}(rr, k); W(rr,k) = W[rr*K + k] (ROWS) or W[k*r + rr].
-template <int XD, bool ROWS>
-__global__ void k_rowdot(const void* __restrict__ X, int K, int r, const float* __restrict__ W0, const float* __restrict__ W1,
-                         float* __restrict__ out0, float* __restrict__ out1) {
-  const int t = blockIdx.x;
-  float a0[32], a1[32];
-#pragma unroll
-  for (int i = 0; i < 32; i++) { a0[i] = 0.f; a1[i] = 0.f; }
-  for (int k = threadIdx.x; k < K; k += blockDim.x) {
-    const float xv = XD == 0 ? reinterpret_cast<const float*>(X)[(int64_t)t * K + k]
-                             : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(X)[(int64_t)t * K + k]);
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-      if (i < r) {
-        a0[i] = fmaf(xv, ROWS ? W0[(int64_t)i * K + k] : W0[(int64_t)k * r + i], a0[i]);
-        if (W1) a1[i] = fmaf(xv, ROWS ? W1[(int64_t)i * K + k] : W1[(int64_t)k * r + i], a1[i]);
-      }
-    }
-  }
-  __shared__ float red[2][8][32];
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-#pragma unroll
-  for (int i = 0; i < 32; i++) {
-    if (i >= r) break;
-    float s0 = a0[i], s1 = a1[i];
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      s0 += __shfl_xor_sync(0xffffffffu, s0, off);
-      s1 += __shfl_xor_sync(0xffffffffu, s1, off);
-    }
-    if (lane == 0) { red[0][warp][i] = s0; red[1][warp][i] = s1; }
-  }
-  __syncthreads();
-  if (threadIdx.x < r) {
-    float s0 = 0.f, s1 = 0.f;
-    for (int wi = 0; wi < (int)(blockDim.x / 32); wi++) { s0 += red[0][wi][threadIdx.x]; s1 += red[1][wi][threadIdx.x]; }
-    out0[(int64_t)t * r + threadIdx.x] = s0;
-    if (out1) out1[(int64_t)t * r + threadIdx.x] = s1;
-  }
-}
-
-// delta{g,u}[t][m] = s * sum_rr xa{g,u}[t][rr] * B{g,u}[m][rr]
-__global__ void k_lora_delta(const float* __restrict__ xa_g, const float* __restrict__ xa_u, const float* __restrict__ B_g,
-                             const float* __restrict__ B_u, int T, int f, int r, float s, float* __restrict__ dg,
-                             float* __restrict__ du) {
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= (int64_t)T * f) return;
-  const int t = (int)(i / f), m = (int)(i % f);
-  float ag = 0.f, au = 0.f;
-  for (int rr = 0; rr < r; rr++) {
-    ag = fmaf(xa_g[(int64_t)t * r + rr], B_g[(int64_t)m * r + rr], ag);
-    au = fmaf(xa_u[(int64_t)t * r + rr], B_u[(int64_t)m * r + rr], au);
-  }
-  dg[i] = s * ag;
-  du[i] = s * au;
-}
-
-// z[p][rr] = sum_m situ(G[p][m], U[p][m]) * A_d[rr][m] for the valid pairs p < offsets[E]
-__global__ void k_z(const float* __restrict__ G, const float* __restrict__ U, const float* __restrict__ A_d, int f, int r,
-                    const int* __restrict__ n_valid, float* __restrict__ z) {
-  const int p = blockIdx.x;
-  if (p >= *n_valid) return;
-  float a[32];
-#pragma unroll
-  for (int i = 0; i < 32; i++) a[i] = 0.f;
-  for (int m = threadIdx.x; m < f; m += blockDim.x) {
-    const float h = situ_glu_fwd(G[(int64_t)p * f + m], U[(int64_t)p * f + m]);
-#pragma unroll
-    for (int i = 0; i < 32; i++)
-      if (i < r) a[i] = fmaf(h, A_d[(int64_t)i * f + m], a[i]);
-  }
-  __shared__ float red[8][32];
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-#pragma unroll
-  for (int i = 0; i < 32; i++) {
-    if (i >= r) break;
-    float s0 = a[i];
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s0 += __shfl_xor_sync(0xffffffffu, s0, off);
-    if (lane == 0) red[warp][i] = s0;
-  }
-  __syncthreads();
-  if (threadIdx.x < r) {
-    float s0 = 0.f;
-    for (int wi = 0; wi < (int)(blockDim.x / 32); wi++) s0 += red[wi][threadIdx.x];
-    z[(int64_t)p * r + threadIdx.x] = s0;
-  }
-}
-
 // q[t][rr] = sum over the token's pairs (ascending expert) of tw * z
 __global__ void k_q(const int* __restrict__ tok_pos, const float* __restrict__ tw, const float* __restrict__ z, int T, int k,
                     int r, float* __restrict__ q) {
@@ -235,37 +146,6 @@ __global__ void k_q(const int* __restrict__ tok_pos, const float* __restrict__ t
     acc = fmaf(tw[pos], z[(int64_t)pos * r + rr], acc);
   }
   q[i] = acc;
-}
-
-// out[t][c] = sum_j Y[pos_j][c] (ascending expert) + s * sum_rr L0[t][rr] * R0(rr, c) (+ L1 R1)
-// R(rr, c) = R[c*r + rr] (COLS, B_d [d][r]) or R[rr*C + c] (A [r][C]).
-template <bool COLS>
-__global__ void k_combine(const int* __restrict__ tok_pos, const float* __restrict__ Y, int k, int C, int r, float s,
-                          const float* __restrict__ L0, const float* __restrict__ R0, const float* __restrict__ L1,
-                          const float* __restrict__ R1, float* __restrict__ out) {
-  const int t = blockIdx.y;
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  __shared__ int pos[32];
-  __shared__ float l0[32], l1[32];
-  if (threadIdx.x < 32) {
-    pos[threadIdx.x] = threadIdx.x < k ? tok_pos[(int64_t)t * k + threadIdx.x] : -1;
-    l0[threadIdx.x] = threadIdx.x < r ? L0[(int64_t)t * r + threadIdx.x] : 0.f;
-    l1[threadIdx.x] = (L1 && threadIdx.x < r) ? L1[(int64_t)t * r + threadIdx.x] : 0.f;
-  }
-  __syncthreads();
-  if (c >= C) return;
-  float acc = 0.f;
-  for (int j = 0; j < k; j++) {
-    const int p = pos[j];
-    if (p < 0) break;
-    acc += Y[(int64_t)p * C + c];
-  }
-  float lo = 0.f;
-  for (int rr = 0; rr < r; rr++) {
-    lo = fmaf(l0[rr], COLS ? R0[(int64_t)c * r + rr] : R0[(int64_t)rr * C + c], lo);
-    if (L1) lo = fmaf(l1[rr], COLS ? R1[(int64_t)c * r + rr] : R1[(int64_t)rr * C + c], lo);
-  }
-  out[(int64_t)t * C + c] = acc + s * lo;
 }
 
 // Per valid pair: one power-of-two scale for both rows of dg / du, fp16 copies for B2.
@@ -324,51 +204,6 @@ __global__ void k_grad_w(const int* __restrict__ pair_pos, const float* __restri
   grad_w[q] = s;
 }
 
-// Outer-product reductions for the LoRA gradients:
-//   part[seg][rr][c] = sum_{n in seg} Pm(n, rr) * Q(n, c)
-// Pm: [N][r] fp32, or (PGATHER) tw[n] * gB[perm_token[n]][rr].
-// Q:  QK 0 fp32 [N][C], 1 bf16 [N][C], 2 situ(G, U) from two fp32 [N][C].
-template <int QK, bool PGATHER>
-__global__ void k_outer(const float* __restrict__ Pm, const int* __restrict__ perm_token, const float* __restrict__ tw,
-                        const void* __restrict__ Q, const float* __restrict__ Q2, int N, const int* __restrict__ n_dev,
-                        int C, int r, int nseg, float* __restrict__ part) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  const int seg = blockIdx.y;
-  const int n_total = n_dev ? *n_dev : N;
-  const int per = (n_total + nseg - 1) / nseg;
-  const int n0 = seg * per, n1 = min(n_total, n0 + per);
-  __shared__ float ps[32][33];
-  float acc[32];
-#pragma unroll
-  for (int i = 0; i < 32; i++) acc[i] = 0.f;
-  for (int nb = n0; nb < n1; nb += 32) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < 32 * r; i += blockDim.x) {
-      const int nn = i / r, rr = i % r;
-      const int n = nb + nn;
-      float v = 0.f;
-      if (n < n1) v = PGATHER ? tw[n] * Pm[(int64_t)perm_token[n] * r + rr] : Pm[(int64_t)n * r + rr];
-      ps[nn][rr] = v;
-    }
-    __syncthreads();
-    if (c < C) {
-      const int lim = min(32, n1 - nb);
-      for (int nn = 0; nn < lim; nn++) {
-        const int64_t o = (int64_t)(nb + nn) * C + c;
-        float qv;
-        if (QK == 0) qv = reinterpret_cast<const float*>(Q)[o];
-        else if (QK == 1) qv = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(Q)[o]);
-        else qv = situ_glu_fwd(reinterpret_cast<const float*>(Q)[o], Q2[o]);
-#pragma unroll
-        for (int i = 0; i < 32; i++)
-          if (i < r) acc[i] = fmaf(ps[nn][i], qv, acc[i]);
-      }
-    }
-  }
-  if (c < C)
-    for (int i = 0; i < r; i++) part[((int64_t)seg * r + i) * C + c] = acc[i];
-}
-
 // out = s * sum_seg part, stored [r][C] or transposed [C][r]
 __global__ void k_outer_reduce(const float* __restrict__ part, int nseg, int r, int C, float s, bool transposed,
                                float* __restrict__ out) {
@@ -420,6 +255,7 @@ struct LayerWs {
   float* hg;
   float* hu;
   float* opart;
+  float* skpart;
   int nmax;
   int nseg_max;
 };
@@ -475,6 +311,10 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   w.hg = c.take<float>((size_t)T * r);
   w.hu = c.take<float>((size_t)T * r);
   w.opart = c.take<float>((size_t)nseg_max * r * (d > f ? d : f));
+  {  // split-K partials of the skinny products: at most ~2 * SMs / mblocks splits of >= 64
+    const int64_t rows = P > T ? P : T;
+    w.skpart = c.take<float>((size_t)(2 * 160 + 64) * 64 * 64 + (size_t)rows * 2 * r * 8);
+  }
   if (out) *out = w;
   return c.off + 256;
 }
@@ -497,18 +337,66 @@ static int gemm_nmax(int nmax, const CUtensorMap* pk, const CUtensorMap* sc, con
   return launch_gemm<EPI, NMAT, NB, COLSCALE, 128>(pk, sc, act, a, s);
 }
 
-template <int QK, bool PG>
-static int outer(const float* Pm, const int* perm_token, const float* tw, const void* Q, const float* Q2, int N,
-                 const int* n_dev, int C, int r, float s, bool transposed, float* part, int nseg_max, float* out,
-                 cudaStream_t st) {
+// C0 (and C1) = alpha * A[M][K] . B, with B given as rows ([N][K], split over B0 / B1 at N0)
+// or columns ([K][N]); split-K partials in `part`, summed in a fixed order.
+static int skinny(const void* A, int adt, bool brows, int M, int K, const float* B0, const float* B1, int N0, int N,
+                  float alpha, float* C0, float* C1, float* part, cudaStream_t s) {
+  const int mblocks = (M + kSkBM - 1) / kSkBM;
+  int nsplit = (2 * device_info().sms + mblocks - 1) / mblocks;
+  nsplit = std::max(1, std::min(nsplit, (K + kSkBK - 1) / kSkBK));
+  const int kc = ((K + nsplit - 1) / nsplit + kSkBK - 1) / kSkBK * kSkBK;
+  nsplit = (K + kc - 1) / kc;
+  dim3 grid(mblocks, 1, nsplit);
+#define LL_SK(ADT, BR) k_skinny<ADT, BR><<<grid, 256, 0, s>>>(A, M, K, K, B0, B1, N0, N, kc, part)
+  if (brows) {
+    if (adt == 0) LL_SK(0, true); else if (adt == 1) LL_SK(1, true); else LL_SK(2, true);
+  } else {
+    if (adt == 0) LL_SK(0, false); else if (adt == 1) LL_SK(1, false); else LL_SK(2, false);
+  }
+#undef LL_SK
+  LL_TRY(check_launch("k_skinny"));
+  const int64_t n = (int64_t)M * N;
+  k_skinny_reduce<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, nsplit, M, N, N0, alpha, C0, C1);
+  return check_launch("k_skinny_reduce");
+}
+
+// Rank-r expand with the optional ascending-expert sum of per-pair rows (see k_expand).
+static int expand(bool rrows, const int* tok_pos, const float* Y, int k, int T, int C, int r, float alpha,
+                  const float* L0, const float* R0, const float* L1, const float* R1, float* out, cudaStream_t s) {
+  dim3 grid((C + kExCols - 1) / kExCols, (T + kExTok - 1) / kExTok);
+  const bool hasy = Y != nullptr, two = L1 != nullptr;
+#define LL_EX(RR, HY, TW) k_expand<RR, HY, TW><<<grid, kExCols, 0, s>>>(tok_pos, Y, k, T, C, r, alpha, L0, R0, L1, R1, out)
+  if (rrows) {
+    if (hasy) { if (two) LL_EX(true, true, true); else LL_EX(true, true, false); }
+    else { if (two) LL_EX(true, false, true); else LL_EX(true, false, false); }
+  } else {
+    if (hasy) { if (two) LL_EX(false, true, true); else LL_EX(false, true, false); }
+    else { if (two) LL_EX(false, false, true); else LL_EX(false, false, false); }
+  }
+#undef LL_EX
+  return check_launch("k_expand");
+}
+
+// out = s * sum_n Pm(n, :)^T Q[n][:], stored [r][C] or transposed [C][r]
+static int outer(const float* Pm, const int* perm_token, const float* tw, const void* Q, int qdt, int N,
+                 const int* n_dev, int C, int r, float sc, bool transposed, float* part, int nseg_max, float* out,
+                 cudaStream_t s) {
   const int cblocks = (C + 255) / 256;
   int nseg = (2 * device_info().sms + cblocks - 1) / cblocks;
   nseg = std::max(1, std::min(nseg, nseg_max));
-  nseg = std::min(nseg, std::max(1, N / 32));
-  k_outer<QK, PG><<<dim3(cblocks, nseg), 256, 0, st>>>(Pm, perm_token, tw, Q, Q2, N, n_dev, C, r, nseg, part);
-  LL_TRY(check_launch("k_outer"));
+  nseg = std::min(nseg, std::max(1, N / 16));
+  dim3 grid(cblocks, nseg);
+  const bool pg = perm_token != nullptr;
+#define LL_OU(QD, PG) k_outer4<QD, PG><<<grid, 64, 0, s>>>(Pm, perm_token, tw, Q, N, n_dev, C, r, nseg, part)
+  if (pg) {
+    if (qdt == 0) LL_OU(0, true); else if (qdt == 1) LL_OU(1, true); else LL_OU(2, true);
+  } else {
+    if (qdt == 0) LL_OU(0, false); else if (qdt == 1) LL_OU(1, false); else LL_OU(2, false);
+  }
+#undef LL_OU
+  LL_TRY(check_launch("k_outer4"));
   const int64_t n = (int64_t)r * C;
-  k_outer_reduce<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, nseg, r, C, s, transposed, out);
+  k_outer_reduce<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, nseg, r, C, sc, transposed, out);
   return check_launch("k_outer_reduce");
 }
 
@@ -567,17 +455,9 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
                                                             W.pair_pos, W.tw, W.tok_pos);
   LL_TRY(check_launch("k_scatter"));
   LL_TRY(launch_rows_to_half(x, x_dtype, W.perm_token, P, d, W.xh, W.xinv, s));
-  if (x_dtype == 0)
-    k_rowdot<0, true><<<T, 256, 0, s>>>(x, d, r, L->A_g, L->A_u, W.xa_g, W.xa_u);
-  else
-    k_rowdot<1, true><<<T, 256, 0, s>>>(x, d, r, L->A_g, L->A_u, W.xa_g, W.xa_u);
-  LL_TRY(check_launch("k_rowdot"));
-  {
-    const int64_t n = (int64_t)T * f;
-    k_lora_delta<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(W.xa_g, W.xa_u, L->B_g, L->B_u, T, f, r, L->lora_scaling,
-                                                             W.dlt_g, W.dlt_u);
-    LL_TRY(check_launch("k_lora_delta"));
-  }
+  LL_TRY(skinny(x, x_dtype, true, T, d, L->A_g, L->A_u, r, 2 * r, 1.f, W.xa_g, W.xa_u, W.skpart, s));
+  LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_g, L->B_g, nullptr, nullptr, W.dlt_g, s));
+  LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_u, L->B_u, nullptr, nullptr, W.dlt_u, s));
   // F1: gate / up
   {
     CUtensorMap pk[2], sc[2], act[1];
@@ -605,8 +485,8 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
     LL_TRY((gemm_nmax<EPI_F1, 2, 1, false>(W.nmax, pk, sc, act, a, s)));
   }
   const int* n_valid = W.offsets + E;
-  k_z<<<P, 256, 0, s>>>(W.G, W.U, L->A_d, f, r, n_valid, W.z);
-  LL_TRY(check_launch("k_z"));
+  // z = h . A_d^T per pair (h as the fp16 rows the down GEMM reads)
+  LL_TRY(skinny(W.H, 2, true, P, f, L->A_d, nullptr, r, r, 1.f, W.z, nullptr, W.skpart, s));
   {
     const int64_t n = (int64_t)T * r;
     k_q<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(W.tok_pos, W.tw, W.z, T, k, r, W.q);
@@ -633,9 +513,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
     a.epi.Y = W.Y;
     LL_TRY((gemm_nmax<EPI_F2, 1, 1, false>(W.nmax, pk, sc, act, a, s)));
   }
-  k_combine<true><<<dim3((d + 255) / 256, T), 256, 0, s>>>(W.tok_pos, W.Y, k, d, r, L->lora_scaling, W.q, L->B_d,
-                                                          nullptr, nullptr, out);
-  return check_launch("k_combine");
+  return expand(false, W.tok_pos, W.Y, k, T, d, r, L->lora_scaling, W.q, L->B_d, nullptr, nullptr, out, s);
 }
 
 int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dtype, const int64_t* idx, const float* w,
@@ -657,11 +535,7 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
   g_launch_count = 0;
 
   LL_TRY(launch_rows_to_half(g, g_dtype, W.perm_token, P, d, W.gh, W.ginv, s));
-  if (g_dtype == 0)
-    k_rowdot<0, false><<<T, 256, 0, s>>>(g, d, r, L->B_d, nullptr, W.gB, nullptr);
-  else
-    k_rowdot<1, false><<<T, 256, 0, s>>>(g, d, r, L->B_d, nullptr, W.gB, nullptr);
-  LL_TRY(check_launch("k_rowdot"));
+  LL_TRY(skinny(g, g_dtype, false, T, d, L->B_d, nullptr, r, r, 1.f, W.gB, nullptr, W.skpart, s));
   // B1: v = g . W2 (+ LoRA down), SiTU-GLU backward
   {
     CUtensorMap pk[1], sc[1], act[1];
@@ -719,31 +593,18 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
   }
   k_token_sum<<<dim3((f + 255) / 256, T), 256, 0, s>>>(W.tok_pos, W.DG, W.DU, T, k, f, W.Dg, W.Du);
   LL_TRY(check_launch("k_token_sum"));
-  k_rowdot<0, false><<<T, 256, 0, s>>>(W.Dg, f, r, L->B_g, nullptr, W.hg, nullptr);
-  LL_TRY(check_launch("k_rowdot"));
-  k_rowdot<0, false><<<T, 256, 0, s>>>(W.Du, f, r, L->B_u, nullptr, W.hu, nullptr);
-  LL_TRY(check_launch("k_rowdot"));
-  k_combine<false><<<dim3((d + 255) / 256, T), 256, 0, s>>>(W.tok_pos, W.Y, k, d, r, sc_l, W.hg, L->A_g, W.hu, L->A_u,
-                                                           grad_h);
-  LL_TRY(check_launch("k_combine"));
+  LL_TRY(skinny(W.Dg, 0, false, T, f, L->B_g, nullptr, r, r, 1.f, W.hg, nullptr, W.skpart, s));
+  LL_TRY(skinny(W.Du, 0, false, T, f, L->B_u, nullptr, r, r, 1.f, W.hu, nullptr, W.skpart, s));
+  LL_TRY(expand(true, W.tok_pos, W.Y, k, T, d, r, sc_l, W.hg, L->A_g, W.hu, L->A_u, grad_h, s));
   k_grad_w<<<(P + 255) / 256, 256, 0, s>>>(W.pair_pos, W.gw_part, (f / 128) * 4, P, P, grad_w);
   LL_TRY(check_launch("k_grad_w"));
   // LoRA gradients
-  if (x_dtype == 0)
-    LL_TRY((outer<0, false>(W.hg, nullptr, nullptr, x, nullptr, T, nullptr, d, r, sc_l, false, W.opart, W.nseg_max, dA_g, s)));
-  else
-    LL_TRY((outer<1, false>(W.hg, nullptr, nullptr, x, nullptr, T, nullptr, d, r, sc_l, false, W.opart, W.nseg_max, dA_g, s)));
-  LL_TRY((outer<0, false>(W.xa_g, nullptr, nullptr, W.Dg, nullptr, T, nullptr, f, r, sc_l, true, W.opart, W.nseg_max, dB_g, s)));
-  if (x_dtype == 0)
-    LL_TRY((outer<0, false>(W.hu, nullptr, nullptr, x, nullptr, T, nullptr, d, r, sc_l, false, W.opart, W.nseg_max, dA_u, s)));
-  else
-    LL_TRY((outer<1, false>(W.hu, nullptr, nullptr, x, nullptr, T, nullptr, d, r, sc_l, false, W.opart, W.nseg_max, dA_u, s)));
-  LL_TRY((outer<0, false>(W.xa_u, nullptr, nullptr, W.Du, nullptr, T, nullptr, f, r, sc_l, true, W.opart, W.nseg_max, dB_u, s)));
-  LL_TRY((outer<2, true>(W.gB, W.perm_token, W.tw, W.G, W.U, P, n_valid, f, r, sc_l, false, W.opart, W.nseg_max, dA_d, s)));
-  if (g_dtype == 0)
-    LL_TRY((outer<0, false>(W.q, nullptr, nullptr, g, nullptr, T, nullptr, d, r, sc_l, true, W.opart, W.nseg_max, dB_d, s)));
-  else
-    LL_TRY((outer<1, false>(W.q, nullptr, nullptr, g, nullptr, T, nullptr, d, r, sc_l, true, W.opart, W.nseg_max, dB_d, s)));
+  LL_TRY(outer(W.hg, nullptr, nullptr, x, x_dtype, T, nullptr, d, r, sc_l, false, W.opart, W.nseg_max, dA_g, s));
+  LL_TRY(outer(W.xa_g, nullptr, nullptr, W.Dg, 0, T, nullptr, f, r, sc_l, true, W.opart, W.nseg_max, dB_g, s));
+  LL_TRY(outer(W.hu, nullptr, nullptr, x, x_dtype, T, nullptr, d, r, sc_l, false, W.opart, W.nseg_max, dA_u, s));
+  LL_TRY(outer(W.xa_u, nullptr, nullptr, W.Du, 0, T, nullptr, f, r, sc_l, true, W.opart, W.nseg_max, dB_u, s));
+  LL_TRY(outer(W.gB, W.perm_token, W.tw, W.H, 2, P, n_valid, f, r, sc_l, false, W.opart, W.nseg_max, dA_d, s));
+  LL_TRY(outer(W.q, nullptr, nullptr, g, g_dtype, T, nullptr, d, r, sc_l, true, W.opart, W.nseg_max, dB_d, s));
   return LL_OK;
 }
 
