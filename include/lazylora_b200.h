@@ -55,6 +55,18 @@ int ll_mxfp4_gemm(float* y, const float* x, const uint8_t* packed, const uint8_t
                   int M, int K, int R, int64_t scale_stride, void* ws, size_t ws_bytes,
                   void* stream);
 
+/* No counterpart in the reference. ll_mxfp4_gemm without a workspace argument, for callers
+ * that cannot allocate device memory (a binding that holds raw pointers and no device
+ * allocator, or code running where allocation is not allowed). Its scratch is a static
+ * device array of LL_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps until
+ * exit; M * K must fit it (about M * K * 2 + M * 4 bytes, 8 MiB: e.g. M <= 580 at K = 7168),
+ * larger sizes return LL_ERR_WORKSPACE. The first call on a device looks up the array's
+ * device address (make it before any stream capture). All calls share the array: calls
+ * that overlap on the GPU race and must be serialised by the caller. Allocates nothing. */
+#define LL_NOALLOC_SCRATCH_BYTES (8u << 20)
+int ll_mxfp4_gemm_noalloc(float* y, const float* x, const uint8_t* packed, const uint8_t* scales,
+                          int M, int K, int R, int64_t scale_stride, void* stream);
+
 /* Replaces mxfp4_gemm_t (lazy_lora/native/mxfp4_gemm.c:96-129): y[M,K] += dy[M,R] . W
  * (accumulates into y, as the reference does). */
 int ll_mxfp4_gemm_t(float* y, const float* dy, const uint8_t* packed, const uint8_t* scales,

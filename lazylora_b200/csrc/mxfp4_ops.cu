@@ -262,6 +262,11 @@ int launch_transpose_mxfp4(const uint8_t* packed, const uint8_t* scales, int64_t
   return check_launch("k_transpose_mxfp4");
 }
 
+int launch_single_expert_chunks(Chunk* chunks, int* n_chunks, int M, int nmax, cudaStream_t s) {
+  k_single_expert_chunks<<<1, 128, 0, s>>>(chunks, n_chunks, M, nmax);
+  return check_launch("k_single_expert_chunks");
+}
+
 int launch_rows_to_half(const void* src, int src_dtype, const int* index, int rows, int K, __half* dst, float* inv,
                         cudaStream_t s) {
   if (rows <= 0) return LL_OK;

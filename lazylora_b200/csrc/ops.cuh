@@ -14,6 +14,9 @@ int launch_prepare_beta(const uint8_t* s_a, const uint8_t* s_b, int E, int rows,
 int launch_transpose_mxfp4(const uint8_t* packed, const uint8_t* scales, int64_t sstride, int E, int R, int C,
                            const int32_t* beta, int col, uint8_t* codes_t, __half* scales_t, cudaStream_t s);
 
+// chunks[i] = {expert 0, rows i*nmax .. } covering M rows of a single matrix, and their count.
+int launch_single_expert_chunks(Chunk* chunks, int* n_chunks, int M, int nmax, cudaStream_t s);
+
 // dst[row] = fp16(src[index[row]] * 2^sigma_row), inv[row] = 2^-sigma_row (index may be null;
 // a negative index gives a zero row). src_dtype: 0 fp32, 1 bf16.
 int launch_rows_to_half(const void* src, int src_dtype, const int* index, int rows, int K, __half* dst, float* inv,
