@@ -29,10 +29,18 @@
 // segment of a 128-K stage), 20..23 epilogue. The two issuers accumulate into separate
 // accumulators (gate / up, W1 / W3, or even / odd K stages), so neither waits on the other
 // and the sums stay deterministic; the epilogue adds them where they are one product.
-// Per 128-K stage there is one "full" barrier (16 dequant warps + the activation TMA) and
-// one "empty" commit, which keeps the MMA issuers' synchronisation off the critical path.
+// Packed weights move in 128-K TMA stages; the tensor-memory A stages and the activation
+// slots move in ring stages of 128/LL_GEMM_SUBSTAGES K, each with one "full" barrier (the
+// dequant warps that fill it + the activation TMA) and one "empty" commit from the issuers.
 #pragma once
 #include "common.cuh"
+
+// A/B ring granularity: 1 = 128-K stages (default), 2 = 64-K stages (twice as many in-flight
+// stages in the same tensor memory, half the MMAs per barrier; measured 15-20% slower at
+// d=7168, f=2048, 9 tokens per expert).
+#ifndef LL_GEMM_SUBSTAGES
+#define LL_GEMM_SUBSTAGES 1
+#endif
 
 namespace ll {
 
@@ -97,28 +105,33 @@ struct GemmCfg {
   static constexpr int kIssuerWarp0 = 2;
   static constexpr int kDqWarp0 = 4, kDqWarps = 16;
   static constexpr int kEpWarp0 = 20, kEpWarps = 4;
-  static constexpr int BK = 128;                          // K per stage
+  static constexpr int BK = 128;                          // K per packed (TMA) stage
+  static constexpr int SUB = LL_GEMM_SUBSTAGES;           // A/B ring stages per packed stage
+  static constexpr int KS = BK / SUB;                     // K per A/B ring stage
+  static constexpr int SEGS = 4 / SUB;                    // 32-K dequant segments per A/B stage
+  static constexpr int kDqPerStage = kDqWarps / SUB;      // dequant warps that fill one A/B stage
   static constexpr int PK_BYTES = 128 * 64;               // 128 rows x 64 packed bytes
   static constexpr int SC_BYTES = COLSCALE ? 4 * 128 * 2  // 4 row groups x 128 k x fp16
                                            : 128 * 16;    // 128 rows x 16 scale bytes
   static constexpr int P_STAGE = NMAT * (PK_BYTES + SC_BYTES);
   static constexpr int B_HALF = N_MAX * 128;              // one 64-K half of one operand
-  static constexpr int B_SLOT = NB * 2 * B_HALF;
+  static constexpr int B_SLOT = NB * (KS / 64) * B_HALF;
   // tensor memory: two accumulators per buffer (one per issuer), then the A stages
   static constexpr int ACC_COLS = 2 * N_MAX;
-  static constexpr int NACC = (2 * ACC_COLS + 2 * NMAT * 64 <= 512) ? 2 : 1;
+  static constexpr int A_STAGE_COLS = NMAT * KS / 2;      // fp16 pairs: KS/2 columns per matrix
+  static constexpr int NACC = (2 * ACC_COLS + 2 * A_STAGE_COLS * SUB <= 512) ? 2 : 1;
   static constexpr int A_BASE = NACC * ACC_COLS;
-  static constexpr int S_AB0 = (512 - A_BASE) / (NMAT * 64);
-  static constexpr int S_AB = S_AB0 > 6 ? 6 : S_AB0;
+  static constexpr int S_AB0 = (512 - A_BASE) / A_STAGE_COLS;
+  static constexpr int S_AB = S_AB0 > 12 ? 12 : S_AB0;
   static_assert(S_AB >= 2, "tensor memory budget");
-  static constexpr int TMEM_COLS0 = A_BASE + S_AB * NMAT * 64;
+  static constexpr int TMEM_COLS0 = A_BASE + S_AB * A_STAGE_COLS;
   static constexpr int TMEM_COLS = TMEM_COLS0 <= 32 ? 32 : TMEM_COLS0 <= 64 ? 64 : TMEM_COLS0 <= 128 ? 128
                                    : TMEM_COLS0 <= 256 ? 256 : 512;
   // shared memory: activation ring (S_AB slots) and the deeper packed-weight ring
   static constexpr int AVAIL = 227 * 1024 - 2048;
   static constexpr int S_P0 = (AVAIL - S_AB * B_SLOT) / P_STAGE;
   static constexpr int S_P = S_P0 > 10 ? 10 : S_P0;
-  static_assert(S_P >= S_AB, "shared memory budget");
+  static_assert(S_P >= 2, "shared memory budget");
   static constexpr int OFF_B = 0;
   static constexpr int OFF_P = OFF_B + S_AB * B_SLOT;
   static constexpr int OFF_BAR = OFF_P + S_P * P_STAGE;
@@ -158,13 +171,14 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
   if ((int)blockIdx.x >= n_units) return;   // uniform over the CTA: nothing allocated yet
 
   const int K = args.K;
-  const int n_stage = (K + C::BK - 1) / C::BK;
+  const int n_stage = (K + C::BK - 1) / C::BK;   // packed (TMA) stages per unit
+  const int n_sub = (K + C::KS - 1) / C::KS;     // A/B ring stages per unit
   // with one weight matrix the two issuers take alternate stages; a 1-stage K leaves one idle
-  const bool two_acc_sum = NMAT == 1 ? n_stage > 1 : EPI != EPI_F1;
+  const bool two_acc_sum = NMAT == 1 ? n_sub > 1 : EPI != EPI_F1;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::S_P; i++) { mbar_init(&pfull[i], 1); mbar_init(&pempty[i], C::kDqWarps); }
-    for (int i = 0; i < C::S_AB; i++) { mbar_init(&full[i], C::kDqWarps + 1); mbar_init(&empty[i], NMAT == 2 ? 2 : 1); }
+    for (int i = 0; i < C::S_AB; i++) { mbar_init(&full[i], C::kDqPerStage + 1); mbar_init(&empty[i], NMAT == 2 ? 2 : 1); }
     for (int i = 0; i < 2; i++) { mbar_init(&accfull[i], 2); mbar_init(&accempty[i], C::kEpWarps); }
     mbar_init(drain, 2);
     *abort_flag = 0;
@@ -223,15 +237,15 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const Chunk ch = args.chunks[u / args.mtiles];
         const int npad = (ch.n + 15) & ~15;
-        for (int ks = 0; ks < n_stage && ok; ks++) {
+        for (int sb = 0; sb < n_sub && ok; sb++) {
           if (!(ok = mbar_wait(&empty[s], ph ^ 1, abort_flag, st, 2))) break;
           uint8_t* slot = smem + C::OFF_B + s * C::B_SLOT;
-          mbar_arrive_expect_tx(&full[s], NB * 2 * npad * 128);
+          mbar_arrive_expect_tx(&full[s], NB * (C::KS / 64) * npad * 128);
           for (int b = 0; b < NB; b++)
-            for (int h = 0; h < 2; h++)
+            for (int h = 0; h < C::KS / 64; h++)
               for (int rb = 0; rb < npad; rb += 16)
-                tma_load_2d(slot + (b * 2 + h) * C::B_HALF + rb * 128, &tm.act[b], &full[s], ks * C::BK + h * 64,
-                            ch.p0 + rb);
+                tma_load_2d(slot + (b * (C::KS / 64) + h) * C::B_HALF + rb * 128, &tm.act[b], &full[s],
+                            sb * C::KS + h * 64, ch.p0 + rb);
           issued++;
           if (++s == C::S_AB) { s = 0; ph ^= 1; }
         }
@@ -256,15 +270,16 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
         tc_fence_after();
         const uint32_t d = tmem + (ab * 2 + issuer) * N_MAX;
         bool first = true;
-        for (int ks = 0; ks < n_stage && ok; ks++) {
-          const bool mine = NMAT == 2 || (ks & 1) == issuer;
+        for (int sb = 0; sb < n_sub && ok; sb++) {
+          const bool mine = NMAT == 2 || (sb & 1) == issuer;
           if (mine) {
             if (!(ok = mbar_wait(&full[s], ph, abort_flag, st, 4))) break;
             tc_fence_after();
-            const uint32_t a_tmem = tmem + C::A_BASE + (s * NMAT + (NMAT == 2 ? issuer : 0)) * 64;
-            const uint32_t b_addr = smem_u32(smem + C::OFF_B + s * C::B_SLOT) + (NB == 2 ? issuer : 0) * 2 * C::B_HALF;
+            const uint32_t a_tmem = tmem + C::A_BASE + s * C::A_STAGE_COLS + (NMAT == 2 ? issuer : 0) * (C::KS / 2);
+            const uint32_t b_addr =
+                smem_u32(smem + C::OFF_B + s * C::B_SLOT) + (NB == 2 ? issuer : 0) * (C::KS / 64) * C::B_HALF;
 #pragma unroll
-            for (int kk = 0; kk < 8; kk++) {
+            for (int kk = 0; kk < C::KS / 16; kk++) {
               const uint64_t bdesc = umma_desc(b_addr + (kk >> 2) * C::B_HALF + (kk & 3) * 32, 16, 1024, kSwizzle128B);
               mma_f16_ts(d, a_tmem + kk * 8, bdesc, idesc, first ? 0u : 1u);
               first = false;
@@ -285,14 +300,17 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
     const int dw = warp - C::kDqWarp0;           // 0..15
     const int q = warp & 3;
     const int seg = dw >> 2;                     // 0..3 = 16-byte chunk of the 64-byte packed row
+    const int sub = seg / C::SEGS;               // A/B ring stage of this segment within the packed stage
+    const int hseg = seg % C::SEGS;              // segment within that ring stage
     const int m = q * 32 + lane;                 // weight row within the 128-row tile
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    int sub_base = 0;                            // ring stages of the units before this one
     const int32_t* beta = args.epi.beta;
     const int bcol = args.epi.beta_col;
-    int ps = 0, as = 0;
-    uint32_t pph = 0, aph = 0;
+    int ps = 0;
+    uint32_t pph = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, sub_base += n_sub) {
       const Chunk ch = args.chunks[u / args.mtiles];
       const int bias = (!COLSCALE && beta) ? beta[ch.e * 2 + bcol] : 0;
       for (int ks = 0; ks < n_stage && ok; ks++) {
@@ -328,15 +346,20 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
         __syncwarp();
         if (lane == 0) mbar_arrive(&pempty[ps]);      // packed bytes consumed (in registers now)
         if (++ps == C::S_P) { ps = 0; pph ^= 1; }
+        const int gs = ks * C::SUB + sub;          // ring stage of this segment within the unit
+        if (gs >= n_sub) continue;                 // K ends inside this packed stage
+        const int g = sub_base + gs;               // ring stage counted over this CTA's units
+        const int as = g % C::S_AB;
+        const uint32_t aph = (uint32_t)(g / C::S_AB) & 1u;
         if (!(ok = mbar_wait(&empty[as], aph ^ 1, abort_flag, st, 7))) break;
         tc_fence_after();
 #pragma unroll
-        for (int i = 0; i < NMAT; i++) tmem_st16(tmem + lane_base + C::A_BASE + (as * NMAT + i) * 64 + seg * 16, o[i]);
+        for (int i = 0; i < NMAT; i++)
+          tmem_st16(tmem + lane_base + C::A_BASE + as * C::A_STAGE_COLS + i * (C::KS / 2) + hseg * 16, o[i]);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&full[as]);
-        if (++as == C::S_AB) { as = 0; aph ^= 1; }
       }
     }
   } else {
