@@ -38,6 +38,15 @@ METRIC = "MoE-layer fwd+bwd tokens/s (d=7168, f=2048, E=896, top-8, LoRA r=16)"
 UNIT = "tokens/s"
 
 
+# DRAM bytes (read + write) per touched expert of each grouped-GEMM launch (F1, F2, B1, B2),
+# from one ncu capture of the same kernels at d=7168, f=2048, 64 experts, 9 tokens per expert.
+# Weight reads dominate, so a launch's traffic scales with the number of experts it touches.
+NCU_DRAM_BYTES_PER_EXPERT = {
+    (7168, 2048): [(1021.256e6 + 13.821184e6) / 64, (501.545e6 + 17.194752e6) / 64,
+                   (547.218e6 + 11.422208e6) / 64, (1061.840e6 + 18.673664e6) / 64],
+}
+
+
 def _peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -294,6 +303,7 @@ def run_ours(args, cfg, rank, local, world, dist):
     names = ["F1 gate/up (W1,W3 . x)", "F2 down (W2 . h)", "B1 (g . W2)", "B2 dX (dg . W1 + du . W3)"]
     per_kernel_bytes = [U * 2 * cfg.f * cfg.d * 17 // 32, U * cfg.f * cfg.d * 17 // 32,
                         U * cfg.f * cfg.d * 17 // 32, U * 2 * cfg.f * cfg.d * 17 // 32]
+    traffic_pe = NCU_DRAM_BYTES_PER_EXPERT.get((cfg.d, cfg.f))
     avg_ms = [statistics.mean(s[j] for s in gemm_ms) for j in range(4)]
     shares = [a / ms_step for a in avg_ms]
     dom = max(range(4), key=lambda j: avg_ms[j])
@@ -314,7 +324,10 @@ def run_ours(args, cfg, rank, local, world, dist):
         "hbm_roofline_ms": 2 * U * eb / (hbm_peak * 1e9) * 1e3,
         "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "peak_kind": peak_kind,
-                     "traffic": None,
+                     "traffic": None if traffic_pe is None else round(U * traffic_pe[dom]),
+                     "traffic_source": None if traffic_pe is None else
+                     "ncu dram__bytes_read.sum + dram__bytes_write.sum of the same kernel at d=7168, f=2048, "
+                     "64 experts x 9 tokens, per touched expert, times the experts this launch touches",
                      "algorithmic_bytes_per_launch": per_kernel_bytes[dom], "avg_launch_ms": avg_ms[dom]},
         "kernel_ms": {n: round(a, 4) for n, a in zip(names, avg_ms)},
         "kernel_share": {n: round(s, 4) for n, s in zip(names, shares)},
