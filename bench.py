@@ -207,8 +207,17 @@ def run_ours(args, cfg, rank, local, world, dist):
 
     dev = torch.device("cuda", local)
     lib = L.load()
-    inp = make_layer_device(cfg, device=dev)
-    layer = RoutedExpertsLayer.from_inputs(inp, cfg.scaling, device=dev)
+    ep = None
+    if world > 1:
+        # expert parallel: this rank's block of experts and its own cfg.T tokens
+        from lazylora_b200.synthetic import make_ep_rank_device
+        from lazylora_b200.trainer.expert_parallel import ExpertParallelLayer
+        inp = make_ep_rank_device(cfg, rank, world, device=dev)
+        layer = RoutedExpertsLayer.from_inputs(inp, cfg.scaling, device=dev)
+        ep = ExpertParallelLayer(layer, cfg.E)
+    else:
+        inp = make_layer_device(cfg, device=dev)
+        layer = RoutedExpertsLayer.from_inputs(inp, cfg.scaling, device=dev)
     router = KimiK3MoERouter(hidden_size=cfg.d, num_experts=cfg.E, top_k=cfg.k, device=dev)
     x = inp["x"].to(torch.bfloat16).contiguous()
     g = inp["g"].to(torch.bfloat16).contiguous()
@@ -220,19 +229,31 @@ def run_ours(args, cfg, rank, local, world, dist):
     def step(xx, gg):
         idx, w = router.forward(xx, weight=Wr, bias=br)
         n = 2                                   # router: logits + select
-        out = layer.forward(xx, idx, w)
-        n += lib.ll_last_launch_count()
-        gh, gw, grads = layer.backward(xx, idx, w, gg)
-        n += lib.ll_last_launch_count()
+        if ep is not None:
+            l0 = ep.ops.launches
+            out = ep.forward(xx, idx, w)
+            gh, gw, grads = ep.backward(gg)
+            n += ep.ops.launches - l0 + ep.local_launches
+        else:
+            out = layer.forward(xx, idx, w)
+            n += lib.ll_last_launch_count()
+            gh, gw, grads = layer.backward(xx, idx, w, gg)
+            n += lib.ll_last_launch_count()
         launches[0] += n
         return out, gh, gw, grads, idx, w
 
     # ---- warm-up + correctness status
     for _ in range(args.warmup):
         res = step(x, g)
-    layer.check_status(cfg.T, cfg.k)
+    if ep is not None:
+        if ep._ctx["R"]:
+            layer.check_status(ep._ctx["R"], cfg.k)
+        local_idx = ep._ctx["idx_recv"]
+        U = int(torch.unique(local_idx[local_idx >= 0]).numel())
+    else:
+        layer.check_status(cfg.T, cfg.k)
+        U = int(torch.unique(res[4]).numel())
     idx = res[4]
-    U = int(torch.unique(idx).numel())
     torch.cuda.synchronize()
 
     def barrier():
@@ -260,7 +281,10 @@ def run_ours(args, cfg, rank, local, world, dist):
         end.record(stream)
         barrier()
     lib.ll_profile_gemm_events(None, 0)
-    layer.check_status(cfg.T, cfg.k)
+    if ep is None:
+        layer.check_status(cfg.T, cfg.k)
+    elif ep._ctx["R"]:
+        layer.check_status(ep._ctx["R"], cfg.k)
     total_ms = start.elapsed_time(end)
     gemm_ms = [[gemm_events[i][2 * j].elapsed_time(gemm_events[i][2 * j + 1]) for j in range(4)]
                for i in range(args.steps)]
@@ -316,10 +340,14 @@ def run_ours(args, cfg, rank, local, world, dist):
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp16 operands / fp32 accumulate (MXFP4 weights decoded exactly)",
         "data": "synthetic",
-        "config": {"workload": "configs[1]: 896-expert MXFP4 MoE layer, route + fwd + full LoRA bwd",
-                   "d": cfg.d, "f": cfg.f, "E": cfg.E, "k": cfg.k, "T_per_gpu": cfg.T, "r": cfg.r,
-                   "active_experts": U, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": "weights 21 GB >> 126 MB L2: every step streams them from HBM"},
+        "config": {"workload": ("configs[1]: 896-expert MXFP4 MoE layer, route + fwd + full LoRA bwd" if world == 1
+                                else f"expert parallel over {world} GPUs ({cfg.E // world} experts each), "
+                                     f"{cfg.T} tokens per GPU ({cfg.T * world} total; configs[2] at 8 GPUs), "
+                                     f"route + NCCL all-to-all dispatch + fwd + full LoRA bwd + combine"),
+                   "d": cfg.d, "f": cfg.f, "E": cfg.E, "k": cfg.k, "T_per_gpu": cfg.T, "T_total": cfg.T * world,
+                   "r": cfg.r, "active_experts_rank0": U,
+                   "parallelism": f"ep{world}" if world > 1 else "single GPU",
+                   "l2": "weights >> 126 MB L2: every step streams them from HBM"},
         "weight_TBps": weight_tbs,
         "hbm_roofline_ms": 2 * U * eb / (hbm_peak * 1e9) * 1e3,
         "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
@@ -363,12 +391,13 @@ def main():
     rank, local, world, dist = dist_setup(args)
     try:
         if args.impl == "reference":
-            run_reference(args, cfg, rank, world, dist)
+            run_reference(args, cfg, rank, world, dist)   # rank 0 only; no collective
         else:
             run_ours(args, cfg, rank, local, world, dist)
+            if dist is not None:
+                dist.barrier()
     finally:
         if dist is not None:
-            dist.barrier()
             dist.destroy_process_group()
 
 

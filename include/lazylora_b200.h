@@ -169,6 +169,42 @@ int ll_moe_status(const ll_moe_layer* L, int T, int k, void* ws, void* stream);
 int ll_moe_permutation(const ll_moe_layer* L, int T, int k, void* ws, int* offsets,
                        int* perm_token, int* perm_slot, void* stream);
 
+/* ------------------------------------------------------------------ expert parallelism
+ * No counterpart in the reference, which runs the routed experts in one process
+ * (lazy_trainer.py:806-880 loops over every expert locally); these are the index kernels
+ * around the two all-to-all exchanges of an expert-parallel layer. Expert e lives on rank
+ * floor(e * n / E). Each rank routes its own T tokens and sends every token row once to each
+ * rank owning one of its experts; that rank runs ll_moe_forward / ll_moe_backward on the rows
+ * it received and returns per-row fp32 partials, which the origin rank adds in ascending
+ * rank order. The exchanges themselves (NCCL all-to-all) are the caller's.
+ */
+
+/* First expert id and expert count of `rank` (contiguous blocks). */
+int ll_ep_experts_of_rank(int E, int n_ranks, int rank, int* first, int* count);
+
+/* Send plan of this rank's tokens. idx int64 [T,k] global expert ids, w fp32 [T,k].
+ * counts int32 [n_ranks + 1]: rows for each destination rank, then the number of slots whose
+ * id is outside [0, E) (those slots are routed nowhere; callers treat nonzero as an error).
+ * pos int32 [T, n_ranks]: send-buffer row of token t for rank r, or -1.
+ * Send rows (at most T * n_ranks) are grouped by destination rank ascending, tokens
+ * ascending: send_tok int32 [rows] source token, send_idx int64 [rows, k] expert id local to
+ * the destination rank or -1 where that slot's expert is elsewhere, send_w fp32 [rows, k]
+ * (0 where send_idx is -1). Deterministic (no order-dependent atomics in the outputs). */
+int ll_ep_plan(int T, int k, int E, int n_ranks, const int64_t* idx, const float* w, int* counts, int* pos,
+               int* send_tok, int64_t* send_idx, float* send_w, void* stream);
+
+/* dst[i, :] = src[tok[i], :] for i < rows; row_bytes a multiple of 16, 16-byte aligned buffers. */
+int ll_ep_gather_rows(void* dst, const void* src, const int* tok, int rows, int64_t row_bytes, void* stream);
+
+/* out[t, :] = sum over r = 0..n_ranks-1 (ascending) of part[pos[t, r], :] where pos >= 0;
+ * fp32 rows of width d (a multiple of 4); part holds the returned partials in send order. */
+int ll_ep_combine(float* out, const float* part, const int* pos, int T, int n_ranks, int d, void* stream);
+
+/* grad_w[t, j] = part[pos[t, owner(idx[t, j])], j] (fp32 [rows, k] partials in send order);
+ * 0 for a slot whose id is outside [0, E). */
+int ll_ep_combine_slots(float* grad_w, const float* part, const int* pos, const int64_t* idx, int T, int k, int E,
+                        int n_ranks, void* stream);
+
 /* Profiling hook: record events[2i] / events[2i+1] (cudaEvent_t handles) on the launching
  * stream around the i-th grouped-GEMM launch that follows on this thread, for the first n/2
  * launches; n = 0 turns it off. Calling it again restarts at i = 0. */

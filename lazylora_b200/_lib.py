@@ -72,6 +72,12 @@ _SIGS = {
     "ll_moe_status": (c_int, [ctypes.POINTER(MoELayerDesc), c_int, c_int, c_void_p, c_void_p]),
     "ll_moe_permutation": (c_int, [ctypes.POINTER(MoELayerDesc), c_int, c_int, c_void_p, c_void_p, c_void_p,
                                    c_void_p, c_void_p]),
+    "ll_ep_experts_of_rank": (c_int, [c_int, c_int, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+    "ll_ep_plan": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                           c_void_p, c_void_p]),
+    "ll_ep_gather_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int64, c_void_p]),
+    "ll_ep_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "ll_ep_combine_slots": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
     "ll_profile_gemm_events": (c_int, [ctypes.POINTER(c_void_p), c_int]),
 }
 

@@ -158,5 +158,51 @@ def make_layer_device(cfg: LayerConfig, device="cuda", with_grad: bool = True) -
     return out
 
 
+def make_ep_rank_device(cfg: LayerConfig, rank: int, world: int, device="cuda",
+                        with_grad: bool = True) -> Dict[str, torch.Tensor]:
+    """One rank's inputs for an expert-parallel layer of `world` ranks, drawn on `device`.
+
+    Replicated on every rank (stream seeded `cfg.seed`): the router weight and bias and the
+    three LoRA adapters. Rank-local (stream seeded `cfg.seed + 1 + rank`): the MXFP4 weights
+    of the rank's experts (the contiguous block of expert e = floor(e * world / E)) and its
+    cfg.T tokens x and upstream gradient g. Same distributions as make_layer.
+    """
+    d, f, E, r = cfg.d, cfg.f, cfg.E, cfg.r
+    lo = (rank * E + world - 1) // world
+    n_loc = ((rank + 1) * E + world - 1) // world - lo
+    dev = torch.device(device)
+    gs = torch.Generator(device=device).manual_seed(cfg.seed)
+    gl = torch.Generator(device=device).manual_seed(cfg.seed + 1 + rank)
+    out: Dict[str, torch.Tensor] = {"first_expert": torch.tensor(lo), "n_local": torch.tensor(n_loc)}
+    out["router_w"] = torch.randn(E, d, generator=gs, device=dev) * 0.02
+    out["router_b"] = torch.zeros(E, device=dev)
+    if cfg.zipf_s is not None:
+        gc = torch.Generator(device="cpu").manual_seed(cfg.seed + 1)
+        out["router_b"] = zipf_bias(E, cfg.zipf_s, gamma=0.05, gen=gc).to(dev)
+    out["A_g"] = torch.randn(r, d, generator=gs, device=dev) / math.sqrt(d)
+    out["B_g"] = torch.randn(f, r, generator=gs, device=dev) * 0.01
+    out["A_u"] = torch.randn(r, d, generator=gs, device=dev) / math.sqrt(d)
+    out["B_u"] = torch.randn(f, r, generator=gs, device=dev) * 0.01
+    out["A_d"] = torch.randn(r, f, generator=gs, device=dev) / math.sqrt(f)
+    out["B_d"] = torch.randn(d, r, generator=gs, device=dev) * 0.01
+
+    def packed(rows, cols):
+        return torch.randint(0, 256, (n_loc, rows, cols // 2), dtype=torch.uint8, generator=gl, device=dev)
+
+    def scales(rows, cols):
+        return (torch.randint(-10, -5, (n_loc, rows, cols // 32), generator=gl, device=dev,
+                              dtype=torch.int32) + 127).to(torch.uint8)
+
+    out["w1p"], out["w1s"] = packed(f, d), scales(f, d)
+    out["w3p"], out["w3s"] = packed(f, d), scales(f, d)
+    out["w2p"], out["w2s"] = packed(d, f), scales(d, f)
+    x = torch.randn(cfg.T, d, generator=gl, device=dev)
+    out["x"] = x if cfg.x_dtype == "f32" else _round_bf16(x)
+    if with_grad:
+        gr = torch.randn(cfg.T, d, generator=gl, device=dev)
+        out["g"] = gr if cfg.x_dtype == "f32" else _round_bf16(gr)
+    return out
+
+
 def with_config(name: str, **kw) -> LayerConfig:
     return replace(CONFIGS[name], **kw)

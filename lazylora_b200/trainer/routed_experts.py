@@ -92,6 +92,15 @@ class RoutedExpertsLayer:
         self.A_d, self.B_d = A_d.detach().float().contiguous(), B_d.detach().float().contiguous()
         self._fill_desc()
 
+    def last_launch_count(self) -> int:
+        """Kernels the last forward or backward call on this thread launched."""
+        return int(self.lib.ll_last_launch_count())
+
+    def lora_shapes(self) -> Dict[str, tuple]:
+        """Shapes of the six LoRA gradients backward returns."""
+        d, f, r = self.d, self.f, self.r
+        return {"dA_g": (r, d), "dB_g": (f, r), "dA_u": (r, d), "dB_u": (f, r), "dA_d": (r, f), "dB_d": (d, r)}
+
     def workspace(self, T: int, k: int) -> torch.Tensor:
         n = self.lib.ll_moe_workspace_bytes(ctypes.byref(self.desc), T, k)
         if self._ws is None or self._ws.numel() < n:
