@@ -375,6 +375,80 @@ def run_ours(args, cfg, rank, local, world, dist):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------- decode
+def run_decode(args, cfg, rank, local, world, dist):
+    """Forward-only decode steps (router + routed experts) at T in {1, 4, 16} with Zipf-skewed
+    routing. The HBM bound is the MXFP4 bytes of the U experts the step touches; L2 is flushed
+    (a 256 MB write) before every timed step, so those bytes come from HBM. Each step is timed
+    by its own CUDA events; --graph replays the step as one CUDA graph."""
+    from lazylora_b200 import _lib as L
+    from lazylora_b200.core.moe_router import KimiK3MoERouter
+    from lazylora_b200.synthetic import make_layer_device
+    from lazylora_b200.trainer.routed_experts import RoutedExpertsLayer
+    dev = torch.device("cuda", local)
+    lib = L.load()
+    inp = make_layer_device(cfg, device=dev, with_grad=False)
+    layer = RoutedExpertsLayer.from_inputs(inp, cfg.scaling, device=dev)
+    router = KimiK3MoERouter(hidden_size=cfg.d, num_experts=cfg.E, top_k=cfg.k, device=dev)
+    x = inp["x"].to(torch.bfloat16).contiguous()
+    Wr, br = inp["router_w"], inp["router_b"]
+    del inp["w1p"], inp["w3p"], inp["w2p"]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    state = {}
+
+    def step():
+        idx, w = router.forward(x, weight=Wr, bias=br)
+        state["idx"] = idx
+        state["out"] = layer.forward(x, idx, w)
+        state["n"] = 2 + lib.ll_last_launch_count()
+
+    for _ in range(args.warmup):
+        step()
+    layer.check_status(cfg.T, cfg.k)
+    run = step
+    if args.graph:
+        gr = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            step()                                  # allocations happen outside the capture
+            with torch.cuda.graph(gr, stream=side):
+                step()
+        stream.wait_stream(side)
+        run = gr.replay
+    torch.cuda.synchronize()
+    times, us = [], []
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            flush.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            run()
+            b.record(stream)
+            times.append((a, b))
+        torch.cuda.synchronize()
+    layer.check_status(cfg.T, cfg.k)
+    us = sorted(a.elapsed_time(b) * 1e3 for a, b in times)
+    med = statistics.median(us)
+    U = int(torch.unique(state["idx"]).numel())
+    wbytes = U * expert_bytes(cfg)
+    hbm_peak, _, peak_kind = _peaks()
+    gbs = wbytes / (med * 1e-6) / 1e9
+    line = {"metric": f"decode forward weight GB/s (T={cfg.T}, Zipf s={cfg.zipf_s} routing)", "value": gbs,
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "us_per_step": med,
+            "us_min": us[0], "higher_is_better": True, "dtype": "fp16 operands / fp32 accumulate", "data": "synthetic",
+            "config": {"workload": f"configs[3]: decode T={cfg.T}, router + routed experts forward",
+                       "d": cfg.d, "f": cfg.f, "E": cfg.E, "k": cfg.k, "T": cfg.T, "r": cfg.r,
+                       "zipf_s": cfg.zipf_s, "zipf_gamma": cfg.zipf_gamma, "active_experts": U,
+                       "graph": bool(args.graph), "l2": "256 MB written before every timed step"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                         "peak_kind": peak_kind, "algorithmic_bytes_per_step": wbytes,
+                         "roofline_us": wbytes / (hbm_peak * 1e9) * 1e6},
+            "gpu_launches": state["n"] * args.steps, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -384,14 +458,22 @@ def main():
     ap.add_argument("--config", default="c1")
     ap.add_argument("--ref-experts", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--decode", action="store_true", help="forward-only decode steps (configs[3]: c3_t1/4/16)")
+    ap.add_argument("--graph", action="store_true", help="with --decode: replay each step as a CUDA graph")
+    ap.add_argument("--zipf-gamma", type=float, default=None, help="override the config's Zipf bias scale")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    from dataclasses import replace
     from lazylora_b200.synthetic import CONFIGS
     cfg = CONFIGS[args.config]
+    if args.zipf_gamma is not None:
+        cfg = replace(cfg, zipf_gamma=args.zipf_gamma)
     rank, local, world, dist = dist_setup(args)
     try:
         if args.impl == "reference":
             run_reference(args, cfg, rank, world, dist)   # rank 0 only; no collective
+        elif args.decode:
+            run_decode(args, cfg, rank, local, world, dist)
         else:
             run_ours(args, cfg, rank, local, world, dist)
             if dist is not None:

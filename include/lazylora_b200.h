@@ -85,8 +85,11 @@ int ll_mxfp4_dequant(void* out, const uint8_t* packed, const uint8_t* scales, in
  * descending order (ties: lower expert id first), weights gathered from the unbiased
  * scores, renormalised by (sum + 1e-20) when renormalize != 0 and k > 1, times scale.
  * x_dtype: 0 = fp32, 1 = bf16. idx is int64 [T,k] like torch.topk's indices.
+ * The logits run on the tensor cores with Wr split exactly into three bf16 planes (and fp32
+ * x likewise), accumulating in fp32: fp32-level accuracy, another summation order than the
+ * reference's F.linear. d must be a multiple of 8, x 16-byte aligned, ws 256-byte aligned.
  */
-size_t ll_route_workspace_bytes(int T, int E);
+size_t ll_route_workspace_bytes(int T, int d, int E);
 int ll_route_topk(const void* x, int x_dtype, const float* router_w, const float* bias,
                   int T, int d, int E, int k, int renormalize, float routed_scaling_factor,
                   int64_t* idx, float* w, float* scores_out /* optional [T,E] */,

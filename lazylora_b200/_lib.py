@@ -56,7 +56,7 @@ _SIGS = {
     "ll_mxfp4_gemm_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64,
                                       c_void_p]),
     "ll_mxfp4_dequant": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int64, c_int, c_void_p]),
-    "ll_route_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "ll_route_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "ll_route_topk": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float,
                               c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "ll_route_select": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_void_p, c_void_p,

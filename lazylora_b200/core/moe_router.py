@@ -43,7 +43,7 @@ class KimiK3MoERouter(torch.nn.Module):
         w = weight.detach().to(torch.float32).contiguous()
         b = None if bias is None else bias.detach().to(torch.float32).contiguous()
         T, E, k = xf.shape[0], self.num_experts, self.top_k
-        nbytes = lib.ll_route_workspace_bytes(T, E)
+        nbytes = lib.ll_route_workspace_bytes(T, self.hidden_size, E)
         if self._ws is None or self._ws.numel() < nbytes or self._ws.device != xf.device:
             self._ws = torch.empty(nbytes, dtype=torch.uint8, device=xf.device)
         idx = torch.empty((T, k), dtype=torch.int64, device=xf.device)

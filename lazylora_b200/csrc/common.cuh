@@ -89,6 +89,35 @@ LL_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, 
   }
 }
 
+// Bounded wait for a warp off the critical path (a producer that is ahead, an issuer, an
+// epilogue waiting for the next tile): polls with a __nanosleep back-off that doubles from
+// 32 ns up to ns_max, so the waiting warp stops taking issue slots from the warps that work.
+LL_DEV bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort_flag, DevStatus* st, int where,
+                            uint32_t ns_max) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  uint32_t ns = 32;
+  while (true) {
+    __nanosleep(ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      *abort_flag = 1;
+      report(st, LL_ERR_TIMEOUT, where, 0);
+      return false;
+    }
+    ns = ns < ns_max ? ns * 2 : ns_max;
+  }
+}
+
+// Named barriers (bar.sync / bar.arrive): warp-granular, all 32 lanes of a warp execute them.
+LL_DEV void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+LL_DEV void named_bar_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // --------------------------------------------------------------------------------- TMA
 LL_DEV void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -264,10 +293,6 @@ LL_DEV uint4 ld_shared_v4(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
-}
-
-LL_DEV void named_bar_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // -------------------------------------------------------------------------- SiTU-GLU

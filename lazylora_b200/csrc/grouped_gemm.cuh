@@ -24,23 +24,20 @@
 // k) with the decode bias folded in, so the dequant thread multiplies each element pair by
 // its own pair of scales.
 //
-// Warp roles (24 warps): 0 packed/scale TMA, 1 activation TMA, 2 and 3 MMA issuers (warp 2
+// Warp roles (25 warps): 0 packed/scale TMA, 1 activation TMA, 2 and 3 MMA issuers (warp 2
 // owns the TMEM allocation), 4..19 dequant (four warps per TMEM lane quarter, one per 32-K
-// segment of a 128-K stage), 20..23 epilogue. The two issuers accumulate into separate
-// accumulators (gate / up, W1 / W3, or even / odd K stages), so neither waits on the other
-// and the sums stay deterministic; the epilogue adds them where they are one product.
-// Packed weights move in 128-K TMA stages; the tensor-memory A stages and the activation
-// slots move in ring stages of 128/LL_GEMM_SUBSTAGES K, each with one "full" barrier (the
-// dequant warps that fill it + the activation TMA) and one "empty" commit from the issuers.
+// segment of a 128-K stage), 20..23 epilogue, 24 stage watcher (waits on the mbarriers for
+// the issuers and releases them through named barriers), 25 and 26 two more MMA issuers.
+// The issuers accumulate into separate accumulators (chains: gate / up and even / odd K
+// stages, or K stages mod 4), so none waits on another and the sums stay deterministic; the
+// epilogue adds the chains of one product in a fixed order.
+// Packed weights move in 128-K TMA stages through a deep shared-memory ring; the
+// tensor-memory A stages and the activation slots move in a shorter ring of 128-K stages,
+// each with one "full" barrier (the 16 dequant warps + the activation TMA) and one "empty"
+// commit per consuming chain. A dequant warp decodes stage s + 1 while its tensor-memory
+// store of stage s completes.
 #pragma once
 #include "common.cuh"
-
-// A/B ring granularity: 1 = 128-K stages (default), 2 = 64-K stages (twice as many in-flight
-// stages in the same tensor memory, half the MMAs per barrier; measured 15-20% slower at
-// d=7168, f=2048, 9 tokens per expert).
-#ifndef LL_GEMM_SUBSTAGES
-#define LL_GEMM_SUBSTAGES 1
-#endif
 
 namespace ll {
 
@@ -101,15 +98,22 @@ struct GemmArgs {
 
 template <int NMAT, int NB, bool COLSCALE, int N_MAX>
 struct GemmCfg {
-  static constexpr int kThreads = 24 * 32;
+  static constexpr int kWatchWarp = 24;
+  static constexpr int kIssuerWarpX = 25;                 // issuers 2 and 3 live at warps 25, 26
+  // Independent accumulation chains, one MMA issuer warp each: a warp issues one tcgen05.mma
+  // per ~50 cycles at small N however many accumulators it rotates, so small-N tiles need
+  // several issuing warps; N = 128 MMAs are long enough for two.
+#ifndef LL_CHAINS_SMALL_N
+#define LL_CHAINS_SMALL_N 2
+#endif
+  static constexpr int CH = N_MAX <= 32 ? LL_CHAINS_SMALL_N : 2;
+  static constexpr int PM = CH / NMAT;                    // chains per weight matrix
+  static constexpr int kThreads = (CH > 2 ? 27 : 25) * 32;
   static constexpr int kIssuerWarp0 = 2;
   static constexpr int kDqWarp0 = 4, kDqWarps = 16;
   static constexpr int kEpWarp0 = 20, kEpWarps = 4;
   static constexpr int BK = 128;                          // K per packed (TMA) stage
-  static constexpr int SUB = LL_GEMM_SUBSTAGES;           // A/B ring stages per packed stage
-  static constexpr int KS = BK / SUB;                     // K per A/B ring stage
-  static constexpr int SEGS = 4 / SUB;                    // 32-K dequant segments per A/B stage
-  static constexpr int kDqPerStage = kDqWarps / SUB;      // dequant warps that fill one A/B stage
+  static constexpr int KS = BK;                           // K per A/B ring stage
   static constexpr int PK_BYTES = 128 * 64;               // 128 rows x 64 packed bytes
   static constexpr int SC_BYTES = COLSCALE ? 4 * 128 * 2  // 4 row groups x 128 k x fp16
                                            : 128 * 16;    // 128 rows x 16 scale bytes
@@ -117,13 +121,20 @@ struct GemmCfg {
   static constexpr int B_HALF = N_MAX * 128;              // one 64-K half of one operand
   static constexpr int B_SLOT = NB * (KS / 64) * B_HALF;
   // tensor memory: two accumulators per buffer (one per issuer), then the A stages
-  static constexpr int ACC_COLS = 2 * N_MAX;
+  static constexpr int ACC_COLS = CH * N_MAX;
   static constexpr int A_STAGE_COLS = NMAT * KS / 2;      // fp16 pairs: KS/2 columns per matrix
-  static constexpr int NACC = (2 * ACC_COLS + 2 * A_STAGE_COLS * SUB <= 512) ? 2 : 1;
+  static constexpr int NACC = (2 * ACC_COLS + 2 * A_STAGE_COLS <= 512) ? 2 : 1;
   static constexpr int A_BASE = NACC * ACC_COLS;
   static constexpr int S_AB0 = (512 - A_BASE) / A_STAGE_COLS;
-  static constexpr int S_AB = S_AB0 > 12 ? 12 : S_AB0;
+  static constexpr int S_AB = S_AB0 > 7 ? 7 : S_AB0;     // 2 named barriers a slot, ids 1..14
   static_assert(S_AB >= 2, "tensor memory budget");
+  // Dequant stage groups: group j of dequant warps fills ring stages g with g % GROUPS == j,
+  // SEGW 32-K segments per warp, so GROUPS stages fill at once and a warp pays its barrier
+  // round trip once per SEGW segments.
+  static constexpr int GROUPS = S_AB >= 5 ? 4 : (S_AB >= 3 ? 2 : 1);
+  static constexpr int SEGW = GROUPS;                     // segments a warp decodes per stage
+  static_assert((kDqWarps / 4) % GROUPS == 0 && (kDqWarps / 4 / GROUPS) * SEGW == 4, "segment cover");
+  static constexpr int kDqPerStage = kDqWarps / GROUPS;   // warps that fill one stage
   static constexpr int TMEM_COLS0 = A_BASE + S_AB * A_STAGE_COLS;
   static constexpr int TMEM_COLS = TMEM_COLS0 <= 32 ? 32 : TMEM_COLS0 <= 64 ? 64 : TMEM_COLS0 <= 128 ? 128
                                    : TMEM_COLS0 <= 256 ? 256 : 512;
@@ -139,6 +150,11 @@ struct GemmCfg {
   static constexpr int SMEM = OFF_BAR + N_BARS * 8 + 64 + 1024;  // + alignment slack
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
   static_assert(N_MAX % 16 == 0 && N_MAX <= 128, "N_MAX");
+  // a ring slot is reused only after every chain that could share its named barrier moved on
+  static_assert(S_AB >= PM, "ring shorter than the chains of one matrix");
+  // named barrier releasing the chain of weight matrix `mat` that takes the stage in ring
+  // slot s (ids 1..14; id 0 is __syncthreads)
+  static __device__ __forceinline__ int ready_bar(int s, int mat) { return 1 + 2 * s + mat; }
 };
 
 template <int NMAT, int NB>
@@ -149,7 +165,7 @@ struct TmaSet {
 };
 
 template <int EPI, int NMAT, int NB, bool COLSCALE, int N_MAX>
-__global__ void __launch_bounds__(24 * 32, 1)
+__global__ void __launch_bounds__(GemmCfg<NMAT, NB, COLSCALE, N_MAX>::kThreads, 1)
 grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs args) {
   using C = GemmCfg<NMAT, NB, COLSCALE, N_MAX>;
   extern __shared__ uint8_t smem_raw[];
@@ -168,19 +184,19 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int n_units = (*args.n_chunks) * args.mtiles;
-  if ((int)blockIdx.x >= n_units) return;   // uniform over the CTA: nothing allocated yet
+  if ((int)blockIdx.x >= n_units || args.K <= 0) return;   // uniform over the CTA: nothing allocated yet
 
   const int K = args.K;
   const int n_stage = (K + C::BK - 1) / C::BK;   // packed (TMA) stages per unit
   const int n_sub = (K + C::KS - 1) / C::KS;     // A/B ring stages per unit
   // with one weight matrix the two issuers take alternate stages; a 1-stage K leaves one idle
-  const bool two_acc_sum = NMAT == 1 ? n_sub > 1 : EPI != EPI_F1;
+  const int chains_used = n_sub < C::PM ? n_sub : C::PM;   // chains of a matrix that got a stage
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < C::S_P; i++) { mbar_init(&pfull[i], 1); mbar_init(&pempty[i], C::kDqWarps); }
+    for (int i = 0; i < C::S_P; i++) { mbar_init(&pfull[i], 1); mbar_init(&pempty[i], C::kDqPerStage); }
     for (int i = 0; i < C::S_AB; i++) { mbar_init(&full[i], C::kDqPerStage + 1); mbar_init(&empty[i], NMAT == 2 ? 2 : 1); }
-    for (int i = 0; i < 2; i++) { mbar_init(&accfull[i], 2); mbar_init(&accempty[i], C::kEpWarps); }
-    mbar_init(drain, 2);
+    for (int i = 0; i < 2; i++) { mbar_init(&accfull[i], C::CH); mbar_init(&accempty[i], C::kEpWarps); }
+    mbar_init(drain, C::CH);
     *abort_flag = 0;
     fence_barrier_init();
     fence_async_smem();
@@ -206,7 +222,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
         const int row = ch.e * args.e_rows + mt * 128;
         const int grp = (ch.e * args.e_rows) / 32 + mt * 4;
         for (int ks = 0; ks < n_stage && ok; ks++) {
-          if (!(ok = mbar_wait(&pempty[s], ph ^ 1, abort_flag, st, 1))) break;
+          if (!(ok = mbar_wait_sleep(&pempty[s], ph ^ 1, abort_flag, st, 1, 256))) break;
           uint8_t* stage = smem + C::OFF_P + s * C::P_STAGE;
           mbar_arrive_expect_tx(&pfull[s], C::P_STAGE);
           for (int i = 0; i < NMAT; i++) {
@@ -223,7 +239,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
       }
       for (int i = 0; i < C::S_P && i < issued; i++) {   // drain: bytes of the last stages landed
         if (--s < 0) { s = C::S_P - 1; ph ^= 1; }
-        mbar_wait(&pfull[s], ph, abort_flag, st, 11);
+        mbar_wait_sleep(&pfull[s], ph, abort_flag, st, 11, 256);
       }
     }
   } else if (warp == 1) {
@@ -238,7 +254,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
         const Chunk ch = args.chunks[u / args.mtiles];
         const int npad = (ch.n + 15) & ~15;
         for (int sb = 0; sb < n_sub && ok; sb++) {
-          if (!(ok = mbar_wait(&empty[s], ph ^ 1, abort_flag, st, 2))) break;
+          if (!(ok = mbar_wait_sleep(&empty[s], ph ^ 1, abort_flag, st, 2, 256))) break;
           uint8_t* slot = smem + C::OFF_B + s * C::B_SLOT;
           mbar_arrive_expect_tx(&full[s], NB * (C::KS / 64) * npad * 128);
           for (int b = 0; b < NB; b++)
@@ -252,76 +268,112 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
       }
       for (int i = 0; i < C::S_AB && i < issued; i++) {
         if (--s < 0) { s = C::S_AB - 1; ph ^= 1; }
-        mbar_wait(&full[s], ph, abort_flag, st, 12);
+        mbar_wait_sleep(&full[s], ph, abort_flag, st, 12, 256);
       }
     }
-  } else if (warp < C::kDqWarp0) {
+  } else if (warp < C::kDqWarp0 || warp >= C::kIssuerWarpX) {
     // ---------------------------------------------------------------- MMA issuers
-    const int issuer = warp - C::kIssuerWarp0;   // 0 or 1
-    if (lane == 0) {
+    // Chain c = mat * PM + k accumulates weight matrix `mat` over the stages sb with
+    // sb % PM == k. The whole warp takes part in the named barriers the watcher releases
+    // stages on; lane 0 issues. An issuer never touches an mbarrier in its loop: an mbarrier
+    // wait in the thread that issues tcgen05.mma stalls the MMA stream by hundreds of cycles.
+    const int c = warp < C::kDqWarp0 ? warp - C::kIssuerWarp0 : 2 + warp - C::kIssuerWarpX;
+    if (c < C::CH) {
+      const int mat = c / C::PM, kc = c % C::PM;
       int s = 0, ab = 0;
-      uint32_t ph = 0, abph = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const Chunk ch = args.chunks[u / args.mtiles];
         const int npad = (ch.n + 15) & ~15;
         const uint32_t idesc = idesc_f16_m128(npad, false, false);
-        if (!(ok = mbar_wait(&accempty[ab], abph ^ 1, abort_flag, st, 3))) break;
-        tc_fence_after();
-        const uint32_t d = tmem + (ab * 2 + issuer) * N_MAX;
+        const uint32_t d = tmem + (ab * C::CH + c) * N_MAX;
         bool first = true;
-        for (int sb = 0; sb < n_sub && ok; sb++) {
-          const bool mine = NMAT == 2 || (sb & 1) == issuer;
-          if (mine) {
-            if (!(ok = mbar_wait(&full[s], ph, abort_flag, st, 4))) break;
-            tc_fence_after();
-            const uint32_t a_tmem = tmem + C::A_BASE + s * C::A_STAGE_COLS + (NMAT == 2 ? issuer : 0) * (C::KS / 2);
-            const uint32_t b_addr =
-                smem_u32(smem + C::OFF_B + s * C::B_SLOT) + (NB == 2 ? issuer : 0) * (C::KS / 64) * C::B_HALF;
+        for (int sb = 0; sb < n_sub; sb++) {
+          if (sb % C::PM == kc) {
+            if (*abort_flag) { ok = false; break; }   // the watcher may run ahead after an abort
+            named_bar_sync(C::ready_bar(s, mat), 64);
+            if (lane == 0) {
+              tc_fence_after();
+              const uint32_t a_tmem = tmem + C::A_BASE + s * C::A_STAGE_COLS + mat * (C::KS / 2);
+              const uint32_t b_addr =
+                  smem_u32(smem + C::OFF_B + s * C::B_SLOT) + (NB == 2 ? mat : 0) * (C::KS / 64) * C::B_HALF;
 #pragma unroll
-            for (int kk = 0; kk < C::KS / 16; kk++) {
-              const uint64_t bdesc = umma_desc(b_addr + (kk >> 2) * C::B_HALF + (kk & 3) * 32, 16, 1024, kSwizzle128B);
-              mma_f16_ts(d, a_tmem + kk * 8, bdesc, idesc, first ? 0u : 1u);
-              first = false;
+              for (int kk = 0; kk < C::KS / 16; kk++) {
+                const uint64_t bdesc =
+                    umma_desc(b_addr + (kk >> 2) * C::B_HALF + (kk & 3) * 32, 16, 1024, kSwizzle128B);
+                mma_f16_ts(d, a_tmem + kk * 8, bdesc, idesc, first ? 0u : 1u);
+                first = false;
+              }
+              mma_commit(&empty[s]);
             }
-            mma_commit(&empty[s]);
+            __syncwarp();
           }
-          if (++s == C::S_AB) { s = 0; ph ^= 1; }
+          if (++s == C::S_AB) s = 0;
         }
-        mma_commit(&accfull[ab]);
-        if (++ab == C::NACC) { ab = 0; abph ^= 1; }
+        if (lane == 0) mma_commit(&accfull[ab]);
+        __syncwarp();
+        if (++ab == C::NACC) ab = 0;
       }
-      mma_commit(drain);            // completes once every MMA issued above has finished
-      mbar_wait(drain, 0, abort_flag, st, 13);
+      if (lane == 0) {
+        mma_commit(drain);              // completes once every MMA issued above has finished
+        volatile int keep_waiting = 0;  // wait for them even after an abort
+        mbar_wait_sleep(drain, 0, &keep_waiting, st, 13, 256);
+      }
+    }
+  } else if (warp == C::kWatchWarp) {
+    // ------------------------------------------------------------------ stage watcher
+    // Waits (bounded) for each ring stage to fill (dequant warps + activation TMA) and for
+    // each unit's accumulator buffer to drain (epilogue), then releases the issuer(s) of that
+    // stage through named barrier (stage slot, issuer). It never leaves the loop early and
+    // never blocks without a bound, so every barrier an issuer syncs on gets its arrival,
+    // also after an abort (when the waits return at once).
+    int s = 0, ab = 0;
+    uint32_t ph = 0, abph = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      if (lane == 0) mbar_wait(&accempty[ab], abph ^ 1, abort_flag, st, 3);
+      __syncwarp();
+      for (int sb = 0; sb < n_sub; sb++) {
+        if (lane == 0) mbar_wait(&full[s], ph, abort_flag, st, 4);
+        __syncwarp();
+        for (int mat = 0; mat < NMAT; mat++) named_bar_arrive(C::ready_bar(s, mat), 64);
+        if (++s == C::S_AB) { s = 0; ph ^= 1; }
+      }
+      if (++ab == C::NACC) { ab = 0; abph ^= 1; }
     }
   } else if (warp < C::kEpWarp0) {
     // ---------------------------------------------------------------- dequant warps
-    // warp -> (TMEM lane quarter q, 32-element K segment seg of each 128-K stage); thread -> row
+    // warp -> (TMEM lane quarter q, stage group grp, segments seg0 .. seg0 + SEGW - 1 of the
+    // 128-K stages of that group); thread -> weight row. Each 32-K segment is decoded to
+    // registers and stored to tensor memory at once; the stage is marked full after the
+    // last store of the warp completes.
     const int dw = warp - C::kDqWarp0;           // 0..15
     const int q = warp & 3;
-    const int seg = dw >> 2;                     // 0..3 = 16-byte chunk of the 64-byte packed row
-    const int sub = seg / C::SEGS;               // A/B ring stage of this segment within the packed stage
-    const int hseg = seg % C::SEGS;              // segment within that ring stage
+    const int sub = dw >> 2;                     // 0..3
+    const int grp = sub % C::GROUPS;
+    const int seg0 = (sub / C::GROUPS) * C::SEGW;
     const int m = q * 32 + lane;                 // weight row within the 128-row tile
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    int sub_base = 0;                            // ring stages of the units before this one
     const int32_t* beta = args.epi.beta;
     const int bcol = args.epi.beta_col;
-    int ps = 0;
-    uint32_t pph = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, sub_base += n_sub) {
-      const Chunk ch = args.chunks[u / args.mtiles];
-      const int bias = (!COLSCALE && beta) ? beta[ch.e * 2 + bcol] : 0;
-      for (int ks = 0; ks < n_stage && ok; ks++) {
-        if (!(ok = mbar_wait(&pfull[ps], pph, abort_flag, st, 6))) break;
-        const uint8_t* stage = smem + C::OFF_P + ps * C::P_STAGE;
-        uint32_t o[NMAT][16];
+    int g = grp;                                 // ring stage index over this CTA's stages
+    int u = blockIdx.x, ks = grp;
+    while (ks >= n_stage) { ks -= n_stage; u += gridDim.x; }
+    int bias = (u < n_units && !COLSCALE && beta) ? beta[args.chunks[u / args.mtiles].e * 2 + bcol] : 0;
+    while (u < n_units) {
+      const int ps = g % C::S_P, as = g % C::S_AB;
+      const uint32_t pph = (uint32_t)(g / C::S_P) & 1u, aph = (uint32_t)(g / C::S_AB) & 1u;
+      if (!mbar_wait(&pfull[ps], pph, abort_flag, st, 6)) break;
+      const uint8_t* stage = smem + C::OFF_P + ps * C::P_STAGE;
+      bool waited = false, ok = true;
+#pragma unroll
+      for (int j = 0; j < C::SEGW; j++) {
+        const int seg = seg0 + j;
 #pragma unroll
         for (int i = 0; i < NMAT; i++) {
           const uint8_t* pk = stage + i * (C::PK_BYTES + C::SC_BYTES);
           const uint8_t* sc = pk + C::PK_BYTES;
           const uint4 raw = ld_shared_v4(smem_u32(pk + m * 64 + ((seg ^ ((m >> 1) & 3)) << 4)));
+          uint32_t o[16];
           if (COLSCALE) {
             // fp16 multipliers of k = 32 seg .. 32 seg + 31 for this warp's 32-row group q
             const uint32_t sa = smem_u32(sc + (q * 128 + seg * 32) * 2);
@@ -329,37 +381,41 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
             const uint4 s2 = ld_shared_v4(sa + 32), s3 = ld_shared_v4(sa + 48);
             const uint32_t sv[16] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w,
                                      s2.x, s2.y, s2.z, s2.w, s3.x, s3.y, s3.z, s3.w};
-            decode8v(raw.x, &sv[0], &o[i][0]);
-            decode8v(raw.y, &sv[4], &o[i][4]);
-            decode8v(raw.z, &sv[8], &o[i][8]);
-            decode8v(raw.w, &sv[12], &o[i][12]);
+            decode8v(raw.x, &sv[0], &o[0]);
+            decode8v(raw.y, &sv[4], &o[4]);
+            decode8v(raw.z, &sv[8], &o[8]);
+            decode8v(raw.w, &sv[12], &o[12]);
           } else {
             const uint32_t sbyte = sc[m * 16 + (((ks * C::BK) / 32) & 15) + seg];
             const uint32_t s1 = e8m0_to_half_bits(sbyte, bias);
             const uint32_t s2 = s1 | (s1 << 16);
-            decode8(raw.x, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[i][0]));
-            decode8(raw.y, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[i][4]));
-            decode8(raw.z, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[i][8]));
-            decode8(raw.w, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[i][12]));
+            decode8(raw.x, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[0]));
+            decode8(raw.y, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[4]));
+            decode8(raw.z, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[8]));
+            decode8(raw.w, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[12]));
           }
+          if (!waited) {                         // the slot's previous MMAs are done
+            if (!(ok = mbar_wait(&empty[as], aph ^ 1, abort_flag, st, 7))) break;
+            tc_fence_after();
+            waited = true;
+          }
+          tmem_st16(tmem + lane_base + C::A_BASE + as * C::A_STAGE_COLS + i * (C::KS / 2) + seg * 16, o);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&pempty[ps]);      // packed bytes consumed (in registers now)
-        if (++ps == C::S_P) { ps = 0; pph ^= 1; }
-        const int gs = ks * C::SUB + sub;          // ring stage of this segment within the unit
-        if (gs >= n_sub) continue;                 // K ends inside this packed stage
-        const int g = sub_base + gs;               // ring stage counted over this CTA's units
-        const int as = g % C::S_AB;
-        const uint32_t aph = (uint32_t)(g / C::S_AB) & 1u;
-        if (!(ok = mbar_wait(&empty[as], aph ^ 1, abort_flag, st, 7))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int i = 0; i < NMAT; i++)
-          tmem_st16(tmem + lane_base + C::A_BASE + as * C::A_STAGE_COLS + i * (C::KS / 2) + hseg * 16, o[i]);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&full[as]);
+        if (!ok) break;
+      }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pempty[ps]);   // packed bytes consumed
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[as]);
+      g += C::GROUPS;
+      ks += C::GROUPS;
+      while (ks >= n_stage) {                    // into the next unit(s)
+        ks -= n_stage;
+        u += gridDim.x;
+        if (u < n_units && !COLSCALE && beta) bias = beta[args.chunks[u / args.mtiles].e * 2 + bcol];
       }
     }
   } else {
@@ -378,17 +434,31 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
       const int npad = (ch.n + 15) & ~15;
       const int bias = ep.beta ? ep.beta[ch.e * 2 + ep.beta_col] : 0;
       const float wunscale = exp2f((float)(-bias));
-      if (!(ok = mbar_wait(&accfull[ab], abph, abort_flag, st, 8))) break;
+      if (!(ok = mbar_wait_sleep(&accfull[ab], abph, abort_flag, st, 8, 512))) break;
       tc_fence_after();
-      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * 2 * N_MAX;
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * C::CH * N_MAX;
       for (int j0 = 0; j0 < npad; j0 += 16) {
-        float v0[16], v1[16];
+        // v0 = sum of matrix 0's chains (all chains unless F1), v1 = matrix 1's (F1: up)
+        float v0[16], v1[16], t[16];
         tmem_ld16(tbase + j0, v0);
-        tmem_ld16(tbase + N_MAX + j0, v1);
         tmem_ld_wait();
-        if (EPI != EPI_F1) {
+        if (EPI == EPI_F1) {
+          tmem_ld16(tbase + C::PM * N_MAX + j0, v1);
+          tmem_ld_wait();
+        }
+        for (int cc = 1; cc < C::CH; cc++) {
+          const int kc = cc % C::PM;
+          if (kc >= chains_used) continue;        // a chain that got no stage holds no sum
+          if (EPI == EPI_F1 && kc == 0) continue; // first chain of matrix 1, loaded above
+          tmem_ld16(tbase + cc * N_MAX + j0, t);
+          tmem_ld_wait();
+          if (EPI == EPI_F1 && cc >= C::PM) {
 #pragma unroll
-          for (int jj = 0; jj < 16; jj++) v0[jj] = two_acc_sum ? v0[jj] + v1[jj] : v0[jj];
+            for (int jj = 0; jj < 16; jj++) v1[jj] += t[jj];
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 16; jj++) v0[jj] += t[jj];
+          }
         }
         float gwp[16];
 #pragma unroll

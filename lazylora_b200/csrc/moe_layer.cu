@@ -260,9 +260,12 @@ struct LayerWs {
   int nseg_max;
 };
 
+#ifndef LL_NMAX_SMALL
+#define LL_NMAX_SMALL 32
+#endif
 static int choose_nmax(int T, int k, int E) {
   const double mean = (double)T * k / (E > 0 ? E : 1);
-  return mean <= 12.0 ? 32 : 128;
+  return mean <= 12.0 ? LL_NMAX_SMALL : 128;
 }
 
 static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, LayerWs* out) {
@@ -333,6 +336,7 @@ static int validate(const ll_moe_layer* L, int T, int k) {
 template <int EPI, int NMAT, int NB, bool COLSCALE>
 static int gemm_nmax(int nmax, const CUtensorMap* pk, const CUtensorMap* sc, const CUtensorMap* act, const GemmArgs& a,
                      cudaStream_t s) {
+  if (nmax == 16) return launch_gemm<EPI, NMAT, NB, COLSCALE, 16>(pk, sc, act, a, s);
   if (nmax == 32) return launch_gemm<EPI, NMAT, NB, COLSCALE, 32>(pk, sc, act, a, s);
   return launch_gemm<EPI, NMAT, NB, COLSCALE, 128>(pk, sc, act, a, s);
 }

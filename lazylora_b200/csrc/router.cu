@@ -4,76 +4,17 @@
 //   renormalised by (sum + 1e-20) when asked and k > 1, times the routed scaling factor.
 #include "host_common.cuh"
 #include "ops.cuh"
+#include "router_tc.cuh"
 
 namespace ll {
 
-// logits[T][E] = x[T][d] . W[E][d]^T in fp32, 64 x 64 tiles, 4 x 4 outputs per thread.
-template <int XD>  // x dtype: 0 fp32, 1 bf16
-__global__ void __launch_bounds__(256) k_router_logits(const void* __restrict__ xv, const float* __restrict__ W,
-                                                       float* __restrict__ out, int T, int d, int E) {
-  constexpr int BM = 64, BN = 64, BK = 16;
-  __shared__ float xs[BK][BM + 4];
-  __shared__ float ws[BK][BN + 4];
-  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-  const int t0 = blockIdx.y * BM, e0 = blockIdx.x * BN;
-  float acc[4][4] = {};
-  const int lr = threadIdx.x / 4;          // 0..63 row within tile
-  const int lk = (threadIdx.x % 4) * 4;    // 0,4,8,12
-  for (int k0 = 0; k0 < d; k0 += BK) {
-    {
-      const int t = t0 + lr;
-      float v[4] = {0.f, 0.f, 0.f, 0.f};
-      if (t < T) {
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const int k = k0 + lk + i;
-          if (k < d)
-            v[i] = XD == 0 ? reinterpret_cast<const float*>(xv)[(int64_t)t * d + k]
-                           : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(xv)[(int64_t)t * d + k]);
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 4; i++) xs[lk + i][lr] = v[i];
-      const int e = e0 + lr;
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const int k = k0 + lk + i;
-        ws[lk + i][lr] = (e < E && k < d) ? W[(int64_t)e * d + k] : 0.f;
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int kk = 0; kk < BK; kk++) {
-      float a[4], b[4];
-#pragma unroll
-      for (int i = 0; i < 4; i++) a[i] = xs[kk][ty * 4 + i];
-#pragma unroll
-      for (int j = 0; j < 4; j++) b[j] = ws[kk][tx * 4 + j];
-#pragma unroll
-      for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const int t = t0 + ty * 4 + i;
-    if (t >= T) continue;
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const int e = e0 + tx * 4 + j;
-      if (e < E) out[(int64_t)t * E + e] = acc[i][j];
-    }
-  }
-}
-
 // One warp per token. MODE 0: `a` holds logits (scores = sigmoid, choice = scores + bias).
 // MODE 1: `a` holds scores and `b` the scores used for the choice, as given.
+// In MODE 0 the logits are the sum of `nsplit` fp32 partials [nsplit][T][E], added in order.
 template <int MODE, int PER_LANE>
 __global__ void k_route_select(const float* __restrict__ a, const float* __restrict__ b, const float* __restrict__ bias,
                                int T, int E, int k, int renorm, float rsf, int64_t* __restrict__ idx,
-                               float* __restrict__ w, float* __restrict__ scores_out) {
+                               float* __restrict__ w, float* __restrict__ scores_out, int nsplit) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (warp >= T) return;
@@ -86,7 +27,9 @@ __global__ void k_route_select(const float* __restrict__ a, const float* __restr
     ch[i] = -INFINITY;
     if (e < E) {
       if (MODE == 0) {
-        const float s = 1.0f / (1.0f + expf(-a[(int64_t)t * E + e]));
+        float logit = a[(int64_t)t * E + e];
+        for (int sp = 1; sp < nsplit; sp++) logit += a[((int64_t)sp * T + t) * E + e];
+        const float s = 1.0f / (1.0f + expf(-logit));
         sc[i] = s;
         ch[i] = bias ? s + bias[e] : s;
         if (scores_out) scores_out[(int64_t)t * E + e] = s;
@@ -155,13 +98,89 @@ __global__ void k_route_select(const float* __restrict__ a, const float* __restr
 
 template <int MODE>
 static int launch_select(const float* a, const float* b, const float* bias, int T, int E, int k, int renorm, float rsf,
-                         int64_t* idx, float* w, float* scores_out, cudaStream_t s) {
+                         int64_t* idx, float* w, float* scores_out, cudaStream_t s, int nsplit = 1) {
   const int blocks = (T * 32 + 255) / 256;
   if (E <= 32 * 32)
-    k_route_select<MODE, 32><<<blocks, 256, 0, s>>>(a, b, bias, T, E, k, renorm, rsf, idx, w, scores_out);
+    k_route_select<MODE, 32><<<blocks, 256, 0, s>>>(a, b, bias, T, E, k, renorm, rsf, idx, w, scores_out, nsplit);
   else
-    k_route_select<MODE, 64><<<blocks, 256, 0, s>>>(a, b, bias, T, E, k, renorm, rsf, idx, w, scores_out);
+    k_route_select<MODE, 64><<<blocks, 256, 0, s>>>(a, b, bias, T, E, k, renorm, rsf, idx, w, scores_out, nsplit);
   return check_launch("k_route_select");
+}
+
+// ------------------------------------------------------------ tensor-core logits: plan + launch
+struct RouterPlan {
+  int BN = 16, NP = 1, mt = 1, nt = 1, nsplit = 1, kbps = 1, kb_total = 1;
+  size_t off_w = 0, off_x = 0, off_part = 0, off_st = 0, bytes = 0;
+};
+
+static RouterPlan router_plan(int T, int d, int E, int x_dtype) {
+  RouterPlan p;
+  p.BN = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128;
+  p.NP = x_dtype == 0 ? 3 : 1;
+  p.mt = (E + 127) / 128;
+  p.nt = (T + p.BN - 1) / p.BN;
+  p.kb_total = (d + 63) / 64;
+  const int sms = device_info().sms > 0 ? device_info().sms : 148;
+  const int tiles = p.mt * p.nt;
+  int want = tiles >= sms ? 1 : sms / tiles;                 // K splits that fill the SMs once
+  if (want > p.kb_total) want = p.kb_total;
+  p.kbps = (p.kb_total + want - 1) / want;
+  p.nsplit = (p.kb_total + p.kbps - 1) / p.kbps;               // every split non-empty
+  {
+    size_t off = 0;
+    auto take = [&](size_t n) { off = (off + 255) & ~size_t(255); const size_t o = off; off += n; return o; };
+    p.off_w = take((size_t)3 * E * d * 2);
+    p.off_x = take(p.NP == 3 ? (size_t)3 * T * d * 2 : 0);
+    p.off_part = take((size_t)p.nsplit * T * E * 4);
+    p.off_st = take(sizeof(DevStatus));
+    p.bytes = (off + 255) & ~size_t(255);
+  }
+  return p;
+}
+
+template <int NP, int BN>
+static int launch_router_mma(const RouterMaps& maps, float* part, int T, int E, const RouterPlan& p, DevStatus* st,
+                             cudaStream_t s) {
+  using Cf = RouterCfg<NP, BN>;
+  auto kern = k_router_mma<NP, BN>;
+  LL_TRY(set_smem_attr(reinterpret_cast<const void*>(kern), Cf::SMEM));
+  dim3 grid(p.mt, p.nt, p.nsplit);
+  kern<<<grid, kRtWarps * 32, Cf::SMEM, s>>>(maps, part, T, E, p.kb_total, p.kbps, st);
+  return check_launch("k_router_mma");
+}
+
+static int router_logits_tc(const void* x, int x_dtype, const float* W, int T, int d, int E, void* ws,
+                            const RouterPlan& p, cudaStream_t s) {
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  __nv_bfloat16* wp = reinterpret_cast<__nv_bfloat16*>(base + p.off_w);
+  const int64_t nw = (int64_t)E * d;
+  k_split_bf16x3<<<148 * 4, 256, 0, s>>>(W, wp, wp + nw, wp + 2 * nw, nw);
+  LL_TRY(check_launch("k_split_bf16x3"));
+  const __nv_bfloat16* xp[3] = {static_cast<const __nv_bfloat16*>(x), nullptr, nullptr};
+  if (p.NP == 3) {
+    __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(base + p.off_x);
+    const int64_t nx = (int64_t)T * d;
+    k_split_bf16x3<<<148 * 4, 256, 0, s>>>(static_cast<const float*>(x), xs, xs + nx, xs + 2 * nx, nx);
+    LL_TRY(check_launch("k_split_bf16x3"));
+    xp[0] = xs; xp[1] = xs + nx; xp[2] = xs + 2 * nx;
+  }
+  RouterMaps maps;
+  for (int i = 0; i < 3; i++)
+    LL_TRY(make_map_2d(&maps.a[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, wp + i * nw, (uint64_t)d, (uint64_t)E,
+                       (uint64_t)d * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B));
+  for (int i = 0; i < p.NP; i++)
+    LL_TRY(make_map_2d(&maps.b[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xp[i], (uint64_t)d, (uint64_t)T,
+                       (uint64_t)d * 2, 64, p.BN, CU_TENSOR_MAP_SWIZZLE_128B));
+  if (p.NP == 1) maps.b[1] = maps.b[2] = maps.b[0];
+  DevStatus* st = reinterpret_cast<DevStatus*>(base + p.off_st);
+  LL_TRY(reset_status(st, s));
+  float* part = reinterpret_cast<float*>(base + p.off_part);
+#define LL_RT(NPv, BNv) \
+  if (p.NP == NPv && p.BN == BNv) return launch_router_mma<NPv, BNv>(maps, part, T, E, p, st, s);
+  LL_RT(1, 16) LL_RT(1, 32) LL_RT(1, 64) LL_RT(1, 128)
+  LL_RT(3, 16) LL_RT(3, 32) LL_RT(3, 64) LL_RT(3, 128)
+#undef LL_RT
+  return LL_ERR_ARG;
 }
 
 }  // namespace ll
@@ -170,23 +189,24 @@ using namespace ll;
 
 extern "C" {
 
-size_t ll_route_workspace_bytes(int T, int E) { return ((size_t)T * E * sizeof(float) + 255) & ~size_t(255); }
+size_t ll_route_workspace_bytes(int T, int d, int E) {
+  if (T <= 0 || d <= 0 || E <= 0) return 0;
+  return router_plan(T, d, E, 0).bytes;     // fp32 activations need the most (their planes)
+}
 
 int ll_route_topk(const void* x, int x_dtype, const float* router_w, const float* bias, int T, int d, int E, int k,
                   int renormalize, float routed_scaling_factor, int64_t* idx, float* w, float* scores_out, void* ws,
                   size_t ws_bytes, void* stream) {
-  if (T <= 0 || d <= 0 || E <= 0 || k <= 0 || k > 32 || k > E || E > 2048) return LL_ERR_ARG;
+  if (T <= 0 || d <= 0 || E <= 0 || k <= 0 || k > 32 || k > E || E > 2048 || d % 8) return LL_ERR_ARG;
   if (!x || !router_w || !idx || !w || !ws || (x_dtype != 0 && x_dtype != 1)) return LL_ERR_ARG;
-  if (ws_bytes < ll_route_workspace_bytes(T, E)) return LL_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(ws) % 256) return LL_ERR_ARG;
+  const RouterPlan p = router_plan(T, d, E, x_dtype);
+  if (ws_bytes < p.bytes) return LL_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  float* logits = static_cast<float*>(ws);
-  dim3 grid((E + 63) / 64, (T + 63) / 64);
-  if (x_dtype == 0)
-    k_router_logits<0><<<grid, 256, 0, s>>>(x, router_w, logits, T, d, E);
-  else
-    k_router_logits<1><<<grid, 256, 0, s>>>(x, router_w, logits, T, d, E);
-  LL_TRY(check_launch("k_router_logits"));
-  return launch_select<0>(logits, nullptr, bias, T, E, k, renormalize, routed_scaling_factor, idx, w, scores_out, s);
+  LL_TRY(router_logits_tc(x, x_dtype, router_w, T, d, E, ws, p, s));
+  const float* part = reinterpret_cast<const float*>(static_cast<uint8_t*>(ws) + p.off_part);
+  return launch_select<0>(part, nullptr, bias, T, E, k, renormalize, routed_scaling_factor, idx, w, scores_out, s,
+                          p.nsplit);
 }
 
 int ll_route_select(const float* scores, const float* scores_for_choice, int T, int E, int k, int renormalize,

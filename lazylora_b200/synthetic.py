@@ -36,6 +36,7 @@ class LayerConfig:
     alpha: int = 32   # LoRA alpha (scaling = alpha / r)
     x_dtype: str = "bf16"   # "f32" or "bf16" (values rounded to bf16, held as fp32 for the oracle)
     zipf_s: Optional[float] = None   # router-bias skew, None = uniform-ish routing
+    zipf_gamma: float = 0.05         # bias_e = gamma * ln(p_e / p_max) (fit_zipf_gamma picks it)
     seed: int = 0
 
     @property
@@ -76,12 +77,55 @@ def _round_bf16(t: torch.Tensor) -> torch.Tensor:
 
 def zipf_bias(E: int, s: float, gamma: float, gen: torch.Generator) -> torch.Tensor:
     """bias_e = gamma * ln(p_e / p_max) with p_e proportional to rank_e^-s, ranks a seeded permutation."""
+    p = zipf_target(E, s, gen)
+    return (gamma * torch.log(p / p.max())).to(torch.float32)
+
+
+def zipf_target(E: int, s: float, gen: torch.Generator) -> torch.Tensor:
+    """p_e proportional to rank_e^-s over a seeded permutation of ranks (same draw as zipf_bias)."""
     perm = torch.randperm(E, generator=gen)
     rank = torch.empty(E, dtype=torch.float64)
     rank[perm] = torch.arange(1, E + 1, dtype=torch.float64)
     p = rank.pow(-s)
-    p = p / p.sum()
-    return (gamma * torch.log(p / p.max())).to(torch.float32)
+    return p / p.sum()
+
+
+def fit_zipf_gamma(cfg: LayerConfig, device="cuda", tokens: int = 65536, chunk: int = 8192):
+    """The router-bias scale gamma whose top-k selection frequencies over `tokens` seeded
+    N(0,1) tokens best match the Zipf target p in L1 (1-D search, log grid then refinement).
+    Returns (gamma, L1). The router arithmetic is the reference's: sigmoid(x Wr^T) + bias,
+    top-k of that (lazy_lora/core/moe_router.py:80-100); ties do not matter for frequencies."""
+    dev = torch.device(device)
+    E, d, k = cfg.E, cfg.d, cfg.k
+    g = torch.Generator(device=device).manual_seed(cfg.seed)
+    Wr = torch.randn(E, d, generator=g, device=dev) * 0.02
+    gx = torch.Generator(device=device).manual_seed(cfg.seed + 7)
+    scores = torch.empty((tokens, E), dtype=torch.float32, device=dev)
+    for t0 in range(0, tokens, chunk):
+        n = min(chunk, tokens - t0)
+        x = torch.randn(n, d, generator=gx, device=dev).to(torch.bfloat16).float()
+        scores[t0:t0 + n] = torch.sigmoid(x @ Wr.t())
+    p = zipf_target(E, cfg.zipf_s, torch.Generator(device="cpu").manual_seed(cfg.seed + 1)).to(dev)
+    lnp = torch.log(p / p.max()).float()
+
+    def l1(gamma: float) -> float:
+        idx = torch.topk(scores + gamma * lnp, k, dim=-1).indices
+        freq = torch.bincount(idx.reshape(-1), minlength=E).double() / (tokens * k)
+        return float((freq - p).abs().sum())
+
+    grid = [10 ** (-3 + 4 * i / 80) for i in range(81)]
+    vals = [l1(x) for x in grid]
+    i = min(range(len(grid)), key=vals.__getitem__)
+    lo, hi = grid[max(i - 1, 0)], grid[min(i + 1, len(grid) - 1)]
+    for _ in range(30):                       # golden-section refinement on [lo, hi]
+        a = hi - (hi - lo) / 1.618034
+        b = lo + (hi - lo) / 1.618034
+        if l1(a) < l1(b):
+            hi = b
+        else:
+            lo = a
+    gamma = (lo + hi) / 2
+    return gamma, l1(gamma)
 
 
 def make_layer(cfg: LayerConfig, with_grad: bool = True) -> Dict[str, torch.Tensor]:
@@ -118,7 +162,7 @@ def make_layer(cfg: LayerConfig, with_grad: bool = True) -> Dict[str, torch.Tens
         gr = torch.randn(cfg.T, d, generator=g)
         out["g"] = gr if cfg.x_dtype == "f32" else _round_bf16(gr)
     if cfg.zipf_s is not None:
-        out["router_b"] = zipf_bias(E, cfg.zipf_s, gamma=0.05, gen=g)
+        out["router_b"] = zipf_bias(E, cfg.zipf_s, gamma=cfg.zipf_gamma, gen=g)
     return out
 
 
@@ -154,7 +198,7 @@ def make_layer_device(cfg: LayerConfig, device="cuda", with_grad: bool = True) -
         out["g"] = gr if cfg.x_dtype == "f32" else _round_bf16(gr)
     if cfg.zipf_s is not None:
         gc = torch.Generator(device="cpu").manual_seed(cfg.seed + 1)
-        out["router_b"] = zipf_bias(E, cfg.zipf_s, gamma=0.05, gen=gc).to(dev)
+        out["router_b"] = zipf_bias(E, cfg.zipf_s, gamma=cfg.zipf_gamma, gen=gc).to(dev)
     return out
 
 
@@ -178,7 +222,7 @@ def make_ep_rank_device(cfg: LayerConfig, rank: int, world: int, device="cuda",
     out["router_b"] = torch.zeros(E, device=dev)
     if cfg.zipf_s is not None:
         gc = torch.Generator(device="cpu").manual_seed(cfg.seed + 1)
-        out["router_b"] = zipf_bias(E, cfg.zipf_s, gamma=0.05, gen=gc).to(dev)
+        out["router_b"] = zipf_bias(E, cfg.zipf_s, gamma=cfg.zipf_gamma, gen=gc).to(dev)
     out["A_g"] = torch.randn(r, d, generator=gs, device=dev) / math.sqrt(d)
     out["B_g"] = torch.randn(f, r, generator=gs, device=dev) * 0.01
     out["A_u"] = torch.randn(r, d, generator=gs, device=dev) / math.sqrt(d)
