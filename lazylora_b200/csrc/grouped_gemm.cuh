@@ -138,15 +138,20 @@ struct GemmCfg {
   static constexpr int TMEM_COLS0 = A_BASE + S_AB * A_STAGE_COLS;
   static constexpr int TMEM_COLS = TMEM_COLS0 <= 32 ? 32 : TMEM_COLS0 <= 64 ? 64 : TMEM_COLS0 <= 128 ? 128
                                    : TMEM_COLS0 <= 256 ? 256 : 512;
-  // shared memory: activation ring (S_AB slots) and the deeper packed-weight ring
+  // shared memory: the activation (B) ring and the packed-weight ring, each with its own
+  // barriers and as deep as half the budget allows: the activation tiles come through L2
+  // with a latency of a few microseconds under the weight stream, so they are fetched many
+  // stages ahead of the tensor-memory A ring
   static constexpr int AVAIL = 227 * 1024 - 2048;
-  static constexpr int S_P0 = (AVAIL - S_AB * B_SLOT) / P_STAGE;
+  static constexpr int S_B0 = (AVAIL / 2) / B_SLOT;
+  static constexpr int S_B = S_B0 > 16 ? 16 : (S_B0 < 2 ? 2 : S_B0);
+  static constexpr int S_P0 = (AVAIL - S_B * B_SLOT) / P_STAGE;
   static constexpr int S_P = S_P0 > 10 ? 10 : S_P0;
   static_assert(S_P >= 2, "shared memory budget");
   static constexpr int OFF_B = 0;
-  static constexpr int OFF_P = OFF_B + S_AB * B_SLOT;
+  static constexpr int OFF_P = OFF_B + S_B * B_SLOT;
   static constexpr int OFF_BAR = OFF_P + S_P * P_STAGE;
-  static constexpr int N_BARS = 2 * S_P + 2 * S_AB + 4 + 1;
+  static constexpr int N_BARS = 2 * S_P + 2 * S_AB + 2 * S_B + 4 + 1;
   static constexpr int SMEM = OFF_BAR + N_BARS * 8 + 64 + 1024;  // + alignment slack
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
   static_assert(N_MAX % 16 == 0 && N_MAX <= 128, "N_MAX");
@@ -175,7 +180,9 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
   uint64_t* pempty = pfull + C::S_P;
   uint64_t* full = pempty + C::S_P;
   uint64_t* empty = full + C::S_AB;
-  uint64_t* accfull = empty + C::S_AB;
+  uint64_t* bfull = empty + C::S_AB;
+  uint64_t* bempty = bfull + C::S_B;
+  uint64_t* accfull = bempty + C::S_B;
   uint64_t* accempty = accfull + 2;
   uint64_t* drain = accempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -194,7 +201,8 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::S_P; i++) { mbar_init(&pfull[i], 1); mbar_init(&pempty[i], C::kDqPerStage); }
-    for (int i = 0; i < C::S_AB; i++) { mbar_init(&full[i], C::kDqPerStage + 1); mbar_init(&empty[i], NMAT == 2 ? 2 : 1); }
+    for (int i = 0; i < C::S_AB; i++) { mbar_init(&full[i], C::kDqPerStage); mbar_init(&empty[i], NMAT); }
+    for (int i = 0; i < C::S_B; i++) { mbar_init(&bfull[i], 1); mbar_init(&bempty[i], NMAT); }
     for (int i = 0; i < 2; i++) { mbar_init(&accfull[i], C::CH); mbar_init(&accempty[i], C::kEpWarps); }
     mbar_init(drain, C::CH);
     *abort_flag = 0;
@@ -254,21 +262,21 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
         const Chunk ch = args.chunks[u / args.mtiles];
         const int npad = (ch.n + 15) & ~15;
         for (int sb = 0; sb < n_sub && ok; sb++) {
-          if (!(ok = mbar_wait_sleep(&empty[s], ph ^ 1, abort_flag, st, 2, 256))) break;
+          if (!(ok = mbar_wait_sleep(&bempty[s], ph ^ 1, abort_flag, st, 2, 256))) break;
           uint8_t* slot = smem + C::OFF_B + s * C::B_SLOT;
-          mbar_arrive_expect_tx(&full[s], NB * (C::KS / 64) * npad * 128);
+          mbar_arrive_expect_tx(&bfull[s], NB * (C::KS / 64) * npad * 128);
           for (int b = 0; b < NB; b++)
             for (int h = 0; h < C::KS / 64; h++)
               for (int rb = 0; rb < npad; rb += 16)
-                tma_load_2d(slot + (b * (C::KS / 64) + h) * C::B_HALF + rb * 128, &tm.act[b], &full[s],
+                tma_load_2d(slot + (b * (C::KS / 64) + h) * C::B_HALF + rb * 128, &tm.act[b], &bfull[s],
                             sb * C::KS + h * 64, ch.p0 + rb);
           issued++;
-          if (++s == C::S_AB) { s = 0; ph ^= 1; }
+          if (++s == C::S_B) { s = 0; ph ^= 1; }
         }
       }
-      for (int i = 0; i < C::S_AB && i < issued; i++) {
-        if (--s < 0) { s = C::S_AB - 1; ph ^= 1; }
-        mbar_wait_sleep(&full[s], ph, abort_flag, st, 12, 256);
+      for (int i = 0; i < C::S_B && i < issued; i++) {   // drain: bytes of the last stages landed
+        if (--s < 0) { s = C::S_B - 1; ph ^= 1; }
+        mbar_wait_sleep(&bfull[s], ph, abort_flag, st, 12, 256);
       }
     }
   } else if (warp < C::kDqWarp0 || warp >= C::kIssuerWarpX) {
@@ -280,7 +288,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
     const int c = warp < C::kDqWarp0 ? warp - C::kIssuerWarp0 : 2 + warp - C::kIssuerWarpX;
     if (c < C::CH) {
       const int mat = c / C::PM, kc = c % C::PM;
-      int s = 0, ab = 0;
+      int s = 0, bs = 0, ab = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const Chunk ch = args.chunks[u / args.mtiles];
@@ -296,7 +304,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
               tc_fence_after();
               const uint32_t a_tmem = tmem + C::A_BASE + s * C::A_STAGE_COLS + mat * (C::KS / 2);
               const uint32_t b_addr =
-                  smem_u32(smem + C::OFF_B + s * C::B_SLOT) + (NB == 2 ? mat : 0) * (C::KS / 64) * C::B_HALF;
+                  smem_u32(smem + C::OFF_B + bs * C::B_SLOT) + (NB == 2 ? mat : 0) * (C::KS / 64) * C::B_HALF;
 #pragma unroll
               for (int kk = 0; kk < C::KS / 16; kk++) {
                 const uint64_t bdesc =
@@ -304,11 +312,13 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
                 mma_f16_ts(d, a_tmem + kk * 8, bdesc, idesc, first ? 0u : 1u);
                 first = false;
               }
-              mma_commit(&empty[s]);
+              mma_commit(&empty[s]);    // A slot free once these MMAs completed
+              mma_commit(&bempty[bs]);  // and the activation slot
             }
             __syncwarp();
           }
           if (++s == C::S_AB) s = 0;
+          if (++bs == C::S_B) bs = 0;
         }
         if (lane == 0) mma_commit(&accfull[ab]);
         __syncwarp();
@@ -322,21 +332,25 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
     }
   } else if (warp == C::kWatchWarp) {
     // ------------------------------------------------------------------ stage watcher
-    // Waits (bounded) for each ring stage to fill (dequant warps + activation TMA) and for
+    // Waits (bounded) for each ring stage to fill (A: dequant warps; B: activation TMA) and for
     // each unit's accumulator buffer to drain (epilogue), then releases the issuer(s) of that
     // stage through named barrier (stage slot, issuer). It never leaves the loop early and
     // never blocks without a bound, so every barrier an issuer syncs on gets its arrival,
     // also after an abort (when the waits return at once).
-    int s = 0, ab = 0;
-    uint32_t ph = 0, abph = 0;
+    int s = 0, bs = 0, ab = 0;
+    uint32_t ph = 0, bph = 0, abph = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
       if (lane == 0) mbar_wait(&accempty[ab], abph ^ 1, abort_flag, st, 3);
       __syncwarp();
       for (int sb = 0; sb < n_sub; sb++) {
-        if (lane == 0) mbar_wait(&full[s], ph, abort_flag, st, 4);
+        if (lane == 0) {
+          mbar_wait(&bfull[bs], bph, abort_flag, st, 5);
+          mbar_wait(&full[s], ph, abort_flag, st, 4);
+        }
         __syncwarp();
         for (int mat = 0; mat < NMAT; mat++) named_bar_arrive(C::ready_bar(s, mat), 64);
         if (++s == C::S_AB) { s = 0; ph ^= 1; }
+        if (++bs == C::S_B) { bs = 0; bph ^= 1; }
       }
       if (++ab == C::NACC) { ab = 0; abph ^= 1; }
     }
