@@ -135,6 +135,8 @@ struct GemmCfg {
   static constexpr int SEGW = GROUPS;                     // segments a warp decodes per stage
   static_assert((kDqWarps / 4) % GROUPS == 0 && (kDqWarps / 4 / GROUPS) * SEGW == 4, "segment cover");
   static constexpr int kDqPerStage = kDqWarps / GROUPS;   // warps that fill one stage
+  // a dequant group may wait on a stage up to GROUPS - 1 stages ahead of the others; a ring
+  // shorter than that would let a parity wait match a phase one ring cycle early
   static constexpr int TMEM_COLS0 = A_BASE + S_AB * A_STAGE_COLS;
   static constexpr int TMEM_COLS = TMEM_COLS0 <= 32 ? 32 : TMEM_COLS0 <= 64 ? 64 : TMEM_COLS0 <= 128 ? 128
                                    : TMEM_COLS0 <= 256 ? 256 : 512;
@@ -148,6 +150,7 @@ struct GemmCfg {
   static constexpr int S_P0 = (AVAIL - S_B * B_SLOT) / P_STAGE;
   static constexpr int S_P = S_P0 > 10 ? 10 : S_P0;
   static_assert(S_P >= 2, "shared memory budget");
+  static_assert(S_P >= GROUPS && S_AB >= GROUPS, "ring shorter than the dequant stage groups");
   static constexpr int OFF_B = 0;
   static constexpr int OFF_P = OFF_B + S_B * B_SLOT;
   static constexpr int OFF_BAR = OFF_P + S_P * P_STAGE;
