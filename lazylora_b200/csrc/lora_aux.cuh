@@ -88,54 +88,81 @@ __global__ void k_skinny_reduce(const float* __restrict__ part, int nsplit, int 
 // out[t][c] = [sum_j Y[pos_j][c], pairs of t in ascending expert order]
 //           + alpha * (sum_rr L0[t][rr] R0(rr, c) + sum_rr L1[t][rr] R1(rr, c))
 // R(rr, c): RROWS -> R[rr*C + c] ([r][C]);  else R[c*r + rr] ([C][r]).
-// Block: 128 columns x 8 tokens; the R slices are staged in shared memory once per block.
-constexpr int kExTok = 8, kExCols = 128;
+// Block: 512 columns (4 a thread, 16-byte loads and stores) x 8 tokens; the R slices of the
+// block's columns are staged in shared memory once and reused by the 8 tokens, and a
+// token's k rows of Y are all requested before the first is added (k <= 8 per batch), so the
+// kernel streams Y at memory speed instead of one dependent load at a time.
+constexpr int kExTok = 8, kExThreads = 128, kExCols = 4 * kExThreads;
 
 template <bool RROWS, bool HASY, bool TWO>
-__global__ void __launch_bounds__(kExCols) k_expand(const int* __restrict__ tok_pos, const float* __restrict__ Y, int k,
-                                                int T, int C, int r, float alpha, const float* __restrict__ L0,
-                                                const float* __restrict__ R0, const float* __restrict__ L1,
-                                                const float* __restrict__ R1, float* __restrict__ out) {
-  __shared__ float Rs[2][32][kExCols];
+__global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ tok_pos, const float* __restrict__ Y, int k,
+                                                   int T, int C, int r, float alpha, const float* __restrict__ L0,
+                                                   const float* __restrict__ R0, const float* __restrict__ L1,
+                                                   const float* __restrict__ R1, float* __restrict__ out) {
+  extern __shared__ float ex_smem[];
+  float* Rs = ex_smem;                                   // [TWO ? 2 : 1][r][kExCols]
   __shared__ float Ls[2][kExTok][32];
   __shared__ int ps[kExTok][32];
   const int c0 = blockIdx.x * kExCols, t0 = blockIdx.y * kExTok;
   const int nc = min(kExCols, C - c0);
   for (int w = 0; w < (TWO ? 2 : 1); w++) {
     const float* R = w == 0 ? R0 : R1;
-    for (int i = threadIdx.x; i < r * kExCols; i += kExCols) {
-      int rr, c;
-      if (RROWS) { rr = i / kExCols; c = i % kExCols; } else { c = i / r; rr = i % r; }
-      Rs[w][rr][c] = c < nc ? (RROWS ? R[(int64_t)rr * C + c0 + c] : R[(int64_t)(c0 + c) * r + rr]) : 0.f;
+    float* Rw = Rs + (size_t)w * r * kExCols;
+    if (RROWS) {
+      for (int i = threadIdx.x; i < r * kExCols; i += kExThreads) {
+        const int rr = i / kExCols, c = i % kExCols;
+        Rw[rr * kExCols + c] = c < nc ? R[(int64_t)rr * C + c0 + c] : 0.f;
+      }
+    } else {   // [C][r]: the block's columns are one contiguous run of kExCols * r floats
+      for (int i = threadIdx.x; i < r * kExCols; i += kExThreads) {
+        const int c = i / r, rr = i % r;
+        Rw[rr * kExCols + c] = c < nc ? R[(int64_t)(c0 + c) * r + rr] : 0.f;
+      }
     }
     const float* Lm = w == 0 ? L0 : L1;
-    for (int i = threadIdx.x; i < kExTok * r; i += kExCols) {
+    for (int i = threadIdx.x; i < kExTok * r; i += kExThreads) {
       const int tt = i / r, rr = i % r;
       Ls[w][tt][rr] = (t0 + tt < T) ? Lm[(int64_t)(t0 + tt) * r + rr] : 0.f;
     }
   }
   if (HASY)
-    for (int i = threadIdx.x; i < kExTok * k; i += kExCols) {
+    for (int i = threadIdx.x; i < kExTok * k; i += kExThreads) {
       const int tt = i / k, j = i % k;
       ps[tt][j] = (t0 + tt < T) ? tok_pos[(int64_t)(t0 + tt) * k + j] : -1;
     }
   __syncthreads();
-  const int c = threadIdx.x;
+  const int c = 4 * threadIdx.x;
   if (c >= nc) return;
   for (int tt = 0; tt < kExTok && t0 + tt < T; tt++) {
-    float acc = 0.f;
-    if (HASY)
-      for (int j = 0; j < k; j++) {
-        const int p = ps[tt][j];
-        if (p < 0) break;
-        acc += Y[(int64_t)p * C + c0 + c];
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (HASY) {
+      for (int j0 = 0; j0 < k; j0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {                    // all requests first
+          const int p = j0 + j < k ? ps[tt][j0 + j] : -1;
+          v[j] = p >= 0 ? *reinterpret_cast<const float4*>(Y + (int64_t)p * C + c0 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {                    // then the sum, in slot order
+          acc.x += v[j].x; acc.y += v[j].y; acc.z += v[j].z; acc.w += v[j].w;
+        }
       }
-    float lo = 0.f;
-    for (int rr = 0; rr < r; rr++) {
-      lo = fmaf(Ls[0][tt][rr], Rs[0][rr][c], lo);
-      if (TWO) lo = fmaf(Ls[1][tt][rr], Rs[1][rr][c], lo);
     }
-    out[(int64_t)(t0 + tt) * C + c0 + c] = acc + alpha * lo;
+    float4 lo = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int rr = 0; rr < r; rr++) {
+      const float l0 = Ls[0][tt][rr];
+      const float4 r0 = *reinterpret_cast<const float4*>(Rs + rr * kExCols + c);
+      lo.x = fmaf(l0, r0.x, lo.x); lo.y = fmaf(l0, r0.y, lo.y); lo.z = fmaf(l0, r0.z, lo.z); lo.w = fmaf(l0, r0.w, lo.w);
+      if (TWO) {
+        const float l1 = Ls[1][tt][rr];
+        const float4 r1 = *reinterpret_cast<const float4*>(Rs + (r + rr) * kExCols + c);
+        lo.x = fmaf(l1, r1.x, lo.x); lo.y = fmaf(l1, r1.y, lo.y); lo.z = fmaf(l1, r1.z, lo.z); lo.w = fmaf(l1, r1.w, lo.w);
+      }
+    }
+    float4 o;
+    o.x = acc.x + alpha * lo.x; o.y = acc.y + alpha * lo.y; o.z = acc.z + alpha * lo.z; o.w = acc.w + alpha * lo.w;
+    *reinterpret_cast<float4*>(out + (int64_t)(t0 + tt) * C + c0 + c) = o;
   }
 }
 

@@ -367,9 +367,16 @@ static int skinny(const void* A, int adt, bool brows, int M, int K, const float*
 // Rank-r expand with the optional ascending-expert sum of per-pair rows (see k_expand).
 static int expand(bool rrows, const int* tok_pos, const float* Y, int k, int T, int C, int r, float alpha,
                   const float* L0, const float* R0, const float* L1, const float* R1, float* out, cudaStream_t s) {
+  if (C % 4 || r > 32) return LL_ERR_ARG;
   dim3 grid((C + kExCols - 1) / kExCols, (T + kExTok - 1) / kExTok);
   const bool hasy = Y != nullptr, two = L1 != nullptr;
-#define LL_EX(RR, HY, TW) k_expand<RR, HY, TW><<<grid, kExCols, 0, s>>>(tok_pos, Y, k, T, C, r, alpha, L0, R0, L1, R1, out)
+  const int smem = (two ? 2 : 1) * r * kExCols * (int)sizeof(float);   // <= 128 KB at r = 32
+  auto attr = [&](const void* f) { return set_smem_attr(f, smem); };
+#define LL_EX(RR, HY, TW)                                                                                   \
+  do {                                                                                                      \
+    LL_TRY(attr(reinterpret_cast<const void*>(k_expand<RR, HY, TW>)));                                     \
+    k_expand<RR, HY, TW><<<grid, kExThreads, smem, s>>>(tok_pos, Y, k, T, C, r, alpha, L0, R0, L1, R1, out); \
+  } while (0)
   if (rrows) {
     if (hasy) { if (two) LL_EX(true, true, true); else LL_EX(true, true, false); }
     else { if (two) LL_EX(true, false, true); else LL_EX(true, false, false); }
