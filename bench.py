@@ -449,6 +449,102 @@ def run_decode(args, cfg, rank, local, world, dist):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------ streaming (configs[4])
+def run_stream(args, cfg, rank, local, world, dist):
+    """configs[4]: an 8-layer fwd + bwd whose expert weights live in pinned host memory and
+    are streamed into HBM for every use (2 x 8 layer loads a step), group by group on a copy
+    stream while the previous group computes. --stream-distinct N keeps N distinct layers
+    pinned (the host RAM bound); layer l uses distinct layer l % N, so the bytes moved per
+    step are those of 8 layers either way. Reports tokens/s, the achieved host->device GB/s,
+    and the share of the compute hidden under the copies."""
+    from lazylora_b200.core.moe_router import KimiK3MoERouter
+    from lazylora_b200.synthetic import make_layer_device
+    from lazylora_b200.trainer.expert_streamer import (ExpertStreamer, HostExpertStore, streamed_backward,
+                                                       streamed_forward)
+    from lazylora_b200.trainer.routed_experts import RoutedExpertsLayer
+    dev = torch.device("cuda", local)
+    n_layers, D = 8, max(1, args.stream_distinct)
+    store = HostExpertStore()
+    inp = None
+    for l in range(D):
+        inp = make_layer_device(cfg if l == 0 else cfg.__class__(**{**cfg.__dict__, "seed": cfg.seed + 100 * l}),
+                                device=dev)
+        store.add_layer(l, {n: inp[n] for n in ("w1p", "w1s", "w3p", "w3s", "w2p", "w2s")})
+        if l + 1 < D:
+            del inp
+            torch.cuda.empty_cache()
+    lora = {n: inp[n] for n in ("A_g", "B_g", "A_u", "B_u", "A_d", "B_d")}
+    x = inp["x"].to(torch.bfloat16).contiguous()
+    g = inp["g"].to(torch.bfloat16).contiguous()
+    Wr, br = inp["router_w"], inp["router_b"]
+    router = KimiK3MoERouter(hidden_size=cfg.d, num_experts=cfg.E, top_k=cfg.k, device=dev)
+    stream = torch.cuda.current_stream()
+
+    # compute alone: one layer fwd + bwd with its weights resident
+    res = RoutedExpertsLayer(*(inp[n] for n in ("w1p", "w1s", "w3p", "w3s", "w2p", "w2s")), *(lora[n] for n in (
+        "A_g", "B_g", "A_u", "B_u", "A_d", "B_d")), cfg.scaling)
+    idx, w = router.forward(x, weight=Wr, bias=br)
+    for _ in range(2):
+        res.forward(x, idx, w); res.backward(x, idx, w, g)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(3):
+        res.forward(x, idx, w); res.backward(x, idx, w, g)
+    b.record(stream)
+    torch.cuda.synchronize()
+    compute_layer_ms = a.elapsed_time(b) / 3
+    del res, inp
+    torch.cuda.empty_cache()
+
+    streamer = ExpertStreamer(store, lora, cfg.scaling, group_experts=args.stream_group, device=dev)
+
+    every = list(range(cfg.E))   # T * k = 16384 slots over 896 experts: every expert is active
+
+    def step():
+        saved = []
+        for l in range(n_layers):
+            i, ww = router.forward(x, weight=Wr, bias=br)
+            streamer.prefetch((l + 1) % D if l + 1 < n_layers else (n_layers - 1) % D, every)
+            out, ids = streamed_forward(streamer, l % D, x, i, ww, expert_ids=every)
+            saved.append((i, ww, ids))
+        for l in reversed(range(n_layers)):
+            i, ww, ids = saved[l]
+            if l > 0:
+                streamer.prefetch((l - 1) % D, saved[l - 1][2])
+            streamed_backward(streamer, l % D, x, i, ww, g, ids)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    b0 = streamer.bytes_copied
+    with ClockSampler(local) as clk:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            step()
+        b.record(stream)
+        torch.cuda.synchronize()
+    step_ms = a.elapsed_time(b) / args.steps
+    bytes_step = (streamer.bytes_copied - b0) / args.steps
+    h2d = bytes_step / (step_ms * 1e-3) / 1e9
+    compute_ms = 2 * n_layers * compute_layer_ms / 2       # fwd+bwd of 8 layers (resident-weight time)
+    copy_ms = bytes_step / (args.h2d_peak * 1e9) * 1e3
+    hidden = max(0.0, min(1.0, (copy_ms + compute_ms - step_ms) / compute_ms)) if compute_ms > 0 else None
+    line = {"metric": "streamed 8-layer MoE fwd+bwd tokens/s (configs[4], weights in pinned host memory)",
+            "value": cfg.T / (step_ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "dtype": "fp16 operands / fp32 "
+            "accumulate", "data": "synthetic",
+            "config": {"workload": "configs[4]: 8 layers, T=2048, r=64, every layer's experts streamed host->HBM "
+                                   "for the forward and again for the backward",
+                       "d": cfg.d, "f": cfg.f, "E": cfg.E, "k": cfg.k, "T": cfg.T, "r": cfg.r,
+                       "distinct_pinned_layers": D, "group_experts": args.stream_group},
+            "h2d": {"bytes_per_step": bytes_step, "achieved_GBps": h2d, "peak_GBps": args.h2d_peak,
+                    "frac": h2d / args.h2d_peak, "peak_kind": "measured pinned cudaMemcpyAsync on this box"},
+            "compute_ms_resident": compute_ms, "copy_ms_at_peak": copy_ms, "compute_hidden_frac": hidden,
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -461,6 +557,10 @@ def main():
     ap.add_argument("--decode", action="store_true", help="forward-only decode steps (configs[3]: c3_t1/4/16)")
     ap.add_argument("--graph", action="store_true", help="with --decode: replay each step as a CUDA graph")
     ap.add_argument("--zipf-gamma", type=float, default=None, help="override the config's Zipf bias scale")
+    ap.add_argument("--stream", action="store_true", help="configs[4]: experts streamed from pinned host memory")
+    ap.add_argument("--stream-distinct", type=int, default=1, help="distinct layers kept in pinned host memory")
+    ap.add_argument("--stream-group", type=int, default=224, help="experts per streamed group")
+    ap.add_argument("--h2d-peak", type=float, default=55.6, help="measured pinned H2D GB/s of the box")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     from dataclasses import replace
@@ -474,6 +574,8 @@ def main():
             run_reference(args, cfg, rank, world, dist)   # rank 0 only; no collective
         elif args.decode:
             run_decode(args, cfg, rank, local, world, dist)
+        elif args.stream:
+            run_stream(args, cfg, rank, local, world, dist)
         else:
             run_ours(args, cfg, rank, local, world, dist)
             if dist is not None:

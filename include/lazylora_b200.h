@@ -112,7 +112,7 @@ typedef struct {
   int d;          /* expert input width (K of gate/up), multiple of 128 */
   int f;          /* expert intermediate width, multiple of 128 */
   int E;          /* experts resident in these arrays (local experts under expert parallelism) */
-  int r;          /* LoRA rank, 1..32 */
+  int r;          /* LoRA rank, 1..64 */
   float lora_scaling;          /* alpha / r */
   const uint8_t* w1p;  const uint8_t* w1s;   /* gate  [E,f,d/2], scales [E,f,*] */
   const uint8_t* w3p;  const uint8_t* w3s;   /* up    [E,f,d/2], scales [E,f,*] */

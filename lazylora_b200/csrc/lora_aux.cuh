@@ -14,7 +14,7 @@ LL_DEV float load_as_float(const void* p, int64_t i) {
 }
 
 // ---------------------------------------------------------------- skinny split-K GEMM
-// part[split][m][n] = sum_{k in split} A[m][k] * B(k, n),  n < N <= 32.
+// part[split][m][n] = sum_{k in split} A[m][k] * B(k, n); blockIdx.y picks 32 of the N columns.
 // B(k, n): BROWS -> n < N0 ? B0[n*K + k] : B1[(n-N0)*K + k]  ([N][K], e.g. LoRA A matrices)
 //          else  -> B0[k*N + n]                             ([K][N], e.g. LoRA B matrices)
 // Tile 64 rows x 32 columns x 64 k per step; thread = 2 rows x 4 columns.
@@ -26,7 +26,7 @@ __global__ void __launch_bounds__(256) k_skinny(const void* __restrict__ A, int 
                                                 int N, int kc, float* __restrict__ part) {
   __shared__ float As[kSkBK][kSkBM + 4];
   __shared__ float Bs[kSkBK][kSkBN + 4];
-  const int m0 = blockIdx.x * kSkBM;
+  const int m0 = blockIdx.x * kSkBM, nb0 = blockIdx.y * kSkBN;
   const int k_begin = blockIdx.z * kc, k_end = min(K, k_begin + kc);
   const int tm = threadIdx.x / 8, tn = threadIdx.x % 8;   // rows tm, tm+32; columns 4tn..4tn+3
   float acc[2][4] = {};
@@ -39,11 +39,11 @@ __global__ void __launch_bounds__(256) k_skinny(const void* __restrict__ A, int 
     for (int i = threadIdx.x; i < kSkBN * kSkBK; i += 256) {
       int n, c;
       if (BROWS) { n = i / kSkBK; c = i % kSkBK; } else { c = i / kSkBN; n = i % kSkBN; }
-      const int k = k0 + c;
+      const int k = k0 + c, ng = nb0 + n;
       float v = 0.f;
-      if (n < N && k < k_end) {
-        if (BROWS) v = n < N0 ? B0[(int64_t)n * K + k] : B1[(int64_t)(n - N0) * K + k];
-        else v = B0[(int64_t)k * N + n];
+      if (ng < N && k < k_end) {
+        if (BROWS) v = ng < N0 ? B0[(int64_t)ng * K + k] : B1[(int64_t)(ng - N0) * K + k];
+        else v = B0[(int64_t)k * N + ng];
       }
       Bs[c][n] = v;
     }
@@ -66,7 +66,7 @@ __global__ void __launch_bounds__(256) k_skinny(const void* __restrict__ A, int 
     if (m >= M) continue;
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-      const int n = tn * 4 + j;
+      const int n = nb0 + tn * 4 + j;
       if (n < N) out[(int64_t)m * N + n] = acc[i][j];
     }
   }
@@ -94,46 +94,62 @@ __global__ void k_skinny_reduce(const float* __restrict__ part, int nsplit, int 
 // kernel streams Y at memory speed instead of one dependent load at a time.
 constexpr int kExTok = 8, kExThreads = 128, kExCols = 4 * kExThreads;
 
+constexpr int kExMaxR = 64;
+
 template <bool RROWS, bool HASY, bool TWO>
 __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ tok_pos, const float* __restrict__ Y, int k,
                                                    int T, int C, int r, float alpha, const float* __restrict__ L0,
                                                    const float* __restrict__ R0, const float* __restrict__ L1,
                                                    const float* __restrict__ R1, float* __restrict__ out) {
-  extern __shared__ float ex_smem[];
-  float* Rs = ex_smem;                                   // [TWO ? 2 : 1][r][kExCols]
-  __shared__ float Ls[2][kExTok][32];
+  extern __shared__ float Rs[];                          // [r][kExCols], one R at a time
+  __shared__ float Ls[kExTok][kExMaxR];
   __shared__ int ps[kExTok][32];
   const int c0 = blockIdx.x * kExCols, t0 = blockIdx.y * kExTok;
   const int nc = min(kExCols, C - c0);
-  for (int w = 0; w < (TWO ? 2 : 1); w++) {
-    const float* R = w == 0 ? R0 : R1;
-    float* Rw = Rs + (size_t)w * r * kExCols;
-    if (RROWS) {
-      for (int i = threadIdx.x; i < r * kExCols; i += kExThreads) {
-        const int rr = i / kExCols, c = i % kExCols;
-        Rw[rr * kExCols + c] = c < nc ? R[(int64_t)rr * C + c0 + c] : 0.f;
-      }
-    } else {   // [C][r]: the block's columns are one contiguous run of kExCols * r floats
-      for (int i = threadIdx.x; i < r * kExCols; i += kExThreads) {
-        const int c = i / r, rr = i % r;
-        Rw[rr * kExCols + c] = c < nc ? R[(int64_t)(c0 + c) * r + rr] : 0.f;
-      }
-    }
-    const float* Lm = w == 0 ? L0 : L1;
-    for (int i = threadIdx.x; i < kExTok * r; i += kExThreads) {
-      const int tt = i / r, rr = i % r;
-      Ls[w][tt][rr] = (t0 + tt < T) ? Lm[(int64_t)(t0 + tt) * r + rr] : 0.f;
-    }
-  }
+  const int c = 4 * threadIdx.x;
   if (HASY)
     for (int i = threadIdx.x; i < kExTok * k; i += kExThreads) {
       const int tt = i / k, j = i % k;
       ps[tt][j] = (t0 + tt < T) ? tok_pos[(int64_t)(t0 + tt) * k + j] : -1;
     }
-  __syncthreads();
-  const int c = 4 * threadIdx.x;
+  float4 lo[kExTok];
+#pragma unroll
+  for (int tt = 0; tt < kExTok; tt++) lo[tt] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int w = 0; w < (TWO ? 2 : 1); w++) {
+    const float* R = w == 0 ? R0 : R1;
+    const float* Lm = w == 0 ? L0 : L1;
+    __syncthreads();                                     // the previous R is no longer read
+    if (RROWS) {
+      for (int i = threadIdx.x; i < r * kExCols; i += kExThreads) {
+        const int rr = i / kExCols, cc = i % kExCols;
+        Rs[rr * kExCols + cc] = cc < nc ? R[(int64_t)rr * C + c0 + cc] : 0.f;
+      }
+    } else {   // [C][r]: the block's columns are one contiguous run of kExCols * r floats
+      for (int i = threadIdx.x; i < r * kExCols; i += kExThreads) {
+        const int cc = i / r, rr = i % r;
+        Rs[rr * kExCols + cc] = cc < nc ? R[(int64_t)(c0 + cc) * r + rr] : 0.f;
+      }
+    }
+    for (int i = threadIdx.x; i < kExTok * r; i += kExThreads) {
+      const int tt = i / r, rr = i % r;
+      Ls[tt][rr] = (t0 + tt < T) ? Lm[(int64_t)(t0 + tt) * r + rr] : 0.f;
+    }
+    __syncthreads();
+    if (c < nc)
+      for (int rr = 0; rr < r; rr++) {
+        const float4 rv = *reinterpret_cast<const float4*>(Rs + rr * kExCols + c);
+#pragma unroll
+        for (int tt = 0; tt < kExTok; tt++) {
+          const float l = Ls[tt][rr];
+          lo[tt].x = fmaf(l, rv.x, lo[tt].x); lo[tt].y = fmaf(l, rv.y, lo[tt].y);
+          lo[tt].z = fmaf(l, rv.z, lo[tt].z); lo[tt].w = fmaf(l, rv.w, lo[tt].w);
+        }
+      }
+  }
   if (c >= nc) return;
-  for (int tt = 0; tt < kExTok && t0 + tt < T; tt++) {
+#pragma unroll
+  for (int tt = 0; tt < kExTok; tt++) {
+    if (t0 + tt >= T) break;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     if (HASY) {
       for (int j0 = 0; j0 < k; j0 += 8) {
@@ -149,25 +165,16 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
         }
       }
     }
-    float4 lo = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int rr = 0; rr < r; rr++) {
-      const float l0 = Ls[0][tt][rr];
-      const float4 r0 = *reinterpret_cast<const float4*>(Rs + rr * kExCols + c);
-      lo.x = fmaf(l0, r0.x, lo.x); lo.y = fmaf(l0, r0.y, lo.y); lo.z = fmaf(l0, r0.z, lo.z); lo.w = fmaf(l0, r0.w, lo.w);
-      if (TWO) {
-        const float l1 = Ls[1][tt][rr];
-        const float4 r1 = *reinterpret_cast<const float4*>(Rs + (r + rr) * kExCols + c);
-        lo.x = fmaf(l1, r1.x, lo.x); lo.y = fmaf(l1, r1.y, lo.y); lo.z = fmaf(l1, r1.z, lo.z); lo.w = fmaf(l1, r1.w, lo.w);
-      }
-    }
     float4 o;
-    o.x = acc.x + alpha * lo.x; o.y = acc.y + alpha * lo.y; o.z = acc.z + alpha * lo.z; o.w = acc.w + alpha * lo.w;
+    o.x = acc.x + alpha * lo[tt].x; o.y = acc.y + alpha * lo[tt].y;
+    o.z = acc.z + alpha * lo[tt].z; o.w = acc.w + alpha * lo[tt].w;
     *reinterpret_cast<float4*>(out + (int64_t)(t0 + tt) * C + c0 + c) = o;
   }
 }
 
 // --------------------------------------------------------------- outer-product sums
-// part[seg][rr][c] = sum_{n in seg} Pm(n, rr) * Q[n][c]; 4 consecutive columns per thread.
+// part[seg][rr][c] = sum_{n in seg} Pm(n, rr) * Q[n][c]; 4 consecutive columns per thread,
+// ranks rr = 32 blockIdx.z .. + 31 (any r, 32 at a time).
 // Pm: [N][r] fp32, or (PGATHER) tw[n] * Pm[perm_token[n]][rr]. Q dtype QDT (0 f32, 1 bf16, 2 f16).
 template <int QDT, bool PGATHER>
 __global__ void __launch_bounds__(64) k_outer4(const float* __restrict__ Pm, const int* __restrict__ perm_token,
@@ -176,6 +183,7 @@ __global__ void __launch_bounds__(64) k_outer4(const float* __restrict__ Pm, con
                                                float* __restrict__ part) {
   const int c = (blockIdx.x * 64 + threadIdx.x) * 4;
   const int seg = blockIdx.y;
+  const int rb = blockIdx.z * 32, rn = min(32, r - rb);   // this block's ranks
   const int n_total = n_dev ? *n_dev : N;
   const int per = (n_total + nseg - 1) / nseg;
   const int n0 = seg * per, n1 = min(n_total, n0 + per);
@@ -185,11 +193,11 @@ __global__ void __launch_bounds__(64) k_outer4(const float* __restrict__ Pm, con
   for (int i = 0; i < 32; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   for (int nb = n0; nb < n1; nb += 16) {
     __syncthreads();
-    for (int i = threadIdx.x; i < 16 * r; i += 64) {
-      const int nn = i / r, rr = i % r;
+    for (int i = threadIdx.x; i < 16 * rn; i += 64) {
+      const int nn = i / rn, rr = i % rn;
       const int n = nb + nn;
       float v = 0.f;
-      if (n < n1) v = PGATHER ? tw[n] * Pm[(int64_t)perm_token[n] * r + rr] : Pm[(int64_t)n * r + rr];
+      if (n < n1) v = PGATHER ? tw[n] * Pm[(int64_t)perm_token[n] * r + rb + rr] : Pm[(int64_t)n * r + rb + rr];
       ps[nn][rr] = v;
     }
     __syncthreads();
@@ -215,7 +223,7 @@ __global__ void __launch_bounds__(64) k_outer4(const float* __restrict__ Pm, con
         }
 #pragma unroll
         for (int i = 0; i < 32; i++) {
-          if (i < r) {
+          if (i < rn) {
             const float p = ps[nn][i];
             acc[i][0] = fmaf(p, q0, acc[i][0]);
             acc[i][1] = fmaf(p, q1, acc[i][1]);
@@ -229,8 +237,8 @@ __global__ void __launch_bounds__(64) k_outer4(const float* __restrict__ Pm, con
   if (c < C) {
 #pragma unroll
     for (int i = 0; i < 32; i++)
-      if (i < r)
-        *reinterpret_cast<float4*>(part + ((int64_t)seg * r + i) * C + c) =
+      if (i < rn)
+        *reinterpret_cast<float4*>(part + ((int64_t)seg * r + rb + i) * C + c) =
             make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
   }
 }

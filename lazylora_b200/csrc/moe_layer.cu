@@ -314,9 +314,10 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   w.hg = c.take<float>((size_t)T * r);
   w.hu = c.take<float>((size_t)T * r);
   w.opart = c.take<float>((size_t)nseg_max * r * (d > f ? d : f));
-  {  // split-K partials of the skinny products: at most ~2 * SMs / mblocks splits of >= 64
+  {  // split-K partials of the skinny products: nsplit <= ceil(2 * SMs / mblocks), so
+     // nsplit * M <= 2 * SMs * 64 + M + 64 rows of at most 2r columns (SMs <= 160)
     const int64_t rows = P > T ? P : T;
-    w.skpart = c.take<float>((size_t)(2 * 160 + 64) * 64 * 64 + (size_t)rows * 2 * r * 8);
+    w.skpart = c.take<float>(((size_t)2 * 160 * 64 + rows + 64) * 2 * r);
   }
   if (out) *out = w;
   return c.off + 256;
@@ -325,7 +326,7 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
 static int validate(const ll_moe_layer* L, int T, int k) {
   if (!L || T <= 0 || k <= 0 || k > 32) return LL_ERR_ARG;
   if (L->d <= 0 || L->f <= 0 || L->d % 128 || L->f % 128 || L->E <= 0 || L->E > 8192) return LL_ERR_ARG;
-  if (L->r <= 0 || L->r > 32) return LL_ERR_ARG;
+  if (L->r <= 0 || L->r > kExMaxR) return LL_ERR_ARG;
   if (L->s13_stride < L->d / 32 || L->s13_stride % 16 || L->s2_stride < L->f / 32 || L->s2_stride % 16) return LL_ERR_ARG;
   if (!L->w1p || !L->w1s || !L->w3p || !L->w3s || !L->w2p || !L->w2s || !L->beta) return LL_ERR_ARG;
   if (!L->A_g || !L->B_g || !L->A_u || !L->B_u || !L->A_d || !L->B_d) return LL_ERR_ARG;
@@ -350,7 +351,7 @@ static int skinny(const void* A, int adt, bool brows, int M, int K, const float*
   nsplit = std::max(1, std::min(nsplit, (K + kSkBK - 1) / kSkBK));
   const int kc = ((K + nsplit - 1) / nsplit + kSkBK - 1) / kSkBK * kSkBK;
   nsplit = (K + kc - 1) / kc;
-  dim3 grid(mblocks, 1, nsplit);
+  dim3 grid(mblocks, (N + kSkBN - 1) / kSkBN, nsplit);
 #define LL_SK(ADT, BR) k_skinny<ADT, BR><<<grid, 256, 0, s>>>(A, M, K, K, B0, B1, N0, N, kc, part)
   if (brows) {
     if (adt == 0) LL_SK(0, true); else if (adt == 1) LL_SK(1, true); else LL_SK(2, true);
@@ -367,10 +368,10 @@ static int skinny(const void* A, int adt, bool brows, int M, int K, const float*
 // Rank-r expand with the optional ascending-expert sum of per-pair rows (see k_expand).
 static int expand(bool rrows, const int* tok_pos, const float* Y, int k, int T, int C, int r, float alpha,
                   const float* L0, const float* R0, const float* L1, const float* R1, float* out, cudaStream_t s) {
-  if (C % 4 || r > 32) return LL_ERR_ARG;
+  if (C % 4 || r > kExMaxR || k > 32) return LL_ERR_ARG;
   dim3 grid((C + kExCols - 1) / kExCols, (T + kExTok - 1) / kExTok);
   const bool hasy = Y != nullptr, two = L1 != nullptr;
-  const int smem = (two ? 2 : 1) * r * kExCols * (int)sizeof(float);   // <= 128 KB at r = 32
+  const int smem = r * kExCols * (int)sizeof(float);   // <= 128 KB at r = 64
   auto attr = [&](const void* f) { return set_smem_attr(f, smem); };
 #define LL_EX(RR, HY, TW)                                                                                   \
   do {                                                                                                      \
@@ -396,7 +397,7 @@ static int outer(const float* Pm, const int* perm_token, const float* tw, const 
   int nseg = (2 * device_info().sms + cblocks - 1) / cblocks;
   nseg = std::max(1, std::min(nseg, nseg_max));
   nseg = std::min(nseg, std::max(1, N / 16));
-  dim3 grid(cblocks, nseg);
+  dim3 grid(cblocks, nseg, (r + 31) / 32);
   const bool pg = perm_token != nullptr;
 #define LL_OU(QD, PG) k_outer4<QD, PG><<<grid, 64, 0, s>>>(Pm, perm_token, tw, Q, N, n_dev, C, r, nseg, part)
   if (pg) {

@@ -170,3 +170,19 @@ def test_full_width_deterministic(c1_layer):
     b = _run(layer, x, idx, w, g)
     for key in KEYS:
         assert torch.equal(a[key], b[key]), key
+
+
+@pytest.mark.parametrize("r,T", [(64, 48), (48, 40), (8, 600)])
+def test_lora_rank_and_many_tokens_vs_oracle(r, T):
+    """LoRA ranks above 32 (configs[4] uses r = 64; the rank-r kernels work 32 ranks at a
+    time) and a token count that takes the 128-row tile path, against the oracle."""
+    from lazylora_b200.trainer.routed_experts import RoutedExpertsLayer
+    cfg = dataclasses.replace(CONFIGS["small"], r=r, T=T)
+    inp = make_layer(cfg)
+    layer = RoutedExpertsLayer.from_inputs(inp, cfg.scaling)
+    idx, w = O.route(inp["x"].float(), inp["router_w"], inp["router_b"], cfg.k)
+    want = _oracle(inp, idx, w, inp["g"].float(), cfg.scaling)
+    x = inp["x"].cuda().to(torch.bfloat16)
+    got = _run(layer, x, idx.cuda(), w.cuda(), inp["g"].cuda().to(torch.bfloat16))
+    for key in KEYS:
+        assert O.rel_l2(got[key].cpu(), want[key]) <= TOL, f"r={r} T={T} {key}"
