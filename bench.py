@@ -42,8 +42,8 @@ UNIT = "tokens/s"
 # from one ncu capture of the same kernels at d=7168, f=2048, 64 experts, 9 tokens per expert.
 # Weight reads dominate, so a launch's traffic scales with the number of experts it touches.
 NCU_DRAM_BYTES_PER_EXPERT = {
-    (7168, 2048): [(1021.256e6 + 13.821184e6) / 64, (501.545e6 + 17.194752e6) / 64,
-                   (547.218e6 + 11.422208e6) / 64, (1061.840e6 + 18.673664e6) / 64],
+    (7168, 2048): [(1020.520e6 + 17.177344e6) / 64, (501.553e6 + 18.935040e6) / 64,
+                   (546.961e6 + 11.003392e6) / 64, (1061.981e6 + 19.554304e6) / 64],
 }
 
 
@@ -228,7 +228,7 @@ def run_ours(args, cfg, rank, local, world, dist):
 
     def step(xx, gg):
         idx, w = router.forward(xx, weight=Wr, bias=br)
-        n = 2                                   # router: logits + select
+        n = lib.ll_last_launch_count()          # router kernels
         if ep is not None:
             l0 = ep.ops.launches
             out = ep.forward(xx, idx, w)
@@ -399,9 +399,10 @@ def run_decode(args, cfg, rank, local, world, dist):
 
     def step():
         idx, w = router.forward(x, weight=Wr, bias=br)
+        n = lib.ll_last_launch_count()
         state["idx"] = idx
         state["out"] = layer.forward(x, idx, w)
-        state["n"] = 2 + lib.ll_last_launch_count()
+        state["n"] = n + lib.ll_last_launch_count()
 
     for _ in range(args.warmup):
         step()

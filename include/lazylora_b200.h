@@ -213,7 +213,8 @@ int ll_ep_combine_slots(float* grad_w, const float* part, const int* pos, const 
  * launches; n = 0 turns it off. Calling it again restarts at i = 0. */
 int ll_profile_gemm_events(void* const* events, int n);
 
-/* Number of kernel launches the last ll_moe_forward / ll_moe_backward on this thread made. */
+/* Number of kernel launches the last ll_moe_forward / ll_moe_backward / ll_route_topk on this
+ * thread made. */
 int ll_last_launch_count(void);
 
 #ifdef __cplusplus

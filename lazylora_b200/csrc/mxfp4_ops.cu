@@ -200,6 +200,71 @@ __global__ void k_rows_to_half(const void* __restrict__ src, const int* __restri
   }
 }
 
+// The same, one pass: each thread holds up to 4 chunks of 8 values of the row in registers
+// (16- or 32-byte loads, 16-byte stores), K % 8 == 0 and K <= 8 * 4 * blockDim.x.
+template <int SRC>
+__global__ void __launch_bounds__(256) k_rows_to_half_v(const void* __restrict__ src, const int* __restrict__ index,
+                                                        int rows, int K, __half* __restrict__ dst,
+                                                        float* __restrict__ inv) {
+  const int row = blockIdx.x;
+  if (row >= rows) return;
+  const int sr = index ? index[row] : row;
+  const int nch = K / 8;
+  float v[4][8];
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int ch = threadIdx.x + i * blockDim.x;
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[i][j] = 0.f;
+    if (ch < nch && sr >= 0) {
+      if (SRC == 0) {
+        const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + (int64_t)sr * K) + 2 * ch;
+        const float4 a = p[0], b = p[1];
+        v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+        v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+      } else {
+        const uint4 u = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(src) + (int64_t)sr * K)[ch];
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+          v[i][2 * j] = f.x;
+          v[i][2 * j + 1] = f.y;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) mx = fmaxf(mx, fabsf(v[i][j]));
+    }
+  }
+  __shared__ float red[32];
+  __shared__ float sh_scale;
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = 0.f;
+    for (int i = 0; i < (int)(blockDim.x / 32); i++) m = fmaxf(m, red[i]);
+    const int e = row_scale_exp(m);
+    sh_scale = ldexpf(1.f, e);
+    if (inv) inv[row] = ldexpf(1.f, -e);
+  }
+  __syncthreads();
+  const float sc = sh_scale;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int ch = threadIdx.x + i * blockDim.x;
+    if (ch >= nch) continue;
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const __half2 h = __floats2half2_rn(v[i][2 * j] * sc, v[i][2 * j + 1] * sc);
+      o[j] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    reinterpret_cast<uint4*>(dst + (int64_t)row * K)[ch] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // Transposed copy of an MXFP4 stack for the backward GEMMs. For every expert:
 //   codes_t[c][r/2]  = the E2M1 codes of W[r][c], transposed (element 2j of a row still in
 //                      the low nibble of byte j), and
@@ -270,10 +335,18 @@ int launch_single_expert_chunks(Chunk* chunks, int* n_chunks, int M, int nmax, c
 int launch_rows_to_half(const void* src, int src_dtype, const int* index, int rows, int K, __half* dst, float* inv,
                         cudaStream_t s) {
   if (rows <= 0) return LL_OK;
-  if (src_dtype == 0)
+  const bool vec = K % 8 == 0 && K <= 8 * 4 * 256 && reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(dst) % 16 == 0;
+  if (vec) {
+    if (src_dtype == 0)
+      k_rows_to_half_v<0><<<rows, 256, 0, s>>>(src, index, rows, K, dst, inv);
+    else
+      k_rows_to_half_v<1><<<rows, 256, 0, s>>>(src, index, rows, K, dst, inv);
+  } else if (src_dtype == 0) {
     k_rows_to_half<0><<<rows, 256, 0, s>>>(src, index, rows, K, dst, inv);
-  else
+  } else {
     k_rows_to_half<1><<<rows, 256, 0, s>>>(src, index, rows, K, dst, inv);
+  }
   return check_launch("k_rows_to_half");
 }
 

@@ -107,10 +107,19 @@ static int launch_select(const float* a, const float* b, const float* bias, int 
   return check_launch("k_route_select");
 }
 
+// logits[i] = sum over the nsplit partials of element i, added in split order.
+__global__ void k_sum_partials(const float* __restrict__ part, int nsplit, int64_t n, float* __restrict__ logits) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float acc = part[i];
+  for (int sp = 1; sp < nsplit; sp++) acc += part[(int64_t)sp * n + i];
+  logits[i] = acc;
+}
+
 // ------------------------------------------------------------ tensor-core logits: plan + launch
 struct RouterPlan {
   int BN = 16, NP = 1, mt = 1, nt = 1, nsplit = 1, kbps = 1, kb_total = 1;
-  size_t off_w = 0, off_x = 0, off_part = 0, off_st = 0, bytes = 0;
+  size_t off_w = 0, off_x = 0, off_part = 0, off_logits = 0, off_st = 0, bytes = 0;
 };
 
 static RouterPlan router_plan(int T, int d, int E, int x_dtype) {
@@ -132,6 +141,7 @@ static RouterPlan router_plan(int T, int d, int E, int x_dtype) {
     p.off_w = take((size_t)3 * E * d * 2);
     p.off_x = take(p.NP == 3 ? (size_t)3 * T * d * 2 : 0);
     p.off_part = take((size_t)p.nsplit * T * E * 4);
+    p.off_logits = take((size_t)T * E * 4);
     p.off_st = take(sizeof(DevStatus));
     p.bytes = (off + 255) & ~size_t(255);
   }
@@ -203,10 +213,17 @@ int ll_route_topk(const void* x, int x_dtype, const float* router_w, const float
   const RouterPlan p = router_plan(T, d, E, x_dtype);
   if (ws_bytes < p.bytes) return LL_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  g_launch_count = 0;
   LL_TRY(router_logits_tc(x, x_dtype, router_w, T, d, E, ws, p, s));
   const float* part = reinterpret_cast<const float*>(static_cast<uint8_t*>(ws) + p.off_part);
-  return launch_select<0>(part, nullptr, bias, T, E, k, renormalize, routed_scaling_factor, idx, w, scores_out, s,
-                          p.nsplit);
+  if (p.nsplit > 1) {   // the K splits' partials, summed in split order by a wide kernel
+    float* logits = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + p.off_logits);
+    const int64_t n = (int64_t)T * E;
+    k_sum_partials<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, p.nsplit, n, logits);
+    LL_TRY(check_launch("k_sum_partials"));
+    part = logits;
+  }
+  return launch_select<0>(part, nullptr, bias, T, E, k, renormalize, routed_scaling_factor, idx, w, scores_out, s, 1);
 }
 
 int ll_route_select(const float* scores, const float* scores_for_choice, int T, int E, int k, int renormalize,
