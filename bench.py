@@ -118,6 +118,7 @@ def dist_setup(args):
         local = int(os.environ.get("LOCAL_RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", "1"))
         backend = "nccl" if torch.cuda.is_available() else "gloo"
+        os.environ.setdefault("NCCL_DEBUG", "WARN")   # no version banner on stdout: one JSON line only
         if torch.cuda.is_available():
             torch.cuda.set_device(local)
         dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))

@@ -128,6 +128,10 @@ typedef struct {
    * fp16 multipliers with the decode bias folded in ([E,d/32,f] gate/up, [E,f/32,d] down). */
   const uint8_t* w1t; const uint8_t* w3t; const uint8_t* w2t;
   const uint16_t* s1t; const uint16_t* s3t; const uint16_t* s2t;
+  /* Valid (token, expert) pairs the next forward / backward will see, or 0: taken as T*k. Sets
+   * the token-tile width; give it when many slots are -1 (expert parallelism). The forward and
+   * the backward that follows must see the same value. */
+  int rows_hint;
 } ll_moe_layer;
 
 /* One-time preparation per weight load (the base weights are frozen): the per-expert

@@ -40,6 +40,7 @@ class MoELayerDesc(ctypes.Structure):
         ("A_d", c_void_p), ("B_d", c_void_p),
         ("w1t", c_void_p), ("w3t", c_void_p), ("w2t", c_void_p),
         ("s1t", c_void_p), ("s3t", c_void_p), ("s2t", c_void_p),
+        ("rows_hint", c_int),
     ]
 
 

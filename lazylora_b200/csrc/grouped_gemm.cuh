@@ -76,8 +76,7 @@ struct EpiParams {
   // F2 / B2 / STORE / ACCUM
   float* Y;                   // [P][M] (or [rows][M] for STORE / ACCUM)
   // B1
-  const float* gB;            // [T][r] g . B_d
-  const float* A_d;           // [r][M]
+  const float* lora_d;        // [T][M] (g B_d) A_d: the down adapter's term of dL/dh per token
   const float* Gs;            // saved G
   const float* Us;            // saved U
   float* DG;                  // [P][M]
@@ -102,11 +101,13 @@ struct GemmCfg {
   static constexpr int kIssuerWarpX = 25;                 // issuers 2 and 3 live at warps 25, 26
   // Independent accumulation chains, one MMA issuer warp each: a warp issues one tcgen05.mma
   // per ~50 cycles at small N however many accumulators it rotates, so small-N tiles need
-  // several issuing warps; N = 128 MMAs are long enough for two.
+  // several issuing warps.
 #ifndef LL_CHAINS_SMALL_N
 #define LL_CHAINS_SMALL_N 2
 #endif
-  static constexpr int CH = N_MAX <= 32 ? LL_CHAINS_SMALL_N : 2;
+  // (N = 128 MMAs are long enough for one chain per weight matrix, which leaves room for two
+  // accumulator buffers when there is one matrix, so its epilogue overlaps the next unit)
+  static constexpr int CH = N_MAX <= 32 ? LL_CHAINS_SMALL_N : (N_MAX >= 128 ? NMAT : 2);
   static constexpr int PM = CH / NMAT;                    // chains per weight matrix
   static constexpr int kThreads = (CH > 2 ? 27 : 25) * 32;
   static constexpr int kIssuerWarp0 = 2;
@@ -440,6 +441,20 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;          // accumulator row = M index within the tile
     const EpiParams& ep = args.epi;
+    const int* __restrict__ perm = ep.perm_token;
+    const float* __restrict__ rsi = ep.row_scale_inv;
+    const float* __restrict__ tw = ep.tw;
+    const float* __restrict__ dlt_g = ep.delta_g;
+    const float* __restrict__ dlt_u = ep.delta_u;
+    const float* __restrict__ lora_d = ep.lora_d;
+    const float* __restrict__ Gs = ep.Gs;
+    const float* __restrict__ Us = ep.Us;
+    float* __restrict__ Go = ep.G;
+    float* __restrict__ Uo = ep.U;
+    __half* __restrict__ Ho = ep.H;
+    float* __restrict__ Yo = ep.Y;
+    float* __restrict__ DGo = ep.DG;
+    float* __restrict__ DUo = ep.DU;
     int ab = 0;
     uint32_t abph = 0;
     bool ok = true;
@@ -478,40 +493,68 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
           }
         }
         float gwp[16];
+        // Batches of EB tokens: the per-token indices and scalars of a batch, then its
+        // per-element loads, are all requested before anything is computed or stored (the
+        // pointers are restrict-qualified, so loads are not held behind the stores).
+        constexpr int EB = (EPI == EPI_F1 || EPI == EPI_B1) ? 4 : 8;
 #pragma unroll
-        for (int jj = 0; jj < 16; jj++) {
-          gwp[jj] = 0.f;
-          const int j = j0 + jj;
-          if (j >= ch.n || !mvalid) continue;
-          const int p = ch.p0 + j;
-          const int t = ep.perm_token ? ep.perm_token[p] : p;
-          const size_t o = (size_t)p * ep.M + m;
-          if (EPI == EPI_F1) {
-            const float cs = ep.row_scale_inv[p] * wunscale;
-            const float gate = v0[jj] * cs + ep.delta_g[(size_t)t * ep.M + m];
-            const float up = v1[jj] * cs + ep.delta_u[(size_t)t * ep.M + m];
-            ep.G[o] = gate;
-            ep.U[o] = up;
-            ep.H[o] = __float2half_rn(situ_glu_fwd(gate, up));
-          } else if (EPI == EPI_F2) {
-            ep.Y[o] = v0[jj] * wunscale * ep.tw[p];
-          } else if (EPI == EPI_B1) {
-            const float ys = v0[jj] * ep.row_scale_inv[p] * wunscale;
-            float lorad = 0.f;
-            for (int rr = 0; rr < ep.r; rr++) lorad += ep.gB[(size_t)t * ep.r + rr] * ep.A_d[(size_t)rr * ep.M + m];
-            const float v = ys + ep.lora_scaling * lorad;
-            const float g = ep.Gs[o], uu = ep.Us[o];
-            gwp[jj] = situ_glu_fwd(g, uu) * v;
-            float dg, du;
-            situ_glu_bwd(ep.tw[p] * v, g, uu, dg, du);
-            ep.DG[o] = dg;
-            ep.DU[o] = du;
-          } else if (EPI == EPI_B2) {
-            ep.Y[o] = v0[jj] * ep.row_scale_inv[p] * wunscale;
-          } else if (EPI == EPI_STORE) {
-            ep.Y[o] = v0[jj] * ep.row_scale_inv[p] * wunscale;
-          } else if (EPI == EPI_ACCUM) {
-            ep.Y[o] += v0[jj] * ep.row_scale_inv[p] * wunscale;
+        for (int h = 0; h < 16; h += EB) {
+          int pp[EB];
+          size_t tm[EB];
+          float sc[EB], a0[EB], a1[EB], a2[EB];
+#pragma unroll
+          for (int i = 0; i < EB; i++) {
+            const int j = j0 + h + i;
+            const bool ok = j < ch.n && mvalid;
+            const int p = ch.p0 + j;
+            pp[i] = ok ? p : -1;
+            const int t = ok ? (perm ? perm[p] : p) : 0;
+            tm[i] = (size_t)t * ep.M + m;
+            if (EPI == EPI_F2) sc[i] = ok ? tw[p] : 0.f;
+            else if (EPI == EPI_B1) { sc[i] = ok ? rsi[p] : 0.f; a2[i] = ok ? tw[p] : 0.f; }
+            else sc[i] = ok ? rsi[p] : 0.f;
+          }
+#pragma unroll
+          for (int i = 0; i < EB; i++) {
+            const size_t o = (size_t)(pp[i] < 0 ? 0 : pp[i]) * ep.M + m;
+            if (pp[i] < 0) { a0[i] = a1[i] = 0.f; continue; }
+            if (EPI == EPI_F1) { a0[i] = dlt_g[tm[i]]; a1[i] = dlt_u[tm[i]]; }
+            else if (EPI == EPI_B1) { a0[i] = Gs[o]; a1[i] = Us[o]; sc[i] = sc[i] * wunscale; }
+            else if (EPI == EPI_ACCUM) a0[i] = Yo[o];
+          }
+          float ld[EB];
+          if (EPI == EPI_B1) {
+#pragma unroll
+            for (int i = 0; i < EB; i++) ld[i] = pp[i] < 0 ? 0.f : lora_d[tm[i]];
+          }
+#pragma unroll
+          for (int i = 0; i < EB; i++) {
+            const int jj = h + i;
+            gwp[jj] = 0.f;
+            if (pp[i] < 0) continue;
+            const size_t o = (size_t)pp[i] * ep.M + m;
+            if (EPI == EPI_F1) {
+              const float cs = sc[i] * wunscale;
+              const float gate = v0[jj] * cs + a0[i];
+              const float up = v1[jj] * cs + a1[i];
+              Go[o] = gate;
+              Uo[o] = up;
+              Ho[o] = __float2half_rn(situ_glu_fwd(gate, up));
+            } else if (EPI == EPI_F2) {
+              Yo[o] = v0[jj] * wunscale * sc[i];
+            } else if (EPI == EPI_B1) {
+              const float v = v0[jj] * sc[i] + ep.lora_scaling * ld[i];
+              const float g = a0[i], uu = a1[i];
+              gwp[jj] = situ_glu_fwd(g, uu) * v;
+              float dg, du;
+              situ_glu_bwd(a2[i] * v, g, uu, dg, du);
+              DGo[o] = dg;
+              DUo[o] = du;
+            } else if (EPI == EPI_B2 || EPI == EPI_STORE) {
+              Yo[o] = v0[jj] * sc[i] * wunscale;
+            } else if (EPI == EPI_ACCUM) {
+              Yo[o] = a0[i] + v0[jj] * sc[i] * wunscale;
+            }
           }
         }
         if (EPI == EPI_B1) {

@@ -244,6 +244,7 @@ struct LayerWs {
   float* ginv;
   __half* gh;
   float* gB;
+  float* lora_d;
   float* gw_part;
   float* DG;
   float* DU;
@@ -260,18 +261,20 @@ struct LayerWs {
   int nseg_max;
 };
 
-#ifndef LL_NMAX_SMALL
-#define LL_NMAX_SMALL 32
-#endif
-static int choose_nmax(int T, int k, int E) {
-  const double mean = (double)T * k / (E > 0 ? E : 1);
-  return mean <= 12.0 ? LL_NMAX_SMALL : 128;
+// Token rows per chunk (the MMA N): the smallest tile that holds most experts' rows in one
+// chunk, from the mean valid (token, expert) pairs per expert (L->rows_hint when the caller
+// knows how many of the T * k slots are routed here, else T * k).
+static int choose_nmax(const ll_moe_layer* L, int T, int k) {
+  const int64_t slots = (int64_t)T * k;
+  const int64_t pairs = L->rows_hint > 0 && L->rows_hint < slots ? L->rows_hint : slots;
+  const double mean = (double)pairs / (L->E > 0 ? L->E : 1);
+  return mean <= 12.0 ? 32 : (mean <= 40.0 ? 64 : 128);
 }
 
 static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, LayerWs* out) {
   const int d = L->d, f = L->f, E = L->E, r = L->r;
   const int64_t P = (int64_t)T * k;
-  const int nmax = choose_nmax(T, k, E);
+  const int nmax = choose_nmax(L, T, k);
   const int nblk = (T + kTokBlock - 1) / kTokBlock;
   const int nseg_max = 64;
   Carver c(base);
@@ -281,7 +284,7 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   w.st = c.take<DevStatus>(1);
   w.cnt = c.take<int>((size_t)nblk * E);
   w.offsets = c.take<int>(E + 1);
-  w.chunks = c.take<Chunk>(E + P / nmax + 2);
+  w.chunks = c.take<Chunk>(E + P / 32 + 2);     // enough for any nmax >= 32
   w.n_chunks = c.take<int>(1);
   w.perm_token = c.take<int>(P);
   w.perm_slot = c.take<int>(P);
@@ -303,6 +306,7 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   w.ginv = c.take<float>(P);
   w.gh = c.take<__half>(P * d);
   w.gB = c.take<float>((size_t)T * r);
+  w.lora_d = c.take<float>((size_t)T * f);
   w.gw_part = c.take<float>((size_t)((f + 127) / 128) * 4 * P);
   w.DG = c.take<float>(P * f);
   w.DU = c.take<float>(P * f);
@@ -337,8 +341,8 @@ static int validate(const ll_moe_layer* L, int T, int k) {
 template <int EPI, int NMAT, int NB, bool COLSCALE>
 static int gemm_nmax(int nmax, const CUtensorMap* pk, const CUtensorMap* sc, const CUtensorMap* act, const GemmArgs& a,
                      cudaStream_t s) {
-  if (nmax == 16) return launch_gemm<EPI, NMAT, NB, COLSCALE, 16>(pk, sc, act, a, s);
   if (nmax == 32) return launch_gemm<EPI, NMAT, NB, COLSCALE, 32>(pk, sc, act, a, s);
+  if (nmax == 64) return launch_gemm<EPI, NMAT, NB, COLSCALE, 64>(pk, sc, act, a, s);
   return launch_gemm<EPI, NMAT, NB, COLSCALE, 128>(pk, sc, act, a, s);
 }
 
@@ -548,6 +552,8 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
 
   LL_TRY(launch_rows_to_half(g, g_dtype, W.perm_token, P, d, W.gh, W.ginv, s));
   LL_TRY(skinny(g, g_dtype, false, T, d, L->B_d, nullptr, r, r, 1.f, W.gB, nullptr, W.skpart, s));
+  // the down adapter's term of dL/dh, once per token: (g B_d) A_d [T][f]
+  LL_TRY(expand(true, nullptr, nullptr, k, T, f, r, 1.f, W.gB, L->A_d, nullptr, nullptr, W.lora_d, s));
   // B1: v = g . W2 (+ LoRA down), SiTU-GLU backward
   {
     CUtensorMap pk[1], sc[1], act[1];
@@ -569,8 +575,7 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
     a.epi.M = f;
     a.epi.r = r;
     a.epi.lora_scaling = sc_l;
-    a.epi.gB = W.gB;
-    a.epi.A_d = L->A_d;
+    a.epi.lora_d = W.lora_d;
     a.epi.Gs = W.G;
     a.epi.Us = W.U;
     a.epi.DG = W.DG;

@@ -161,7 +161,10 @@ class ExpertParallelLayer:
                            recv_counts, send_counts)
         self.local_launches = 0
         if R:
-            out_recv = self.local.forward(x_recv, idx_recv, w_recv)
+            kw = {}
+            if getattr(self.local, "accepts_rows_hint", False):   # size the token tiles by the routed slots
+                kw["rows_hint"] = int((idx_recv >= 0).sum().item())
+            out_recv = self.local.forward(x_recv, idx_recv, w_recv, **kw)
             self.local_launches += self._local_count()
         else:
             out_recv = torch.zeros((0, d), dtype=torch.float32, device=x.device)

@@ -115,9 +115,13 @@ class RoutedExpertsLayer:
             return 1
         raise TypeError(f"activations must be float32 or bfloat16, got {t.dtype}")
 
-    def forward(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-        """out[T, d] fp32 = sum over each token's k experts (ascending id) of w * expert(x)."""
+    accepts_rows_hint = True
+
+    def forward(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, rows_hint: Optional[int] = None) -> torch.Tensor:
+        """out[T, d] fp32 = sum over each token's k experts (ascending id) of w * expert(x).
+        rows_hint: how many of the T*k slots are routed (>= 0), when many are -1."""
         L.require_cuda(x, idx, w)
+        self.desc.rows_hint = int(rows_hint) if rows_hint else 0
         x = x.contiguous()
         idx = idx.to(torch.int64).contiguous()
         w = w.to(torch.float32).contiguous()

@@ -172,10 +172,10 @@ def test_full_width_deterministic(c1_layer):
         assert torch.equal(a[key], b[key]), key
 
 
-@pytest.mark.parametrize("r,T", [(64, 48), (48, 40), (8, 600)])
+@pytest.mark.parametrize("r,T", [(64, 48), (48, 40), (8, 600), (16, 120)])
 def test_lora_rank_and_many_tokens_vs_oracle(r, T):
     """LoRA ranks above 32 (configs[4] uses r = 64; the rank-r kernels work 32 ranks at a
-    time) and a token count that takes the 128-row tile path, against the oracle."""
+    time) and token counts that take the 64- and 128-row tile paths, against the oracle."""
     from lazylora_b200.trainer.routed_experts import RoutedExpertsLayer
     cfg = dataclasses.replace(CONFIGS["small"], r=r, T=T)
     inp = make_layer(cfg)
