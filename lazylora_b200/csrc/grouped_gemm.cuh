@@ -496,7 +496,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
         // Batches of EB tokens: the per-token indices and scalars of a batch, then its
         // per-element loads, are all requested before anything is computed or stored (the
         // pointers are restrict-qualified, so loads are not held behind the stores).
-        constexpr int EB = (EPI == EPI_F1 || EPI == EPI_B1) ? 4 : 8;
+        constexpr int EB = EPI == EPI_F1 ? 2 : (EPI == EPI_B1 ? 4 : 8);
 #pragma unroll
         for (int h = 0; h < 16; h += EB) {
           int pp[EB];
