@@ -28,6 +28,8 @@
 // owns the TMEM allocation), 4..19 dequant (four warps per TMEM lane quarter, one per 32-K
 // segment of a 128-K stage), 20..23 epilogue, 24 stage watcher (waits on the mbarriers for
 // the issuers and releases them through named barriers), 25 and 26 two more MMA issuers.
+// A product with one weight matrix (the down projection, its backward, the drop-ins) can
+// run with NMAT = 2 over two adjacent 128-row tiles of the same stack (PAIR below).
 // The issuers accumulate into separate accumulators (chains: gate / up and even / odd K
 // stages, or K stages mod 4), so none waits on another and the sums stay deterministic; the
 // epilogue adds the chains of one product in a fixed order.
@@ -87,7 +89,7 @@ struct EpiParams {
 struct GemmArgs {
   const Chunk* chunks;
   const int* n_chunks;
-  int mtiles;        // ceil(M / 128)
+  int mtiles;        // units per chunk: ceil(M / 128), ceil(M / 256) with paired tiles
   int K;             // reduction length
   int e_rows;        // stored weight rows per expert (= M)
   DevStatus* status;
@@ -107,7 +109,9 @@ struct GemmCfg {
 #endif
   // (N = 128 MMAs are long enough for one chain per weight matrix, which leaves room for two
   // accumulator buffers when there is one matrix, so its epilogue overlaps the next unit)
-  static constexpr int CH = N_MAX <= 32 ? LL_CHAINS_SMALL_N : (N_MAX >= 128 ? NMAT : 2);
+  // At 16-row tiles four chains fit in tensor memory next to a 3-deep A ring, and the issue
+  // rate of one warp (not the tensor pipe) bounds a 16-wide MMA.
+  static constexpr int CH = N_MAX <= 16 ? 4 : N_MAX <= 32 ? LL_CHAINS_SMALL_N : (N_MAX >= 128 ? NMAT : 2);
   static constexpr int PM = CH / NMAT;                    // chains per weight matrix
   static constexpr int kThreads = (CH > 2 ? 27 : 25) * 32;
   static constexpr int kIssuerWarp0 = 2;
@@ -166,17 +170,22 @@ struct GemmCfg {
   static __device__ __forceinline__ int ready_bar(int s, int mat) { return 1 + 2 * s + mat; }
 };
 
-template <int NMAT, int NB>
+template <int NMAT, int N_MAX>
 struct TmaSet {
   CUtensorMap pk[NMAT];
   CUtensorMap sc[NMAT];
-  CUtensorMap act[NB];
+  CUtensorMap act[N_MAX / 16];   // act[c - 1]: one ring stage of a 16 c-row chunk (all operands)
 };
 
 template <int EPI, int NMAT, int NB, bool COLSCALE, int N_MAX>
 __global__ void __launch_bounds__(GemmCfg<NMAT, NB, COLSCALE, N_MAX>::kThreads, 1)
-grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs args) {
+grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, N_MAX> tm, const GemmArgs args) {
   using C = GemmCfg<NMAT, NB, COLSCALE, N_MAX>;
+  // A single-product epilogue with two weight matrices takes two adjacent 128-row tiles of
+  // one stack as its two matrices (both maps name the same stack): one activation stage then
+  // feeds twice the weight bytes, and the per-stage barrier work is paid once per 256 rows.
+  constexpr bool PAIR = NMAT == 2 && EPI != EPI_F1 && EPI != EPI_B2;
+  constexpr int TILE_ROWS = PAIR ? 256 : 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -231,19 +240,20 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const Chunk ch = args.chunks[u / args.mtiles];
         const int mt = u % args.mtiles;
-        const int row = ch.e * args.e_rows + mt * 128;
-        const int grp = (ch.e * args.e_rows) / 32 + mt * 4;
+        const int row = ch.e * args.e_rows + mt * TILE_ROWS;
+        const int grp = (ch.e * args.e_rows) / 32 + mt * (TILE_ROWS / 32);
         for (int ks = 0; ks < n_stage && ok; ks++) {
           if (!(ok = mbar_wait_sleep(&pempty[s], ph ^ 1, abort_flag, st, 1, 256))) break;
           uint8_t* stage = smem + C::OFF_P + s * C::P_STAGE;
           mbar_arrive_expect_tx(&pfull[s], C::P_STAGE);
           for (int i = 0; i < NMAT; i++) {
             uint8_t* pk = stage + i * (C::PK_BYTES + C::SC_BYTES);
-            tma_load_2d(pk, &tm.pk[i], &pfull[s], ks * (C::BK / 2), row);
+            const int r_i = row + (PAIR ? i * 128 : 0);
+            tma_load_2d(pk, &tm.pk[i], &pfull[s], ks * (C::BK / 2), r_i);
             if (COLSCALE)
-              tma_load_2d(pk + C::PK_BYTES, &tm.sc[i], &pfull[s], ks * C::BK, grp);
+              tma_load_2d(pk + C::PK_BYTES, &tm.sc[i], &pfull[s], ks * C::BK, grp + (PAIR ? i * 4 : 0));
             else
-              tma_load_2d(pk + C::PK_BYTES, &tm.sc[i], &pfull[s], ((ks * C::BK) / 32) & ~15, row);
+              tma_load_2d(pk + C::PK_BYTES, &tm.sc[i], &pfull[s], ((ks * C::BK) / 32) & ~15, r_i);
           }
           issued++;
           if (++s == C::S_P) { s = 0; ph ^= 1; }
@@ -257,7 +267,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
   } else if (warp == 1) {
     // -------------------------------------------------------- activation (B) producer
     if (lane == 0) {
-      for (int i = 0; i < NB; i++) tma_prefetch_desc(&tm.act[i]);
+      for (int i = 0; i < N_MAX / 16; i++) tma_prefetch_desc(&tm.act[i]);
       int s = 0;
       uint32_t ph = 0;
       int issued = 0;
@@ -268,12 +278,12 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
         for (int sb = 0; sb < n_sub && ok; sb++) {
           if (!(ok = mbar_wait_sleep(&bempty[s], ph ^ 1, abort_flag, st, 2, 256))) break;
           uint8_t* slot = smem + C::OFF_B + s * C::B_SLOT;
+          // one instruction: [operand][64-K half][npad rows][128 bytes]
           mbar_arrive_expect_tx(&bfull[s], NB * (C::KS / 64) * npad * 128);
-          for (int b = 0; b < NB; b++)
-            for (int h = 0; h < C::KS / 64; h++)
-              for (int rb = 0; rb < npad; rb += 16)
-                tma_load_2d(slot + (b * (C::KS / 64) + h) * C::B_HALF + rb * 128, &tm.act[b], &bfull[s],
-                            sb * C::KS + h * 64, ch.p0 + rb);
+          if (NB == 2)
+            tma_load_4d(slot, &tm.act[npad / 16 - 1], &bfull[s], 0, ch.p0, sb * (C::KS / 64), 0);
+          else
+            tma_load_3d(slot, &tm.act[npad / 16 - 1], &bfull[s], 0, ch.p0, sb * (C::KS / 64));
           issued++;
           if (++s == C::S_B) { s = 0; ph ^= 1; }
         }
@@ -307,12 +317,13 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
             if (lane == 0) {
               tc_fence_after();
               const uint32_t a_tmem = tmem + C::A_BASE + s * C::A_STAGE_COLS + mat * (C::KS / 2);
+              const uint32_t half_bytes = (uint32_t)npad * 128;   // one 64-K half of the chunk's rows
               const uint32_t b_addr =
-                  smem_u32(smem + C::OFF_B + bs * C::B_SLOT) + (NB == 2 ? mat : 0) * (C::KS / 64) * C::B_HALF;
+                  smem_u32(smem + C::OFF_B + bs * C::B_SLOT) + (NB == 2 ? mat : 0) * (C::KS / 64) * half_bytes;
 #pragma unroll
               for (int kk = 0; kk < C::KS / 16; kk++) {
                 const uint64_t bdesc =
-                    umma_desc(b_addr + (kk >> 2) * C::B_HALF + (kk & 3) * 32, 16, 1024, kSwizzle128B);
+                    umma_desc(b_addr + (kk >> 2) * half_bytes + (kk & 3) * 32, 16, 1024, kSwizzle128B);
                 mma_f16_ts(d, a_tmem + kk * 8, bdesc, idesc, first ? 0u : 1u);
                 first = false;
               }
@@ -460,116 +471,122 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, NB> tm, const GemmArgs a
     bool ok = true;
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
       const Chunk ch = args.chunks[u / args.mtiles];
-      const int mt = u % args.mtiles;
-      const int m = mt * 128 + row;
-      const bool mvalid = m < ep.M;
       const int npad = (ch.n + 15) & ~15;
       const int bias = ep.beta ? ep.beta[ch.e * 2 + ep.beta_col] : 0;
       const float wunscale = exp2f((float)(-bias));
       if (!(ok = mbar_wait_sleep(&accfull[ab], abph, abort_flag, st, 8, 512))) break;
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * C::CH * N_MAX;
-      for (int j0 = 0; j0 < npad; j0 += 16) {
-        // v0 = sum of matrix 0's chains (all chains unless F1), v1 = matrix 1's (F1: up)
-        float v0[16], v1[16], t[16];
-        tmem_ld16(tbase + j0, v0);
-        tmem_ld_wait();
-        if (EPI == EPI_F1) {
-          tmem_ld16(tbase + C::PM * N_MAX + j0, v1);
+#pragma unroll 1
+      for (int pm = 0; pm < (PAIR ? 2 : 1); pm++) {
+        const int mt = (u % args.mtiles) * (PAIR ? 2 : 1) + pm;   // 128-row tile of the output
+        const int m = mt * 128 + row;
+        const bool mvalid = m < ep.M;
+        const int c0 = PAIR ? pm * C::PM : 0;                     // first chain of this product
+        const int c1 = PAIR ? c0 + C::PM : C::CH;
+        for (int j0 = 0; j0 < npad; j0 += 16) {
+          // v0 = sum of matrix 0's chains (all chains unless F1 or paired tiles), v1 = matrix
+          // 1's (F1: up)
+          float v0[16], v1[16], t[16];
+          tmem_ld16(tbase + c0 * N_MAX + j0, v0);
           tmem_ld_wait();
-        }
-        for (int cc = 1; cc < C::CH; cc++) {
-          const int kc = cc % C::PM;
-          if (kc >= chains_used) continue;        // a chain that got no stage holds no sum
-          if (EPI == EPI_F1 && kc == 0) continue; // first chain of matrix 1, loaded above
-          tmem_ld16(tbase + cc * N_MAX + j0, t);
-          tmem_ld_wait();
-          if (EPI == EPI_F1 && cc >= C::PM) {
-#pragma unroll
-            for (int jj = 0; jj < 16; jj++) v1[jj] += t[jj];
-          } else {
-#pragma unroll
-            for (int jj = 0; jj < 16; jj++) v0[jj] += t[jj];
+          if (EPI == EPI_F1) {
+            tmem_ld16(tbase + C::PM * N_MAX + j0, v1);
+            tmem_ld_wait();
           }
-        }
-        float gwp[16];
-        // Batches of EB tokens: the per-token indices and scalars of a batch, then its
-        // per-element loads, are all requested before anything is computed or stored (the
-        // pointers are restrict-qualified, so loads are not held behind the stores).
-        constexpr int EB = EPI == EPI_F1 ? 2 : (EPI == EPI_B1 ? 4 : 8);
+          for (int cc = c0 + 1; cc < c1; cc++) {
+            const int kc = cc % C::PM;
+            if (kc >= chains_used) continue;        // a chain that got no stage holds no sum
+            if (EPI == EPI_F1 && kc == 0) continue; // first chain of matrix 1, loaded above
+            tmem_ld16(tbase + cc * N_MAX + j0, t);
+            tmem_ld_wait();
+            if (EPI == EPI_F1 && cc >= C::PM) {
 #pragma unroll
-        for (int h = 0; h < 16; h += EB) {
-          int pp[EB];
-          size_t tm[EB];
-          float sc[EB], a0[EB], a1[EB], a2[EB];
+              for (int jj = 0; jj < 16; jj++) v1[jj] += t[jj];
+            } else {
 #pragma unroll
-          for (int i = 0; i < EB; i++) {
-            const int j = j0 + h + i;
-            const bool ok = j < ch.n && mvalid;
-            const int p = ch.p0 + j;
-            pp[i] = ok ? p : -1;
-            const int t = ok ? (perm ? perm[p] : p) : 0;
-            tm[i] = (size_t)t * ep.M + m;
-            if (EPI == EPI_F2) sc[i] = ok ? tw[p] : 0.f;
-            else if (EPI == EPI_B1) { sc[i] = ok ? rsi[p] : 0.f; a2[i] = ok ? tw[p] : 0.f; }
-            else sc[i] = ok ? rsi[p] : 0.f;
-          }
-#pragma unroll
-          for (int i = 0; i < EB; i++) {
-            const size_t o = (size_t)(pp[i] < 0 ? 0 : pp[i]) * ep.M + m;
-            if (pp[i] < 0) { a0[i] = a1[i] = 0.f; continue; }
-            if (EPI == EPI_F1) { a0[i] = dlt_g[tm[i]]; a1[i] = dlt_u[tm[i]]; }
-            else if (EPI == EPI_B1) { a0[i] = Gs[o]; a1[i] = Us[o]; sc[i] = sc[i] * wunscale; }
-            else if (EPI == EPI_ACCUM) a0[i] = Yo[o];
-          }
-          float ld[EB];
-          if (EPI == EPI_B1) {
-#pragma unroll
-            for (int i = 0; i < EB; i++) ld[i] = pp[i] < 0 ? 0.f : lora_d[tm[i]];
-          }
-#pragma unroll
-          for (int i = 0; i < EB; i++) {
-            const int jj = h + i;
-            gwp[jj] = 0.f;
-            if (pp[i] < 0) continue;
-            const size_t o = (size_t)pp[i] * ep.M + m;
-            if (EPI == EPI_F1) {
-              const float cs = sc[i] * wunscale;
-              const float gate = v0[jj] * cs + a0[i];
-              const float up = v1[jj] * cs + a1[i];
-              Go[o] = gate;
-              Uo[o] = up;
-              Ho[o] = __float2half_rn(situ_glu_fwd(gate, up));
-            } else if (EPI == EPI_F2) {
-              Yo[o] = v0[jj] * wunscale * sc[i];
-            } else if (EPI == EPI_B1) {
-              const float v = v0[jj] * sc[i] + ep.lora_scaling * ld[i];
-              const float g = a0[i], uu = a1[i];
-              gwp[jj] = situ_glu_fwd(g, uu) * v;
-              float dg, du;
-              situ_glu_bwd(a2[i] * v, g, uu, dg, du);
-              DGo[o] = dg;
-              DUo[o] = du;
-            } else if (EPI == EPI_B2 || EPI == EPI_STORE) {
-              Yo[o] = v0[jj] * sc[i] * wunscale;
-            } else if (EPI == EPI_ACCUM) {
-              Yo[o] = a0[i] + v0[jj] * sc[i] * wunscale;
+              for (int jj = 0; jj < 16; jj++) v0[jj] += t[jj];
             }
           }
-        }
-        if (EPI == EPI_B1) {
-          // grad_w partial over this warp's 32 rows (fixed shuffle order); the four warps of
-          // the tile write separate partials, summed later in a fixed order.
-          float mine = 0.f;
+          float gwp[16];
+          // Batches of EB tokens: the per-token indices and scalars of a batch, then its
+          // per-element loads, are all requested before anything is computed or stored (the
+          // pointers are restrict-qualified, so loads are not held behind the stores).
+          constexpr int EB = (EPI == EPI_F1 || (EPI == EPI_B1 && PAIR)) ? 2 : (EPI == EPI_B1 ? 4 : 8);
 #pragma unroll
-          for (int jj = 0; jj < 16; jj++) {
-            float s = gwp[jj];
+          for (int h = 0; h < 16; h += EB) {
+            int pp[EB];
+            size_t tm[EB];
+            float sc[EB], a0[EB], a1[EB], a2[EB];
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-            if (jj == lane) mine = s;
+            for (int i = 0; i < EB; i++) {
+              const int j = j0 + h + i;
+              const bool ok = j < ch.n && mvalid;
+              const int p = ch.p0 + j;
+              pp[i] = ok ? p : -1;
+              const int t = ok ? (perm ? perm[p] : p) : 0;
+              tm[i] = (size_t)t * ep.M + m;
+              if (EPI == EPI_F2) sc[i] = ok ? tw[p] : 0.f;
+              else if (EPI == EPI_B1) { sc[i] = ok ? rsi[p] : 0.f; a2[i] = ok ? tw[p] : 0.f; }
+              else sc[i] = ok ? rsi[p] : 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < EB; i++) {
+              const size_t o = (size_t)(pp[i] < 0 ? 0 : pp[i]) * ep.M + m;
+              if (pp[i] < 0) { a0[i] = a1[i] = 0.f; continue; }
+              if (EPI == EPI_F1) { a0[i] = dlt_g[tm[i]]; a1[i] = dlt_u[tm[i]]; }
+              else if (EPI == EPI_B1) { a0[i] = Gs[o]; a1[i] = Us[o]; sc[i] = sc[i] * wunscale; }
+              else if (EPI == EPI_ACCUM) a0[i] = Yo[o];
+            }
+            float ld[EB];
+            if (EPI == EPI_B1) {
+#pragma unroll
+              for (int i = 0; i < EB; i++) ld[i] = pp[i] < 0 ? 0.f : lora_d[tm[i]];
+            }
+#pragma unroll
+            for (int i = 0; i < EB; i++) {
+              const int jj = h + i;
+              gwp[jj] = 0.f;
+              if (pp[i] < 0) continue;
+              const size_t o = (size_t)pp[i] * ep.M + m;
+              if (EPI == EPI_F1) {
+                const float cs = sc[i] * wunscale;
+                const float gate = v0[jj] * cs + a0[i];
+                const float up = v1[jj] * cs + a1[i];
+                Go[o] = gate;
+                Uo[o] = up;
+                Ho[o] = __float2half_rn(situ_glu_fwd(gate, up));
+              } else if (EPI == EPI_F2) {
+                Yo[o] = v0[jj] * wunscale * sc[i];
+              } else if (EPI == EPI_B1) {
+                const float v = v0[jj] * sc[i] + ep.lora_scaling * ld[i];
+                const float g = a0[i], uu = a1[i];
+                gwp[jj] = situ_glu_fwd(g, uu) * v;
+                float dg, du;
+                situ_glu_bwd(a2[i] * v, g, uu, dg, du);
+                DGo[o] = dg;
+                DUo[o] = du;
+              } else if (EPI == EPI_B2 || EPI == EPI_STORE) {
+                Yo[o] = v0[jj] * sc[i] * wunscale;
+              } else if (EPI == EPI_ACCUM) {
+                Yo[o] = a0[i] + v0[jj] * sc[i] * wunscale;
+              }
+            }
           }
-          if (lane < 16 && j0 + lane < ch.n)
-            ep.gw_part[((size_t)mt * 4 + q) * ep.P + ch.p0 + j0 + lane] = mine;
+          if (EPI == EPI_B1) {
+            // grad_w partial over this warp's 32 rows (fixed shuffle order); the four warps of
+            // the tile write separate partials, summed later in a fixed order.
+            float mine = 0.f;
+#pragma unroll
+            for (int jj = 0; jj < 16; jj++) {
+              float s = gwp[jj];
+#pragma unroll
+              for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+              if (jj == lane) mine = s;
+            }
+            if (lane < 16 && j0 + lane < ch.n && mt * 128 < ep.M)
+              ep.gw_part[((size_t)mt * 4 + q) * ep.P + ch.p0 + j0 + lane] = mine;
+          }
         }
       }
       tc_fence_before();

@@ -75,10 +75,26 @@ inline int make_colscale_maps(CUtensorMap* pk, CUtensorMap* sc, const uint8_t* c
   return LL_OK;
 }
 
-// fp16 activation rows [rows][K], K-major 128-byte-swizzled boxes of 16 rows x 64 columns.
-inline int make_act_map(CUtensorMap* m, const __half* base, int64_t rows, int K) {
-  return make_map_2d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base, (uint64_t)K, (uint64_t)rows, (uint64_t)K * 2, 64, 16,
-                     CU_TENSOR_MAP_SWIZZLE_128B);
+int make_map_nd(CUtensorMap* m, CUtensorMapDataType dt, const void* base, int rank, const uint64_t* dims,
+                const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle sw);
+
+// fp16 activation rows [rows][K] (K % 64 == 0), one map per tile height 16 c (c = 1..n): a
+// box holds one 128-K ring stage as two 64-column halves, [half][16 c rows][128 bytes], K-major
+// with the 128-byte swizzle, so a stage of a chunk of up to 16 c rows is one TMA instruction.
+// The halves are a third dimension of stride 128 bytes. With nb = 2 a fourth dimension of
+// stride mat_stride elements reaches the second operand (the gate and up gradients), and the
+// box is [operand][half][rows][128 bytes].
+inline int make_act_maps(CUtensorMap* maps, int n, const __half* base, int64_t rows, int K, int nb = 1,
+                         int64_t mat_stride = 0) {
+  if (K <= 0 || K % 64 || n < 1 || n > 8 || (nb != 1 && nb != 2)) return LL_ERR_ARG;
+  const uint64_t dims[4] = {64, (uint64_t)rows, (uint64_t)K / 64, (uint64_t)nb};
+  const uint64_t strides[3] = {(uint64_t)K * 2, 128, (uint64_t)mat_stride * 2};
+  for (int c = 1; c <= n; c++) {
+    const uint32_t box[4] = {64, (uint32_t)(16 * c), 2, (uint32_t)nb};
+    LL_TRY(make_map_nd(&maps[c - 1], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base, nb == 2 ? 4 : 3, dims, strides, box,
+                       CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  return LL_OK;
 }
 
 int set_smem_attr(const void* func, int bytes);
@@ -87,9 +103,9 @@ template <int EPI, int NMAT, int NB, bool COLSCALE, int N_MAX>
 int launch_gemm(const CUtensorMap* pk, const CUtensorMap* sc, const CUtensorMap* act, const GemmArgs& a,
                 cudaStream_t stream) {
   using Cfg = GemmCfg<NMAT, NB, COLSCALE, N_MAX>;
-  TmaSet<NMAT, NB> tm;
+  TmaSet<NMAT, N_MAX> tm;
   for (int i = 0; i < NMAT; i++) { tm.pk[i] = pk[i]; tm.sc[i] = sc[i]; }
-  for (int i = 0; i < NB; i++) tm.act[i] = act[i];
+  for (int i = 0; i < N_MAX / 16; i++) tm.act[i] = act[i];
   auto kern = grouped_mxfp4_gemm<EPI, NMAT, NB, COLSCALE, N_MAX>;
   LL_TRY(set_smem_attr(reinterpret_cast<const void*>(kern), Cfg::SMEM));
   const DeviceInfo di = device_info();

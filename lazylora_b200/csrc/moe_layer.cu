@@ -268,7 +268,7 @@ static int choose_nmax(const ll_moe_layer* L, int T, int k) {
   const int64_t slots = (int64_t)T * k;
   const int64_t pairs = L->rows_hint > 0 && L->rows_hint < slots ? L->rows_hint : slots;
   const double mean = (double)pairs / (L->E > 0 ? L->E : 1);
-  return mean <= 12.0 ? 32 : (mean <= 40.0 ? 64 : 128);
+  return mean <= 10.0 ? 16 : mean <= 12.0 ? 32 : (mean <= 40.0 ? 64 : 128);
 }
 
 static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, LayerWs* out) {
@@ -284,7 +284,7 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   w.st = c.take<DevStatus>(1);
   w.cnt = c.take<int>((size_t)nblk * E);
   w.offsets = c.take<int>(E + 1);
-  w.chunks = c.take<Chunk>(E + P / 32 + 2);     // enough for any nmax >= 32
+  w.chunks = c.take<Chunk>(E + P / 16 + 2);     // enough for any nmax >= 16
   w.n_chunks = c.take<int>(1);
   w.perm_token = c.take<int>(P);
   w.perm_slot = c.take<int>(P);
@@ -311,8 +311,8 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   w.DG = c.take<float>(P * f);
   w.DU = c.take<float>(P * f);
   w.rinv = c.take<float>(P);
-  w.DGh = c.take<__half>(P * f);
-  w.DUh = c.take<__half>(P * f);
+  w.DGh = c.take<__half>(2 * P * f);            // DG rows then DU rows: one 4-D tensor map reads both
+  w.DUh = w.DGh ? w.DGh + P * f : nullptr;
   w.Dg = c.take<float>((size_t)T * f);
   w.Du = c.take<float>((size_t)T * f);
   w.hg = c.take<float>((size_t)T * r);
@@ -341,6 +341,7 @@ static int validate(const ll_moe_layer* L, int T, int k) {
 template <int EPI, int NMAT, int NB, bool COLSCALE>
 static int gemm_nmax(int nmax, const CUtensorMap* pk, const CUtensorMap* sc, const CUtensorMap* act, const GemmArgs& a,
                      cudaStream_t s) {
+  if (nmax == 16) return launch_gemm<EPI, NMAT, NB, COLSCALE, 16>(pk, sc, act, a, s);
   if (nmax == 32) return launch_gemm<EPI, NMAT, NB, COLSCALE, 32>(pk, sc, act, a, s);
   if (nmax == 64) return launch_gemm<EPI, NMAT, NB, COLSCALE, 64>(pk, sc, act, a, s);
   return launch_gemm<EPI, NMAT, NB, COLSCALE, 128>(pk, sc, act, a, s);
@@ -476,10 +477,10 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_u, L->B_u, nullptr, nullptr, W.dlt_u, s));
   // F1: gate / up
   {
-    CUtensorMap pk[2], sc[2], act[1];
+    CUtensorMap pk[2], sc[2], act[8];
     LL_TRY(make_rowscale_maps(&pk[0], &sc[0], L->w1p, L->w1s, (int64_t)E * f, d, L->s13_stride));
     LL_TRY(make_rowscale_maps(&pk[1], &sc[1], L->w3p, L->w3s, (int64_t)E * f, d, L->s13_stride));
-    LL_TRY(make_act_map(&act[0], W.xh, P, d));
+    LL_TRY(make_act_maps(act, W.nmax / 16, W.xh, P, d));
     GemmArgs a{};
     a.chunks = W.chunks;
     a.n_chunks = W.n_chunks;
@@ -510,13 +511,15 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   }
   // F2: down
   {
-    CUtensorMap pk[1], sc[1], act[1];
+    CUtensorMap pk[2], sc[2], act[8];
     LL_TRY(make_rowscale_maps(&pk[0], &sc[0], L->w2p, L->w2s, (int64_t)E * d, f, L->s2_stride));
-    LL_TRY(make_act_map(&act[0], W.H, P, f));
+    pk[1] = pk[0];
+    sc[1] = sc[0];
+    LL_TRY(make_act_maps(act, W.nmax / 16, W.H, P, f));
     GemmArgs a{};
     a.chunks = W.chunks;
     a.n_chunks = W.n_chunks;
-    a.mtiles = d / 128;
+    a.mtiles = (d + 255) / 256;                 // paired 128-row tiles
     a.K = f;
     a.e_rows = d;
     a.status = W.st;
@@ -527,7 +530,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
     a.epi.P = P;
     a.epi.M = d;
     a.epi.Y = W.Y;
-    LL_TRY((gemm_nmax<EPI_F2, 1, 1, false>(W.nmax, pk, sc, act, a, s)));
+    LL_TRY((gemm_nmax<EPI_F2, 2, 1, false>(W.nmax, pk, sc, act, a, s)));
   }
   return expand(false, W.tok_pos, W.Y, k, T, d, r, L->lora_scaling, W.q, L->B_d, nullptr, nullptr, out, s);
 }
@@ -556,13 +559,18 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
   LL_TRY(expand(true, nullptr, nullptr, k, T, f, r, 1.f, W.gB, L->A_d, nullptr, nullptr, W.lora_d, s));
   // B1: v = g . W2 (+ LoRA down), SiTU-GLU backward
   {
-    CUtensorMap pk[1], sc[1], act[1];
+    CUtensorMap pk[2], sc[2], act[8];
     LL_TRY(make_colscale_maps(&pk[0], &sc[0], L->w2t, reinterpret_cast<const __half*>(L->s2t), (int64_t)E * f, d));
-    LL_TRY(make_act_map(&act[0], W.gh, P, d));
+    pk[1] = pk[0];
+    sc[1] = sc[0];
+    LL_TRY(make_act_maps(act, W.nmax / 16, W.gh, P, d));
     GemmArgs a{};
     a.chunks = W.chunks;
     a.n_chunks = W.n_chunks;
-    a.mtiles = f / 128;
+    // paired 128-row tiles, except at 128-token tiles: there two accumulators of 128 columns
+    // leave tensor memory for one buffer only, and this epilogue is too heavy to run exposed
+    const bool pair = W.nmax < 128;
+    a.mtiles = pair ? (f + 255) / 256 : f / 128;
     a.K = d;
     a.e_rows = f;
     a.status = W.st;
@@ -581,17 +589,23 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
     a.epi.DG = W.DG;
     a.epi.DU = W.DU;
     a.epi.gw_part = W.gw_part;
-    LL_TRY((gemm_nmax<EPI_B1, 1, 1, true>(W.nmax, pk, sc, act, a, s)));
+    if (!pair)
+      LL_TRY((launch_gemm<EPI_B1, 1, 1, true, 128>(pk, sc, act, a, s)));
+    else if (W.nmax == 16)
+      LL_TRY((launch_gemm<EPI_B1, 2, 1, true, 16>(pk, sc, act, a, s)));
+    else if (W.nmax == 32)
+      LL_TRY((launch_gemm<EPI_B1, 2, 1, true, 32>(pk, sc, act, a, s)));
+    else
+      LL_TRY((launch_gemm<EPI_B1, 2, 1, true, 64>(pk, sc, act, a, s)));
   }
   k_pair_rows_half<<<P, 256, 0, s>>>(W.DG, W.DU, f, n_valid, W.DGh, W.DUh, W.rinv);
   LL_TRY(check_launch("k_pair_rows_half"));
   // B2: dX = dg . W1 + du . W3
   {
-    CUtensorMap pk[2], sc[2], act[2];
+    CUtensorMap pk[2], sc[2], act[8];
     LL_TRY(make_colscale_maps(&pk[0], &sc[0], L->w1t, reinterpret_cast<const __half*>(L->s1t), (int64_t)E * d, f));
     LL_TRY(make_colscale_maps(&pk[1], &sc[1], L->w3t, reinterpret_cast<const __half*>(L->s3t), (int64_t)E * d, f));
-    LL_TRY(make_act_map(&act[0], W.DGh, P, f));
-    LL_TRY(make_act_map(&act[1], W.DUh, P, f));
+    LL_TRY(make_act_maps(act, W.nmax / 16, W.DGh, P, f, 2, (int64_t)(W.DUh - W.DGh)));
     GemmArgs a{};
     a.chunks = W.chunks;
     a.n_chunks = W.n_chunks;

@@ -46,25 +46,39 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-int make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t dim0, uint64_t dim1,
-                uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle sw) {
+int make_map_nd(CUtensorMap* m, CUtensorMapDataType dt, const void* base, int rank, const uint64_t* dims,
+                const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle sw) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "cuTensorMapEncodeTiled unavailable");
     return LL_ERR_CUDA;
   }
-  if ((reinterpret_cast<uintptr_t>(base) & 15) || (stride1_bytes & 15)) return LL_ERR_ARG;
-  cuuint64_t dims[2] = {dim0, dim1};
-  cuuint64_t strides[1] = {stride1_bytes};
-  cuuint32_t box[2] = {box0, box1};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+  if (rank < 1 || rank > 5 || (reinterpret_cast<uintptr_t>(base) & 15)) return LL_ERR_ARG;
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], estr[5];
+  for (int i = 0; i < rank; i++) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    estr[i] = 1;
+    if (i + 1 < rank) {
+      if (strides_bytes[i] & 15) return LL_ERR_ARG;
+      st[i] = strides_bytes[i];
+    }
+  }
+  CUresult r = fn(m, dt, (cuuint32_t)rank, const_cast<void*>(base), d, st, b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return LL_ERR_ARG;
   }
   return LL_OK;
+}
+
+int make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t dim0, uint64_t dim1,
+                uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle sw) {
+  const uint64_t dims[2] = {dim0, dim1};
+  const uint32_t box[2] = {box0, box1};
+  return make_map_nd(m, dt, base, 2, dims, &stride1_bytes, box, sw);
 }
 
 int set_smem_attr(const void* func, int bytes) {
@@ -162,10 +176,11 @@ __global__ void k_prepare_beta(const uint8_t* __restrict__ s_a, const uint8_t* _
 
 // Row scaling into fp16: for each of `rows` output rows, src row = index ? index[row] : row,
 // sigma = row_scale_exp(max|src row|); dst = fp16(src * 2^sigma); inv[row] = 2^-sigma.
-// A row index < 0 yields a zero row. SRC: 0 fp32, 1 bf16.
+// A row index < 0 yields a zero row. SRC: 0 fp32, 1 bf16. dst rows are ld >= K elements apart,
+// columns K..ld-1 written as 0.
 template <int SRC>
 __global__ void k_rows_to_half(const void* __restrict__ src, const int* __restrict__ index, int rows, int K,
-                               __half* __restrict__ dst, float* __restrict__ inv) {
+                               int ld, __half* __restrict__ dst, float* __restrict__ inv) {
   const int row = blockIdx.x;
   if (row >= rows) return;
   const int sr = index ? index[row] : row;
@@ -196,15 +211,16 @@ __global__ void k_rows_to_half(const void* __restrict__ src, const int* __restri
     if (sr >= 0)
       v = SRC == 0 ? reinterpret_cast<const float*>(src)[(int64_t)sr * K + k]
                    : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(src)[(int64_t)sr * K + k]);
-    dst[(int64_t)row * K + k] = __float2half_rn(v * sc);
+    dst[(int64_t)row * ld + k] = __float2half_rn(v * sc);
   }
+  for (int k = K + threadIdx.x; k < ld; k += blockDim.x) dst[(int64_t)row * ld + k] = __float2half_rn(0.f);
 }
 
 // The same, one pass: each thread holds up to 4 chunks of 8 values of the row in registers
-// (16- or 32-byte loads, 16-byte stores), K % 8 == 0 and K <= 8 * 4 * blockDim.x.
+// (16- or 32-byte loads, 16-byte stores), K % 8 == 0, ld % 8 == 0 and K <= 8 * 4 * blockDim.x.
 template <int SRC>
 __global__ void __launch_bounds__(256) k_rows_to_half_v(const void* __restrict__ src, const int* __restrict__ index,
-                                                        int rows, int K, __half* __restrict__ dst,
+                                                        int rows, int K, int ld, __half* __restrict__ dst,
                                                         float* __restrict__ inv) {
   const int row = blockIdx.x;
   if (row >= rows) return;
@@ -261,8 +277,10 @@ __global__ void __launch_bounds__(256) k_rows_to_half_v(const void* __restrict__
       const __half2 h = __floats2half2_rn(v[i][2 * j] * sc, v[i][2 * j + 1] * sc);
       o[j] = *reinterpret_cast<const uint32_t*>(&h);
     }
-    reinterpret_cast<uint4*>(dst + (int64_t)row * K)[ch] = make_uint4(o[0], o[1], o[2], o[3]);
+    reinterpret_cast<uint4*>(dst + (int64_t)row * ld)[ch] = make_uint4(o[0], o[1], o[2], o[3]);
   }
+  for (int ch = nch + threadIdx.x; ch < ld / 8; ch += blockDim.x)
+    reinterpret_cast<uint4*>(dst + (int64_t)row * ld)[ch] = make_uint4(0, 0, 0, 0);
 }
 
 // Transposed copy of an MXFP4 stack for the backward GEMMs. For every expert:
@@ -333,19 +351,21 @@ int launch_single_expert_chunks(Chunk* chunks, int* n_chunks, int M, int nmax, c
 }
 
 int launch_rows_to_half(const void* src, int src_dtype, const int* index, int rows, int K, __half* dst, float* inv,
-                        cudaStream_t s) {
+                        cudaStream_t s, int ld) {
   if (rows <= 0) return LL_OK;
-  const bool vec = K % 8 == 0 && K <= 8 * 4 * 256 && reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
+  if (ld < 0) ld = K;
+  if (ld < K) return LL_ERR_ARG;
+  const bool vec = K % 8 == 0 && ld % 8 == 0 && K <= 8 * 4 * 256 && reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(dst) % 16 == 0;
   if (vec) {
     if (src_dtype == 0)
-      k_rows_to_half_v<0><<<rows, 256, 0, s>>>(src, index, rows, K, dst, inv);
+      k_rows_to_half_v<0><<<rows, 256, 0, s>>>(src, index, rows, K, ld, dst, inv);
     else
-      k_rows_to_half_v<1><<<rows, 256, 0, s>>>(src, index, rows, K, dst, inv);
+      k_rows_to_half_v<1><<<rows, 256, 0, s>>>(src, index, rows, K, ld, dst, inv);
   } else if (src_dtype == 0) {
-    k_rows_to_half<0><<<rows, 256, 0, s>>>(src, index, rows, K, dst, inv);
+    k_rows_to_half<0><<<rows, 256, 0, s>>>(src, index, rows, K, ld, dst, inv);
   } else {
-    k_rows_to_half<1><<<rows, 256, 0, s>>>(src, index, rows, K, dst, inv);
+    k_rows_to_half<1><<<rows, 256, 0, s>>>(src, index, rows, K, ld, dst, inv);
   }
   return check_launch("k_rows_to_half");
 }
@@ -376,7 +396,7 @@ static size_t dropin_layout(void* base, int rows, int width, int R, int K, DropI
   t.n_chunks = c.take<int>(1);
   t.beta = c.take<int32_t>(2);
   t.inv = c.take<float>(rows);
-  t.act = c.take<__half>((size_t)rows * width);
+  t.act = c.take<__half>((size_t)rows * ((width + 63) / 64 * 64));   // rows padded to whole 64-K halves
   t.codes_t = c.take<uint8_t>((size_t)R * K / 2);
   t.scales_t = c.take<__half>((size_t)(K / 32) * R);
   if (w) *w = t;
@@ -445,10 +465,11 @@ int ll_mxfp4_gemm(float* y, const float* x, const uint8_t* packed, const uint8_t
   k_single_expert_chunks<<<1, 128, 0, s>>>(w.chunks, w.n_chunks, M, kDropInNmax);
   LL_TRY(check_launch("k_single_expert_chunks"));
   LL_TRY(launch_prepare_beta(scales, nullptr, 1, R, K, scale_stride, w.beta, 0, s));
-  LL_TRY(launch_rows_to_half(x, 0, nullptr, M, K, w.act, w.inv, s));
-  CUtensorMap pk, sc, act;
+  const int Kp = (K + 63) / 64 * 64;
+  LL_TRY(launch_rows_to_half(x, 0, nullptr, M, K, w.act, w.inv, s, Kp));
+  CUtensorMap pk, sc, act[kDropInNmax / 16];
   LL_TRY(make_rowscale_maps(&pk, &sc, packed, scales, R, K, scale_stride));
-  LL_TRY(make_act_map(&act, w.act, M, K));
+  LL_TRY(make_act_maps(act, kDropInNmax / 16, w.act, M, Kp));
   GemmArgs a{};
   a.chunks = w.chunks;
   a.n_chunks = w.n_chunks;
@@ -462,7 +483,7 @@ int ll_mxfp4_gemm(float* y, const float* x, const uint8_t* packed, const uint8_t
   a.epi.P = M;
   a.epi.M = R;
   a.epi.Y = y;
-  LL_TRY((launch_gemm<EPI_STORE, 1, 1, false, kDropInNmax>(&pk, &sc, &act, a, s)));
+  LL_TRY((launch_gemm<EPI_STORE, 1, 1, false, kDropInNmax>(&pk, &sc, act, a, s)));
   return read_status(w.st, s);
 }
 
@@ -480,12 +501,13 @@ int ll_mxfp4_gemm_t(float* y, const float* dy, const uint8_t* packed, const uint
   k_single_expert_chunks<<<1, 128, 0, s>>>(w.chunks, w.n_chunks, M, kDropInNmax);
   LL_TRY(check_launch("k_single_expert_chunks"));
   LL_TRY(launch_prepare_beta(scales, nullptr, 1, R, K, scale_stride, w.beta, 0, s));
-  LL_TRY(launch_rows_to_half(dy, 0, nullptr, M, R, w.act, w.inv, s));
+  const int Rp = (R + 63) / 64 * 64;
+  LL_TRY(launch_rows_to_half(dy, 0, nullptr, M, R, w.act, w.inv, s, Rp));
   // the backward orientation reads a transposed copy: codes [K][R/2], fp16 multipliers [K/32][R]
   LL_TRY(launch_transpose_mxfp4(packed, scales, scale_stride, 1, R, K, w.beta, 0, w.codes_t, w.scales_t, s));
-  CUtensorMap pk, sc, act;
+  CUtensorMap pk, sc, act[kDropInNmax / 16];
   LL_TRY(make_colscale_maps(&pk, &sc, w.codes_t, w.scales_t, K, R));
-  LL_TRY(make_act_map(&act, w.act, M, R));
+  LL_TRY(make_act_maps(act, kDropInNmax / 16, w.act, M, Rp));
   GemmArgs a{};
   a.chunks = w.chunks;
   a.n_chunks = w.n_chunks;
@@ -499,7 +521,7 @@ int ll_mxfp4_gemm_t(float* y, const float* dy, const uint8_t* packed, const uint
   a.epi.P = M;
   a.epi.M = K;
   a.epi.Y = y;
-  LL_TRY((launch_gemm<EPI_ACCUM, 1, 1, true, kDropInNmax>(&pk, &sc, &act, a, s)));
+  LL_TRY((launch_gemm<EPI_ACCUM, 1, 1, true, kDropInNmax>(&pk, &sc, act, a, s)));
   return read_status(w.st, s);
 }
 

@@ -47,7 +47,7 @@ size_t noalloc_layout(void* base, int M, int K, NoAllocLayout* out) {
   w.n_chunks = c.take<int>(1);
   w.beta = c.take<int32_t>(2);
   w.inv = c.take<float>(M);
-  w.act = c.take<__half>((size_t)M * K);
+  w.act = c.take<__half>((size_t)M * ((K + 63) / 64 * 64));   // rows padded to whole 64-K halves
   if (out) *out = w;
   return c.off;
 }
@@ -93,10 +93,11 @@ extern "C" int ll_mxfp4_gemm_noalloc(float* y, const float* x, const uint8_t* pa
   LL_TRY(reset_status(w.st, s));
   LL_TRY(launch_single_expert_chunks(w.chunks, w.n_chunks, M, kNoAllocNmax, s));
   LL_TRY(launch_prepare_beta(scales, nullptr, 1, R, K, scale_stride, w.beta, 0, s));
-  LL_TRY(launch_rows_to_half(x, 0, nullptr, M, K, w.act, w.inv, s));
-  CUtensorMap pk, sc, act;
+  const int Kp = (K + 63) / 64 * 64;
+  LL_TRY(launch_rows_to_half(x, 0, nullptr, M, K, w.act, w.inv, s, Kp));
+  CUtensorMap pk, sc, act[kNoAllocNmax / 16];
   LL_TRY(make_rowscale_maps(&pk, &sc, packed, scales, R, K, scale_stride));
-  LL_TRY(make_act_map(&act, w.act, M, K));
+  LL_TRY(make_act_maps(act, kNoAllocNmax / 16, w.act, M, Kp));
   GemmArgs a{};
   a.chunks = w.chunks;
   a.n_chunks = w.n_chunks;
@@ -110,6 +111,6 @@ extern "C" int ll_mxfp4_gemm_noalloc(float* y, const float* x, const uint8_t* pa
   a.epi.P = M;
   a.epi.M = R;
   a.epi.Y = y;
-  LL_TRY((launch_gemm<EPI_STORE, 1, 1, false, kNoAllocNmax>(&pk, &sc, &act, a, s)));
+  LL_TRY((launch_gemm<EPI_STORE, 1, 1, false, kNoAllocNmax>(&pk, &sc, act, a, s)));
   return read_status(w.st, s);
 }

@@ -20,6 +20,6 @@ int launch_single_expert_chunks(Chunk* chunks, int* n_chunks, int M, int nmax, c
 // dst[row] = fp16(src[index[row]] * 2^sigma_row), inv[row] = 2^-sigma_row (index may be null;
 // a negative index gives a zero row). src_dtype: 0 fp32, 1 bf16.
 int launch_rows_to_half(const void* src, int src_dtype, const int* index, int rows, int K, __half* dst, float* inv,
-                        cudaStream_t s);
+                        cudaStream_t s, int ld = -1);   // ld: dst row stride (>= K, default K)
 
 }  // namespace ll
