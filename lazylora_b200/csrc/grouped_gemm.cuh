@@ -27,7 +27,8 @@
 // Warp roles (25 warps): 0 packed/scale TMA, 1 activation TMA, 2 and 3 MMA issuers (warp 2
 // owns the TMEM allocation), 4..19 dequant (four warps per TMEM lane quarter, one per 32-K
 // segment of a 128-K stage), 20..23 epilogue, 24 stage watcher (waits on the mbarriers for
-// the issuers and releases them through named barriers), 25 and 26 two more MMA issuers.
+// the issuers and releases them through named barriers). With four issuers (27 warps) the
+// extra two are warps 24 and 25 and the watcher is warp 26.
 // A product with one weight matrix (the down projection, its backward, the drop-ins) can
 // run with NMAT = 2 over two adjacent 128-row tiles of the same stack (PAIR below).
 // The issuers accumulate into separate accumulators (chains: gate / up and even / odd K
@@ -99,8 +100,7 @@ struct GemmArgs {
 
 template <int NMAT, int NB, bool COLSCALE, int N_MAX>
 struct GemmCfg {
-  static constexpr int kWatchWarp = 24;
-  static constexpr int kIssuerWarpX = 25;                 // issuers 2 and 3 live at warps 25, 26
+  static constexpr int kIssuerWarpX = 24;                 // issuers 2 and 3 (when present): warps 24, 25
   // Independent accumulation chains, one MMA issuer warp each: a warp issues one tcgen05.mma
   // per ~50 cycles at small N however many accumulators it rotates, so small-N tiles need
   // several issuing warps.
@@ -114,6 +114,9 @@ struct GemmCfg {
   static constexpr int CH = N_MAX <= 16 ? 4 : N_MAX <= 32 ? LL_CHAINS_SMALL_N : (N_MAX >= 128 ? NMAT : 2);
   static constexpr int PM = CH / NMAT;                    // chains per weight matrix
   static constexpr int kThreads = (CH > 2 ? 27 : 25) * 32;
+  // with four issuers each sits on its own SM sub-partition (warp % 4), away from the others'
+  // instruction issue; the watcher then moves to warp 26
+  static constexpr int kWatchWarp = CH > 2 ? 26 : 24;
   static constexpr int kIssuerWarp0 = 2;
   static constexpr int kDqWarp0 = 4, kDqWarps = 16;
   static constexpr int kEpWarp0 = 20, kEpWarps = 4;
@@ -246,14 +249,16 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, N_MAX> tm, const GemmArg
           if (!(ok = mbar_wait_sleep(&pempty[s], ph ^ 1, abort_flag, st, 1, 256))) break;
           uint8_t* stage = smem + C::OFF_P + s * C::P_STAGE;
           mbar_arrive_expect_tx(&pfull[s], C::P_STAGE);
-          for (int i = 0; i < NMAT; i++) {
-            uint8_t* pk = stage + i * (C::PK_BYTES + C::SC_BYTES);
-            const int r_i = row + (PAIR ? i * 128 : 0);
-            tma_load_2d(pk, &tm.pk[i], &pfull[s], ks * (C::BK / 2), r_i);
+          // stage layout: the NMAT packed tiles, then their NMAT scale tiles; paired tiles are
+          // adjacent rows of one stack, so one box of 256 rows (8 column groups) brings both
+          for (int i = 0; i < (PAIR ? 1 : NMAT); i++) {
+            uint8_t* pk = stage + i * C::PK_BYTES;
+            uint8_t* sc = stage + NMAT * C::PK_BYTES + i * C::SC_BYTES;
+            tma_load_2d(pk, &tm.pk[i], &pfull[s], ks * (C::BK / 2), row);
             if (COLSCALE)
-              tma_load_2d(pk + C::PK_BYTES, &tm.sc[i], &pfull[s], ks * C::BK, grp + (PAIR ? i * 4 : 0));
+              tma_load_2d(sc, &tm.sc[i], &pfull[s], ks * C::BK, grp);
             else
-              tma_load_2d(pk + C::PK_BYTES, &tm.sc[i], &pfull[s], ((ks * C::BK) / 32) & ~15, r_i);
+              tma_load_2d(sc, &tm.sc[i], &pfull[s], ((ks * C::BK) / 32) & ~15, row);
           }
           issued++;
           if (++s == C::S_P) { s = 0; ph ^= 1; }
@@ -293,7 +298,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, N_MAX> tm, const GemmArg
         mbar_wait_sleep(&bfull[s], ph, abort_flag, st, 12, 256);
       }
     }
-  } else if (warp < C::kDqWarp0 || warp >= C::kIssuerWarpX) {
+  } else if (warp < C::kDqWarp0 || (warp >= C::kIssuerWarpX && warp != C::kWatchWarp)) {
     // ---------------------------------------------------------------- MMA issuers
     // Chain c = mat * PM + k accumulates weight matrix `mat` over the stages sb with
     // sb % PM == k. The whole warp takes part in the named barriers the watcher releases
@@ -320,10 +325,13 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, N_MAX> tm, const GemmArg
               const uint32_t half_bytes = (uint32_t)npad * 128;   // one 64-K half of the chunk's rows
               const uint32_t b_addr =
                   smem_u32(smem + C::OFF_B + bs * C::B_SLOT) + (NB == 2 ? mat : 0) * (C::KS / 64) * half_bytes;
+              // the descriptor's address field is addr >> 4 in its low bits (shared memory is
+              // below 256 KB, so the sums stay in the field): one base descriptor per stage
+              const uint64_t bdesc0 = umma_desc(b_addr, 16, 1024, kSwizzle128B);
+              const uint64_t half16 = half_bytes >> 4;
 #pragma unroll
               for (int kk = 0; kk < C::KS / 16; kk++) {
-                const uint64_t bdesc =
-                    umma_desc(b_addr + (kk >> 2) * half_bytes + (kk & 3) * 32, 16, 1024, kSwizzle128B);
+                const uint64_t bdesc = bdesc0 + (kk >> 2) * half16 + (kk & 3) * 2;
                 mma_f16_ts(d, a_tmem + kk * 8, bdesc, idesc, first ? 0u : 1u);
                 first = false;
               }
@@ -399,8 +407,8 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, N_MAX> tm, const GemmArg
         const int seg = seg0 + j;
 #pragma unroll
         for (int i = 0; i < NMAT; i++) {
-          const uint8_t* pk = stage + i * (C::PK_BYTES + C::SC_BYTES);
-          const uint8_t* sc = pk + C::PK_BYTES;
+          const uint8_t* pk = stage + i * C::PK_BYTES;
+          const uint8_t* sc = stage + NMAT * C::PK_BYTES + i * C::SC_BYTES;
           const uint4 raw = ld_shared_v4(smem_u32(pk + m * 64 + ((seg ^ ((m >> 1) & 3)) << 4)));
           uint32_t o[16];
           if (COLSCALE) {

@@ -53,25 +53,26 @@ DeviceInfo device_info();   // of the current device, cached
 int make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t dim0, uint64_t dim1,
                 uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle sw);
 
-// Packed weight bytes [rows_total][cols/2] (boxes of 128 rows x 64 bytes, 64-byte swizzle)
-// with the reference's E8M0 scale bytes [rows_total][scale_stride] (boxes of 128 x 16 bytes).
+// Packed weight bytes [rows_total][cols/2] (boxes of `box_rows` rows x 64 bytes, 64-byte
+// swizzle) with the reference's E8M0 scale bytes [rows_total][scale_stride] (boxes of
+// box_rows x 16 bytes). box_rows: 128, or 256 for a pair of adjacent 128-row tiles.
 inline int make_rowscale_maps(CUtensorMap* pk, CUtensorMap* sc, const uint8_t* packed, const uint8_t* scales,
-                              int64_t rows_total, int cols, int64_t scale_stride) {
+                              int64_t rows_total, int cols, int64_t scale_stride, int box_rows = 128) {
   LL_TRY(make_map_2d(pk, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, (uint64_t)cols / 2, (uint64_t)rows_total,
-                     (uint64_t)cols / 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_64B));
+                     (uint64_t)cols / 2, 64, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_64B));
   LL_TRY(make_map_2d(sc, CU_TENSOR_MAP_DATA_TYPE_UINT8, scales, (uint64_t)cols / 32, (uint64_t)rows_total,
-                     (uint64_t)scale_stride, 16, 128, CU_TENSOR_MAP_SWIZZLE_NONE));
+                     (uint64_t)scale_stride, 16, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_NONE));
   return LL_OK;
 }
 
 // Transposed codes [rows_total][K/2] with the fp16 column-scale table [rows_total/32][K]
-// (boxes of 4 row groups x 128 k).
+// (boxes of box_rows / 32 row groups x 128 k).
 inline int make_colscale_maps(CUtensorMap* pk, CUtensorMap* sc, const uint8_t* codes, const __half* cscales,
-                              int64_t rows_total, int K) {
+                              int64_t rows_total, int K, int box_rows = 128) {
   LL_TRY(make_map_2d(pk, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, (uint64_t)K / 2, (uint64_t)rows_total, (uint64_t)K / 2,
-                     64, 128, CU_TENSOR_MAP_SWIZZLE_64B));
+                     64, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_64B));
   LL_TRY(make_map_2d(sc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, cscales, (uint64_t)K, (uint64_t)rows_total / 32,
-                     (uint64_t)K * 2, 128, 4, CU_TENSOR_MAP_SWIZZLE_NONE));
+                     (uint64_t)K * 2, 128, (uint32_t)box_rows / 32, CU_TENSOR_MAP_SWIZZLE_NONE));
   return LL_OK;
 }
 

@@ -512,7 +512,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   // F2: down
   {
     CUtensorMap pk[2], sc[2], act[8];
-    LL_TRY(make_rowscale_maps(&pk[0], &sc[0], L->w2p, L->w2s, (int64_t)E * d, f, L->s2_stride));
+    LL_TRY(make_rowscale_maps(&pk[0], &sc[0], L->w2p, L->w2s, (int64_t)E * d, f, L->s2_stride, 256));
     pk[1] = pk[0];
     sc[1] = sc[0];
     LL_TRY(make_act_maps(act, W.nmax / 16, W.H, P, f));
@@ -559,17 +559,18 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
   LL_TRY(expand(true, nullptr, nullptr, k, T, f, r, 1.f, W.gB, L->A_d, nullptr, nullptr, W.lora_d, s));
   // B1: v = g . W2 (+ LoRA down), SiTU-GLU backward
   {
+    // paired 128-row tiles, except at 128-token tiles: there two accumulators of 128 columns
+    // leave tensor memory for one buffer only, and this epilogue is too heavy to run exposed
+    const bool pair = W.nmax < 128;
     CUtensorMap pk[2], sc[2], act[8];
-    LL_TRY(make_colscale_maps(&pk[0], &sc[0], L->w2t, reinterpret_cast<const __half*>(L->s2t), (int64_t)E * f, d));
+    LL_TRY(make_colscale_maps(&pk[0], &sc[0], L->w2t, reinterpret_cast<const __half*>(L->s2t), (int64_t)E * f, d,
+                              pair ? 256 : 128));
     pk[1] = pk[0];
     sc[1] = sc[0];
     LL_TRY(make_act_maps(act, W.nmax / 16, W.gh, P, d));
     GemmArgs a{};
     a.chunks = W.chunks;
     a.n_chunks = W.n_chunks;
-    // paired 128-row tiles, except at 128-token tiles: there two accumulators of 128 columns
-    // leave tensor memory for one buffer only, and this epilogue is too heavy to run exposed
-    const bool pair = W.nmax < 128;
     a.mtiles = pair ? (f + 255) / 256 : f / 128;
     a.K = d;
     a.e_rows = f;
