@@ -14,31 +14,71 @@ LL_DEV float load_as_float(const void* p, int64_t i) {
 }
 
 // ---------------------------------------------------------------- skinny split-K GEMM
-// part[split][m][n] = sum_{k in split} A[m][k] * B(k, n); blockIdx.y picks 32 of the N columns.
+// part[split][m][n] = sum_{k in split} A[m][k] * B(k, n) for the NC columns n = blockIdx.y * NC
+// .. + NC - 1 (N a few tens: the LoRA rank, or twice it).
 // B(k, n): BROWS -> n < N0 ? B0[n*K + k] : B1[(n-N0)*K + k]  ([N][K], e.g. LoRA A matrices)
 //          else  -> B0[k*N + n]                             ([K][N], e.g. LoRA B matrices)
-// Tile 64 rows x 32 columns x 64 k per step; thread = 2 rows x 4 columns.
-constexpr int kSkBM = 64, kSkBN = 32, kSkBK = 64;
+// Thread = one column x 8 rows: per k one B value (its own column) and the 8 A values as two
+// broadcast 16-byte reads, 8 FMAs. The A tile is staged transposed ([k][row]) from 16-byte
+// global loads of 8 consecutive k. K % 8 == 0; split boundaries are multiples of kSkBK.
+constexpr int kSkBK = 32, kSkTM = 8;
 
-template <int ADT, bool BROWS>
+template <int NC>
+struct SkinnyCfg {
+  static constexpr int RG = 256 / NC;         // row groups
+  static constexpr int BM = RG * kSkTM;       // rows per block: 64 (NC = 32) or 128 (NC = 16)
+};
+
+template <int ADT>
+LL_DEV void load8_as_float(const void* A, int64_t off, float (&v)[8]) {
+  if (ADT == 0) {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(A) + off);
+    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(A) + off + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(A) + off);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      float2 f;
+      if (ADT == 1) f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+      else f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  }
+}
+
+template <int ADT, bool BROWS, int NC>
 __global__ void __launch_bounds__(256) k_skinny(const void* __restrict__ A, int M, int K, int lda,
                                                 const float* __restrict__ B0, const float* __restrict__ B1, int N0,
                                                 int N, int kc, float* __restrict__ part) {
-  __shared__ float As[kSkBK][kSkBM + 4];
-  __shared__ float Bs[kSkBK][kSkBN + 4];
-  const int m0 = blockIdx.x * kSkBM, nb0 = blockIdx.y * kSkBN;
+  using SC = SkinnyCfg<NC>;
+  __shared__ __align__(16) float As[kSkBK][SC::BM + 4];
+  __shared__ float Bs[kSkBK][NC];
+  const int m0 = blockIdx.x * SC::BM, nb0 = blockIdx.y * NC;
   const int k_begin = blockIdx.z * kc, k_end = min(K, k_begin + kc);
-  const int tm = threadIdx.x / 8, tn = threadIdx.x % 8;   // rows tm, tm+32; columns 4tn..4tn+3
-  float acc[2][4] = {};
+  const int n_l = threadIdx.x % NC, rg = threadIdx.x / NC;
+  float acc[kSkTM];
+#pragma unroll
+  for (int i = 0; i < kSkTM; i++) acc[i] = 0.f;
   for (int k0 = k_begin; k0 < k_end; k0 += kSkBK) {
-    for (int i = threadIdx.x; i < kSkBM * kSkBK; i += 256) {
-      const int r = i / kSkBK, c = i % kSkBK;
-      const int m = m0 + r, k = k0 + c;
-      As[c][r] = (m < M && k < k_end) ? load_as_float<ADT>(A, (int64_t)m * lda + k) : 0.f;
+    for (int i = threadIdx.x; i < SC::BM * (kSkBK / 8); i += 256) {
+      const int r = i / (kSkBK / 8), c8 = (i % (kSkBK / 8)) * 8;
+      const int m = m0 + r, k = k0 + c8;
+      float v[8];
+      if (m < M && k < k_end) {
+        load8_as_float<ADT>(A, (int64_t)m * lda + k, v);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) As[c8 + j][r] = v[j];
     }
-    for (int i = threadIdx.x; i < kSkBN * kSkBK; i += 256) {
+    for (int i = threadIdx.x; i < NC * kSkBK; i += 256) {
       int n, c;
-      if (BROWS) { n = i / kSkBK; c = i % kSkBK; } else { c = i / kSkBN; n = i % kSkBN; }
+      if (BROWS) { n = i / kSkBK; c = i % kSkBK; } else { c = i / NC; n = i % NC; }
       const int k = k0 + c, ng = nb0 + n;
       float v = 0.f;
       if (ng < N && k < k_end) {
@@ -48,27 +88,25 @@ __global__ void __launch_bounds__(256) k_skinny(const void* __restrict__ A, int 
       Bs[c][n] = v;
     }
     __syncthreads();
-#pragma unroll 16
+#pragma unroll 8
     for (int kk = 0; kk < kSkBK; kk++) {
-      const float a0 = As[kk][tm], a1 = As[kk][tm + 32];
-      const float4 b = *reinterpret_cast<const float4*>(&Bs[kk][tn * 4]);
-      acc[0][0] = fmaf(a0, b.x, acc[0][0]); acc[0][1] = fmaf(a0, b.y, acc[0][1]);
-      acc[0][2] = fmaf(a0, b.z, acc[0][2]); acc[0][3] = fmaf(a0, b.w, acc[0][3]);
-      acc[1][0] = fmaf(a1, b.x, acc[1][0]); acc[1][1] = fmaf(a1, b.y, acc[1][1]);
-      acc[1][2] = fmaf(a1, b.z, acc[1][2]); acc[1][3] = fmaf(a1, b.w, acc[1][3]);
+      const float b = Bs[kk][n_l];
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[kk][rg * kSkTM]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[kk][rg * kSkTM + 4]);
+      acc[0] = fmaf(a0.x, b, acc[0]); acc[1] = fmaf(a0.y, b, acc[1]);
+      acc[2] = fmaf(a0.z, b, acc[2]); acc[3] = fmaf(a0.w, b, acc[3]);
+      acc[4] = fmaf(a1.x, b, acc[4]); acc[5] = fmaf(a1.y, b, acc[5]);
+      acc[6] = fmaf(a1.z, b, acc[6]); acc[7] = fmaf(a1.w, b, acc[7]);
     }
     __syncthreads();
   }
+  const int n = nb0 + n_l;
+  if (n >= N) return;
   float* out = part + (int64_t)blockIdx.z * M * N;
 #pragma unroll
-  for (int i = 0; i < 2; i++) {
-    const int m = m0 + tm + 32 * i;
-    if (m >= M) continue;
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const int n = nb0 + tn * 4 + j;
-      if (n < N) out[(int64_t)m * N + n] = acc[i][j];
-    }
+  for (int i = 0; i < kSkTM; i++) {
+    const int m = m0 + rg * kSkTM + i;
+    if (m < M) out[(int64_t)m * N + n] = acc[i];
   }
 }
 
@@ -173,73 +211,89 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
 }
 
 // --------------------------------------------------------------- outer-product sums
-// part[seg][rr][c] = sum_{n in seg} Pm(n, rr) * Q[n][c]; 4 consecutive columns per thread,
-// ranks rr = 32 blockIdx.z .. + 31 (any r, 32 at a time).
-// Pm: [N][r] fp32, or (PGATHER) tw[n] * Pm[perm_token[n]][rr]. Q dtype QDT (0 f32, 1 bf16, 2 f16).
+// part[seg][rr][c] = sum_{n in seg} Pm(n, rr) * Q[n][c] for the ranks rr = kOuRB blockIdx.z ..
+// + kOuRB - 1 and the 128 columns of blockIdx.x. Pm: [N][r] fp32, or (PGATHER) tw[n] *
+// Pm[perm_token[n]][rr]. Q dtype QDT (0 f32, 1 bf16, 2 f16), C % 4 == 0.
+// Block = 8 warps, lane = 4 consecutive columns; the 8 warps take interleaved batches of 8
+// rows n of the segment (the 8 Q loads of a batch issued before the FMAs), then their sums
+// are added in warp order through shared memory.
+constexpr int kOuRB = 16, kOuCW = 128, kOuNB = 8;
+
+template <int QDT>
+LL_DEV float4 load4_as_float(const void* Q, int64_t off) {
+  if (QDT == 0) return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(Q) + off);
+  const uint2 v = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(Q) + off);
+  float2 a, b;
+  if (QDT == 1) {
+    a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
+    b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+  } else {
+    a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+    b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+  }
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
 template <int QDT, bool PGATHER>
-__global__ void __launch_bounds__(64) k_outer4(const float* __restrict__ Pm, const int* __restrict__ perm_token,
-                                               const float* __restrict__ tw, const void* __restrict__ Q, int N,
-                                               const int* __restrict__ n_dev, int C, int r, int nseg,
-                                               float* __restrict__ part) {
-  const int c = (blockIdx.x * 64 + threadIdx.x) * 4;
+__global__ void __launch_bounds__(256) k_outer8(const float* __restrict__ Pm, const int* __restrict__ perm_token,
+                                                const float* __restrict__ tw, const void* __restrict__ Q, int N,
+                                                const int* __restrict__ n_dev, int C, int r, int nseg,
+                                                float* __restrict__ part) {
+  extern __shared__ float4 red4[];                    // [8 warps][kOuRB][32 lanes] float4
+  __shared__ float ps[8][kOuNB][kOuRB];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int c = blockIdx.x * kOuCW + lane * 4;
+  const bool cok = c < C;
   const int seg = blockIdx.y;
-  const int rb = blockIdx.z * 32, rn = min(32, r - rb);   // this block's ranks
+  const int rb = blockIdx.z * kOuRB, rn = min(kOuRB, r - rb);
   const int n_total = n_dev ? *n_dev : N;
   const int per = (n_total + nseg - 1) / nseg;
   const int n0 = seg * per, n1 = min(n_total, n0 + per);
-  __shared__ float ps[16][33];
-  float acc[32][4];
+  float4 acc[kOuRB];
 #pragma unroll
-  for (int i = 0; i < 32; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-  for (int nb = n0; nb < n1; nb += 16) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < 16 * rn; i += 64) {
-      const int nn = i / rn, rr = i % rn;
+  for (int i = 0; i < kOuRB; i++) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int nb = n0 + warp * kOuNB; nb < n1; nb += 8 * kOuNB) {
+    // this warp's batch: rows nb .. nb + 7 of Pm (rank slice) into shared memory
+    for (int i = lane; i < kOuNB * kOuRB; i += 32) {
+      const int nn = i / kOuRB, rr = i % kOuRB;
       const int n = nb + nn;
       float v = 0.f;
-      if (n < n1) v = PGATHER ? tw[n] * Pm[(int64_t)perm_token[n] * r + rb + rr] : Pm[(int64_t)n * r + rb + rr];
-      ps[nn][rr] = v;
+      if (n < n1 && rr < rn) v = PGATHER ? tw[n] * Pm[(int64_t)perm_token[n] * r + rb + rr] : Pm[(int64_t)n * r + rb + rr];
+      ps[warp][nn][rr] = v;
     }
-    __syncthreads();
-    if (c < C) {
-      const int lim = min(16, n1 - nb);
-#pragma unroll 4
-      for (int nn = 0; nn < lim; nn++) {
-        const int64_t o = (int64_t)(nb + nn) * C + c;
-        float q0, q1, q2, q3;
-        if (QDT == 0) {
-          const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(Q) + o);
-          q0 = v.x; q1 = v.y; q2 = v.z; q3 = v.w;
-        } else if (QDT == 1) {
-          const uint2 v = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(Q) + o);
-          const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
-          const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
-          q0 = a.x; q1 = a.y; q2 = b.x; q3 = b.y;
-        } else {
-          const uint2 v = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(Q) + o);
-          const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
-          const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
-          q0 = a.x; q1 = a.y; q2 = b.x; q3 = b.y;
-        }
+    float4 q[kOuNB];
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
-          if (i < rn) {
-            const float p = ps[nn][i];
-            acc[i][0] = fmaf(p, q0, acc[i][0]);
-            acc[i][1] = fmaf(p, q1, acc[i][1]);
-            acc[i][2] = fmaf(p, q2, acc[i][2]);
-            acc[i][3] = fmaf(p, q3, acc[i][3]);
-          }
-        }
+    for (int nn = 0; nn < kOuNB; nn++)
+      q[nn] = (cok && nb + nn < n1) ? load4_as_float<QDT>(Q, (int64_t)(nb + nn) * C + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    __syncwarp();
+#pragma unroll
+    for (int nn = 0; nn < kOuNB; nn++) {
+#pragma unroll
+      for (int i = 0; i < kOuRB; i++) {
+        const float p = ps[warp][nn][i];
+        acc[i].x = fmaf(p, q[nn].x, acc[i].x);
+        acc[i].y = fmaf(p, q[nn].y, acc[i].y);
+        acc[i].z = fmaf(p, q[nn].z, acc[i].z);
+        acc[i].w = fmaf(p, q[nn].w, acc[i].w);
       }
     }
+    __syncwarp();
   }
-  if (c < C) {
 #pragma unroll
-    for (int i = 0; i < 32; i++)
-      if (i < rn)
-        *reinterpret_cast<float4*>(part + ((int64_t)seg * r + rb + i) * C + c) =
-            make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+  for (int i = 0; i < kOuRB; i++) red4[(warp * kOuRB + i) * 32 + lane] = acc[i];
+  __syncthreads();
+  // thread -> (rank i, lane l): the 8 warps' sums in warp order
+  for (int o = threadIdx.x; o < kOuRB * 32; o += 256) {
+    const int i = o / 32, l = o % 32;
+    const int cc = blockIdx.x * kOuCW + l * 4;
+    if (i >= rn || cc >= C) continue;
+    float4 s = red4[i * 32 + l];
+#pragma unroll
+    for (int w = 1; w < 8; w++) {
+      const float4 t = red4[(w * kOuRB + i) * 32 + l];
+      s.x += t.x; s.y += t.y; s.z += t.z; s.w += t.w;
+    }
+    *reinterpret_cast<float4*>(part + ((int64_t)seg * r + rb + i) * C + cc) = s;
   }
 }
 

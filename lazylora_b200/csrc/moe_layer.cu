@@ -318,10 +318,10 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   w.hg = c.take<float>((size_t)T * r);
   w.hu = c.take<float>((size_t)T * r);
   w.opart = c.take<float>((size_t)nseg_max * r * (d > f ? d : f));
-  {  // split-K partials of the skinny products: nsplit <= ceil(2 * SMs / mblocks), so
-     // nsplit * M <= 2 * SMs * 64 + M + 64 rows of at most 2r columns (SMs <= 160)
+  {  // split-K partials of the skinny products: nsplit * mblocks * nblocks <= 4 * SMs +
+     // mblocks * nblocks blocks of 2048 outputs (BM * NC); SMs <= 160
     const int64_t rows = P > T ? P : T;
-    w.skpart = c.take<float>(((size_t)2 * 160 * 64 + rows + 64) * 2 * r);
+    w.skpart = c.take<float>((size_t)4 * 160 * 2048 + (size_t)(rows + 128) * (2 * r + 32));
   }
   if (out) *out = w;
   return c.off + 256;
@@ -351,13 +351,21 @@ static int gemm_nmax(int nmax, const CUtensorMap* pk, const CUtensorMap* sc, con
 // or columns ([K][N]); split-K partials in `part`, summed in a fixed order.
 static int skinny(const void* A, int adt, bool brows, int M, int K, const float* B0, const float* B1, int N0, int N,
                   float alpha, float* C0, float* C1, float* part, cudaStream_t s) {
-  const int mblocks = (M + kSkBM - 1) / kSkBM;
-  int nsplit = (2 * device_info().sms + mblocks - 1) / mblocks;
+  if (K % 8 || M <= 0 || N <= 0) return LL_ERR_ARG;
+  const bool nc16 = N <= 16;
+  const int BM = nc16 ? SkinnyCfg<16>::BM : SkinnyCfg<32>::BM, NC = nc16 ? 16 : 32;
+  const int mblocks = (M + BM - 1) / BM, nblocks = (N + NC - 1) / NC;
+  // about four blocks per SM, split over K
+  int nsplit = (4 * device_info().sms + mblocks * nblocks - 1) / (mblocks * nblocks);
   nsplit = std::max(1, std::min(nsplit, (K + kSkBK - 1) / kSkBK));
   const int kc = ((K + nsplit - 1) / nsplit + kSkBK - 1) / kSkBK * kSkBK;
   nsplit = (K + kc - 1) / kc;
-  dim3 grid(mblocks, (N + kSkBN - 1) / kSkBN, nsplit);
-#define LL_SK(ADT, BR) k_skinny<ADT, BR><<<grid, 256, 0, s>>>(A, M, K, K, B0, B1, N0, N, kc, part)
+  dim3 grid(mblocks, nblocks, nsplit);
+#define LL_SK(ADT, BR)                                                                             \
+  do {                                                                                             \
+    if (nc16) k_skinny<ADT, BR, 16><<<grid, 256, 0, s>>>(A, M, K, K, B0, B1, N0, N, kc, part);     \
+    else k_skinny<ADT, BR, 32><<<grid, 256, 0, s>>>(A, M, K, K, B0, B1, N0, N, kc, part);          \
+  } while (0)
   if (brows) {
     if (adt == 0) LL_SK(0, true); else if (adt == 1) LL_SK(1, true); else LL_SK(2, true);
   } else {
@@ -398,20 +406,27 @@ static int expand(bool rrows, const int* tok_pos, const float* Y, int k, int T, 
 static int outer(const float* Pm, const int* perm_token, const float* tw, const void* Q, int qdt, int N,
                  const int* n_dev, int C, int r, float sc, bool transposed, float* part, int nseg_max, float* out,
                  cudaStream_t s) {
-  const int cblocks = (C + 255) / 256;
-  int nseg = (2 * device_info().sms + cblocks - 1) / cblocks;
+  if (C % 4 || r <= 0) return LL_ERR_ARG;
+  const int cblocks = (C + kOuCW - 1) / kOuCW, zb = (r + kOuRB - 1) / kOuRB;
+  // about three blocks per SM; each warp gets at least one batch of rows
+  int nseg = (3 * device_info().sms + cblocks * zb - 1) / (cblocks * zb);
   nseg = std::max(1, std::min(nseg, nseg_max));
-  nseg = std::min(nseg, std::max(1, N / 16));
-  dim3 grid(cblocks, nseg, (r + 31) / 32);
+  nseg = std::min(nseg, std::max(1, N / (8 * kOuNB)));
+  dim3 grid(cblocks, nseg, zb);
+  const int smem = 8 * kOuRB * 32 * (int)sizeof(float4);
   const bool pg = perm_token != nullptr;
-#define LL_OU(QD, PG) k_outer4<QD, PG><<<grid, 64, 0, s>>>(Pm, perm_token, tw, Q, N, n_dev, C, r, nseg, part)
+#define LL_OU(QD, PG)                                                                                \
+  do {                                                                                               \
+    LL_TRY(set_smem_attr(reinterpret_cast<const void*>(k_outer8<QD, PG>), smem));                   \
+    k_outer8<QD, PG><<<grid, 256, smem, s>>>(Pm, perm_token, tw, Q, N, n_dev, C, r, nseg, part);      \
+  } while (0)
   if (pg) {
     if (qdt == 0) LL_OU(0, true); else if (qdt == 1) LL_OU(1, true); else LL_OU(2, true);
   } else {
     if (qdt == 0) LL_OU(0, false); else if (qdt == 1) LL_OU(1, false); else LL_OU(2, false);
   }
 #undef LL_OU
-  LL_TRY(check_launch("k_outer4"));
+  LL_TRY(check_launch("k_outer8"));
   const int64_t n = (int64_t)r * C;
   k_outer_reduce<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, nseg, r, C, sc, transposed, out);
   return check_launch("k_outer_reduce");
