@@ -58,56 +58,66 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event (throttle) reasons polled through NVML (read-only queries)
+    every 20 ms by one background thread, started before the warm-up; a `with` block marks
+    the timed region and summary() reports the samples taken inside it (or, for a region
+    shorter than five samples, those of the 0.25 s before it too: the warm-up of the same
+    work). Reports nothing when NVML is absent."""
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
+    _samples = []          # (time, sm MHz, reason bits)
+    _mx = None
+    _thread = None
+
+    @classmethod
+    def start(cls, gpu_index: int):
+        if cls._thread is not None:
+            return
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            try:   # the CUDA device's PCI address (CUDA and NVML may number GPUs differently)
+                p = torch.cuda.get_device_properties(gpu_index)
+                h = nv.nvmlDeviceGetHandleByPciBusId("%08x:%02x:%02x.0" % (p.pci_domain_id, p.pci_bus_id,
+                                                                          p.pci_device_id))
+            except Exception:
+                h = nv.nvmlDeviceGetHandleByIndex(gpu_index)
+            cls._mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception:
+            cls._thread = False
+            return
+
+        def run():
+            while True:
+                try:
+                    cls._samples.append((time.time(), float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                         int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))))
+                except Exception:
+                    return
+                time.sleep(0.02)
+
+        cls._thread = threading.Thread(target=run, daemon=True)
+        cls._thread.start()
 
     def __init__(self, gpu_index: int):
-        self.idx = gpu_index
-        self.proc = None
-        self.lines = []
+        ClockSampler.start(gpu_index)
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except Exception:
-            self.proc = None
+        self.t0 = time.time()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self.t1 = time.time()
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        win = [x for x in list(self._samples) if self.t0 <= x[0] <= self.t1]
+        extended = len(win) < 5
+        if extended:
+            win = [x for x in list(self._samples) if self.t0 - 0.25 <= x[0] <= self.t1]
+        reasons = sorted({name for _, _, r in win for name, bit in self.REASONS if r & bit})
+        return {"sm_mhz": statistics.median(x[1] for x in win) if win else None, "sm_max_mhz": self._mx,
+                "reasons": reasons, "samples": len(win), "source": "nvml every 20 ms" +
+                (", window includes the 0.25 s warm-up before the timed region" if extended else "")}
 
 
 def dist_setup(args):
@@ -244,6 +254,7 @@ def run_ours(args, cfg, rank, local, world, dist):
         return out, gh, gw, grads, idx, w
 
     # ---- warm-up + correctness status
+    ClockSampler.start(local)
     for _ in range(args.warmup):
         res = step(x, g)
     if ep is not None:
@@ -378,6 +389,7 @@ def run_ours(args, cfg, rank, local, world, dist):
 
 # ----------------------------------------------------------------------- decode
 def run_decode(args, cfg, rank, local, world, dist):
+    ClockSampler.start(local)
     """Forward-only decode steps (router + routed experts) at T in {1, 4, 16} with Zipf-skewed
     routing. The HBM bound is the MXFP4 bytes of the U experts the step touches; L2 is flushed
     (a 256 MB write) before every timed step, so those bytes come from HBM. Each step is timed
@@ -453,6 +465,7 @@ def run_decode(args, cfg, rank, local, world, dist):
 
 # ------------------------------------------------------------ streaming
 def run_stream(args, cfg, rank, local, world, dist):
+    ClockSampler.start(local)
     """configs[4]: an 8-layer fwd + bwd whose expert weights live in pinned host memory and
     are streamed into HBM for every use (2 x 8 layer loads a step), group by group on a copy
     stream while the previous group computes. --stream-distinct N keeps N distinct layers
