@@ -42,8 +42,8 @@ UNIT = "tokens/s"
 # from one ncu capture of the same kernels at d=7168, f=2048, 64 experts, 9 tokens per expert.
 # Weight reads dominate, so a launch's traffic scales with the number of experts it touches.
 NCU_DRAM_BYTES_PER_EXPERT = {
-    (7168, 2048): [(1020.520e6 + 17.177344e6) / 64, (501.553e6 + 18.935040e6) / 64,
-                   (546.961e6 + 11.003392e6) / 64, (1061.981e6 + 19.554304e6) / 64],
+    (7168, 2048): [(1020.624e6 + 15.785984e6) / 64, (501.543e6 + 16.321280e6) / 64,
+                   (548.367e6 + 9.828096e6) / 64, (1061.762e6 + 18.684928e6) / 64],
 }
 
 
@@ -302,6 +302,26 @@ def run_ours(args, cfg, rank, local, world, dist):
                for i in range(args.steps)]
     clocks = clk.summary()
 
+    # ---- per-kernel breakdown (untimed pass): an event after every launch of the library
+    breakdown = {}
+    nb_steps = min(args.steps, 5)
+    for _ in range(nb_steps):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(128)]
+        for e in evs:
+            e.record(stream)
+        t0 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        lib.ll_profile_launch_events((L.c_void_p * 128)(*[e.cuda_event for e in evs]), 128)
+        step(x, g)
+        nrec = lib.ll_profile_launch_recorded()
+        names_rec = [lib.ll_profile_launch_name(i).decode() for i in range(nrec)]
+        lib.ll_profile_launch_events(None, 0)
+        torch.cuda.synchronize()
+        prev = t0
+        for i, nm in enumerate(names_rec):
+            breakdown[nm] = breakdown.get(nm, 0.0) + prev.elapsed_time(evs[i]) * 1e3 / nb_steps
+            prev = evs[i]
+
     # ---- end to end through the public API, host buffers, copies inside the timed region
     x_h = x.cpu().pin_memory()
     g_h = g.cpu().pin_memory()
@@ -352,7 +372,9 @@ def run_ours(args, cfg, rank, local, world, dist):
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp16 operands / fp32 accumulate (MXFP4 weights decoded exactly)",
         "data": "synthetic",
-        "config": {"workload": ("configs[1]: 896-expert MXFP4 MoE layer, route + fwd + full LoRA bwd" if world == 1
+        "config": {"workload": ((f"{args.config}: {cfg.E}-expert MXFP4 MoE layer, route + fwd + full LoRA bwd"
+                                 if args.config != "c1" else
+                                 "configs[1]: 896-expert MXFP4 MoE layer, route + fwd + full LoRA bwd") if world == 1
                                 else f"expert parallel over {world} GPUs ({cfg.E // world} experts each), "
                                      f"{cfg.T} tokens per GPU ({cfg.T * world} total; configs[2] at 8 GPUs), "
                                      f"route + NCCL all-to-all dispatch + fwd + full LoRA bwd + combine"),
@@ -371,6 +393,9 @@ def run_ours(args, cfg, rank, local, world, dist):
                      "algorithmic_bytes_per_launch": per_kernel_bytes[dom], "avg_launch_ms": avg_ms[dom]},
         "kernel_ms": {n: round(a, 4) for n, a in zip(names, avg_ms)},
         "kernel_share": {n: round(s, 4) for n, s in zip(names, shares)},
+        "kernel_breakdown_us": {"source": f"CUDA events after every launch of the library, mean of {nb_steps} "
+                                          "untimed steps (includes the launch gaps on the stream)",
+                                **{k: round(v, 1) for k, v in sorted(breakdown.items(), key=lambda kv: -kv[1])}},
         "e2e": {"value": world * cfg.T / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": launches[0],

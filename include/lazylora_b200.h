@@ -221,6 +221,16 @@ int ll_profile_gemm_events(void* const* events, int n);
  * thread made. */
 int ll_last_launch_count(void);
 
+/* Profiling hook: record events[i] (cudaEvent_t handles), on the stream of the call in
+ * progress, right after the i-th kernel launch of this library that follows on this thread,
+ * for the first n launches; n = 0 turns it off, calling it again restarts at i = 0. The time
+ * from the previous event (or from one the caller recorded before the call) to events[i] is
+ * the i-th kernel's time on the stream. ll_profile_launch_recorded: events recorded so far;
+ * ll_profile_launch_name(i): the i-th kernel's name (a static string). */
+int ll_profile_launch_events(void* const* events, int n);
+int ll_profile_launch_recorded(void);
+const char* ll_profile_launch_name(int i);
+
 #ifdef __cplusplus
 }
 #endif

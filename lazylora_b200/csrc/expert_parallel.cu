@@ -160,6 +160,7 @@ int ll_ep_plan(int T, int k, int E, int n_ranks, const int64_t* idx, const float
                int* send_tok, int64_t* send_idx, float* send_w, void* stream) {
   if (T < 0 || k <= 0 || k > 64 || E <= 0 || n_ranks <= 0 || n_ranks > 64) return LL_ERR_ARG;
   if (!counts || (T > 0 && (!idx || !w || !pos || !send_tok || !send_idx || !send_w))) return LL_ERR_ARG;
+  g_launch_stream = static_cast<cudaStream_t>(stream);
   k_ep_plan<<<1, kPlanThreads, 0, static_cast<cudaStream_t>(stream)>>>(idx, w, T, k, E, n_ranks, counts, pos,
                                                                          send_tok, send_idx, send_w);
   return check_launch("k_ep_plan");
@@ -172,6 +173,7 @@ int ll_ep_gather_rows(void* dst, const void* src, const int* tok, int rows, int6
     return LL_ERR_ARG;
   const int vecs = (int)(row_bytes / 16);
   const int grid = rows < 148 * 16 ? rows : 148 * 16;
+  g_launch_stream = static_cast<cudaStream_t>(stream);
   k_ep_gather_rows<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<uint4*>(dst), static_cast<const uint4*>(src), tok, rows, vecs);
   return check_launch("k_ep_gather_rows");
@@ -182,6 +184,7 @@ int ll_ep_combine(float* out, const float* part, const int* pos, int T, int n_ra
   if (T == 0) return LL_OK;
   if (!out || !pos || (reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(part)) % 16) return LL_ERR_ARG;
   const int grid = T < 148 * 8 ? T : 148 * 8;
+  g_launch_stream = static_cast<cudaStream_t>(stream);
   k_ep_combine<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<float4*>(out), reinterpret_cast<const float4*>(part), pos, T, n_ranks, d / 4);
   return check_launch("k_ep_combine");
@@ -193,6 +196,7 @@ int ll_ep_combine_slots(float* grad_w, const float* part, const int* pos, const 
   if (T == 0) return LL_OK;
   if (!grad_w || !pos || !idx) return LL_ERR_ARG;
   const int64_t n = (int64_t)T * k;
+  g_launch_stream = static_cast<cudaStream_t>(stream);
   k_ep_combine_slots<<<(unsigned)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       grad_w, part, pos, idx, T, k, E, n_ranks);
   return check_launch("k_ep_combine_slots");

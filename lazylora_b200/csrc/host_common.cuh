@@ -16,6 +16,13 @@ extern thread_local int g_launch_count;
 extern thread_local cudaEvent_t* g_prof_events;
 extern thread_local int g_prof_n;
 extern thread_local int g_prof_i;
+// Optional CUDA event recorded after every kernel launch (profiling hook), on the stream of
+// the C call in progress, with the kernel's name.
+extern thread_local cudaStream_t g_launch_stream;
+extern thread_local cudaEvent_t* g_lev;
+extern thread_local const char** g_lev_names;
+extern thread_local int g_lev_n;
+extern thread_local int g_lev_i;
 
 inline int cuda_fail(cudaError_t e, const char* what) {
   snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s", what, cudaGetErrorString(e));
@@ -38,8 +45,17 @@ inline int check_launch(const char* what) {
   g_launch_count++;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, what);
+  if (g_lev && g_lev_i < g_lev_n) {
+    g_lev_names[g_lev_i] = what;
+    LL_CUDA(cudaEventRecord(g_lev[g_lev_i++], g_launch_stream));
+  }
   return LL_OK;
 }
+
+// The stream argument of a C entry point, remembered for the launch-event hook.
+#define LL_STREAM(stream_arg) \
+  cudaStream_t s = static_cast<cudaStream_t>(stream_arg); \
+  ::ll::g_launch_stream = s
 
 struct DeviceInfo {
   int sms = 0;
@@ -113,7 +129,11 @@ int launch_gemm(const CUtensorMap* pk, const CUtensorMap* sc, const CUtensorMap*
   const bool prof = g_prof_events && g_prof_i + 2 <= g_prof_n;
   if (prof) LL_CUDA(cudaEventRecord(g_prof_events[g_prof_i], stream));
   kern<<<di.sms, Cfg::kThreads, Cfg::SMEM, stream>>>(tm, a);
-  const int rc = check_launch("grouped_mxfp4_gemm");
+  const int rc = check_launch(EPI == EPI_F1   ? "grouped_mxfp4_gemm F1 gate/up"
+                              : EPI == EPI_F2 ? "grouped_mxfp4_gemm F2 down"
+                              : EPI == EPI_B1 ? "grouped_mxfp4_gemm B1 g.W2"
+                              : EPI == EPI_B2 ? "grouped_mxfp4_gemm B2 dg.W1+du.W3"
+                                              : "grouped_mxfp4_gemm");
   if (prof) {
     LL_CUDA(cudaEventRecord(g_prof_events[g_prof_i + 1], stream));
     g_prof_i += 2;

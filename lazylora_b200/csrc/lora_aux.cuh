@@ -18,15 +18,20 @@ LL_DEV float load_as_float(const void* p, int64_t i) {
 // .. + NC - 1 (N a few tens: the LoRA rank, or twice it).
 // B(k, n): BROWS -> n < N0 ? B0[n*K + k] : B1[(n-N0)*K + k]  ([N][K], e.g. LoRA A matrices)
 //          else  -> B0[k*N + n]                             ([K][N], e.g. LoRA B matrices)
-// Thread = one column x 8 rows: per k one B value (its own column) and the 8 A values as two
-// broadcast 16-byte reads, 8 FMAs. The A tile is staged transposed ([k][row]) from 16-byte
-// global loads of 8 consecutive k. K % 8 == 0; split boundaries are multiples of kSkBK.
-constexpr int kSkBK = 32, kSkTM = 8;
+// Thread = 4 columns x TM rows (TM = 8 for 32-column blocks, 4 for 16): per k one 16-byte
+// read of its 4 B values and TM/4 16-byte reads of its A values (shared by the lanes of the
+// warp on the same rows), 4 TM FMAs. The A tile is staged transposed ([k][row]) from 16-byte
+// global loads of 8 consecutive k, with the row index XOR-ed by 8 ((k / 8) % 4) so that the
+// transposing stores hit 32 distinct banks while 8-row groups stay contiguous and aligned.
+// K % 8 == 0; split boundaries are multiples of kSkBK.
+constexpr int kSkBK = 32;
 
 template <int NC>
 struct SkinnyCfg {
-  static constexpr int RG = 256 / NC;         // row groups
-  static constexpr int BM = RG * kSkTM;       // rows per block: 64 (NC = 32) or 128 (NC = 16)
+  static constexpr int CQ = NC / 4;           // column quads
+  static constexpr int RG = 256 / CQ;         // row groups
+  static constexpr int TM = NC == 32 ? 8 : 4; // rows per thread
+  static constexpr int BM = RG * TM;          // 256 rows per block
 };
 
 template <int ADT>
@@ -49,19 +54,22 @@ LL_DEV void load8_as_float(const void* A, int64_t off, float (&v)[8]) {
   }
 }
 
+LL_DEV int sk_swz(int k) { return ((k >> 3) & 3) << 3; }
+
 template <int ADT, bool BROWS, int NC>
 __global__ void __launch_bounds__(256) k_skinny(const void* __restrict__ A, int M, int K, int lda,
                                                 const float* __restrict__ B0, const float* __restrict__ B1, int N0,
                                                 int N, int kc, float* __restrict__ part) {
   using SC = SkinnyCfg<NC>;
+  constexpr int TM = SC::TM;
   __shared__ __align__(16) float As[kSkBK][SC::BM + 4];
-  __shared__ float Bs[kSkBK][NC];
+  __shared__ __align__(16) float Bs[kSkBK][NC];
   const int m0 = blockIdx.x * SC::BM, nb0 = blockIdx.y * NC;
   const int k_begin = blockIdx.z * kc, k_end = min(K, k_begin + kc);
-  const int n_l = threadIdx.x % NC, rg = threadIdx.x / NC;
-  float acc[kSkTM];
+  const int cq = threadIdx.x % SC::CQ, rg = threadIdx.x / SC::CQ;
+  float acc[TM][4];
 #pragma unroll
-  for (int i = 0; i < kSkTM; i++) acc[i] = 0.f;
+  for (int i = 0; i < TM; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   for (int k0 = k_begin; k0 < k_end; k0 += kSkBK) {
     for (int i = threadIdx.x; i < SC::BM * (kSkBK / 8); i += 256) {
       const int r = i / (kSkBK / 8), c8 = (i % (kSkBK / 8)) * 8;
@@ -73,8 +81,9 @@ __global__ void __launch_bounds__(256) k_skinny(const void* __restrict__ A, int 
 #pragma unroll
         for (int j = 0; j < 8; j++) v[j] = 0.f;
       }
+      const int rs = r ^ sk_swz(c8);
 #pragma unroll
-      for (int j = 0; j < 8; j++) As[c8 + j][r] = v[j];
+      for (int j = 0; j < 8; j++) As[c8 + j][rs] = v[j];
     }
     for (int i = threadIdx.x; i < NC * kSkBK; i += 256) {
       int n, c;
@@ -88,25 +97,34 @@ __global__ void __launch_bounds__(256) k_skinny(const void* __restrict__ A, int 
       Bs[c][n] = v;
     }
     __syncthreads();
-#pragma unroll 8
+#pragma unroll 4
     for (int kk = 0; kk < kSkBK; kk++) {
-      const float b = Bs[kk][n_l];
-      const float4 a0 = *reinterpret_cast<const float4*>(&As[kk][rg * kSkTM]);
-      const float4 a1 = *reinterpret_cast<const float4*>(&As[kk][rg * kSkTM + 4]);
-      acc[0] = fmaf(a0.x, b, acc[0]); acc[1] = fmaf(a0.y, b, acc[1]);
-      acc[2] = fmaf(a0.z, b, acc[2]); acc[3] = fmaf(a0.w, b, acc[3]);
-      acc[4] = fmaf(a1.x, b, acc[4]); acc[5] = fmaf(a1.y, b, acc[5]);
-      acc[6] = fmaf(a1.z, b, acc[6]); acc[7] = fmaf(a1.w, b, acc[7]);
+      const float4 b = *reinterpret_cast<const float4*>(&Bs[kk][cq * 4]);
+      const float* ar = &As[kk][(rg * TM) ^ sk_swz(kk)];
+      float a[TM];
+#pragma unroll
+      for (int t = 0; t < TM; t += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(ar + t);
+        a[t] = v.x; a[t + 1] = v.y; a[t + 2] = v.z; a[t + 3] = v.w;
+      }
+#pragma unroll
+      for (int t = 0; t < TM; t++) {
+        acc[t][0] = fmaf(a[t], b.x, acc[t][0]); acc[t][1] = fmaf(a[t], b.y, acc[t][1]);
+        acc[t][2] = fmaf(a[t], b.z, acc[t][2]); acc[t][3] = fmaf(a[t], b.w, acc[t][3]);
+      }
     }
     __syncthreads();
   }
-  const int n = nb0 + n_l;
-  if (n >= N) return;
   float* out = part + (int64_t)blockIdx.z * M * N;
 #pragma unroll
-  for (int i = 0; i < kSkTM; i++) {
-    const int m = m0 + rg * kSkTM + i;
-    if (m < M) out[(int64_t)m * N + n] = acc[i];
+  for (int t = 0; t < TM; t++) {
+    const int m = m0 + rg * TM + t;
+    if (m >= M) continue;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const int n = nb0 + cq * 4 + c;
+      if (n < N) out[(int64_t)m * N + n] = acc[t][c];
+    }
   }
 }
 

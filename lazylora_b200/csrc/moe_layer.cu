@@ -318,10 +318,10 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   w.hg = c.take<float>((size_t)T * r);
   w.hu = c.take<float>((size_t)T * r);
   w.opart = c.take<float>((size_t)nseg_max * r * (d > f ? d : f));
-  {  // split-K partials of the skinny products: nsplit * mblocks * nblocks <= 4 * SMs +
-     // mblocks * nblocks blocks of 2048 outputs (BM * NC); SMs <= 160
+  {  // split-K partials of the skinny products: nsplit * mblocks * nblocks <= 2 * SMs +
+     // mblocks * nblocks blocks of at most 8192 outputs (BM * NC); SMs <= 160
     const int64_t rows = P > T ? P : T;
-    w.skpart = c.take<float>((size_t)4 * 160 * 2048 + (size_t)(rows + 128) * (2 * r + 32));
+    w.skpart = c.take<float>((size_t)2 * 160 * 8192 + (size_t)(rows + 256) * (2 * r + 32));
   }
   if (out) *out = w;
   return c.off + 256;
@@ -355,8 +355,8 @@ static int skinny(const void* A, int adt, bool brows, int M, int K, const float*
   const bool nc16 = N <= 16;
   const int BM = nc16 ? SkinnyCfg<16>::BM : SkinnyCfg<32>::BM, NC = nc16 ? 16 : 32;
   const int mblocks = (M + BM - 1) / BM, nblocks = (N + NC - 1) / NC;
-  // about four blocks per SM, split over K
-  int nsplit = (4 * device_info().sms + mblocks * nblocks - 1) / (mblocks * nblocks);
+  // about two blocks per SM, split over K
+  int nsplit = (2 * device_info().sms + mblocks * nblocks - 1) / (mblocks * nblocks);
   nsplit = std::max(1, std::min(nsplit, (K + kSkBK - 1) / kSkBK));
   const int kc = ((K + nsplit - 1) / nsplit + kSkBK - 1) / kSkBK * kSkBK;
   nsplit = (K + kc - 1) / kc;
@@ -446,7 +446,7 @@ size_t ll_mxfp4_transposed_bytes(int E, int R, int C, int which) {
 int ll_moe_prepare(const ll_moe_layer* L, int32_t* beta_out, void* stream) {
   if (!L || !beta_out || L->E <= 0 || L->d <= 0 || L->f <= 0 || L->d % 128 || L->f % 128) return LL_ERR_ARG;
   if (!L->w1t || !L->w3t || !L->w2t || !L->s1t || !L->s3t || !L->s2t) return LL_ERR_ARG;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LL_STREAM(stream);
   const int E = L->E, d = L->d, f = L->f;
   LL_TRY(launch_prepare_beta(L->w1s, L->w3s, E, f, d, L->s13_stride, beta_out, 0, s));
   LL_TRY(launch_prepare_beta(L->w2s, nullptr, E, d, f, L->s2_stride, beta_out, 1, s));
@@ -469,7 +469,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   if (!x || !idx || !w || !out || !ws || (x_dtype != 0 && x_dtype != 1)) return LL_ERR_ARG;
   LL_TRY(check_arch());
   if (ws_bytes < ll_moe_workspace_bytes(L, T, k)) return LL_ERR_WORKSPACE;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LL_STREAM(stream);
   LayerWs W;
   layer_layout(ws, L, T, k, &W);
   const int d = L->d, f = L->f, E = L->E, r = L->r;
@@ -559,7 +559,7 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
   if ((x_dtype != 0 && x_dtype != 1) || (g_dtype != 0 && g_dtype != 1)) return LL_ERR_ARG;
   LL_TRY(check_arch());
   if (ws_bytes < ll_moe_workspace_bytes(L, T, k)) return LL_ERR_WORKSPACE;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LL_STREAM(stream);
   LayerWs W;
   layer_layout(ws, L, T, k, &W);
   const int d = L->d, f = L->f, E = L->E, r = L->r;
@@ -662,7 +662,7 @@ int ll_moe_permutation(const ll_moe_layer* L, int T, int k, void* ws, int* offse
   if (!L || !ws || !offsets || !perm_token || !perm_slot || T <= 0 || k <= 0) return LL_ERR_ARG;
   LayerWs W;
   layer_layout(ws, L, T, k, &W);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LL_STREAM(stream);
   LL_CUDA(cudaMemcpyAsync(offsets, W.offsets, sizeof(int) * (L->E + 1), cudaMemcpyDeviceToDevice, s));
   LL_CUDA(cudaMemcpyAsync(perm_token, W.perm_token, sizeof(int) * T * k, cudaMemcpyDeviceToDevice, s));
   LL_CUDA(cudaMemcpyAsync(perm_slot, W.perm_slot, sizeof(int) * T * k, cudaMemcpyDeviceToDevice, s));
@@ -674,7 +674,7 @@ int ll_moe_status(const ll_moe_layer* L, int T, int k, void* ws, void* stream) {
   if (!L || !ws) return LL_ERR_ARG;
   LayerWs W;
   layer_layout(ws, L, T, k, &W);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LL_STREAM(stream);
   LL_CUDA(cudaStreamSynchronize(s));
   LL_CUDA(cudaGetLastError());
   const int rc = read_status(W.st, s);

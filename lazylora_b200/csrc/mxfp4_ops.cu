@@ -13,6 +13,13 @@ thread_local cudaEvent_t* g_prof_events = nullptr;
 thread_local int g_prof_n = 0;
 thread_local int g_prof_i = 0;
 static thread_local cudaEvent_t g_prof_store[64];
+thread_local cudaStream_t g_launch_stream = nullptr;
+thread_local cudaEvent_t* g_lev = nullptr;
+thread_local const char** g_lev_names = nullptr;
+thread_local int g_lev_n = 0;
+thread_local int g_lev_i = 0;
+static thread_local cudaEvent_t g_lev_store[512];
+static thread_local const char* g_lev_name_store[512];
 
 DeviceInfo device_info() {
   static DeviceInfo cache[64];
@@ -422,6 +429,20 @@ const char* ll_last_cuda_error(void) { return g_last_cuda_error; }
 
 int ll_last_launch_count(void) { return g_launch_count; }
 
+int ll_profile_launch_events(void* const* events, int n) {
+  if (n < 0 || n > 512 || (n > 0 && !events)) return LL_ERR_ARG;
+  for (int i = 0; i < n; i++) g_lev_store[i] = static_cast<cudaEvent_t>(events[i]);
+  g_lev = n > 0 ? g_lev_store : nullptr;
+  g_lev_names = g_lev_name_store;
+  g_lev_n = n;
+  g_lev_i = 0;
+  return LL_OK;
+}
+
+int ll_profile_launch_recorded(void) { return g_lev_i; }
+
+const char* ll_profile_launch_name(int i) { return (i >= 0 && i < g_lev_i) ? g_lev_name_store[i] : ""; }
+
 int ll_mxfp4_threads(void) { return device_info().sms; }
 
 int ll_profile_gemm_events(void* const* events, int n) {
@@ -441,7 +462,7 @@ int ll_mxfp4_dequant(void* out, const uint8_t* packed, const uint8_t* scales, in
                      int out_dtype, void* stream) {
   if (K <= 0 || R <= 0 || K % 32 || !out || !packed || !scales || scale_stride < K / 32) return LL_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(packed) & 15)) return LL_ERR_ARG;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LL_STREAM(stream);
   const int64_t groups = (int64_t)R * (K / 32);
   const int grid = (int)std::min<int64_t>((groups + 255) / 256, 148 * 16);
   if (out_dtype == 0) k_dequant<0><<<grid, 256, 0, s>>>(out, packed, scales, K, R, scale_stride);
@@ -457,7 +478,7 @@ int ll_mxfp4_gemm(float* y, const float* x, const uint8_t* packed, const uint8_t
   if (!y || !x || !packed || !scales || !ws) return LL_ERR_ARG;
   LL_TRY(check_arch());
   if (ws_bytes < ll_mxfp4_workspace_bytes(M, K, R)) return LL_ERR_WORKSPACE;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LL_STREAM(stream);
   DropInWs w;
   dropin_layout(ws, M, K > R ? K : R, R, K, &w);
   g_launch_count = 0;
@@ -493,7 +514,7 @@ int ll_mxfp4_gemm_t(float* y, const float* dy, const uint8_t* packed, const uint
   if (!y || !dy || !packed || !scales || !ws) return LL_ERR_ARG;
   LL_TRY(check_arch());
   if (ws_bytes < ll_mxfp4_workspace_bytes(M, K, R)) return LL_ERR_WORKSPACE;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LL_STREAM(stream);
   DropInWs w;
   dropin_layout(ws, M, K > R ? K : R, R, K, &w);
   g_launch_count = 0;

@@ -88,7 +88,7 @@ extern "C" int ll_mxfp4_gemm_noalloc(float* y, const float* x, const uint8_t* pa
   LL_TRY(scratch_address(&base));
   NoAllocLayout w;
   noalloc_layout(base, M, K, &w);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LL_STREAM(stream);
   g_launch_count = 0;
   LL_TRY(reset_status(w.st, s));
   LL_TRY(launch_single_expert_chunks(w.chunks, w.n_chunks, M, kNoAllocNmax, s));

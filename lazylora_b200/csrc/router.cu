@@ -212,7 +212,7 @@ int ll_route_topk(const void* x, int x_dtype, const float* router_w, const float
   if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(ws) % 256) return LL_ERR_ARG;
   const RouterPlan p = router_plan(T, d, E, x_dtype);
   if (ws_bytes < p.bytes) return LL_ERR_WORKSPACE;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LL_STREAM(stream);
   g_launch_count = 0;
   LL_TRY(router_logits_tc(x, x_dtype, router_w, T, d, E, ws, p, s));
   const float* part = reinterpret_cast<const float*>(static_cast<uint8_t*>(ws) + p.off_part);
@@ -230,8 +230,9 @@ int ll_route_select(const float* scores, const float* scores_for_choice, int T, 
                     float routed_scaling_factor, int64_t* idx, float* w, void* stream) {
   if (T <= 0 || E <= 0 || k <= 0 || k > 32 || k > E || E > 2048 || !scores || !scores_for_choice || !idx || !w)
     return LL_ERR_ARG;
+  LL_STREAM(stream);
   return launch_select<1>(scores, scores_for_choice, nullptr, T, E, k, renormalize, routed_scaling_factor, idx, w,
-                          nullptr, static_cast<cudaStream_t>(stream));
+                          nullptr, s);
 }
 
 }  // extern "C"

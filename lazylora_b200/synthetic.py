@@ -64,6 +64,9 @@ CONFIGS: Dict[str, LayerConfig] = {
     # configs[1]'s per-expert load (9 tokens per expert) on 64 experts: 1.5 GB of weights,
     # larger than L2 but small enough for multi-pass ncu captures
     "prof": LayerConfig(d=7168, f=2048, E=64, k=8, T=72),
+    # configs[1]'s token count (the LoRA products, combines and router see T = 1024, 8192 pairs)
+    # on 64 experts, for captures of the small kernels around the GEMMs
+    "prof_aux": LayerConfig(d=7168, f=2048, E=64, k=8, T=1024),
     # small parity cases (K <= 4096 so the reference C kernel runs unchunked)
     "tiny": LayerConfig(d=256, f=128, E=8, k=2, T=16, r=4, alpha=8, x_dtype="f32"),
     "small": LayerConfig(d=1024, f=512, E=16, k=4, T=48, r=16, x_dtype="bf16"),
