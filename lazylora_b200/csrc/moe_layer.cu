@@ -268,7 +268,10 @@ static int choose_nmax(const ll_moe_layer* L, int T, int k) {
   const int64_t slots = (int64_t)T * k;
   const int64_t pairs = L->rows_hint > 0 && L->rows_hint < slots ? L->rows_hint : slots;
   const double mean = (double)pairs / (L->E > 0 ? L->E : 1);
-  return mean <= 10.0 ? 16 : mean <= 12.0 ? 32 : (mean <= 40.0 ? 64 : 128);
+  // the narrowest tile that holds nearly every expert's rows in one chunk (a second chunk
+  // re-reads the expert's weights): Poisson-like counts exceed 16 rows for ~1% of experts at a
+  // mean of 9, 32 rows for ~0.1% at 18, 64 rows for ~1% at 48
+  return mean <= 10.0 ? 16 : mean <= 22.0 ? 32 : (mean <= 48.0 ? 64 : 128);
 }
 
 static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, LayerWs* out) {
