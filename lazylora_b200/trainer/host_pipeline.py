@@ -19,19 +19,49 @@ from typing import Callable, List, Sequence
 import torch
 
 
+class CapturedStep:
+    """`step_fn(x, g)` captured once as a CUDA graph over the fixed device tensors x and g;
+    replay() reruns the whole step (tens of kernels) as one graph launch and returns the
+    same output tensors, overwritten. The step must not synchronise with the host (the
+    library's routing, forward and backward calls do not). Work of a replay is ordered after
+    the current stream's earlier work and before its later work."""
+
+    def __init__(self, step_fn: Callable, x: torch.Tensor, g: torch.Tensor, warmup: int = 1):
+        cur = torch.cuda.current_stream(x.device)
+        side = torch.cuda.Stream(device=x.device)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            for _ in range(warmup):             # lazily allocated workspaces exist before capture
+                step_fn(x, g)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=side):
+                self.outputs = step_fn(x, g)
+        cur.wait_stream(side)
+        self.x, self.g = x, g
+
+    def replay(self):
+        self.graph.replay()
+        return self.outputs
+
+
 class HostStepPipeline:
     """Runs `step_fn` over batches held in pinned host memory, copies overlapped with compute.
 
     step_fn: (x_dev, g_dev) -> sequence of device tensors (the step's results).
     out_index: which results to copy back to host, in the order of the host buffers.
+    graph: run each step as a CUDA graph (one per input slot, captured on first use); a
+        graph's outputs are rewritten by its next replay, which therefore waits for their
+        copies to the host.
     """
 
-    def __init__(self, step_fn: Callable, out_index: Sequence[int], device=None):
+    def __init__(self, step_fn: Callable, out_index: Sequence[int], device=None, graph: bool = False):
         self.step_fn = step_fn
         self.out_index = list(out_index)
         self.device = torch.device(device if device is not None else "cuda")
         self.h2d = torch.cuda.Stream(device=self.device)
         self.d2h = torch.cuda.Stream(device=self.device)
+        self.graph = graph
+        self._captured = None
         self._slots = None
 
     def _buffers(self, x_h: torch.Tensor, g_h: torch.Tensor):
@@ -39,7 +69,17 @@ class HostStepPipeline:
         if self._slots is None or self._slots[0] != want:
             mk = lambda t: torch.empty(t.shape, dtype=t.dtype, device=self.device)
             self._slots = (want, [(mk(x_h), mk(g_h)) for _ in range(2)])
+            self._captured = None
         return self._slots[1]
+
+    def _graphs(self, slots, x_h, g_h):
+        if self._captured is None:
+            for s in range(2):                   # capture on real data so the warm-up is valid
+                slots[s][0].copy_(x_h)
+                slots[s][1].copy_(g_h)
+            self._captured = [CapturedStep(self.step_fn, slots[s][0], slots[s][1]) for s in range(2)]
+            torch.cuda.current_stream(self.device).synchronize()
+        return self._captured
 
     def run(self, xs_h: Sequence[torch.Tensor], gs_h: Sequence[torch.Tensor],
             outs_h: Sequence[Sequence[torch.Tensor]]) -> List:
@@ -58,6 +98,8 @@ class HostStepPipeline:
                 raise ValueError("host buffers must be pinned CPU tensors")
         comp = torch.cuda.current_stream(self.device)
         slots = self._buffers(xs_h[0], gs_h[0])
+        graphs = self._graphs(slots, xs_h[0], gs_h[0]) if self.graph else None
+        copied = [None, None]     # event: the outputs of slot s's graph reached the host
         start = torch.cuda.Event()
         start.record(comp)
         self.h2d.wait_event(start)
@@ -83,7 +125,12 @@ class HostStepPipeline:
         for i in range(n):
             s = i % 2
             comp.wait_event(loaded[s])
-            res = self.step_fn(slots[s][0], slots[s][1])
+            if graphs is not None:
+                if copied[s] is not None:
+                    comp.wait_event(copied[s])
+                res = graphs[s].replay()
+            else:
+                res = self.step_fn(slots[s][0], slots[s][1])
             done = torch.cuda.Event()
             done.record(comp)
             freed[s] = done
@@ -91,7 +138,11 @@ class HostStepPipeline:
                 self.d2h.wait_event(done)
                 for j, o in zip(self.out_index, outs_h[i]):
                     o.copy_(res[j], non_blocking=True)
-                    res[j].record_stream(self.d2h)
+                    if graphs is None:
+                        res[j].record_stream(self.d2h)
+                ev = torch.cuda.Event()
+                ev.record(self.d2h)
+                copied[s] = ev
             if i + 2 < n:
                 load(i + 2)
         end = torch.cuda.Event()

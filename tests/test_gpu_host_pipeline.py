@@ -61,3 +61,28 @@ def test_pipeline_rejects_pageable_buffers():
     pipe = HostStepPipeline(step, out_index=[0])
     with pytest.raises(ValueError):
         pipe.run([x], [x], [(torch.zeros(cfg.T, cfg.d),)])
+
+
+def test_captured_step_and_graph_pipeline_match_eager():
+    from lazylora_b200.trainer.host_pipeline import CapturedStep, HostStepPipeline
+    cfg, step = _setup()
+    gen = torch.Generator().manual_seed(5)
+    x = torch.randn(cfg.T, cfg.d, generator=gen).to(torch.bfloat16).cuda()
+    g = torch.randn(cfg.T, cfg.d, generator=gen).to(torch.bfloat16).cuda()
+    want = step(x, g)
+    cap = CapturedStep(step, x, g)
+    got = cap.replay()
+    torch.cuda.synchronize()
+    for j in range(3):
+        assert torch.equal(got[j], want[j]), j
+    n = 3
+    xs = [torch.randn(cfg.T, cfg.d, generator=gen).to(torch.bfloat16).pin_memory() for _ in range(n)]
+    gs = [torch.randn(cfg.T, cfg.d, generator=gen).to(torch.bfloat16).pin_memory() for _ in range(n)]
+    pinned = lambda *shape: torch.empty(shape, dtype=torch.float32).pin_memory()
+    outs = [(pinned(cfg.T, cfg.d), pinned(cfg.T, cfg.d), pinned(cfg.T, cfg.k)) for _ in range(n)]
+    HostStepPipeline(step, out_index=[0, 1, 2], graph=True).run(xs, gs, outs)
+    torch.cuda.synchronize()
+    for i in range(n):
+        ref = step(xs[i].cuda(), gs[i].cuda())
+        for j in range(3):
+            assert torch.equal(outs[i][j], ref[j].cpu()), (i, j)
