@@ -12,6 +12,14 @@
 
 #define LL_DEV __device__ __forceinline__
 
+// K per tensor-memory / activation ring stage of the grouped GEMM (64 or 128); each 128-K
+// packed weight stage feeds 128 / LL_KS ring stages. 64-K stages double the ring depth for the
+// same tensor memory but also every per-stage barrier and commit; they measured 16 % slower
+// on configs[1] and 3 % on 128-row tiles, so 128 is the default.
+#ifndef LL_KS
+#define LL_KS 128
+#endif
+
 namespace ll {
 
 // ------------------------------------------------------------------------------ status

@@ -121,7 +121,9 @@ struct GemmCfg {
   static constexpr int kDqWarp0 = 4, kDqWarps = 16;
   static constexpr int kEpWarp0 = 20, kEpWarps = 4;
   static constexpr int BK = 128;                          // K per packed (TMA) stage
-  static constexpr int KS = BK;                           // K per A/B ring stage
+  static constexpr int KS = LL_KS;                        // K per A/B ring stage (64 or 128)
+  static constexpr int SUBS = BK / KS;                    // ring stages per packed stage
+  static_assert(KS == 64 || KS == 128, "ring stage");
   static constexpr int PK_BYTES = 128 * 64;               // 128 rows x 64 packed bytes
   static constexpr int SC_BYTES = COLSCALE ? 4 * 128 * 2  // 4 row groups x 128 k x fp16
                                            : 128 * 16;    // 128 rows x 16 scale bytes
@@ -139,10 +141,11 @@ struct GemmCfg {
   // Dequant stage groups: group j of dequant warps fills ring stages g with g % GROUPS == j,
   // SEGW 32-K segments per warp, so GROUPS stages fill at once and a warp pays its barrier
   // round trip once per SEGW segments.
-  static constexpr int GROUPS = S_AB >= 5 ? 4 : (S_AB >= 3 ? 2 : 1);
-  static constexpr int SEGW = GROUPS;                     // segments a warp decodes per stage
-  static_assert((kDqWarps / 4) % GROUPS == 0 && (kDqWarps / 4 / GROUPS) * SEGW == 4, "segment cover");
-  static constexpr int kDqPerStage = kDqWarps / GROUPS;   // warps that fill one stage
+  static constexpr int GROUPS = KS == 64 ? 2 : (S_AB >= 5 ? 4 : (S_AB >= 3 ? 2 : 1));
+  static constexpr int SEGW = (KS / 32) * GROUPS / 4;     // segments a warp decodes per stage
+  static_assert(SEGW >= 1 && (kDqWarps / 4) % GROUPS == 0 && (kDqWarps / 4 / GROUPS) * SEGW == KS / 32,
+                "segment cover");
+  static constexpr int kDqPerStage = kDqWarps / GROUPS;   // warps that fill one ring stage
   // a dequant group may wait on a stage up to GROUPS - 1 stages ahead of the others; a ring
   // shorter than that would let a parity wait match a phase one ring cycle early
   static constexpr int TMEM_COLS0 = A_BASE + S_AB * A_STAGE_COLS;
@@ -211,12 +214,13 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, N_MAX> tm, const GemmArg
 
   const int K = args.K;
   const int n_stage = (K + C::BK - 1) / C::BK;   // packed (TMA) stages per unit
-  const int n_sub = (K + C::KS - 1) / C::KS;     // A/B ring stages per unit
+  const int n_sub = n_stage * C::SUBS;          // A/B ring stages per unit (a K tail past the
+                                                 // last 64 columns decodes zeros)
   // with one weight matrix the two issuers take alternate stages; a 1-stage K leaves one idle
   const int chains_used = n_sub < C::PM ? n_sub : C::PM;   // chains of a matrix that got a stage
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < C::S_P; i++) { mbar_init(&pfull[i], 1); mbar_init(&pempty[i], C::kDqPerStage); }
+    for (int i = 0; i < C::S_P; i++) { mbar_init(&pfull[i], 1); mbar_init(&pempty[i], C::kDqPerStage * C::SUBS); }
     for (int i = 0; i < C::S_AB; i++) { mbar_init(&full[i], C::kDqPerStage); mbar_init(&empty[i], NMAT); }
     for (int i = 0; i < C::S_B; i++) { mbar_init(&bfull[i], 1); mbar_init(&bempty[i], NMAT); }
     for (int i = 0; i < 2; i++) { mbar_init(&accfull[i], C::CH); mbar_init(&accempty[i], C::kEpWarps); }
@@ -393,18 +397,21 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, N_MAX> tm, const GemmArg
     const int32_t* beta = args.epi.beta;
     const int bcol = args.epi.beta_col;
     int g = grp;                                 // ring stage index over this CTA's stages
-    int u = blockIdx.x, ks = grp;
-    while (ks >= n_stage) { ks -= n_stage; u += gridDim.x; }
+    int u = blockIdx.x, kss = grp;               // kss: ring stage within the unit
+    while (kss >= n_sub) { kss -= n_sub; u += gridDim.x; }
     int bias = (u < n_units && !COLSCALE && beta) ? beta[args.chunks[u / args.mtiles].e * 2 + bcol] : 0;
     while (u < n_units) {
-      const int ps = g % C::S_P, as = g % C::S_AB;
-      const uint32_t pph = (uint32_t)(g / C::S_P) & 1u, aph = (uint32_t)(g / C::S_AB) & 1u;
+      const int gp = g / C::SUBS;                // packed stage (global over the CTA's stages)
+      const int ks = kss / C::SUBS;              // packed stage within the unit
+      const int segb = (g % C::SUBS) * (C::KS / 32);   // first 32-K segment of this ring stage
+      const int ps = gp % C::S_P, as = g % C::S_AB;
+      const uint32_t pph = (uint32_t)(gp / C::S_P) & 1u, aph = (uint32_t)(g / C::S_AB) & 1u;
       if (!mbar_wait(&pfull[ps], pph, abort_flag, st, 6)) break;
       const uint8_t* stage = smem + C::OFF_P + ps * C::P_STAGE;
       bool waited = false, ok = true;
 #pragma unroll
       for (int j = 0; j < C::SEGW; j++) {
-        const int seg = seg0 + j;
+        const int seg = segb + seg0 + j;         // 32-K segment within the packed stage
 #pragma unroll
         for (int i = 0; i < NMAT; i++) {
           const uint8_t* pk = stage + i * C::PK_BYTES;
@@ -436,7 +443,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, N_MAX> tm, const GemmArg
             tc_fence_after();
             waited = true;
           }
-          tmem_st16(tmem + lane_base + C::A_BASE + as * C::A_STAGE_COLS + i * (C::KS / 2) + seg * 16, o);
+          tmem_st16(tmem + lane_base + C::A_BASE + as * C::A_STAGE_COLS + i * (C::KS / 2) + (seg0 + j) * 16, o);
         }
         if (!ok) break;
       }
@@ -448,9 +455,9 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, N_MAX> tm, const GemmArg
       __syncwarp();
       if (lane == 0) mbar_arrive(&full[as]);
       g += C::GROUPS;
-      ks += C::GROUPS;
-      while (ks >= n_stage) {                    // into the next unit(s)
-        ks -= n_stage;
+      kss += C::GROUPS;
+      while (kss >= n_sub) {                     // into the next unit(s)
+        kss -= n_sub;
         u += gridDim.x;
         if (u < n_units && !COLSCALE && beta) bias = beta[args.chunks[u / args.mtiles].e * 2 + bcol];
       }

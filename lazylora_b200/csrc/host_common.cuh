@@ -96,7 +96,7 @@ int make_map_nd(CUtensorMap* m, CUtensorMapDataType dt, const void* base, int ra
                 const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle sw);
 
 // fp16 activation rows [rows][K] (K % 64 == 0), one map per tile height 16 c (c = 1..n): a
-// box holds one 128-K ring stage as two 64-column halves, [half][16 c rows][128 bytes], K-major
+// box holds one ring stage (LL_KS columns) as 64-column halves, [half][16 c rows][128 bytes], K-major
 // with the 128-byte swizzle, so a stage of a chunk of up to 16 c rows is one TMA instruction.
 // The halves are a third dimension of stride 128 bytes. With nb = 2 a fourth dimension of
 // stride mat_stride elements reaches the second operand (the gate and up gradients), and the
@@ -107,7 +107,7 @@ inline int make_act_maps(CUtensorMap* maps, int n, const __half* base, int64_t r
   const uint64_t dims[4] = {64, (uint64_t)rows, (uint64_t)K / 64, (uint64_t)nb};
   const uint64_t strides[3] = {(uint64_t)K * 2, 128, (uint64_t)mat_stride * 2};
   for (int c = 1; c <= n; c++) {
-    const uint32_t box[4] = {64, (uint32_t)(16 * c), 2, (uint32_t)nb};
+    const uint32_t box[4] = {64, (uint32_t)(16 * c), LL_KS / 64, (uint32_t)nb};
     LL_TRY(make_map_nd(&maps[c - 1], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base, nb == 2 ? 4 : 3, dims, strides, box,
                        CU_TENSOR_MAP_SWIZZLE_128B));
   }
