@@ -490,6 +490,77 @@ def run_decode(args, cfg, rank, local, world, dist):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------ latent routed block (Kimi K3 shape)
+def run_latent(args, cfg, rank, local, world, dist):
+    """Route + forward + backward of the latent routed block: down-projection 7168 -> d_l
+    (cfg.d), the routed experts at width d_l, RMSNorm of their fp32 sum, up-projection back
+    (lazy_trainer.py:722-735). HBM bound: twice the touched experts' MXFP4 bytes plus the two
+    projections' bf16 weights read in the forward and again in the backward."""
+    ClockSampler.start(local)
+    from lazylora_b200 import _lib as L
+    from lazylora_b200.core.moe_router import KimiK3MoERouter
+    from lazylora_b200.synthetic import make_layer_device
+    from lazylora_b200.trainer.latent_moe import LatentRoutedMoE
+    from lazylora_b200.trainer.routed_experts import RoutedExpertsLayer
+    d_h = args.latent_hidden
+    dev = torch.device("cuda", local)
+    lib = L.load()
+    inp = make_layer_device(cfg, device=dev)
+    layer = RoutedExpertsLayer.from_inputs(inp, cfg.scaling, device=dev)
+    del inp["w1p"], inp["w3p"], inp["w2p"]
+    gen = torch.Generator(device=dev).manual_seed(cfg.seed + 7)
+    down_w = (torch.randn(cfg.d, d_h, generator=gen, device=dev) / d_h ** 0.5).to(torch.bfloat16)
+    up_w = (torch.randn(d_h, cfg.d, generator=gen, device=dev) / cfg.d ** 0.5).to(torch.bfloat16)
+    norm_w = torch.ones(cfg.d, device=dev)
+    blk = LatentRoutedMoE(layer, down_w, up_w, norm_w)
+    router = KimiK3MoERouter(hidden_size=d_h, num_experts=cfg.E, top_k=cfg.k, device=dev)
+    Wr = torch.randn(cfg.E, d_h, generator=gen, device=dev) * 0.02
+    br = torch.zeros(cfg.E, device=dev)
+    x = torch.randn(cfg.T, d_h, generator=gen, device=dev).to(torch.bfloat16)
+    g = torch.randn(cfg.T, d_h, generator=gen, device=dev).to(torch.bfloat16)
+    stream = torch.cuda.current_stream()
+    state = {}
+
+    def step(xx, gg):
+        idx, w = router.forward(xx, weight=Wr, bias=br)
+        out = blk.forward(xx, idx, w)
+        gx, gw, grads = blk.backward(gg)
+        state["idx"] = idx
+        return out, gx, gw, grads
+
+    for _ in range(args.warmup):
+        step(x, g)
+    layer.check_status(cfg.T, cfg.k)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        a.record(stream)
+        for _ in range(args.steps):
+            step(x, g)
+        b.record(stream)
+        torch.cuda.synchronize()
+    layer.check_status(cfg.T, cfg.k)
+    ms = a.elapsed_time(b) / args.steps
+    U = int(torch.unique(state["idx"]).numel())
+    proj_bytes = 2 * cfg.d * d_h * 2
+    wbytes = 2 * U * expert_bytes(cfg) + 2 * proj_bytes
+    hbm_peak, _, peak_kind = _peaks()
+    roof_ms = wbytes / (hbm_peak * 1e9) * 1e3
+    line = {"metric": f"latent MoE block fwd+bwd tokens/s (d_h={d_h}, d_l={cfg.d}, f={cfg.f}, E={cfg.E}, "
+                      f"top-{cfg.k}, LoRA r={cfg.r})",
+            "value": cfg.T / (ms * 1e-3), "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 projections / fp16 expert operands, fp32 accumulate", "data": "synthetic",
+            "config": {"workload": "latent routed block (SURVEY 8(f) 1): route + down-proj + experts + RMSNorm + "
+                                   "up-proj, forward and backward", "d_h": d_h, "d_l": cfg.d, "f": cfg.f,
+                       "E": cfg.E, "k": cfg.k, "T": cfg.T, "r": cfg.r, "active_experts": U},
+            "roofline": {"bound": "hbm", "achieved": wbytes / (ms * 1e-3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": roof_ms / ms, "peak_kind": peak_kind, "algorithmic_bytes_per_step": wbytes,
+                         "roofline_ms": roof_ms},
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------------------ streaming (configs[4])
 def run_stream(args, cfg, rank, local, world, dist):
     ClockSampler.start(local)
@@ -600,6 +671,8 @@ def main():
     ap.add_argument("--graph", action="store_true", help="with --decode: replay each step as a CUDA graph")
     ap.add_argument("--zipf-gamma", type=float, default=None, help="override the config's Zipf bias scale")
     ap.add_argument("--stream", action="store_true", help="configs[4]: experts streamed from pinned host memory")
+    ap.add_argument("--latent", action="store_true", help="the latent routed block (use --config c1_latent)")
+    ap.add_argument("--latent-hidden", type=int, default=7168, help="hidden width around the latent block")
     ap.add_argument("--stream-distinct", type=int, default=1, help="distinct layers kept in pinned host memory")
     ap.add_argument("--stream-group", type=int, default=224, help="experts per streamed group")
     ap.add_argument("--h2d-peak", type=float, default=55.6, help="measured pinned H2D GB/s of the box")
@@ -618,6 +691,8 @@ def main():
             run_decode(args, cfg, rank, local, world, dist)
         elif args.stream:
             run_stream(args, cfg, rank, local, world, dist)
+        elif args.latent:
+            run_latent(args, cfg, rank, local, world, dist)
         else:
             run_ours(args, cfg, rank, local, world, dist)
             if dist is not None:

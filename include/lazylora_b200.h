@@ -212,6 +212,18 @@ int ll_ep_combine(float* out, const float* part, const int* pos, int T, int n_ra
 int ll_ep_combine_slots(float* grad_w, const float* part, const int* pos, const int64_t* idx, int T, int k, int E,
                         int n_ranks, void* stream);
 
+/* ------------------------------------------------------------------ latent RMSNorm
+ * The norm between the routed-expert sum and the latent up-projection of the Kimi K3 MoE
+ * block (lazy_trainer.py:731-733; RMSNormFunction.forward, trunk_streamer.py:27-31):
+ * y[t] = x[t] * rsqrt(mean(x[t]^2) + eps) * w, x fp32 [N, D], w fp32 [D], y fp32 (y_dtype 0)
+ * or bf16 (1); rstd fp32 [N] (optional in the forward) receives rsqrt(mean + eps) per row.
+ * The backward gives dL/dx for a frozen w from gy (fp32 or bf16) and the saved rstd. Row sums
+ * are reduced in a fixed order: bitwise reproducible. */
+int ll_rmsnorm_forward(const float* x, const float* w, int N, int D, float eps, void* y, int y_dtype, float* rstd,
+                       void* stream);
+int ll_rmsnorm_backward(const float* x, const float* w, const float* rstd, const void* gy, int gy_dtype, int N, int D,
+                        float* gx, void* stream);
+
 /* Profiling hook: record events[2i] / events[2i+1] (cudaEvent_t handles) on the launching
  * stream around the i-th grouped-GEMM launch that follows on this thread, for the first n/2
  * launches; n = 0 turns it off. Calling it again restarts at i = 0. */

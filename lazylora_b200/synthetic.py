@@ -64,6 +64,9 @@ CONFIGS: Dict[str, LayerConfig] = {
     # configs[1]'s per-expert load (9 tokens per expert) on 64 experts: 1.5 GB of weights,
     # larger than L2 but small enough for multi-pass ncu captures
     "prof": LayerConfig(d=7168, f=2048, E=64, k=8, T=72),
+    # configs[1] with the routed experts at Kimi K3's latent width (routed_expert_hidden_size
+    # 3584; the block projects 7168 -> 3584 -> experts -> RMSNorm -> 7168)
+    "c1_latent": LayerConfig(d=3584, f=2048, E=896, k=8, T=1024),
     # configs[1]'s token count (the LoRA products, combines and router see T = 1024, 8192 pairs)
     # on 64 experts, for captures of the small kernels around the GEMMs
     "prof_aux": LayerConfig(d=7168, f=2048, E=64, k=8, T=1024),
