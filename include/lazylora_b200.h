@@ -30,7 +30,8 @@ typedef enum {
   LL_ERR_TIMEOUT = 3,    /* a device-side bounded wait ran out; the kernel wound down */
   LL_ERR_WORKSPACE = 4,  /* workspace smaller than *_workspace_bytes asked for */
   LL_ERR_RANGE = 5,      /* value outside what the kernel represents exactly */
-  LL_ERR_ARCH = 6        /* device is not sm_100 */
+  LL_ERR_ARCH = 6,       /* device is not sm_100 */
+  LL_ERR_IO = 7          /* a host file read failed (ll_pread_batch) */
 } ll_status;
 
 /* Human-readable text for a status code (static storage). */
@@ -211,6 +212,17 @@ int ll_ep_combine(float* out, const float* part, const int* pos, int T, int n_ra
  * 0 for a slot whose id is outside [0, E). */
 int ll_ep_combine_slots(float* grad_w, const float* part, const int* pos, const int64_t* idx, int T, int k, int E,
                         int n_ranks, void* stream);
+
+/* ------------------------------------------------------------- checkpoint reads
+ * Reads n byte ranges of files into host buffers (pinned, when they feed host-to-device
+ * copies) with `threads` worker threads: range i is [offsets[i], offsets[i] + sizes[i]) of
+ * paths[i] into dsts[i]. Short reads continue; a transient EIO is retried up to `retries`
+ * times, sleeping retry_ms * attempt and reopening the file, the policy of the reference's
+ * MmapTensorStreamer._read_range (mmap_loader.py:260-294). On failure returns LL_ERR_IO with
+ * the first failing range in *failed_index and the reason in ll_last_cuda_error(); the bytes
+ * read are counted in *bytes_done. No CUDA call is made. */
+int ll_pread_batch(int n, const char* const* paths, const int64_t* offsets, const int64_t* sizes, void* const* dsts,
+                   int threads, int retries, int retry_ms, int64_t* bytes_done, int* failed_index);
 
 /* ------------------------------------------------------------------ latent RMSNorm
  * The norm between the routed-expert sum and the latent up-projection of the Kimi K3 MoE

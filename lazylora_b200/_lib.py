@@ -80,6 +80,9 @@ _SIGS = {
     "ll_ep_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "ll_ep_combine_slots": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
     "ll_profile_gemm_events": (c_int, [ctypes.POINTER(c_void_p), c_int]),
+    "ll_pread_batch": (c_int, [c_int, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(c_int64),
+                               ctypes.POINTER(c_int64), ctypes.POINTER(c_void_p), c_int, c_int, c_int,
+                               ctypes.POINTER(c_int64), ctypes.POINTER(c_int)]),
     "ll_rmsnorm_forward": (c_int, [c_void_p, c_void_p, c_int, c_int, ctypes.c_float, c_void_p, c_int, c_void_p,
                                    c_void_p]),
     "ll_rmsnorm_backward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),

@@ -421,6 +421,7 @@ const char* ll_status_string(int status) {
     case LL_ERR_WORKSPACE: return "workspace too small";
     case LL_ERR_RANGE: return "value outside the exactly representable range";
     case LL_ERR_ARCH: return "device is not sm_100 (B200)";
+    case LL_ERR_IO: return "host file read failed";
     default: return "unknown status";
   }
 }

@@ -55,6 +55,15 @@ class HostExpertStore:
             raise ValueError("all stacks of a layer need the same expert count")
         self.layers[layer_idx] = pinned
 
+    def add_layer_from_checkpoint(self, layer_idx: int, index, num_experts: int, threads: int = 16) -> int:
+        """Read layer `layer_idx`'s experts 0..num_experts-1 from a safetensors checkpoint
+        (lazylora_b200.streaming.safetensors_reader.SafetensorsIndex) straight into pinned
+        stacks, with one parallel batch of reads; returns the bytes read."""
+        from ..streaming.safetensors_reader import read_layer_experts
+        stacks, nbytes = read_layer_experts(index, layer_idx, range(num_experts), pin=True, threads=threads)
+        self.layers[layer_idx] = {n: stacks[n] for n in STACKS}
+        return nbytes
+
     def num_experts(self, layer_idx: int) -> int:
         return self.layers[layer_idx]["w1p"].shape[0]
 

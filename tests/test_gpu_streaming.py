@@ -96,3 +96,20 @@ def test_prefetch_across_layers():
                    A_d=inps[0]["A_d"], B_d=inps[0]["B_d"])
         want = RoutedExpertsLayer.from_inputs(src, cfg.scaling).forward(x, idx, w)
         assert O.rel_l2(out.cpu(), want.cpu()) < 1e-5, l
+
+
+def test_checkpoint_to_pinned_stage_to_streamed_layer(tmp_path):
+    """A layer written as a safetensors checkpoint with the reference's tensor names, read by
+    the parallel reader straight into the pinned stage, streams to the resident layer's result."""
+    from lazylora_b200.streaming.safetensors_reader import SafetensorsIndex, write_layer_experts
+    from lazylora_b200.trainer.expert_streamer import ExpertStreamer, HostExpertStore, streamed_forward
+    cfg, inp, _store, lora, resident, x, g, idx, w, _ES = _setup("small")
+    stacks = {n: inp[n] for n in ("w1p", "w1s", "w3p", "w3s", "w2p", "w2s")}
+    write_layer_experts(str(tmp_path / "experts.safetensors"), 5, stacks, range(cfg.E))
+    store = HostExpertStore()
+    nbytes = store.add_layer_from_checkpoint(5, SafetensorsIndex(str(tmp_path)), cfg.E, threads=4)
+    assert nbytes == cfg.E * store.expert_bytes(5)
+    assert all(store.layers[5][n].is_pinned() for n in stacks)
+    streamer = ExpertStreamer(store, lora, cfg.scaling, group_experts=5)
+    out, _ = streamed_forward(streamer, 5, x, idx, w)
+    assert O.rel_l2(out.cpu(), resident.forward(x, idx, w).cpu()) < 1e-5
