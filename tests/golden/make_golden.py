@@ -2,7 +2,7 @@
 Regenerate the golden vectors in this folder from the reference implementation itself.
 
 Run from the repository root on a machine that has the reference tree:
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <path of the reference tree>
 
 What it writes:
   ref_<case>.npz       outputs of the reference's own routed-expert code on the seeded inputs
@@ -59,7 +59,7 @@ def _fixture(path, out_path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="path of the reference tree")
     ap.add_argument("--cases", default=",".join(CASES))
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
