@@ -193,6 +193,78 @@ __global__ void k_token_sum(const int* __restrict__ tok_pos, const float* __rest
   Du[(int64_t)t * f + m] = au;
 }
 
+// The two passes over the backward's per-pair gradients of the gate / up pre-activations in
+// one: block per token; for each of its pairs in ascending expert order, the pair rows DG, DU
+// are read once, converted to fp16 with the pair's power-of-two row scale (the B2 GEMM's
+// activation, as k_pair_rows_half) and added to the token sums Dg, Du (as k_token_sum, same
+// order, so both results are bitwise those of the two-kernel path). f = 1024, 2048 or 4096.
+constexpr int kPTThreads = 256;
+template <int NV>   // float4 per thread per row: f = 1024 NV
+__global__ void __launch_bounds__(kPTThreads) k_pair_rows_tokens(
+    const int* __restrict__ tok_pos, const float* __restrict__ DG, const float* __restrict__ DU, int k, int f,
+    __half* __restrict__ DGh, __half* __restrict__ DUh, float* __restrict__ inv, float* __restrict__ Dg,
+    float* __restrict__ Du) {
+  const int t = blockIdx.x;
+  __shared__ float red[kPTThreads / 32];
+  __shared__ float sh;
+  float4 ag[NV], au[NV];
+#pragma unroll
+  for (int i = 0; i < NV; i++) ag[i] = au[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < k; j++) {
+    const int p = tok_pos[(int64_t)t * k + j];
+    if (p < 0) break;
+    const float4* g4 = reinterpret_cast<const float4*>(DG + (int64_t)p * f);
+    const float4* u4 = reinterpret_cast<const float4*>(DU + (int64_t)p * f);
+    float4 gv[NV], uv[NV];
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      {
+        gv[i] = g4[threadIdx.x + i * kPTThreads];
+        uv[i] = u4[threadIdx.x + i * kPTThreads];
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(gv[i].x), fabsf(gv[i].y)), fmaxf(fabsf(gv[i].z), fabsf(gv[i].w))));
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(uv[i].x), fabsf(uv[i].y)), fmaxf(fabsf(uv[i].z), fabsf(uv[i].w))));
+      }
+    }
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = mx;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float m = 0.f;
+      for (int i = 0; i < kPTThreads / 32; i++) m = fmaxf(m, red[i]);
+      const int e = row_scale_exp(m);
+      sh = ldexpf(1.f, e);
+      inv[p] = ldexpf(1.f, -e);
+    }
+    __syncthreads();
+    const float scl = sh;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      {
+        const int64_t o = (int64_t)p * f + 4 * (threadIdx.x + i * kPTThreads);
+        const __half2 g01 = __floats2half2_rn(gv[i].x * scl, gv[i].y * scl);
+        const __half2 g23 = __floats2half2_rn(gv[i].z * scl, gv[i].w * scl);
+        const __half2 u01 = __floats2half2_rn(uv[i].x * scl, uv[i].y * scl);
+        const __half2 u23 = __floats2half2_rn(uv[i].z * scl, uv[i].w * scl);
+        *reinterpret_cast<uint2*>(DGh + o) = make_uint2(*reinterpret_cast<const uint32_t*>(&g01),
+                                                        *reinterpret_cast<const uint32_t*>(&g23));
+        *reinterpret_cast<uint2*>(DUh + o) = make_uint2(*reinterpret_cast<const uint32_t*>(&u01),
+                                                        *reinterpret_cast<const uint32_t*>(&u23));
+        ag[i].x += gv[i].x; ag[i].y += gv[i].y; ag[i].z += gv[i].z; ag[i].w += gv[i].w;
+        au[i].x += uv[i].x; au[i].y += uv[i].y; au[i].z += uv[i].z; au[i].w += uv[i].w;
+      }
+    }
+    __syncthreads();                             // sh and red are rewritten by the next pair
+  }
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    {
+      reinterpret_cast<float4*>(Dg + (int64_t)t * f)[threadIdx.x + i * kPTThreads] = ag[i];
+      reinterpret_cast<float4*>(Du + (int64_t)t * f)[threadIdx.x + i * kPTThreads] = au[i];
+    }
+  }
+}
+
 __global__ void k_grad_w(const int* __restrict__ pair_pos, const float* __restrict__ parts, int nparts, int P, int Tk,
                          float* __restrict__ grad_w) {
   const int q = blockIdx.x * blockDim.x + threadIdx.x;
@@ -617,8 +689,18 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
     else
       LL_TRY((launch_gemm<EPI_B1, 2, 1, true, 64>(pk, sc, act, a, s)));
   }
-  k_pair_rows_half<<<P, 256, 0, s>>>(W.DG, W.DU, f, n_valid, W.DGh, W.DUh, W.rinv);
-  LL_TRY(check_launch("k_pair_rows_half"));
+  // the pairs' fp16 rows for B2 and the per-token sums of the gate / up gradients, one pass
+  const int nv = f / (4 * kPTThreads);
+  const bool fused_rows = f % (4 * kPTThreads) == 0 && (nv == 1 || nv == 2 || nv == 4);
+  if (fused_rows) {
+    if (nv == 1) k_pair_rows_tokens<1><<<T, kPTThreads, 0, s>>>(W.tok_pos, W.DG, W.DU, k, f, W.DGh, W.DUh, W.rinv, W.Dg, W.Du);
+    else if (nv == 2) k_pair_rows_tokens<2><<<T, kPTThreads, 0, s>>>(W.tok_pos, W.DG, W.DU, k, f, W.DGh, W.DUh, W.rinv, W.Dg, W.Du);
+    else k_pair_rows_tokens<4><<<T, kPTThreads, 0, s>>>(W.tok_pos, W.DG, W.DU, k, f, W.DGh, W.DUh, W.rinv, W.Dg, W.Du);
+    LL_TRY(check_launch("k_pair_rows_tokens"));
+  } else {
+    k_pair_rows_half<<<P, 256, 0, s>>>(W.DG, W.DU, f, n_valid, W.DGh, W.DUh, W.rinv);
+    LL_TRY(check_launch("k_pair_rows_half"));
+  }
   // B2: dX = dg . W1 + du . W3
   {
     CUtensorMap pk[2], sc[2], act[8];
@@ -641,8 +723,10 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
     a.epi.Y = W.Y;
     LL_TRY((gemm_nmax<EPI_B2, 2, 2, true>(W.nmax, pk, sc, act, a, s)));
   }
-  k_token_sum<<<dim3((f + 255) / 256, T), 256, 0, s>>>(W.tok_pos, W.DG, W.DU, T, k, f, W.Dg, W.Du);
-  LL_TRY(check_launch("k_token_sum"));
+  if (!fused_rows) {
+    k_token_sum<<<dim3((f + 255) / 256, T), 256, 0, s>>>(W.tok_pos, W.DG, W.DU, T, k, f, W.Dg, W.Du);
+    LL_TRY(check_launch("k_token_sum"));
+  }
   LL_TRY(skinny(W.Dg, 0, false, T, f, L->B_g, nullptr, r, r, 1.f, W.hg, nullptr, W.skpart, s));
   LL_TRY(skinny(W.Du, 0, false, T, f, L->B_u, nullptr, r, r, 1.f, W.hu, nullptr, W.skpart, s));
   LL_TRY(expand(true, W.tok_pos, W.Y, k, T, d, r, sc_l, W.hg, L->A_g, W.hu, L->A_u, grad_h, s));
