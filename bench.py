@@ -561,6 +561,54 @@ def run_traces(args, cfg, rank, local, world, dist):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------- shared expert (Kimi K3 shape)
+def run_shared(args, cfg, rank, local, world, dist):
+    """fwd + bwd of the shared expert (dense SiTU-GLU 7168 -> 6144 -> 7168 with LoRA on its
+    three projections) at T = cfg.T tokens. Tensor-bound: the three bf16 projections forward and
+    the three input-gradient GEMMs backward (the base weights are frozen)."""
+    ClockSampler.start(local)
+    from lazylora_b200.trainer.shared_expert import SharedExpert
+    dev = torch.device("cuda", local)
+    d, F, r, N = args.shared_hidden, args.shared_inter, cfg.r, cfg.T
+    gen = torch.Generator(device=dev).manual_seed(cfg.seed + 11)
+    W = lambda o, i: (torch.randn(o, i, generator=gen, device=dev) / i ** 0.5).to(torch.bfloat16)
+    rnd = lambda *sh: torch.randn(*sh, generator=gen, device=dev) * 0.05
+    se = SharedExpert(W(F, d), W(F, d), W(d, F), rnd(r, d), rnd(F, r), rnd(r, d), rnd(F, r), rnd(r, F), rnd(d, r),
+                      cfg.scaling)
+    x = torch.randn(N, d, generator=gen, device=dev).to(torch.bfloat16)
+    g = torch.randn(N, d, generator=gen, device=dev).to(torch.bfloat16)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        se.forward(x)
+        se.backward(g)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        a.record(stream)
+        for _ in range(args.steps):
+            step()
+        b.record(stream)
+        torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    flops = 2 * 3 * 2 * N * d * F
+    _, tf_peak, peak_kind = _peaks()
+    tfs = flops / (ms * 1e-3) / 1e12
+    line = {"metric": f"shared expert fwd+bwd tokens/s (d={d}, F={F}, LoRA r={r})", "value": N / (ms * 1e-3),
+            "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 operands / fp32 accumulate", "data": "synthetic",
+            "config": {"workload": "shared expert (SURVEY 8(f) 3): 3 bf16 projections + LoRA, forward and "
+                                   "input-gradient backward", "d": d, "F": F, "r": r, "T": N},
+            "roofline": {"bound": "tensor", "achieved": tfs, "peak": tf_peak, "unit": "TFLOP/s",
+                         "frac": tfs / tf_peak, "peak_kind": peak_kind, "flops_per_step": flops},
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------ latent routed block (Kimi K3 shape)
 def run_latent(args, cfg, rank, local, world, dist):
     """Route + forward + backward of the latent routed block: down-projection 7168 -> d_l
@@ -744,6 +792,9 @@ def main():
     ap.add_argument("--stream", action="store_true", help="configs[4]: experts streamed from pinned host memory")
     ap.add_argument("--latent", action="store_true", help="the latent routed block (use --config c1_latent)")
     ap.add_argument("--traces", action="store_true", help="fwd+bwd steps on the recorded K3 routings (top-16)")
+    ap.add_argument("--shared", action="store_true", help="the shared expert (dense SiTU-GLU with LoRA)")
+    ap.add_argument("--shared-hidden", type=int, default=7168)
+    ap.add_argument("--shared-inter", type=int, default=6144)
     ap.add_argument("--latent-hidden", type=int, default=7168, help="hidden width around the latent block")
     ap.add_argument("--stream-distinct", type=int, default=1, help="distinct layers kept in pinned host memory")
     ap.add_argument("--stream-group", type=int, default=224, help="experts per streamed group")
@@ -767,6 +818,8 @@ def main():
             run_latent(args, cfg, rank, local, world, dist)
         elif args.traces:
             run_traces(args, cfg, rank, local, world, dist)
+        elif args.shared:
+            run_shared(args, cfg, rank, local, world, dist)
         else:
             run_ours(args, cfg, rank, local, world, dist)
             if dist is not None:

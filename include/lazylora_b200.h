@@ -224,6 +224,20 @@ int ll_ep_combine_slots(float* grad_w, const float* part, const int* pos, const 
 int ll_pread_batch(int n, const char* const* paths, const int64_t* offsets, const int64_t* sizes, void* const* dsts,
                    int threads, int retries, int retry_ms, int64_t* bytes_done, int* failed_index);
 
+/* ------------------------------------------------------------------ shared expert
+ * The element-wise middle of the shared expert (dense SiTU-GLU MLP with LoRA on its three
+ * projections, lazy_trainer.py:702-707) between its bf16 GEMMs. Forward: from the bf16
+ * projections G, U [N, F] and the LoRA A products xa_g, xa_u [N, r] fp32 with B_g, B_u [F, r]
+ * fp32: SG = bf16(G + bf16(s xa_g B_g^T)), SU likewise, H = bf16(situ_glu(SG, SU)), all bf16
+ * [N, F]. Backward: from Dh (bf16 [N, F], the down projection's input gradient g W_d) and
+ * gB = g B_d [N, r] fp32 with A_d [r, F] fp32: dh = bf16(Dh + bf16(s gB A_d)), then the
+ * SiTU-GLU gradients DSG, DSU (bf16 [N, F]) at the saved SG, SU. r in {4, 8, 16, 32}. */
+int ll_shared_glu_forward(const void* G, const void* U, const float* xa_g, const float* xa_u, const float* B_g,
+                          const float* B_u, float scaling, int N, int F, int r, void* SG, void* SU, void* H,
+                          void* stream);
+int ll_shared_glu_backward(const void* Dh, const float* gB, const float* A_d, float scaling, const void* SG,
+                           const void* SU, int N, int F, int r, void* DSG, void* DSU, void* stream);
+
 /* ------------------------------------------------------------------ latent RMSNorm
  * The norm between the routed-expert sum and the latent up-projection of the Kimi K3 MoE
  * block (lazy_trainer.py:731-733; RMSNormFunction.forward, trunk_streamer.py:27-31):

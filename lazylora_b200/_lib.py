@@ -83,6 +83,10 @@ _SIGS = {
     "ll_pread_batch": (c_int, [c_int, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(c_int64),
                                ctypes.POINTER(c_int64), ctypes.POINTER(c_void_p), c_int, c_int, c_int,
                                ctypes.POINTER(c_int64), ctypes.POINTER(c_int)]),
+    "ll_shared_glu_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_int,
+                                      c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "ll_shared_glu_backward": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_int, c_int,
+                                       c_int, c_void_p, c_void_p, c_void_p]),
     "ll_rmsnorm_forward": (c_int, [c_void_p, c_void_p, c_int, c_int, ctypes.c_float, c_void_p, c_int, c_void_p,
                                    c_void_p]),
     "ll_rmsnorm_backward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
