@@ -601,7 +601,7 @@ def run_shared(args, cfg, rank, local, world, dist):
             "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16 operands / fp32 accumulate", "data": "synthetic",
-            "config": {"workload": "shared expert (SURVEY 8(f) 3): 3 bf16 projections + LoRA, forward and "
+            "config": {"workload": "shared expert of the K3 MoE layer: 3 bf16 projections + LoRA, forward and "
                                    "input-gradient backward", "d": d, "F": F, "r": r, "T": N},
             "roofline": {"bound": "tensor", "achieved": tfs, "peak": tf_peak, "unit": "TFLOP/s",
                          "frac": tfs / tf_peak, "peak_kind": peak_kind, "flops_per_step": flops},
@@ -670,7 +670,7 @@ def run_latent(args, cfg, rank, local, world, dist):
             "value": cfg.T / (ms * 1e-3), "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16 projections / fp16 expert operands, fp32 accumulate", "data": "synthetic",
-            "config": {"workload": "latent routed block (SURVEY 8(f) 1): route + down-proj + experts + RMSNorm + "
+            "config": {"workload": "latent routed block of the K3 MoE layer: route + down-proj + experts + RMSNorm + "
                                    "up-proj, forward and backward", "d_h": d_h, "d_l": cfg.d, "f": cfg.f,
                        "E": cfg.E, "k": cfg.k, "T": cfg.T, "r": cfg.r, "active_experts": U},
             "roofline": {"bound": "hbm", "achieved": wbytes / (ms * 1e-3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
