@@ -149,6 +149,10 @@ __global__ void k_skinny_reduce(const float* __restrict__ part, int nsplit, int 
 // token's k rows of Y are all requested before the first is added (k <= 8 per batch), so the
 // kernel streams Y at memory speed instead of one dependent load at a time.
 constexpr int kExTok = 8, kExThreads = 128, kExCols = 4 * kExThreads;
+// shared row pitch of the staged R slices: 4 floats of padding keep the float4 reads aligned and
+// spread the transposing stores of a [C][r] R (16 consecutive rr of one column) over 8 banks
+// instead of one
+constexpr int kExPitch = kExCols + 4;
 
 constexpr int kExMaxR = 64;
 
@@ -157,7 +161,7 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
                                                    int T, int C, int r, float alpha, const float* __restrict__ L0,
                                                    const float* __restrict__ R0, const float* __restrict__ L1,
                                                    const float* __restrict__ R1, float* __restrict__ out) {
-  extern __shared__ float Rs[];                          // [r][kExCols], one R at a time
+  extern __shared__ float Rs[];                          // [r][kExPitch], one R at a time
   __shared__ float Ls[kExTok][kExMaxR];
   __shared__ int ps[kExTok][32];
   const int c0 = blockIdx.x * kExCols, t0 = blockIdx.y * kExTok;
@@ -178,12 +182,12 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
     if (RROWS) {
       for (int i = threadIdx.x; i < r * kExCols; i += kExThreads) {
         const int rr = i / kExCols, cc = i % kExCols;
-        Rs[rr * kExCols + cc] = cc < nc ? R[(int64_t)rr * C + c0 + cc] : 0.f;
+        Rs[rr * kExPitch + cc] = cc < nc ? R[(int64_t)rr * C + c0 + cc] : 0.f;
       }
     } else {   // [C][r]: the block's columns are one contiguous run of kExCols * r floats
       for (int i = threadIdx.x; i < r * kExCols; i += kExThreads) {
         const int cc = i / r, rr = i % r;
-        Rs[rr * kExCols + cc] = cc < nc ? R[(int64_t)(c0 + cc) * r + rr] : 0.f;
+        Rs[rr * kExPitch + cc] = cc < nc ? R[(int64_t)(c0 + cc) * r + rr] : 0.f;
       }
     }
     for (int i = threadIdx.x; i < kExTok * r; i += kExThreads) {
@@ -193,7 +197,7 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
     __syncthreads();
     if (c < nc)
       for (int rr = 0; rr < r; rr++) {
-        const float4 rv = *reinterpret_cast<const float4*>(Rs + rr * kExCols + c);
+        const float4 rv = *reinterpret_cast<const float4*>(Rs + rr * kExPitch + c);
 #pragma unroll
         for (int tt = 0; tt < kExTok; tt++) {
           const float l = Ls[tt][rr];

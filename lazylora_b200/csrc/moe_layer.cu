@@ -459,7 +459,7 @@ static int expand(bool rrows, const int* tok_pos, const float* Y, int k, int T, 
   if (C % 4 || r > kExMaxR || k > 32) return LL_ERR_ARG;
   dim3 grid((C + kExCols - 1) / kExCols, (T + kExTok - 1) / kExTok);
   const bool hasy = Y != nullptr, two = L1 != nullptr;
-  const int smem = r * kExCols * (int)sizeof(float);   // <= 128 KB at r = 64
+  const int smem = r * kExPitch * (int)sizeof(float);  // <= 129 KB at r = 64
   auto attr = [&](const void* f) { return set_smem_attr(f, smem); };
 #define LL_EX(RR, HY, TW)                                                                                   \
   do {                                                                                                      \
