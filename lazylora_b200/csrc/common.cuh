@@ -255,11 +255,11 @@ LL_DEV uint32_t idesc_f16_m128(uint32_t n, bool a_mn_major, bool b_mn_major) {
 // unrepresentable / damaged group contributes nothing) and for exponents below fp16's
 // smallest subnormal 2^-24. The caller picks `bias` so that 6 * 2^(b-127+bias) <= 2^15.
 LL_DEV uint32_t e8m0_to_half_bits(uint32_t b, int bias) {
-  if (b >= 253u) return 0u;
-  const int e = (int)b - 127 + bias;
-  if (e >= -14) return (uint32_t)(e + 15) << 10;     // normal (e <= 15 guaranteed by bias)
-  if (e >= -24) return 1u << (e + 24);                // subnormal power of two
-  return 0u;
+  // 2^(b - 127 + bias) built as an fp32 power of two and rounded to fp16: exact for normal
+  // and subnormal fp16 powers of two, 0 below 2^-24 (2^-25 rounds to even, 0)
+  const int t = (int)b + bias;                      // biased fp32 exponent of the scale
+  const uint32_t h = __half_as_ushort(__float2half_rn(__int_as_float(t << 23)));
+  return (b >= 253u || t <= 0) ? 0u : h;
 }
 
 // Two E2M1 codes (low nibble = even element) -> fp16x2 (even element in the low half),
