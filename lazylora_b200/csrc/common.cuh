@@ -262,6 +262,15 @@ LL_DEV uint32_t e8m0_to_half_bits(uint32_t b, int bias) {
   return (b >= 253u || t <= 0) ? 0u : h;
 }
 
+// The same scale in both halves of an fp16x2 (one f32x2 -> f16x2 conversion packs the pair).
+LL_DEV uint32_t e8m0_to_half2_bits(uint32_t b, int bias) {
+  const int t = (int)b + bias;
+  const float f = __int_as_float(t << 23);
+  uint32_t h2;
+  asm("cvt.rn.f16x2.f32 %0, %1, %1;" : "=r"(h2) : "f"(f));
+  return (b >= 253u || t <= 0) ? 0u : h2;
+}
+
 // Two E2M1 codes (low nibble = even element) -> fp16x2 (even element in the low half),
 // exact. One hardware conversion per byte.
 LL_DEV uint32_t e2m1x2_to_half2(uint32_t byte) {

@@ -431,8 +431,7 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, N_MAX> tm, const GemmArg
             decode8v(raw.w, &sv[12], &o[12]);
           } else {
             const uint32_t sbyte = sc[m * 16 + (((ks * C::BK) / 32) & 15) + seg];
-            const uint32_t s1 = e8m0_to_half_bits(sbyte, bias);
-            const uint32_t s2 = s1 | (s1 << 16);
+            const uint32_t s2 = e8m0_to_half2_bits(sbyte, bias);
             decode8(raw.x, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[0]));
             decode8(raw.y, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[4]));
             decode8(raw.z, s2, *reinterpret_cast<uint32_t(*)[4]>(&o[8]));
