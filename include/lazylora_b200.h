@@ -238,6 +238,30 @@ int ll_shared_glu_forward(const void* G, const void* U, const float* xa_g, const
 int ll_shared_glu_backward(const void* Dh, const float* gB, const float* A_d, float scaling, const void* SG,
                            const void* SU, int N, int F, int r, void* DSG, void* DSU, void* stream);
 
+/* ------------------------------------------------------------------ LoRA products
+ * The rank-r products of a LoRA adapter (lora_layer.py:104-123: delta = s (x A^T) B^T) around a
+ * bf16 projection, reading the bf16 activations directly (the reference casts them to fp32
+ * first). Sums run in a fixed order: results are bitwise reproducible.
+ * ll_lora_down: C = alpha X B, X [M, K] (x_dtype 0 fp32, 1 bf16, 2 fp16; 16-byte aligned,
+ *   K % 8 == 0). b_rows = 1: B given as rows [n, K] (LoRA A matrices), B0 the first n0 rows
+ *   into C0 [M, n0], B1 the other n - n0 into C1 [M, n - n0] (both A_g and A_u of a gate/up
+ *   pair in one pass). b_rows = 0: B0 [K, n] (a LoRA B matrix), n0 == n, into C0 [M, n].
+ *   Split-K partials go to `workspace` (16-byte aligned, at least 4 M n bytes, else
+ *   LL_ERR_WORKSPACE; fewer splits when it is small).
+ * ll_lora_outer: out = scale sum_n P[n]^T Q[n], P [N, r] fp32, Q [N, C] (q_dtype as above,
+ *   C % 4 == 0), stored [r, C] (dA = s (gB)^T x) or, transposed, [C, r] (dB = s g^T (x A^T)).
+ *   `workspace` holds at least 4 r C bytes (else LL_ERR_WORKSPACE).
+ * ll_lora_add_bf16: out = bf16(Y + bf16(scale L0 R0) [+ bf16(scale L1 R1)]), Y and out bf16
+ *   [N, C] (may be the same buffer), L [N, r] fp32, R(rr, c) = R[rr C + c] ([r, C], r_rows = 1)
+ *   or R[c r + rr] ([C, r], r_rows = 0). r in {4, 8, 16, 32}; L1 = NULL for one delta. */
+int ll_lora_down(const void* X, int x_dtype, int M, int K, const float* B0, const float* B1, int n0, int n,
+                 int b_rows, float alpha, float* C0, float* C1, void* workspace, size_t workspace_bytes,
+                 void* stream);
+int ll_lora_outer(const float* P, const void* Q, int q_dtype, int N, int C, int r, float scale, int transposed,
+                  float* out, void* workspace, size_t workspace_bytes, void* stream);
+int ll_lora_add_bf16(const void* Y, const float* L0, const float* R0, const float* L1, const float* R1, int r,
+                     int r_rows, float scale, int N, int C, void* out, void* stream);
+
 /* ------------------------------------------------------------------ latent RMSNorm
  * The norm between the routed-expert sum and the latent up-projection of the Kimi K3 MoE
  * block (lazy_trainer.py:731-733; RMSNormFunction.forward, trunk_streamer.py:27-31):

@@ -87,6 +87,12 @@ _SIGS = {
                                       c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "ll_shared_glu_backward": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_int, c_int,
                                        c_int, c_void_p, c_void_p, c_void_p]),
+    "ll_lora_down": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_float,
+                             c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_void_p]),
+    "ll_lora_outer": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_int, c_void_p, c_void_p,
+                              ctypes.c_size_t, c_void_p]),
+    "ll_lora_add_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_int,
+                                 c_int, c_void_p, c_void_p]),
     "ll_rmsnorm_forward": (c_int, [c_void_p, c_void_p, c_int, c_int, ctypes.c_float, c_void_p, c_int, c_void_p,
                                    c_void_p]),
     "ll_rmsnorm_backward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),

@@ -3,6 +3,7 @@
 // so results are bitwise reproducible.
 #pragma once
 #include "common.cuh"
+#include "lora_ops.cuh"
 
 namespace ll {
 

@@ -329,6 +329,7 @@ struct LayerWs {
   float* hu;
   float* opart;
   float* skpart;
+  size_t skpart_floats;
   int nmax;
   int nseg_max;
 };
@@ -396,7 +397,8 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   {  // split-K partials of the skinny products: nsplit * mblocks * nblocks <= 2 * SMs +
      // mblocks * nblocks blocks of at most 8192 outputs (BM * NC); SMs <= 160
     const int64_t rows = P > T ? P : T;
-    w.skpart = c.take<float>((size_t)2 * 160 * 8192 + (size_t)(rows + 256) * (2 * r + 32));
+    w.skpart_floats = (size_t)2 * 160 * 8192 + (size_t)(rows + 256) * (2 * r + 32);
+    w.skpart = c.take<float>(w.skpart_floats);
   }
   if (out) *out = w;
   return c.off + 256;
@@ -423,16 +425,18 @@ static int gemm_nmax(int nmax, const CUtensorMap* pk, const CUtensorMap* sc, con
 }
 
 // C0 (and C1) = alpha * A[M][K] . B, with B given as rows ([N][K], split over B0 / B1 at N0)
-// or columns ([K][N]); split-K partials in `part`, summed in a fixed order.
-static int skinny(const void* A, int adt, bool brows, int M, int K, const float* B0, const float* B1, int N0, int N,
-                  float alpha, float* C0, float* C1, float* part, cudaStream_t s) {
-  if (K % 8 || M <= 0 || N <= 0) return LL_ERR_ARG;
+// or columns ([K][N]); split-K partials in `part` (room for part_floats floats), summed in a
+// fixed order.
+int skinny(const void* A, int adt, bool brows, int M, int K, const float* B0, const float* B1, int N0, int N,
+           float alpha, float* C0, float* C1, float* part, size_t part_floats, cudaStream_t s) {
+  if (K % 8 || M <= 0 || N <= 0 || part_floats < (size_t)M * N) return LL_ERR_ARG;
   const bool nc16 = N <= 16;
   const int BM = nc16 ? SkinnyCfg<16>::BM : SkinnyCfg<32>::BM, NC = nc16 ? 16 : 32;
   const int mblocks = (M + BM - 1) / BM, nblocks = (N + NC - 1) / NC;
   // about two blocks per SM, split over K
   int nsplit = (2 * device_info().sms + mblocks * nblocks - 1) / (mblocks * nblocks);
   nsplit = std::max(1, std::min(nsplit, (K + kSkBK - 1) / kSkBK));
+  nsplit = std::min<int64_t>(nsplit, (int64_t)(part_floats / ((size_t)M * N)));
   const int kc = ((K + nsplit - 1) / nsplit + kSkBK - 1) / kSkBK * kSkBK;
   nsplit = (K + kc - 1) / kc;
   dim3 grid(mblocks, nblocks, nsplit);
@@ -454,8 +458,8 @@ static int skinny(const void* A, int adt, bool brows, int M, int K, const float*
 }
 
 // Rank-r expand with the optional ascending-expert sum of per-pair rows (see k_expand).
-static int expand(bool rrows, const int* tok_pos, const float* Y, int k, int T, int C, int r, float alpha,
-                  const float* L0, const float* R0, const float* L1, const float* R1, float* out, cudaStream_t s) {
+int expand(bool rrows, const int* tok_pos, const float* Y, int k, int T, int C, int r, float alpha, const float* L0,
+           const float* R0, const float* L1, const float* R1, float* out, cudaStream_t s) {
   if (C % 4 || r > kExMaxR || k > 32) return LL_ERR_ARG;
   dim3 grid((C + kExCols - 1) / kExCols, (T + kExTok - 1) / kExTok);
   const bool hasy = Y != nullptr, two = L1 != nullptr;
@@ -478,9 +482,8 @@ static int expand(bool rrows, const int* tok_pos, const float* Y, int k, int T, 
 }
 
 // out = s * sum_n Pm(n, :)^T Q[n][:], stored [r][C] or transposed [C][r]
-static int outer(const float* Pm, const int* perm_token, const float* tw, const void* Q, int qdt, int N,
-                 const int* n_dev, int C, int r, float sc, bool transposed, float* part, int nseg_max, float* out,
-                 cudaStream_t s) {
+int outer(const float* Pm, const int* perm_token, const float* tw, const void* Q, int qdt, int N, const int* n_dev,
+          int C, int r, float sc, bool transposed, float* part, int nseg_max, float* out, cudaStream_t s) {
   if (C % 4 || r <= 0) return LL_ERR_ARG;
   const int cblocks = (C + kOuCW - 1) / kOuCW, zb = (r + kOuRB - 1) / kOuRB;
   // about three blocks per SM; each warp gets at least one batch of rows
@@ -562,7 +565,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
                                                             W.pair_pos, W.tw, W.tok_pos);
   LL_TRY(check_launch("k_scatter"));
   LL_TRY(launch_rows_to_half(x, x_dtype, W.perm_token, P, d, W.xh, W.xinv, s));
-  LL_TRY(skinny(x, x_dtype, true, T, d, L->A_g, L->A_u, r, 2 * r, 1.f, W.xa_g, W.xa_u, W.skpart, s));
+  LL_TRY(skinny(x, x_dtype, true, T, d, L->A_g, L->A_u, r, 2 * r, 1.f, W.xa_g, W.xa_u, W.skpart, W.skpart_floats, s));
   LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_g, L->B_g, nullptr, nullptr, W.dlt_g, s));
   LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_u, L->B_u, nullptr, nullptr, W.dlt_u, s));
   // F1: gate / up
@@ -593,7 +596,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   }
   const int* n_valid = W.offsets + E;
   // z = h . A_d^T per pair (h as the fp16 rows the down GEMM reads)
-  LL_TRY(skinny(W.H, 2, true, P, f, L->A_d, nullptr, r, r, 1.f, W.z, nullptr, W.skpart, s));
+  LL_TRY(skinny(W.H, 2, true, P, f, L->A_d, nullptr, r, r, 1.f, W.z, nullptr, W.skpart, W.skpart_floats, s));
   {
     const int64_t n = (int64_t)T * r;
     k_q<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(W.tok_pos, W.tw, W.z, T, k, r, W.q);
@@ -644,7 +647,7 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
   g_launch_count = 0;
 
   LL_TRY(launch_rows_to_half(g, g_dtype, W.perm_token, P, d, W.gh, W.ginv, s));
-  LL_TRY(skinny(g, g_dtype, false, T, d, L->B_d, nullptr, r, r, 1.f, W.gB, nullptr, W.skpart, s));
+  LL_TRY(skinny(g, g_dtype, false, T, d, L->B_d, nullptr, r, r, 1.f, W.gB, nullptr, W.skpart, W.skpart_floats, s));
   // the down adapter's term of dL/dh, once per token: (g B_d) A_d [T][f]
   LL_TRY(expand(true, nullptr, nullptr, k, T, f, r, 1.f, W.gB, L->A_d, nullptr, nullptr, W.lora_d, s));
   // B1: v = g . W2 (+ LoRA down), SiTU-GLU backward
@@ -727,8 +730,8 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
     k_token_sum<<<dim3((f + 255) / 256, T), 256, 0, s>>>(W.tok_pos, W.DG, W.DU, T, k, f, W.Dg, W.Du);
     LL_TRY(check_launch("k_token_sum"));
   }
-  LL_TRY(skinny(W.Dg, 0, false, T, f, L->B_g, nullptr, r, r, 1.f, W.hg, nullptr, W.skpart, s));
-  LL_TRY(skinny(W.Du, 0, false, T, f, L->B_u, nullptr, r, r, 1.f, W.hu, nullptr, W.skpart, s));
+  LL_TRY(skinny(W.Dg, 0, false, T, f, L->B_g, nullptr, r, r, 1.f, W.hg, nullptr, W.skpart, W.skpart_floats, s));
+  LL_TRY(skinny(W.Du, 0, false, T, f, L->B_u, nullptr, r, r, 1.f, W.hu, nullptr, W.skpart, W.skpart_floats, s));
   LL_TRY(expand(true, W.tok_pos, W.Y, k, T, d, r, sc_l, W.hg, L->A_g, W.hu, L->A_u, grad_h, s));
   k_grad_w<<<(P + 255) / 256, 256, 0, s>>>(W.pair_pos, W.gw_part, (f / 128) * 4, P, P, grad_w);
   LL_TRY(check_launch("k_grad_w"));

@@ -11,7 +11,17 @@
 //   A_d [r, F] fp32 (the down adapter's A, whose input is h).
 // Block: 256 columns x 8 tokens; a thread keeps its column's r adapter values in registers and
 // reads the 8 tokens' r-vectors from shared memory.
+//
+// Also here, the C-ABI of the LoRA products around such bf16 GEMMs (the shared expert's, or any
+// dense projection's), which read the bf16 activations directly instead of an fp32 copy:
+//   ll_lora_down      C = alpha * X . B   (X [M][K] bf16/f16/f32; B: the rank-r A matrices as
+//                     rows, or a B matrix as columns), split-K with a fixed-order sum
+//   ll_lora_outer     out = scale * sum_n P[n]^T Q[n]  (the adapter gradients dA, dB)
+//   ll_lora_add_bf16  out = bf16(Y + bf16(scale * L0 . R0) [+ bf16(scale * L1 . R1)]): the bf16
+//                     projection output plus its rounded LoRA delta(s), as the reference adds
+//                     the two bf16 tensors (lora_layer.py:104-123)
 #include "host_common.cuh"
+#include "lora_ops.cuh"
 
 namespace ll {
 
@@ -97,6 +107,51 @@ __global__ void __launch_bounds__(kSgCols) k_shared_glu_bwd(const __nv_bfloat16*
   }
 }
 
+// out[t][c] = bf16(Y[t][c] + bf16(s * sum_rr L0[t][rr] R0(rr, c)) [+ bf16(s * L1[t] . R1(:, c))])
+// R(rr, c): RROWS -> R[rr * C + c] ([r][C]); else R[c * r + rr] ([C][r]). Y may alias out.
+// Block: 256 columns x 32 tokens; a thread keeps its column's adapter values in registers.
+constexpr int kLaCols = 256, kLaTok = 32;
+
+template <int R, bool TWO, bool RROWS>
+__global__ void __launch_bounds__(kLaCols) k_lora_add_bf16(const __nv_bfloat16* Y, const float* __restrict__ L0,
+                                                           const float* __restrict__ R0, const float* __restrict__ L1,
+                                                           const float* __restrict__ R1, float s, int N, int C,
+                                                           __nv_bfloat16* out) {
+  constexpr int NW = TWO ? 2 : 1;
+  __shared__ float ls[kLaTok][NW * R];
+  const int j = blockIdx.x * kLaCols + threadIdx.x;
+  const int t0 = blockIdx.y * kLaTok;
+  for (int i = threadIdx.x; i < kLaTok * NW * R; i += kLaCols) {
+    const int tt = i / (NW * R), rr = i % (NW * R);
+    const int t = t0 + tt;
+    ls[tt][rr] = t < N ? (rr < R ? L0[(int64_t)t * R + rr] : L1[(int64_t)t * R + rr - R]) : 0.f;
+  }
+  __syncthreads();
+  if (j >= C) return;
+  float rv[NW][R];
+#pragma unroll
+  for (int w = 0; w < NW; w++) {
+    const float* Rm = w == 0 ? R0 : R1;
+#pragma unroll
+    for (int rr = 0; rr < R; rr++) rv[w][rr] = RROWS ? Rm[(int64_t)rr * C + j] : Rm[(int64_t)j * R + rr];
+  }
+#pragma unroll 4
+  for (int tt = 0; tt < kLaTok; tt++) {
+    const int t = t0 + tt;
+    if (t >= N) break;
+    const int64_t o = (int64_t)t * C + j;
+    float v = __bfloat162float(Y[o]);
+#pragma unroll
+    for (int w = 0; w < NW; w++) {
+      float dl = 0.f;
+#pragma unroll
+      for (int rr = 0; rr < R; rr++) dl = fmaf(ls[tt][w * R + rr], rv[w][rr], dl);
+      v += bf16r(s * dl);
+    }
+    out[o] = __float2bfloat16_rn(v);
+  }
+}
+
 }  // namespace ll
 
 using namespace ll;
@@ -138,6 +193,59 @@ int ll_shared_glu_backward(const void* Dh, const float* gB, const float* A_d, fl
   if (r == 4) LL_SGB(4); else if (r == 8) LL_SGB(8); else if (r == 16) LL_SGB(16); else LL_SGB(32);
 #undef LL_SGB
   return check_launch("k_shared_glu_bwd");
+}
+
+int ll_lora_down(const void* X, int x_dtype, int M, int K, const float* B0, const float* B1, int n0, int n,
+                 int b_rows, float alpha, float* C0, float* C1, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  if (M < 0 || K <= 0 || K % 8 || n <= 0 || n0 <= 0 || n0 > n || x_dtype < 0 || x_dtype > 2) return LL_ERR_ARG;
+  if (M == 0) return LL_OK;
+  if (!X || !B0 || !C0 || !workspace || (reinterpret_cast<uintptr_t>(X) & 15) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 15))
+    return LL_ERR_ARG;
+  if (b_rows ? (n0 < n && (!B1 || !C1)) : n0 != n) return LL_ERR_ARG;
+  if (workspace_bytes / sizeof(float) < (size_t)M * n) return LL_ERR_WORKSPACE;
+  LL_STREAM(stream);
+  return skinny(X, x_dtype, b_rows != 0, M, K, B0, B1, n0, n, alpha, C0, C1, static_cast<float*>(workspace),
+                workspace_bytes / sizeof(float), s);
+}
+
+int ll_lora_outer(const float* P, const void* Q, int q_dtype, int N, int C, int r, float scale, int transposed,
+                  float* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (N < 0 || C <= 0 || C % 4 || r <= 0 || q_dtype < 0 || q_dtype > 2) return LL_ERR_ARG;
+  if (!out || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 15)) return LL_ERR_ARG;
+  if (N > 0 && (!P || !Q || (reinterpret_cast<uintptr_t>(Q) & (q_dtype == 0 ? 15 : 7)))) return LL_ERR_ARG;
+  const size_t per_seg = (size_t)r * C;
+  const size_t nseg_max = workspace_bytes / sizeof(float) / per_seg;
+  if (nseg_max < 1) return LL_ERR_WORKSPACE;
+  LL_STREAM(stream);
+  return outer(P, nullptr, nullptr, Q, q_dtype, N, nullptr, C, r, scale, transposed != 0,
+               static_cast<float*>(workspace), (int)(nseg_max > 64 ? 64 : nseg_max), out, s);
+}
+
+int ll_lora_add_bf16(const void* Y, const float* L0, const float* R0, const float* L1, const float* R1, int r,
+                     int r_rows, float scale, int N, int C, void* out, void* stream) {
+  if (N < 0 || C <= 0 || !(r == 4 || r == 8 || r == 16 || r == 32)) return LL_ERR_ARG;
+  if (N == 0) return LL_OK;
+  if (!Y || !L0 || !R0 || !out || (L1 && !R1)) return LL_ERR_ARG;
+  LL_STREAM(stream);
+  const dim3 grid((C + kLaCols - 1) / kLaCols, (N + kLaTok - 1) / kLaTok);
+  auto y = static_cast<const __nv_bfloat16*>(Y);
+  auto o = static_cast<__nv_bfloat16*>(out);
+#define LL_LA(RR, TW, RW) k_lora_add_bf16<RR, TW, RW><<<grid, kLaCols, 0, s>>>(y, L0, R0, L1, R1, scale, N, C, o)
+#define LL_LA_R(TW, RW)                                                                          \
+  do {                                                                                           \
+    if (r == 4) LL_LA(4, TW, RW); else if (r == 8) LL_LA(8, TW, RW);                             \
+    else if (r == 16) LL_LA(16, TW, RW); else LL_LA(32, TW, RW);                                 \
+  } while (0)
+  if (L1) {
+    if (r_rows) LL_LA_R(true, true); else LL_LA_R(true, false);
+  } else {
+    if (r_rows) LL_LA_R(false, true); else LL_LA_R(false, false);
+  }
+#undef LL_LA_R
+#undef LL_LA
+  return check_launch("k_lora_add_bf16");
 }
 
 }  // extern "C"

@@ -8,12 +8,16 @@ weights, frozen) with a rank-r LoRA adapter on each of its three projections
     out    = linear32(h, W_d) + lora_d(h)
 
 The three projections are bf16 GEMMs with fp32 accumulation (cuBLAS through torch.matmul, as
-F.linear runs them on CUDA in the reference); the LoRA products are small fp32 GEMMs; the
+F.linear runs them on CUDA in the reference). The LoRA products read the bf16 activations
+directly (ll_lora_down, ll_lora_outer: fixed-order split-K sums) instead of fp32 copies; the
 element-wise middle — both LoRA deltas added in bf16 and the SiTU-GLU, and in the backward the
 down adapter's input-gradient term plus the SiTU-GLU gradient — is one kernel each way
-(ll_shared_glu_forward / ll_shared_glu_backward). The backward returns dL/dx and the six LoRA
-gradients, following the autograd graph of the reference's forward (lora_layer.py:104-123:
-the adapter casts its bf16 input to fp32 and its fp32 delta back to bf16).
+(ll_shared_glu_forward / ll_shared_glu_backward); the down projection's delta, and the gate/up
+adapters' input-gradient terms, are added to the bf16 GEMM outputs in place
+(ll_lora_add_bf16). The backward returns dL/dx and the six LoRA gradients, following the
+autograd graph of the reference's forward (lora_layer.py:104-123: the adapter casts its bf16
+input to fp32 and its fp32 delta back to bf16); the two gate/up input-gradient GEMMs
+accumulate into one bf16 buffer (cuBLAS with beta = 1).
 """
 import ctypes
 from typing import Dict, Tuple
@@ -43,54 +47,95 @@ class SharedExpert:
         self.s = float(scaling)
         self.lib = L.load()
         self._saved = None
+        self._ws = None
+
+    def _workspace(self, N: int, device) -> torch.Tensor:
+        """Split-K partials of the LoRA products: 16 MB covers the splits that fill the GPU at the
+        shapes here, plus one full [N, 2r] product for a single split."""
+        need = 16 * 1024 * 1024 + 4 * N * 2 * self.r
+        if self._ws is None or self._ws.numel() * 4 < need or self._ws.device != device:
+            self._ws = torch.empty(need // 4, dtype=torch.float32, device=device)
+        return self._ws
+
+    def _down(self, X, B0, B1, n0, n, b_rows, C0, C1, ws):
+        L.check(self.lib.ll_lora_down(X.data_ptr(), 1, X.shape[0], X.shape[1], B0.data_ptr(),
+                                      B1.data_ptr() if B1 is not None else None, n0, n, b_rows, ctypes.c_float(1.0),
+                                      C0.data_ptr(), C1.data_ptr() if C1 is not None else None, ws.data_ptr(),
+                                      ws.numel() * 4, L.stream_ptr()), "ll_lora_down")
+
+    def _outer(self, P, Q, transposed, out, ws):
+        L.check(self.lib.ll_lora_outer(P.data_ptr(), Q.data_ptr(), 1, Q.shape[0], Q.shape[1], self.r,
+                                       ctypes.c_float(self.s), 1 if transposed else 0, out.data_ptr(), ws.data_ptr(),
+                                       ws.numel() * 4, L.stream_ptr()), "ll_lora_outer")
+
+    def _add(self, Y, L0, R0, L1, R1, r_rows):
+        L.check(self.lib.ll_lora_add_bf16(Y.data_ptr(), L0.data_ptr(), R0.data_ptr(),
+                                          L1.data_ptr() if L1 is not None else None,
+                                          R1.data_ptr() if R1 is not None else None, self.r, r_rows,
+                                          ctypes.c_float(self.s), Y.shape[0], Y.shape[1], Y.data_ptr(),
+                                          L.stream_ptr()), "ll_lora_add_bf16")
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """out [N, d] bf16 for x [N, d]."""
         L.require_cuda(x)
         xb = x.reshape(-1, self.d).to(torch.bfloat16).contiguous()
-        N, F = xb.shape[0], self.F
+        N, F, r, dev = xb.shape[0], self.F, self.r, x.device
+        ws = self._workspace(N, dev)
         G = torch.matmul(xb, self.W_g.t())
         U = torch.matmul(xb, self.W_u.t())
-        xf = xb.float()
-        xa_g = torch.matmul(xf, self.A_g.t()).contiguous()
-        xa_u = torch.matmul(xf, self.A_u.t()).contiguous()
-        SG = torch.empty((N, F), dtype=torch.bfloat16, device=x.device)
+        xa_g = torch.empty((N, r), dtype=torch.float32, device=dev)
+        xa_u = torch.empty_like(xa_g)
+        if N:
+            self._down(xb, self.A_g, self.A_u, r, 2 * r, 1, xa_g, xa_u, ws)
+        SG = torch.empty((N, F), dtype=torch.bfloat16, device=dev)
         SU = torch.empty_like(SG)
         H = torch.empty_like(SG)
         L.check(self.lib.ll_shared_glu_forward(G.data_ptr(), U.data_ptr(), xa_g.data_ptr(), xa_u.data_ptr(),
                                                self.B_g.data_ptr(), self.B_u.data_ptr(), ctypes.c_float(self.s),
-                                               N, F, self.r, SG.data_ptr(), SU.data_ptr(), H.data_ptr(),
+                                               N, F, r, SG.data_ptr(), SU.data_ptr(), H.data_ptr(),
                                                L.stream_ptr()), "ll_shared_glu_forward")
-        ha = torch.matmul(H.float(), self.A_d.t())                                  # [N, r]
-        out = torch.matmul(H, self.W_d.t()) + (torch.matmul(ha, self.B_d.t()) * self.s).to(torch.bfloat16)
-        self._saved = (xf, xa_g, xa_u, SG, SU, H, ha)
+        ha = torch.empty((N, r), dtype=torch.float32, device=dev)                    # H A_d^T
+        out = torch.matmul(H, self.W_d.t())
+        if N:
+            self._down(H, self.A_d, None, r, r, 1, ha, None, ws)
+            self._add(out, ha, self.B_d, None, None, 0)
+        self._saved = (xb, xa_g, xa_u, SG, SU, H, ha)
         return out
 
     def backward(self, g: torch.Tensor) -> Tuple[torch.Tensor, Dict[str, torch.Tensor]]:
         """(dL/dx [N, d] bf16, {dA_g, dB_g, dA_u, dB_u, dA_d, dB_d} fp32) of the last forward."""
         if self._saved is None:
             raise RuntimeError("backward before forward")
-        xf, xa_g, xa_u, SG, SU, H, ha = self._saved
-        N, F, s = xf.shape[0], self.F, self.s
-        gb = g.reshape(N, self.d).to(torch.bfloat16).contiguous()
-        gf = gb.float()
-        gB = torch.matmul(gf, self.B_d).contiguous()                                # [N, r]
-        grads = {"dB_d": s * torch.matmul(gf.t(), ha), "dA_d": s * torch.matmul(gB.t(), H.float())}
-        Dh = torch.matmul(gb, self.W_d)                                             # [N, F] bf16
-        DSG = torch.empty((N, F), dtype=torch.bfloat16, device=g.device)
+        xb, xa_g, xa_u, SG, SU, H, ha = self._saved
+        N, F, d, r, s, dev = xb.shape[0], self.F, self.d, self.r, self.s, xb.device
+        gb = g.reshape(N, d).to(torch.bfloat16).contiguous()
+        f32 = lambda *shape: torch.empty(shape, dtype=torch.float32, device=dev)
+        grads = {"dB_d": f32(d, r), "dA_d": f32(r, F), "dB_g": f32(F, r), "dA_g": f32(r, d),
+                 "dB_u": f32(F, r), "dA_u": f32(r, d)}
+        if N == 0:
+            for t in grads.values():
+                t.zero_()
+            return torch.empty((0, d), dtype=torch.bfloat16, device=dev), grads
+        ws = self._workspace(N, dev)
+        gB = f32(N, r)                                                               # g B_d
+        self._down(gb, self.B_d, None, r, r, 0, gB, None, ws)
+        self._outer(ha, gb, True, grads["dB_d"], ws)
+        self._outer(gB, H, False, grads["dA_d"], ws)
+        Dh = torch.matmul(gb, self.W_d)                                              # [N, F] bf16
+        DSG = torch.empty((N, F), dtype=torch.bfloat16, device=dev)
         DSU = torch.empty_like(DSG)
         L.check(self.lib.ll_shared_glu_backward(Dh.data_ptr(), gB.data_ptr(), self.A_d.data_ptr(),
-                                                ctypes.c_float(s), SG.data_ptr(), SU.data_ptr(), N, F, self.r,
+                                                ctypes.c_float(s), SG.data_ptr(), SU.data_ptr(), N, F, r,
                                                 DSG.data_ptr(), DSU.data_ptr(), L.stream_ptr()),
                 "ll_shared_glu_backward")
-        dg, du = DSG.float(), DSU.float()
-        gg = torch.matmul(dg, self.B_g)                                             # [N, r]
-        gu = torch.matmul(du, self.B_u)
-        grads["dB_g"] = s * torch.matmul(dg.t(), xa_g)
-        grads["dA_g"] = s * torch.matmul(gg.t(), xf)
-        grads["dB_u"] = s * torch.matmul(du.t(), xa_u)
-        grads["dA_u"] = s * torch.matmul(gu.t(), xf)
-        dx = (torch.matmul(DSG, self.W_g).float() + torch.matmul(DSU, self.W_u).float()
-              + (s * torch.matmul(gg, self.A_g)).to(torch.bfloat16).float()
-              + (s * torch.matmul(gu, self.A_u)).to(torch.bfloat16).float())
-        return dx.to(torch.bfloat16), grads
+        gg, gu = f32(N, r), f32(N, r)                                                # dSG B_g, dSU B_u
+        self._down(DSG, self.B_g, None, r, r, 0, gg, None, ws)
+        self._down(DSU, self.B_u, None, r, r, 0, gu, None, ws)
+        self._outer(xa_g, DSG, True, grads["dB_g"], ws)
+        self._outer(gg, xb, False, grads["dA_g"], ws)
+        self._outer(xa_u, DSU, True, grads["dB_u"], ws)
+        self._outer(gu, xb, False, grads["dA_u"], ws)
+        dx = torch.matmul(DSG, self.W_g)
+        dx.addmm_(DSU, self.W_u)
+        self._add(dx, gg, self.A_g, gu, self.A_u, 1)
+        return dx, grads

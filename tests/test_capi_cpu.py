@@ -78,3 +78,26 @@ def test_synthetic_distributions():
     # deterministic
     inp2 = make_layer(cfg)
     assert torch.equal(inp["w1p"], inp2["w1p"]) and torch.equal(inp["x"], inp2["x"])
+
+
+def test_lora_entry_points_check_arguments_without_gpu():
+    """Shape and workspace checks of the LoRA products return before any CUDA call."""
+    L = _lib.load()
+    p = ctypes.c_void_p(16)                      # never dereferenced: the checks come first
+    one = ctypes.c_float(1.0)
+    # K % 8 != 0
+    assert L.ll_lora_down(p, 1, 4, 12, p, None, 4, 4, 1, one, p, None, p, 1 << 20, None) == 1
+    # n0 > n; columns form with n0 != n
+    assert L.ll_lora_down(p, 1, 4, 64, p, None, 8, 4, 1, one, p, None, p, 1 << 20, None) == 1
+    assert L.ll_lora_down(p, 1, 4, 64, p, None, 4, 8, 0, one, p, None, p, 1 << 20, None) == 1
+    # a pair of row blocks without the second matrix
+    assert L.ll_lora_down(p, 1, 4, 64, p, None, 4, 8, 1, one, p, None, p, 1 << 20, None) == 1
+    # workspace below one split of M x n
+    assert L.ll_lora_down(p, 1, 64, 64, p, None, 16, 16, 1, one, p, None, p, 4 * 64 * 16 - 4, None) == 4
+    assert L.ll_lora_down(p, 1, 0, 64, p, None, 16, 16, 1, one, p, None, p, 0, None) == 0     # M = 0
+    # C % 4 != 0; workspace below r x C
+    assert L.ll_lora_outer(p, p, 1, 8, 30, 4, one, 0, p, p, 1 << 20, None) == 1
+    assert L.ll_lora_outer(p, p, 1, 8, 32, 4, one, 0, p, p, 4 * 32 * 4 - 4, None) == 4
+    # rank outside {4, 8, 16, 32}
+    assert L.ll_lora_add_bf16(p, p, p, None, None, 12, 1, one, 8, 64, p, None) == 1
+    assert L.ll_lora_add_bf16(p, p, p, None, None, 16, 1, one, 0, 64, p, None) == 0          # N = 0
