@@ -14,6 +14,22 @@ LL_DEV float load_as_float(const void* p, int64_t i) {
   return __half2float(reinterpret_cast<const __half*>(p)[i]);
 }
 
+// sum_{sp < n} p[sp * stride], added in split order (the result of the plain loop); the loads of
+// 8 splits are issued together instead of one at a time
+LL_DEV float sum_splits(const float* __restrict__ p, int64_t stride, int n) {
+  float s = 0.f;
+  int sp = 0;
+  for (; sp + 8 <= n; sp += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = p[(int64_t)(sp + j) * stride];
+#pragma unroll
+    for (int j = 0; j < 8; j++) s += v[j];
+  }
+  for (; sp < n; sp++) s += p[(int64_t)sp * stride];
+  return s;
+}
+
 // ---------------------------------------------------------------- skinny split-K GEMM
 // part[split][m][n] = sum_{k in split} A[m][k] * B(k, n) for the NC columns n = blockIdx.y * NC
 // .. + NC - 1 (N a few tens: the LoRA rank, or twice it).
@@ -35,15 +51,15 @@ struct SkinnyCfg {
   static constexpr int BM = RG * TM;          // 256 rows per block
 };
 
+// 8 elements held as raw 16-byte words (two for fp32, one for bf16 / fp16) -> fp32
 template <int ADT>
-LL_DEV void load8_as_float(const void* A, int64_t off, float (&v)[8]) {
-  if (ADT == 0) {
-    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(A) + off);
-    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(A) + off + 4);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+LL_DEV void words8_as_float(const uint4 (&u)[ADT == 0 ? 2 : 1], float (&v)[8]) {
+  if constexpr (ADT == 0) {
+    const uint32_t w[8] = {u[0].x, u[0].y, u[0].z, u[0].w, u[1].x, u[1].y, u[1].z, u[1].w};
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = __uint_as_float(w[j]);
   } else {
-    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(A) + off);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    const uint32_t w[4] = {u[0].x, u[0].y, u[0].z, u[0].w};
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       float2 f;
@@ -71,22 +87,31 @@ __global__ void __launch_bounds__(256) k_skinny(const void* __restrict__ A, int 
   float acc[TM][4];
 #pragma unroll
   for (int i = 0; i < TM; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-  for (int k0 = k_begin; k0 < k_end; k0 += kSkBK) {
-    for (int i = threadIdx.x; i < SC::BM * (kSkBK / 8); i += 256) {
+  // the next k-step's A rows (raw 16-byte words) and B values are fetched into registers before
+  // the current step's products, so their latency overlaps the FMAs; they are converted and
+  // stored to shared memory at the top of the next step
+  constexpr int LD = SC::BM * (kSkBK / 8) / 256;     // 8-element A loads per thread per step
+  constexpr int LW = ADT == 0 ? 2 : 1;               // 16-byte words per 8 elements
+  constexpr int BLD = NC * kSkBK / 256;              // B values per thread per step
+  static_assert(SC::BM * (kSkBK / 8) % 256 == 0 && NC * kSkBK % 256 == 0, "thread cover");
+  uint4 raw[LD][LW];
+  float bv[BLD];
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int l = 0; l < LD; l++) {
+      const int i = threadIdx.x + l * 256;
       const int r = i / (kSkBK / 8), c8 = (i % (kSkBK / 8)) * 8;
       const int m = m0 + r, k = k0 + c8;
-      float v[8];
-      if (m < M && k < k_end) {
-        load8_as_float<ADT>(A, (int64_t)m * lda + k, v);
-      } else {
+      const bool in = m < M && k < k_end;
 #pragma unroll
-        for (int j = 0; j < 8; j++) v[j] = 0.f;
+      for (int w = 0; w < LW; w++) {
+        const char* src = reinterpret_cast<const char*>(A) + ((int64_t)m * lda + k) * (ADT == 0 ? 4 : 2) + 16 * w;
+        raw[l][w] = in ? *reinterpret_cast<const uint4*>(src) : make_uint4(0u, 0u, 0u, 0u);
       }
-      const int rs = r ^ sk_swz(c8);
-#pragma unroll
-      for (int j = 0; j < 8; j++) As[c8 + j][rs] = v[j];
     }
-    for (int i = threadIdx.x; i < NC * kSkBK; i += 256) {
+#pragma unroll
+    for (int l = 0; l < BLD; l++) {
+      const int i = threadIdx.x + l * 256;
       int n, c;
       if (BROWS) { n = i / kSkBK; c = i % kSkBK; } else { c = i / NC; n = i % NC; }
       const int k = k0 + c, ng = nb0 + n;
@@ -95,9 +120,30 @@ __global__ void __launch_bounds__(256) k_skinny(const void* __restrict__ A, int 
         if (BROWS) v = ng < N0 ? B0[(int64_t)ng * K + k] : B1[(int64_t)(ng - N0) * K + k];
         else v = B0[(int64_t)k * N + ng];
       }
-      Bs[c][n] = v;
+      bv[l] = v;
+    }
+  };
+  if (k_begin < k_end) fetch(k_begin);
+  for (int k0 = k_begin; k0 < k_end; k0 += kSkBK) {
+#pragma unroll
+    for (int l = 0; l < LD; l++) {
+      const int i = threadIdx.x + l * 256;
+      const int r = i / (kSkBK / 8), c8 = (i % (kSkBK / 8)) * 8;
+      float v[8];
+      words8_as_float<ADT>(raw[l], v);
+      const int rs = r ^ sk_swz(c8);
+#pragma unroll
+      for (int j = 0; j < 8; j++) As[c8 + j][rs] = v[j];
+    }
+#pragma unroll
+    for (int l = 0; l < BLD; l++) {
+      const int i = threadIdx.x + l * 256;
+      int n, c;
+      if (BROWS) { n = i / kSkBK; c = i % kSkBK; } else { c = i / NC; n = i % NC; }
+      Bs[c][n] = bv[l];
     }
     __syncthreads();
+    if (k0 + kSkBK < k_end) fetch(k0 + kSkBK);
 #pragma unroll 4
     for (int kk = 0; kk < kSkBK; kk++) {
       const float4 b = *reinterpret_cast<const float4*>(&Bs[kk][cq * 4]);
@@ -134,8 +180,7 @@ __global__ void k_skinny_reduce(const float* __restrict__ part, int nsplit, int 
                                 float* __restrict__ C0, float* __restrict__ C1) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= (int64_t)M * N) return;
-  float s = 0.f;
-  for (int sp = 0; sp < nsplit; sp++) s += part[(int64_t)sp * M * N + i];
+  const float s = sum_splits(part + i, (int64_t)M * N, nsplit);
   const int m = (int)(i / N), n = (int)(i % N);
   if (n < N0) C0[(int64_t)m * N0 + n] = alpha * s;
   else C1[(int64_t)m * (N - N0) + (n - N0)] = alpha * s;
@@ -156,6 +201,62 @@ constexpr int kExTok = 8, kExThreads = 128, kExCols = 4 * kExThreads;
 constexpr int kExPitch = kExCols + 4;
 
 constexpr int kExMaxR = 64;
+
+// The block's R slice into shared memory ([r][kExPitch]; columns >= nc zero), in batches of 8
+// 16-byte loads a thread, so one batch's latency is paid once instead of once per element.
+template <bool RROWS>
+LL_DEV void ex_stage_r(float* Rs, const float* __restrict__ R, int r, int C, int c0, int nc) {
+  const int tid = threadIdx.x;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  const bool vec = (reinterpret_cast<uintptr_t>(R) & 15) == 0 && (RROWS || (r & 3) == 0);
+  if (RROWS && vec) {
+    // row rr of R: the thread's columns 4 tid .. 4 tid + 3 (kExCols = 4 kExThreads)
+    const int cc = 4 * tid;
+    for (int rb = 0; rb < r; rb += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int b = 0; b < 8; b++)
+        v[b] = (cc < nc && rb + b < r) ? *reinterpret_cast<const float4*>(R + (int64_t)(rb + b) * C + c0 + cc) : z4;
+#pragma unroll
+      for (int b = 0; b < 8; b++)
+        if (rb + b < r) *reinterpret_cast<float4*>(Rs + (rb + b) * kExPitch + cc) = v[b];
+    }
+  } else if (vec) {
+    // [C][r]: the block's columns are one contiguous run; 16-byte chunk f holds column 4 f / r,
+    // ranks 4 f % r .. + 3 (r % 4 == 0)
+    const float* base = R + (int64_t)c0 * r;
+    const int nchunk = kExCols * r / 4;
+    for (int f0 = tid; f0 < nchunk; f0 += 8 * kExThreads) {
+      float4 v[8];
+#pragma unroll
+      for (int b = 0; b < 8; b++) {
+        const int f = f0 + b * kExThreads;
+        v[b] = (f < nchunk && (4 * f) / r < nc) ? *reinterpret_cast<const float4*>(base + 4 * (int64_t)f) : z4;
+      }
+#pragma unroll
+      for (int b = 0; b < 8; b++) {
+        const int f = f0 + b * kExThreads;
+        if (f < nchunk) {
+          const int cc = (4 * f) / r, rr = (4 * f) % r;
+          Rs[rr * kExPitch + cc] = v[b].x;
+          Rs[(rr + 1) * kExPitch + cc] = v[b].y;
+          Rs[(rr + 2) * kExPitch + cc] = v[b].z;
+          Rs[(rr + 3) * kExPitch + cc] = v[b].w;
+        }
+      }
+    }
+  } else if (RROWS) {
+    for (int i = tid; i < r * kExCols; i += kExThreads) {
+      const int rr = i / kExCols, cc = i % kExCols;
+      Rs[rr * kExPitch + cc] = cc < nc ? R[(int64_t)rr * C + c0 + cc] : 0.f;
+    }
+  } else {
+    for (int i = tid; i < r * kExCols; i += kExThreads) {
+      const int cc = i / r, rr = i % r;
+      Rs[rr * kExPitch + cc] = cc < nc ? R[(int64_t)(c0 + cc) * r + rr] : 0.f;
+    }
+  }
+}
 
 template <bool RROWS, bool HASY, bool TWO>
 __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ tok_pos, const float* __restrict__ Y, int k,
@@ -180,17 +281,7 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
     const float* R = w == 0 ? R0 : R1;
     const float* Lm = w == 0 ? L0 : L1;
     __syncthreads();                                     // the previous R is no longer read
-    if (RROWS) {
-      for (int i = threadIdx.x; i < r * kExCols; i += kExThreads) {
-        const int rr = i / kExCols, cc = i % kExCols;
-        Rs[rr * kExPitch + cc] = cc < nc ? R[(int64_t)rr * C + c0 + cc] : 0.f;
-      }
-    } else {   // [C][r]: the block's columns are one contiguous run of kExCols * r floats
-      for (int i = threadIdx.x; i < r * kExCols; i += kExThreads) {
-        const int cc = i / r, rr = i % r;
-        Rs[rr * kExPitch + cc] = cc < nc ? R[(int64_t)(c0 + cc) * r + rr] : 0.f;
-      }
-    }
+    ex_stage_r<RROWS>(Rs, R, r, C, c0, nc);
     for (int i = threadIdx.x; i < kExTok * r; i += kExThreads) {
       const int tt = i / r, rr = i % r;
       Ls[tt][rr] = (t0 + tt < T) ? Lm[(int64_t)(t0 + tt) * r + rr] : 0.f;
@@ -242,10 +333,18 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
 // are added in warp order through shared memory.
 constexpr int kOuRB = 16, kOuCW = 128, kOuNB = 8;
 
+// 4 consecutive Q elements as raw words (fp32: 4 words; bf16 / fp16: 2 words, in .x .y), loaded
+// now and converted by raw4_as_float when used, so the conversion does not wait on the load
 template <int QDT>
-LL_DEV float4 load4_as_float(const void* Q, int64_t off) {
-  if (QDT == 0) return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(Q) + off);
+LL_DEV uint4 load4_raw(const void* Q, int64_t off) {
+  if (QDT == 0) return *reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(Q) + off);
   const uint2 v = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(Q) + off);
+  return make_uint4(v.x, v.y, 0u, 0u);
+}
+
+template <int QDT>
+LL_DEV float4 raw4_as_float(const uint4 v) {
+  if (QDT == 0) return make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
   float2 a, b;
   if (QDT == 1) {
     a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
@@ -276,7 +375,12 @@ __global__ void __launch_bounds__(256) k_outer8(const float* __restrict__ Pm, co
 #pragma unroll
   for (int i = 0; i < kOuRB; i++) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int nb = n0 + warp * kOuNB; nb < n1; nb += 8 * kOuNB) {
-    // this warp's batch: rows nb .. nb + 7 of Pm (rank slice) into shared memory
+    // the batch's 8 Q rows are requested first, then rows nb .. nb + 7 of Pm (rank slice) go
+    // to shared memory while they are in flight
+    uint4 qr[kOuNB];
+#pragma unroll
+    for (int nn = 0; nn < kOuNB; nn++)
+      qr[nn] = (cok && nb + nn < n1) ? load4_raw<QDT>(Q, (int64_t)(nb + nn) * C + c) : make_uint4(0u, 0u, 0u, 0u);
     for (int i = lane; i < kOuNB * kOuRB; i += 32) {
       const int nn = i / kOuRB, rr = i % kOuRB;
       const int n = nb + nn;
@@ -284,20 +388,17 @@ __global__ void __launch_bounds__(256) k_outer8(const float* __restrict__ Pm, co
       if (n < n1 && rr < rn) v = PGATHER ? tw[n] * Pm[(int64_t)perm_token[n] * r + rb + rr] : Pm[(int64_t)n * r + rb + rr];
       ps[warp][nn][rr] = v;
     }
-    float4 q[kOuNB];
-#pragma unroll
-    for (int nn = 0; nn < kOuNB; nn++)
-      q[nn] = (cok && nb + nn < n1) ? load4_as_float<QDT>(Q, (int64_t)(nb + nn) * C + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     __syncwarp();
 #pragma unroll
     for (int nn = 0; nn < kOuNB; nn++) {
+      const float4 q = raw4_as_float<QDT>(qr[nn]);
 #pragma unroll
       for (int i = 0; i < kOuRB; i++) {
         const float p = ps[warp][nn][i];
-        acc[i].x = fmaf(p, q[nn].x, acc[i].x);
-        acc[i].y = fmaf(p, q[nn].y, acc[i].y);
-        acc[i].z = fmaf(p, q[nn].z, acc[i].z);
-        acc[i].w = fmaf(p, q[nn].w, acc[i].w);
+        acc[i].x = fmaf(p, q.x, acc[i].x);
+        acc[i].y = fmaf(p, q.y, acc[i].y);
+        acc[i].z = fmaf(p, q.z, acc[i].z);
+        acc[i].w = fmaf(p, q.w, acc[i].w);
       }
     }
     __syncwarp();

@@ -282,8 +282,7 @@ __global__ void k_outer_reduce(const float* __restrict__ part, int nseg, int r, 
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= (int64_t)r * C) return;
   const int rr = (int)(i / C), c = (int)(i % C);
-  float acc = 0.f;
-  for (int sg = 0; sg < nseg; sg++) acc += part[((int64_t)sg * r + rr) * C + c];
+  const float acc = sum_splits(part + i, (int64_t)r * C, nseg);
   if (transposed) out[(int64_t)c * r + rr] = s * acc;
   else out[i] = s * acc;
 }

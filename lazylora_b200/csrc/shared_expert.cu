@@ -9,8 +9,8 @@
 // backward: dh = bf16(Dh + bf16(s * gB . A_d)),  (dsg, dsu) = bf16(situ_glu_backward(dh, sg, su))
 //   Dh: the bf16 input gradient of the down projection (g W_d); gB = g B_d [N, r] fp32;
 //   A_d [r, F] fp32 (the down adapter's A, whose input is h).
-// Block: 256 columns x 8 tokens; a thread keeps its column's r adapter values in registers and
-// reads the 8 tokens' r-vectors from shared memory.
+// Block: 256 columns x 32 tokens; a thread keeps its column's r adapter values in registers and
+// reads the tokens' r-vectors from shared memory.
 //
 // Also here, the C-ABI of the LoRA products around such bf16 GEMMs (the shared expert's, or any
 // dense projection's), which read the bf16 activations directly instead of an fp32 copy:
@@ -25,10 +25,12 @@
 
 namespace ll {
 
-constexpr int kSgCols = 256, kSgTok = 8;
+constexpr int kSgCols = 256, kSgTok = 32, kSgB = 4;
 
 LL_DEV float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
+// Tokens t0 .. t0 + kSgTok - 1 in batches of kSgB: a batch's bf16 inputs are all requested
+// (predicated, no early exit) before the first is used, so kSgB loads per input are in flight.
 template <int R>
 __global__ void __launch_bounds__(kSgCols) k_shared_glu_fwd(const __nv_bfloat16* __restrict__ G,
                                                             const __nv_bfloat16* __restrict__ U,
@@ -52,22 +54,32 @@ __global__ void __launch_bounds__(kSgCols) k_shared_glu_fwd(const __nv_bfloat16*
     bg[rr] = Bg[(int64_t)j * R + rr];
     bu[rr] = Bu[(int64_t)j * R + rr];
   }
-#pragma unroll 2
-  for (int tt = 0; tt < kSgTok; tt++) {
-    const int t = t0 + tt;
-    if (t >= N) break;
-    float dg = 0.f, du = 0.f;
+  for (int tb = 0; tb < kSgTok && t0 + tb < N; tb += kSgB) {
+    float gv[kSgB], uv[kSgB];
 #pragma unroll
-    for (int rr = 0; rr < R; rr++) {
-      dg = fmaf(la[tt][rr], bg[rr], dg);
-      du = fmaf(la[tt][R + rr], bu[rr], du);
+    for (int q = 0; q < kSgB; q++) {
+      const int t = t0 + tb + q;
+      const int64_t o = (int64_t)t * F + j;
+      gv[q] = t < N ? __bfloat162float(G[o]) : 0.f;
+      uv[q] = t < N ? __bfloat162float(U[o]) : 0.f;
     }
-    const int64_t o = (int64_t)t * F + j;
-    const float sg = bf16r(__bfloat162float(G[o]) + bf16r(s * dg));
-    const float su = bf16r(__bfloat162float(U[o]) + bf16r(s * du));
-    SG[o] = __float2bfloat16_rn(sg);
-    SU[o] = __float2bfloat16_rn(su);
-    H[o] = __float2bfloat16_rn(situ_glu_fwd(sg, su));
+#pragma unroll
+    for (int q = 0; q < kSgB; q++) {
+      const int t = t0 + tb + q;
+      if (t >= N) break;
+      float dg = 0.f, du = 0.f;
+#pragma unroll
+      for (int rr = 0; rr < R; rr++) {
+        dg = fmaf(la[tb + q][rr], bg[rr], dg);
+        du = fmaf(la[tb + q][R + rr], bu[rr], du);
+      }
+      const int64_t o = (int64_t)t * F + j;
+      const float sg = bf16r(gv[q] + bf16r(s * dg));
+      const float su = bf16r(uv[q] + bf16r(s * du));
+      SG[o] = __float2bfloat16_rn(sg);
+      SU[o] = __float2bfloat16_rn(su);
+      H[o] = __float2bfloat16_rn(situ_glu_fwd(sg, su));
+    }
   }
 }
 
@@ -91,37 +103,47 @@ __global__ void __launch_bounds__(kSgCols) k_shared_glu_bwd(const __nv_bfloat16*
   float ad[R];
 #pragma unroll
   for (int rr = 0; rr < R; rr++) ad[rr] = Ad[(int64_t)rr * F + j];
-#pragma unroll 2
-  for (int tt = 0; tt < kSgTok; tt++) {
-    const int t = t0 + tt;
-    if (t >= N) break;
-    float dl = 0.f;
+  for (int tb = 0; tb < kSgTok && t0 + tb < N; tb += kSgB) {
+    float hv[kSgB], gv[kSgB], uv[kSgB];
 #pragma unroll
-    for (int rr = 0; rr < R; rr++) dl = fmaf(lg[tt][rr], ad[rr], dl);
-    const int64_t o = (int64_t)t * F + j;
-    const float go = bf16r(__bfloat162float(Dh[o]) + bf16r(s * dl));
-    float dsg, dsu;
-    situ_glu_bwd(go, __bfloat162float(SG[o]), __bfloat162float(SU[o]), dsg, dsu);
-    DSG[o] = __float2bfloat16_rn(dsg);
-    DSU[o] = __float2bfloat16_rn(dsu);
+    for (int q = 0; q < kSgB; q++) {
+      const int t = t0 + tb + q;
+      const int64_t o = (int64_t)t * F + j;
+      hv[q] = t < N ? __bfloat162float(Dh[o]) : 0.f;
+      gv[q] = t < N ? __bfloat162float(SG[o]) : 0.f;
+      uv[q] = t < N ? __bfloat162float(SU[o]) : 0.f;
+    }
+#pragma unroll
+    for (int q = 0; q < kSgB; q++) {
+      const int t = t0 + tb + q;
+      if (t >= N) break;
+      float dl = 0.f;
+#pragma unroll
+      for (int rr = 0; rr < R; rr++) dl = fmaf(lg[tb + q][rr], ad[rr], dl);
+      const int64_t o = (int64_t)t * F + j;
+      const float go = bf16r(hv[q] + bf16r(s * dl));
+      float dsg, dsu;
+      situ_glu_bwd(go, gv[q], uv[q], dsg, dsu);
+      DSG[o] = __float2bfloat16_rn(dsg);
+      DSU[o] = __float2bfloat16_rn(dsu);
+    }
   }
 }
 
 // out[t][c] = bf16(Y[t][c] + bf16(s * sum_rr L0[t][rr] R0(rr, c)) [+ bf16(s * L1[t] . R1(:, c))])
 // R(rr, c): RROWS -> R[rr * C + c] ([r][C]); else R[c * r + rr] ([C][r]). Y may alias out.
-// Block: 256 columns x 32 tokens; a thread keeps its column's adapter values in registers.
-constexpr int kLaCols = 256, kLaTok = 32;
-
+// Block: 256 columns x 32 tokens (batches of 4 as above); a thread keeps its column's adapter
+// values in registers.
 template <int R, bool TWO, bool RROWS>
-__global__ void __launch_bounds__(kLaCols) k_lora_add_bf16(const __nv_bfloat16* Y, const float* __restrict__ L0,
+__global__ void __launch_bounds__(kSgCols) k_lora_add_bf16(const __nv_bfloat16* Y, const float* __restrict__ L0,
                                                            const float* __restrict__ R0, const float* __restrict__ L1,
                                                            const float* __restrict__ R1, float s, int N, int C,
                                                            __nv_bfloat16* out) {
   constexpr int NW = TWO ? 2 : 1;
-  __shared__ float ls[kLaTok][NW * R];
-  const int j = blockIdx.x * kLaCols + threadIdx.x;
-  const int t0 = blockIdx.y * kLaTok;
-  for (int i = threadIdx.x; i < kLaTok * NW * R; i += kLaCols) {
+  __shared__ float ls[kSgTok][NW * R];
+  const int j = blockIdx.x * kSgCols + threadIdx.x;
+  const int t0 = blockIdx.y * kSgTok;
+  for (int i = threadIdx.x; i < kSgTok * NW * R; i += kSgCols) {
     const int tt = i / (NW * R), rr = i % (NW * R);
     const int t = t0 + tt;
     ls[tt][rr] = t < N ? (rr < R ? L0[(int64_t)t * R + rr] : L1[(int64_t)t * R + rr - R]) : 0.f;
@@ -135,20 +157,27 @@ __global__ void __launch_bounds__(kLaCols) k_lora_add_bf16(const __nv_bfloat16* 
 #pragma unroll
     for (int rr = 0; rr < R; rr++) rv[w][rr] = RROWS ? Rm[(int64_t)rr * C + j] : Rm[(int64_t)j * R + rr];
   }
-#pragma unroll 4
-  for (int tt = 0; tt < kLaTok; tt++) {
-    const int t = t0 + tt;
-    if (t >= N) break;
-    const int64_t o = (int64_t)t * C + j;
-    float v = __bfloat162float(Y[o]);
+  for (int tb = 0; tb < kSgTok && t0 + tb < N; tb += kSgB) {
+    float yv[kSgB];
 #pragma unroll
-    for (int w = 0; w < NW; w++) {
-      float dl = 0.f;
-#pragma unroll
-      for (int rr = 0; rr < R; rr++) dl = fmaf(ls[tt][w * R + rr], rv[w][rr], dl);
-      v += bf16r(s * dl);
+    for (int q = 0; q < kSgB; q++) {
+      const int t = t0 + tb + q;
+      yv[q] = t < N ? __bfloat162float(Y[(int64_t)t * C + j]) : 0.f;
     }
-    out[o] = __float2bfloat16_rn(v);
+#pragma unroll
+    for (int q = 0; q < kSgB; q++) {
+      const int t = t0 + tb + q;
+      if (t >= N) break;
+      float v = yv[q];
+#pragma unroll
+      for (int w = 0; w < NW; w++) {
+        float dl = 0.f;
+#pragma unroll
+        for (int rr = 0; rr < R; rr++) dl = fmaf(ls[tb + q][w * R + rr], rv[w][rr], dl);
+        v += bf16r(s * dl);
+      }
+      out[(int64_t)t * C + j] = __float2bfloat16_rn(v);
+    }
   }
 }
 
@@ -229,10 +258,10 @@ int ll_lora_add_bf16(const void* Y, const float* L0, const float* R0, const floa
   if (N == 0) return LL_OK;
   if (!Y || !L0 || !R0 || !out || (L1 && !R1)) return LL_ERR_ARG;
   LL_STREAM(stream);
-  const dim3 grid((C + kLaCols - 1) / kLaCols, (N + kLaTok - 1) / kLaTok);
+  const dim3 grid((C + kSgCols - 1) / kSgCols, (N + kSgTok - 1) / kSgTok);
   auto y = static_cast<const __nv_bfloat16*>(Y);
   auto o = static_cast<__nv_bfloat16*>(out);
-#define LL_LA(RR, TW, RW) k_lora_add_bf16<RR, TW, RW><<<grid, kLaCols, 0, s>>>(y, L0, R0, L1, R1, scale, N, C, o)
+#define LL_LA(RR, TW, RW) k_lora_add_bf16<RR, TW, RW><<<grid, kSgCols, 0, s>>>(y, L0, R0, L1, R1, scale, N, C, o)
 #define LL_LA_R(TW, RW)                                                                          \
   do {                                                                                           \
     if (r == 4) LL_LA(4, TW, RW); else if (r == 8) LL_LA(8, TW, RW);                             \
