@@ -328,32 +328,49 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
 // part[seg][rr][c] = sum_{n in seg} Pm(n, rr) * Q[n][c] for the ranks rr = kOuRB blockIdx.z ..
 // + kOuRB - 1 and the 128 columns of blockIdx.x. Pm: [N][r] fp32, or (PGATHER) tw[n] *
 // Pm[perm_token[n]][rr]. Q dtype QDT (0 f32, 1 bf16, 2 f16), C % 4 == 0.
-// Block = 8 warps, lane = 4 consecutive columns; the 8 warps take interleaved batches of 8
-// rows n of the segment (the 8 Q loads of a batch issued before the FMAs), then their sums
-// are added in warp order through shared memory.
-constexpr int kOuRB = 16, kOuCW = 128, kOuNB = 8;
+// Block = 8 warps, lane = 4 consecutive columns; the 8 warps take interleaved batches of
+// kOuNB rows n of the segment (a batch's Q loads issued before its FMAs, and for 16-bit Q the
+// next batch's during them), then their sums are added in warp order through shared memory.
+constexpr int kOuRB = 16, kOuCW = 128, kOuNB = 4;
 
-// 4 consecutive Q elements as raw words (fp32: 4 words; bf16 / fp16: 2 words, in .x .y), loaded
-// now and converted by raw4_as_float when used, so the conversion does not wait on the load
+// 4 consecutive Q elements as raw words (fp32: uint4; bf16 / fp16: uint2), loaded now and
+// converted by raw4_as_float when used, so the conversion does not wait on the load
 template <int QDT>
-LL_DEV uint4 load4_raw(const void* Q, int64_t off) {
-  if (QDT == 0) return *reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(Q) + off);
-  const uint2 v = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(Q) + off);
-  return make_uint4(v.x, v.y, 0u, 0u);
+struct QRaw {
+  using T = uint2;
+};
+template <>
+struct QRaw<0> {
+  using T = uint4;
+};
+
+template <int QDT>
+LL_DEV typename QRaw<QDT>::T load4_raw(const void* Q, int64_t off) {
+  if constexpr (QDT == 0) return *reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(Q) + off);
+  else return *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(Q) + off);
 }
 
 template <int QDT>
-LL_DEV float4 raw4_as_float(const uint4 v) {
-  if (QDT == 0) return make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
-  float2 a, b;
-  if (QDT == 1) {
-    a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
-    b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+LL_DEV typename QRaw<QDT>::T raw_zero() {
+  if constexpr (QDT == 0) return make_uint4(0u, 0u, 0u, 0u);
+  else return make_uint2(0u, 0u);
+}
+
+template <int QDT>
+LL_DEV float4 raw4_as_float(const typename QRaw<QDT>::T v) {
+  if constexpr (QDT == 0) {
+    return make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
   } else {
-    a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
-    b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+    float2 a, b;
+    if (QDT == 1) {
+      a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
+      b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+    } else {
+      a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+      b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+    }
+    return make_float4(a.x, a.y, b.x, b.y);
   }
-  return make_float4(a.x, a.y, b.x, b.y);
 }
 
 template <int QDT, bool PGATHER>
@@ -362,7 +379,7 @@ __global__ void __launch_bounds__(256) k_outer8(const float* __restrict__ Pm, co
                                                 const int* __restrict__ n_dev, int C, int r, int nseg,
                                                 float* __restrict__ part) {
   extern __shared__ float4 red4[];                    // [8 warps][kOuRB][32 lanes] float4
-  __shared__ float ps[8][kOuNB][kOuRB];
+  __shared__ __align__(16) float ps[8][kOuNB][kOuRB];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int c = blockIdx.x * kOuCW + lane * 4;
   const bool cok = c < C;
@@ -374,31 +391,67 @@ __global__ void __launch_bounds__(256) k_outer8(const float* __restrict__ Pm, co
   float4 acc[kOuRB];
 #pragma unroll
   for (int i = 0; i < kOuRB; i++) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int nb = n0 + warp * kOuNB; nb < n1; nb += 8 * kOuNB) {
-    // the batch's 8 Q rows are requested first, then rows nb .. nb + 7 of Pm (rank slice) go
-    // to shared memory while they are in flight
-    uint4 qr[kOuNB];
+  // software pipeline over this warp's batches of kOuNB rows: the next batch's Q words and Pm
+  // values are requested before the current batch's FMAs (16-bit Q; fp32 Q, twice the
+  // registers, requests each batch's rows just before staging its Pm)
+  constexpr bool PIPE = QDT != 0;
+  auto pm_val = [&](int nb, int i) {
+    const int nn = i / kOuRB, rr = i % kOuRB;
+    const int n = nb + nn;
+    float v = 0.f;
+    if (n < n1 && rr < rn) v = PGATHER ? tw[n] * Pm[(int64_t)perm_token[n] * r + rb + rr] : Pm[(int64_t)n * r + rb + rr];
+    return v;
+  };
+  constexpr int PV = kOuNB * kOuRB / 32;              // Pm values a lane stages per batch
+  typename QRaw<QDT>::T qr[kOuNB];
+  float pv[PV];
+  int nb = n0 + warp * kOuNB;
+  if (PIPE && nb < n1) {
 #pragma unroll
     for (int nn = 0; nn < kOuNB; nn++)
-      qr[nn] = (cok && nb + nn < n1) ? load4_raw<QDT>(Q, (int64_t)(nb + nn) * C + c) : make_uint4(0u, 0u, 0u, 0u);
-    for (int i = lane; i < kOuNB * kOuRB; i += 32) {
-      const int nn = i / kOuRB, rr = i % kOuRB;
-      const int n = nb + nn;
-      float v = 0.f;
-      if (n < n1 && rr < rn) v = PGATHER ? tw[n] * Pm[(int64_t)perm_token[n] * r + rb + rr] : Pm[(int64_t)n * r + rb + rr];
-      ps[warp][nn][rr] = v;
+      qr[nn] = (cok && nb + nn < n1) ? load4_raw<QDT>(Q, (int64_t)(nb + nn) * C + c) : raw_zero<QDT>();
+#pragma unroll
+    for (int j = 0; j < PV; j++) pv[j] = pm_val(nb, lane + 32 * j);
+  }
+  for (; nb < n1; nb += 8 * kOuNB) {
+    if (!PIPE) {
+#pragma unroll
+      for (int nn = 0; nn < kOuNB; nn++)
+        qr[nn] = (cok && nb + nn < n1) ? load4_raw<QDT>(Q, (int64_t)(nb + nn) * C + c) : raw_zero<QDT>();
+#pragma unroll
+      for (int j = 0; j < PV; j++) pv[j] = pm_val(nb, lane + 32 * j);
+    }
+#pragma unroll
+    for (int j = 0; j < PV; j++) {
+      const int i = lane + 32 * j;
+      ps[warp][i / kOuRB][i % kOuRB] = pv[j];
     }
     __syncwarp();
+    typename QRaw<QDT>::T qc[kOuNB];
+#pragma unroll
+    for (int nn = 0; nn < kOuNB; nn++) qc[nn] = qr[nn];
+    const int nx = nb + 8 * kOuNB;                   // this warp's next batch
+    if (PIPE && nx < n1) {
+#pragma unroll
+      for (int nn = 0; nn < kOuNB; nn++)
+        qr[nn] = (cok && nx + nn < n1) ? load4_raw<QDT>(Q, (int64_t)(nx + nn) * C + c) : raw_zero<QDT>();
+#pragma unroll
+      for (int j = 0; j < PV; j++) pv[j] = pm_val(nx, lane + 32 * j);
+    }
 #pragma unroll
     for (int nn = 0; nn < kOuNB; nn++) {
-      const float4 q = raw4_as_float<QDT>(qr[nn]);
+      const float4 q = raw4_as_float<QDT>(qc[nn]);
 #pragma unroll
-      for (int i = 0; i < kOuRB; i++) {
-        const float p = ps[warp][nn][i];
-        acc[i].x = fmaf(p, q.x, acc[i].x);
-        acc[i].y = fmaf(p, q.y, acc[i].y);
-        acc[i].z = fmaf(p, q.z, acc[i].z);
-        acc[i].w = fmaf(p, q.w, acc[i].w);
+      for (int i = 0; i < kOuRB; i += 4) {
+        const float4 p4 = *reinterpret_cast<const float4*>(&ps[warp][nn][i]);
+        const float pp[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          acc[i + u].x = fmaf(pp[u], q.x, acc[i + u].x);
+          acc[i + u].y = fmaf(pp[u], q.y, acc[i + u].y);
+          acc[i + u].z = fmaf(pp[u], q.z, acc[i + u].z);
+          acc[i + u].w = fmaf(pp[u], q.w, acc[i + u].w);
+        }
       }
     }
     __syncwarp();
