@@ -42,8 +42,8 @@ UNIT = "tokens/s"
 # from one ncu capture of the same kernels at d=7168, f=2048, 64 experts, 9 tokens per expert.
 # Weight reads dominate, so a launch's traffic scales with the number of experts it touches.
 NCU_DRAM_BYTES_PER_EXPERT = {
-    (7168, 2048): [(1020.624e6 + 15.785984e6) / 64, (501.543e6 + 16.321280e6) / 64,
-                   (548.367e6 + 9.828096e6) / 64, (1061.762e6 + 18.684928e6) / 64],
+    (7168, 2048): [(1020.498e6 + 13.916672e6) / 64, (501.540e6 + 16.182016e6) / 64,
+                   (548.347e6 + 9.062400e6) / 64, (1061.752e6 + 18.494720e6) / 64],
 }
 
 
