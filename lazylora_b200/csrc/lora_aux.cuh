@@ -190,11 +190,11 @@ __global__ void k_skinny_reduce(const float* __restrict__ part, int nsplit, int 
 // out[t][c] = [sum_j Y[pos_j][c], pairs of t in ascending expert order]
 //           + alpha * (sum_rr L0[t][rr] R0(rr, c) + sum_rr L1[t][rr] R1(rr, c))
 // R(rr, c): RROWS -> R[rr*C + c] ([r][C]);  else R[c*r + rr] ([C][r]).
-// Block: 512 columns (4 a thread, 16-byte loads and stores) x 8 tokens; the R slices of the
-// block's columns are staged in shared memory once and reused by the 8 tokens, and a
-// token's k rows of Y are all requested before the first is added (k <= 8 per batch), so the
-// kernel streams Y at memory speed instead of one dependent load at a time.
-constexpr int kExTok = 8, kExThreads = 128, kExCols = 4 * kExThreads;
+// Block: 512 columns (2 a thread, 8-byte loads and stores; 8 warps, so that the shared-memory
+// bound occupancy of ~6 blocks per SM still keeps 48 warps streaming) x 8 tokens; the R slices
+// of the block's columns are staged in shared memory once and reused by the 8 tokens, and a
+// token's k rows of Y are all requested before the first is added (k <= 8 per batch).
+constexpr int kExTok = 8, kExThreads = 256, kExCols = 2 * kExThreads;
 // shared row pitch of the staged R slices: 4 floats of padding keep the float4 reads aligned and
 // spread the transposing stores of a [C][r] R (16 consecutive rr of one column) over 8 banks
 // instead of one
@@ -210,16 +210,22 @@ LL_DEV void ex_stage_r(float* Rs, const float* __restrict__ R, int r, int C, int
   const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
   const bool vec = (reinterpret_cast<uintptr_t>(R) & 15) == 0 && (RROWS || (r & 3) == 0);
   if (RROWS && vec) {
-    // row rr of R: the thread's columns 4 tid .. 4 tid + 3 (kExCols = 4 kExThreads)
-    const int cc = 4 * tid;
-    for (int rb = 0; rb < r; rb += 8) {
+    // 16-byte chunk f: row f / (kExCols / 4) of R, columns 4 (f % (kExCols / 4)) .. + 3
+    constexpr int CPR = kExCols / 4;
+    const int nchunk = r * CPR;
+    for (int f0 = tid; f0 < nchunk; f0 += 8 * kExThreads) {
       float4 v[8];
 #pragma unroll
-      for (int b = 0; b < 8; b++)
-        v[b] = (cc < nc && rb + b < r) ? *reinterpret_cast<const float4*>(R + (int64_t)(rb + b) * C + c0 + cc) : z4;
+      for (int b = 0; b < 8; b++) {
+        const int f = f0 + b * kExThreads;
+        const int rr = f / CPR, cc = (f % CPR) * 4;
+        v[b] = (f < nchunk && cc < nc) ? *reinterpret_cast<const float4*>(R + (int64_t)rr * C + c0 + cc) : z4;
+      }
 #pragma unroll
-      for (int b = 0; b < 8; b++)
-        if (rb + b < r) *reinterpret_cast<float4*>(Rs + (rb + b) * kExPitch + cc) = v[b];
+      for (int b = 0; b < 8; b++) {
+        const int f = f0 + b * kExThreads;
+        if (f < nchunk) *reinterpret_cast<float4*>(Rs + (f / CPR) * kExPitch + (f % CPR) * 4) = v[b];
+      }
     }
   } else if (vec) {
     // [C][r]: the block's columns are one contiguous run; 16-byte chunk f holds column 4 f / r,
@@ -268,15 +274,15 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
   __shared__ int ps[kExTok][32];
   const int c0 = blockIdx.x * kExCols, t0 = blockIdx.y * kExTok;
   const int nc = min(kExCols, C - c0);
-  const int c = 4 * threadIdx.x;
+  const int c = 2 * threadIdx.x;
   if (HASY)
     for (int i = threadIdx.x; i < kExTok * k; i += kExThreads) {
       const int tt = i / k, j = i % k;
       ps[tt][j] = (t0 + tt < T) ? tok_pos[(int64_t)(t0 + tt) * k + j] : -1;
     }
-  float4 lo[kExTok];
+  float2 lo[kExTok];
 #pragma unroll
-  for (int tt = 0; tt < kExTok; tt++) lo[tt] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int tt = 0; tt < kExTok; tt++) lo[tt] = make_float2(0.f, 0.f);
   for (int w = 0; w < (TWO ? 2 : 1); w++) {
     const float* R = w == 0 ? R0 : R1;
     const float* Lm = w == 0 ? L0 : L1;
@@ -289,12 +295,11 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
     __syncthreads();
     if (c < nc)
       for (int rr = 0; rr < r; rr++) {
-        const float4 rv = *reinterpret_cast<const float4*>(Rs + rr * kExPitch + c);
+        const float2 rv = *reinterpret_cast<const float2*>(Rs + rr * kExPitch + c);
 #pragma unroll
         for (int tt = 0; tt < kExTok; tt++) {
           const float l = Ls[tt][rr];
           lo[tt].x = fmaf(l, rv.x, lo[tt].x); lo[tt].y = fmaf(l, rv.y, lo[tt].y);
-          lo[tt].z = fmaf(l, rv.z, lo[tt].z); lo[tt].w = fmaf(l, rv.w, lo[tt].w);
         }
       }
   }
@@ -302,25 +307,24 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
 #pragma unroll
   for (int tt = 0; tt < kExTok; tt++) {
     if (t0 + tt >= T) break;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float2 acc = make_float2(0.f, 0.f);
     if (HASY) {
       for (int j0 = 0; j0 < k; j0 += 8) {
-        float4 v[8];
+        float2 v[8];
 #pragma unroll
         for (int j = 0; j < 8; j++) {                    // all requests first
           const int p = j0 + j < k ? ps[tt][j0 + j] : -1;
-          v[j] = p >= 0 ? *reinterpret_cast<const float4*>(Y + (int64_t)p * C + c0 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+          v[j] = p >= 0 ? *reinterpret_cast<const float2*>(Y + (int64_t)p * C + c0 + c) : make_float2(0.f, 0.f);
         }
 #pragma unroll
         for (int j = 0; j < 8; j++) {                    // then the sum, in slot order
-          acc.x += v[j].x; acc.y += v[j].y; acc.z += v[j].z; acc.w += v[j].w;
+          acc.x += v[j].x; acc.y += v[j].y;
         }
       }
     }
-    float4 o;
+    float2 o;
     o.x = acc.x + alpha * lo[tt].x; o.y = acc.y + alpha * lo[tt].y;
-    o.z = acc.z + alpha * lo[tt].z; o.w = acc.w + alpha * lo[tt].w;
-    *reinterpret_cast<float4*>(out + (int64_t)(t0 + tt) * C + c0 + c) = o;
+    *reinterpret_cast<float2*>(out + (int64_t)(t0 + tt) * C + c0 + c) = o;
   }
 }
 
