@@ -101,3 +101,13 @@ def test_lora_entry_points_check_arguments_without_gpu():
     # rank outside {4, 8, 16, 32}
     assert L.ll_lora_add_bf16(p, p, p, None, None, 12, 1, one, 8, 64, p, None) == 1
     assert L.ll_lora_add_bf16(p, p, p, None, None, 16, 1, one, 0, 64, p, None) == 0          # N = 0
+
+
+def test_shared_expert_refuses_cpu_tensors():
+    """The shared expert has no CPU path: CPU weights are refused, not computed on the host."""
+    from lazylora_b200.trainer.shared_expert import SharedExpert
+    d, F, r = 64, 96, 4
+    W = lambda o, i: torch.zeros(o, i, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        SharedExpert(W(F, d), W(F, d), W(d, F), torch.zeros(r, d), torch.zeros(F, r), torch.zeros(r, d),
+                     torch.zeros(F, r), torch.zeros(r, F), torch.zeros(d, r), 2.0)
