@@ -17,7 +17,9 @@ adapters' input-gradient terms, are added to the bf16 GEMM outputs in place
 (ll_lora_add_bf16). The backward returns dL/dx and the six LoRA gradients, following the
 autograd graph of the reference's forward (lora_layer.py:104-123: the adapter casts its bf16
 input to fp32 and its fp32 delta back to bf16); the two gate/up input-gradient GEMMs
-accumulate into one bf16 buffer (cuBLAS with beta = 1).
+accumulate into one bf16 buffer (cuBLAS with beta = 1). The LoRA products and adapter gradients
+run on a second stream beside the bf16 GEMMs (events order each consumer after its producer), so
+the small latency-bound kernels fill the GEMMs' gaps instead of adding to the step.
 """
 import ctypes
 from typing import Dict, Tuple
@@ -48,13 +50,22 @@ class SharedExpert:
         self.lib = L.load()
         self._saved = None
         self._ws = None
+        self._side = None
+
+    def _side_stream(self, device) -> torch.cuda.Stream:
+        """The stream the LoRA products run on, beside the bf16 GEMMs on the caller's stream."""
+        if self._side is None or self._side.device != device:
+            self._side = torch.cuda.Stream(device=device)
+        return self._side
 
     def _workspace(self, N: int, device) -> torch.Tensor:
         """Split-K partials of the LoRA products: 16 MB covers the splits that fill the GPU at the
-        shapes here, plus one full [N, 2r] product for a single split."""
+        shapes here, plus one full [N, 2r] product for a single split. Allocated on, and used only
+        by, the side stream, so its memory is reused in that stream's order."""
         need = 16 * 1024 * 1024 + 4 * N * 2 * self.r
         if self._ws is None or self._ws.numel() * 4 < need or self._ws.device != device:
-            self._ws = torch.empty(need // 4, dtype=torch.float32, device=device)
+            with torch.cuda.stream(self._side_stream(device)):
+                self._ws = torch.empty(need // 4, dtype=torch.float32, device=device)
         return self._ws
 
     def _down(self, X, B0, B1, n0, n, b_rows, C0, C1, ws):
@@ -76,34 +87,45 @@ class SharedExpert:
                                           L.stream_ptr()), "ll_lora_add_bf16")
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        """out [N, d] bf16 for x [N, d]."""
+        """out [N, d] bf16 for x [N, d]. The LoRA products run on a side stream while the bf16
+        GEMMs run on the caller's stream; the caller's stream waits for them before returning."""
         L.require_cuda(x)
         xb = x.reshape(-1, self.d).to(torch.bfloat16).contiguous()
         N, F, r, dev = xb.shape[0], self.F, self.r, x.device
+        main, side = torch.cuda.current_stream(dev), self._side_stream(dev)
         ws = self._workspace(N, dev)
-        G = torch.matmul(xb, self.W_g.t())
-        U = torch.matmul(xb, self.W_u.t())
         xa_g = torch.empty((N, r), dtype=torch.float32, device=dev)
         xa_u = torch.empty_like(xa_g)
+        ha = torch.empty((N, r), dtype=torch.float32, device=dev)                    # H A_d^T
+        side.wait_stream(main)
         if N:
-            self._down(xb, self.A_g, self.A_u, r, 2 * r, 1, xa_g, xa_u, ws)
+            with torch.cuda.stream(side):
+                self._down(xb, self.A_g, self.A_u, r, 2 * r, 1, xa_g, xa_u, ws)
+        G = torch.matmul(xb, self.W_g.t())
+        U = torch.matmul(xb, self.W_u.t())
         SG = torch.empty((N, F), dtype=torch.bfloat16, device=dev)
         SU = torch.empty_like(SG)
         H = torch.empty_like(SG)
+        main.wait_stream(side)
         L.check(self.lib.ll_shared_glu_forward(G.data_ptr(), U.data_ptr(), xa_g.data_ptr(), xa_u.data_ptr(),
                                                self.B_g.data_ptr(), self.B_u.data_ptr(), ctypes.c_float(self.s),
                                                N, F, r, SG.data_ptr(), SU.data_ptr(), H.data_ptr(),
                                                L.stream_ptr()), "ll_shared_glu_forward")
-        ha = torch.empty((N, r), dtype=torch.float32, device=dev)                    # H A_d^T
-        out = torch.matmul(H, self.W_d.t())
+        side.wait_stream(main)
         if N:
-            self._down(H, self.A_d, None, r, r, 1, ha, None, ws)
+            with torch.cuda.stream(side):
+                self._down(H, self.A_d, None, r, r, 1, ha, None, ws)
+        out = torch.matmul(H, self.W_d.t())
+        main.wait_stream(side)
+        if N:
             self._add(out, ha, self.B_d, None, None, 0)
         self._saved = (xb, xa_g, xa_u, SG, SU, H, ha)
         return out
 
     def backward(self, g: torch.Tensor) -> Tuple[torch.Tensor, Dict[str, torch.Tensor]]:
-        """(dL/dx [N, d] bf16, {dA_g, dB_g, dA_u, dB_u, dA_d, dB_d} fp32) of the last forward."""
+        """(dL/dx [N, d] bf16, {dA_g, dB_g, dA_u, dB_u, dA_d, dB_d} fp32) of the last forward. The
+        LoRA products and adapter gradients run on the side stream beside the three input-gradient
+        GEMMs; everything is ordered before the caller's stream continues."""
         if self._saved is None:
             raise RuntimeError("backward before forward")
         xb, xa_g, xa_u, SG, SU, H, ha = self._saved
@@ -116,26 +138,36 @@ class SharedExpert:
             for t in grads.values():
                 t.zero_()
             return torch.empty((0, d), dtype=torch.bfloat16, device=dev), grads
+        main, side = torch.cuda.current_stream(dev), self._side_stream(dev)
         ws = self._workspace(N, dev)
         gB = f32(N, r)                                                               # g B_d
-        self._down(gb, self.B_d, None, r, r, 0, gB, None, ws)
-        self._outer(ha, gb, True, grads["dB_d"], ws)
-        self._outer(gB, H, False, grads["dA_d"], ws)
-        Dh = torch.matmul(gb, self.W_d)                                              # [N, F] bf16
+        gg, gu = f32(N, r), f32(N, r)                                                # dSG B_g, dSU B_u
         DSG = torch.empty((N, F), dtype=torch.bfloat16, device=dev)
         DSU = torch.empty_like(DSG)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            self._down(gb, self.B_d, None, r, r, 0, gB, None, ws)
+            gB_ready = side.record_event()
+            self._outer(ha, gb, True, grads["dB_d"], ws)
+            self._outer(gB, H, False, grads["dA_d"], ws)
+        Dh = torch.matmul(gb, self.W_d)                                              # [N, F] bf16
+        main.wait_event(gB_ready)
         L.check(self.lib.ll_shared_glu_backward(Dh.data_ptr(), gB.data_ptr(), self.A_d.data_ptr(),
                                                 ctypes.c_float(s), SG.data_ptr(), SU.data_ptr(), N, F, r,
                                                 DSG.data_ptr(), DSU.data_ptr(), L.stream_ptr()),
                 "ll_shared_glu_backward")
-        gg, gu = f32(N, r), f32(N, r)                                                # dSG B_g, dSU B_u
-        self._down(DSG, self.B_g, None, r, r, 0, gg, None, ws)
-        self._down(DSU, self.B_u, None, r, r, 0, gu, None, ws)
-        self._outer(xa_g, DSG, True, grads["dB_g"], ws)
-        self._outer(gg, xb, False, grads["dA_g"], ws)
-        self._outer(xa_u, DSU, True, grads["dB_u"], ws)
-        self._outer(gu, xb, False, grads["dA_u"], ws)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            self._down(DSG, self.B_g, None, r, r, 0, gg, None, ws)
+            self._down(DSU, self.B_u, None, r, r, 0, gu, None, ws)
+            gu_ready = side.record_event()
+            self._outer(xa_g, DSG, True, grads["dB_g"], ws)
+            self._outer(gg, xb, False, grads["dA_g"], ws)
+            self._outer(xa_u, DSU, True, grads["dB_u"], ws)
+            self._outer(gu, xb, False, grads["dA_u"], ws)
         dx = torch.matmul(DSG, self.W_g)
         dx.addmm_(DSU, self.W_u)
+        main.wait_event(gu_ready)
         self._add(dx, gg, self.A_g, gu, self.A_u, 1)
+        main.wait_stream(side)
         return dx, grads
