@@ -393,10 +393,10 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   w.hg = c.take<float>((size_t)T * r);
   w.hu = c.take<float>((size_t)T * r);
   w.opart = c.take<float>((size_t)nseg_max * r * (d > f ? d : f));
-  {  // split-K partials of the skinny products: nsplit * mblocks * nblocks <= 2 * SMs +
+  {  // split-K partials of the skinny products: nsplit * mblocks * nblocks <= 4 * SMs +
      // mblocks * nblocks blocks of at most 8192 outputs (BM * NC); SMs <= 160
     const int64_t rows = P > T ? P : T;
-    w.skpart_floats = (size_t)2 * 160 * 8192 + (size_t)(rows + 256) * (2 * r + 32);
+    w.skpart_floats = (size_t)4 * 160 * 8192 + (size_t)(rows + 256) * (2 * r + 32);
     w.skpart = c.take<float>(w.skpart_floats);
   }
   if (out) *out = w;
@@ -432,8 +432,9 @@ int skinny(const void* A, int adt, bool brows, int M, int K, const float* B0, co
   const bool nc16 = N <= 16;
   const int BM = nc16 ? SkinnyCfg<16>::BM : SkinnyCfg<32>::BM, NC = nc16 ? 16 : 32;
   const int mblocks = (M + BM - 1) / BM, nblocks = (N + NC - 1) / NC;
-  // about two blocks per SM, split over K
-  int nsplit = (2 * device_info().sms + mblocks * nblocks - 1) / (mblocks * nblocks);
+  // about four blocks per SM, split over K (a block's 256 threads keep ~1 K-step in flight, so
+  // the product is occupancy-bound below that)
+  int nsplit = (4 * device_info().sms + mblocks * nblocks - 1) / (mblocks * nblocks);
   nsplit = std::max(1, std::min(nsplit, (K + kSkBK - 1) / kSkBK));
   nsplit = std::min<int64_t>(nsplit, (int64_t)(part_floats / ((size_t)M * N)));
   const int kc = ((K + nsplit - 1) / nsplit + kSkBK - 1) / kSkBK * kSkBK;

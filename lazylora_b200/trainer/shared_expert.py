@@ -59,10 +59,10 @@ class SharedExpert:
         return self._side
 
     def _workspace(self, N: int, device) -> torch.Tensor:
-        """Split-K partials of the LoRA products: 16 MB covers the splits that fill the GPU at the
+        """Split-K partials of the LoRA products: 24 MB covers the splits that fill the GPU at the
         shapes here, plus one full [N, 2r] product for a single split. Allocated on, and used only
         by, the side stream, so its memory is reused in that stream's order."""
-        need = 16 * 1024 * 1024 + 4 * N * 2 * self.r
+        need = 24 * 1024 * 1024 + 4 * N * 2 * self.r
         if self._ws is None or self._ws.numel() * 4 < need or self._ws.device != device:
             with torch.cuda.stream(self._side_stream(device)):
                 self._ws = torch.empty(need // 4, dtype=torch.float32, device=device)
