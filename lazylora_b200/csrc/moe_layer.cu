@@ -486,8 +486,9 @@ int outer(const float* Pm, const int* perm_token, const float* tw, const void* Q
           int C, int r, float sc, bool transposed, float* part, int nseg_max, float* out, cudaStream_t s) {
   if (C % 4 || r <= 0) return LL_ERR_ARG;
   const int cblocks = (C + kOuCW - 1) / kOuCW, zb = (r + kOuRB - 1) / kOuRB;
-  // about three blocks per SM; each warp gets at least one batch of rows
-  int nseg = (3 * device_info().sms + cblocks * zb - 1) / (cblocks * zb);
+  // about four blocks per SM, two waves of the two that fit (measured against 2, 3, 6 and 8);
+  // each warp gets at least one batch of rows
+  int nseg = (4 * device_info().sms + cblocks * zb - 1) / (cblocks * zb);
   nseg = std::max(1, std::min(nseg, nseg_max));
   nseg = std::min(nseg, std::max(1, N / (8 * kOuNB)));
   dim3 grid(cblocks, nseg, zb);
