@@ -565,7 +565,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   k_scatter<<<nblk, 256, kTokBlock * k * sizeof(int), s>>>(idx, w, T, k, E, W.cnt, W.perm_token, W.perm_slot,
                                                             W.pair_pos, W.tw, W.tok_pos);
   LL_TRY(check_launch("k_scatter"));
-  LL_TRY(launch_rows_to_half(x, x_dtype, W.perm_token, P, d, W.xh, W.xinv, s));
+  LL_TRY(launch_token_rows_to_half(x, x_dtype, W.perm_token, W.tok_pos, T, k, d, W.xh, W.xinv, s));
   LL_TRY(skinny(x, x_dtype, true, T, d, L->A_g, L->A_u, r, 2 * r, 1.f, W.xa_g, W.xa_u, W.skpart, W.skpart_floats, s));
   LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_g, L->B_g, nullptr, nullptr, W.dlt_g, s));
   LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_u, L->B_u, nullptr, nullptr, W.dlt_u, s));
@@ -647,7 +647,7 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
   const int* n_valid = W.offsets + E;
   g_launch_count = 0;
 
-  LL_TRY(launch_rows_to_half(g, g_dtype, W.perm_token, P, d, W.gh, W.ginv, s));
+  LL_TRY(launch_token_rows_to_half(g, g_dtype, W.perm_token, W.tok_pos, T, k, d, W.gh, W.ginv, s));
   LL_TRY(skinny(g, g_dtype, false, T, d, L->B_d, nullptr, r, r, 1.f, W.gB, nullptr, W.skpart, W.skpart_floats, s));
   // the down adapter's term of dL/dh, once per token: (g B_d) A_d [T][f]
   LL_TRY(expand(true, nullptr, nullptr, k, T, f, r, 1.f, W.gB, L->A_d, nullptr, nullptr, W.lora_d, s));

@@ -377,6 +377,94 @@ int launch_rows_to_half(const void* src, int src_dtype, const int* index, int ro
   return check_launch("k_rows_to_half");
 }
 
+// The same conversion, one block per source token: the token's row is read and its scale found
+// once, then written to each of its k pair rows (tok_pos[t * k + j], -1 for none). The pair
+// rows match k_rows_to_half_v's bit for bit; rows no token maps to are left as they are.
+template <int SRC>
+__global__ void __launch_bounds__(256) k_token_rows_to_half(const void* __restrict__ src, const int* __restrict__ tok_pos,
+                                                            int T, int k, int K, __half* __restrict__ dst,
+                                                            float* __restrict__ inv) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  const int nch = K / 8;
+  float v[4][8];
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int ch = threadIdx.x + i * blockDim.x;
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[i][j] = 0.f;
+    if (ch < nch) {
+      if (SRC == 0) {
+        const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + (int64_t)t * K) + 2 * ch;
+        const float4 a = p[0], b = p[1];
+        v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+        v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+      } else {
+        const uint4 u = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(src) + (int64_t)t * K)[ch];
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+          v[i][2 * j] = f.x;
+          v[i][2 * j + 1] = f.y;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) mx = fmaxf(mx, fabsf(v[i][j]));
+    }
+  }
+  __shared__ float red[32];
+  __shared__ float sh_scale, sh_inv;
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = 0.f;
+    for (int i = 0; i < (int)(blockDim.x / 32); i++) m = fmaxf(m, red[i]);
+    const int e = row_scale_exp(m);
+    sh_scale = ldexpf(1.f, e);
+    sh_inv = ldexpf(1.f, -e);
+  }
+  __syncthreads();
+  const float sc = sh_scale;
+  uint4 o[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    uint32_t h2[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const __half2 h = __floats2half2_rn(v[i][2 * j] * sc, v[i][2 * j + 1] * sc);
+      h2[j] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    o[i] = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+  }
+  for (int j = 0; j < k; j++) {
+    const int p = tok_pos[(int64_t)t * k + j];
+    if (p < 0) continue;
+    if (threadIdx.x == 0) inv[p] = sh_inv;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int ch = threadIdx.x + i * blockDim.x;
+      if (ch < nch) reinterpret_cast<uint4*>(dst + (int64_t)p * K)[ch] = o[i];
+    }
+  }
+}
+
+int launch_token_rows_to_half(const void* src, int src_dtype, const int* perm_token, const int* tok_pos, int T, int k,
+                              int K, __half* dst, float* inv, cudaStream_t s) {
+  if (T <= 0) return LL_OK;
+  const bool vec = K % 8 == 0 && K <= 8 * 4 * 256 && reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(dst) % 16 == 0;
+  if (!vec) return launch_rows_to_half(src, src_dtype, perm_token, T * k, K, dst, inv, s);
+  if (src_dtype == 0)
+    k_token_rows_to_half<0><<<T, 256, 0, s>>>(src, tok_pos, T, k, K, dst, inv);
+  else
+    k_token_rows_to_half<1><<<T, 256, 0, s>>>(src, tok_pos, T, k, K, dst, inv);
+  return check_launch("k_rows_to_half");
+}
+
+
 }  // namespace ll
 
 using namespace ll;

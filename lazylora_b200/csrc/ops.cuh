@@ -21,5 +21,10 @@ int launch_single_expert_chunks(Chunk* chunks, int* n_chunks, int M, int nmax, c
 // a negative index gives a zero row). src_dtype: 0 fp32, 1 bf16.
 int launch_rows_to_half(const void* src, int src_dtype, const int* index, int rows, int K, __half* dst, float* inv,
                         cudaStream_t s, int ld = -1);   // ld: dst row stride (>= K, default K)
+// The per-pair rows from the T source rows through tok_pos ([T][k] pair positions, -1 for
+// none): one read and one scale per token (falls back to the per-pair conversion through
+// perm_token for shapes the vector kernel does not take).
+int launch_token_rows_to_half(const void* src, int src_dtype, const int* perm_token, const int* tok_pos, int T, int k,
+                              int K, __half* dst, float* inv, cudaStream_t s);
 
 }  // namespace ll
