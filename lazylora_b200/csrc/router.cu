@@ -20,23 +20,41 @@ __global__ void k_route_select(const float* __restrict__ a, const float* __restr
   if (warp >= T) return;
   const int t = warp;
   float sc[PER_LANE], ch[PER_LANE];
+  if (MODE == 0) {
+    // the K-split partials of the lane's logits, added in split order; each split's PER_LANE
+    // loads are issued together (one round of latency per split, not one per element)
 #pragma unroll
-  for (int i = 0; i < PER_LANE; i++) {
-    const int e = lane + 32 * i;
-    sc[i] = 0.f;
-    ch[i] = -INFINITY;
-    if (e < E) {
-      if (MODE == 0) {
-        float logit = a[(int64_t)t * E + e];
-        for (int sp = 1; sp < nsplit; sp++) logit += a[((int64_t)sp * T + t) * E + e];
-        const float s = 1.0f / (1.0f + expf(-logit));
+    for (int i = 0; i < PER_LANE; i++) {                   // sc[] holds the logits first
+      const int e = lane + 32 * i;
+      sc[i] = e < E ? a[(int64_t)t * E + e] : 0.f;
+    }
+    for (int sp = 1; sp < nsplit; sp++) {
+      const float* ap = a + ((int64_t)sp * T + t) * E;
+#pragma unroll
+      for (int i = 0; i < PER_LANE; i++) {
+        const int e = lane + 32 * i;
+        if (e < E) sc[i] += ap[e];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PER_LANE; i++) {
+      const int e = lane + 32 * i;
+      ch[i] = -INFINITY;
+      if (e < E) {
+        const float s = 1.0f / (1.0f + expf(-sc[i]));
         sc[i] = s;
         ch[i] = bias ? s + bias[e] : s;
         if (scores_out) scores_out[(int64_t)t * E + e] = s;
       } else {
-        sc[i] = a[(int64_t)t * E + e];
-        ch[i] = b[(int64_t)t * E + e];
+        sc[i] = 0.f;
       }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < PER_LANE; i++) {
+      const int e = lane + 32 * i;
+      sc[i] = e < E ? a[(int64_t)t * E + e] : 0.f;
+      ch[i] = e < E ? b[(int64_t)t * E + e] : -INFINITY;
     }
   }
   uint64_t taken = 0;
