@@ -126,7 +126,8 @@ typedef struct {
   const float* A_d; const float* B_d;   /* down LoRA A [r,f], B [d,r] */
   /* Transposed copies for the backward, built by ll_moe_prepare into caller buffers:
    * codes of W^T ([E,d,f/2] for gate/up, [E,f,d/2] for down) and the per-element scales as
-   * fp16 multipliers with the decode bias folded in ([E,d/32,f] gate/up, [E,f/32,d] down). */
+   * fp16 multipliers with the decode bias folded in ([E,d/32,f] gate/up, [E,f/32,d] down).
+   * ll_moe_forward does not read them (they may be NULL there); ll_moe_backward needs them. */
   const uint8_t* w1t; const uint8_t* w3t; const uint8_t* w2t;
   const uint16_t* s1t; const uint16_t* s3t; const uint16_t* s2t;
   /* Valid (token, expert) pairs the next forward / backward will see, or 0: taken as T*k. Sets
@@ -138,7 +139,9 @@ typedef struct {
 /* One-time preparation per weight load (the base weights are frozen): the per-expert
  * decode bias beta (beta[e][0] gate+up, beta[e][1] down, so that every scale byte within 36
  * of the matrix maximum decodes exactly to fp16), then the transposed copies w1t..s2t that
- * L points at (beta_out must be L->beta). */
+ * L points at (beta_out must be L->beta). With all six transposed pointers NULL only beta is
+ * built: enough for ll_moe_forward; call again with the buffers set before a backward.
+ * Some but not all of them NULL is LL_ERR_ARG. */
 int ll_moe_prepare(const ll_moe_layer* L, int32_t* beta_out, void* stream);
 
 /* Bytes of each transposed copy ll_moe_prepare fills: codes (same as the packed stack) and

@@ -403,14 +403,15 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   return c.off + 256;
 }
 
-static int validate(const ll_moe_layer* L, int T, int k) {
+// The forward reads the weights as stored; only the backward needs the transposed copies.
+static int validate(const ll_moe_layer* L, int T, int k, bool backward) {
   if (!L || T <= 0 || k <= 0 || k > 32) return LL_ERR_ARG;
   if (L->d <= 0 || L->f <= 0 || L->d % 128 || L->f % 128 || L->E <= 0 || L->E > 8192) return LL_ERR_ARG;
   if (L->r <= 0 || L->r > kExMaxR) return LL_ERR_ARG;
   if (L->s13_stride < L->d / 32 || L->s13_stride % 16 || L->s2_stride < L->f / 32 || L->s2_stride % 16) return LL_ERR_ARG;
   if (!L->w1p || !L->w1s || !L->w3p || !L->w3s || !L->w2p || !L->w2s || !L->beta) return LL_ERR_ARG;
   if (!L->A_g || !L->B_g || !L->A_u || !L->B_u || !L->A_d || !L->B_d) return LL_ERR_ARG;
-  if (!L->w1t || !L->w3t || !L->w2t || !L->s1t || !L->s3t || !L->s2t) return LL_ERR_ARG;
+  if (backward && (!L->w1t || !L->w3t || !L->w2t || !L->s1t || !L->s3t || !L->s2t)) return LL_ERR_ARG;
   return LL_OK;
 }
 
@@ -524,11 +525,13 @@ size_t ll_mxfp4_transposed_bytes(int E, int R, int C, int which) {
 
 int ll_moe_prepare(const ll_moe_layer* L, int32_t* beta_out, void* stream) {
   if (!L || !beta_out || L->E <= 0 || L->d <= 0 || L->f <= 0 || L->d % 128 || L->f % 128) return LL_ERR_ARG;
-  if (!L->w1t || !L->w3t || !L->w2t || !L->s1t || !L->s3t || !L->s2t) return LL_ERR_ARG;
+  const int n_t = !!L->w1t + !!L->w3t + !!L->w2t + !!L->s1t + !!L->s3t + !!L->s2t;
+  if (n_t != 0 && n_t != 6) return LL_ERR_ARG;
   LL_STREAM(stream);
   const int E = L->E, d = L->d, f = L->f;
   LL_TRY(launch_prepare_beta(L->w1s, L->w3s, E, f, d, L->s13_stride, beta_out, 0, s));
   LL_TRY(launch_prepare_beta(L->w2s, nullptr, E, d, f, L->s2_stride, beta_out, 1, s));
+  if (n_t == 0) return LL_OK;                 // forward-only use: no transposed copies
   auto cw = [](const uint8_t* p) { return const_cast<uint8_t*>(p); };
   auto ch = [](const uint16_t* p) { return reinterpret_cast<__half*>(const_cast<uint16_t*>(p)); };
   LL_TRY(launch_transpose_mxfp4(L->w1p, L->w1s, L->s13_stride, E, f, d, beta_out, 0, cw(L->w1t), ch(L->s1t), s));
@@ -544,7 +547,7 @@ size_t ll_moe_workspace_bytes(const ll_moe_layer* L, int T, int k) {
 
 int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dtype, const int64_t* idx, const float* w,
                    float* out, void* ws, size_t ws_bytes, void* stream) {
-  LL_TRY(validate(L, T, k));
+  LL_TRY(validate(L, T, k, false));
   if (!x || !idx || !w || !out || !ws || (x_dtype != 0 && x_dtype != 1)) return LL_ERR_ARG;
   LL_TRY(check_arch());
   if (ws_bytes < ll_moe_workspace_bytes(L, T, k)) return LL_ERR_WORKSPACE;
@@ -632,7 +635,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
 int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dtype, const int64_t* idx, const float* w,
                     const void* g, int g_dtype, float* grad_h, float* grad_w, float* dA_g, float* dB_g, float* dA_u,
                     float* dB_u, float* dA_d, float* dB_d, void* ws, size_t ws_bytes, void* stream) {
-  LL_TRY(validate(L, T, k));
+  LL_TRY(validate(L, T, k, true));
   if (!x || !idx || !w || !g || !grad_h || !grad_w || !ws) return LL_ERR_ARG;
   if (!dA_g || !dB_g || !dA_u || !dB_u || !dA_d || !dB_d) return LL_ERR_ARG;
   if ((x_dtype != 0 && x_dtype != 1) || (g_dtype != 0 && g_dtype != 1)) return LL_ERR_ARG;

@@ -13,8 +13,10 @@ known once the router ran (its sort_by_disk_order, :286-304, orders the reads). 
     ascending id order, i.e. disk order for a packed checkpoint) into groups and copies
     group i + 1 host -> HBM on a copy stream (one cudaMemcpyAsync per contiguous run of
     experts per stack, at PCIe speed) while the caller computes on group i; each group is
-    handed out as a RoutedExpertsLayer over the staged stacks (ll_moe_prepare runs on the
-    compute stream once the copy event fired). Two staging slots bound the HBM held.
+    handed out as a RoutedExpertsLayer over the staged stacks (the decode bias is computed on
+    the compute stream once the copy event fired; the transposed copy the backward reads is
+    built only for a group that runs a backward, into buffers each staging slot keeps). Two
+    staging slots bound the HBM held.
     `prefetch(next_layer, ids)` lets the copy engine start the next layer's first group
     during the current layer's last group when the next expert set is known (all experts
     when every expert is active, the forward's set during the backward), so the copies
@@ -115,6 +117,7 @@ class ExpertStreamer:
         self.copy_stream = torch.cuda.Stream(device=self.device)
         self.n_slots = slots
         self._slots: List[Optional[Dict[str, torch.Tensor]]] = [None] * slots
+        self._tslots: List[Optional[Dict[str, torch.Tensor]]] = [None] * slots
         self._slot_free: List[Optional[torch.cuda.Event]] = [None] * slots
         self._rot = 0                 # next staging slot
         self._hint = None             # (layer, ids) streamed next, see prefetch
@@ -129,6 +132,19 @@ class ExpertStreamer:
             s = {n: torch.empty(shapes[n], dtype=L[n].dtype, device=self.device) for n in STACKS}
             self._slots[i] = s
         return s
+
+    def _tslot(self, i: int, layer_idx: int) -> Dict[str, torch.Tensor]:
+        """The transposed-copy buffers of staging slot i, sized for a full group: allocated
+        the first time a group in that slot runs a backward, reused by every later group."""
+        _, f, dh = self.store.layers[layer_idx]["w1p"].shape
+        d, G, u8, f16 = 2 * dh, self.group, torch.uint8, torch.float16
+        want = {"w1t": ((G, d, f // 2), u8), "w3t": ((G, d, f // 2), u8), "w2t": ((G, f, d // 2), u8),
+                "s1t": ((G, d // 32, f), f16), "s3t": ((G, d // 32, f), f16), "s2t": ((G, f // 32, d), f16)}
+        t = self._tslots[i]
+        if t is None or any(tuple(t[n].shape) != want[n][0] or t[n].dtype != want[n][1] for n in want):
+            t = {n: torch.empty(shape, dtype=dt, device=self.device) for n, (shape, dt) in want.items()}
+            self._tslots[i] = t
+        return t
 
     def _copy_group(self, layer_idx: int, ids: List[int], slot: int) -> torch.cuda.Event:
         L = self.store.layers[layer_idx]
@@ -179,9 +195,12 @@ class ExpertStreamer:
             st = self._slots[slot]
             n = len(g)
             lo = self.lora
+            # the transposed copy is built only if this group runs a backward, into the slot's
+            # persistent buffers (no allocation per group)
             layer = RoutedExpertsLayer(st["w1p"][:n], st["w1s"][:n], st["w3p"][:n], st["w3s"][:n], st["w2p"][:n],
                                        st["w2s"][:n], lo["A_g"], lo["B_g"], lo["A_u"], lo["B_u"], lo["A_d"],
-                                       lo["B_d"], self.scaling)
+                                       lo["B_d"], self.scaling, prepare_backward=False,
+                                       transposed=lambda sl=slot, li=layer_idx: self._tslot(sl, li))
             yield g, layer
             done = torch.cuda.Event()
             done.record(cur)

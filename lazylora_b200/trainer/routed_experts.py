@@ -34,10 +34,20 @@ def _pad_scale_rows(s: torch.Tensor) -> torch.Tensor:
     return out
 
 
-class RoutedExpertsLayer:
-    """Expert weights + shared LoRA of one layer, resident on one GPU."""
+TRANSPOSED = ("w1t", "w3t", "w2t", "s1t", "s3t", "s2t")
 
-    def __init__(self, w1p, w1s, w3p, w3s, w2p, w2s, A_g, B_g, A_u, B_u, A_d, B_d, lora_scaling: float):
+
+class RoutedExpertsLayer:
+    """Expert weights + shared LoRA of one layer, resident on one GPU.
+
+    The backward reads transposed copies of the weights, built once per weight load.
+    prepare_backward=False defers that build to the first backward (a forward-only user never
+    pays it); `transposed` supplies the buffers for it: a dict of the six tensors (or a
+    callable returning one) whose leading dimension is at least E, e.g. one set per staging
+    slot of a streamer, reused by every group copied into that slot."""
+
+    def __init__(self, w1p, w1s, w3p, w3s, w2p, w2s, A_g, B_g, A_u, B_u, A_d, B_d, lora_scaling: float,
+                 transposed=None, prepare_backward: bool = True):
         L.require_cuda(w1p, w1s, w3p, w3s, w2p, w2s, A_g, B_g, A_u, B_u, A_d, B_d)
         self.lib = L.load()
         E, f, dh = w1p.shape
@@ -52,19 +62,42 @@ class RoutedExpertsLayer:
         self.A_u, self.B_u = A_u.float().contiguous(), B_u.float().contiguous()
         self.A_d, self.B_d = A_d.float().contiguous(), B_d.float().contiguous()
         self.beta = torch.zeros((E, 2), dtype=torch.int32, device=w1p.device)
-        # transposed copies the backward GEMMs read (built once by ll_moe_prepare)
-        dev = w1p.device
-        self.w1t = torch.empty((E, d, f // 2), dtype=torch.uint8, device=dev)
-        self.w3t = torch.empty((E, d, f // 2), dtype=torch.uint8, device=dev)
-        self.w2t = torch.empty((E, f, d // 2), dtype=torch.uint8, device=dev)
-        self.s1t = torch.empty((E, d // 32, f), dtype=torch.float16, device=dev)
-        self.s3t = torch.empty((E, d // 32, f), dtype=torch.float16, device=dev)
-        self.s2t = torch.empty((E, f // 32, d), dtype=torch.float16, device=dev)
+        self.w1t = self.w3t = self.w2t = self.s1t = self.s3t = self.s2t = None
+        self._tbufs = transposed
         self.desc = L.MoELayerDesc()
         self._fill_desc()
+        # the decode bias alone (the forward needs nothing else)
         L.check(self.lib.ll_moe_prepare(ctypes.byref(self.desc), self.beta.data_ptr(), L.stream_ptr()), "ll_moe_prepare")
         self._ws: Optional[torch.Tensor] = None
         self._ws_key = None
+        if prepare_backward:
+            self.prepare_backward()
+
+    def transposed_shapes(self) -> Dict[str, tuple]:
+        """(shape, dtype) of the six transposed copies the backward reads."""
+        E, d, f = self.E, self.d, self.f
+        u8, f16 = torch.uint8, torch.float16
+        return {"w1t": ((E, d, f // 2), u8), "w3t": ((E, d, f // 2), u8), "w2t": ((E, f, d // 2), u8),
+                "s1t": ((E, d // 32, f), f16), "s3t": ((E, d // 32, f), f16), "s2t": ((E, f // 32, d), f16)}
+
+    def prepare_backward(self):
+        """Build the transposed weight copies the backward GEMMs read (once per weight load)."""
+        if self.w1t is not None:
+            return
+        bufs = self._tbufs() if callable(self._tbufs) else self._tbufs
+        dev = self.w1p.device
+        for name, (shape, dt) in self.transposed_shapes().items():
+            if bufs is None:
+                t = torch.empty(shape, dtype=dt, device=dev)
+            else:
+                b = bufs[name]
+                if b.dtype != dt or b.device != dev or b.shape[0] < shape[0] or tuple(b.shape[1:]) != shape[1:]:
+                    raise ValueError(f"transposed buffer {name}: need {shape} {dt} on {dev}, got "
+                                     f"{tuple(b.shape)} {b.dtype} on {b.device}")
+                t = b[:shape[0]]
+            setattr(self, name, t)
+        self._fill_desc()
+        L.check(self.lib.ll_moe_prepare(ctypes.byref(self.desc), self.beta.data_ptr(), L.stream_ptr()), "ll_moe_prepare")
 
     @classmethod
     def from_inputs(cls, inp: Dict[str, torch.Tensor], lora_scaling: float, device="cuda"):
@@ -82,8 +115,9 @@ class RoutedExpertsLayer:
         D.beta = self.beta.data_ptr()
         D.A_g, D.B_g, D.A_u, D.B_u = self.A_g.data_ptr(), self.B_g.data_ptr(), self.A_u.data_ptr(), self.B_u.data_ptr()
         D.A_d, D.B_d = self.A_d.data_ptr(), self.B_d.data_ptr()
-        D.w1t, D.w3t, D.w2t = self.w1t.data_ptr(), self.w3t.data_ptr(), self.w2t.data_ptr()
-        D.s1t, D.s3t, D.s2t = self.s1t.data_ptr(), self.s3t.data_ptr(), self.s2t.data_ptr()
+        for name in TRANSPOSED:
+            t = getattr(self, name)
+            setattr(D, name, t.data_ptr() if t is not None else 0)
 
     def set_lora(self, A_g, B_g, A_u, B_u, A_d, B_d):
         """Point the layer at (updated) adapter tensors, e.g. after an optimizer step."""
@@ -147,6 +181,7 @@ class RoutedExpertsLayer:
             forward_done = self._ws_key == key
         if not forward_done:        # the workspace does not hold this forward: recompute it
             self.forward(x, idx, w)
+        self.prepare_backward()
         ws = self.workspace(T, k)
         dev = x.device
         grad_h = torch.empty((T, self.d), dtype=torch.float32, device=dev)

@@ -7,9 +7,10 @@ GPU parity of the routed-expert layer (forward + manual backward) through the C 
     stable (expert, token) permutation bit-exact;
   * edge cases the reference's loop handles: experts with no tokens, an expert with more
     tokens than one MMA tile takes, slots routed elsewhere (-1), a single token;
-  * the full-width configuration (d=7168, f=2048, E=896, k=8, T=1024) through
-    size-independent properties: token independence (outputs of a token subset against
-    the oracle run on that subset alone), and bitwise determinism across runs.
+  * the full-width configurations (d=7168, f=2048, E=896, k=8; T=1024 for configs[1] and
+    T=8192 for configs[2]'s single-GPU shape) through size-independent properties: token
+    independence (outputs of a token subset against the oracle run on that subset alone),
+    and bitwise determinism across runs.
 """
 import dataclasses
 import os
@@ -125,11 +126,10 @@ def test_expert_over_tile_width():
         assert O.rel_l2(got[key].cpu(), want[key]) <= TOL, key
 
 
-@pytest.fixture(scope="module")
-def c1_layer():
+def _full_width_layer(name):
     from lazylora_b200.trainer.routed_experts import RoutedExpertsLayer
     from lazylora_b200.core.moe_router import KimiK3MoERouter
-    cfg = CONFIGS["c1"]
+    cfg = CONFIGS[name]
     inp = make_layer_device(cfg)
     layer = RoutedExpertsLayer.from_inputs(inp, cfg.scaling)
     router = KimiK3MoERouter(hidden_size=cfg.d, num_experts=cfg.E, top_k=cfg.k)
@@ -138,29 +138,57 @@ def c1_layer():
     return cfg, inp, layer, x, idx, w
 
 
-def test_full_width_token_subset(c1_layer):
-    cfg, inp, layer, x, idx, w = c1_layer
+@pytest.fixture(scope="module")
+def c1_layer():
+    return _full_width_layer("c1")
+
+
+def _token_subset_vs_oracle(cfg, inp, layer, x, idx, w, tokens):
+    """Token independence: the layer's outputs for `tokens` (run inside the full batch) against
+    the oracle run on those tokens alone, over only the experts they touch; the LoRA gradients
+    of the full-batch run with the upstream gradient zeroed outside `tokens`. Returns the
+    number of experts the tokens touch."""
     g = inp["g"].to(torch.bfloat16)
     got = _run(layer, x, idx, w, g)
-    tokens = torch.tensor([0, 517, 1023])
-    sub = idx[tokens].cpu()
+    tk = tokens.to(idx.device)
+    sub = idx[tk].cpu()
     experts = sorted(set(sub.flatten().tolist()))
-    # oracle on the subset: only the experts those tokens use, remapped to 0..n-1
     remap = {e: i for i, e in enumerate(experts)}
     ev = torch.tensor(experts, device=idx.device)
     cpu = {key: inp[key][ev].cpu() for key in ("w1p", "w1s", "w3p", "w3s", "w2p", "w2s")}
     cpu.update({key: inp[key].cpu() for key in ("A_g", "B_g", "A_u", "B_u", "A_d", "B_d")})
-    cpu["x"] = x[tokens].float().cpu()
+    cpu["x"] = x[tk].float().cpu()
     sub_idx = sub.clone().apply_(lambda e: remap[e])
-    # restrict the LoRA gradients to the subset: zero upstream gradient elsewhere
     g_sub = torch.zeros_like(g)
-    g_sub[tokens.cuda()] = g[tokens.cuda()]
+    g_sub[tk] = g[tk]
     got_sub = _run(layer, x, idx, w, g_sub)
-    want = _oracle(cpu, sub_idx, w[tokens].cpu(), g[tokens].float().cpu(), cfg.scaling)
+    want = _oracle(cpu, sub_idx, w[tk].cpu(), g[tk].float().cpu(), cfg.scaling)
     for key in ("out", "grad_h", "grad_w"):
-        assert O.rel_l2(got[key][tokens.cuda()].cpu(), want[key]) <= TOL, key
+        err = O.rel_l2(got[key][tk].cpu(), want[key])
+        assert err <= TOL, f"{key}: rel-L2 {err:.3e}"
     for key in ("dA_g", "dB_g", "dA_u", "dB_u", "dA_d", "dB_d"):
-        assert O.rel_l2(got_sub[key].cpu(), want[key]) <= TOL, key
+        err = O.rel_l2(got_sub[key].cpu(), want[key])
+        assert err <= TOL, f"{key}: rel-L2 {err:.3e}"
+    return len(experts)
+
+
+def test_full_width_token_subset(c1_layer):
+    """configs[1] (896 experts, 16-row token tiles): 64 tokens spread over the batch, which
+    touch a few hundred experts, against the oracle."""
+    cfg, inp, layer, x, idx, w = c1_layer
+    tokens = torch.linspace(0, cfg.T - 1, 64).round().long()
+    n_exp = _token_subset_vs_oracle(cfg, inp, layer, x, idx, w, tokens)
+    assert n_exp >= 200, n_exp
+
+
+def test_configs2_shape_token_subset():
+    """configs[2]'s single-GPU shape (T = 8192, about 73 rows per expert: the 128-row token
+    tiles, experts split over two chunks): 24 tokens spread over the batch against the oracle."""
+    cfg, inp, layer, x, idx, w = _full_width_layer("c2")
+    tokens = torch.linspace(0, cfg.T - 1, 24).round().long()
+    _token_subset_vs_oracle(cfg, inp, layer, x, idx, w, tokens)
+    del layer, inp
+    torch.cuda.empty_cache()
 
 
 def test_full_width_deterministic(c1_layer):

@@ -1,9 +1,20 @@
 """
-GPU checks of expert streaming (pinned host memory -> HBM, group by group): a layer run
-through ExpertStreamer gives the resident layer's results (up to the fp32 order in which
-the groups' partial sums are added), for every group size including ragged last groups and
-an active set with gaps; the reference-interface generator yields the right bytes.
+GPU checks of expert streaming (pinned host memory -> HBM, group by group):
+
+  * the streamed layer against the reference's own outputs (tests/golden/ref_<case>.npz,
+    made by LazyLoRATrainer._routed_experts_forward / _backward, whose expert loop is fed by
+    DynamicExpertStreamer.stream_experts, lazy_lora/streaming/expert_streamer.py:315-369):
+    out, grad_h, grad_w and the six LoRA gradients within relative L2 2e-3, for group sizes
+    that split the active set evenly, raggedly and one expert at a time;
+  * the streamed layer against the resident layer (the same kernels; only the fp32 order in
+    which the groups' partial sums are added differs), including an active set with gaps;
+  * the reference-interface generator yields the right bytes; forward-only streaming never
+    builds the backward's transposed copy, and backward groups reuse one set of transposed
+    buffers per staging slot.
 """
+import os
+
+import numpy as np
 import pytest
 import torch
 
@@ -28,6 +39,31 @@ def _setup(case):
         x, g = x.to(torch.bfloat16), g.to(torch.bfloat16)
     idx, w = O.route(inp["x"].float(), inp["router_w"], inp["router_b"], cfg.k)
     return cfg, inp, store, lora, resident, x, g, idx.cuda(), w.cuda(), ExpertStreamer
+
+
+KEYS = ("out", "grad_h", "grad_w", "dA_g", "dB_g", "dA_u", "dB_u", "dA_d", "dB_d")
+
+
+@pytest.mark.parametrize("case,group", [("small", 16), ("small", 5), ("small", 1), ("c0", 6), ("k3", 7)])
+def test_streamed_layer_matches_reference_goldens(golden_dir, case, group):
+    from lazylora_b200.trainer.expert_streamer import streamed_backward, streamed_forward
+    fx = np.load(os.path.join(golden_dir, f"ref_{case}.npz"))
+    cfg, inp, store, lora, resident, x, g, _idx, _w, ES = _setup(case)
+    idx = torch.from_numpy(fx["idx"]).cuda()
+    w = torch.from_numpy(fx["w"]).cuda()
+    streamer = ES(store, lora, cfg.scaling, group_experts=group)
+    out, ids = streamed_forward(streamer, 0, x, idx, w)
+    assert all(t is None for t in streamer._tslots), "forward-only streaming built a transposed copy"
+    gh, gw, grads = streamed_backward(streamer, 0, x, idx, w, g, ids)
+    got = {"out": out, "grad_h": gh, "grad_w": gw, **grads}
+    for key in KEYS:
+        err = O.rel_l2(got[key].float().cpu(), torch.from_numpy(fx[key]))
+        assert err <= 2e-3, f"{case} group {group}: {key} rel-L2 {err:.3e}"
+    # a second backward pass re-streams into the same slots and reuses their transposed buffers
+    bufs = [None if t is None else {n: v.data_ptr() for n, v in t.items()} for t in streamer._tslots]
+    gh2, _, _ = streamed_backward(streamer, 0, x, idx, w, g, ids)
+    assert torch.equal(gh2, gh)
+    assert bufs == [None if t is None else {n: v.data_ptr() for n, v in t.items()} for t in streamer._tslots]
 
 
 @pytest.mark.parametrize("case,group", [("small", 16), ("small", 5), ("small", 3), ("c0", 6)])
