@@ -42,10 +42,12 @@ REF_SO = os.path.join(HERE, "_ref", "libmxfp4_ref.so")
 REF_K_CHUNK = 3584          # largest K the reference's stack tile takes, multiple of 32
 
 
-def build() -> None:
-    """Compile the checkers (oracle/_build, and oracle/_ref when the reference tree exists)."""
+def build(ref_root: Optional[str] = None) -> None:
+    """Compile the checkers: oracle/_build always, and oracle/_ref from the reference tree at
+    `ref_root` (default: the LAZYLORA_REFERENCE_ROOT environment variable) when it exists."""
     import subprocess
-    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    ref_root = ref_root or os.environ.get("LAZYLORA_REFERENCE_ROOT", "")
+    subprocess.run(["make", "-s", "-C", HERE, f"REF_ROOT={ref_root}"], check=True)
 
 
 class MXFP4Checker:

@@ -20,7 +20,7 @@ import torch.nn.functional as F
 from lazylora_b200.synthetic import CONFIGS, make_layer
 from oracle import moe_oracle as O
 
-HAVE_REF = os.path.exists(O.REF_SO) or os.path.isdir("/root/reference/lazy_lora")
+HAVE_REF = os.path.exists(O.REF_SO)
 
 
 def _npz(golden_dir, name):
@@ -102,30 +102,66 @@ def test_situ_glu_fixture(golden_dir):
     _matches(got.numpy(), fx["out"])
 
 
-def test_moe_block_fixture(golden_dir):
-    """The latent MoE block (test_reference_ops.py:259-309): router + per-expert SiTU-GLU + combine."""
-    fx = _npz(golden_dir, "fx_moe.npz")
+def _fx_moe_parts(fx):
     t = lambda k: torch.from_numpy(fx[k])
-    x = t("in")
+    E = int(fx["n_experts"])
+    experts = {e: (t(f"experts_{e}_w1_weight"), t(f"experts_{e}_w3_weight"), t(f"experts_{e}_w2_weight"))
+               for e in range(E)}
+    return t, experts
+
+
+def test_moe_block_fixture(golden_dir):
+    """The MoE block of test_reference_ops.py:259-309 through the oracles' own compositions:
+    shared_oracle.shared_expert (no LoRA) plus latent_oracle.latent_block_with (down-projection,
+    the fixture's fp32 experts, RMSNorm of their sum, up-projection), routed by moe_oracle.route."""
+    from oracle import latent_oracle as LO
+    from oracle import shared_oracle as SO
+    fx = _npz(golden_dir, "fx_moe.npz")
+    t, experts = _fx_moe_parts(fx)
     hidden = int(fx["hidden"])
-    s_act = O.situ_glu_forward(F.linear(x, t("shared_w1_weight")), F.linear(x, t("shared_w3_weight")),
-                               float(fx["situ_b1"]), float(fx["situ_b2"]))
-    shared = F.linear(s_act, t("shared_w2_weight"))
+    x = t("in").reshape(-1, hidden)
+    b1, b2 = float(fx["situ_b1"]), float(fx["situ_b2"])
+    assert (b1, b2) == (O.SITU_BETA, O.SITU_LINEAR_BETA)      # shared_oracle's SiTU-GLU constants
+    F_s = t("shared_w1_weight").shape[0]
+    zero_lora = {"A_g": torch.zeros(1, hidden), "B_g": torch.zeros(F_s, 1), "A_u": torch.zeros(1, hidden),
+                 "B_u": torch.zeros(F_s, 1), "A_d": torch.zeros(1, F_s), "B_d": torch.zeros(hidden, 1)}
+    shared = SO.shared_expert(x, t("shared_w1_weight"), t("shared_w3_weight"), t("shared_w2_weight"), zero_lora,
+                              1.0)["out"]
     idx, w = O.route(x, t("gate_weight"), t("e_score_correction_bias"), int(fx["top_k"]),
                      routed_scaling_factor=float(fx["routed_scale"]))
-    h = F.linear(x.reshape(-1, hidden), t("down_weight"))
-    routed = torch.zeros_like(h)
-    for e in O.active_experts(idx):
-        mask = idx == e
-        rows = mask.any(-1).nonzero().squeeze(-1)
-        xe = h.index_select(0, rows)
-        act = O.situ_glu_forward(F.linear(xe, t(f"experts_{e}_w1_weight")), F.linear(xe, t(f"experts_{e}_w3_weight")),
-                                 float(fx["situ_b1"]), float(fx["situ_b2"]))
-        tw = (w.index_select(0, rows) * mask.index_select(0, rows).float()).sum(-1, keepdim=True)
-        routed.index_add_(0, rows, F.linear(act, t(f"experts_{e}_w2_weight")) * tw)
-    routed = routed * torch.rsqrt(routed.pow(2).mean(-1, keepdim=True) + float(fx["rms_eps"])) * t("norm_weight")
-    got = shared + F.linear(routed, t("up_weight")).view_as(shared)
-    _matches(got.numpy(), fx["out"], abs_tol=2e-4)
+    blk = LO.latent_block_with(lambda h, i, ww: LO.dense_experts_forward(h, i, ww, experts, b1, b2), None,
+                               x, t("down_weight"), t("up_weight"), t("norm_weight"), idx, w,
+                               eps=float(fx["rms_eps"]))
+    got = shared + blk["out"]
+    _matches(got.numpy(), fx["out"].reshape(got.shape), abs_tol=2e-4)
+
+
+def test_latent_block_backward_composition(golden_dir):
+    """latent_oracle's manual backward chain (up-projection grad, RMSNorm and cast by autograd,
+    the experts' own backward, down-projection grad) equals autograd of its forward, on the
+    fixture's block with a seeded upstream gradient: pins the composition the GPU latent block
+    is checked against."""
+    from oracle import latent_oracle as LO
+    fx = _npz(golden_dir, "fx_moe.npz")
+    t, experts = _fx_moe_parts(fx)
+    hidden = int(fx["hidden"])
+    gen = torch.Generator().manual_seed(3)
+    x = torch.randn(16, hidden, generator=gen)
+    g = torch.randn(16, hidden, generator=gen)
+    idx, w = O.route(x, t("gate_weight"), t("e_score_correction_bias"), int(fx["top_k"]))
+    down_w, up_w, norm_w, eps = t("down_weight"), t("up_weight"), t("norm_weight"), float(fx["rms_eps"])
+    res = LO.latent_block_with(lambda h, i, ww: LO.dense_experts_forward(h, i, ww, experts),
+                               lambda h, i, ww, gg: LO.dense_experts_backward(h, i, ww, gg, experts),
+                               x, down_w, up_w, norm_w, idx, w, grad_out=g, eps=eps)
+    xr = x.clone().requires_grad_(True)
+    wr = w.clone().requires_grad_(True)
+    h = F.linear(xr, down_w)
+    routed = LO.dense_experts_forward(h, idx, wr, experts)
+    out = F.linear(routed * torch.rsqrt(routed.pow(2).mean(-1, keepdim=True) + eps) * norm_w, up_w)
+    assert O.rel_l2(res["out"], out.detach()) < 1e-6
+    gx, gw = torch.autograd.grad(out, (xr, wr), g)
+    assert O.rel_l2(res["grad_x"], gx) < 1e-5
+    assert O.rel_l2(res["grad_w"], gw) < 1e-5
 
 
 GOLDEN_KEYS = ("out", "grad_h", "grad_w", "dA_g", "dB_g", "dA_u", "dB_u", "dA_d", "dB_d")
