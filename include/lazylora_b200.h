@@ -61,9 +61,13 @@ int ll_mxfp4_gemm(float* y, const float* x, const uint8_t* packed, const uint8_t
  * allocator, or code running where allocation is not allowed). Its scratch is a static
  * device array of LL_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps until
  * exit; M * K must fit it (about M * K * 2 + M * 4 bytes, 8 MiB: e.g. M <= 580 at K = 7168),
- * larger sizes return LL_ERR_WORKSPACE. The first call on a device looks up the array's
- * device address (make it before any stream capture). All calls share the array: calls
- * that overlap on the GPU race and must be serialised by the caller. Allocates nothing. */
+ * larger sizes return LL_ERR_WORKSPACE. scale_stride must be >= K/32 and a multiple of 16
+ * (such a caller pads its scale rows itself; K a multiple of 512 needs no padding). The
+ * first call on a device looks up the array's device address (make it before any stream
+ * capture; it is looked up again if the device's context was recreated, e.g. after
+ * cudaDeviceReset). The call returns once its GPU work finished (it reads the device status
+ * word back). All calls share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller. Allocates nothing. */
 #define LL_NOALLOC_SCRATCH_BYTES (8u << 20)
 int ll_mxfp4_gemm_noalloc(float* y, const float* x, const uint8_t* packed, const uint8_t* scales,
                           int M, int K, int R, int64_t scale_stride, void* stream);
@@ -219,11 +223,12 @@ int ll_ep_combine_slots(float* grad_w, const float* part, const int* pos, const 
 /* ------------------------------------------------------------- checkpoint reads
  * Reads n byte ranges of files into host buffers (pinned, when they feed host-to-device
  * copies) with `threads` worker threads: range i is [offsets[i], offsets[i] + sizes[i]) of
- * paths[i] into dsts[i]. Short reads continue; a transient EIO is retried up to `retries`
- * times, sleeping retry_ms * attempt and reopening the file, the policy of the reference's
- * MmapTensorStreamer._read_range (mmap_loader.py:260-294). On failure returns LL_ERR_IO with
- * the first failing range in *failed_index and the reason in ll_last_cuda_error(); the bytes
- * read are counted in *bytes_done. No CUDA call is made. */
+ * paths[i] into dsts[i]. Short reads continue; a transient EIO (from the open or a read) is
+ * retried up to `retries` times per range, sleeping retry_ms * attempt and reopening the file,
+ * the policy of the reference's MmapTensorStreamer._read_range (mmap_loader.py:260-294). On
+ * failure returns LL_ERR_IO with the lowest failing range index in *failed_index and the
+ * reason in ll_last_cuda_error(); the bytes read are counted in *bytes_done. No CUDA call is
+ * made. */
 int ll_pread_batch(int n, const char* const* paths, const int64_t* offsets, const int64_t* sizes, void* const* dsts,
                    int threads, int retries, int retry_ms, int64_t* bytes_done, int* failed_index);
 

@@ -5,8 +5,9 @@
 // (lazy_lora/streaming/mmap_loader.py:260-294), one tensor at a time. Here a batch of ranges
 // (all six tensors of every expert of a layer, say) is split over worker threads; each range is
 // read with pread in a loop until complete (short reads continue where they stopped), with
-// the same EIO policy per range: up to `retries` retries, sleeping retry_ms * attempt between
-// them, reopening the file each time. No CUDA call is made: the buffers are plain host memory
+// the same EIO policy per range (its open included): up to `retries` retries, sleeping
+// retry_ms * attempt between them, reopening the file each time. On failure the lowest
+// failing range index is reported. No CUDA call is made: the buffers are plain host memory
 // (pinned, when they feed host-to-device copies).
 #include <fcntl.h>
 #include <unistd.h>
@@ -16,6 +17,7 @@
 #include <chrono>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <vector>
@@ -30,13 +32,30 @@ struct Range {
   uint8_t* dst;
 };
 
+// Opens r.path for reading; a transient EIO is retried like one from pread (sleep
+// retry_ms * attempt, up to `retries` attempts shared with the reads of the same range).
+int open_retry(const Range& r, int retries, int retry_ms, int* attempts, int* fd_out) {
+  for (;;) {
+    const int fd = open(r.path, O_RDONLY | O_CLOEXEC);
+    if (fd >= 0) {
+      *fd_out = fd;
+      return 0;
+    }
+    const int e = errno ? errno : EIO;
+    if (e == EINTR) continue;
+    if (e != EIO || *attempts >= retries) return e;
+    ++*attempts;
+    std::this_thread::sleep_for(std::chrono::milliseconds((int64_t)retry_ms * *attempts));
+  }
+}
+
 // 0 on success, else an errno value (or -1 for an unexpected end of file).
 int read_range(const Range& r, int retries, int retry_ms, int64_t* done) {
-  int fd = open(r.path, O_RDONLY | O_CLOEXEC);
-  if (fd < 0) return errno ? errno : EIO;
-  int64_t got = 0;
   int attempts = 0;
-  int rc = 0;
+  int fd = -1;
+  int rc = open_retry(r, retries, retry_ms, &attempts, &fd);
+  if (rc != 0) return rc;
+  int64_t got = 0;
   while (got < r.size) {
     const ssize_t n = pread(fd, r.dst + got, (size_t)(r.size - got), (off_t)(r.offset + got));
     if (n > 0) {
@@ -55,12 +74,8 @@ int read_range(const Range& r, int retries, int retry_ms, int64_t* done) {
     ++attempts;                                     // transient EIO: wait, reopen, retry
     std::this_thread::sleep_for(std::chrono::milliseconds((int64_t)retry_ms * attempts));
     close(fd);
-    fd = open(r.path, O_RDONLY | O_CLOEXEC);
-    if (fd < 0) {
-      rc = errno ? errno : EIO;
-      fd = -1;
-      break;
-    }
+    fd = -1;
+    if ((rc = open_retry(r, retries, retry_ms, &attempts, &fd)) != 0) break;
   }
   if (fd >= 0) close(fd);
   *done += got;
@@ -85,18 +100,24 @@ int ll_pread_batch(int n, const char* const* paths, const int64_t* offsets, cons
     ranges[(size_t)i] = Range{paths[i], offsets[i], sizes[i], static_cast<uint8_t*>(dsts[i])};
   }
   const int nt = threads < 1 ? 1 : (threads > 64 ? 64 : (threads > n ? n : threads));
+  // Ranges are handed out in index order and a worker finishes the range it holds, so once a
+  // failure stops the batch every lower index has been read or has failed too: the lowest
+  // failing index is the one reported, the same from run to run.
   std::atomic<int> next{0};
-  std::atomic<int> first_bad{-1};
-  std::atomic<int> first_err{0};
+  std::atomic<bool> stop{false};
+  std::mutex bad_mu;
+  int bad = -1, bad_err = 0;
   std::vector<int64_t> done((size_t)nt, 0);
   auto worker = [&](int t) {
     for (;;) {
+      if (stop.load()) return;
       const int i = next.fetch_add(1);
-      if (i >= n || first_bad.load() >= 0) return;
+      if (i >= n) return;
       const int rc = read_range(ranges[(size_t)i], retries, retry_ms, &done[(size_t)t]);
       if (rc != 0) {
-        int expect = -1;
-        if (first_bad.compare_exchange_strong(expect, i)) first_err.store(rc);
+        std::lock_guard<std::mutex> lock(bad_mu);
+        if (bad < 0 || i < bad) { bad = i; bad_err = rc; }
+        stop.store(true);
         return;
       }
     }
@@ -108,10 +129,9 @@ int ll_pread_batch(int n, const char* const* paths, const int64_t* offsets, cons
   int64_t total = 0;
   for (int64_t d : done) total += d;
   if (bytes_done) *bytes_done = total;
-  const int bad = first_bad.load();
   if (bad >= 0) {
     if (failed_index) *failed_index = bad;
-    const int e = first_err.load();
+    const int e = bad_err;
     snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "read of %s [%lld, +%lld) failed: %s",
              ranges[(size_t)bad].path, (long long)ranges[(size_t)bad].offset, (long long)ranges[(size_t)bad].size,
              e == -1 ? "file ends before the range" : strerror(e));

@@ -10,8 +10,10 @@
 //
 // In host code the array's name is only a host-side handle, not a device address, so the
 // address passed to the kernels comes from cudaGetSymbolAddress, looked up once per device
-// (with that device current) on the entry point's first call there. Make that first call
-// before any stream capture.
+// (with that device current) on the entry point's first call there, and again if that
+// device's context was created anew since (after cudaDeviceReset). Make the first call on a
+// device before any stream capture. A call returns after its GPU work finished: it reads the
+// device status word back, so it waits on its stream.
 //
 // Every call shares the one array and leaves its contents behind; each call re-initialises
 // what it reads (status word, chunk list, bias, activation rows). Calls that overlap on the
@@ -52,21 +54,39 @@ size_t noalloc_layout(void* base, int M, int K, NoAllocLayout* out) {
   return c.off;
 }
 
-// Device address of the scratch array for the current device, looked up once per device.
+// The current CUDA context (driver API, reached through the runtime's entry-point query).
+CUcontext current_context() {
+  typedef CUresult (*CtxGetCurrent)(CUcontext*);
+  static CtxGetCurrent fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    return (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) ? reinterpret_cast<CtxGetCurrent>(p) : nullptr;
+  }();
+  CUcontext c = nullptr;
+  if (fn) fn(&c);
+  return c;
+}
+
+// Device address of the scratch array for the current device, looked up once per device and
+// context: a context created anew on that device (after cudaDeviceReset) loads the module
+// again, so the address is looked up again then.
 int scratch_address(void** out) {
-  static void* addr[64] = {};
+  struct Entry { CUcontext ctx; void* addr; };
+  static Entry cache[64] = {};
   static std::mutex mu;
   int dev = 0;
   LL_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return LL_ERR_ARG;
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
+  const CUcontext ctx = current_context();
+  if (!cache[dev].addr || !ctx || cache[dev].ctx != ctx) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
-    addr[dev] = p;
+    cache[dev] = Entry{current_context(), p};     // the lookup made the device's context current
   }
-  *out = addr[dev];
+  *out = cache[dev].addr;
   return LL_OK;
 }
 

@@ -75,3 +75,29 @@ def test_range_past_end_of_file_is_an_error(tmp_path):
     os.remove(p)
     with pytest.raises(LLError):
         read_layer_experts(idx, 3, [5], pin=False, retries=0)
+
+
+def test_lowest_failing_range_is_reported(tmp_path):
+    """With several failing ranges and many worker threads, ll_pread_batch reports the lowest
+    failing index every time (ranges are handed out in index order and every range below a
+    failure is finished before the batch returns)."""
+    import ctypes
+    from lazylora_b200 import _lib as L
+    lib = L.load()
+    p = tmp_path / "blob.bin"
+    p.write_bytes(bytes(range(256)) * 64)                   # 16 KB
+    n = 64
+    bufs = [ctypes.create_string_buffer(256) for _ in range(n)]
+    offs = [i * 256 for i in range(n)]
+    for bad in (5, 17, 40):                                 # these ranges start past the end
+        offs[bad] = 1 << 20
+    paths = (ctypes.c_char_p * n)(*[str(p).encode()] * n)
+    o = (ctypes.c_int64 * n)(*offs)
+    sz = (ctypes.c_int64 * n)(*[256] * n)
+    dst = (ctypes.c_void_p * n)(*[ctypes.addressof(b) for b in bufs])
+    for _ in range(20):
+        done, failed = ctypes.c_int64(0), ctypes.c_int(-2)
+        rc = lib.ll_pread_batch(n, paths, o, sz, dst, 16, 0, 0, ctypes.byref(done), ctypes.byref(failed))
+        assert rc == 7 and failed.value == 5                # LL_ERR_IO, the lowest failing range
+    for i in range(5):                                      # every range below it was read
+        assert bufs[i].raw == bytes(range(256))

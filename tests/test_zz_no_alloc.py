@@ -5,8 +5,9 @@ It exists for callers that cannot allocate device memory (a binding holding raw 
 and no device allocator, or code running where allocation is not allowed): instead of a
 caller-sized workspace it uses a static device array inside the library. These checks call
 it through the C ABI and compare it with the allocating entry point, ll_mxfp4_gemm, on the
-same inputs, for two calls in a row (the second call finds the first call's leftovers in
-the shared array), within the GEMM tolerance of the other parity tests (rel-L2 1e-3); and
+same inputs, for calls in a row of different sizes (each later call finds an earlier call's
+leftovers in the shared array), within the GEMM tolerance of the other parity tests
+(rel-L2 1e-3); and
 check that a size beyond the static array is refused with an error, not run.
 
 This file is named to be collected last, so a run that stops at the first failure has
@@ -30,12 +31,15 @@ def test_noalloc_gemm_matches_workspace_gemm():
     from lazylora_b200 import _lib as L
     lib = L.load()
     g = torch.Generator().manual_seed(11)
-    M, K, R = 48, 7168, 512
+    K, R = 7168, 512
     packed = torch.randint(0, 256, (R, K // 2), dtype=torch.uint8, generator=g).cuda()
     scales = torch.randint(112, 126, (R, K // 32), dtype=torch.uint8, generator=g).cuda()
     scales[5, 3] = 255                                    # a damaged group contributes nothing
     stream = torch.cuda.current_stream().cuda_stream
-    for call in range(2):
+    # calls in a row over the shared array: a three-chunk call (300 rows of 128-row chunks),
+    # then smaller ones that must not read the larger call's leftovers (chunk list, rows), one
+    # of them not a multiple of 16 rows, then the three-chunk size again
+    for call, M in enumerate((300, 48, 37, 300)):
         x = torch.randn(M, K, generator=g).cuda()
         want = torch.empty((M, R), dtype=torch.float32, device="cuda")
         nbytes = lib.ll_mxfp4_workspace_bytes(M, K, R)
@@ -48,8 +52,8 @@ def test_noalloc_gemm_matches_workspace_gemm():
                                        K // 32, stream)
         assert rc == 0, lib.ll_last_cuda_error()
         torch.cuda.synchronize()
-        assert torch.isfinite(got).all(), f"call {call}"
-        assert _rel_l2(got, want) <= TOL, f"call {call}"
+        assert torch.isfinite(got).all(), f"call {call} (M={M})"
+        assert _rel_l2(got, want) <= TOL, f"call {call} (M={M})"
 
 
 def test_noalloc_gemm_refuses_sizes_beyond_its_array():
