@@ -215,6 +215,16 @@ int ll_ep_gather_rows(void* dst, const void* src, const int* tok, int rows, int6
  * fp32 rows of width d (a multiple of 4); part holds the returned partials in send order. */
 int ll_ep_combine(float* out, const float* part, const int* pos, int T, int n_ranks, int d, void* stream);
 
+/* Packs fp32 partial rows [rows, d] (d a multiple of 4) for the return exchange: each row as
+ * d fp16 values scaled by a power of two 2^e that brings its largest magnitude into
+ * [2^14, 2^15), then the fp32 2^-e and 12 bytes of padding: 2d + 16 bytes a row (half the
+ * fp32 payload; 2^-11 relative rounding). 16-byte aligned buffers. */
+int ll_ep_pack_rows(void* dst, const float* src, int rows, int d, void* stream);
+
+/* ll_ep_combine over packed rows (ll_ep_pack_rows layout): out[t, :] = sum over r ascending of
+ * the unpacked row pos[t, r], in fp32. */
+int ll_ep_combine_packed(float* out, const void* part, const int* pos, int T, int n_ranks, int d, void* stream);
+
 /* grad_w[t, j] = part[pos[t, owner(idx[t, j])], j] (fp32 [rows, k] partials in send order);
  * 0 for a slot whose id is outside [0, E). */
 int ll_ep_combine_slots(float* grad_w, const float* part, const int* pos, const int64_t* idx, int T, int k, int E,

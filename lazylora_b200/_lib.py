@@ -78,6 +78,8 @@ _SIGS = {
                            c_void_p, c_void_p]),
     "ll_ep_gather_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int64, c_void_p]),
     "ll_ep_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "ll_ep_pack_rows": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "ll_ep_combine_packed": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "ll_ep_combine_slots": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
     "ll_profile_gemm_events": (c_int, [ctypes.POINTER(c_void_p), c_int]),
     "ll_pread_batch": (c_int, [c_int, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(c_int64),

@@ -11,7 +11,8 @@
 //
 // The exchanges themselves are the caller's (NCCL all-to-all through torch.distributed in
 // lazylora_b200.trainer.expert_parallel); these kernels build the send plan, gather the rows
-// and reduce what comes back. Send rows are grouped by destination rank (ascending), tokens
+// and reduce what comes back. The partial sums travel back packed: fp16 with a power-of-two
+// row scale (half the bytes of fp32, 2^-11 relative rounding), unpacked by the combine. Send rows are grouped by destination rank (ascending), tokens
 // ascending inside a group, so a rank receives its rows grouped by source rank, and the
 // reverse exchange returns the partials in exactly the send order.
 #include <cub/block/block_scan.cuh>
@@ -141,6 +142,63 @@ __global__ void k_ep_combine_slots(float* __restrict__ grad_w, const float* __re
   grad_w[i] = v;
 }
 
+// Packed partial rows for the return exchanges: row i of `src` (fp32, d4 float4) as d fp16
+// values times 2^e_i, e_i the power of two that brings max|row| into [2^14, 2^15), followed
+// by the fp32 2^-e_i and 12 bytes of padding (2d + 16 bytes a row). One warp per row.
+__global__ void k_ep_pack_rows(uint8_t* __restrict__ dst, const float4* __restrict__ src, int rows, int d4) {
+  const int warps = blockDim.x / 32, lane = threadIdx.x % 32;
+  const int64_t row_bytes = (int64_t)d4 * 8 + 16;
+  for (int64_t i = (int64_t)blockIdx.x * warps + threadIdx.x / 32; i < rows; i += (int64_t)gridDim.x * warps) {
+    const float4* s = src + i * d4;
+    float mx = 0.f;
+    for (int v = lane; v < d4; v += 32) {
+      const float4 x = s[v];
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+    }
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    const int e = row_scale_exp(mx);
+    const float sc = ldexpf(1.f, e);
+    uint2* o = reinterpret_cast<uint2*>(dst + i * row_bytes);
+    for (int v = lane; v < d4; v += 32) {
+      const float4 x = s[v];
+      const __half2 a = __floats2half2_rn(x.x * sc, x.y * sc), b = __floats2half2_rn(x.z * sc, x.w * sc);
+      o[v] = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+    }
+    if (lane == 0)
+      *reinterpret_cast<float4*>(dst + i * row_bytes + (int64_t)d4 * 8) = make_float4(ldexpf(1.f, -e), 0.f, 0.f, 0.f);
+  }
+}
+
+// out[t, :] = sum over ranks r ascending of the packed row pos[t, r] (fp16 x its 2^-e, in fp32).
+__global__ void k_ep_combine_packed(float4* __restrict__ out, const uint8_t* __restrict__ part,
+                                    const int* __restrict__ pos, int T, int n, int d4) {
+  __shared__ int s_pos[64];
+  __shared__ float s_inv[64];
+  const int64_t row_bytes = (int64_t)d4 * 8 + 16;
+  for (int t = blockIdx.x; t < T; t += gridDim.x) {
+    __syncthreads();
+    if (threadIdx.x < n) {
+      const int p = pos[(int64_t)t * n + threadIdx.x];
+      s_pos[threadIdx.x] = p;
+      s_inv[threadIdx.x] = p < 0 ? 0.f : *reinterpret_cast<const float*>(part + p * row_bytes + (int64_t)d4 * 8);
+    }
+    __syncthreads();
+    for (int v = threadIdx.x; v < d4; v += blockDim.x) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int r = 0; r < n; r++) {
+        const int p = s_pos[r];
+        if (p < 0) continue;
+        const uint2 h = reinterpret_cast<const uint2*>(part + p * row_bytes)[v];
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+        const float iv = s_inv[r];
+        acc.x += a.x * iv; acc.y += a.y * iv; acc.z += b.x * iv; acc.w += b.y * iv;
+      }
+      out[(int64_t)t * d4 + v] = acc;
+    }
+  }
+}
+
 }  // namespace ll
 
 using namespace ll;
@@ -188,6 +246,28 @@ int ll_ep_combine(float* out, const float* part, const int* pos, int T, int n_ra
   k_ep_combine<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<float4*>(out), reinterpret_cast<const float4*>(part), pos, T, n_ranks, d / 4);
   return check_launch("k_ep_combine");
+}
+
+int ll_ep_pack_rows(void* dst, const float* src, int rows, int d, void* stream) {
+  if (rows < 0 || d <= 0 || d % 4) return LL_ERR_ARG;
+  if (rows == 0) return LL_OK;
+  if (!dst || !src || (reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) % 16) return LL_ERR_ARG;
+  const int grid = (rows + 7) / 8 < 148 * 8 ? (rows + 7) / 8 : 148 * 8;
+  g_launch_stream = static_cast<cudaStream_t>(stream);
+  k_ep_pack_rows<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint8_t*>(dst), reinterpret_cast<const float4*>(src), rows, d / 4);
+  return check_launch("k_ep_pack_rows");
+}
+
+int ll_ep_combine_packed(float* out, const void* part, const int* pos, int T, int n_ranks, int d, void* stream) {
+  if (T < 0 || n_ranks <= 0 || n_ranks > 64 || d <= 0 || d % 4) return LL_ERR_ARG;
+  if (T == 0) return LL_OK;
+  if (!out || !pos || (reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(part)) % 16) return LL_ERR_ARG;
+  const int grid = T < 148 * 8 ? T : 148 * 8;
+  g_launch_stream = static_cast<cudaStream_t>(stream);
+  k_ep_combine_packed<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<float4*>(out), static_cast<const uint8_t*>(part), pos, T, n_ranks, d / 4);
+  return check_launch("k_ep_combine_packed");
 }
 
 int ll_ep_combine_slots(float* grad_w, const float* part, const int* pos, const int64_t* idx, int T, int k, int E,

@@ -5,8 +5,9 @@ The reference has no expert parallelism: lazy_lora/trainer/lazy_trainer.py:806-8
 routed experts in one process. Parity of the expert-parallel layer is therefore anchored on
 that single-process result (moe_oracle.experts_forward / experts_backward over all tokens and
 all experts): an n-rank run must reproduce it. This module restates, in plain torch CPU
-loops, the four index operations the CUDA kernels of lazylora_b200/csrc/expert_parallel.cu
-implement (plan, row gather, ordered combine, slot combine), so that
+loops, the index operations the CUDA kernels of lazylora_b200/csrc/expert_parallel.cu
+implement (plan, row gather, ordered combine, packing of the returned partial rows and the
+combine over them, slot combine), so that
 
   * the CUDA plan can be checked bit-exactly against `plan` on the GPU, and
   * the rank orchestration (lazylora_b200.trainer.expert_parallel.ExpertParallelLayer) can run
@@ -75,6 +76,34 @@ class OracleEPOps:
                 p = int(pos[t, r])
                 if p >= 0:
                     out[t] += part[p]
+        return out
+
+    def pack_rows(self, part: torch.Tensor) -> torch.Tensor:
+        """fp32 rows [R, d] -> packed rows [R, 2d + 16] bytes (as int32 [R, d/2 + 4]): d fp16
+        values times 2^e, e bringing the row's largest magnitude into [2^14, 2^15), then the fp32
+        2^-e and 12 zero bytes (the layout of ll_ep_pack_rows)."""
+        R, d = part.shape
+        out = torch.zeros((R, 2 * d + 16), dtype=torch.uint8)
+        for i in range(R):
+            mx = float(part[i].abs().max()) if d else 0.0
+            e = 0
+            if mx > 0 and mx != float("inf") and mx == mx:
+                e = 15 - int(torch.frexp(torch.tensor(mx, dtype=torch.float32)).exponent)
+            out[i, :2 * d] = (part[i] * 2.0 ** e).to(torch.float16).view(torch.uint8)
+            out[i, 2 * d:2 * d + 4] = torch.tensor([2.0 ** -e], dtype=torch.float32).view(torch.uint8)
+        return out.view(torch.int32)
+
+    def combine_packed(self, part: torch.Tensor, pos: torch.Tensor, T: int, d: int) -> torch.Tensor:
+        """combine over packed rows: each row unpacked to fp32 (fp16 value x its 2^-e), then the
+        sum over ranks in ascending order."""
+        b = part.view(torch.uint8).reshape(-1, 2 * d + 16)
+        out = torch.zeros((T, d), dtype=torch.float32)
+        for t in range(T):
+            for r in range(pos.shape[1]):
+                p = int(pos[t, r])
+                if p >= 0:
+                    inv = float(b[p, 2 * d:2 * d + 4].view(torch.float32)[0])
+                    out[t] += b[p, :2 * d].view(torch.float16).float() * inv
         return out
 
     def combine_slots(self, part: torch.Tensor, pos: torch.Tensor, idx: torch.Tensor, E: int) -> torch.Tensor:

@@ -1,10 +1,10 @@
 """
 Expert-parallel layer on CPU `gloo` ranks (no GPU): the rank orchestration of
 lazylora_b200.trainer.expert_parallel.ExpertParallelLayer (plan, count exchange, row
-dispatch, partial return, ordered combine, slot combine, LoRA all-reduce), driven with the
+dispatch, packed partial return, ordered combine, slot combine, LoRA all-reduce), driven with the
 CPU restatement of the index operations (oracle/ep_oracle.py) and the reference-algorithm
 expert loop (oracle/moe_oracle.py) as each rank's local layer. An n-rank run must give the
-single-process result over all tokens.
+single-process result over all tokens (to the fp16 rounding of the returned partial rows).
 """
 import os
 import socket
@@ -84,8 +84,10 @@ def _rank_main(rank, world, port, cfg, bias_hot):
         out = ep.forward(x[t0:t1], idx[t0:t1], w[t0:t1])
         grad_h, grad_w, grads = ep.backward(g[t0:t1])
 
-        assert O.rel_l2(out, want["out"][t0:t1]) < 1e-6
-        assert O.rel_l2(grad_h, want["grad_h"][t0:t1]) < 1e-6
+        # out and grad_h come back as fp16 rows with a power-of-two row scale (2^-11 relative
+        # rounding of each rank's partial); grad_w and the LoRA gradients stay fp32
+        assert O.rel_l2(out, want["out"][t0:t1]) < 1e-3
+        assert O.rel_l2(grad_h, want["grad_h"][t0:t1]) < 1e-3
         assert O.rel_l2(grad_w, want["grad_w"][t0:t1]) < 1e-6
         for name, t in want_grads.items():
             assert O.rel_l2(grads[name], t) < 1e-5, name
@@ -166,3 +168,19 @@ def _bad_id_main(rank, world, port):
 
 def test_bad_expert_id_fails_every_rank():
     mp.start_processes(_bad_id_main, args=(2, _free_port()), nprocs=2, start_method="spawn")
+
+
+def test_packed_rows_round_trip():
+    """The packed return rows: fp16 with a power-of-two row scale, exact for values fp16 holds,
+    2^-11 relative otherwise; zero rows and rows of very small or large values survive."""
+    ops = EPO.OracleEPOps()
+    g = torch.Generator().manual_seed(2)
+    part = torch.randn(5, 64, generator=g) * torch.tensor([1e-6, 1.0, 3e4, 1e9, 0.0]).unsqueeze(1)
+    packed = ops.pack_rows(part)
+    assert packed.shape == (5, 64 // 2 + 4) and packed.dtype == torch.int32
+    pos = torch.tensor([[0, 3], [1, -1], [2, 4]], dtype=torch.int32)
+    got = ops.combine_packed(packed, pos, 3, 64)
+    want = torch.stack([part[0] + part[3], part[1], part[2] + part[4]])
+    assert O.rel_l2(got, want) < 1e-3
+    exact = torch.tensor([[1.0, -2.0, 0.5, 0.0] * 16])
+    assert torch.equal(ops.combine_packed(ops.pack_rows(exact), torch.tensor([[0]], dtype=torch.int32), 1, 64), exact)

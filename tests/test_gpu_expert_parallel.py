@@ -2,7 +2,8 @@
 GPU checks of the expert-parallel path.
 
   * one GPU: the CUDA index kernels (ll_ep_plan, ll_ep_gather_rows, ll_ep_combine,
-    ll_ep_combine_slots) bit-exact against their CPU restatement (oracle/ep_oracle.py), at
+    ll_ep_pack_rows, ll_ep_combine_packed, ll_ep_combine_slots) bit-exact against their CPU
+    restatement (oracle/ep_oracle.py), at
     the full-width shape (T=1024, k=8, E=896, n=8) and ragged ones, invalid ids included;
   * two GPUs: ExpertParallelLayer over NCCL, each rank holding its block of experts and half
     of the tokens, against the single-process reference-algorithm oracle over all tokens and
@@ -52,6 +53,11 @@ def test_plan_and_combines_bit_exact(T, k, E, n, bad):
                        ref.gather_rows(x.to(torch.bfloat16), rtok, S))
     part = torch.randn(S, d, generator=gen)
     assert torch.equal(got.combine(part.cuda(), gpos, T, d).cpu(), ref.combine(part, rpos, T, d))
+    # the packed return rows: same bits as the restatement, rounding included
+    part[:1] *= 1e6
+    gp, rp = got.pack_rows(part.cuda()), ref.pack_rows(part)
+    assert torch.equal(gp.cpu(), rp)
+    assert torch.equal(got.combine_packed(gp, gpos, T, d).cpu(), ref.combine_packed(rp, rpos, T, d))
     pw = torch.randn(S, k, generator=gen)
     assert torch.equal(got.combine_slots(pw.cuda(), gpos, idx.cuda(), E).cpu(), ref.combine_slots(pw, rpos, idx, E))
 
