@@ -3,22 +3,27 @@ Benchmark of the routed-expert MoE layer (router + forward + manual backward wit
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-One step = route T tokens (KimiK3MoERouter), run the routed-expert forward (gate/up with
+One step = route the tokens (KimiK3MoERouter), run the routed-expert forward (gate/up with
 SiTU-GLU, down, weighted combine, LoRA fused) and the full backward (grad_h, grad_w and the
-six LoRA gradients) of one 896-expert MXFP4 layer, d=7168, f=2048, top-8 (BASELINE configs[1]
-at N=1: T=1024). Expert weights (~21 GB) are resident in HBM, far larger than the 126 MB L2,
-so every step streams them from DRAM. Inputs are seeded synthetic tensors with the
-distributions of BASELINE.json (the Kimi K3 checkpoint is not available).
+six LoRA gradients) of one 896-expert MXFP4 layer, d=7168, f=2048, top-8. Expert weights
+(~21 GB) are resident in HBM, far larger than the 126 MB L2, so every step streams them from
+DRAM. Inputs are seeded synthetic tensors with the distributions of BASELINE.json (the Kimi
+K3 checkpoint is not available).
 
-Under torchrun (N>1) each rank runs the same layer on its own 1024 tokens and its own copy
-of the experts (replicas; expert-parallel dispatch is a separate path), so per-GPU work is
-fixed: "scaling": "weak". Timing is device time (CUDA events on the launching stream),
-barrier + synchronize on both sides, max over ranks.
+  N = 1   BASELINE configs[1]: T = 1024 tokens on one GPU.
+  N > 1   BASELINE configs[2]: T = 8192 tokens in total, 8192 / N per rank, the experts split
+          expert-parallel over the N ranks (896 / N each) with NCCL all-to-all dispatch and
+          combine: "scaling": "strong". Rank 0 also times the same 8192-token layer on its own
+          GPU in the same job, and the line reports strong_efficiency = t(1 GPU) / (N t(N)).
+Timing is device time (CUDA events on the launching stream), barrier + synchronize on both
+sides, max over ranks.
 
 --impl reference times the reference's own CPU implementation of the path on this box's
 host cores: the reference's C kernel (lazy_lora/native/mxfp4_gemm.c, compiled from source into
-oracle/_ref) driven by the restated expert loop of oracle/moe_oracle.py, on a bounded sample
-of the same layer (a subset of experts with all their routed tokens), scaled to the full layer.
+oracle/_ref) driven by the restated expert loop of oracle/moe_oracle.py, with the router on
+the CPU. At N = 1 each timed step is the whole configs[1] layer; at N > 1 (configs[2], 8192
+tokens, too long for a bounded run) each step is a sample of the layer's experts with all
+their routed tokens, scaled to the layer.
 """
 import argparse
 import json
@@ -28,6 +33,7 @@ import subprocess
 import sys
 import threading
 import time
+from typing import Optional
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -143,17 +149,21 @@ def expert_bytes(cfg):
 
 
 # --------------------------------------------------------------------- reference arm
-def cpu_reference_sample(cfg, inp_dev, idx, w, n_experts: int, kind: str = "ref"):
-    """Time the reference CPU path (fwd + bwd sweep) over a subset of experts; returns
-    (seconds for the sample, fraction of the layer's expert work it covers, threads)."""
+def cpu_reference_sample(cfg, inp_dev, idx, w, n_experts: Optional[int], kind: str = "ref"):
+    """Time the reference CPU path (fwd + bwd sweep) over the layer's active experts, or over a
+    seeded sample of n_experts of them with all their routed tokens; returns (seconds, fraction
+    of the layer's active experts covered, threads)."""
     from oracle import moe_oracle as O
     nthreads = os.cpu_count() or 1
     torch.set_num_threads(nthreads)
     os.environ.setdefault("OMP_NUM_THREADS", str(nthreads))
     kern = O.MXFP4Checker(kind)
-    active = torch.unique(idx).tolist()
-    g = torch.Generator().manual_seed(123)
-    pick = sorted(active[i] for i in torch.randperm(len(active), generator=g)[:n_experts].tolist())
+    active = torch.unique(idx[idx >= 0]).tolist()
+    if n_experts is None or n_experts >= len(active):
+        pick = active
+    else:
+        g = torch.Generator().manual_seed(123)
+        pick = sorted(active[i] for i in torch.randperm(len(active), generator=g)[:n_experts].tolist())
     ev = torch.tensor(pick, device=idx.device)
     cpu = {key: inp_dev[key][ev].cpu() for key in ("w1p", "w1s", "w3p", "w3s", "w2p", "w2s")}
     cpu.update({key: inp_dev[key].float().cpu() for key in ("A_g", "B_g", "A_u", "B_u", "A_d", "B_d")})
@@ -173,7 +183,35 @@ def cpu_reference_sample(cfg, inp_dev, idx, w, n_experts: int, kind: str = "ref"
     return dt, len(pick) / max(1, len(active)), kern.threads()
 
 
+def workload_config(cfg, world, U=None):
+    """The `config` object both arms print for the same workload."""
+    if world == 1:
+        wl = (("configs[1]" if cfg.T == 1024 else f"configs[2]'s {cfg.T} tokens on one GPU") +
+              f": {cfg.E}-expert MXFP4 MoE layer, route + fwd + full LoRA bwd")
+        par = "single GPU"
+    else:
+        wl = (f"configs[2]: 896-expert MXFP4 MoE layer, {cfg.T * world} tokens, route + fwd + full LoRA bwd, "
+              f"expert parallel over {world} GPUs ({cfg.E // world} experts and {cfg.T} tokens each, NCCL "
+              f"all-to-all dispatch + combine)")
+        par = f"ep{world}"
+    c = {"workload": wl, "d": cfg.d, "f": cfg.f, "E": cfg.E, "k": cfg.k, "T_total": cfg.T * world,
+         "T_per_gpu": cfg.T, "r": cfg.r, "parallelism": par,
+         "l2": "weights >> 126 MB L2: every step streams them from HBM"}
+    if U is not None:
+        c["active_experts_rank0"] = U
+    return c
+
+
+REF_SAMPLE_EXPERTS_EP = 64     # configs[2] reference steps: experts sampled, all their tokens
+
+
 def run_reference(args, cfg, rank, world, dist):
+    """The reference's CPU path on the box's host cores, on the same workload as our arm (cfg
+    is the per-rank config; the workload is its T times world tokens): rank 0 only (the other
+    ranks of a torchrun launch exit without work). Each timed step routes every token on the
+    CPU (KimiK3MoERouter arithmetic: fp32 logits, torch.topk) and runs the reference expert loop
+    forward + backward; warm-up steps run a 16-expert sample (they only warm the code paths)."""
+    from dataclasses import replace
     from lazylora_b200.synthetic import make_layer_device
     if rank != 0:
         return
@@ -181,30 +219,36 @@ def run_reference(args, cfg, rank, world, dist):
     if dev == "cpu":
         print(json.dumps({"impl": "reference", "unavailable": "no CUDA device to generate the layer inputs on"}))
         return
-    inp = make_layer_device(cfg, device=dev)
+    total = replace(cfg, T=cfg.T * world)
+    inp = make_layer_device(total, device=dev)
     from oracle import moe_oracle as O
-    x = inp["x"].float()
-    # routing with the reference's router arithmetic on CPU (fp32 logits, torch.topk)
-    idx, w = O.route(x.cpu(), inp["router_w"].cpu(), inp["router_b"].cpu(), cfg.k)
     kind = "ref" if os.path.exists(O.REF_SO) else "oracle"
-    n_exp = args.ref_experts
+    x_cpu, wr, br = inp["x"].float().cpu(), inp["router_w"].cpu(), inp["router_b"].cpu()
+    sample = None if world == 1 else REF_SAMPLE_EXPERTS_EP
     times = []
+    threads = os.cpu_count() or 1
     for i in range(args.warmup + args.steps):
-        dt, frac, threads = cpu_reference_sample(cfg, inp, idx.to(dev), w.to(dev), n_exp, kind)
+        t0 = time.perf_counter()
+        idx, w = O.route(x_cpu, wr, br, total.k)
+        t_route = time.perf_counter() - t0
+        dt, frac, threads = cpu_reference_sample(total, inp, idx.to(dev), w.to(dev),
+                                                 16 if i < args.warmup else sample, kind)
         if i >= args.warmup:
-            times.append(dt / frac)            # seconds for the whole layer
+            times.append(t_route + dt / frac)            # seconds for the whole layer
     step_s = statistics.median(times)
-    value = cfg.T / step_s
-    sample = (f"fwd+bwd over {n_exp} of the layer's active experts with all their routed tokens "
-              f"(expert-sampled, scaled by active/{n_exp}); router on CPU not included")
-    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "configs[1]: 896-expert MXFP4 MoE layer fwd+bwd", "d": cfg.d, "f": cfg.f,
-                       "E": cfg.E, "k": cfg.k, "T": cfg.T, "r": cfg.r},
-            "impl": "reference",
+    value = total.T / step_s
+    if sample is None:
+        desc = ("the whole layer each step: CPU router over all tokens, then the reference expert loop "
+                "fwd+bwd over every active expert")
+    else:
+        desc = (f"CPU router over all {total.T} tokens, then the reference expert loop fwd+bwd over {sample} of "
+                f"the active experts with all their routed tokens, scaled by active/{sample}")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload_config(cfg, world), "impl": "reference",
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads,
-                             "kind": "reference" if kind == "ref" else "port", "sample": sample},
+                             "kind": "reference" if kind == "ref" else "port", "sample": desc},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -220,7 +264,13 @@ def run_ours(args, cfg, rank, local, world, dist):
     dev = torch.device("cuda", local)
     lib = L.load()
     ep = None
+    single_ms = None
     if world > 1:
+        # the same total workload on one GPU, timed by rank 0 in this job (the denominator of
+        # strong_efficiency); the other ranks wait at the barrier
+        if rank == 0:
+            single_ms = time_single_gpu(args, cfg, world, dev)
+        dist.barrier()
         # expert parallel: this rank's block of experts and its own cfg.T tokens
         from lazylora_b200.synthetic import make_ep_rank_device
         from lazylora_b200.trainer.expert_parallel import ExpertParallelLayer
@@ -323,6 +373,23 @@ def run_ours(args, cfg, rank, local, world, dist):
             breakdown[nm] = breakdown.get(nm, 0.0) + prev.elapsed_time(evs[i]) * 1e3 / nb_steps
             prev = evs[i]
 
+    # ---- all-to-all time per exchange (untimed pass, CUDA events around each collective)
+    a2a = None
+    if ep is not None:
+        ep.profile = []
+        step(x, g)
+        torch.cuda.synchronize()
+        prof, ep.profile = ep.profile, None
+        names = [nm for nm, _, _ in prof]
+        ms = torch.tensor([e[0].elapsed_time(e[1]) for _, _, e in prof], device=dev, dtype=torch.float64)
+        byts = torch.tensor([b for _, b, _ in prof], device=dev, dtype=torch.float64)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(byts, op=dist.ReduceOp.MAX)
+        a2a = {"source": "CUDA events around each collective in one untimed step, max over ranks",
+               "total_ms": round(float(ms.sum()), 4),
+               **{nm: {"ms": round(float(m), 4), "bytes_sent_max_rank": int(b)}
+                  for nm, m, b in zip(names, ms.tolist(), byts.tolist())}}
+
     # ---- end to end through the public API, host buffers, copies inside the timed region
     x_h = x.cpu().pin_memory()
     g_h = g.cpu().pin_memory()
@@ -368,19 +435,13 @@ def run_ours(args, cfg, rank, local, world, dist):
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak" if world == 1 else "strong",
         "vs_baseline": None, "dtype": "fp16 operands / fp32 accumulate (MXFP4 weights decoded exactly)",
         "data": "synthetic",
-        "config": {"workload": ((f"{args.config}: {cfg.E}-expert MXFP4 MoE layer, route + fwd + full LoRA bwd"
-                                 if args.config != "c1" else
-                                 "configs[1]: 896-expert MXFP4 MoE layer, route + fwd + full LoRA bwd") if world == 1
-                                else f"expert parallel over {world} GPUs ({cfg.E // world} experts each), "
-                                     f"{cfg.T} tokens per GPU ({cfg.T * world} total; configs[2] at 8 GPUs), "
-                                     f"route + NCCL all-to-all dispatch + fwd + full LoRA bwd + combine"),
-                   "d": cfg.d, "f": cfg.f, "E": cfg.E, "k": cfg.k, "T_per_gpu": cfg.T, "T_total": cfg.T * world,
-                   "r": cfg.r, "active_experts_rank0": U,
-                   "parallelism": f"ep{world}" if world > 1 else "single GPU",
-                   "l2": "weights >> 126 MB L2: every step streams them from HBM"},
+        "config": workload_config(cfg, world, U) if args.config in ("c1", "c2") else
+        {**workload_config(cfg, world, U), "workload": f"{args.config}: {cfg.E}-expert MXFP4 MoE layer, "
+                                                       f"route + fwd + full LoRA bwd"},
         "weight_TBps": weight_tbs,
         "hbm_roofline_ms": 2 * U * eb / (hbm_peak * 1e9) * 1e3,
         "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
@@ -403,15 +464,60 @@ def run_ours(args, cfg, rank, local, world, dist):
         "gpu_launches": launches[0],
         "clocks": clocks,
     }
+    if world > 1:
+        line["layer_ms_max_over_ranks"] = ms_step
+        line["single_gpu_same_workload_ms"] = single_ms
+        line["strong_efficiency"] = single_ms / (world * ms_step) if single_ms else None
+        line["all_to_all"] = a2a
     if args.cpu_baseline and world == 1:
         weights = {"w1p": layer.w1p, "w3p": layer.w3p, "w2p": layer.w2p, "w1s": layer.w1s[..., :cfg.d // 32],
                    "w3s": layer.w3s[..., :cfg.d // 32], "w2s": layer.w2s[..., :cfg.f // 32]}
-        dt, frac, threads = cpu_reference_sample(cfg, {**inp, **weights}, idx, res[5], args.ref_experts)
-        full = dt / frac
-        line["cpu_baseline"] = {"value": cfg.T / full, "unit": UNIT, "cores": threads, "kind": "reference",
-                                "sample": f"reference C kernel (oracle/_ref) + restated expert loop, fwd+bwd over "
-                                          f"{args.ref_experts} of {U} active experts, scaled to the layer"}
+        dt, frac, threads = cpu_reference_sample(cfg, {**inp, **weights}, idx, res[5], None)
+        line["cpu_baseline"] = {"value": cfg.T / dt, "unit": UNIT, "cores": threads, "kind": "reference",
+                                "sample": f"one whole-layer step: the reference C kernel (oracle/_ref) driven by the "
+                                          f"restated expert loop, fwd+bwd over all {U} active experts with the GPU "
+                                          f"step's routing"}
     print(json.dumps(line), flush=True)
+
+
+def time_single_gpu(args, cfg, world, dev):
+    """ms per step of the N-rank run's whole workload (world * cfg.T tokens, all experts) on this
+    GPU alone: route + forward + full backward, CUDA events, after warm-up. Frees its memory."""
+    from dataclasses import replace
+    from lazylora_b200.core.moe_router import KimiK3MoERouter
+    from lazylora_b200.synthetic import make_layer_device
+    from lazylora_b200.trainer.routed_experts import RoutedExpertsLayer
+    total = replace(cfg, T=cfg.T * world)
+    inp = make_layer_device(total, device=dev)
+    layer = RoutedExpertsLayer.from_inputs(inp, total.scaling, device=dev)
+    router = KimiK3MoERouter(hidden_size=total.d, num_experts=total.E, top_k=total.k, device=dev)
+    x = inp["x"].to(torch.bfloat16).contiguous()
+    g = inp["g"].to(torch.bfloat16).contiguous()
+    Wr, br = inp["router_w"], inp["router_b"]
+    del inp
+
+    def step():
+        idx, w = router.forward(x, weight=Wr, bias=br)
+        layer.forward(x, idx, w)
+        layer.backward(x, idx, w, g)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    layer.check_status(total.T, total.k)
+    stream = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(3, min(args.steps, 10))
+    torch.cuda.synchronize()
+    a.record(stream)
+    for _ in range(n):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    layer.check_status(total.T, total.k)
+    ms = a.elapsed_time(b) / n
+    del layer, router, x, g
+    torch.cuda.empty_cache()
+    return ms
 
 
 # ----------------------------------------------------------------------- decode (configs[3])
@@ -784,7 +890,6 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c1")
-    ap.add_argument("--ref-experts", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--decode", action="store_true", help="forward-only decode steps (configs[3]: c3_t1/4/16)")
     ap.add_argument("--graph", action="store_true", help="with --decode: replay each step as a CUDA graph")
@@ -807,6 +912,14 @@ def main():
     if args.zipf_gamma is not None:
         cfg = replace(cfg, zipf_gamma=args.zipf_gamma)
     rank, local, world, dist = dist_setup(args)
+    if world > 1 and args.config in ("c1", "c2") and not (args.decode or args.stream or args.latent or
+                                                          args.traces or args.shared):
+        # 8192 tokens in total over the N ranks (strong scaling)
+        total = CONFIGS["c2"]
+        if total.T % world:
+            raise SystemExit(f"--gpus {world} does not divide configs[2]'s {total.T} tokens")
+        cfg = replace(total, T=total.T // world)
+        args.config = "c2"
     try:
         if args.impl == "reference":
             run_reference(args, cfg, rank, world, dist)   # rank 0 only; no collective
