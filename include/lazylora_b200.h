@@ -138,12 +138,21 @@ typedef struct {
    * the token-tile width; give it when many slots are -1 (expert parallelism). The forward and
    * the backward that follows must see the same value. */
   int rows_hint;
+  /* The forward GEMMs' weight scales in the layout the block-scaled tensor-core MMA reads,
+   * built by ll_moe_prepare into caller buffers of ll_mxfp4_sf_bytes(E, rows, cols) bytes:
+   * gate and up ([E, f, d]) and down ([E, d, f]). Required by ll_moe_forward. */
+  const uint8_t* w1sf; const uint8_t* w3sf; const uint8_t* w2sf;
 } ll_moe_layer;
+
+/* Bytes of the block-scaled MMA's scale layout of a stack of E matrices of R rows and C
+ * columns (R, C multiples of 128): E * R * C / 32. */
+size_t ll_mxfp4_sf_bytes(int E, int R, int C);
 
 /* One-time preparation per weight load (the base weights are frozen): the per-expert
  * decode bias beta (beta[e][0] gate+up, beta[e][1] down, so that every scale byte within 36
  * of the matrix maximum decodes exactly to fp16), then the transposed copies w1t..s2t that
- * L points at (beta_out must be L->beta). With all six transposed pointers NULL only beta is
+ * L points at (beta_out must be L->beta). It also lays out the scale blocks w1sf, w2sf, w3sf
+ * the forward reads. With all six transposed pointers NULL only beta and the scale blocks are
  * built: enough for ll_moe_forward; call again with the buffers set before a backward.
  * Some but not all of them NULL is LL_ERR_ARG. */
 int ll_moe_prepare(const ll_moe_layer* L, int32_t* beta_out, void* stream);

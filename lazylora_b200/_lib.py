@@ -41,6 +41,7 @@ class MoELayerDesc(ctypes.Structure):
         ("w1t", c_void_p), ("w3t", c_void_p), ("w2t", c_void_p),
         ("s1t", c_void_p), ("s3t", c_void_p), ("s2t", c_void_p),
         ("rows_hint", c_int),
+        ("w1sf", c_void_p), ("w3sf", c_void_p), ("w2sf", c_void_p),
     ]
 
 
@@ -50,6 +51,7 @@ _SIGS = {
     "ll_last_launch_count": (c_int, []),
     "ll_mxfp4_threads": (c_int, []),
     "ll_mxfp4_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "ll_mxfp4_sf_bytes": (c_size_t, [c_int, c_int, c_int]),
     "ll_mxfp4_gemm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64,
                               c_void_p, c_size_t, c_void_p]),
     "ll_mxfp4_gemm_t": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64,

@@ -1,0 +1,152 @@
+// Operand preparation for the block-scaled forward GEMMs (bs_gemm.cuh): the weights' E8M0
+// scale blocks in the layout tcgen05.cp copies into tensor memory (once per weight load), and
+// activation rows as three E4M3 terms with power-of-two row scales (once per GEMM input).
+#include "host_common.cuh"
+#include "ops.cuh"
+
+namespace ll {
+
+// One thread per (row, 128-K stage): the row's 4 scale bytes of that stage, bytes >= 253 (the
+// reference's "contributes zero") replaced by 0, written to line (row % 32), word
+// ((row % 128) / 32) of the stage's block of the row's 128-row tile.
+__global__ void k_prepare_sfa(const uint8_t* __restrict__ scales, int64_t sstride, int64_t rows_total, int R,
+                              int n_stage, uint8_t* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows_total * n_stage) return;
+  const int64_t row = i / n_stage;
+  const int ks = (int)(i % n_stage);
+  uint32_t w = *reinterpret_cast<const uint32_t*>(scales + row * sstride + 4 * ks);
+  uint32_t fixed = 0;
+#pragma unroll
+  for (int b = 0; b < 4; b++) {
+    const uint32_t byte = (w >> (8 * b)) & 0xffu;
+    fixed |= (byte >= 253u ? 0u : byte) << (8 * b);
+  }
+  const int64_t e = row / R;
+  const int r = (int)(row % R);
+  const int64_t tile = e * (R / 128) + r / 128;
+  const int m = r % 128;
+  uint32_t* blk = reinterpret_cast<uint32_t*>(out + (tile * n_stage + ks) * kBsSfBlock);
+  blk[(m % 32) * 4 + m / 32] = fixed;
+}
+
+int launch_prepare_sfa(const uint8_t* scales, int64_t sstride, int E, int R, int C, uint8_t* out, cudaStream_t s) {
+  if (E <= 0 || R <= 0 || R % 128 || C <= 0 || C % 128 || sstride < C / 32 || sstride % 4 || !scales || !out)
+    return LL_ERR_ARG;
+  const int64_t rows = (int64_t)E * R;
+  const int n_stage = C / 128;
+  const int64_t n = rows * n_stage;
+  k_prepare_sfa<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(scales, sstride, rows, R, n_stage, out);
+  return check_launch("k_prepare_sfa");
+}
+
+// ------------------------------------------------------------------------------------
+constexpr int kE3Threads = 256;
+constexpr int kE3Chunks = 4;       // 8-element chunks a thread holds: K <= 8 * 4 * 256
+
+template <int SRC>   // 0 fp32, 1 bf16, 2 fp16
+LL_DEV void load8(const void* src, int64_t row, int K, int ch, float (&v)[8]) {
+  if (SRC == 0) {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + row * K) + 2 * ch;
+    const float4 a = p[0], b = p[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 u = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(src) + row * K)[ch];
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float2 f = SRC == 1 ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]))
+                                : __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  }
+}
+
+// Block-wide max of v (every thread gets it); `red` holds kE3Threads / 32 floats.
+LL_DEV float block_max(float v, float* red) {
+  for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+  __syncthreads();                                   // red is reused term after term
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = v;
+  __syncthreads();
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < kE3Threads / 32; i++) m = fmaxf(m, red[i]);
+  return m;
+}
+
+// One block per source row: the row in registers, three rounds of (block max, scale, round to
+// E4M3, subtract), each term stored to every destination row.
+template <int SRC, bool TOK>
+__global__ void __launch_bounds__(kE3Threads) k_rows_to_e4m3x3(const void* __restrict__ src, int src_rows,
+                                                               const int* __restrict__ tok_pos, int k,
+                                                               const int* __restrict__ n_valid, int K, int64_t P,
+                                                               uint8_t* __restrict__ dst, float* __restrict__ inv3) {
+  const int r = blockIdx.x;
+  if (r >= src_rows) return;
+  if (!TOK && n_valid && r >= *n_valid) return;
+  __shared__ float red[kE3Threads / 32];
+  const int nch = K / 8;
+  float v[kE3Chunks][8];
+#pragma unroll
+  for (int i = 0; i < kE3Chunks; i++) {
+    const int ch = threadIdx.x + i * kE3Threads;
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[i][j] = 0.f;
+    if (ch < nch) load8<SRC>(src, r, K, ch, v[i]);
+  }
+#pragma unroll 1
+  for (int t = 0; t < kBsTerms; t++) {
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < kE3Chunks; i++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) mx = fmaxf(mx, fabsf(v[i][j]));
+    const int e = e4m3_scale_exp(block_max(mx, red));
+    const float sc = ldexpf(1.f, e), inv = ldexpf(1.f, -e);
+    uint2 q[kE3Chunks];
+#pragma unroll
+    for (int i = 0; i < kE3Chunks; i++) {
+      uint32_t b[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        b[j] = f32x2_to_e4m3x2(v[i][2 * j] * sc, v[i][2 * j + 1] * sc);
+        const float2 d = e4m3x2_to_f32x2(b[j]);
+        v[i][2 * j] -= d.x * inv;                // the residual the next term takes
+        v[i][2 * j + 1] -= d.y * inv;
+      }
+      q[i] = make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
+    }
+    for (int j = 0; j < (TOK ? k : 1); j++) {
+      const int p = TOK ? tok_pos[(int64_t)r * k + j] : r;
+      if (p < 0) continue;
+      if (threadIdx.x == 0) inv3[t * P + p] = inv;
+      uint2* row = reinterpret_cast<uint2*>(dst + ((int64_t)t * P + p) * K);
+#pragma unroll
+      for (int i = 0; i < kE3Chunks; i++) {
+        const int ch = threadIdx.x + i * kE3Threads;
+        if (ch < nch) row[ch] = q[i];
+      }
+    }
+  }
+}
+
+int launch_rows_to_e4m3x3(const void* src, int src_dtype, int src_rows, const int* tok_pos, int k,
+                          const int* n_valid, int K, int64_t P, uint8_t* dst, float* inv3, cudaStream_t s) {
+  if (src_rows <= 0) return LL_OK;
+  if (!src || !dst || !inv3 || K <= 0 || K % 8 || K > 8 * kE3Chunks * kE3Threads || src_dtype < 0 || src_dtype > 2)
+    return LL_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) % 16) return LL_ERR_ARG;
+  const bool tok = tok_pos != nullptr;
+#define LL_E3(SRC, TOKV)                                                                              \
+  k_rows_to_e4m3x3<SRC, TOKV><<<src_rows, kE3Threads, 0, s>>>(src, src_rows, tok_pos, k, n_valid, K, P, dst, inv3)
+  if (tok) {
+    if (src_dtype == 0) LL_E3(0, true); else if (src_dtype == 1) LL_E3(1, true); else LL_E3(2, true);
+  } else {
+    if (src_dtype == 0) LL_E3(0, false); else if (src_dtype == 1) LL_E3(1, false); else LL_E3(2, false);
+  }
+#undef LL_E3
+  return check_launch("k_rows_to_e4m3x3");
+}
+
+}  // namespace ll

@@ -223,6 +223,26 @@ LL_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// The same load without the conversion: the registers are valid only after tcgen05.wait::ld
+// and tmem_regs_ready (which ties them to a point after the wait, so no use is scheduled
+// earlier).
+LL_DEV void tmem_ld16_u(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+LL_DEV void tmem_regs_ready(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
+}
+
 // UMMA shared-memory descriptor (tcgen05 format): start address, leading / stride byte
 // offsets (all >> 4), version 1 at bits 46-47, layout type at bits 61-63.
 enum : uint32_t { kSwizzleNone = 0, kSwizzle128B = 2, kSwizzle64B = 4, kSwizzle32B = 6 };
@@ -248,6 +268,87 @@ LL_DEV uint32_t idesc_f16_m128(uint32_t n, bool a_mn_major, bool b_mn_major) {
   d |= (n >> 3) << 17;
   d |= (128u >> 4) << 24;
   return d;
+}
+
+// ------------------------------------------------------------- block-scaled tcgen05 MMA
+// D[tmem] (+)= (A * SFA)[smem desc] * (B * SFB)[smem desc], kind::mxf8f6f4 with one E8M0 scale
+// per 32 K elements of every A row and B row, read from tensor memory at sfa / sfb (the byte
+// of each 32-bit word selected by bits 30-31 of the address and the ids in the descriptor).
+LL_DEV void mma_mxf8f6f4_bs(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t sfa,
+                            uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor, kind::mxf8f6f4 block-scaled: A E2M1 (K-major), B E4M3 (K-major), fp32
+// D, E8M0 scales, M = 128, N = n (multiple of 16, <= 256), K = 32; sf_a / sf_b select the scale
+// byte (the 32-K block within a 32-bit scale word) of A and B.
+LL_DEV uint32_t idesc_mxf4xe4m3_m128(uint32_t n, uint32_t sf_a, uint32_t sf_b) {
+  uint32_t d = 0;
+  d |= (sf_b & 3u) << 4;        // B scale-factor id
+  d |= 5u << 7;                 // A format E2M1
+  d |= 0u << 10;                // B format E4M3
+  d |= (n >> 3) << 17;          // N
+  d |= 1u << 23;                // scale format E8M0
+  d |= (128u >> 4) << 24;       // M
+  d |= (sf_a & 3u) << 29;       // A scale-factor id
+  return d;
+}
+
+// 32 rows x 128 bits from shared memory (descriptor, no swizzle, 16-byte rows) into tensor
+// memory lanes 0..31 at columns taddr .. taddr + 3, replicated into all four lane quarters.
+LL_DEV void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// L2 prefetch of a 2-D TMA box (no shared memory, no barrier).
+LL_DEV void tma_prefetch_l2_2d(const CUtensorMap* m, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(m)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
+// L2 prefetch of a contiguous range (16-byte aligned, size % 16 == 0).
+LL_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
+
+// Contiguous global -> shared copy on the async proxy (16-byte aligned, size % 16 == 0),
+// completing `bytes` transactions on bar.
+LL_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Two floats -> two E4M3 bytes, round to nearest, saturating to +-448 (lo in the low byte).
+LL_DEV uint32_t f32x2_to_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Two E4M3 bytes (low byte = first) -> their exact values.
+LL_DEV float2 e4m3x2_to_f32x2(uint32_t b2) {
+  uint32_t h2;
+  const uint16_t b = (uint16_t)b2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(b));
+  return __half22float2(*reinterpret_cast<const __half2*>(&h2));
+}
+
+// Power-of-two exponent e that brings max|row| into [2^7, 2^8): the first E4M3 term of a row
+// scaled by 2^e keeps its largest entries at full E4M3 precision, well inside the +-448 range.
+LL_DEV int e4m3_scale_exp(float maxabs) {
+  if (!(maxabs > 0.f) || !isfinite(maxabs)) return 0;
+  int e;
+  frexpf(maxabs, &e);   // maxabs in [2^(e-1), 2^e)
+  return 8 - e;
 }
 
 // ------------------------------------------------------------------------ MXFP4 decode

@@ -7,6 +7,7 @@
 #include <mutex>
 
 #include "grouped_gemm.cuh"
+#include "bs_gemm.cuh"
 
 namespace ll {
 
@@ -134,6 +135,52 @@ int launch_gemm(const CUtensorMap* pk, const CUtensorMap* sc, const CUtensorMap*
                               : EPI == EPI_B1 ? "grouped_mxfp4_gemm B1 g.W2"
                               : EPI == EPI_B2 ? "grouped_mxfp4_gemm B2 dg.W1+du.W3"
                                               : "grouped_mxfp4_gemm");
+  if (prof) {
+    LL_CUDA(cudaEventRecord(g_prof_events[g_prof_i + 1], stream));
+    g_prof_i += 2;
+  }
+  return rc;
+}
+
+// Weight codes [rows_total][K/2] bytes as the block-scaled MMA reads them: 16 x 4-bit values
+// per 16-byte chunk in shared memory (TMA unpacks each 8 packed bytes into 16), boxes of
+// box_rows rows x 128 K, 128-byte swizzle. K a multiple of 128; the row stride (K/2 bytes)
+// and the base must be 32-byte aligned.
+inline int make_fp4_map(CUtensorMap* m, const uint8_t* packed, int64_t rows_total, int K, int box_rows) {
+  if (K % 128 || (reinterpret_cast<uintptr_t>(packed) & 31)) return LL_ERR_ARG;
+  return make_map_2d(m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, packed, (uint64_t)K, (uint64_t)rows_total,
+                     (uint64_t)K / 2, 128, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// E4M3 activation terms [3][rows][K] bytes, one map per chunk height 16 c (c = 1..n): a box is
+// [3 terms][16 c rows][128 K], 128-byte swizzle.
+inline int make_e4m3x3_maps(CUtensorMap* maps, int n, const uint8_t* base, int64_t rows, int K) {
+  if (K % 128 || n < 1 || n > 4) return LL_ERR_ARG;
+  const uint64_t dims[3] = {(uint64_t)K, (uint64_t)rows, (uint64_t)kBsTerms};
+  const uint64_t strides[2] = {(uint64_t)K, (uint64_t)rows * K};
+  for (int c = 1; c <= n; c++) {
+    const uint32_t box[3] = {128, (uint32_t)(16 * c), (uint32_t)kBsTerms};
+    LL_TRY(make_map_nd(&maps[c - 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, base, 3, dims, strides, box,
+                       CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  return LL_OK;
+}
+
+template <int EPI, int NMAT, int N_MAX>
+int launch_bs_gemm(const CUtensorMap* a, const CUtensorMap* b, const BsArgs& args, cudaStream_t stream) {
+  using Cfg = BsCfg<NMAT, N_MAX>;
+  BsTma<NMAT, N_MAX> tm;
+  for (int i = 0; i < NMAT; i++) tm.a[i] = a[i];
+  for (int i = 0; i < N_MAX / 16; i++) tm.b[i] = b[i];
+  auto kern = grouped_mxfp4_bs_gemm<EPI, NMAT, N_MAX>;
+  LL_TRY(set_smem_attr(reinterpret_cast<const void*>(kern), Cfg::SMEM));
+  const DeviceInfo di = device_info();
+  const bool prof = g_prof_events && g_prof_i + 2 <= g_prof_n;
+  if (prof) LL_CUDA(cudaEventRecord(g_prof_events[g_prof_i], stream));
+  kern<<<di.sms, Cfg::kThreads, Cfg::SMEM, stream>>>(tm, args);
+  const int rc = check_launch(EPI == EPI_F1   ? "grouped_mxfp4_bs_gemm F1 gate/up"
+                              : EPI == EPI_F2 ? "grouped_mxfp4_bs_gemm F2 down"
+                                              : "grouped_mxfp4_bs_gemm");
   if (prof) {
     LL_CUDA(cudaEventRecord(g_prof_events[g_prof_i + 1], stream));
     g_prof_i += 2;

@@ -301,6 +301,10 @@ struct LayerWs {
   float* tw;
   float* xinv;
   __half* xh;
+  uint8_t* xq;        // [3][P][d] E4M3 terms of the pair rows (block-scaled F1)
+  float* xinv3;       // [3][P]
+  uint8_t* hq;        // [3][P][f] E4M3 terms of h (block-scaled F2)
+  float* hinv3;       // [3][P]
   float* xa_g;
   float* xa_u;
   float* dlt_g;
@@ -368,6 +372,10 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   w.tw = c.take<float>(P);
   w.xinv = c.take<float>(P);
   w.xh = c.take<__half>(P * d);
+  w.xq = c.take<uint8_t>((size_t)kBsTerms * P * d);
+  w.xinv3 = c.take<float>((size_t)kBsTerms * P);
+  w.hq = c.take<uint8_t>((size_t)kBsTerms * P * f);
+  w.hinv3 = c.take<float>((size_t)kBsTerms * P);
   w.xa_g = c.take<float>((size_t)T * r);
   w.xa_u = c.take<float>((size_t)T * r);
   w.dlt_g = c.take<float>((size_t)T * f);
@@ -411,6 +419,7 @@ static int validate(const ll_moe_layer* L, int T, int k, bool backward) {
   if (L->s13_stride < L->d / 32 || L->s13_stride % 16 || L->s2_stride < L->f / 32 || L->s2_stride % 16) return LL_ERR_ARG;
   if (!L->w1p || !L->w1s || !L->w3p || !L->w3s || !L->w2p || !L->w2s || !L->beta) return LL_ERR_ARG;
   if (!L->A_g || !L->B_g || !L->A_u || !L->B_u || !L->A_d || !L->B_d) return LL_ERR_ARG;
+  if (!L->w1sf || !L->w3sf || !L->w2sf) return LL_ERR_ARG;
   if (backward && (!L->w1t || !L->w3t || !L->w2t || !L->s1t || !L->s3t || !L->s2t)) return LL_ERR_ARG;
   return LL_OK;
 }
@@ -422,6 +431,23 @@ static int gemm_nmax(int nmax, const CUtensorMap* pk, const CUtensorMap* sc, con
   if (nmax == 32) return launch_gemm<EPI, NMAT, NB, COLSCALE, 32>(pk, sc, act, a, s);
   if (nmax == 64) return launch_gemm<EPI, NMAT, NB, COLSCALE, 64>(pk, sc, act, a, s);
   return launch_gemm<EPI, NMAT, NB, COLSCALE, 128>(pk, sc, act, a, s);
+}
+
+// Stages the block-scaled GEMMs prefetch weight tiles into L2 ahead of their loads
+// (LL_BS_PREFETCH_STAGES overrides the default, for tuning).
+static int bs_prefetch_stages() {
+  static const int v = [] {
+    const char* e = getenv("LL_BS_PREFETCH_STAGES");
+    return e ? atoi(e) : 8;
+  }();
+  return v;
+}
+
+template <int EPI>
+static int bs_nmax(int nmax, const CUtensorMap* a, const CUtensorMap* b, const BsArgs& args, cudaStream_t s) {
+  if (nmax == 16) return launch_bs_gemm<EPI, 2, 16>(a, b, args, s);
+  if (nmax == 32) return launch_bs_gemm<EPI, 2, 32>(a, b, args, s);
+  return launch_bs_gemm<EPI, 2, 64>(a, b, args, s);
 }
 
 // C0 (and C1) = alpha * A[M][K] . B, with B given as rows ([N][K], split over B0 / B1 at N0)
@@ -531,6 +557,13 @@ int ll_moe_prepare(const ll_moe_layer* L, int32_t* beta_out, void* stream) {
   const int E = L->E, d = L->d, f = L->f;
   LL_TRY(launch_prepare_beta(L->w1s, L->w3s, E, f, d, L->s13_stride, beta_out, 0, s));
   LL_TRY(launch_prepare_beta(L->w2s, nullptr, E, d, f, L->s2_stride, beta_out, 1, s));
+  if (L->w1sf || L->w3sf || L->w2sf) {        // the forward's scale blocks
+    if (!L->w1sf || !L->w3sf || !L->w2sf) return LL_ERR_ARG;
+    auto cw = [](const uint8_t* p) { return const_cast<uint8_t*>(p); };
+    LL_TRY(launch_prepare_sfa(L->w1s, L->s13_stride, E, f, d, cw(L->w1sf), s));
+    LL_TRY(launch_prepare_sfa(L->w3s, L->s13_stride, E, f, d, cw(L->w3sf), s));
+    LL_TRY(launch_prepare_sfa(L->w2s, L->s2_stride, E, d, f, cw(L->w2sf), s));
+  }
   if (n_t == 0) return LL_OK;                 // forward-only use: no transposed copies
   auto cw = [](const uint8_t* p) { return const_cast<uint8_t*>(p); };
   auto ch = [](const uint16_t* p) { return reinterpret_cast<__half*>(const_cast<uint16_t*>(p)); };
@@ -538,6 +571,11 @@ int ll_moe_prepare(const ll_moe_layer* L, int32_t* beta_out, void* stream) {
   LL_TRY(launch_transpose_mxfp4(L->w3p, L->w3s, L->s13_stride, E, f, d, beta_out, 0, cw(L->w3t), ch(L->s3t), s));
   LL_TRY(launch_transpose_mxfp4(L->w2p, L->w2s, L->s2_stride, E, d, f, beta_out, 1, cw(L->w2t), ch(L->s2t), s));
   return LL_OK;
+}
+
+size_t ll_mxfp4_sf_bytes(int E, int R, int C) {
+  if (E <= 0 || R <= 0 || C <= 0 || R % 128 || C % 128) return 0;
+  return (size_t)E * R * C / 32;
 }
 
 size_t ll_moe_workspace_bytes(const ll_moe_layer* L, int T, int k) {
@@ -568,12 +606,43 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   k_scatter<<<nblk, 256, kTokBlock * k * sizeof(int), s>>>(idx, w, T, k, E, W.cnt, W.perm_token, W.perm_slot,
                                                             W.pair_pos, W.tw, W.tok_pos);
   LL_TRY(check_launch("k_scatter"));
-  LL_TRY(launch_token_rows_to_half(x, x_dtype, W.perm_token, W.tok_pos, T, k, d, W.xh, W.xinv, s));
+  // Tiles up to 64 rows: the forward GEMMs run on the block-scaled MMA (E4M3 activation terms,
+  // weights not decoded); 128-row tiles (the large-T regime) on the fp16 dequant path.
+  const bool bs = W.nmax <= 64;
+  if (bs)
+    LL_TRY(launch_rows_to_e4m3x3(x, x_dtype, T, W.tok_pos, k, nullptr, d, P, W.xq, W.xinv3, s));
+  else
+    LL_TRY(launch_token_rows_to_half(x, x_dtype, W.perm_token, W.tok_pos, T, k, d, W.xh, W.xinv, s));
   LL_TRY(skinny(x, x_dtype, true, T, d, L->A_g, L->A_u, r, 2 * r, 1.f, W.xa_g, W.xa_u, W.skpart, W.skpart_floats, s));
   LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_g, L->B_g, nullptr, nullptr, W.dlt_g, s));
   LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_u, L->B_u, nullptr, nullptr, W.dlt_u, s));
   // F1: gate / up
-  {
+  if (bs) {
+    CUtensorMap a[2], b[4];
+    LL_TRY(make_fp4_map(&a[0], L->w1p, (int64_t)E * f, d, 128));
+    LL_TRY(make_fp4_map(&a[1], L->w3p, (int64_t)E * f, d, 128));
+    LL_TRY(make_e4m3x3_maps(b, W.nmax / 16, W.xq, P, d));
+    BsArgs a1{};
+    a1.chunks = W.chunks;
+    a1.n_chunks = W.n_chunks;
+    a1.mtiles = f / 128;
+    a1.K = d;
+    a1.e_rows = f;
+    a1.sfa[0] = L->w1sf;
+    a1.sfa[1] = L->w3sf;
+    a1.inv3 = W.xinv3;
+    a1.prefetch = bs_prefetch_stages();
+    a1.status = W.st;
+    a1.epi.perm_token = W.perm_token;
+    a1.epi.P = P;
+    a1.epi.M = f;
+    a1.epi.delta_g = W.dlt_g;
+    a1.epi.delta_u = W.dlt_u;
+    a1.epi.G = W.G;
+    a1.epi.U = W.U;
+    a1.epi.H = W.H;
+    LL_TRY(bs_nmax<EPI_F1>(W.nmax, a, b, a1, s));
+  } else {
     CUtensorMap pk[2], sc[2], act[8];
     LL_TRY(make_rowscale_maps(&pk[0], &sc[0], L->w1p, L->w1s, (int64_t)E * f, d, L->s13_stride));
     LL_TRY(make_rowscale_maps(&pk[1], &sc[1], L->w3p, L->w3s, (int64_t)E * f, d, L->s13_stride));
@@ -606,8 +675,30 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
     k_q<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(W.tok_pos, W.tw, W.z, T, k, r, W.q);
     LL_TRY(check_launch("k_q"));
   }
-  // F2: down
-  {
+  // F2: down (paired 128-row tiles of the stack: d a multiple of 256)
+  if (bs && d % 256 == 0) {
+    LL_TRY(launch_rows_to_e4m3x3(W.H, 2, P, nullptr, 0, n_valid, f, P, W.hq, W.hinv3, s));
+    CUtensorMap a[2], b[4];
+    LL_TRY(make_fp4_map(&a[0], L->w2p, (int64_t)E * d, f, 256));
+    a[1] = a[0];
+    LL_TRY(make_e4m3x3_maps(b, W.nmax / 16, W.hq, P, f));
+    BsArgs a2{};
+    a2.chunks = W.chunks;
+    a2.n_chunks = W.n_chunks;
+    a2.mtiles = d / 256;
+    a2.K = f;
+    a2.e_rows = d;
+    a2.sfa[0] = a2.sfa[1] = L->w2sf;
+    a2.inv3 = W.hinv3;
+    a2.prefetch = bs_prefetch_stages();
+    a2.status = W.st;
+    a2.epi.perm_token = W.perm_token;
+    a2.epi.tw = W.tw;
+    a2.epi.P = P;
+    a2.epi.M = d;
+    a2.epi.Y = W.Y;
+    LL_TRY(bs_nmax<EPI_F2>(W.nmax, a, b, a2, s));
+  } else {
     CUtensorMap pk[2], sc[2], act[8];
     LL_TRY(make_rowscale_maps(&pk[0], &sc[0], L->w2p, L->w2s, (int64_t)E * d, f, L->s2_stride, 256));
     pk[1] = pk[0];

@@ -27,4 +27,19 @@ int launch_rows_to_half(const void* src, int src_dtype, const int* index, int ro
 int launch_token_rows_to_half(const void* src, int src_dtype, const int* perm_token, const int* tok_pos, int T, int k,
                               int K, __half* dst, float* inv, cudaStream_t s);
 
+// The block-scaled MMA's weight scales of a stack of MXFP4 matrices W[E][R][C] (R % 128 == 0,
+// C % 128 == 0): for every 128-row tile and 128-K stage, a 512-byte block of 32 lines x 16
+// bytes, line l holding the 4 scale bytes of rows l, l + 32, l + 64, l + 96 (the layout
+// tcgen05.cp copies into tensor memory); bytes >= 253 become 0. out: E * R * C / 32 bytes.
+int launch_prepare_sfa(const uint8_t* scales, int64_t sstride, int E, int R, int C, uint8_t* out, cudaStream_t s);
+
+// Rows as three E4M3 terms ([3][rows][K] bytes) with their inverse power-of-two scales
+// ([3][rows] floats): per row, term t is the nearest E4M3 values of (x - earlier terms) * 2^e_t,
+// e_t bringing that residual's largest entry into [2^7, 2^8). tok_pos given: source rows are
+// the T tokens and each is written to its pair positions tok_pos[t][0..k) (-1 skipped);
+// otherwise source row p -> row p for p < *n_valid (n_valid may be null: all rows).
+// src_dtype: 0 fp32, 1 bf16, 2 fp16. K % 8 == 0, K <= 8192.
+int launch_rows_to_e4m3x3(const void* src, int src_dtype, int src_rows, const int* tok_pos, int k,
+                          const int* n_valid, int K, int64_t P, uint8_t* dst, float* inv3, cudaStream_t s);
+
 }  // namespace ll

@@ -62,6 +62,10 @@ class RoutedExpertsLayer:
         self.A_u, self.B_u = A_u.float().contiguous(), B_u.float().contiguous()
         self.A_d, self.B_d = A_d.float().contiguous(), B_d.float().contiguous()
         self.beta = torch.zeros((E, 2), dtype=torch.int32, device=w1p.device)
+        # the forward GEMMs' weight scales, laid out for the block-scaled MMA by ll_moe_prepare
+        sf = lambda R, C: torch.empty(int(self.lib.ll_mxfp4_sf_bytes(E, R, C)), dtype=torch.uint8,
+                                      device=w1p.device)
+        self.w1sf, self.w3sf, self.w2sf = sf(f, d), sf(f, d), sf(d, f)
         self.w1t = self.w3t = self.w2t = self.s1t = self.s3t = self.s2t = None
         self._tbufs = transposed
         self.desc = L.MoELayerDesc()
@@ -113,6 +117,7 @@ class RoutedExpertsLayer:
         D.w2p, D.w2s = self.w2p.data_ptr(), self.w2s.data_ptr()
         D.s13_stride, D.s2_stride = self.w1s.shape[-1], self.w2s.shape[-1]
         D.beta = self.beta.data_ptr()
+        D.w1sf, D.w3sf, D.w2sf = self.w1sf.data_ptr(), self.w3sf.data_ptr(), self.w2sf.data_ptr()
         D.A_g, D.B_g, D.A_u, D.B_u = self.A_g.data_ptr(), self.B_g.data_ptr(), self.A_u.data_ptr(), self.B_u.data_ptr()
         D.A_d, D.B_d = self.A_d.data_ptr(), self.B_d.data_ptr()
         for name in TRANSPOSED:
