@@ -534,7 +534,7 @@ def run_decode(args, cfg, rank, local, world, dist):
     dev = torch.device("cuda", local)
     lib = L.load()
     inp = make_layer_device(cfg, device=dev, with_grad=False)
-    layer = RoutedExpertsLayer.from_inputs(inp, cfg.scaling, device=dev)
+    layer = RoutedExpertsLayer.from_inputs(inp, cfg.scaling, device=dev, prepare_backward=False)
     router = KimiK3MoERouter(hidden_size=cfg.d, num_experts=cfg.E, top_k=cfg.k, device=dev)
     x = inp["x"].to(torch.bfloat16).contiguous()
     Wr, br = inp["router_w"], inp["router_b"]
@@ -553,6 +553,26 @@ def run_decode(args, cfg, rank, local, world, dist):
     for _ in range(args.warmup):
         step()
     layer.check_status(cfg.T, cfg.k)
+    # per-kernel breakdown (untimed, eager launches, L2 flushed first): an event after every launch
+    breakdown = {}
+    nb = 5
+    for _ in range(nb):
+        flush.fill_(1)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(64)]
+        for e in evs:
+            e.record(stream)
+        t0 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        lib.ll_profile_launch_events((L.c_void_p * 64)(*[e.cuda_event for e in evs]), 64)
+        step()
+        nrec = lib.ll_profile_launch_recorded()
+        names_rec = [lib.ll_profile_launch_name(i).decode() for i in range(nrec)]
+        lib.ll_profile_launch_events(None, 0)
+        torch.cuda.synchronize()
+        prev = t0
+        for i, nm in enumerate(names_rec):
+            breakdown[nm] = breakdown.get(nm, 0.0) + prev.elapsed_time(evs[i]) * 1e3 / nb
+            prev = evs[i]
     run = step
     if args.graph:
         gr = torch.cuda.CUDAGraph()
@@ -592,7 +612,10 @@ def run_decode(args, cfg, rank, local, world, dist):
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                          "peak_kind": peak_kind, "algorithmic_bytes_per_step": wbytes,
                          "roofline_us": wbytes / (hbm_peak * 1e9) * 1e6},
-            "gpu_launches": state["n"] * args.steps, "clocks": clk.summary()}
+            "gpu_launches": state["n"] * args.steps, "clocks": clk.summary(),
+            "kernel_breakdown_us": {"source": f"CUDA events after every launch of the library, eager launches, "
+                                              f"L2 flushed before each step, mean of {nb} untimed steps",
+                                    **{k: round(v, 1) for k, v in sorted(breakdown.items(), key=lambda kv: -kv[1])}}}
     print(json.dumps(line), flush=True)
 
 

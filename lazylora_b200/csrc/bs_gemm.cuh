@@ -21,9 +21,10 @@
 //
 // Work units are (chunk of <= N_MAX rows of one expert, m-tile) as in grouped_gemm.cuh, with two
 // weight tiles per unit (gate and up for F1; two adjacent 128-row tiles of one stack for F2).
-// Warp roles (6 warps): 0 TMA producer (weights, activations, scale blocks of a stage on one
+// Warp roles (7 warps): 0 TMA producer (weights, activations, scale blocks of a stage on one
 // mbarrier), 1 MMA issuer (tcgen05.cp of the stage's scales, then 4 K-steps x 2 tiles of MMAs,
-// one commit releasing the stage), 2..5 epilogue (one TMEM lane quarter each). Accumulators are
+// one commit releasing the stage), 2..5 epilogue (one TMEM lane quarter each), 6 watcher (waits
+// on the mbarriers the issuer depends on and publishes a count it polls). Accumulators are
 // double-buffered when tensor memory allows, so the epilogue of a unit overlaps the next unit's
 // MMAs. Every wait is bounded (see common.cuh).
 #pragma once
@@ -49,8 +50,8 @@ struct BsArgs {
 
 template <int NMAT, int N_MAX>
 struct BsCfg {
-  static constexpr int kThreads = 6 * 32;
-  static constexpr int kEpWarp0 = 2, kEpWarps = 4;
+  static constexpr int kThreads = 7 * 32;
+  static constexpr int kEpWarp0 = 2, kEpWarps = 4, kWatchWarp = 6;
   static constexpr int BN = kBsTerms * N_MAX;            // MMA N of a full chunk
   static constexpr int A_TILE = 128 * 128;               // shared bytes of a 128 x 128-K weight tile
   static constexpr int A_TX = 128 * 64;                  // its transaction (packed global) bytes
@@ -63,7 +64,7 @@ struct BsCfg {
   static constexpr int OFF_SFB = S * STAGE;              // 512 bytes of 0x7f: every B scale 1.0
   static constexpr int OFF_BAR = OFF_SFB + kBsSfBlock;
   static constexpr int N_BARS = 2 * S + 5;
-  static constexpr int SMEM = OFF_BAR + N_BARS * 8 + 16 + 1024;
+  static constexpr int SMEM = OFF_BAR + N_BARS * 8 + 32 + 1024;
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
   // tensor memory: accumulators [buffer][tile][BN], then a scale slot (4 columns: 128 rows) per
   // stage and tile, then the constant B scale slot (8 columns: B rows up to 256)
@@ -103,6 +104,7 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX> tm, const BsArg
   uint64_t* drain = accempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint32_t* ready_seq = tmem_slot + 2;      // events the watcher has seen complete (see below)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -116,6 +118,7 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX> tm, const BsArg
     for (int i = 0; i < 2; i++) { mbar_init(&accfull[i], 1); mbar_init(&accempty[i], C::kEpWarps); }
     mbar_init(drain, 1);
     *abort_flag = 0;
+    *ready_seq = 0;
     fence_barrier_init();
   }
   if (threadIdx.x < kBsSfBlock / 4) reinterpret_cast<uint32_t*>(smem + C::OFF_SFB)[threadIdx.x] = 0x7f7f7f7fu;
@@ -193,17 +196,21 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX> tm, const BsArg
       // B rows 0..127 and 128..255 (an MMA of N > 128 reads the second block)
       tmem_cp_32x128b_x4(tmem + C::SFB_BASE, umma_desc(smem_u32(smem + C::OFF_SFB), 128, 128, kSwizzleNone));
       tmem_cp_32x128b_x4(tmem + C::SFB_BASE + 4, umma_desc(smem_u32(smem + C::OFF_SFB), 128, 128, kSwizzleNone));
+      // The issuer never waits on an mbarrier (a wait in the thread that issues tcgen05.mma
+      // stalls its MMA stream by hundreds of cycles): the watcher warp waits for each event (an
+      // accumulator buffer drained, a stage's bytes landed) in the order the issuer needs them
+      // and counts them in ready_seq, which the issuer polls.
       int s = 0, ab = 0;
-      uint32_t ph = 0, abph = 0;
+      uint32_t ev = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const Chunk ch = args.chunks[u / args.mtiles];
         const int npad = (ch.n + 15) & ~15;
         const uint32_t n_mma = kBsTerms * npad;
-        if (!(ok = mbar_wait(&accempty[ab], abph ^ 1, abort_flag, st, 23))) break;
+        if (!(ok = seq_wait(ready_seq, ++ev, abort_flag, st, 23))) break;
         tc_fence_after();
         for (int ks = 0; ks < n_stage; ks++) {
-          if (!(ok = mbar_wait(&full[s], ph, abort_flag, st, 24))) break;
+          if (!(ok = seq_wait(ready_seq, ++ev, abort_flag, st, 24))) break;
           tc_fence_after();
           uint8_t* stage = smem + s * C::STAGE;
           const uint32_t a0 = smem_u32(stage), b0 = smem_u32(stage + NMAT * C::A_TILE);
@@ -225,15 +232,35 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX> tm, const BsArg
             }
           }
           mma_commit(&empty[s]);                 // stage (and its scale slots) free once these finish
-          if (++s == C::S) { s = 0; ph ^= 1; }
+          if (++s == C::S) s = 0;
         }
         if (!ok) break;
         mma_commit(&accfull[ab]);
-        if (++ab == C::NACC) { ab = 0; abph ^= 1; }
+        if (++ab == C::NACC) ab = 0;
       }
       mma_commit(drain);                         // completes once every MMA issued above finished
       volatile int keep_waiting = 0;             // wait for them even after an abort
       mbar_wait_sleep(drain, 0, &keep_waiting, st, 25, 256);
+    }
+    __syncwarp();
+  } else if (warp == C::kWatchWarp) {
+    // ---------------------------------------------------------------------- watcher
+    // The issuer's events in its order: per unit, its accumulator buffer drained by the
+    // epilogue, then each stage's bytes landed. Bounded waits; after an abort the count still
+    // advances (the issuer sees the abort flag and stops).
+    if (lane == 0) {
+      int s = 0, ab = 0;
+      uint32_t ph = 0, abph = 0, ev = 0;
+      for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+        mbar_wait(&accempty[ab], abph ^ 1, abort_flag, st, 27);
+        seq_publish(ready_seq, ++ev);
+        for (int ks = 0; ks < n_stage; ks++) {
+          mbar_wait(&full[s], ph, abort_flag, st, 28);
+          seq_publish(ready_seq, ++ev);
+          if (++s == C::S) { s = 0; ph ^= 1; }
+        }
+        if (++ab == C::NACC) { ab = 0; abph ^= 1; }
+      }
     }
     __syncwarp();
   } else {

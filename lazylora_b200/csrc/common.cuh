@@ -118,6 +118,32 @@ LL_DEV bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort_
   }
 }
 
+// A monotonic event counter in shared memory, published by one thread and polled by another:
+// release / acquire at CTA scope carry the publisher's observations (e.g. an mbarrier phase it
+// waited for) to the poller.
+LL_DEV void seq_publish(uint32_t* seq, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(seq)), "r"(v) : "memory");
+}
+LL_DEV uint32_t seq_read(uint32_t* seq) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(seq)) : "memory");
+  return v;
+}
+// Bounded poll until *seq >= target; false after a timeout (recorded) or another role's abort.
+LL_DEV bool seq_wait(uint32_t* seq, uint32_t target, volatile int* abort_flag, DevStatus* st, int where) {
+  if (seq_read(seq) >= target) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (seq_read(seq) >= target) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      *abort_flag = 1;
+      report(st, LL_ERR_TIMEOUT, where, 0);
+      return false;
+    }
+  }
+}
+
 // Named barriers (bar.sync / bar.arrive): warp-granular, all 32 lanes of a warp execute them.
 LL_DEV void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

@@ -434,11 +434,12 @@ static int gemm_nmax(int nmax, const CUtensorMap* pk, const CUtensorMap* sc, con
 }
 
 // Stages the block-scaled GEMMs prefetch weight tiles into L2 ahead of their loads
-// (LL_BS_PREFETCH_STAGES overrides the default, for tuning).
+// (LL_BS_PREFETCH_STAGES, for tuning; off by default: measured slower at 4, 8 and 16 stages
+// on configs[1], the prefetches competing with the loads for L2).
 static int bs_prefetch_stages() {
   static const int v = [] {
     const char* e = getenv("LL_BS_PREFETCH_STAGES");
-    return e ? atoi(e) : 8;
+    return e ? atoi(e) : 0;
   }();
   return v;
 }

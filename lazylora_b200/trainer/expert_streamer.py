@@ -224,6 +224,13 @@ def _local_ids(idx: torch.Tensor, group: List[int], num_experts: int) -> torch.T
     return torch.where(idx >= 0, lut[safe], idx)
 
 
+def _group_rows_hint(idx: torch.Tensor, group: List[int], ids: Sequence[int]) -> int:
+    """Routed slots a group's layer sees, estimated without reading the routing back: the
+    layer's T * k slots spread evenly over its active experts (it sets the token-tile width;
+    forward and backward compute the same value)."""
+    return max(1, round(idx.numel() * len(group) / max(1, len(ids))))
+
+
 def streamed_forward(streamer: ExpertStreamer, layer_idx: int, x: torch.Tensor, idx: torch.Tensor,
                      w: torch.Tensor, expert_ids: Optional[Sequence[int]] = None):
     """out [T, d] of one layer, its experts streamed group by group. Returns (out, staged)
@@ -232,7 +239,7 @@ def streamed_forward(streamer: ExpertStreamer, layer_idx: int, x: torch.Tensor, 
     ids = expert_ids if expert_ids is not None else torch.unique(idx[idx >= 0]).tolist()
     out = None
     for g, layer in streamer.stream_layer(layer_idx, ids):
-        o = layer.forward(x, _local_ids(idx, g, E), w)
+        o = layer.forward(x, _local_ids(idx, g, E), w, rows_hint=_group_rows_hint(idx, g, ids))
         out = o if out is None else out.add_(o)
     if out is None:
         out = torch.zeros((x.shape[0], x.shape[1]), dtype=torch.float32, device=x.device)
@@ -246,7 +253,7 @@ def streamed_backward(streamer: ExpertStreamer, layer_idx: int, x: torch.Tensor,
     grad_h = grad_w = grads = None
     for grp, layer in streamer.stream_layer(layer_idx, expert_ids):
         li = _local_ids(idx, grp, E)
-        gh, gw, gr = layer.backward(x, li, w, g)
+        gh, gw, gr = layer.backward(x, li, w, g, rows_hint=_group_rows_hint(idx, grp, expert_ids))
         if grad_h is None:
             grad_h, grad_w, grads = gh, gw, gr
         else:

@@ -104,11 +104,11 @@ class RoutedExpertsLayer:
         L.check(self.lib.ll_moe_prepare(ctypes.byref(self.desc), self.beta.data_ptr(), L.stream_ptr()), "ll_moe_prepare")
 
     @classmethod
-    def from_inputs(cls, inp: Dict[str, torch.Tensor], lora_scaling: float, device="cuda"):
+    def from_inputs(cls, inp: Dict[str, torch.Tensor], lora_scaling: float, device="cuda", **kw):
         t = {k: v.to(device) for k, v in inp.items() if k in (
             "w1p", "w1s", "w3p", "w3s", "w2p", "w2s", "A_g", "B_g", "A_u", "B_u", "A_d", "B_d")}
         return cls(t["w1p"], t["w1s"], t["w3p"], t["w3s"], t["w2p"], t["w2s"], t["A_g"], t["B_g"],
-                   t["A_u"], t["B_u"], t["A_d"], t["B_d"], lora_scaling)
+                   t["A_u"], t["B_u"], t["A_d"], t["B_d"], lora_scaling, **kw)
 
     def _fill_desc(self):
         D = self.desc
@@ -173,8 +173,9 @@ class RoutedExpertsLayer:
         self._ws_key = (x.data_ptr(), idx.data_ptr(), w.data_ptr(), T, k)
         return out
 
-    def backward(self, x, idx, w, g, forward_done: bool = None):
-        """(grad_h [T,d], grad_w [T,k], {dA_g, dB_g, dA_u, dB_u, dA_d, dB_d}), all fp32."""
+    def backward(self, x, idx, w, g, forward_done: bool = None, rows_hint: Optional[int] = None):
+        """(grad_h [T,d], grad_w [T,k], {dA_g, dB_g, dA_u, dB_u, dA_d, dB_d}), all fp32.
+        rows_hint: as given to the forward (used when the forward is recomputed here)."""
         L.require_cuda(x, idx, w, g)
         x = x.contiguous()
         idx = idx.to(torch.int64).contiguous()
@@ -185,7 +186,7 @@ class RoutedExpertsLayer:
         if forward_done is None:
             forward_done = self._ws_key == key
         if not forward_done:        # the workspace does not hold this forward: recompute it
-            self.forward(x, idx, w)
+            self.forward(x, idx, w, rows_hint=rows_hint)
         self.prepare_backward()
         ws = self.workspace(T, k)
         dev = x.device
