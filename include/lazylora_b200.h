@@ -100,6 +100,16 @@ int ll_route_topk(const void* x, int x_dtype, const float* router_w, const float
                   int64_t* idx, float* w, float* scores_out /* optional [T,E] */,
                   void* ws, size_t ws_bytes, void* stream);
 
+/* The router weight is frozen during LoRA training, so its split into the three bf16 planes
+ * the logits read can be made once: ll_route_prepare writes planes [3][E][d] (bf16, 16-byte
+ * aligned), and ll_route_topk_prepared is ll_route_topk reading them instead of router_w
+ * (same results bit for bit). Redo the split whenever the weight changes. */
+int ll_route_prepare(const float* router_w, int E, int d, uint16_t* planes, void* stream);
+int ll_route_topk_prepared(const void* x, int x_dtype, const uint16_t* planes, const float* bias,
+                           int T, int d, int E, int k, int renormalize, float routed_scaling_factor,
+                           int64_t* idx, float* w, float* scores_out /* optional [T,E] */,
+                           void* ws, size_t ws_bytes, void* stream);
+
 /* The selection half alone (moe_router.py:92-99) from given fp32 scores / scores_for_choice:
  * bit-exact indices and weights for identical inputs. */
 int ll_route_select(const float* scores, const float* scores_for_choice, int T, int E, int k,

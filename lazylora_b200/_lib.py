@@ -62,6 +62,9 @@ _SIGS = {
     "ll_route_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "ll_route_topk": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float,
                               c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "ll_route_prepare": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "ll_route_topk_prepared": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float,
+                                       c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "ll_route_select": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_void_p, c_void_p,
                                 c_void_p]),
     "ll_moe_prepare": (c_int, [ctypes.POINTER(MoELayerDesc), c_void_p, c_void_p]),

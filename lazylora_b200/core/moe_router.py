@@ -1,7 +1,8 @@
 """
 KimiK3MoERouter on the B200: same constructor and forward contract as
 lazy_lora/core/moe_router.py:23-135, with the logits, sigmoid, biased top-k selection,
-gather and renormalisation done by the library's router kernels (ll_route_topk).
+gather and renormalisation done by the library's router kernels (ll_route_topk_prepared; the
+frozen weight's split into bf16 planes, ll_route_prepare, is kept between calls).
 
 Ties in the selection go to the lower expert id. torch's CPU topk leaves the order of equal
 values unspecified, so on inputs with exact ties the order (not the set) may differ.
@@ -28,6 +29,7 @@ class KimiK3MoERouter(torch.nn.Module):
         self.renormalize = renormalize
         self.use_bias = use_bias
         self._ws = None
+        self._planes = None         # (key of the weight split, bf16 planes [3][E][d])
 
     def forward(self, x: torch.Tensor, weight: Optional[torch.Tensor] = None,
                 bias: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -40,18 +42,27 @@ class KimiK3MoERouter(torch.nn.Module):
         if xf.dtype not in (torch.float32, torch.bfloat16):
             xf = xf.float()
         xf = xf.contiguous()
-        w = weight.detach().to(torch.float32).contiguous()
         b = None if bias is None else bias.detach().to(torch.float32).contiguous()
         T, E, k = xf.shape[0], self.num_experts, self.top_k
         nbytes = lib.ll_route_workspace_bytes(T, self.hidden_size, E)
         if self._ws is None or self._ws.numel() < nbytes or self._ws.device != xf.device:
             self._ws = torch.empty(nbytes, dtype=torch.uint8, device=xf.device)
+        # the (frozen) weight's bf16 planes, split once and again only when the weight changes
+        key = (weight.data_ptr(), weight._version, weight.dtype, tuple(weight.shape), weight.device)
+        if self._planes is None or self._planes[0] != key:
+            w = weight.detach().to(torch.float32).contiguous()
+            planes = torch.empty((3, E, self.hidden_size), dtype=torch.bfloat16, device=w.device)
+            L.check(lib.ll_route_prepare(w.data_ptr(), E, self.hidden_size, planes.data_ptr(), L.stream_ptr()),
+                    "ll_route_prepare")
+            self._planes = (key, planes)
+        planes = self._planes[1]
         idx = torch.empty((T, k), dtype=torch.int64, device=xf.device)
         tw = torch.empty((T, k), dtype=torch.float32, device=xf.device)
-        L.check(lib.ll_route_topk(xf.data_ptr(), 0 if xf.dtype == torch.float32 else 1, w.data_ptr(), L.ptr(b),
-                                  T, self.hidden_size, E, k, int(self.renormalize), float(self.routed_scaling_factor),
-                                  idx.data_ptr(), tw.data_ptr(), None, self._ws.data_ptr(), nbytes, L.stream_ptr()),
-                "ll_route_topk")
+        L.check(lib.ll_route_topk_prepared(xf.data_ptr(), 0 if xf.dtype == torch.float32 else 1, planes.data_ptr(),
+                                           L.ptr(b), T, self.hidden_size, E, k, int(self.renormalize),
+                                           float(self.routed_scaling_factor), idx.data_ptr(), tw.data_ptr(), None,
+                                           self._ws.data_ptr(), nbytes, L.stream_ptr()),
+                "ll_route_topk_prepared")
         return idx, tw
 
     @staticmethod

@@ -177,13 +177,19 @@ static int launch_router_mma(const RouterMaps& maps, float* part, int T, int E, 
   return check_launch("k_router_mma");
 }
 
-static int router_logits_tc(const void* x, int x_dtype, const float* W, int T, int d, int E, void* ws,
-                            const RouterPlan& p, cudaStream_t s) {
+// planes: the router weight split into its three bf16 planes (hi, lo, lo2; [3][E][d]), or null
+// to split W into the workspace on this call.
+static int router_logits_tc(const void* x, int x_dtype, const float* W, const __nv_bfloat16* planes, int T, int d,
+                            int E, void* ws, const RouterPlan& p, cudaStream_t s) {
   uint8_t* base = static_cast<uint8_t*>(ws);
-  __nv_bfloat16* wp = reinterpret_cast<__nv_bfloat16*>(base + p.off_w);
   const int64_t nw = (int64_t)E * d;
-  k_split_bf16x3<<<148 * 4, 256, 0, s>>>(W, wp, wp + nw, wp + 2 * nw, nw);
-  LL_TRY(check_launch("k_split_bf16x3"));
+  const __nv_bfloat16* wp = planes;
+  if (!wp) {
+    __nv_bfloat16* split = reinterpret_cast<__nv_bfloat16*>(base + p.off_w);
+    k_split_bf16x3<<<148 * 4, 256, 0, s>>>(W, split, split + nw, split + 2 * nw, nw);
+    LL_TRY(check_launch("k_split_bf16x3"));
+    wp = split;
+  }
   const __nv_bfloat16* xp[3] = {static_cast<const __nv_bfloat16*>(x), nullptr, nullptr};
   if (p.NP == 3) {
     __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(base + p.off_x);
@@ -222,17 +228,18 @@ size_t ll_route_workspace_bytes(int T, int d, int E) {
   return router_plan(T, d, E, 0).bytes;     // fp32 activations need the most (their planes)
 }
 
-int ll_route_topk(const void* x, int x_dtype, const float* router_w, const float* bias, int T, int d, int E, int k,
-                  int renormalize, float routed_scaling_factor, int64_t* idx, float* w, float* scores_out, void* ws,
-                  size_t ws_bytes, void* stream) {
+static int route_topk(const void* x, int x_dtype, const float* router_w, const __nv_bfloat16* planes,
+                      const float* bias, int T, int d, int E, int k, int renormalize, float routed_scaling_factor,
+                      int64_t* idx, float* w, float* scores_out, void* ws, size_t ws_bytes, void* stream) {
   if (T <= 0 || d <= 0 || E <= 0 || k <= 0 || k > 32 || k > E || E > 2048 || d % 8) return LL_ERR_ARG;
-  if (!x || !router_w || !idx || !w || !ws || (x_dtype != 0 && x_dtype != 1)) return LL_ERR_ARG;
+  if (!x || (!router_w && !planes) || !idx || !w || !ws || (x_dtype != 0 && x_dtype != 1)) return LL_ERR_ARG;
   if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(ws) % 256) return LL_ERR_ARG;
+  if (planes && reinterpret_cast<uintptr_t>(planes) % 16) return LL_ERR_ARG;
   const RouterPlan p = router_plan(T, d, E, x_dtype);
   if (ws_bytes < p.bytes) return LL_ERR_WORKSPACE;
   LL_STREAM(stream);
   g_launch_count = 0;
-  LL_TRY(router_logits_tc(x, x_dtype, router_w, T, d, E, ws, p, s));
+  LL_TRY(router_logits_tc(x, x_dtype, router_w, planes, T, d, E, ws, p, s));
   const float* part = reinterpret_cast<const float*>(static_cast<uint8_t*>(ws) + p.off_part);
   if (p.nsplit > 1) {   // the K splits' partials, summed in split order by a wide kernel
     float* logits = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + p.off_logits);
@@ -242,6 +249,30 @@ int ll_route_topk(const void* x, int x_dtype, const float* router_w, const float
     part = logits;
   }
   return launch_select<0>(part, nullptr, bias, T, E, k, renormalize, routed_scaling_factor, idx, w, scores_out, s, 1);
+}
+
+int ll_route_topk(const void* x, int x_dtype, const float* router_w, const float* bias, int T, int d, int E, int k,
+                  int renormalize, float routed_scaling_factor, int64_t* idx, float* w, float* scores_out, void* ws,
+                  size_t ws_bytes, void* stream) {
+  return route_topk(x, x_dtype, router_w, nullptr, bias, T, d, E, k, renormalize, routed_scaling_factor, idx, w,
+                    scores_out, ws, ws_bytes, stream);
+}
+
+int ll_route_prepare(const float* router_w, int E, int d, uint16_t* planes, void* stream) {
+  if (!router_w || !planes || E <= 0 || d <= 0 || d % 8 || reinterpret_cast<uintptr_t>(planes) % 16) return LL_ERR_ARG;
+  LL_STREAM(stream);
+  g_launch_count = 0;
+  __nv_bfloat16* wp = reinterpret_cast<__nv_bfloat16*>(planes);
+  const int64_t nw = (int64_t)E * d;
+  k_split_bf16x3<<<148 * 4, 256, 0, s>>>(router_w, wp, wp + nw, wp + 2 * nw, nw);
+  return check_launch("k_split_bf16x3");
+}
+
+int ll_route_topk_prepared(const void* x, int x_dtype, const uint16_t* planes, const float* bias, int T, int d, int E,
+                           int k, int renormalize, float routed_scaling_factor, int64_t* idx, float* w,
+                           float* scores_out, void* ws, size_t ws_bytes, void* stream) {
+  return route_topk(x, x_dtype, nullptr, reinterpret_cast<const __nv_bfloat16*>(planes), bias, T, d, E, k,
+                    renormalize, routed_scaling_factor, idx, w, scores_out, ws, ws_bytes, stream);
 }
 
 int ll_route_select(const float* scores, const float* scores_for_choice, int T, int E, int k, int renormalize,

@@ -131,3 +131,50 @@ def test_router_fixture(golden_dir):
     assert sorted(got) == sorted(want)
     for key in want:
         assert abs(got[key] - want[key]) <= 1e-5 + 1e-4 * abs(want[key])
+
+
+def test_router_prepared_planes_bit_exact():
+    """The weight split made once (ll_route_prepare) and reused (ll_route_topk_prepared) routes
+    exactly as the per-call split (ll_route_topk), for bf16 and fp32 activations; the router
+    module re-splits when its weight changes."""
+    import ctypes
+    from lazylora_b200 import _lib as L
+    from lazylora_b200.core.moe_router import KimiK3MoERouter
+    lib = L.load()
+    g = torch.Generator().manual_seed(8)
+    T, d, E, k = 40, 7168, 896, 8
+    W = (torch.randn(E, d, generator=g) * 0.02).cuda()
+    b = (torch.randn(E, generator=g) * 0.01).cuda()
+    planes = torch.empty((3, E, d), dtype=torch.bfloat16, device="cuda")
+    assert lib.ll_route_prepare(W.data_ptr(), E, d, planes.data_ptr(), L.stream_ptr()) == 0
+    for xd in (torch.float32, torch.bfloat16):
+        x = torch.randn(T, d, generator=g).cuda().to(xd)
+        code = 0 if xd == torch.float32 else 1
+        nb = lib.ll_route_workspace_bytes(T, d, E)
+        ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+        out = []
+        for prepared in (False, True):
+            idx = torch.empty((T, k), dtype=torch.int64, device="cuda")
+            w = torch.empty((T, k), dtype=torch.float32, device="cuda")
+            if prepared:
+                rc = lib.ll_route_topk_prepared(x.data_ptr(), code, planes.data_ptr(), b.data_ptr(), T, d, E, k, 1,
+                                                ctypes.c_float(1.0), idx.data_ptr(), w.data_ptr(), None, ws.data_ptr(),
+                                                nb, L.stream_ptr())
+            else:
+                rc = lib.ll_route_topk(x.data_ptr(), code, W.data_ptr(), b.data_ptr(), T, d, E, k, 1,
+                                       ctypes.c_float(1.0), idx.data_ptr(), w.data_ptr(), None, ws.data_ptr(), nb,
+                                       L.stream_ptr())
+            assert rc == 0, lib.ll_last_cuda_error()
+            out.append((idx, w))
+        assert torch.equal(out[0][0], out[1][0]) and torch.equal(out[0][1], out[1][1])
+    r = KimiK3MoERouter(hidden_size=d, num_experts=E, top_k=k)
+    x = torch.randn(T, d, generator=g).cuda().to(torch.bfloat16)
+    with torch.no_grad():
+        r.weight.copy_(W)
+        r.bias.copy_(b)
+    i0, _ = r.forward(x)
+    with torch.no_grad():
+        r.weight.mul_(-1.0)                                  # a changed weight is split again
+    i1, _ = r.forward(x)
+    want, _ = KimiK3MoERouter.forward(KimiK3MoERouter(hidden_size=d, num_experts=E, top_k=k), x, weight=-W, bias=b)
+    assert torch.equal(i1, want) and not torch.equal(i0, i1)
