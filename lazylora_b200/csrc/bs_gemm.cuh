@@ -1,39 +1,50 @@
-// Grouped MXFP4 GEMM on the block-scaled tcgen05 MMA (kind::mxf8f6f4), one persistent CTA per
-// SM: the forward GEMMs of the routed-expert layer (gate/up with SiTU-GLU, down).
+// Grouped MXFP4 GEMM on the block-scaled tcgen05 MMAs, one persistent CTA per SM: the forward
+// GEMMs of the routed-expert layer (gate/up with SiTU-GLU, down).
 //
-// The weights are never decoded. Their E2M1 codes go from HBM to shared memory by TMA (the
-// 16 x 4-bit, 16-byte-aligned form the MMA reads: each 8 packed bytes land in 16), their E8M0
-// block-32 scales go into tensor memory (tcgen05.cp from a 512-byte block per 128 rows x 128 K,
-// laid out once per weight load by ll_moe_prepare), and the MMA applies them itself: W row m,
-// K block b contributes code * 2^(scale - 127) exactly. An E8M0 byte >= 253, which the
+// The weights are never decoded. Their E2M1 codes go from HBM to shared memory by TMA and their
+// E8M0 block-32 scales into tensor memory (tcgen05.cp from a 512-byte block per 128 rows x 128
+// K, laid out once per weight load by ll_moe_prepare); the MMA applies the scales itself: W row
+// m, K block b contributes code * 2^(scale - 127) exactly. An E8M0 byte >= 253, which the
 // reference treats as "this group contributes zero", is laid out as byte 0 (2^-127): its
-// products stay below 2^-116 of the activation scale and vanish in the fp32 sums.
+// products vanish in the fp32 sums.
 //
-// The activations (the B operand) are E4M3 and carry no exponent of their own beyond a power
-// of two per row, so a row x is held as three E4M3 terms x = (q0 2^-e0 + q1 2^-e1 + q2 2^-e2):
-// each term the nearest E4M3 values of what the previous terms left, scaled by a power of two
-// that brings the residual's largest entry into [2^7, 2^8). Three terms keep ~12 significant
-// bits of every entry (fp16 keeps 11). The terms are stacked along N: the B tile of a chunk of
-// n rows is [term][npad rows][128 K], so one MMA of N = 3 npad computes all three partial
-// products into adjacent accumulator columns, and the epilogue adds them with their row
-// scales: y[m, j] = sum_t D[m, t npad + j] 2^-e_t(j). The B scale factors are all 1.0 (one
-// constant block in tensor memory for the whole kernel).
+// The activations (the B operand) are a short sum of low-precision terms stacked along N: the B
+// tile of a chunk of n rows is [term][npad rows][K], so one MMA of N = terms * npad computes
+// every term's partial product into adjacent accumulator columns, and the epilogue adds them.
+// Two kinds:
+//   BS_FP4  kind::mxf4 (K = 64 per MMA): the weights stay packed in shared memory (half the
+//           bytes the tensor core reads per weight element), and the activations are four E2M1
+//           terms, each with its own E8M0 scale per 32 K elements (the nearest E2M1 values of
+//           what the earlier terms left, scaled into [-6, 6] block by block); four terms keep an
+//           activation row to ~4e-5 relative. The B scales come per stage from blocks laid out
+//           per chunk (bs_ops.cu). Used for chunks of up to 32 rows.
+//   BS_FP8  kind::mxf8f6f4 (K = 32 per MMA): the weights' codes unpacked to one per byte (TMA
+//           16 x 4-bit 16-byte-aligned form), the activations three E4M3 terms with one
+//           power-of-two scale per row and term (applied in the epilogue; the B scale factors
+//           are a constant 1.0 block). Three terms keep ~12 significant bits. Used for chunks of
+//           up to 64 rows (four E2M1 terms of 64 rows would need 2 x 256 accumulator columns).
 //
 // Work units are (chunk of <= N_MAX rows of one expert, m-tile) as in grouped_gemm.cuh, with two
 // weight tiles per unit (gate and up for F1; two adjacent 128-row tiles of one stack for F2).
 // Warp roles (7 warps): 0 TMA producer (weights, activations, scale blocks of a stage on one
-// mbarrier), 1 MMA issuer (tcgen05.cp of the stage's scales, then 4 K-steps x 2 tiles of MMAs,
-// one commit releasing the stage), 2..5 epilogue (one TMEM lane quarter each), 6 watcher (waits
-// on the mbarriers the issuer depends on and publishes a count it polls). Accumulators are
-// double-buffered when tensor memory allows, so the epilogue of a unit overlaps the next unit's
-// MMAs. Every wait is bounded (see common.cuh).
+// mbarrier), 1 MMA issuer (tcgen05.cp of the stage's scales, then the K-steps x 2 tiles of
+// MMAs, one commit releasing the stage), 2..5 epilogue (one TMEM lane quarter each), 6 watcher
+// (waits on the mbarriers the issuer depends on and publishes a count it polls). Accumulators
+// are double-buffered when tensor memory allows, so the epilogue of a unit overlaps the next
+// unit's MMAs. Every wait is bounded (see common.cuh).
 #pragma once
 #include "grouped_gemm.cuh"
 
 namespace ll {
 
-constexpr int kBsTerms = 3;          // E4M3 terms per activation row
+enum BsKind : int { BS_FP8 = 0, BS_FP4 = 1 };
+
 constexpr int kBsSfBlock = 512;      // scale bytes of 128 rows x 128 K (4 per row), tcgen05.cp layout
+
+template <int KIND>
+struct BsTerms {
+  static constexpr int value = KIND == BS_FP4 ? 4 : 3;
+};
 
 struct BsArgs {
   const Chunk* chunks;
@@ -41,55 +52,71 @@ struct BsArgs {
   int mtiles;                 // units per chunk
   int K;                      // reduction length, a multiple of 128
   int e_rows;                 // weight rows per expert
-  const uint8_t* sfa[2];      // prepared scale blocks [E][e_rows/128][K/128][512] of tile 0 / 1
-  const float* inv3;          // [3][P] 2^-e_t of each activation row's term t
+  const uint8_t* sfa[2];      // prepared weight scale blocks [E][e_rows/128][K/128][512] of tile 0 / 1
+  const uint8_t* sfb;         // BS_FP4: activation scale blocks [chunk][K/128][blocks][512]
+  const float* inv3;          // BS_FP8: [3][P] 2^-e_t of each activation row's term t
   int prefetch;               // stages the L2 prefetch of weight tiles runs ahead of the loads
   DevStatus* status;
   EpiParams epi;
 };
 
-template <int NMAT, int N_MAX>
+template <int NMAT, int N_MAX, int KIND>
 struct BsCfg {
   static constexpr int kThreads = 7 * 32;
   static constexpr int kEpWarp0 = 2, kEpWarps = 4, kWatchWarp = 6;
-  static constexpr int BN = kBsTerms * N_MAX;            // MMA N of a full chunk
-  static constexpr int A_TILE = 128 * 128;               // shared bytes of a 128 x 128-K weight tile
-  static constexpr int A_TX = 128 * 64;                  // its transaction (packed global) bytes
-  static constexpr int B_TILE = BN * 128;
-  static constexpr int STAGE0 = NMAT * A_TILE + B_TILE + NMAT * kBsSfBlock;
+  static constexpr bool FP4 = KIND == BS_FP4;
+  static constexpr int NT = BsTerms<KIND>::value;         // activation terms
+  static constexpr int BN = NT * N_MAX;                   // MMA N of a full chunk
+  static constexpr int KMMA = FP4 ? 64 : 32;              // K per MMA instruction
+  static constexpr int ROWB = FP4 ? 64 : 128;             // shared bytes of one operand row (128 K)
+  static constexpr int A_TILE = 128 * ROWB;               // shared bytes of a 128 x 128-K weight tile
+  static constexpr int A_TX = 128 * 64;                   // its transaction (packed global) bytes
+  static constexpr int B_TILE = BN * ROWB;
+  static constexpr int SFB_BLKS = FP4 ? (BN + 127) / 128 : 0;   // B scale blocks per stage
+  static constexpr int STAGE0 = NMAT * A_TILE + B_TILE + (NMAT + SFB_BLKS) * kBsSfBlock;
   static constexpr int STAGE = (STAGE0 + 1023) / 1024 * 1024;
   static constexpr int S0 = (227 * 1024 - 4096) / STAGE;
-  static constexpr int S = S0 > 8 ? 8 : S0;
+  static constexpr int S = S0 > 10 ? 10 : S0;
   static_assert(S >= 2, "shared memory budget");
-  static constexpr int OFF_SFB = S * STAGE;              // 512 bytes of 0x7f: every B scale 1.0
+  static constexpr int OFF_SFB = S * STAGE;               // BS_FP8: 512 bytes of 0x7f (every B scale 1.0)
   static constexpr int OFF_BAR = OFF_SFB + kBsSfBlock;
   static constexpr int N_BARS = 2 * S + 5;
   static constexpr int SMEM = OFF_BAR + N_BARS * 8 + 32 + 1024;
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
-  // tensor memory: accumulators [buffer][tile][BN], then a scale slot (4 columns: 128 rows) per
-  // stage and tile, then the constant B scale slot (8 columns: B rows up to 256)
+  // tensor memory: accumulators [buffer][tile][BN], the A scale slots (4 columns: 128 rows) per
+  // stage and tile, then the B scale slots (8 columns: B rows up to 256), one per stage (BS_FP4)
+  // or one constant slot (BS_FP8)
   static constexpr int ACC_COLS = NMAT * BN;
-  static constexpr int SF_COLS = S * NMAT * 4 + 8;
+  static constexpr int SFB_SLOTS = FP4 ? S : 1;
+  static constexpr int SF_COLS = S * NMAT * 4 + SFB_SLOTS * 8;
   static_assert(ACC_COLS + SF_COLS <= 512, "tensor memory budget");
   static constexpr int NACC = 2 * ACC_COLS + SF_COLS <= 512 ? 2 : 1;
   static constexpr int SFA_BASE = NACC * ACC_COLS;
   static constexpr int SFB_BASE = SFA_BASE + S * NMAT * 4;
-  static constexpr int TMEM_COLS0 = SFB_BASE + 8;
+  static constexpr int TMEM_COLS0 = SFB_BASE + SFB_SLOTS * 8;
   static constexpr int TMEM_COLS = TMEM_COLS0 <= 32 ? 32 : TMEM_COLS0 <= 64 ? 64 : TMEM_COLS0 <= 128 ? 128
                                    : TMEM_COLS0 <= 256 ? 256 : 512;
   static_assert(N_MAX % 16 == 0 && BN <= 256, "MMA N");
+  static_assert(A_TILE % 1024 == 0 && (16 * ROWB) % 1024 == 0, "1024-byte aligned operand tiles and terms");
 };
 
-template <int NMAT, int N_MAX>
+template <int NMAT, int N_MAX, int KIND>
 struct BsTma {
-  CUtensorMap a[NMAT];          // weight codes, 16 x 4-bit 16-byte-aligned, 128-byte swizzle
-  CUtensorMap b[N_MAX / 16];    // b[c - 1]: [3 terms][16 c rows][128 K] E4M3, 128-byte swizzle
+  CUtensorMap a[NMAT];          // weight codes (BS_FP4 packed, 64-byte swizzle; BS_FP8 unpacked, 128)
+  CUtensorMap b[N_MAX / 16];    // b[c - 1]: [terms][16 c rows][128 K] activation terms
 };
 
-template <int EPI, int NMAT, int N_MAX>
-__global__ void __launch_bounds__(BsCfg<NMAT, N_MAX>::kThreads, 1)
-grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX> tm, const BsArgs args) {
-  using C = BsCfg<NMAT, N_MAX>;
+// UMMA descriptor of a K-major operand tile (rows of ROWB bytes, the swizzle of that width).
+template <int KIND>
+LL_DEV uint64_t bs_desc(uint32_t addr) {
+  return KIND == BS_FP4 ? umma_desc(addr, 16, 512, kSwizzle64B) : umma_desc(addr, 16, 1024, kSwizzle128B);
+}
+
+template <int EPI, int NMAT, int N_MAX, int KIND>
+__global__ void __launch_bounds__(BsCfg<NMAT, N_MAX, KIND>::kThreads, 1)
+grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const BsArgs args) {
+  using C = BsCfg<NMAT, N_MAX, KIND>;
+  constexpr int NT = C::NT;
   static_assert(EPI == EPI_F1 || EPI == EPI_F2 || EPI == EPI_STORE, "epilogue");
   // a single-product epilogue takes two adjacent 128-row tiles of one stack as its two tiles
   constexpr bool PAIR = NMAT == 2 && EPI != EPI_F1;
@@ -121,7 +148,7 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX> tm, const BsArg
     *ready_seq = 0;
     fence_barrier_init();
   }
-  if (threadIdx.x < kBsSfBlock / 4) reinterpret_cast<uint32_t*>(smem + C::OFF_SFB)[threadIdx.x] = 0x7f7f7f7fu;
+  if (!C::FP4 && threadIdx.x < kBsSfBlock / 4) reinterpret_cast<uint32_t*>(smem + C::OFF_SFB)[threadIdx.x] = 0x7f7f7f7fu;
   fence_async_smem();                       // the constant block is read by tcgen05.cp (async proxy)
   if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
   tc_fence_before();
@@ -138,8 +165,10 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX> tm, const BsArg
       int s = 0, issued = 0;
       uint32_t ph = 0;
       bool ok = true;
+      // A x coordinate of a stage: packed bytes (BS_FP4, uint8 map) or 4-bit elements (BS_FP8)
+      constexpr int AX = C::FP4 ? 64 : 128;
       // weight tiles and scale blocks are prefetched into L2 args.prefetch stages ahead of their
-      // loads: the shared-memory ring alone holds too few bytes to cover the DRAM latency
+      // loads (off by default: measured slower on configs[1])
       int pu = blockIdx.x, pks = 0;
       auto prefetch_next = [&]() {
         if (pu >= n_units) return;
@@ -148,7 +177,7 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX> tm, const BsArg
         const int prow = pc.e * args.e_rows + pmt * TILE_ROWS;
         const int ptile = pc.e * tiles128 + pmt * (TILE_ROWS / 128);
 #pragma unroll
-        for (int i = 0; i < (PAIR ? 1 : NMAT); i++) tma_prefetch_l2_2d(&tm.a[i], pks * 128, prow);
+        for (int i = 0; i < (PAIR ? 1 : NMAT); i++) tma_prefetch_l2_2d(&tm.a[i], pks * AX, prow);
 #pragma unroll
         for (int i = 0; i < NMAT; i++)
           bulk_prefetch_l2(PAIR ? args.sfa[0] + ((size_t)(ptile + i) * n_stage + pks) * kBsSfBlock
@@ -157,29 +186,34 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX> tm, const BsArg
       };
       for (int i = 0; i < args.prefetch; i++) prefetch_next();
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-        const Chunk ch = args.chunks[u / args.mtiles];
+        const int ci = u / args.mtiles;
+        const Chunk ch = args.chunks[ci];
         const int mt = u % args.mtiles;
         const int row = ch.e * args.e_rows + mt * TILE_ROWS;
         const int tile0 = ch.e * tiles128 + mt * (TILE_ROWS / 128);
         const int npad = (ch.n + 15) & ~15;
-        const uint32_t tx = NMAT * C::A_TX + kBsTerms * npad * 128 + NMAT * kBsSfBlock;
+        const uint32_t tx = NMAT * C::A_TX + NT * npad * C::ROWB + (NMAT + C::SFB_BLKS) * kBsSfBlock;
         for (int ks = 0; ks < n_stage && ok; ks++) {
           if (!(ok = mbar_wait_sleep(&empty[s], ph ^ 1, abort_flag, st, 21, 256))) break;
           uint8_t* stage = smem + s * C::STAGE;
           mbar_arrive_expect_tx(&full[s], tx);
           if (PAIR) {
-            tma_load_2d(stage, &tm.a[0], &full[s], ks * 128, row);     // 256 rows: both tiles
+            tma_load_2d(stage, &tm.a[0], &full[s], ks * AX, row);     // 256 rows: both tiles
           } else {
 #pragma unroll
-            for (int i = 0; i < NMAT; i++) tma_load_2d(stage + i * C::A_TILE, &tm.a[i], &full[s], ks * 128, row);
+            for (int i = 0; i < NMAT; i++) tma_load_2d(stage + i * C::A_TILE, &tm.a[i], &full[s], ks * AX, row);
           }
-          tma_load_3d(stage + NMAT * C::A_TILE, &tm.b[npad / 16 - 1], &full[s], ks * 128, ch.p0, 0);
+          tma_load_3d(stage + NMAT * C::A_TILE, &tm.b[npad / 16 - 1], &full[s], ks * C::ROWB, ch.p0, 0);
+          uint8_t* sf = stage + NMAT * C::A_TILE + C::B_TILE;
 #pragma unroll
           for (int i = 0; i < NMAT; i++) {
             const uint8_t* src = PAIR ? args.sfa[0] + ((size_t)(tile0 + i) * n_stage + ks) * kBsSfBlock
                                       : args.sfa[i] + ((size_t)tile0 * n_stage + ks) * kBsSfBlock;
-            bulk_load(stage + NMAT * C::A_TILE + C::B_TILE + i * kBsSfBlock, src, kBsSfBlock, &full[s]);
+            bulk_load(sf + i * kBsSfBlock, src, kBsSfBlock, &full[s]);
           }
+          if (C::FP4)
+            bulk_load(sf + NMAT * kBsSfBlock, args.sfb + ((size_t)ci * n_stage + ks) * C::SFB_BLKS * kBsSfBlock,
+                      C::SFB_BLKS * kBsSfBlock, &full[s]);
           issued++;
           if (args.prefetch > 0) prefetch_next();
           if (++s == C::S) { s = 0; ph ^= 1; }
@@ -193,9 +227,10 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX> tm, const BsArg
   } else if (warp == 1) {
     // ---------------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      // B rows 0..127 and 128..255 (an MMA of N > 128 reads the second block)
-      tmem_cp_32x128b_x4(tmem + C::SFB_BASE, umma_desc(smem_u32(smem + C::OFF_SFB), 128, 128, kSwizzleNone));
-      tmem_cp_32x128b_x4(tmem + C::SFB_BASE + 4, umma_desc(smem_u32(smem + C::OFF_SFB), 128, 128, kSwizzleNone));
+      if (!C::FP4) {   // constant B scales: rows 0..127 and 128..255 (an MMA of N > 128 reads both)
+        tmem_cp_32x128b_x4(tmem + C::SFB_BASE, umma_desc(smem_u32(smem + C::OFF_SFB), 128, 128, kSwizzleNone));
+        tmem_cp_32x128b_x4(tmem + C::SFB_BASE + 4, umma_desc(smem_u32(smem + C::OFF_SFB), 128, 128, kSwizzleNone));
+      }
       // The issuer never waits on an mbarrier (a wait in the thread that issues tcgen05.mma
       // stalls its MMA stream by hundreds of cycles): the watcher warp waits for each event (an
       // accumulator buffer drained, a stage's bytes landed) in the order the issuer needs them
@@ -206,7 +241,7 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX> tm, const BsArg
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const Chunk ch = args.chunks[u / args.mtiles];
         const int npad = (ch.n + 15) & ~15;
-        const uint32_t n_mma = kBsTerms * npad;
+        const uint32_t n_mma = NT * npad;
         if (!(ok = seq_wait(ready_seq, ++ev, abort_flag, st, 23))) break;
         tc_fence_after();
         for (int ks = 0; ks < n_stage; ks++) {
@@ -219,16 +254,27 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX> tm, const BsArg
           for (int i = 0; i < NMAT; i++)
             tmem_cp_32x128b_x4(tmem + C::SFA_BASE + (s * NMAT + i) * 4,
                                umma_desc(sf0 + i * kBsSfBlock, 128, 128, kSwizzleNone));
-          const uint64_t bdesc0 = umma_desc(b0, 16, 1024, kSwizzle128B);
+          const uint32_t sfb = C::FP4 ? tmem + C::SFB_BASE + s * 8 : tmem + C::SFB_BASE;
+          if (C::FP4) {
 #pragma unroll
-          for (int kb = 0; kb < 4; kb++) {
-            const uint32_t idesc = idesc_mxf4xe4m3_m128(n_mma, kb, kb);
+            for (int bl = 0; bl < C::SFB_BLKS; bl++)
+              tmem_cp_32x128b_x4(sfb + bl * 4, umma_desc(sf0 + (NMAT + bl) * kBsSfBlock, 128, 128, kSwizzleNone));
+          }
+          const uint64_t bdesc0 = bs_desc<KIND>(b0);
+#pragma unroll
+          for (int kk = 0; kk < 128 / C::KMMA; kk++) {
+            const uint32_t sfid = C::FP4 ? 2 * kk : kk;      // first scale byte this MMA reads
+            const uint32_t idesc =
+                C::FP4 ? idesc_mxf4_m128(n_mma, sfid, sfid) : idesc_mxf4xe4m3_m128(n_mma, sfid, sfid);
 #pragma unroll
             for (int i = 0; i < NMAT; i++) {
-              const uint64_t adesc = umma_desc(a0 + i * C::A_TILE, 16, 1024, kSwizzle128B) + kb * 2;
-              mma_mxf8f6f4_bs(tmem + ab * C::ACC_COLS + i * C::BN, adesc, bdesc0 + kb * 2, idesc,
-                              tmem + C::SFA_BASE + (s * NMAT + i) * 4 + ((uint32_t)kb << 30),
-                              tmem + C::SFB_BASE + ((uint32_t)kb << 30), (ks | kb) ? 1u : 0u);
+              const uint64_t adesc = bs_desc<KIND>(a0 + i * C::A_TILE) + kk * 2;   // + 32 bytes of K
+              const uint32_t d = tmem + ab * C::ACC_COLS + i * C::BN;
+              const uint32_t sfa = tmem + C::SFA_BASE + (s * NMAT + i) * 4 + (sfid << 30);
+              if (C::FP4)
+                mma_mxf4_bs(d, adesc, bdesc0 + kk * 2, idesc, sfa, sfb + (sfid << 30), (ks | kk) ? 1u : 0u);
+              else
+                mma_mxf8f6f4_bs(d, adesc, bdesc0 + kk * 2, idesc, sfa, sfb + (sfid << 30), (ks | kk) ? 1u : 0u);
             }
           }
           mma_commit(&empty[s]);                 // stage (and its scale slots) free once these finish
@@ -293,40 +339,42 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX> tm, const BsArg
         const bool mvalid = m < ep.M;
         const uint32_t c0 = tbase + (PAIR ? pm : 0) * C::BN;        // this product's accumulator
         for (int j0 = 0; j0 < npad; j0 += 16) {
-          // the three terms' partial products of 16 tokens (and of the up projection for F1)
-          uint32_t d0[16], d1[16], d2[16], e0[16], e1[16], e2[16];
-          tmem_ld16_u(c0 + j0, d0);
-          tmem_ld16_u(c0 + npad + j0, d1);
-          tmem_ld16_u(c0 + 2 * npad + j0, d2);
+          // the terms' partial products of 16 tokens (and of the up projection for F1)
+          uint32_t d[NT][16], e[EPI == EPI_F1 ? NT : 1][16];
+#pragma unroll
+          for (int t = 0; t < NT; t++) tmem_ld16_u(c0 + t * npad + j0, d[t]);
           if (EPI == EPI_F1) {                   // the up projection: tile 1's accumulator
-            tmem_ld16_u(c0 + C::BN + j0, e0);
-            tmem_ld16_u(c0 + C::BN + npad + j0, e1);
-            tmem_ld16_u(c0 + C::BN + 2 * npad + j0, e2);
+#pragma unroll
+            for (int t = 0; t < NT; t++) tmem_ld16_u(c0 + C::BN + t * npad + j0, e[t]);
           }
           tmem_ld_wait();
-          tmem_regs_ready(d0);
-          tmem_regs_ready(d1);
-          tmem_regs_ready(d2);
+#pragma unroll
+          for (int t = 0; t < NT; t++) tmem_regs_ready(d[t]);
           if (EPI == EPI_F1) {
-            tmem_regs_ready(e0);
-            tmem_regs_ready(e1);
-            tmem_regs_ready(e2);
+#pragma unroll
+            for (int t = 0; t < NT; t++) tmem_regs_ready(e[t]);
           }
 #pragma unroll
           for (int jj = 0; jj < 16; jj++) {
             const int j = j0 + jj;
             if (j >= ch.n || !mvalid) continue;
             const int p = ch.p0 + j;
-            const float i0 = inv3[p], i1 = inv3[ep.P + p], i2 = inv3[2 * ep.P + p];
-            const float v = fmaf(__uint_as_float(d2[jj]), i2,
-                                 fmaf(__uint_as_float(d1[jj]), i1, __uint_as_float(d0[jj]) * i0));
+            float sc[NT];
+#pragma unroll
+            for (int t = 0; t < NT; t++) sc[t] = C::FP4 ? 1.f : inv3[t * ep.P + p];
+            // terms added from the smallest up (the last term first)
+            float v = __uint_as_float(d[NT - 1][jj]) * sc[NT - 1];
+#pragma unroll
+            for (int t = NT - 2; t >= 0; t--) v = fmaf(__uint_as_float(d[t][jj]), sc[t], v);
             const size_t o = (size_t)p * ep.M + m;
             if (EPI == EPI_F1) {
-              const int t = perm ? perm[p] : p;
-              const size_t tmo = (size_t)t * ep.M + m;
+              float up = __uint_as_float(e[NT - 1][jj]) * sc[NT - 1];
+#pragma unroll
+              for (int t = NT - 2; t >= 0; t--) up = fmaf(__uint_as_float(e[t][jj]), sc[t], up);
+              const int tk = perm ? perm[p] : p;
+              const size_t tmo = (size_t)tk * ep.M + m;
               const float gate = v + dlt_g[tmo];
-              const float up = fmaf(__uint_as_float(e2[jj]), i2,
-                                    fmaf(__uint_as_float(e1[jj]), i1, __uint_as_float(e0[jj]) * i0)) + dlt_u[tmo];
+              up += dlt_u[tmo];
               Go[o] = gate;
               Uo[o] = up;
               Ho[o] = __float2half_rn(situ_glu_fwd(gate, up));

@@ -1,6 +1,8 @@
 // Operand preparation for the block-scaled forward GEMMs (bs_gemm.cuh): the weights' E8M0
 // scale blocks in the layout tcgen05.cp copies into tensor memory (once per weight load), and
-// activation rows as three E4M3 terms with power-of-two row scales (once per GEMM input).
+// activation rows as low-precision terms (once per GEMM input): four E2M1 terms with E8M0
+// block-32 scales (BS_FP4, their scales then laid out per chunk and stage) or three E4M3 terms
+// with power-of-two row scales (BS_FP8).
 #include "host_common.cuh"
 #include "ops.cuh"
 
@@ -43,6 +45,7 @@ int launch_prepare_sfa(const uint8_t* scales, int64_t sstride, int E, int R, int
 // ------------------------------------------------------------------------------------
 constexpr int kE3Threads = 256;
 constexpr int kE3Chunks = 4;       // 8-element chunks a thread holds: K <= 8 * 4 * 256
+constexpr int kBsTermsFp4 = BsTerms<BS_FP4>::value;
 
 template <int SRC>   // 0 fp32, 1 bf16, 2 fp16
 LL_DEV void load8(const void* src, int64_t row, int K, int ch, float (&v)[8]) {
@@ -96,7 +99,7 @@ __global__ void __launch_bounds__(kE3Threads) k_rows_to_e4m3x3(const void* __res
     if (ch < nch) load8<SRC>(src, r, K, ch, v[i]);
   }
 #pragma unroll 1
-  for (int t = 0; t < kBsTerms; t++) {
+  for (int t = 0; t < BsTerms<BS_FP8>::value; t++) {
     float mx = 0.f;
 #pragma unroll
     for (int i = 0; i < kE3Chunks; i++)
@@ -129,6 +132,125 @@ __global__ void __launch_bounds__(kE3Threads) k_rows_to_e4m3x3(const void* __res
       }
     }
   }
+}
+
+// The BS_FP4 activation terms: per row, four rounds of (per 32-element block: max |r|, scale
+// 2^e with e the smallest exponent bringing that max into [-6, 6], round r / 2^e to E2M1,
+// subtract). Term t of row p: packed codes dst[t][p][K/2] (two per byte, even element in the low
+// nibble) and E8M0 scale bytes sc[t][p][K/32] (e + 127). A 32-element block is 4 neighbouring
+// threads' 8 values, so the block max is two shuffles.
+template <int SRC, bool TOK>
+__global__ void __launch_bounds__(kE3Threads) k_rows_to_e2m1x4(const void* __restrict__ src, int src_rows,
+                                                               const int* __restrict__ tok_pos, int k,
+                                                               const int* __restrict__ n_valid, int K, int64_t P,
+                                                               uint8_t* __restrict__ dst, uint8_t* __restrict__ sc) {
+  const int r = blockIdx.x;
+  if (r >= src_rows) return;
+  if (!TOK && n_valid && r >= *n_valid) return;
+  const int nch = K / 8;
+  float v[kE3Chunks][8];
+#pragma unroll
+  for (int i = 0; i < kE3Chunks; i++) {
+    const int ch = threadIdx.x + i * kE3Threads;
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[i][j] = 0.f;
+    if (ch < nch) load8<SRC>(src, r, K, ch, v[i]);
+  }
+#pragma unroll 1
+  for (int t = 0; t < kBsTermsFp4; t++) {
+    uint32_t q[kE3Chunks];
+    uint8_t sbyte[kE3Chunks];
+#pragma unroll
+    for (int i = 0; i < kE3Chunks; i++) {
+      float mx = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; j++) mx = fmaxf(mx, fabsf(v[i][j]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      // smallest e with mx / 2^e <= 6
+      int e = -127;
+      if (mx > 0.f && isfinite(mx)) {
+        int E;
+        const float m = frexpf(mx, &E);            // mx = m 2^E, m in [0.5, 1)
+        e = m <= 0.75f ? E - 3 : E - 2;
+        e = e < -127 ? -127 : (e > 127 ? 127 : e);
+      }
+      sbyte[i] = (uint8_t)(e + 127);
+      const float inv = ldexpf(1.f, -e), scl = ldexpf(1.f, e);
+      uint32_t word = 0;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const uint32_t b = f32x2_to_e2m1x2(v[i][2 * j] * inv, v[i][2 * j + 1] * inv);
+        word |= b << (8 * j);
+        const uint32_t h = e2m1x2_to_half2(b);
+        const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&h));
+        v[i][2 * j] -= d.x * scl;                   // the residual the next term takes
+        v[i][2 * j + 1] -= d.y * scl;
+      }
+      q[i] = word;
+    }
+    for (int j = 0; j < (TOK ? k : 1); j++) {
+      const int p = TOK ? tok_pos[(int64_t)r * k + j] : r;
+      if (p < 0) continue;
+      uint32_t* row = reinterpret_cast<uint32_t*>(dst + ((int64_t)t * P + p) * (K / 2));
+      uint8_t* srow = sc + ((int64_t)t * P + p) * (K / 32);
+#pragma unroll
+      for (int i = 0; i < kE3Chunks; i++) {
+        const int ch = threadIdx.x + i * kE3Threads;
+        if (ch < nch) {
+          row[ch] = q[i];
+          if ((ch & 3) == 0) srow[ch / 4] = sbyte[i];
+        }
+      }
+    }
+  }
+}
+
+int launch_rows_to_e2m1x4(const void* src, int src_dtype, int src_rows, const int* tok_pos, int k,
+                          const int* n_valid, int K, int64_t P, uint8_t* dst, uint8_t* sc, cudaStream_t s) {
+  if (src_rows <= 0) return LL_OK;
+  if (!src || !dst || !sc || K <= 0 || K % 32 || K > 8 * kE3Chunks * kE3Threads || src_dtype < 0 || src_dtype > 2)
+    return LL_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) % 16) return LL_ERR_ARG;
+  const bool tok = tok_pos != nullptr;
+#define LL_E2(SRC, TOKV)                                                                              \
+  k_rows_to_e2m1x4<SRC, TOKV><<<src_rows, kE3Threads, 0, s>>>(src, src_rows, tok_pos, k, n_valid, K, P, dst, sc)
+  if (tok) {
+    if (src_dtype == 0) LL_E2(0, true); else if (src_dtype == 1) LL_E2(1, true); else LL_E2(2, true);
+  } else {
+    if (src_dtype == 0) LL_E2(0, false); else if (src_dtype == 1) LL_E2(1, false); else LL_E2(2, false);
+  }
+#undef LL_E2
+  return check_launch("k_rows_to_e2m1x4");
+}
+
+// The B scale blocks of every (chunk, 128-K stage): B row n = t npad + j (term t, chunk row j)
+// takes the 4 scale bytes of activation row p0 + j, term t, for that stage, at line n % 32,
+// word (n % 128) / 32 of block n / 128 (the layout tcgen05.cp copies into tensor memory). Rows
+// past the chunk's rows (padding, and the rows of the next chunk a 16-row box also loads) get
+// scale byte 0.
+__global__ void k_arrange_sfb(const Chunk* __restrict__ chunks, const int* __restrict__ n_chunks,
+                              const uint8_t* __restrict__ sc, int64_t P, int K, int blks, uint8_t* __restrict__ out) {
+  const int c = blockIdx.x, ks = blockIdx.y;
+  if (c >= *n_chunks) return;
+  const Chunk ch = chunks[c];
+  const int npad = (ch.n + 15) & ~15;
+  const int n_stage = K / 128;
+  uint32_t* blk = reinterpret_cast<uint32_t*>(out + ((size_t)c * n_stage + ks) * blks * kBsSfBlock);
+  for (int n = threadIdx.x; n < blks * 128; n += blockDim.x) {
+    const int t = n / npad, j = n % npad;
+    uint32_t w = 0;
+    if (t < kBsTermsFp4 && j < ch.n)
+      w = *reinterpret_cast<const uint32_t*>(sc + ((int64_t)t * P + ch.p0 + j) * (K / 32) + 4 * ks);
+    blk[(n / 128) * (kBsSfBlock / 4) + (n % 32) * 4 + (n % 128) / 32] = w;
+  }
+}
+
+int launch_arrange_sfb(const Chunk* chunks, const int* n_chunks, int max_chunks, const uint8_t* sc, int64_t P, int K,
+                       int blks, uint8_t* out, cudaStream_t s) {
+  if (max_chunks <= 0 || K % 128 || blks < 1 || blks > 2 || !chunks || !n_chunks || !sc || !out) return LL_ERR_ARG;
+  k_arrange_sfb<<<dim3(max_chunks, K / 128), 128, 0, s>>>(chunks, n_chunks, sc, P, K, blks, out);
+  return check_launch("k_arrange_sfb");
 }
 
 int launch_rows_to_e4m3x3(const void* src, int src_dtype, int src_rows, const int* tok_pos, int k,

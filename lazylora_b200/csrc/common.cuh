@@ -325,6 +325,45 @@ LL_DEV uint32_t idesc_mxf4xe4m3_m128(uint32_t n, uint32_t sf_a, uint32_t sf_b) {
   return d;
 }
 
+// D[tmem] (+)= (A * SFA) * (B * SFB), kind::mxf4: A and B packed E2M1 (two per byte) in shared
+// memory, one E8M0 scale per 32 K elements of every row, K = 64 per instruction (two scale
+// bytes of each row: those at sf_id and sf_id + 1).
+LL_DEV void mma_mxf4_bs(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t sfa,
+                        uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor, kind::mxf4: A and B E2M1 (K-major), fp32 D, E8M0 scales, M = 128,
+// N = n (multiple of 16, <= 256), K = 64; sf_a / sf_b the first scale byte of each row used.
+LL_DEV uint32_t idesc_mxf4_m128(uint32_t n, uint32_t sf_a, uint32_t sf_b) {
+  uint32_t d = 0;
+  d |= (sf_b & 3u) << 4;        // B scale-factor id
+  d |= 1u << 7;                 // A format E2M1
+  d |= 1u << 10;                // B format E2M1
+  d |= (n >> 3) << 17;          // N
+  d |= 1u << 23;                // scale format E8M0
+  d |= (128u >> 4) << 24;       // M
+  d |= (sf_a & 3u) << 29;       // A scale-factor id
+  return d;
+}
+
+// Two floats -> two E2M1 codes in one byte (lo in the low nibble), round to nearest even,
+// saturating to +-6.
+LL_DEV uint32_t f32x2_to_e2m1x2(float lo, float hi) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 b;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b, %1, %2;\n\t"
+      "cvt.u32.u8 %0, b;\n\t}"
+      : "=r"(r)
+      : "f"(hi), "f"(lo));
+  return r;
+}
+
 // 32 rows x 128 bits from shared memory (descriptor, no swizzle, 16-byte rows) into tensor
 // memory lanes 0..31 at columns taddr .. taddr + 3, replicated into all four lane quarters.
 LL_DEV void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {

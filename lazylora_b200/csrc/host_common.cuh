@@ -152,27 +152,51 @@ inline int make_fp4_map(CUtensorMap* m, const uint8_t* packed, int64_t rows_tota
                      (uint64_t)K / 2, 128, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-// E4M3 activation terms [3][rows][K] bytes, one map per chunk height 16 c (c = 1..n): a box is
-// [3 terms][16 c rows][128 K], 128-byte swizzle.
+// E4M3 activation terms [3][rows][K] bytes (BS_FP8), one map per chunk height 16 c (c = 1..n):
+// a box is [3 terms][16 c rows][128 K], 128-byte swizzle.
 inline int make_e4m3x3_maps(CUtensorMap* maps, int n, const uint8_t* base, int64_t rows, int K) {
+  constexpr int NT = BsTerms<BS_FP8>::value;
   if (K % 128 || n < 1 || n > 4) return LL_ERR_ARG;
-  const uint64_t dims[3] = {(uint64_t)K, (uint64_t)rows, (uint64_t)kBsTerms};
+  const uint64_t dims[3] = {(uint64_t)K, (uint64_t)rows, (uint64_t)NT};
   const uint64_t strides[2] = {(uint64_t)K, (uint64_t)rows * K};
   for (int c = 1; c <= n; c++) {
-    const uint32_t box[3] = {128, (uint32_t)(16 * c), (uint32_t)kBsTerms};
+    const uint32_t box[3] = {128, (uint32_t)(16 * c), (uint32_t)NT};
     LL_TRY(make_map_nd(&maps[c - 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, base, 3, dims, strides, box,
                        CU_TENSOR_MAP_SWIZZLE_128B));
   }
   return LL_OK;
 }
 
-template <int EPI, int NMAT, int N_MAX>
+// Packed E2M1 activation terms [4][rows][K/2] bytes (BS_FP4): a box is [4 terms][16 c rows][64
+// bytes = 128 K], 64-byte swizzle.
+inline int make_e2m1x4_maps(CUtensorMap* maps, int n, const uint8_t* base, int64_t rows, int K) {
+  constexpr int NT = BsTerms<BS_FP4>::value;
+  if (K % 128 || n < 1 || n > 4) return LL_ERR_ARG;
+  const uint64_t dims[3] = {(uint64_t)K / 2, (uint64_t)rows, (uint64_t)NT};
+  const uint64_t strides[2] = {(uint64_t)K / 2, (uint64_t)rows * K / 2};
+  for (int c = 1; c <= n; c++) {
+    const uint32_t box[3] = {64, (uint32_t)(16 * c), (uint32_t)NT};
+    LL_TRY(make_map_nd(&maps[c - 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, base, 3, dims, strides, box,
+                       CU_TENSOR_MAP_SWIZZLE_64B));
+  }
+  return LL_OK;
+}
+
+// Packed weight codes [rows_total][K/2] bytes as BS_FP4 reads them: boxes of box_rows rows x 64
+// bytes (128 K), 64-byte swizzle.
+inline int make_fp4_packed_map(CUtensorMap* m, const uint8_t* packed, int64_t rows_total, int K, int box_rows) {
+  if (K % 128) return LL_ERR_ARG;
+  return make_map_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, (uint64_t)K / 2, (uint64_t)rows_total,
+                     (uint64_t)K / 2, 64, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
+template <int EPI, int NMAT, int N_MAX, int KIND>
 int launch_bs_gemm(const CUtensorMap* a, const CUtensorMap* b, const BsArgs& args, cudaStream_t stream) {
-  using Cfg = BsCfg<NMAT, N_MAX>;
-  BsTma<NMAT, N_MAX> tm;
+  using Cfg = BsCfg<NMAT, N_MAX, KIND>;
+  BsTma<NMAT, N_MAX, KIND> tm;
   for (int i = 0; i < NMAT; i++) tm.a[i] = a[i];
   for (int i = 0; i < N_MAX / 16; i++) tm.b[i] = b[i];
-  auto kern = grouped_mxfp4_bs_gemm<EPI, NMAT, N_MAX>;
+  auto kern = grouped_mxfp4_bs_gemm<EPI, NMAT, N_MAX, KIND>;
   LL_TRY(set_smem_attr(reinterpret_cast<const void*>(kern), Cfg::SMEM));
   const DeviceInfo di = device_info();
   const bool prof = g_prof_events && g_prof_i + 2 <= g_prof_n;

@@ -301,10 +301,18 @@ struct LayerWs {
   float* tw;
   float* xinv;
   __half* xh;
-  uint8_t* xq;        // [3][P][d] E4M3 terms of the pair rows (block-scaled F1)
-  float* xinv3;       // [3][P]
-  uint8_t* hq;        // [3][P][f] E4M3 terms of h (block-scaled F2)
-  float* hinv3;       // [3][P]
+  // block-scaled forward operands: the activation terms of the pair rows (x for F1, h for F2),
+  // 3 E4M3 terms ([3][P][K] bytes) or 4 packed E2M1 terms ([4][P][K/2]), their scales (E4M3: row
+  // scales [3][P]; E2M1: block scale bytes [4][P][K/32], laid out per chunk and stage in *sfb)
+  uint8_t* xq;
+  float* xinv3;
+  uint8_t* xsc;
+  uint8_t* xsfb;
+  uint8_t* hq;
+  float* hinv3;
+  uint8_t* hsc;
+  uint8_t* hsfb;
+  int max_chunks;
   float* xa_g;
   float* xa_u;
   float* dlt_g;
@@ -372,10 +380,18 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   w.tw = c.take<float>(P);
   w.xinv = c.take<float>(P);
   w.xh = c.take<__half>(P * d);
-  w.xq = c.take<uint8_t>((size_t)kBsTerms * P * d);
-  w.xinv3 = c.take<float>((size_t)kBsTerms * P);
-  w.hq = c.take<uint8_t>((size_t)kBsTerms * P * f);
-  w.hinv3 = c.take<float>((size_t)kBsTerms * P);
+  {
+    const int max_chunks = E + (int)(P / 16) + 2;       // the chunk list's capacity
+    w.max_chunks = max_chunks;
+    w.xq = c.take<uint8_t>((size_t)3 * P * d);          // 3 E4M3 terms or 4 E2M1 terms (2 P d bytes)
+    w.xinv3 = c.take<float>((size_t)3 * P);
+    w.xsc = c.take<uint8_t>((size_t)4 * P * (d / 32));
+    w.xsfb = c.take<uint8_t>((size_t)max_chunks * (d / 128) * kBsSfBlock);
+    w.hq = c.take<uint8_t>((size_t)3 * P * f);
+    w.hinv3 = c.take<float>((size_t)3 * P);
+    w.hsc = c.take<uint8_t>((size_t)4 * P * (f / 32));
+    w.hsfb = c.take<uint8_t>((size_t)max_chunks * (f / 128) * kBsSfBlock);
+  }
   w.xa_g = c.take<float>((size_t)T * r);
   w.xa_u = c.take<float>((size_t)T * r);
   w.dlt_g = c.take<float>((size_t)T * f);
@@ -444,11 +460,35 @@ static int bs_prefetch_stages() {
   return v;
 }
 
+// The block-scaled forward GEMM kind for a token-tile width: E2M1 activation terms up to 32
+// rows, E4M3 terms at 64 rows, none (fp16 dequant path) at 128.
+static int bs_kind(int nmax) { return nmax <= 32 ? BS_FP4 : nmax <= 64 ? BS_FP8 : -1; }
+
 template <int EPI>
-static int bs_nmax(int nmax, const CUtensorMap* a, const CUtensorMap* b, const BsArgs& args, cudaStream_t s) {
-  if (nmax == 16) return launch_bs_gemm<EPI, 2, 16>(a, b, args, s);
-  if (nmax == 32) return launch_bs_gemm<EPI, 2, 32>(a, b, args, s);
-  return launch_bs_gemm<EPI, 2, 64>(a, b, args, s);
+static int bs_launch(int kind, int nmax, const CUtensorMap* a, const CUtensorMap* b, const BsArgs& args,
+                     cudaStream_t s) {
+  if (kind == BS_FP4)
+    return nmax == 16 ? launch_bs_gemm<EPI, 2, 16, BS_FP4>(a, b, args, s) : launch_bs_gemm<EPI, 2, 32, BS_FP4>(a, b, args, s);
+  return launch_bs_gemm<EPI, 2, 64, BS_FP8>(a, b, args, s);
+}
+
+// The activation operand of a block-scaled GEMM: the rows as the kind's terms (tok_pos given:
+// the T token rows written to their pair rows; else pair rows < *n_valid), and for BS_FP4 their
+// block scales laid out per chunk and stage, plus the tensor maps of the terms.
+static int bs_operand(int kind, const LayerWs& W, const void* src, int src_dtype, int src_rows, const int* tok_pos,
+                      int k, const int* n_valid, int K, int64_t P, uint8_t* q, float* inv3, uint8_t* sc,
+                      uint8_t* sfb, CUtensorMap* maps, BsArgs& a, cudaStream_t s) {
+  if (kind == BS_FP4) {
+    LL_TRY(launch_rows_to_e2m1x4(src, src_dtype, src_rows, tok_pos, k, n_valid, K, P, q, sc, s));
+    LL_TRY(launch_arrange_sfb(W.chunks, W.n_chunks, W.max_chunks, sc, P, K, 1, sfb, s));
+    LL_TRY(make_e2m1x4_maps(maps, W.nmax / 16, q, P, K));
+    a.sfb = sfb;
+  } else {
+    LL_TRY(launch_rows_to_e4m3x3(src, src_dtype, src_rows, tok_pos, k, n_valid, K, P, q, inv3, s));
+    LL_TRY(make_e4m3x3_maps(maps, W.nmax / 16, q, P, K));
+    a.inv3 = inv3;
+  }
+  return LL_OK;
 }
 
 // C0 (and C1) = alpha * A[M][K] . B, with B given as rows ([N][K], split over B0 / B1 at N0)
@@ -607,23 +647,27 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   k_scatter<<<nblk, 256, kTokBlock * k * sizeof(int), s>>>(idx, w, T, k, E, W.cnt, W.perm_token, W.perm_slot,
                                                             W.pair_pos, W.tw, W.tok_pos);
   LL_TRY(check_launch("k_scatter"));
-  // Tiles up to 64 rows: the forward GEMMs run on the block-scaled MMA (E4M3 activation terms,
-  // weights not decoded); 128-row tiles (the large-T regime) on the fp16 dequant path.
-  const bool bs = W.nmax <= 64;
-  if (bs)
-    LL_TRY(launch_rows_to_e4m3x3(x, x_dtype, T, W.tok_pos, k, nullptr, d, P, W.xq, W.xinv3, s));
-  else
-    LL_TRY(launch_token_rows_to_half(x, x_dtype, W.perm_token, W.tok_pos, T, k, d, W.xh, W.xinv, s));
+  // Tiles up to 64 rows: the forward GEMMs run on the block-scaled MMAs (weights not decoded;
+  // E2M1 activation terms up to 32 rows, E4M3 at 64); 128-row tiles (the large-T regime) on the
+  // fp16 dequant path.
+  const int kind = bs_kind(W.nmax);
+  const bool bs = kind >= 0;
+  if (!bs) LL_TRY(launch_token_rows_to_half(x, x_dtype, W.perm_token, W.tok_pos, T, k, d, W.xh, W.xinv, s));
   LL_TRY(skinny(x, x_dtype, true, T, d, L->A_g, L->A_u, r, 2 * r, 1.f, W.xa_g, W.xa_u, W.skpart, W.skpart_floats, s));
   LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_g, L->B_g, nullptr, nullptr, W.dlt_g, s));
   LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_u, L->B_u, nullptr, nullptr, W.dlt_u, s));
   // F1: gate / up
   if (bs) {
     CUtensorMap a[2], b[4];
-    LL_TRY(make_fp4_map(&a[0], L->w1p, (int64_t)E * f, d, 128));
-    LL_TRY(make_fp4_map(&a[1], L->w3p, (int64_t)E * f, d, 128));
-    LL_TRY(make_e4m3x3_maps(b, W.nmax / 16, W.xq, P, d));
+    if (kind == BS_FP4) {
+      LL_TRY(make_fp4_packed_map(&a[0], L->w1p, (int64_t)E * f, d, 128));
+      LL_TRY(make_fp4_packed_map(&a[1], L->w3p, (int64_t)E * f, d, 128));
+    } else {
+      LL_TRY(make_fp4_map(&a[0], L->w1p, (int64_t)E * f, d, 128));
+      LL_TRY(make_fp4_map(&a[1], L->w3p, (int64_t)E * f, d, 128));
+    }
     BsArgs a1{};
+    LL_TRY(bs_operand(kind, W, x, x_dtype, T, W.tok_pos, k, nullptr, d, P, W.xq, W.xinv3, W.xsc, W.xsfb, b, a1, s));
     a1.chunks = W.chunks;
     a1.n_chunks = W.n_chunks;
     a1.mtiles = f / 128;
@@ -631,7 +675,6 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
     a1.e_rows = f;
     a1.sfa[0] = L->w1sf;
     a1.sfa[1] = L->w3sf;
-    a1.inv3 = W.xinv3;
     a1.prefetch = bs_prefetch_stages();
     a1.status = W.st;
     a1.epi.perm_token = W.perm_token;
@@ -642,7 +685,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
     a1.epi.G = W.G;
     a1.epi.U = W.U;
     a1.epi.H = W.H;
-    LL_TRY(bs_nmax<EPI_F1>(W.nmax, a, b, a1, s));
+    LL_TRY(bs_launch<EPI_F1>(kind, W.nmax, a, b, a1, s));
   } else {
     CUtensorMap pk[2], sc[2], act[8];
     LL_TRY(make_rowscale_maps(&pk[0], &sc[0], L->w1p, L->w1s, (int64_t)E * f, d, L->s13_stride));
@@ -678,19 +721,20 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   }
   // F2: down (paired 128-row tiles of the stack: d a multiple of 256)
   if (bs && d % 256 == 0) {
-    LL_TRY(launch_rows_to_e4m3x3(W.H, 2, P, nullptr, 0, n_valid, f, P, W.hq, W.hinv3, s));
     CUtensorMap a[2], b[4];
-    LL_TRY(make_fp4_map(&a[0], L->w2p, (int64_t)E * d, f, 256));
+    if (kind == BS_FP4)
+      LL_TRY(make_fp4_packed_map(&a[0], L->w2p, (int64_t)E * d, f, 256));
+    else
+      LL_TRY(make_fp4_map(&a[0], L->w2p, (int64_t)E * d, f, 256));
     a[1] = a[0];
-    LL_TRY(make_e4m3x3_maps(b, W.nmax / 16, W.hq, P, f));
     BsArgs a2{};
+    LL_TRY(bs_operand(kind, W, W.H, 2, P, nullptr, 0, n_valid, f, P, W.hq, W.hinv3, W.hsc, W.hsfb, b, a2, s));
     a2.chunks = W.chunks;
     a2.n_chunks = W.n_chunks;
     a2.mtiles = d / 256;
     a2.K = f;
     a2.e_rows = d;
     a2.sfa[0] = a2.sfa[1] = L->w2sf;
-    a2.inv3 = W.hinv3;
     a2.prefetch = bs_prefetch_stages();
     a2.status = W.st;
     a2.epi.perm_token = W.perm_token;
@@ -698,7 +742,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
     a2.epi.P = P;
     a2.epi.M = d;
     a2.epi.Y = W.Y;
-    LL_TRY(bs_nmax<EPI_F2>(W.nmax, a, b, a2, s));
+    LL_TRY(bs_launch<EPI_F2>(kind, W.nmax, a, b, a2, s));
   } else {
     CUtensorMap pk[2], sc[2], act[8];
     LL_TRY(make_rowscale_maps(&pk[0], &sc[0], L->w2p, L->w2s, (int64_t)E * d, f, L->s2_stride, 256));
