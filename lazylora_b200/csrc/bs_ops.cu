@@ -3,6 +3,8 @@
 // activation rows as low-precision terms (once per GEMM input): four E2M1 terms with E8M0
 // block-32 scales (BS_FP4, their scales then laid out per chunk and stage) or three E4M3 terms
 // with power-of-two row scales (BS_FP8).
+#include <algorithm>
+
 #include "host_common.cuh"
 #include "ops.cuh"
 
@@ -231,25 +233,30 @@ int launch_rows_to_e2m1x4(const void* src, int src_dtype, int src_rows, const in
 // scale byte 0.
 __global__ void k_arrange_sfb(const Chunk* __restrict__ chunks, const int* __restrict__ n_chunks,
                               const uint8_t* __restrict__ sc, int64_t P, int K, int blks, uint8_t* __restrict__ out) {
-  const int c = blockIdx.x, ks = blockIdx.y;
-  if (c >= *n_chunks) return;
-  const Chunk ch = chunks[c];
-  const int npad = (ch.n + 15) & ~15;
   const int n_stage = K / 128;
-  uint32_t* blk = reinterpret_cast<uint32_t*>(out + ((size_t)c * n_stage + ks) * blks * kBsSfBlock);
-  for (int n = threadIdx.x; n < blks * 128; n += blockDim.x) {
-    const int t = n / npad, j = n % npad;
-    uint32_t w = 0;
-    if (t < kBsTermsFp4 && j < ch.n)
-      w = *reinterpret_cast<const uint32_t*>(sc + ((int64_t)t * P + ch.p0 + j) * (K / 32) + 4 * ks);
-    blk[(n / 128) * (kBsSfBlock / 4) + (n % 32) * 4 + (n % 128) / 32] = w;
+  const int64_t items = (int64_t)(*n_chunks) * n_stage;      // (chunk, stage) blocks to lay out
+  for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+    const int c = (int)(it / n_stage), ks = (int)(it % n_stage);
+    const Chunk ch = chunks[c];
+    const int npad = (ch.n + 15) & ~15;
+    uint32_t* blk = reinterpret_cast<uint32_t*>(out + ((size_t)c * n_stage + ks) * blks * kBsSfBlock);
+    for (int n = threadIdx.x; n < blks * 128; n += blockDim.x) {
+      const int t = n / npad, j = n % npad;
+      uint32_t w = 0;
+      if (t < kBsTermsFp4 && j < ch.n)
+        w = *reinterpret_cast<const uint32_t*>(sc + ((int64_t)t * P + ch.p0 + j) * (K / 32) + 4 * ks);
+      blk[(n / 128) * (kBsSfBlock / 4) + (n % 32) * 4 + (n % 128) / 32] = w;
+    }
   }
 }
 
 int launch_arrange_sfb(const Chunk* chunks, const int* n_chunks, int max_chunks, const uint8_t* sc, int64_t P, int K,
                        int blks, uint8_t* out, cudaStream_t s) {
   if (max_chunks <= 0 || K % 128 || blks < 1 || blks > 2 || !chunks || !n_chunks || !sc || !out) return LL_ERR_ARG;
-  k_arrange_sfb<<<dim3(max_chunks, K / 128), 128, 0, s>>>(chunks, n_chunks, sc, P, K, blks, out);
+  // a grid-stride loop over the (chunk, stage) blocks that exist (the count is on the device)
+  const int64_t most = (int64_t)max_chunks * (K / 128);
+  const int grid = (int)std::min<int64_t>(most, (int64_t)device_info().sms * 8);
+  k_arrange_sfb<<<grid, 128, 0, s>>>(chunks, n_chunks, sc, P, K, blks, out);
   return check_launch("k_arrange_sfb");
 }
 
