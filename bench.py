@@ -917,6 +917,8 @@ def main():
     ap.add_argument("--decode", action="store_true", help="forward-only decode steps (configs[3]: c3_t1/4/16)")
     ap.add_argument("--graph", action="store_true", help="with --decode: replay each step as a CUDA graph")
     ap.add_argument("--zipf-gamma", type=float, default=None, help="override the config's Zipf bias scale")
+    ap.add_argument("--experts", type=int, default=None,
+                    help="override the config's expert count (profiler captures on a smaller weight stack)")
     ap.add_argument("--stream", action="store_true", help="configs[4]: experts streamed from pinned host memory")
     ap.add_argument("--latent", action="store_true", help="the latent routed block (use --config c1_latent)")
     ap.add_argument("--traces", action="store_true", help="fwd+bwd steps on the recorded K3 routings (top-16)")
@@ -934,6 +936,8 @@ def main():
     cfg = CONFIGS[args.config]
     if args.zipf_gamma is not None:
         cfg = replace(cfg, zipf_gamma=args.zipf_gamma)
+    if args.experts is not None:
+        cfg = replace(cfg, E=args.experts)
     rank, local, world, dist = dist_setup(args)
     if world > 1 and args.config in ("c1", "c2") and not (args.decode or args.stream or args.latent or
                                                           args.traces or args.shared):

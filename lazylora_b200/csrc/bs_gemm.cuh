@@ -135,11 +135,15 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int n_units = (*args.n_chunks) * args.mtiles;
-  if ((int)blockIdx.x >= n_units || args.K <= 0 || args.K % 128) return;   // uniform: nothing allocated yet
+  if (args.K <= 0 || args.K % 128) {   // uniform: nothing allocated yet
+    pdl_wait();
+    return;
+  }
   const int n_stage = args.K / 128;
   const int tiles128 = args.e_rows / 128;      // 128-row tiles per expert (scale-block index)
 
+  // Prologue (barriers, tensor memory, descriptor prefetch) before the wait for the kernels
+  // this one depends on: it reads nothing they write.
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::S; i++) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
     for (int i = 0; i < 2; i++) { mbar_init(&accfull[i], 1); mbar_init(&accempty[i], C::kEpWarps); }
@@ -151,17 +155,26 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
   if (!C::FP4 && threadIdx.x < kBsSfBlock / 4) reinterpret_cast<uint32_t*>(smem + C::OFF_SFB)[threadIdx.x] = 0x7f7f7f7fu;
   fence_async_smem();                       // the constant block is read by tcgen05.cp (async proxy)
   if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < NMAT; i++) tma_prefetch_desc(&tm.a[i]);
+    for (int i = 0; i < N_MAX / 16; i++) tma_prefetch_desc(&tm.b[i]);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   DevStatus* st = args.status;
+  pdl_launch_next();                        // (after the allocation: see pdl_launch_next)
+  pdl_wait();
+  const int n_units = (*args.n_chunks) * args.mtiles;
+  if ((int)blockIdx.x >= n_units) {         // uniform per block: no unit for this one
+    if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+    return;
+  }
 
   if (warp == 0) {
     // ------------------------------------------------------------------- TMA producer
     if (lane == 0) {
-      for (int i = 0; i < NMAT; i++) tma_prefetch_desc(&tm.a[i]);
-      for (int i = 0; i < N_MAX / 16; i++) tma_prefetch_desc(&tm.b[i]);
       int s = 0, issued = 0;
       uint32_t ph = 0;
       bool ok = true;

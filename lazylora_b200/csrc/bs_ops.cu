@@ -87,6 +87,8 @@ __global__ void __launch_bounds__(kE3Threads) k_rows_to_e4m3x3(const void* __res
                                                                const int* __restrict__ tok_pos, int k,
                                                                const int* __restrict__ n_valid, int K, int64_t P,
                                                                uint8_t* __restrict__ dst, float* __restrict__ inv3) {
+  pdl_wait();
+  pdl_launch_next();
   const int r = blockIdx.x;
   if (r >= src_rows) return;
   if (!TOK && n_valid && r >= *n_valid) return;
@@ -146,24 +148,30 @@ __global__ void __launch_bounds__(kE3Threads) k_rows_to_e2m1x4(const void* __res
                                                                const int* __restrict__ tok_pos, int k,
                                                                const int* __restrict__ n_valid, int K, int64_t P,
                                                                uint8_t* __restrict__ dst, uint8_t* __restrict__ sc) {
+  pdl_wait();
+  pdl_launch_next();
+  // block (x, y): row x, 8-element chunks [y 256, y 256 + 256) of it (the scales are per
+  // 32-element block, four adjacent threads, so a row splits over blocks with no reduction)
   const int r = blockIdx.x;
   if (r >= src_rows) return;
   if (!TOK && n_valid && r >= *n_valid) return;
   const int nch = K / 8;
-  float v[kE3Chunks][8];
+  const int ch0 = blockIdx.y * kE3Threads;
+  constexpr int NC = 1;
+  float v[NC][8];
 #pragma unroll
-  for (int i = 0; i < kE3Chunks; i++) {
-    const int ch = threadIdx.x + i * kE3Threads;
+  for (int i = 0; i < NC; i++) {
+    const int ch = ch0 + threadIdx.x;
 #pragma unroll
     for (int j = 0; j < 8; j++) v[i][j] = 0.f;
     if (ch < nch) load8<SRC>(src, r, K, ch, v[i]);
   }
 #pragma unroll 1
   for (int t = 0; t < kBsTermsFp4; t++) {
-    uint32_t q[kE3Chunks];
-    uint8_t sbyte[kE3Chunks];
+    uint32_t q[NC];
+    uint8_t sbyte[NC];
 #pragma unroll
-    for (int i = 0; i < kE3Chunks; i++) {
+    for (int i = 0; i < NC; i++) {
       float mx = 0.f;
 #pragma unroll
       for (int j = 0; j < 8; j++) mx = fmaxf(mx, fabsf(v[i][j]));
@@ -197,8 +205,8 @@ __global__ void __launch_bounds__(kE3Threads) k_rows_to_e2m1x4(const void* __res
       uint32_t* row = reinterpret_cast<uint32_t*>(dst + ((int64_t)t * P + p) * (K / 2));
       uint8_t* srow = sc + ((int64_t)t * P + p) * (K / 32);
 #pragma unroll
-      for (int i = 0; i < kE3Chunks; i++) {
-        const int ch = threadIdx.x + i * kE3Threads;
+      for (int i = 0; i < NC; i++) {
+        const int ch = ch0 + threadIdx.x;
         if (ch < nch) {
           row[ch] = q[i];
           if ((ch & 3) == 0) srow[ch / 4] = sbyte[i];
@@ -216,14 +224,16 @@ int launch_rows_to_e2m1x4(const void* src, int src_dtype, int src_rows, const in
   if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) % 16) return LL_ERR_ARG;
   const bool tok = tok_pos != nullptr;
 #define LL_E2(SRC, TOKV)                                                                              \
-  k_rows_to_e2m1x4<SRC, TOKV><<<src_rows, kE3Threads, 0, s>>>(src, src_rows, tok_pos, k, n_valid, K, P, dst, sc)
+  LL_TRY(launch_pdl("k_rows_to_e2m1x4", k_rows_to_e2m1x4<SRC, TOKV>,                                      \
+                    dim3(src_rows, (K / 8 + kE3Threads - 1) / kE3Threads), dim3(kE3Threads), 0, s, src, src_rows, \
+                    tok_pos, k, n_valid, K, P, dst, sc))
   if (tok) {
     if (src_dtype == 0) LL_E2(0, true); else if (src_dtype == 1) LL_E2(1, true); else LL_E2(2, true);
   } else {
     if (src_dtype == 0) LL_E2(0, false); else if (src_dtype == 1) LL_E2(1, false); else LL_E2(2, false);
   }
 #undef LL_E2
-  return check_launch("k_rows_to_e2m1x4");
+  return LL_OK;
 }
 
 // The B scale blocks of every (chunk, 128-K stage): B row n = t npad + j (term t, chunk row j)
@@ -233,6 +243,8 @@ int launch_rows_to_e2m1x4(const void* src, int src_dtype, int src_rows, const in
 // scale byte 0.
 __global__ void k_arrange_sfb(const Chunk* __restrict__ chunks, const int* __restrict__ n_chunks,
                               const uint8_t* __restrict__ sc, int64_t P, int K, int blks, uint8_t* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_next();
   const int n_stage = K / 128;
   const int64_t items = (int64_t)(*n_chunks) * n_stage;      // (chunk, stage) blocks to lay out
   for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
@@ -256,8 +268,7 @@ int launch_arrange_sfb(const Chunk* chunks, const int* n_chunks, int max_chunks,
   // a grid-stride loop over the (chunk, stage) blocks that exist (the count is on the device)
   const int64_t most = (int64_t)max_chunks * (K / 128);
   const int grid = (int)std::min<int64_t>(most, (int64_t)device_info().sms * 8);
-  k_arrange_sfb<<<grid, 128, 0, s>>>(chunks, n_chunks, sc, P, K, blks, out);
-  return check_launch("k_arrange_sfb");
+  return launch_pdl("k_arrange_sfb", k_arrange_sfb, dim3(grid), dim3(128), 0, s, chunks, n_chunks, sc, P, K, blks, out);
 }
 
 int launch_rows_to_e4m3x3(const void* src, int src_dtype, int src_rows, const int* tok_pos, int k,
@@ -268,14 +279,15 @@ int launch_rows_to_e4m3x3(const void* src, int src_dtype, int src_rows, const in
   if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) % 16) return LL_ERR_ARG;
   const bool tok = tok_pos != nullptr;
 #define LL_E3(SRC, TOKV)                                                                              \
-  k_rows_to_e4m3x3<SRC, TOKV><<<src_rows, kE3Threads, 0, s>>>(src, src_rows, tok_pos, k, n_valid, K, P, dst, inv3)
+  LL_TRY(launch_pdl("k_rows_to_e4m3x3", k_rows_to_e4m3x3<SRC, TOKV>, dim3(src_rows), dim3(kE3Threads), 0, s, src, \
+                    src_rows, tok_pos, k, n_valid, K, P, dst, inv3))
   if (tok) {
     if (src_dtype == 0) LL_E3(0, true); else if (src_dtype == 1) LL_E3(1, true); else LL_E3(2, true);
   } else {
     if (src_dtype == 0) LL_E3(0, false); else if (src_dtype == 1) LL_E3(1, false); else LL_E3(2, false);
   }
 #undef LL_E3
-  return check_launch("k_rows_to_e4m3x3");
+  return LL_OK;
 }
 
 }  // namespace ll

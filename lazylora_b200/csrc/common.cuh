@@ -12,6 +12,18 @@
 
 #define LL_DEV __device__ __forceinline__
 
+// Programmatic dependent launch. A kernel launched with the programmatic-serialization
+// attribute (launch_pdl) may be scheduled while the kernel before it on the stream still runs;
+// pdl_wait() returns once that kernel has completed and its writes are visible. Since that
+// kernel waited in the same way, everything earlier on the stream has completed too. A kernel
+// launched so calls pdl_wait() in every block before its first read or write of global memory
+// another kernel produces or consumes, and before it can exit (so that completion stays
+// ordered). pdl_launch_next() lets the next kernel's blocks be scheduled now; kernels that
+// allocate tensor memory call it only after their allocation, so that a waiting successor never
+// holds columns a running predecessor still has to allocate.
+LL_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+LL_DEV void pdl_launch_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // K per tensor-memory / activation ring stage of the grouped GEMM (64 or 128); each 128-K
 // packed weight stage feeds 128 / LL_KS ring stages. 64-K stages double the ring depth for the
 // same tensor memory but also every per-stage barrier and commit; they measured 16 % slower

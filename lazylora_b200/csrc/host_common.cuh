@@ -5,6 +5,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "grouped_gemm.cuh"
 #include "bs_gemm.cuh"
@@ -51,6 +52,30 @@ inline int check_launch(const char* what) {
     LL_CUDA(cudaEventRecord(g_lev[g_lev_i++], g_launch_stream));
   }
   return LL_OK;
+}
+
+// Whether launch_pdl sets the programmatic-serialization attribute (environment LL_PDL=0
+// turns it off; the kernels then run strictly one after another, as with <<<>>>).
+bool pdl_enabled();
+
+// A launch that lets the kernel start before its predecessor on the stream has finished
+// (the kernel must call pdl_wait(): see common.cuh), checked and counted like check_launch.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                      Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return check_launch(what);
 }
 
 // The stream argument of a C entry point, remembered for the launch-event hook.
@@ -201,10 +226,10 @@ int launch_bs_gemm(const CUtensorMap* a, const CUtensorMap* b, const BsArgs& arg
   const DeviceInfo di = device_info();
   const bool prof = g_prof_events && g_prof_i + 2 <= g_prof_n;
   if (prof) LL_CUDA(cudaEventRecord(g_prof_events[g_prof_i], stream));
-  kern<<<di.sms, Cfg::kThreads, Cfg::SMEM, stream>>>(tm, args);
-  const int rc = check_launch(EPI == EPI_F1   ? "grouped_mxfp4_bs_gemm F1 gate/up"
-                              : EPI == EPI_F2 ? "grouped_mxfp4_bs_gemm F2 down"
-                                              : "grouped_mxfp4_bs_gemm");
+  const int rc = launch_pdl(EPI == EPI_F1   ? "grouped_mxfp4_bs_gemm F1 gate/up"
+                            : EPI == EPI_F2 ? "grouped_mxfp4_bs_gemm F2 down"
+                                            : "grouped_mxfp4_bs_gemm",
+                            kern, dim3(di.sms), dim3(Cfg::kThreads), Cfg::SMEM, stream, tm, args);
   if (prof) {
     LL_CUDA(cudaEventRecord(g_prof_events[g_prof_i + 1], stream));
     g_prof_i += 2;

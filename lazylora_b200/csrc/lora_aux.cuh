@@ -77,6 +77,8 @@ template <int ADT, bool BROWS, int NC>
 __global__ void __launch_bounds__(256) k_skinny(const void* __restrict__ A, int M, int K, int lda,
                                                 const float* __restrict__ B0, const float* __restrict__ B1, int N0,
                                                 int N, int kc, float* __restrict__ part) {
+  pdl_wait();
+  pdl_launch_next();
   using SC = SkinnyCfg<NC>;
   constexpr int TM = SC::TM;
   __shared__ __align__(16) float As[kSkBK][SC::BM + 4];
@@ -178,12 +180,87 @@ __global__ void __launch_bounds__(256) k_skinny(const void* __restrict__ A, int 
 // C[m][n] = alpha * sum_split part[split][m][n], split order fixed; n < N0 -> C0, else C1
 __global__ void k_skinny_reduce(const float* __restrict__ part, int nsplit, int M, int N, int N0, float alpha,
                                 float* __restrict__ C0, float* __restrict__ C1) {
+  pdl_wait();
+  pdl_launch_next();
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= (int64_t)M * N) return;
   const float s = sum_splits(part + i, (int64_t)M * N, nsplit);
   const int m = (int)(i / N), n = (int)(i % N);
   if (n < N0) C0[(int64_t)m * N0 + n] = alpha * s;
   else C1[(int64_t)m * (N - N0) + (n - N0)] = alpha * s;
+}
+
+// ------------------------------------------------------------------ few-row products
+// C0 / C1 [m][n] = alpha * sum_k A[m][k] B[n][k] with B given as rows ([N][K], split over B0 /
+// B1 at N0), for few rows m: block (n, g) takes column n and rows g MR .. + MR - 1; its 256
+// threads stride over K in 8-element steps, the 16-byte loads of UN steps issued before their
+// FMAs, and the threads' partial sums are added in a fixed order (lanes by shuffle, then the 8
+// warps in order). One launch, no split partials in global memory. K % 8 == 0, A and B 16-byte
+// aligned.
+template <int ADT, int MR>
+__global__ void __launch_bounds__(256) k_gemv_rows(const void* __restrict__ A, int M, int K,
+                                                   const float* __restrict__ B0, const float* __restrict__ B1, int N0,
+                                                   int N, float alpha, float* __restrict__ C0, float* __restrict__ C1) {
+  pdl_wait();
+  pdl_launch_next();
+  constexpr int LW = ADT == 0 ? 2 : 1;               // 16-byte words per 8 elements of A
+  constexpr int ES = ADT == 0 ? 4 : 2;
+  constexpr int UN = MR >= 16 ? 1 : MR >= 4 ? 4 : 8;  // K steps whose loads are issued together
+  const int n = blockIdx.x, m0 = blockIdx.y * MR;
+  const int mr = min(MR, M - m0);
+  const float* b = n < N0 ? B0 + (int64_t)n * K : B1 + (int64_t)(n - N0) * K;
+  const char* a = reinterpret_cast<const char*>(A) + (int64_t)m0 * K * ES;
+  float acc[MR];
+#pragma unroll
+  for (int m = 0; m < MR; m++) acc[m] = 0.f;
+  const int nch = K / 8;
+  for (int c0 = threadIdx.x; c0 < nch; c0 += 256 * UN) {
+    float4 bq[UN][2];
+    uint4 raw[UN][MR][LW];
+#pragma unroll
+    for (int u = 0; u < UN; u++) {
+      const int c = c0 + 256 * u;
+      const bool in = c < nch;
+      bq[u][0] = in ? *reinterpret_cast<const float4*>(b + 8 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      bq[u][1] = in ? *reinterpret_cast<const float4*>(b + 8 * c + 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int m = 0; m < MR; m++)
+#pragma unroll
+        for (int w = 0; w < LW; w++)
+          raw[u][m][w] = (in && m < mr) ? *reinterpret_cast<const uint4*>(a + ((int64_t)m * K + 8 * c) * ES + 16 * w)
+                                        : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < UN; u++) {
+      const float bv[8] = {bq[u][0].x, bq[u][0].y, bq[u][0].z, bq[u][0].w,
+                           bq[u][1].x, bq[u][1].y, bq[u][1].z, bq[u][1].w};
+#pragma unroll
+      for (int m = 0; m < MR; m++) {
+        float av[8];
+        words8_as_float<ADT>(raw[u][m], av);
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[m] = fmaf(av[j], bv[j], acc[m]);
+      }
+    }
+  }
+  __shared__ float red[8][MR];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+#pragma unroll
+  for (int m = 0; m < MR; m++) {
+    float v = acc[m];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (lane == 0) red[warp][m] = v;
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < mr) {
+    float sum = red[0][threadIdx.x];
+#pragma unroll
+    for (int w = 1; w < 8; w++) sum += red[w][threadIdx.x];
+    const int64_t m = m0 + threadIdx.x;
+    if (n < N0) C0[m * N0 + n] = alpha * sum;
+    else C1[m * (N - N0) + (n - N0)] = alpha * sum;
+  }
 }
 
 // -------------------------------------------------------------------- rank-r expand
@@ -268,7 +345,17 @@ template <bool RROWS, bool HASY, bool TWO>
 __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ tok_pos, const float* __restrict__ Y, int k,
                                                    int T, int C, int r, float alpha, const float* __restrict__ L0,
                                                    const float* __restrict__ R0, const float* __restrict__ L1,
-                                                   const float* __restrict__ R1, float* __restrict__ out) {
+                                                   const float* __restrict__ R1, float* __restrict__ out,
+                                                   float* __restrict__ out1, const float* __restrict__ qtw,
+                                                   const float* __restrict__ qz, float* __restrict__ q_out) {
+  pdl_wait();
+  pdl_launch_next();
+  // gridDim.z == 2 (one product, TWO false): blocks z = 1 compute out1 = alpha L1 R1 instead
+  if (!TWO && blockIdx.z == 1) {
+    L0 = L1;
+    R0 = R1;
+    out = out1;
+  }
   extern __shared__ float Rs[];                          // [r][kExPitch], one R at a time
   __shared__ float Ls[kExTok][kExMaxR];
   __shared__ int ps[kExTok][32];
@@ -290,7 +377,21 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
     ex_stage_r<RROWS>(Rs, R, r, C, c0, nc);
     for (int i = threadIdx.x; i < kExTok * r; i += kExThreads) {
       const int tt = i / r, rr = i % r;
-      Ls[tt][rr] = (t0 + tt < T) ? Lm[(int64_t)(t0 + tt) * r + rr] : 0.f;
+      float l = 0.f;
+      if (t0 + tt < T) {
+        if (qz) {
+          // L0 = q: q[t][rr] = sum over the token's pairs (ascending expert) of tw * z, as k_q
+          for (int j = 0; j < k; j++) {
+            const int pos = tok_pos[(int64_t)(t0 + tt) * k + j];
+            if (pos < 0) break;
+            l = fmaf(qtw[pos], qz[(int64_t)pos * r + rr], l);
+          }
+          if (q_out && blockIdx.x == 0) q_out[(int64_t)(t0 + tt) * r + rr] = l;
+        } else {
+          l = Lm[(int64_t)(t0 + tt) * r + rr];
+        }
+      }
+      Ls[tt][rr] = l;
     }
     __syncthreads();
     if (c < nc)

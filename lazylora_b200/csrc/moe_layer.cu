@@ -32,6 +32,8 @@ constexpr int kTokBlock = 64;   // tokens per block in the counting sort
 
 // ----------------------------------------------------------------- counting sort
 __global__ void k_count(const int64_t* __restrict__ idx, int T, int k, int E, int* __restrict__ cnt) {
+  pdl_wait();
+  pdl_launch_next();
   extern __shared__ int hist[];
   for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
   __syncthreads();
@@ -49,6 +51,8 @@ __global__ void k_count(const int64_t* __restrict__ idx, int T, int k, int E, in
 // chunk list (experts split into runs of at most nmax rows).
 __global__ void __launch_bounds__(1024) k_scan(int* __restrict__ cnt, int nblk, int E, int nmax, int* __restrict__ offsets,
                                                Chunk* __restrict__ chunks, int* __restrict__ n_chunks) {
+  pdl_wait();
+  pdl_launch_next();
   using Scan = cub::BlockScan<int, 1024>;
   __shared__ typename Scan::TempStorage tmp;
   __shared__ int carry_rows, carry_chunks;
@@ -91,6 +95,8 @@ __global__ void __launch_bounds__(1024) k_scan(int* __restrict__ cnt, int nblk, 
 __global__ void k_scatter(const int64_t* __restrict__ idx, const float* __restrict__ w, int T, int k, int E,
                           const int* __restrict__ base, int* __restrict__ perm_token, int* __restrict__ perm_slot,
                           int* __restrict__ pair_pos, float* __restrict__ tw, int* __restrict__ tok_pos) {
+  pdl_wait();
+  pdl_launch_next();
   extern __shared__ int es[];   // [kTokBlock * k] expert of each pair, -1 if not routed here
   const int t0 = blockIdx.x * kTokBlock;
   const int t1 = min(T, t0 + kTokBlock);
@@ -133,19 +139,93 @@ __global__ void k_scatter(const int64_t* __restrict__ idx, const float* __restri
   }
 }
 
-// q[t][rr] = sum over the token's pairs (ascending expert) of tw * z
-__global__ void k_q(const int* __restrict__ tok_pos, const float* __restrict__ tw, const float* __restrict__ z, int T, int k,
-                    int r, float* __restrict__ q) {
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= (int64_t)T * r) return;
-  const int t = (int)(i / r), rr = (int)(i % r);
-  float acc = 0.f;
-  for (int j = 0; j < k; j++) {
-    const int pos = tok_pos[(int64_t)t * k + j];
-    if (pos < 0) break;
-    acc = fmaf(tw[pos], z[(int64_t)pos * r + rr], acc);
+// The three kernels above in one block, for a batch of at most kTokBlock tokens (nblk == 1),
+// with the same outputs bit for bit (the per-block bases of k_scan are the expert offsets
+// here); also clears perm_token (-1) and the status word, so that a few-token forward starts
+// with no copy or memset.
+__global__ void __launch_bounds__(1024) k_plan_small(const int64_t* __restrict__ idx, const float* __restrict__ w,
+                                                     int T, int k, int E, int nmax, int* __restrict__ offsets,
+                                                     Chunk* __restrict__ chunks, int* __restrict__ n_chunks,
+                                                     int* __restrict__ perm_token, int* __restrict__ perm_slot,
+                                                     int* __restrict__ pair_pos, float* __restrict__ tw,
+                                                     int* __restrict__ tok_pos, DevStatus* __restrict__ st) {
+  pdl_wait();
+  pdl_launch_next();
+  using Scan = cub::BlockScan<int, 1024>;
+  __shared__ typename Scan::TempStorage tmp;
+  __shared__ int carry_rows, carry_chunks;
+  extern __shared__ int sm[];
+  int* hist = sm;          // [E] counts, then each expert's first position
+  int* es = sm + E;        // [T k] expert of each pair, -1 if not routed here
+  const int np = T * k;
+  if (threadIdx.x == 0) {
+    carry_rows = 0;
+    carry_chunks = 0;
+    if (st) *st = DevStatus{0, 0, 0, 0};
   }
-  q[i] = acc;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+  for (int i = threadIdx.x; i < np; i += blockDim.x) perm_token[i] = -1;
+  __syncthreads();
+  for (int i = threadIdx.x; i < np; i += blockDim.x) {
+    const int64_t e = idx[i];
+    const bool ok = e >= 0 && e < E;
+    es[i] = ok ? (int)e : -1;
+    if (ok) atomicAdd(&hist[e], 1);
+  }
+  __syncthreads();
+  for (int e0 = 0; e0 < E; e0 += 1024) {
+    const int e = e0 + threadIdx.x;
+    const int total = e < E ? hist[e] : 0;
+    const int nch = (total + nmax - 1) / nmax;
+    int row_off, ch_off, agg_rows, agg_ch;
+    Scan(tmp).ExclusiveSum(total, row_off, agg_rows);
+    __syncthreads();
+    Scan(tmp).ExclusiveSum(nch, ch_off, agg_ch);
+    __syncthreads();
+    if (e < E) {
+      const int base = carry_rows + row_off;
+      offsets[e] = base;
+      hist[e] = base;
+      const int cb = carry_chunks + ch_off;
+      for (int i = 0; i < nch; i++) chunks[cb + i] = Chunk{e, base + i * nmax, min(nmax, total - i * nmax), 0};
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) { carry_rows += agg_rows; carry_chunks += agg_ch; }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    offsets[E] = carry_rows;
+    *n_chunks = carry_chunks;
+  }
+  for (int i = threadIdx.x; i < np; i += blockDim.x) {
+    const int e = es[i];
+    if (e < 0) {
+      pair_pos[i] = -1;
+      continue;
+    }
+    int rank = 0;
+    for (int j = 0; j < i; j++) rank += (es[j] == e);
+    const int pos = hist[e] + rank;
+    pair_pos[i] = pos;
+    perm_token[pos] = i / k;
+    perm_slot[pos] = i % k;
+    tw[pos] = w[i];
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    int ee[32], pp[32];
+    int n = 0;
+    for (int sl = 0; sl < k; sl++) {
+      const int e = es[t * k + sl];
+      if (e < 0) continue;
+      const int pos = pair_pos[(int64_t)t * k + sl];
+      int j = n++;
+      while (j > 0 && ee[j - 1] > e) { ee[j] = ee[j - 1]; pp[j] = pp[j - 1]; j--; }
+      ee[j] = e;
+      pp[j] = pos;
+    }
+    for (int sl = 0; sl < k; sl++) tok_pos[(int64_t)t * k + sl] = sl < n ? pp[sl] : -1;
+  }
 }
 
 // Per valid pair: one power-of-two scale for both rows of dg / du, fp16 copies for B2.
@@ -496,7 +576,26 @@ static int bs_operand(int kind, const LayerWs& W, const void* src, int src_dtype
 // fixed order.
 int skinny(const void* A, int adt, bool brows, int M, int K, const float* B0, const float* B1, int N0, int N,
            float alpha, float* C0, float* C1, float* part, size_t part_floats, cudaStream_t s) {
-  if (K % 8 || M <= 0 || N <= 0 || part_floats < (size_t)M * N) return LL_ERR_ARG;
+  if (K % 8 || M <= 0 || N <= 0) return LL_ERR_ARG;
+  const bool al16 = ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B0) |
+                      reinterpret_cast<uintptr_t>(B1 ? B1 : B0)) & 15) == 0;
+  if (brows && M <= 128 && al16) {        // few rows: one launch, no partials
+#define LL_GV(ADT, MR) \
+  return launch_pdl("k_gemv_rows", k_gemv_rows<ADT, MR>, dim3(N, (M + MR - 1) / MR), dim3(256), 0, s, A, M, K, B0, B1, \
+                    N0, N, alpha, C0, C1)
+#define LL_GVM(ADT) \
+  do {                                     \
+    if (M == 1) LL_GV(ADT, 1);             \
+    if (M <= 4) LL_GV(ADT, 4);             \
+    LL_GV(ADT, 16);                        \
+  } while (0)
+    if (adt == 0) LL_GVM(0);
+    if (adt == 1) LL_GVM(1);
+    LL_GVM(2);
+#undef LL_GVM
+#undef LL_GV
+  }
+  if (part_floats < (size_t)M * N) return LL_ERR_ARG;
   const bool nc16 = N <= 16;
   const int BM = nc16 ? SkinnyCfg<16>::BM : SkinnyCfg<32>::BM, NC = nc16 ? 16 : 32;
   const int mblocks = (M + BM - 1) / BM, nblocks = (N + NC - 1) / NC;
@@ -510,8 +609,10 @@ int skinny(const void* A, int adt, bool brows, int M, int K, const float* B0, co
   dim3 grid(mblocks, nblocks, nsplit);
 #define LL_SK(ADT, BR)                                                                             \
   do {                                                                                             \
-    if (nc16) k_skinny<ADT, BR, 16><<<grid, 256, 0, s>>>(A, M, K, K, B0, B1, N0, N, kc, part);     \
-    else k_skinny<ADT, BR, 32><<<grid, 256, 0, s>>>(A, M, K, K, B0, B1, N0, N, kc, part);          \
+    if (nc16) LL_TRY(launch_pdl("k_skinny", k_skinny<ADT, BR, 16>, grid, dim3(256), 0, s, A, M, K, K, B0, B1, N0, \
+                                N, kc, part));                                                       \
+    else LL_TRY(launch_pdl("k_skinny", k_skinny<ADT, BR, 32>, grid, dim3(256), 0, s, A, M, K, K, B0, B1, N0, N,   \
+                           kc, part));                                                               \
   } while (0)
   if (brows) {
     if (adt == 0) LL_SK(0, true); else if (adt == 1) LL_SK(1, true); else LL_SK(2, true);
@@ -519,24 +620,27 @@ int skinny(const void* A, int adt, bool brows, int M, int K, const float* B0, co
     if (adt == 0) LL_SK(0, false); else if (adt == 1) LL_SK(1, false); else LL_SK(2, false);
   }
 #undef LL_SK
-  LL_TRY(check_launch("k_skinny"));
   const int64_t n = (int64_t)M * N;
-  k_skinny_reduce<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, nsplit, M, N, N0, alpha, C0, C1);
-  return check_launch("k_skinny_reduce");
+  return launch_pdl("k_skinny_reduce", k_skinny_reduce, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, part,
+                    nsplit, M, N, N0, alpha, C0, C1);
 }
 
 // Rank-r expand with the optional ascending-expert sum of per-pair rows (see k_expand).
 int expand(bool rrows, const int* tok_pos, const float* Y, int k, int T, int C, int r, float alpha, const float* L0,
-           const float* R0, const float* L1, const float* R1, float* out, cudaStream_t s) {
+           const float* R0, const float* L1, const float* R1, float* out, cudaStream_t s, float* out1,
+           const float* qtw, const float* qz, float* q_out) {
   if (C % 4 || r > kExMaxR || k > 32) return LL_ERR_ARG;
-  dim3 grid((C + kExCols - 1) / kExCols, (T + kExTok - 1) / kExTok);
-  const bool hasy = Y != nullptr, two = L1 != nullptr;
+  if (out1 && (!L1 || !R1)) return LL_ERR_ARG;
+  if (qz && (!tok_pos || !qtw)) return LL_ERR_ARG;
+  dim3 grid((C + kExCols - 1) / kExCols, (T + kExTok - 1) / kExTok, out1 ? 2 : 1);
+  const bool hasy = Y != nullptr, two = L1 != nullptr && !out1;
   const int smem = r * kExPitch * (int)sizeof(float);  // <= 129 KB at r = 64
   auto attr = [&](const void* f) { return set_smem_attr(f, smem); };
 #define LL_EX(RR, HY, TW)                                                                                   \
   do {                                                                                                      \
     LL_TRY(attr(reinterpret_cast<const void*>(k_expand<RR, HY, TW>)));                                     \
-    k_expand<RR, HY, TW><<<grid, kExThreads, smem, s>>>(tok_pos, Y, k, T, C, r, alpha, L0, R0, L1, R1, out); \
+    LL_TRY(launch_pdl("k_expand", k_expand<RR, HY, TW>, grid, dim3(kExThreads), smem, s, tok_pos, Y, k, T, C, r,   \
+                      alpha, L0, R0, L1, R1, out, out1, qtw, qz, q_out));                                   \
   } while (0)
   if (rrows) {
     if (hasy) { if (two) LL_EX(true, true, true); else LL_EX(true, true, false); }
@@ -546,7 +650,7 @@ int expand(bool rrows, const int* tok_pos, const float* Y, int k, int T, int C, 
     else { if (two) LL_EX(false, false, true); else LL_EX(false, false, false); }
   }
 #undef LL_EX
-  return check_launch("k_expand");
+  return LL_OK;
 }
 
 // out = s * sum_n Pm(n, :)^T Q[n][:], stored [r][C] or transposed [C][r]
@@ -638,15 +742,19 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   const int nblk = (T + kTokBlock - 1) / kTokBlock;
   g_launch_count = 0;
 
-  LL_TRY(reset_status(W.st, s));
-  LL_CUDA(cudaMemsetAsync(W.perm_token, 0xFF, sizeof(int) * P, s));
-  k_count<<<nblk, 256, E * sizeof(int), s>>>(idx, T, k, E, W.cnt);
-  LL_TRY(check_launch("k_count"));
-  k_scan<<<1, 1024, 0, s>>>(W.cnt, nblk, E, W.nmax, W.offsets, W.chunks, W.n_chunks);
-  LL_TRY(check_launch("k_scan"));
-  k_scatter<<<nblk, 256, kTokBlock * k * sizeof(int), s>>>(idx, w, T, k, E, W.cnt, W.perm_token, W.perm_slot,
-                                                            W.pair_pos, W.tw, W.tok_pos);
-  LL_TRY(check_launch("k_scatter"));
+  if (nblk == 1) {    // few tokens: the counting sort in one block, no memset
+    LL_TRY(launch_pdl("k_plan_small", k_plan_small, dim3(1), dim3(1024), (size_t)(E + P) * sizeof(int), s, idx, w, T,
+                      k, E, W.nmax, W.offsets, W.chunks, W.n_chunks, W.perm_token, W.perm_slot, W.pair_pos, W.tw,
+                      W.tok_pos, W.st));
+  } else {
+    LL_TRY(reset_status(W.st, s));
+    LL_CUDA(cudaMemsetAsync(W.perm_token, 0xFF, sizeof(int) * P, s));
+    LL_TRY(launch_pdl("k_count", k_count, dim3(nblk), dim3(256), E * sizeof(int), s, idx, T, k, E, W.cnt));
+    LL_TRY(launch_pdl("k_scan", k_scan, dim3(1), dim3(1024), 0, s, W.cnt, nblk, E, W.nmax, W.offsets, W.chunks,
+                      W.n_chunks));
+    LL_TRY(launch_pdl("k_scatter", k_scatter, dim3(nblk), dim3(256), kTokBlock * k * sizeof(int), s, idx, w, T, k, E,
+                      W.cnt, W.perm_token, W.perm_slot, W.pair_pos, W.tw, W.tok_pos));
+  }
   // Tiles up to 64 rows: the forward GEMMs run on the block-scaled MMAs (weights not decoded;
   // E2M1 activation terms up to 32 rows, E4M3 at 64); 128-row tiles (the large-T regime) on the
   // fp16 dequant path.
@@ -654,8 +762,9 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   const bool bs = kind >= 0;
   if (!bs) LL_TRY(launch_token_rows_to_half(x, x_dtype, W.perm_token, W.tok_pos, T, k, d, W.xh, W.xinv, s));
   LL_TRY(skinny(x, x_dtype, true, T, d, L->A_g, L->A_u, r, 2 * r, 1.f, W.xa_g, W.xa_u, W.skpart, W.skpart_floats, s));
-  LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_g, L->B_g, nullptr, nullptr, W.dlt_g, s));
-  LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_u, L->B_u, nullptr, nullptr, W.dlt_u, s));
+  // the gate and up deltas in one launch
+  LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_g, L->B_g, W.xa_u, L->B_u, W.dlt_g, s,
+                W.dlt_u));
   // F1: gate / up
   if (bs) {
     CUtensorMap a[2], b[4];
@@ -714,11 +823,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   const int* n_valid = W.offsets + E;
   // z = h . A_d^T per pair (h as the fp16 rows the down GEMM reads)
   LL_TRY(skinny(W.H, 2, true, P, f, L->A_d, nullptr, r, r, 1.f, W.z, nullptr, W.skpart, W.skpart_floats, s));
-  {
-    const int64_t n = (int64_t)T * r;
-    k_q<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(W.tok_pos, W.tw, W.z, T, k, r, W.q);
-    LL_TRY(check_launch("k_q"));
-  }
+  // (q = the routing-weighted sum of z per token is formed by the combine below)
   // F2: down (paired 128-row tiles of the stack: d a multiple of 256)
   if (bs && d % 256 == 0) {
     CUtensorMap a[2], b[4];
@@ -765,7 +870,8 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
     a.epi.Y = W.Y;
     LL_TRY((gemm_nmax<EPI_F2, 2, 1, false>(W.nmax, pk, sc, act, a, s)));
   }
-  return expand(false, W.tok_pos, W.Y, k, T, d, r, L->lora_scaling, W.q, L->B_d, nullptr, nullptr, out, s);
+  return expand(false, W.tok_pos, W.Y, k, T, d, r, L->lora_scaling, nullptr, L->B_d, nullptr, nullptr, out, s, nullptr,
+                W.tw, W.z, W.q);
 }
 
 int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dtype, const int64_t* idx, const float* w,

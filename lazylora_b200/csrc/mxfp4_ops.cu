@@ -93,6 +93,14 @@ int set_smem_attr(const void* func, int bytes) {
   return LL_OK;
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("LL_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 int reset_status(DevStatus* st, cudaStream_t s) {
   LL_CUDA(cudaMemsetAsync(st, 0, sizeof(DevStatus), s));
   return LL_OK;

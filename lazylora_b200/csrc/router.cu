@@ -15,6 +15,8 @@ template <int MODE, int PER_LANE>
 __global__ void k_route_select(const float* __restrict__ a, const float* __restrict__ b, const float* __restrict__ bias,
                                int T, int E, int k, int renorm, float rsf, int64_t* __restrict__ idx,
                                float* __restrict__ w, float* __restrict__ scores_out, int nsplit) {
+  pdl_wait();
+  pdl_launch_next();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (warp >= T) return;
@@ -114,22 +116,174 @@ __global__ void k_route_select(const float* __restrict__ a, const float* __restr
   }
 }
 
+// The same selection for few tokens, one block per token: each of the 8 warps takes the top k of
+// its slice of experts (expert e = 256 i + 32 w + lane), then warp 0 merges the 8 lists. The
+// top k of the union of the slices' top k is the top k overall, with the same order and tie
+// rule (higher value, then lower id), and every score is computed in the same order as above,
+// so indices and weights are bit for bit those of k_route_select.
+constexpr int kSelWarps = 8;
+template <int MODE, int PL>
+__global__ void __launch_bounds__(kSelWarps * 32) k_route_select_block(
+    const float* __restrict__ a, const float* __restrict__ b, const float* __restrict__ bias, int T, int E, int k,
+    int renorm, float rsf, int64_t* __restrict__ idx, float* __restrict__ w, float* __restrict__ scores_out,
+    int nsplit) {
+  pdl_wait();
+  pdl_launch_next();
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  const int wp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  __shared__ float c_ch[kSelWarps][32], c_sc[kSelWarps][32];
+  __shared__ int c_e[kSelWarps][32];
+  float sc[PL], ch[PL];
+#pragma unroll
+  for (int i = 0; i < PL; i++) sc[i] = 0.f;
+  if (MODE == 0) {     // the splits' partial logits, added in split order, a split's loads together
+#pragma unroll
+    for (int i = 0; i < PL; i++) {
+      const int e = 256 * i + 32 * wp + lane;
+      if (e < E) sc[i] = a[(int64_t)t * E + e];
+    }
+    int sp = 1;
+    for (; sp + 8 <= nsplit; sp += 8) {        // eight splits' loads in flight, added in order
+      float v[8][PL];
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+#pragma unroll
+        for (int i = 0; i < PL; i++) {
+          const int e = 256 * i + 32 * wp + lane;
+          v[u][i] = e < E ? a[((int64_t)(sp + u) * T + t) * E + e] : 0.f;
+        }
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+#pragma unroll
+        for (int i = 0; i < PL; i++)
+          if (256 * i + 32 * wp + lane < E) sc[i] += v[u][i];
+    }
+    for (; sp < nsplit; sp++) {
+      const float* ap = a + ((int64_t)sp * T + t) * E;
+#pragma unroll
+      for (int i = 0; i < PL; i++) {
+        const int e = 256 * i + 32 * wp + lane;
+        if (e < E) sc[i] += ap[e];
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < PL; i++) {
+    const int e = 256 * i + 32 * wp + lane;
+    ch[i] = -INFINITY;
+    const float l = sc[i];
+    sc[i] = 0.f;
+    if (e >= E) continue;
+    if (MODE == 0) {
+      const float sg = 1.0f / (1.0f + expf(-l));
+      sc[i] = sg;
+      ch[i] = bias ? sg + bias[e] : sg;
+      if (scores_out) scores_out[(int64_t)t * E + e] = sg;
+    } else {
+      sc[i] = a[(int64_t)t * E + e];
+      ch[i] = b[(int64_t)t * E + e];
+    }
+  }
+  // this warp's top k
+  uint32_t taken = 0;
+  for (int kk = 0; kk < k; kk++) {
+    float bv = -INFINITY;
+    int be = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < PL; i++) {
+      const int e = 256 * i + 32 * wp + lane;
+      if (e < E && !((taken >> i) & 1) && (ch[i] > bv || (ch[i] == bv && e < be))) { bv = ch[i]; be = e; }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, off);
+      if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+    }
+    float mine = 0.f;
+#pragma unroll
+    for (int i = 0; i < PL; i++)
+      if (256 * i + 32 * wp + lane == be) { taken |= 1u << i; mine = sc[i]; }
+    const float sv = __shfl_sync(0xffffffffu, mine, (be & 31));
+    if (lane == 0) { c_ch[wp][kk] = bv; c_sc[wp][kk] = sv; c_e[wp][kk] = be; }
+  }
+  __syncthreads();
+  if (wp != 0) return;
+  // merge: lane j holds candidate j of every warp's list
+  float mch[kSelWarps], msc[kSelWarps];
+  int me[kSelWarps];
+#pragma unroll
+  for (int v = 0; v < kSelWarps; v++) {
+    const bool ok = lane < k;
+    mch[v] = ok ? c_ch[v][lane] : -INFINITY;
+    msc[v] = ok ? c_sc[v][lane] : 0.f;
+    me[v] = ok ? c_e[v][lane] : 0x7fffffff;
+  }
+  uint32_t used = 0;
+  float wsel = 0.f, denom_l[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  int esel = 0;
+  for (int kk = 0; kk < k; kk++) {
+    float bv = -INFINITY;
+    int be = 0x7fffffff;
+#pragma unroll
+    for (int v = 0; v < kSelWarps; v++)
+      if (!((used >> v) & 1) && me[v] < E && (mch[v] > bv || (mch[v] == bv && me[v] < be))) { bv = mch[v]; be = me[v]; }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, off);
+      if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+    }
+    float mine = 0.f;
+    bool found = false;
+#pragma unroll
+    for (int v = 0; v < kSelWarps; v++)
+      if (me[v] == be && !((used >> v) & 1)) { used |= 1u << v; mine = msc[v]; found = true; }
+    const uint32_t holder = __ballot_sync(0xffffffffu, found);
+    const float sv = __shfl_sync(0xffffffffu, mine, holder ? __ffs(holder) - 1 : 0);
+    denom_l[kk & 7] += sv;            // every lane, in the order of the warp kernel's lane 0
+    if (lane == kk) { wsel = sv; esel = be; }
+  }
+  float denom = 0.f;
+  if (k > 1 && renorm) {
+    denom = denom_l[0];
+    for (int i = 1; i < 8; i++) denom += denom_l[i];
+    denom += 1e-20f;
+  }
+  if (lane < k) {
+    float v = wsel;
+    if (k > 1 && renorm) v = v / denom;
+    idx[(int64_t)t * k + lane] = esel;
+    w[(int64_t)t * k + lane] = v * rsf;
+  }
+}
+
+// Few tokens: a block of 8 warps per token (k_route_select_block), else a warp per token.
+static bool select_by_block(int T, int E, int k) { return T <= 256 && k <= 32 && E <= 256 * 4; }
+
 template <int MODE>
 static int launch_select(const float* a, const float* b, const float* bias, int T, int E, int k, int renorm, float rsf,
                          int64_t* idx, float* w, float* scores_out, cudaStream_t s, int nsplit = 1) {
-  const int blocks = (T * 32 + 255) / 256;
+  if (select_by_block(T, E, k))
+    return launch_pdl("k_route_select", k_route_select_block<MODE, 4>, dim3(T), dim3(kSelWarps * 32), 0, s, a, b,
+                      bias, T, E, k, renorm, rsf, idx, w, scores_out, nsplit);
+  const dim3 blocks((T * 32 + 255) / 256);
   if (E <= 32 * 32)
-    k_route_select<MODE, 32><<<blocks, 256, 0, s>>>(a, b, bias, T, E, k, renorm, rsf, idx, w, scores_out, nsplit);
-  else
-    k_route_select<MODE, 64><<<blocks, 256, 0, s>>>(a, b, bias, T, E, k, renorm, rsf, idx, w, scores_out, nsplit);
-  return check_launch("k_route_select");
+    return launch_pdl("k_route_select", k_route_select<MODE, 32>, blocks, dim3(256), 0, s, a, b, bias, T, E, k, renorm,
+                      rsf, idx, w, scores_out, nsplit);
+  return launch_pdl("k_route_select", k_route_select<MODE, 64>, blocks, dim3(256), 0, s, a, b, bias, T, E, k, renorm,
+                    rsf, idx, w, scores_out, nsplit);
 }
 
 // logits[i] = sum over the nsplit partials of element i, added in split order.
 __global__ void k_sum_partials(const float* __restrict__ part, int nsplit, int64_t n, float* __restrict__ logits) {
+  pdl_wait();
+  pdl_launch_next();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   float acc = part[i];
+#pragma unroll 8
   for (int sp = 1; sp < nsplit; sp++) acc += part[(int64_t)sp * n + i];
   logits[i] = acc;
 }
@@ -172,9 +326,8 @@ static int launch_router_mma(const RouterMaps& maps, float* part, int T, int E, 
   using Cf = RouterCfg<NP, BN>;
   auto kern = k_router_mma<NP, BN>;
   LL_TRY(set_smem_attr(reinterpret_cast<const void*>(kern), Cf::SMEM));
-  dim3 grid(p.mt, p.nt, p.nsplit);
-  kern<<<grid, kRtWarps * 32, Cf::SMEM, s>>>(maps, part, T, E, p.kb_total, p.kbps, st);
-  return check_launch("k_router_mma");
+  return launch_pdl("k_router_mma", kern, dim3(p.mt, p.nt, p.nsplit), dim3(kRtWarps * 32), Cf::SMEM, s, maps, part, T,
+                    E, p.kb_total, p.kbps, st);
 }
 
 // planes: the router weight split into its three bf16 planes (hi, lo, lo2; [3][E][d]), or null
@@ -241,14 +394,17 @@ static int route_topk(const void* x, int x_dtype, const float* router_w, const _
   g_launch_count = 0;
   LL_TRY(router_logits_tc(x, x_dtype, router_w, planes, T, d, E, ws, p, s));
   const float* part = reinterpret_cast<const float*>(static_cast<uint8_t*>(ws) + p.off_part);
-  if (p.nsplit > 1) {   // the K splits' partials, summed in split order by a wide kernel
+  if (p.nsplit > 1 && !select_by_block(T, E, k)) {   // the K splits' partials, summed in split order by a wide kernel
     float* logits = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + p.off_logits);
     const int64_t n = (int64_t)T * E;
-    k_sum_partials<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, p.nsplit, n, logits);
-    LL_TRY(check_launch("k_sum_partials"));
-    part = logits;
+    LL_TRY(launch_pdl("k_sum_partials", k_sum_partials, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, part,
+                      p.nsplit, n, logits));
+    return launch_select<0>(logits, nullptr, bias, T, E, k, renormalize, routed_scaling_factor, idx, w, scores_out, s,
+                            1);
   }
-  return launch_select<0>(part, nullptr, bias, T, E, k, renormalize, routed_scaling_factor, idx, w, scores_out, s, 1);
+  // few tokens: the selection kernel adds the splits' partials itself (in split order)
+  return launch_select<0>(part, nullptr, bias, T, E, k, renormalize, routed_scaling_factor, idx, w, scores_out, s,
+                          p.nsplit);
 }
 
 int ll_route_topk(const void* x, int x_dtype, const float* router_w, const float* bias, int T, int d, int E, int k,

@@ -79,6 +79,8 @@ k_router_mma(const __grid_constant__ RouterMaps maps, float* __restrict__ part, 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_launch_next();                        // (after the allocation)
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {

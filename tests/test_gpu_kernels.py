@@ -93,6 +93,27 @@ def test_route_select_bit_exact():
         assert float(ulp.max()) <= 1.0
 
 
+def test_route_select_block_path_equals_warp_path():
+    """Up to 256 tokens the selection runs a block per token (8 warps over slices of the
+    experts, then a merge); above that a warp per token. The first rows of a 300-token batch
+    select the same ids with the same weight bits either way, also with many tied scores
+    (scores rounded to 1/64: ties broken to the lower id) and k = 16, 32."""
+    from lazylora_b200.core.moe_router import route_select
+    g = torch.Generator().manual_seed(14)
+    for (E, k, tied) in [(896, 8, False), (896, 8, True), (384, 16, True), (1024, 32, False), (64, 8, True)]:
+        scores = torch.sigmoid(torch.randn(300, E, generator=g))
+        if tied:
+            scores = torch.round(scores * 64) / 64
+        sfc = scores + (0 if tied else torch.randn(E, generator=g) * 0.05)
+        big_i, big_w = route_select(scores.cuda(), sfc.cuda(), k)          # warp per token
+        small_i, small_w = route_select(scores[:37].cuda(), sfc[:37].cuda(), k)   # block per token
+        assert torch.equal(small_i, big_i[:37]), (E, k, tied)
+        assert torch.equal(small_w.view(torch.int32), big_w[:37].view(torch.int32)), (E, k, tied)
+        if not tied:    # (torch.topk leaves the order of ties unspecified)
+            want_i, _ = O.route_select(scores[:37], sfc[:37], k)
+            assert torch.equal(small_i.cpu(), want_i), (E, k, tied)
+
+
 def test_router_forward_matches_reference_routing():
     from lazylora_b200.core.moe_router import KimiK3MoERouter
     g = torch.Generator().manual_seed(5)
