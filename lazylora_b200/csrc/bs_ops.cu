@@ -140,93 +140,113 @@ __global__ void __launch_bounds__(kE3Threads) k_rows_to_e4m3x3(const void* __res
 
 // The BS_FP4 activation terms: per row, four rounds of (per 32-element block: max |r|, scale
 // 2^e with e the smallest exponent bringing that max into [-6, 6], round r / 2^e to E2M1,
-// subtract). Term t of row p: packed codes dst[t][p][K/2] (two per byte, even element in the low
-// nibble) and E8M0 scale bytes sc[t][p][K/32] (e + 127). A 32-element block is 4 neighbouring
-// threads' 8 values, so the block max is two shuffles.
+// subtract). Term t of pair row p: packed codes dst[t][p][K/2] (two per byte, even element in
+// the low nibble). A 32-element block is 4 neighbouring threads' 8 values, so the block max is
+// two shuffles, and a row splits over blocks with no reduction: block (x, y) takes source row x,
+// 8-element chunks [256 y, 256 y + 256) (16 stages of 128 K).
+// The E8M0 scale bytes go straight into the MMA's B scale blocks of the row's chunk: block
+// (chunk c, stage ks) of 512 bytes holds, for B row n = t npad + j (term t, chunk row j), the
+// row's 4 scale bytes of the stage at word (n % 32) * 4 + (n % 128) / 32 (the tcgen05.cp layout).
+// The other words are left as they are: they only scale B rows past the chunk's rows (MMA
+// columns the epilogue never reads, as the MMA's columns are independent) or past the MMA's N.
 template <int SRC, bool TOK>
 __global__ void __launch_bounds__(kE3Threads) k_rows_to_e2m1x4(const void* __restrict__ src, int src_rows,
                                                                const int* __restrict__ tok_pos, int k,
                                                                const int* __restrict__ n_valid, int K, int64_t P,
-                                                               uint8_t* __restrict__ dst, uint8_t* __restrict__ sc) {
+                                                               uint8_t* __restrict__ dst,
+                                                               const Chunk* __restrict__ chunks,
+                                                               const int* __restrict__ chunk_of,
+                                                               uint32_t* __restrict__ sfb) {
   pdl_wait();
   pdl_launch_next();
-  // block (x, y): row x, 8-element chunks [y 256, y 256 + 256) of it (the scales are per
-  // 32-element block, four adjacent threads, so a row splits over blocks with no reduction)
   const int r = blockIdx.x;
   if (r >= src_rows) return;
   if (!TOK && n_valid && r >= *n_valid) return;
-  const int nch = K / 8;
-  const int ch0 = blockIdx.y * kE3Threads;
-  constexpr int NC = 1;
-  float v[NC][8];
+  const int nch = K / 8, n_stage = K / 128;
+  const int ch = blockIdx.y * kE3Threads + threadIdx.x;
+  const int ks = ch / 16;                        // stage of this thread's chunk
+  const bool lead = (ch & 15) == 0;              // writes the stage's scale word
+  constexpr int WPB = kBsSfBlock / 4;            // words per scale block
+  float v[8];
 #pragma unroll
-  for (int i = 0; i < NC; i++) {
-    const int ch = ch0 + threadIdx.x;
-#pragma unroll
-    for (int j = 0; j < 8; j++) v[i][j] = 0.f;
-    if (ch < nch) load8<SRC>(src, r, K, ch, v[i]);
+  for (int j = 0; j < 8; j++) v[j] = 0.f;
+  if (ch < nch) load8<SRC>(src, r, K, ch, v);
+  // destinations (pair row, chunk, row in the chunk, padded chunk rows), looked up by one thread
+  // each so that their loads overlap
+  __shared__ int s_p[32], s_c[32], s_jr[32], s_npad[32];
+  const int nd = TOK ? k : 1;
+  if ((int)threadIdx.x < nd) {
+    const int j = threadIdx.x;
+    const int p = TOK ? tok_pos[(int64_t)r * k + j] : r;
+    s_p[j] = p;
+    if (p >= 0) {
+      const int c = chunk_of[p];
+      const Chunk cc = chunks[c];
+      s_c[j] = c;
+      s_jr[j] = p - cc.p0;
+      s_npad[j] = (cc.n + 15) & ~15;
+    }
   }
+  __syncthreads();
 #pragma unroll 1
   for (int t = 0; t < kBsTermsFp4; t++) {
-    uint32_t q[NC];
-    uint8_t sbyte[NC];
+    float mx = 0.f;
 #pragma unroll
-    for (int i = 0; i < NC; i++) {
-      float mx = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; j++) mx = fmaxf(mx, fabsf(v[i][j]));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      // smallest e with mx / 2^e <= 6
-      int e = -127;
-      if (mx > 0.f && isfinite(mx)) {
-        int E;
-        const float m = frexpf(mx, &E);            // mx = m 2^E, m in [0.5, 1)
-        e = m <= 0.75f ? E - 3 : E - 2;
-        e = e < -127 ? -127 : (e > 127 ? 127 : e);
-      }
-      sbyte[i] = (uint8_t)(e + 127);
-      const float inv = ldexpf(1.f, -e), scl = ldexpf(1.f, e);
-      uint32_t word = 0;
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const uint32_t b = f32x2_to_e2m1x2(v[i][2 * j] * inv, v[i][2 * j + 1] * inv);
-        word |= b << (8 * j);
-        const uint32_t h = e2m1x2_to_half2(b);
-        const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&h));
-        v[i][2 * j] -= d.x * scl;                   // the residual the next term takes
-        v[i][2 * j + 1] -= d.y * scl;
-      }
-      q[i] = word;
+    for (int j = 0; j < 8; j++) mx = fmaxf(mx, fabsf(v[j]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    // smallest e with mx / 2^e <= 6
+    int e = -127;
+    if (mx > 0.f && isfinite(mx)) {
+      int E;
+      const float m = frexpf(mx, &E);            // mx = m 2^E, m in [0.5, 1)
+      e = m <= 0.75f ? E - 3 : E - 2;
+      e = e < -127 ? -127 : (e > 127 ? 127 : e);
     }
-    for (int j = 0; j < (TOK ? k : 1); j++) {
-      const int p = TOK ? tok_pos[(int64_t)r * k + j] : r;
-      if (p < 0) continue;
-      uint32_t* row = reinterpret_cast<uint32_t*>(dst + ((int64_t)t * P + p) * (K / 2));
-      uint8_t* srow = sc + ((int64_t)t * P + p) * (K / 32);
+    const uint32_t sbyte = (uint32_t)(e + 127);
+    const float inv = ldexpf(1.f, -e), scl = ldexpf(1.f, e);
+    uint32_t word = 0;
 #pragma unroll
-      for (int i = 0; i < NC; i++) {
-        const int ch = ch0 + threadIdx.x;
-        if (ch < nch) {
-          row[ch] = q[i];
-          if ((ch & 3) == 0) srow[ch / 4] = sbyte[i];
-        }
+    for (int j = 0; j < 4; j++) {
+      const uint32_t b = f32x2_to_e2m1x2(v[2 * j] * inv, v[2 * j + 1] * inv);
+      word |= b << (8 * j);
+      const uint32_t h = e2m1x2_to_half2(b);
+      const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&h));
+      v[2 * j] -= d.x * scl;                     // the residual the next term takes
+      v[2 * j + 1] -= d.y * scl;
+    }
+    // the stage's four scale bytes (blocks of the threads + 0, 4, 8, 12), lowest block first
+    const uint32_t s1 = __shfl_down_sync(0xffffffffu, sbyte, 4);
+    const uint32_t s2 = __shfl_down_sync(0xffffffffu, sbyte, 8);
+    const uint32_t s3 = __shfl_down_sync(0xffffffffu, sbyte, 12);
+    const uint32_t sw = sbyte | (s1 << 8) | (s2 << 16) | (s3 << 24);
+    for (int j = 0; j < nd; j++) {
+      const int p = s_p[j];
+      if (p < 0) continue;
+      if (ch < nch) reinterpret_cast<uint32_t*>(dst + ((int64_t)t * P + p) * (K / 2))[ch] = word;
+      if (lead && ch < nch) {
+        const int n = t * s_npad[j] + s_jr[j];
+        sfb[((int64_t)s_c[j] * n_stage + ks) * WPB + (n % 32) * 4 + (n % 128) / 32] = sw;
       }
     }
   }
 }
 
 int launch_rows_to_e2m1x4(const void* src, int src_dtype, int src_rows, const int* tok_pos, int k,
-                          const int* n_valid, int K, int64_t P, uint8_t* dst, uint8_t* sc, cudaStream_t s) {
+                          const int* n_valid, int K, int64_t P, uint8_t* dst, const Chunk* chunks, const int* chunk_of,
+                          int nmax, uint8_t* sfb, cudaStream_t s) {
   if (src_rows <= 0) return LL_OK;
-  if (!src || !dst || !sc || K <= 0 || K % 32 || K > 8 * kE3Chunks * kE3Threads || src_dtype < 0 || src_dtype > 2)
+  if (!src || !dst || !chunks || !chunk_of || !sfb || K <= 0 || K % 128 || src_dtype < 0 || src_dtype > 2 ||
+      k > 32 || nmax > 32 || 4 * nmax > 128)
     return LL_ERR_ARG;
-  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) % 16) return LL_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(sfb)) % 16)
+    return LL_ERR_ARG;
   const bool tok = tok_pos != nullptr;
-#define LL_E2(SRC, TOKV)                                                                              \
-  LL_TRY(launch_pdl("k_rows_to_e2m1x4", k_rows_to_e2m1x4<SRC, TOKV>,                                      \
+  uint32_t* sw = reinterpret_cast<uint32_t*>(sfb);
+#define LL_E2(SRC, TOKV)                                                                                      \
+  LL_TRY(launch_pdl("k_rows_to_e2m1x4", k_rows_to_e2m1x4<SRC, TOKV>,                                        \
                     dim3(src_rows, (K / 8 + kE3Threads - 1) / kE3Threads), dim3(kE3Threads), 0, s, src, src_rows, \
-                    tok_pos, k, n_valid, K, P, dst, sc))
+                    tok_pos, k, n_valid, K, P, dst, chunks, chunk_of, sw))
   if (tok) {
     if (src_dtype == 0) LL_E2(0, true); else if (src_dtype == 1) LL_E2(1, true); else LL_E2(2, true);
   } else {
@@ -234,41 +254,6 @@ int launch_rows_to_e2m1x4(const void* src, int src_dtype, int src_rows, const in
   }
 #undef LL_E2
   return LL_OK;
-}
-
-// The B scale blocks of every (chunk, 128-K stage): B row n = t npad + j (term t, chunk row j)
-// takes the 4 scale bytes of activation row p0 + j, term t, for that stage, at line n % 32,
-// word (n % 128) / 32 of block n / 128 (the layout tcgen05.cp copies into tensor memory). Rows
-// past the chunk's rows (padding, and the rows of the next chunk a 16-row box also loads) get
-// scale byte 0.
-__global__ void k_arrange_sfb(const Chunk* __restrict__ chunks, const int* __restrict__ n_chunks,
-                              const uint8_t* __restrict__ sc, int64_t P, int K, int blks, uint8_t* __restrict__ out) {
-  pdl_wait();
-  pdl_launch_next();
-  const int n_stage = K / 128;
-  const int64_t items = (int64_t)(*n_chunks) * n_stage;      // (chunk, stage) blocks to lay out
-  for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
-    const int c = (int)(it / n_stage), ks = (int)(it % n_stage);
-    const Chunk ch = chunks[c];
-    const int npad = (ch.n + 15) & ~15;
-    uint32_t* blk = reinterpret_cast<uint32_t*>(out + ((size_t)c * n_stage + ks) * blks * kBsSfBlock);
-    for (int n = threadIdx.x; n < blks * 128; n += blockDim.x) {
-      const int t = n / npad, j = n % npad;
-      uint32_t w = 0;
-      if (t < kBsTermsFp4 && j < ch.n)
-        w = *reinterpret_cast<const uint32_t*>(sc + ((int64_t)t * P + ch.p0 + j) * (K / 32) + 4 * ks);
-      blk[(n / 128) * (kBsSfBlock / 4) + (n % 32) * 4 + (n % 128) / 32] = w;
-    }
-  }
-}
-
-int launch_arrange_sfb(const Chunk* chunks, const int* n_chunks, int max_chunks, const uint8_t* sc, int64_t P, int K,
-                       int blks, uint8_t* out, cudaStream_t s) {
-  if (max_chunks <= 0 || K % 128 || blks < 1 || blks > 2 || !chunks || !n_chunks || !sc || !out) return LL_ERR_ARG;
-  // a grid-stride loop over the (chunk, stage) blocks that exist (the count is on the device)
-  const int64_t most = (int64_t)max_chunks * (K / 128);
-  const int grid = (int)std::min<int64_t>(most, (int64_t)device_info().sms * 8);
-  return launch_pdl("k_arrange_sfb", k_arrange_sfb, dim3(grid), dim3(128), 0, s, chunks, n_chunks, sc, P, K, blks, out);
 }
 
 int launch_rows_to_e4m3x3(const void* src, int src_dtype, int src_rows, const int* tok_pos, int k,

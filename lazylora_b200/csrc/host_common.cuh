@@ -49,7 +49,11 @@ inline int check_launch(const char* what) {
   if (e != cudaSuccess) return cuda_fail(e, what);
   if (g_lev && g_lev_i < g_lev_n) {
     g_lev_names[g_lev_i] = what;
-    LL_CUDA(cudaEventRecord(g_lev[g_lev_i++], g_launch_stream));
+    // inside a stream capture the event becomes an event-record node of the graph (timed on replay)
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    LL_CUDA(cudaStreamIsCapturing(g_launch_stream, &cs));
+    LL_CUDA(cudaEventRecordWithFlags(g_lev[g_lev_i++], g_launch_stream,
+                                     cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : 0));
   }
   return LL_OK;
 }

@@ -50,7 +50,8 @@ __global__ void k_count(const int64_t* __restrict__ idx, int T, int k, int E, in
 // Single block: expert offsets, per-(token block, expert) bases (in place over cnt), and the
 // chunk list (experts split into runs of at most nmax rows).
 __global__ void __launch_bounds__(1024) k_scan(int* __restrict__ cnt, int nblk, int E, int nmax, int* __restrict__ offsets,
-                                               Chunk* __restrict__ chunks, int* __restrict__ n_chunks) {
+                                               Chunk* __restrict__ chunks, int* __restrict__ n_chunks,
+                                               int* __restrict__ chunk_of) {
   pdl_wait();
   pdl_launch_next();
   using Scan = cub::BlockScan<int, 1024>;
@@ -80,6 +81,7 @@ __global__ void __launch_bounds__(1024) k_scan(int* __restrict__ cnt, int nblk, 
       }
       const int cb = carry_chunks + ch_off;
       for (int i = 0; i < nch; i++) chunks[cb + i] = Chunk{e, base + i * nmax, min(nmax, total - i * nmax), 0};
+      for (int i = 0; i < total; i++) chunk_of[base + i] = cb + i / nmax;
     }
     __syncthreads();
     if (threadIdx.x == 0) { carry_rows += agg_rows; carry_chunks += agg_ch; }
@@ -148,7 +150,8 @@ __global__ void __launch_bounds__(1024) k_plan_small(const int64_t* __restrict__
                                                      Chunk* __restrict__ chunks, int* __restrict__ n_chunks,
                                                      int* __restrict__ perm_token, int* __restrict__ perm_slot,
                                                      int* __restrict__ pair_pos, float* __restrict__ tw,
-                                                     int* __restrict__ tok_pos, DevStatus* __restrict__ st) {
+                                                     int* __restrict__ tok_pos, int* __restrict__ chunk_of,
+                                                     DevStatus* __restrict__ st) {
   pdl_wait();
   pdl_launch_next();
   using Scan = cub::BlockScan<int, 1024>;
@@ -188,6 +191,7 @@ __global__ void __launch_bounds__(1024) k_plan_small(const int64_t* __restrict__
       hist[e] = base;
       const int cb = carry_chunks + ch_off;
       for (int i = 0; i < nch; i++) chunks[cb + i] = Chunk{e, base + i * nmax, min(nmax, total - i * nmax), 0};
+      for (int i = 0; i < total; i++) chunk_of[base + i] = cb + i / nmax;
     }
     __syncthreads();
     if (threadIdx.x == 0) { carry_rows += agg_rows; carry_chunks += agg_ch; }
@@ -378,6 +382,7 @@ struct LayerWs {
   int* perm_slot;
   int* pair_pos;
   int* tok_pos;
+  int* chunk_of;      // [P] chunk of each sorted row
   float* tw;
   float* xinv;
   __half* xh;
@@ -386,11 +391,9 @@ struct LayerWs {
   // scales [3][P]; E2M1: block scale bytes [4][P][K/32], laid out per chunk and stage in *sfb)
   uint8_t* xq;
   float* xinv3;
-  uint8_t* xsc;
   uint8_t* xsfb;
   uint8_t* hq;
   float* hinv3;
-  uint8_t* hsc;
   uint8_t* hsfb;
   int max_chunks;
   float* xa_g;
@@ -457,6 +460,7 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   w.perm_slot = c.take<int>(P);
   w.pair_pos = c.take<int>(P);
   w.tok_pos = c.take<int>(P);
+  w.chunk_of = c.take<int>(P);
   w.tw = c.take<float>(P);
   w.xinv = c.take<float>(P);
   w.xh = c.take<__half>(P * d);
@@ -465,11 +469,9 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
     w.max_chunks = max_chunks;
     w.xq = c.take<uint8_t>((size_t)3 * P * d);          // 3 E4M3 terms or 4 E2M1 terms (2 P d bytes)
     w.xinv3 = c.take<float>((size_t)3 * P);
-    w.xsc = c.take<uint8_t>((size_t)4 * P * (d / 32));
     w.xsfb = c.take<uint8_t>((size_t)max_chunks * (d / 128) * kBsSfBlock);
     w.hq = c.take<uint8_t>((size_t)3 * P * f);
     w.hinv3 = c.take<float>((size_t)3 * P);
-    w.hsc = c.take<uint8_t>((size_t)4 * P * (f / 32));
     w.hsfb = c.take<uint8_t>((size_t)max_chunks * (f / 128) * kBsSfBlock);
   }
   w.xa_g = c.take<float>((size_t)T * r);
@@ -505,6 +507,29 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
   }
   if (out) *out = w;
   return c.off + 256;
+}
+
+// A second stream (non-blocking) with a fork and a join event, one per device and host thread,
+// made on first use: work of a call that does not depend on the call's earlier launches runs
+// there, ordered by the events (captured into a graph as a parallel branch).
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+static int side_stream(SideStream** out) {
+  constexpr int kMaxDev = 16;
+  static thread_local SideStream per_dev[kMaxDev];
+  int dev = 0;
+  LL_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDev) return LL_ERR_ARG;
+  SideStream& ss = per_dev[dev];
+  if (!ss.s) {
+    LL_CUDA(cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking));
+    LL_CUDA(cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming));
+    LL_CUDA(cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming));
+  }
+  *out = &ss;
+  return LL_OK;
 }
 
 // The forward reads the weights as stored; only the backward needs the transposed copies.
@@ -556,11 +581,11 @@ static int bs_launch(int kind, int nmax, const CUtensorMap* a, const CUtensorMap
 // the T token rows written to their pair rows; else pair rows < *n_valid), and for BS_FP4 their
 // block scales laid out per chunk and stage, plus the tensor maps of the terms.
 static int bs_operand(int kind, const LayerWs& W, const void* src, int src_dtype, int src_rows, const int* tok_pos,
-                      int k, const int* n_valid, int K, int64_t P, uint8_t* q, float* inv3, uint8_t* sc,
-                      uint8_t* sfb, CUtensorMap* maps, BsArgs& a, cudaStream_t s) {
+                      int k, const int* n_valid, int K, int64_t P, uint8_t* q, float* inv3, uint8_t* sfb,
+                      CUtensorMap* maps, BsArgs& a, cudaStream_t s) {
   if (kind == BS_FP4) {
-    LL_TRY(launch_rows_to_e2m1x4(src, src_dtype, src_rows, tok_pos, k, n_valid, K, P, q, sc, s));
-    LL_TRY(launch_arrange_sfb(W.chunks, W.n_chunks, W.max_chunks, sc, P, K, 1, sfb, s));
+    LL_TRY(launch_rows_to_e2m1x4(src, src_dtype, src_rows, tok_pos, k, n_valid, K, P, q, W.chunks, W.chunk_of,
+                                 W.nmax, sfb, s));
     LL_TRY(make_e2m1x4_maps(maps, W.nmax / 16, q, P, K));
     a.sfb = sfb;
   } else {
@@ -742,16 +767,30 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   const int nblk = (T + kTokBlock - 1) / kTokBlock;
   g_launch_count = 0;
 
+  // The LoRA gate / up deltas depend on x alone: they run on a side stream beside the sort and
+  // the operand conversion, joined before F1.
+  SideStream* ss = nullptr;
+  LL_TRY(side_stream(&ss));
+  LL_CUDA(cudaEventRecord(ss->fork, s));
+  LL_CUDA(cudaStreamWaitEvent(ss->s, ss->fork, 0));
+  g_launch_stream = ss->s;
+  LL_TRY(skinny(x, x_dtype, true, T, d, L->A_g, L->A_u, r, 2 * r, 1.f, W.xa_g, W.xa_u, W.skpart, W.skpart_floats,
+                ss->s));
+  LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_g, L->B_g, W.xa_u, L->B_u, W.dlt_g, ss->s,
+                W.dlt_u));
+  LL_CUDA(cudaEventRecord(ss->join, ss->s));
+  g_launch_stream = s;
+
   if (nblk == 1) {    // few tokens: the counting sort in one block, no memset
     LL_TRY(launch_pdl("k_plan_small", k_plan_small, dim3(1), dim3(1024), (size_t)(E + P) * sizeof(int), s, idx, w, T,
                       k, E, W.nmax, W.offsets, W.chunks, W.n_chunks, W.perm_token, W.perm_slot, W.pair_pos, W.tw,
-                      W.tok_pos, W.st));
+                      W.tok_pos, W.chunk_of, W.st));
   } else {
     LL_TRY(reset_status(W.st, s));
     LL_CUDA(cudaMemsetAsync(W.perm_token, 0xFF, sizeof(int) * P, s));
     LL_TRY(launch_pdl("k_count", k_count, dim3(nblk), dim3(256), E * sizeof(int), s, idx, T, k, E, W.cnt));
     LL_TRY(launch_pdl("k_scan", k_scan, dim3(1), dim3(1024), 0, s, W.cnt, nblk, E, W.nmax, W.offsets, W.chunks,
-                      W.n_chunks));
+                      W.n_chunks, W.chunk_of));
     LL_TRY(launch_pdl("k_scatter", k_scatter, dim3(nblk), dim3(256), kTokBlock * k * sizeof(int), s, idx, w, T, k, E,
                       W.cnt, W.perm_token, W.perm_slot, W.pair_pos, W.tw, W.tok_pos));
   }
@@ -761,11 +800,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
   const int kind = bs_kind(W.nmax);
   const bool bs = kind >= 0;
   if (!bs) LL_TRY(launch_token_rows_to_half(x, x_dtype, W.perm_token, W.tok_pos, T, k, d, W.xh, W.xinv, s));
-  LL_TRY(skinny(x, x_dtype, true, T, d, L->A_g, L->A_u, r, 2 * r, 1.f, W.xa_g, W.xa_u, W.skpart, W.skpart_floats, s));
-  // the gate and up deltas in one launch
-  LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_g, L->B_g, W.xa_u, L->B_u, W.dlt_g, s,
-                W.dlt_u));
-  // F1: gate / up
+  // F1: gate / up (after the side stream's deltas)
   if (bs) {
     CUtensorMap a[2], b[4];
     if (kind == BS_FP4) {
@@ -776,7 +811,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
       LL_TRY(make_fp4_map(&a[1], L->w3p, (int64_t)E * f, d, 128));
     }
     BsArgs a1{};
-    LL_TRY(bs_operand(kind, W, x, x_dtype, T, W.tok_pos, k, nullptr, d, P, W.xq, W.xinv3, W.xsc, W.xsfb, b, a1, s));
+    LL_TRY(bs_operand(kind, W, x, x_dtype, T, W.tok_pos, k, nullptr, d, P, W.xq, W.xinv3, W.xsfb, b, a1, s));
     a1.chunks = W.chunks;
     a1.n_chunks = W.n_chunks;
     a1.mtiles = f / 128;
@@ -794,6 +829,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
     a1.epi.G = W.G;
     a1.epi.U = W.U;
     a1.epi.H = W.H;
+    LL_CUDA(cudaStreamWaitEvent(s, ss->join, 0));
     LL_TRY(bs_launch<EPI_F1>(kind, W.nmax, a, b, a1, s));
   } else {
     CUtensorMap pk[2], sc[2], act[8];
@@ -818,6 +854,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
     a.epi.G = W.G;
     a.epi.U = W.U;
     a.epi.H = W.H;
+    LL_CUDA(cudaStreamWaitEvent(s, ss->join, 0));
     LL_TRY((gemm_nmax<EPI_F1, 2, 1, false>(W.nmax, pk, sc, act, a, s)));
   }
   const int* n_valid = W.offsets + E;
@@ -833,7 +870,7 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
       LL_TRY(make_fp4_map(&a[0], L->w2p, (int64_t)E * d, f, 256));
     a[1] = a[0];
     BsArgs a2{};
-    LL_TRY(bs_operand(kind, W, W.H, 2, P, nullptr, 0, n_valid, f, P, W.hq, W.hinv3, W.hsc, W.hsfb, b, a2, s));
+    LL_TRY(bs_operand(kind, W, W.H, 2, P, nullptr, 0, n_valid, f, P, W.hq, W.hinv3, W.hsfb, b, a2, s));
     a2.chunks = W.chunks;
     a2.n_chunks = W.n_chunks;
     a2.mtiles = d / 256;

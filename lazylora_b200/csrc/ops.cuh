@@ -42,15 +42,13 @@ int launch_prepare_sfa(const uint8_t* scales, int64_t sstride, int E, int R, int
 int launch_rows_to_e4m3x3(const void* src, int src_dtype, int src_rows, const int* tok_pos, int k,
                           const int* n_valid, int K, int64_t P, uint8_t* dst, float* inv3, cudaStream_t s);
 
-// Rows as four E2M1 terms ([4][rows][K/2] packed bytes) with E8M0 block-32 scales ([4][rows][K/32]
-// bytes): the BS_FP4 activation operand; same source / destination rules as
-// launch_rows_to_e4m3x3. K % 32 == 0, K <= 8192.
+// Rows as four E2M1 terms ([4][rows][K/2] packed bytes), the BS_FP4 activation operand, with
+// their E8M0 block-32 scales written straight into the MMA's B scale blocks of each row's chunk
+// ([max_chunks][K/128][512], chunk_of[p] = the chunk of pair row p; words no row owns are not
+// written: they scale only MMA columns nobody reads); same source / destination rules as
+// launch_rows_to_e4m3x3. K % 128 == 0, chunks of at most nmax <= 32 rows.
 int launch_rows_to_e2m1x4(const void* src, int src_dtype, int src_rows, const int* tok_pos, int k,
-                          const int* n_valid, int K, int64_t P, uint8_t* dst, uint8_t* sc, cudaStream_t s);
-
-// The BS_FP4 B scale blocks of every chunk and 128-K stage ([max_chunks][K/128][blks][512]) from
-// the activation terms' scale bytes sc [4][P][K/32].
-int launch_arrange_sfb(const Chunk* chunks, const int* n_chunks, int max_chunks, const uint8_t* sc, int64_t P, int K,
-                       int blks, uint8_t* out, cudaStream_t s);
+                          const int* n_valid, int K, int64_t P, uint8_t* dst, const Chunk* chunks, const int* chunk_of,
+                          int nmax, uint8_t* sfb, cudaStream_t s);
 
 }  // namespace ll

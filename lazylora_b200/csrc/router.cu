@@ -8,6 +8,22 @@
 
 namespace ll {
 
+// Values compared as order-preserving unsigned words (-0 as +0; NaN as 0, below every number,
+// never preferred to a number): a > b as floats iff f32_order(a) > f32_order(b).
+LL_DEV uint32_t f32_order(float f) {
+  if (isnan(f)) return 0u;
+  const uint32_t u = f == 0.f ? 0u : __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Warp-wide best of each lane's candidate (value word bo, expert be): the highest value, then the
+// lowest id, by two hardware reductions. Every lane gets the winner's value word and id.
+LL_DEV void warp_best(uint32_t bo, int be, uint32_t& vmax, int& emin) {
+  vmax = __reduce_max_sync(0xffffffffu, bo);
+  const uint32_t idw = bo == vmax ? 0x7fffffffu - (uint32_t)be : 0u;
+  emin = (int)(0x7fffffffu - __reduce_max_sync(0xffffffffu, idw));
+}
+
 // One warp per token. MODE 0: `a` holds logits (scores = sigmoid, choice = scores + bias).
 // MODE 1: `a` holds scores and `b` the scores used for the choice, as given.
 // In MODE 0 the logits are the sum of `nsplit` fp32 partials [nsplit][T][E], added in order.
@@ -73,14 +89,9 @@ __global__ void k_route_select(const float* __restrict__ a, const float* __restr
         be = e;
       }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const int oe = __shfl_xor_sync(0xffffffffu, be, off);
-      if (ov > bv || (ov == bv && oe < be)) {
-        bv = ov;
-        be = oe;
-      }
+    {   // the warp's best: highest value, then lowest id (a lane with nothing left offers 0)
+      uint32_t vmax;
+      warp_best(be == 0x7fffffff ? 0u : f32_order(bv), be, vmax, be);
     }
     float mine = 0.f;
 #pragma unroll
@@ -116,24 +127,106 @@ __global__ void k_route_select(const float* __restrict__ a, const float* __restr
   }
 }
 
-// The same selection for few tokens, one block per token: each of the 8 warps takes the top k of
-// its slice of experts (expert e = 256 i + 32 w + lane), then warp 0 merges the 8 lists. The
-// top k of the union of the slices' top k is the top k overall, with the same order and tie
-// rule (higher value, then lower id), and every score is computed in the same order as above,
-// so indices and weights are bit for bit those of k_route_select.
+// ------------------------------------------------------- block-wide top k of one token
 constexpr int kSelWarps = 8;
+struct SelShared {
+  float sc[kSelWarps * 32 * 4];          // score of every expert (E <= 1024)
+  uint32_t cv[kSelWarps][32];            // each warp's top k: value words
+  int ce[kSelWarps][32];                 //                     expert ids
+};
+
+// The top k (k <= 32) of one token by a block of 8 warps (all 256 threads call it, and the block
+// synchronises before reusing `sh`): thread (w, lane) holds the scores sc[i] and choice values
+// ch[i] of experts e = 256 i + 32 w + lane (i < 4, E <= 1024). Each warp takes its slice's top k
+// in k rounds (a lane's best of 4, then the warp's best by reduction); warp 0 merges the 8 lists
+// in k more rounds (lane j holding entry j of each list), and lane 0 writes the k ids and
+// weights (renormalised in torch's CPU order for a short row, times rsf) to idx / w. Order: the
+// highest value first, ties to the lower id, as k_route_select.
+LL_DEV void block_select_token(const float (&sc)[4], const float (&ch)[4], int E, int k, int renorm, float rsf,
+                               SelShared& sh, int64_t* __restrict__ idx, float* __restrict__ w) {
+  const int wp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  uint32_t ov[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int e = 256 * i + 32 * wp + lane;
+    ov[i] = e < E ? f32_order(ch[i]) : 0u;
+    if (e < E) sh.sc[e] = sc[i];
+  }
+  uint32_t taken = 0;
+  for (int kk = 0; kk < k; kk++) {
+    uint32_t bo = 0;
+    int be = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int e = 256 * i + 32 * wp + lane;
+      if (e < E && !((taken >> i) & 1) && (ov[i] > bo || (ov[i] == bo && e < be))) { bo = ov[i]; be = e; }
+    }
+    uint32_t vmax;
+    int emin;
+    warp_best(bo, be, vmax, emin);
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      if (256 * i + 32 * wp + lane == emin) taken |= 1u << i;
+    if (lane == 0) { sh.cv[wp][kk] = vmax; sh.ce[wp][kk] = emin; }
+  }
+  __syncthreads();
+  if (wp != 0) return;
+  uint32_t mv[kSelWarps];
+  int me[kSelWarps];
+#pragma unroll
+  for (int v = 0; v < kSelWarps; v++) {
+    mv[v] = lane < k ? sh.cv[v][lane] : 0u;
+    me[v] = lane < k ? sh.ce[v][lane] : 0x7fffffff;
+  }
+  uint32_t used = 0;
+  float denom_l[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float wsel = 0.f;
+  int esel = 0;
+  for (int kk = 0; kk < k; kk++) {
+    uint32_t bo = 0;
+    int be = 0x7fffffff;
+#pragma unroll
+    for (int v = 0; v < kSelWarps; v++)
+      if (!((used >> v) & 1) && me[v] < E && (mv[v] > bo || (mv[v] == bo && me[v] < be))) { bo = mv[v]; be = me[v]; }
+    uint32_t vmax;
+    int emin;
+    warp_best(bo, be, vmax, emin);
+#pragma unroll
+    for (int v = 0; v < kSelWarps; v++)
+      if (me[v] == emin) used |= 1u << v;
+    const float sv = emin < E ? sh.sc[emin] : 0.f;
+    denom_l[kk & 7] += sv;           // every lane, in the order of k_route_select's lane 0
+    if (lane == kk) { wsel = sv; esel = emin; }
+  }
+  float denom = 0.f;
+  if (k > 1 && renorm) {
+    denom = denom_l[0];
+    for (int i = 1; i < 8; i++) denom += denom_l[i];
+    denom += 1e-20f;
+  }
+  if (lane < k) {
+    float v = wsel;
+    if (k > 1 && renorm) v = v / denom;
+    idx[lane] = esel;
+    w[lane] = v * rsf;
+  }
+}
+
+// The same selection for few tokens, one block per token (block_select_token), with every
+// score computed in the same order as k_route_select: indices and weights are bit for bit
+// those of k_route_select.
 template <int MODE, int PL>
 __global__ void __launch_bounds__(kSelWarps * 32) k_route_select_block(
     const float* __restrict__ a, const float* __restrict__ b, const float* __restrict__ bias, int T, int E, int k,
     int renorm, float rsf, int64_t* __restrict__ idx, float* __restrict__ w, float* __restrict__ scores_out,
     int nsplit) {
+  static_assert(PL == 4, "four experts a thread");
   pdl_wait();
   pdl_launch_next();
   const int t = blockIdx.x;
   if (t >= T) return;
   const int wp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  __shared__ float c_ch[kSelWarps][32], c_sc[kSelWarps][32];
-  __shared__ int c_e[kSelWarps][32];
+  __shared__ SelShared sh;
   float sc[PL], ch[PL];
 #pragma unroll
   for (int i = 0; i < PL; i++) sc[i] = 0.f;
@@ -185,78 +278,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) k_route_select_block(
       ch[i] = b[(int64_t)t * E + e];
     }
   }
-  // this warp's top k
-  uint32_t taken = 0;
-  for (int kk = 0; kk < k; kk++) {
-    float bv = -INFINITY;
-    int be = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < PL; i++) {
-      const int e = 256 * i + 32 * wp + lane;
-      if (e < E && !((taken >> i) & 1) && (ch[i] > bv || (ch[i] == bv && e < be))) { bv = ch[i]; be = e; }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const int oe = __shfl_xor_sync(0xffffffffu, be, off);
-      if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
-    }
-    float mine = 0.f;
-#pragma unroll
-    for (int i = 0; i < PL; i++)
-      if (256 * i + 32 * wp + lane == be) { taken |= 1u << i; mine = sc[i]; }
-    const float sv = __shfl_sync(0xffffffffu, mine, (be & 31));
-    if (lane == 0) { c_ch[wp][kk] = bv; c_sc[wp][kk] = sv; c_e[wp][kk] = be; }
-  }
-  __syncthreads();
-  if (wp != 0) return;
-  // merge: lane j holds candidate j of every warp's list
-  float mch[kSelWarps], msc[kSelWarps];
-  int me[kSelWarps];
-#pragma unroll
-  for (int v = 0; v < kSelWarps; v++) {
-    const bool ok = lane < k;
-    mch[v] = ok ? c_ch[v][lane] : -INFINITY;
-    msc[v] = ok ? c_sc[v][lane] : 0.f;
-    me[v] = ok ? c_e[v][lane] : 0x7fffffff;
-  }
-  uint32_t used = 0;
-  float wsel = 0.f, denom_l[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  int esel = 0;
-  for (int kk = 0; kk < k; kk++) {
-    float bv = -INFINITY;
-    int be = 0x7fffffff;
-#pragma unroll
-    for (int v = 0; v < kSelWarps; v++)
-      if (!((used >> v) & 1) && me[v] < E && (mch[v] > bv || (mch[v] == bv && me[v] < be))) { bv = mch[v]; be = me[v]; }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const int oe = __shfl_xor_sync(0xffffffffu, be, off);
-      if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
-    }
-    float mine = 0.f;
-    bool found = false;
-#pragma unroll
-    for (int v = 0; v < kSelWarps; v++)
-      if (me[v] == be && !((used >> v) & 1)) { used |= 1u << v; mine = msc[v]; found = true; }
-    const uint32_t holder = __ballot_sync(0xffffffffu, found);
-    const float sv = __shfl_sync(0xffffffffu, mine, holder ? __ffs(holder) - 1 : 0);
-    denom_l[kk & 7] += sv;            // every lane, in the order of the warp kernel's lane 0
-    if (lane == kk) { wsel = sv; esel = be; }
-  }
-  float denom = 0.f;
-  if (k > 1 && renorm) {
-    denom = denom_l[0];
-    for (int i = 1; i < 8; i++) denom += denom_l[i];
-    denom += 1e-20f;
-  }
-  if (lane < k) {
-    float v = wsel;
-    if (k > 1 && renorm) v = v / denom;
-    idx[(int64_t)t * k + lane] = esel;
-    w[(int64_t)t * k + lane] = v * rsf;
-  }
+  block_select_token(sc, ch, E, k, renorm, rsf, sh, idx + (int64_t)t * k, w + (int64_t)t * k);
 }
 
 // Few tokens: a block of 8 warps per token (k_route_select_block), else a warp per token.
@@ -288,6 +310,142 @@ __global__ void k_sum_partials(const float* __restrict__ part, int nsplit, int64
   logits[i] = acc;
 }
 
+// ------------------------------------------------ few-token logits and selection, one launch
+// For a handful of tokens the router is a matrix-vector product bound by reading W. Block = 8
+// warps = 2 experts x 4 warps; warp q of an expert takes the runs q, q + 4, ... of 32 16-byte
+// chunks of the expert's row (four runs' loads issued together), W read as stored (fp32) or
+// rebuilt from its three bf16 planes (hi + lo + lo2, which is W exactly); per token, the lanes'
+// sums go through a shuffle tree and the 4 warps' sums are added in warp order. With a counter
+// (one token), the last block to finish (the counter in the workspace, zeroed before the launch)
+// then selects the token's top k from the logits (block_select_token); without, the logits are
+// left for k_route_select_block (a block per token, in parallel).
+constexpr int kRgTok = 8, kRgRun = 4;
+template <bool PLANES, int XT>
+__global__ void __launch_bounds__(256) k_router_gemv_select(const void* __restrict__ x, const void* __restrict__ W,
+                                                            const float* __restrict__ bias, int T, int d, int E,
+                                                            int k, int renorm, float rsf, float* __restrict__ logits,
+                                                            unsigned* __restrict__ counter, int64_t* __restrict__ idx,
+                                                            float* __restrict__ w, float* __restrict__ scores_out) {
+  pdl_wait();
+  pdl_launch_next();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int e = blockIdx.x * 2 + warp / 4, q = warp % 4;
+  const int nch = d / 8;
+  float acc[kRgTok];
+#pragma unroll
+  for (int t = 0; t < kRgTok; t++) acc[t] = 0.f;
+  if (e < E) {
+    for (int g0 = q; g0 * 32 < nch; g0 += 4 * kRgRun) {
+      float wv[kRgRun][8];
+#pragma unroll
+      for (int u = 0; u < kRgRun; u++) {
+        const int ch = (g0 + 4 * u) * 32 + lane;
+        const bool in = ch < nch;
+        if (PLANES) {
+          const __nv_bfloat16* wp = static_cast<const __nv_bfloat16*>(W);
+          const int64_t nw = (int64_t)E * d, o = (int64_t)e * d + 8 * ch;
+          uint4 h = make_uint4(0u, 0u, 0u, 0u), l = h, l2 = h;
+          if (in) {
+            h = *reinterpret_cast<const uint4*>(wp + o);
+            l = *reinterpret_cast<const uint4*>(wp + nw + o);
+            l2 = *reinterpret_cast<const uint4*>(wp + 2 * nw + o);
+          }
+          const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {l.x, l.y, l.z, l.w}, l2w[4] = {l2.x, l2.y, l2.z, l2.w};
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hw[j]));
+            const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lw[j]));
+            const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&l2w[j]));
+            wv[u][2 * j] = (a.x + b.x) + c.x;
+            wv[u][2 * j + 1] = (a.y + b.y) + c.y;
+          }
+        } else {
+          const float* wf = static_cast<const float*>(W) + (int64_t)e * d + 8 * ch;
+          const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 a = in ? *reinterpret_cast<const float4*>(wf) : z;
+          const float4 b = in ? *reinterpret_cast<const float4*>(wf + 4) : z;
+          wv[u][0] = a.x; wv[u][1] = a.y; wv[u][2] = a.z; wv[u][3] = a.w;
+          wv[u][4] = b.x; wv[u][5] = b.y; wv[u][6] = b.z; wv[u][7] = b.w;
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < kRgTok; t++) {
+        if (t >= T) break;
+#pragma unroll
+        for (int u = 0; u < kRgRun; u++) {
+          const int ch = (g0 + 4 * u) * 32 + lane;
+          if (ch >= nch) continue;
+          float xv[8];
+          if (XT == 0) {
+            const float* xf = static_cast<const float*>(x) + (int64_t)t * d + 8 * ch;
+            const float4 a = *reinterpret_cast<const float4*>(xf), b = *reinterpret_cast<const float4*>(xf + 4);
+            xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w; xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+          } else {
+            const uint4 raw = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + (int64_t)t * d + 8 * ch);
+            const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rw[j]));
+              xv[2 * j] = f.x;
+              xv[2 * j + 1] = f.y;
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 8; j++) acc[t] = fmaf(xv[j], wv[u][j], acc[t]);
+        }
+      }
+    }
+  }
+  __shared__ float red[8][kRgTok];
+  __shared__ int s_last;
+#pragma unroll
+  for (int t = 0; t < kRgTok; t++) {
+    float v = acc[t];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (lane == 0) red[warp][t] = v;
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < 2 * T) {
+    const int el = threadIdx.x / T, t = threadIdx.x % T;
+    const int ee = blockIdx.x * 2 + el;
+    if (ee < E) {
+      float v = red[4 * el][t];
+#pragma unroll
+      for (int qq = 1; qq < 4; qq++) v += red[4 * el + qq][t];
+      logits[(int64_t)t * E + ee] = v;
+    }
+  }
+  if (!counter) return;                                // the selection is a kernel of its own
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();                                   // this block's logits before its count
+    s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // the last block: every token's selection, one token at a time by the whole block
+  __shared__ SelShared sh;
+  for (int t = 0; t < T; t++) {
+    float sc[4], ch[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int ei = 256 * i + 32 * warp + lane;
+      sc[i] = 0.f;
+      ch[i] = -INFINITY;
+      if (ei < E) {
+        const float sg = 1.0f / (1.0f + expf(-__ldcg(logits + (int64_t)t * E + ei)));
+        sc[i] = sg;
+        ch[i] = bias ? sg + bias[ei] : sg;
+        if (scores_out) scores_out[(int64_t)t * E + ei] = sg;
+      }
+    }
+    block_select_token(sc, ch, E, k, renorm, rsf, sh, idx + (int64_t)t * k, w + (int64_t)t * k);
+    __syncthreads();
+  }
+}
+
 // ------------------------------------------------------------ tensor-core logits: plan + launch
 struct RouterPlan {
   int BN = 16, NP = 1, mt = 1, nt = 1, nsplit = 1, kbps = 1, kb_total = 1;
@@ -314,7 +472,7 @@ static RouterPlan router_plan(int T, int d, int E, int x_dtype) {
     p.off_x = take(p.NP == 3 ? (size_t)3 * T * d * 2 : 0);
     p.off_part = take((size_t)p.nsplit * T * E * 4);
     p.off_logits = take((size_t)T * E * 4);
-    p.off_st = take(sizeof(DevStatus));
+    p.off_st = take(32);              // the status word, then the few-token path's block counter
     p.bytes = (off + 255) & ~size_t(255);
   }
   return p;
@@ -392,6 +550,25 @@ static int route_topk(const void* x, int x_dtype, const float* router_w, const _
   if (ws_bytes < p.bytes) return LL_ERR_WORKSPACE;
   LL_STREAM(stream);
   g_launch_count = 0;
+  if (T <= kRgTok && E <= 1024 && (reinterpret_cast<uintptr_t>(planes ? (const void*)planes : (const void*)router_w) % 16) == 0) {
+    // few tokens: logits on CUDA cores and the selection in the same launch
+    uint8_t* base = static_cast<uint8_t*>(ws);
+    LL_CUDA(cudaMemsetAsync(base + p.off_st, 0, 32, s));
+    unsigned* counter = reinterpret_cast<unsigned*>(base + p.off_st + sizeof(DevStatus));
+    float* logits = reinterpret_cast<float*>(base + p.off_logits);
+    const dim3 grid((E + 1) / 2);
+    const void* wsrc = planes ? static_cast<const void*>(planes) : static_cast<const void*>(router_w);
+    unsigned* cnt = T == 1 ? counter : nullptr;       // one token: selected by the last block
+#define LL_RG(PL, XTv)                                                                                          \
+  LL_TRY(launch_pdl("k_router_gemv_select", k_router_gemv_select<PL, XTv>, grid, dim3(256), 0, s, x, wsrc, bias, T, \
+                    d, E, k, renormalize, routed_scaling_factor, logits, cnt, idx, w, scores_out))
+    if (planes) { if (x_dtype == 0) LL_RG(true, 0); else LL_RG(true, 1); }
+    else { if (x_dtype == 0) LL_RG(false, 0); else LL_RG(false, 1); }
+#undef LL_RG
+    if (T == 1) return LL_OK;
+    return launch_select<0>(logits, nullptr, bias, T, E, k, renormalize, routed_scaling_factor, idx, w, scores_out, s,
+                            1);
+  }
   LL_TRY(router_logits_tc(x, x_dtype, router_w, planes, T, d, E, ws, p, s));
   const float* part = reinterpret_cast<const float*>(static_cast<uint8_t*>(ws) + p.off_part);
   if (p.nsplit > 1 && !select_by_block(T, E, k)) {   // the K splits' partials, summed in split order by a wide kernel
