@@ -48,7 +48,7 @@ UNIT = "tokens/s"
 # from one ncu capture of the same kernels at d=7168, f=2048, 64 experts, 9 tokens per expert.
 # Weight reads dominate, so a launch's traffic scales with the number of experts it touches.
 NCU_DRAM_BYTES_PER_EXPERT = {
-    (7168, 2048): [(1020.498e6 + 13.916672e6) / 64, (501.540e6 + 16.182016e6) / 64,
+    (7168, 2048): [(1015.426e6 + 13.455616e6) / 64, (502.113e6 + 16.451584e6) / 64,
                    (548.347e6 + 9.062400e6) / 64, (1061.752e6 + 18.494720e6) / 64],
 }
 
@@ -560,26 +560,54 @@ def run_decode(args, cfg, rank, local, world, dist):
     for _ in range(args.warmup):
         step()
     layer.check_status(cfg.T, cfg.k)
-    # per-kernel breakdown (untimed, eager launches, L2 flushed first): an event after every launch
-    breakdown = {}
+    # per-kernel breakdown (untimed, L2 flushed first): an event after every launch of the library.
+    # With --graph the step is captured once more with those events as event-record nodes and
+    # replayed, so the times are those of kernels inside a graph (each event node adds a little);
+    # otherwise the launches are eager. Reported per kernel: the time from the latest earlier
+    # event that had completed to this one's, and the timeline of completion times.
+    breakdown, timeline = {}, []
     nb = 5
+    evs = [torch.cuda.Event(enable_timing=True, external=bool(args.graph)) for _ in range(64)]
+    t0 = torch.cuda.Event(enable_timing=True, external=bool(args.graph))
+    for e in evs + [t0]:
+        e.record(stream)
+    torch.cuda.synchronize()
+    names_rec, ends = [], None
+    if args.graph:
+        pg = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            step()
+            with torch.cuda.graph(pg, stream=side):
+                t0.record(side)
+                lib.ll_profile_launch_events((L.c_void_p * 64)(*[e.cuda_event for e in evs]), 64)
+                step()
+                nrec = lib.ll_profile_launch_recorded()
+                names_rec = [lib.ll_profile_launch_name(i).decode() for i in range(nrec)]
+                lib.ll_profile_launch_events(None, 0)
+        stream.wait_stream(side)
     for _ in range(nb):
         flush_l2()
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(64)]
-        for e in evs:
-            e.record(stream)
-        t0 = torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        lib.ll_profile_launch_events((L.c_void_p * 64)(*[e.cuda_event for e in evs]), 64)
-        step()
-        nrec = lib.ll_profile_launch_recorded()
-        names_rec = [lib.ll_profile_launch_name(i).decode() for i in range(nrec)]
-        lib.ll_profile_launch_events(None, 0)
+        if args.graph:
+            pg.replay()
+        else:
+            t0.record(stream)
+            lib.ll_profile_launch_events((L.c_void_p * 64)(*[e.cuda_event for e in evs]), 64)
+            step()
+            nrec = lib.ll_profile_launch_recorded()
+            names_rec = [lib.ll_profile_launch_name(i).decode() for i in range(nrec)]
+            lib.ll_profile_launch_events(None, 0)
         torch.cuda.synchronize()
-        prev = t0
-        for i, nm in enumerate(names_rec):
-            breakdown[nm] = breakdown.get(nm, 0.0) + prev.elapsed_time(evs[i]) * 1e3 / nb
-            prev = evs[i]
+        e_us = [t0.elapsed_time(evs[i]) * 1e3 for i in range(len(names_rec))]
+        ends = e_us if ends is None else [a + b for a, b in zip(ends, e_us)]
+    ends = [v / nb for v in ends]
+    for i, nm in enumerate(names_rec):
+        before = [v for v in ends[:i] if v <= ends[i]]
+        breakdown[nm] = breakdown.get(nm, 0.0) + ends[i] - (max(before) if before else 0.0)
+        timeline.append([nm, round(ends[i], 1)])
+    if args.graph:
+        del pg
     run = step
     if args.graph:
         gr = torch.cuda.CUDAGraph()
@@ -621,9 +649,12 @@ def run_decode(args, cfg, rank, local, world, dist):
                          "peak_kind": peak_kind, "algorithmic_bytes_per_step": wbytes,
                          "roofline_us": wbytes / (hbm_peak * 1e9) * 1e6},
             "gpu_launches": state["n"] * args.steps, "clocks": clk.summary(),
-            "kernel_breakdown_us": {"source": f"CUDA events after every launch of the library, eager launches, "
-                                              f"L2 flushed before each step, mean of {nb} untimed steps",
-                                    **{k: round(v, 1) for k, v in sorted(breakdown.items(), key=lambda kv: -kv[1])}}}
+            "kernel_breakdown_us": {"source": f"CUDA events after every launch of the library "
+                                              f"({'event nodes in a replayed graph' if args.graph else 'eager launches'}"
+                                              f"), L2 flushed before each step, mean of {nb} untimed steps; per "
+                                              f"kernel: from the latest earlier completion",
+                                    **{k: round(v, 1) for k, v in sorted(breakdown.items(), key=lambda kv: -kv[1])}},
+            "kernel_timeline_us": timeline}
     print(json.dumps(line), flush=True)
 
 
