@@ -765,6 +765,35 @@ def run_shared(args, cfg, rank, local, world, dist):
     flops = 2 * 3 * 2 * N * d * F
     _, tf_peak, peak_kind = _peaks()
     tfs = flops / (ms * 1e-3) / 1e12
+    # the projections alone, on this library's tcgen05 GEMM and, for context, on cuBLAS
+    from lazylora_b200.core import dense
+
+    def timed(fn, n=20):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+    h_ = torch.randn(N, F, generator=gen, device=dev).to(torch.bfloat16)
+    gemms = {
+        "gate+up x.W^T (2 outputs)": (lambda: dense.linear_two(x, se.W_g, se.W_u), 2 * 2 * N * d * F),
+        "down h.W_d^T": (lambda: dense.linear(h_, se.W_d), 2 * N * d * F),
+        "dh = g.W_d": (lambda: dense.matmul(g, se.W_d), 2 * N * d * F),
+        "dx = dG.W_g + dU.W_u": (lambda: dense.matmul_sum2(h_, se.W_g, h_, se.W_u), 2 * 2 * N * d * F),
+        "cuBLAS gate+up (torch.matmul)": (lambda: (torch.matmul(x, se.W_g.t()), torch.matmul(x, se.W_u.t())),
+                                          2 * 2 * N * d * F),
+        "cuBLAS dx (torch.matmul + addmm_)": (lambda: torch.matmul(h_, se.W_g).addmm_(h_, se.W_u),
+                                              2 * 2 * N * d * F),
+    }
+    gemm_rep = {}
+    for name, (fn, fl) in gemms.items():
+        gms = timed(fn)
+        gemm_rep[name] = {"ms": round(gms, 4), "tflops": round(fl / (gms * 1e-3) / 1e12, 1)}
+    dense.check_status()
     line = {"metric": f"shared expert fwd+bwd tokens/s (d={d}, F={F}, LoRA r={r})", "value": N / (ms * 1e-3),
             "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -773,6 +802,7 @@ def run_shared(args, cfg, rank, local, world, dist):
                                    "input-gradient backward", "d": d, "F": F, "r": r, "T": N},
             "roofline": {"bound": "tensor", "achieved": tfs, "peak": tf_peak, "unit": "TFLOP/s",
                          "frac": tfs / tf_peak, "peak_kind": peak_kind, "flops_per_step": flops},
+            "projections": {"source": "CUDA events around 20 calls of each, inputs resident", **gemm_rep},
             "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
 

@@ -299,6 +299,30 @@ int ll_lora_outer(const float* P, const void* Q, int q_dtype, int N, int C, int 
 int ll_lora_add_bf16(const void* Y, const float* L0, const float* R0, const float* L1, const float* R1, int r,
                      int r_rows, float scale, int N, int C, void* out, void* stream);
 
+/* -------------------------------------------------------------- dense bf16 GEMMs
+ * The plain projections around the routed experts (the latent block's down / up projections,
+ * lazy_trainer.py:722-735, and the shared expert's gate / up / down), whose F.linear products
+ * the reference runs as bf16 GEMMs with fp32 accumulation on CUDA; here on tcgen05 tensor
+ * cores (no cuBLAS). bf16 operands, fp32 accumulation, C bf16 (c_dtype 1, round to nearest) or
+ * fp32 (c_dtype 0), row-major with leading dimension ldc.
+ * ll_gemm_bf16: C[M][N] = A[M][K] . B^T with B [N][K] (b_nk = 1, as F.linear's weight), or
+ *   A . B with B [K][N] (b_nk = 0, the input gradient through that weight).
+ * ll_gemm_bf16_two_outputs: C0 = A op(B0) and C1 = A op(B1) in one launch (gate and up).
+ * ll_gemm_bf16_sum2: C = A0 op(B0) + A1 op(B1), both products in one fp32 accumulator and one
+ *   rounding (dG W_g + dU W_u).
+ * Leading dimensions in elements, multiples of 8 (16-byte rows); pointers 16-byte aligned;
+ * M, N, K >= 1 (K need not be a multiple of 64). Waits inside the kernel are bounded; one that
+ * runs out sets a per-device status word that ll_gemm_bf16_status returns (after a stream
+ * synchronisation) and clears. */
+int ll_gemm_bf16(int M, int N, int K, const void* A, int64_t lda, const void* B, int64_t ldb, int b_nk, void* C,
+                 int64_t ldc, int c_dtype, void* stream);
+int ll_gemm_bf16_two_outputs(int M, int N, int K, const void* A, int64_t lda, const void* B0, const void* B1,
+                             int64_t ldb, int b_nk, void* C0, void* C1, int64_t ldc, int c_dtype, void* stream);
+int ll_gemm_bf16_sum2(int M, int N, const void* A0, int K0, int64_t lda0, const void* B0, int64_t ldb0, int b0_nk,
+                      const void* A1, int K1, int64_t lda1, const void* B1, int64_t ldb1, int b1_nk, void* C,
+                      int64_t ldc, int c_dtype, void* stream);
+int ll_gemm_bf16_status(void* stream);
+
 /* ------------------------------------------------------------------ latent RMSNorm
  * The norm between the routed-expert sum and the latent up-projection of the Kimi K3 MoE
  * block (lazy_trainer.py:731-733; RMSNormFunction.forward, trunk_streamer.py:27-31):

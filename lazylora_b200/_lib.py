@@ -100,6 +100,14 @@ _SIGS = {
                               ctypes.c_size_t, c_void_p]),
     "ll_lora_add_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_int,
                                  c_int, c_void_p, c_void_p]),
+    "ll_gemm_bf16": (c_int, [c_int, c_int, c_int, c_void_p, ctypes.c_int64, c_void_p, ctypes.c_int64, c_int, c_void_p,
+                             ctypes.c_int64, c_int, c_void_p]),
+    "ll_gemm_bf16_two_outputs": (c_int, [c_int, c_int, c_int, c_void_p, ctypes.c_int64, c_void_p, c_void_p,
+                                         ctypes.c_int64, c_int, c_void_p, c_void_p, ctypes.c_int64, c_int, c_void_p]),
+    "ll_gemm_bf16_sum2": (c_int, [c_int, c_int, c_void_p, c_int, ctypes.c_int64, c_void_p, ctypes.c_int64, c_int,
+                                  c_void_p, c_int, ctypes.c_int64, c_void_p, ctypes.c_int64, c_int, c_void_p,
+                                  ctypes.c_int64, c_int, c_void_p]),
+    "ll_gemm_bf16_status": (c_int, [c_void_p]),
     "ll_rmsnorm_forward": (c_int, [c_void_p, c_void_p, c_int, c_int, ctypes.c_float, c_void_p, c_int, c_void_p,
                                    c_void_p]),
     "ll_rmsnorm_backward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),

@@ -7,8 +7,8 @@ lazy_trainer.py:697-736): the normed hidden state is projected down (routed_expe
 (routed_expert_norm, trunk_streamer.py:27-31), cast to bf16 and projected back up
 (routed_expert_up_proj, [d_h, d_l]). Here:
 
-  * the two dense projections are plain bf16 GEMMs with fp32 accumulation (cuBLAS through
-    torch.matmul), as F.linear computes them on CUDA in the reference;
+  * the two dense projections are plain bf16 GEMMs with fp32 accumulation, as F.linear
+    computes them on CUDA in the reference, on this library's tcgen05 GEMM (core.dense);
   * the routed experts are a RoutedExpertsLayer at width d_l (this library's grouped MXFP4
     kernels);
   * the RMSNorm and its gradient are this library's row kernels (ll_rmsnorm_forward /
@@ -25,6 +25,7 @@ from typing import Dict, Tuple
 import torch
 
 from .. import _lib as L
+from ..core import dense
 from .routed_experts import RoutedExpertsLayer
 
 
@@ -50,7 +51,7 @@ class LatentRoutedMoE:
         """routed_out [N, d_h] bf16 for the normed hidden state x [N, d_h]."""
         L.require_cuda(x, idx, w)
         xb = x.reshape(-1, self.down_w.shape[1]).to(torch.bfloat16)
-        h_lat = torch.matmul(xb, self.down_w.t())                         # bf16 [N, d_l]
+        h_lat = dense.linear(xb, self.down_w).contiguous()                # bf16 [N, d_l]
         routed = self.layer.forward(h_lat, idx, w)                         # fp32 [N, d_l]
         N, D = routed.shape
         normed = torch.empty((N, D), dtype=torch.bfloat16, device=x.device)
@@ -58,7 +59,7 @@ class LatentRoutedMoE:
         L.check(self.lib.ll_rmsnorm_forward(routed.data_ptr(), self.norm_w.data_ptr(), N, D, ctypes.c_float(self.eps),
                                             normed.data_ptr(), 1, rstd.data_ptr(), L.stream_ptr()),
                 "ll_rmsnorm_forward")
-        out = torch.matmul(normed, self.up_w.t())                          # bf16 [N, d_h]
+        out = dense.linear(normed, self.up_w).contiguous()                 # bf16 [N, d_h]
         self._saved = (h_lat, routed, rstd, idx, w)
         return out
 
@@ -68,11 +69,11 @@ class LatentRoutedMoE:
             raise RuntimeError("backward before forward")
         h_lat, routed, rstd, idx, w = self._saved
         N, D = routed.shape
-        g_normed = torch.matmul(grad_out.reshape(N, -1).to(torch.bfloat16), self.up_w)   # bf16 [N, d_l]
+        g_normed = dense.matmul(grad_out.reshape(N, -1).to(torch.bfloat16), self.up_w).contiguous()  # bf16 [N, d_l]
         g_routed = torch.empty((N, D), dtype=torch.float32, device=routed.device)
         L.check(self.lib.ll_rmsnorm_backward(routed.data_ptr(), self.norm_w.data_ptr(), rstd.data_ptr(),
                                              g_normed.data_ptr(), 1, N, D, g_routed.data_ptr(), L.stream_ptr()),
                 "ll_rmsnorm_backward")
         g_h, g_w, grads = self.layer.backward(h_lat, idx, w, g_routed)
-        grad_x = torch.matmul(g_h.to(torch.bfloat16), self.down_w)                         # bf16 [N, d_h]
+        grad_x = dense.matmul(g_h.to(torch.bfloat16), self.down_w).contiguous()             # bf16 [N, d_h]
         return grad_x, g_w, grads

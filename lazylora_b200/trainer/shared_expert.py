@@ -7,8 +7,9 @@ weights, frozen) with a rank-r LoRA adapter on each of its three projections
     h      = situ_glu(s_gate, s_up)
     out    = linear32(h, W_d) + lora_d(h)
 
-The three projections are bf16 GEMMs with fp32 accumulation (cuBLAS through torch.matmul, as
-F.linear runs them on CUDA in the reference). The LoRA products read the bf16 activations
+The three projections are bf16 GEMMs with fp32 accumulation, as F.linear runs them on CUDA in
+the reference, on the library's tcgen05 GEMM (core.dense: gate and up in one launch; no
+cuBLAS). The LoRA products read the bf16 activations
 directly (ll_lora_down, ll_lora_outer: fixed-order split-K sums) instead of fp32 copies; the
 element-wise middle — both LoRA deltas added in bf16 and the SiTU-GLU, and in the backward the
 down adapter's input-gradient term plus the SiTU-GLU gradient — is one kernel each way
@@ -16,8 +17,8 @@ down adapter's input-gradient term plus the SiTU-GLU gradient — is one kernel 
 adapters' input-gradient terms, are added to the bf16 GEMM outputs in place
 (ll_lora_add_bf16). The backward returns dL/dx and the six LoRA gradients, following the
 autograd graph of the reference's forward (lora_layer.py:104-123: the adapter casts its bf16
-input to fp32 and its fp32 delta back to bf16); the two gate/up input-gradient GEMMs
-accumulate into one bf16 buffer (cuBLAS with beta = 1). The LoRA products and adapter gradients
+input to fp32 and its fp32 delta back to bf16); the two gate/up input-gradient products are
+summed in one fp32 accumulator and rounded to bf16 once. The LoRA products and adapter gradients
 run on a second stream beside the bf16 GEMMs (events order each consumer after its producer), so
 the small latency-bound kernels fill the GEMMs' gaps instead of adding to the step.
 """
@@ -27,6 +28,7 @@ from typing import Dict, Tuple
 import torch
 
 from .. import _lib as L
+from ..core import dense
 
 
 class SharedExpert:
@@ -101,8 +103,8 @@ class SharedExpert:
         if N:
             with torch.cuda.stream(side):
                 self._down(xb, self.A_g, self.A_u, r, 2 * r, 1, xa_g, xa_u, ws)
-        G = torch.matmul(xb, self.W_g.t())
-        U = torch.matmul(xb, self.W_u.t())
+        G, U = dense.linear_two(xb, self.W_g, self.W_u)
+        G, U = G.contiguous(), U.contiguous()
         SG = torch.empty((N, F), dtype=torch.bfloat16, device=dev)
         SU = torch.empty_like(SG)
         H = torch.empty_like(SG)
@@ -115,7 +117,7 @@ class SharedExpert:
         if N:
             with torch.cuda.stream(side):
                 self._down(H, self.A_d, None, r, r, 1, ha, None, ws)
-        out = torch.matmul(H, self.W_d.t())
+        out = dense.linear(H, self.W_d).contiguous()
         main.wait_stream(side)
         if N:
             self._add(out, ha, self.B_d, None, None, 0)
@@ -150,7 +152,7 @@ class SharedExpert:
             gB_ready = side.record_event()
             self._outer(ha, gb, True, grads["dB_d"], ws)
             self._outer(gB, H, False, grads["dA_d"], ws)
-        Dh = torch.matmul(gb, self.W_d)                                              # [N, F] bf16
+        Dh = dense.matmul(gb, self.W_d).contiguous()                                 # [N, F] bf16
         main.wait_event(gB_ready)
         L.check(self.lib.ll_shared_glu_backward(Dh.data_ptr(), gB.data_ptr(), self.A_d.data_ptr(),
                                                 ctypes.c_float(s), SG.data_ptr(), SU.data_ptr(), N, F, r,
@@ -165,8 +167,7 @@ class SharedExpert:
             self._outer(gg, xb, False, grads["dA_g"], ws)
             self._outer(xa_u, DSU, True, grads["dB_u"], ws)
             self._outer(gu, xb, False, grads["dA_u"], ws)
-        dx = torch.matmul(DSG, self.W_g)
-        dx.addmm_(DSU, self.W_u)
+        dx = dense.matmul_sum2(DSG, self.W_g, DSU, self.W_u).contiguous()
         main.wait_event(gu_ready)
         self._add(dx, gg, self.A_g, gu, self.A_u, 1)
         main.wait_stream(side)
