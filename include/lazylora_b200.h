@@ -181,6 +181,14 @@ size_t ll_moe_workspace_bytes(const ll_moe_layer* L, int T, int k);
 int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dtype,
                    const int64_t* idx, const float* w, float* out, void* ws, size_t ws_bytes,
                    void* stream);
+/* ll_moe_forward whose final combine also RMS-normalises each token's row (the latent block's
+ * routed_expert_norm after the routed experts' sum, lazy_trainer.py:731-733, with
+ * RMSNormFunction.forward, trunk_streamer.py:27-31): out as ll_moe_forward (fp32 [T, d]),
+ * normed[t] = bf16(out[t] * rsqrt(mean(out[t]^2) + eps) * norm_w) ([T, d]), rstd[t] the row's
+ * rsqrt (fp32 [T]) for ll_rmsnorm_backward. norm_w fp32 [d]; norm_w and normed 8-byte aligned. */
+int ll_moe_forward_rmsnorm(const ll_moe_layer* L, int T, int k, const void* x, int x_dtype, const int64_t* idx,
+                           const float* w, const float* norm_w, float eps, float* out, void* normed, float* rstd,
+                           void* ws, size_t ws_bytes, void* stream);
 
 /* Backward of the forward that last ran in `ws` for upstream gradient g [T,d] (g_dtype as
  * x_dtype): grad_h [T,d], grad_w [T,k] (fp32, overwritten) and the LoRA gradients

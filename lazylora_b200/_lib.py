@@ -72,6 +72,9 @@ _SIGS = {
     "ll_moe_workspace_bytes": (c_size_t, [ctypes.POINTER(MoELayerDesc), c_int, c_int]),
     "ll_moe_forward": (c_int, [ctypes.POINTER(MoELayerDesc), c_int, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                c_void_p, c_void_p, c_size_t, c_void_p]),
+    "ll_moe_forward_rmsnorm": (c_int, [ctypes.POINTER(MoELayerDesc), c_int, c_int, c_void_p, c_int, c_void_p,
+                                       c_void_p, c_void_p, ctypes.c_float, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_size_t, c_void_p]),
     "ll_moe_backward": (c_int, [ctypes.POINTER(MoELayerDesc), c_int, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                 c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),

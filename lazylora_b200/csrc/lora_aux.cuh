@@ -429,6 +429,125 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
   }
 }
 
+// The latent block's combine with its RMSNorm in one pass (the sum of a token's expert rows,
+// lazy_trainer.py:729-731, then routed_expert_norm, :731-733): a block takes 8 tokens and every
+// column, in 512-column slices (the R slice staged in shared memory per slice, as k_expand):
+//   out[t][c]    = [sum_j Y[pos_j][c], pairs of t in ascending expert order] + alpha (q[t] . R)(c),
+//                  q[t] = sum over the token's pairs of qtw * qz (stored to q_out by the block);
+//   rstd[t]      = rsqrt(mean_c out[t][c]^2 + eps), the squares summed per thread over its
+//                  columns, then across the block in a fixed order;
+//   normed[t][c] = bf16(out[t][c] * rstd[t] * norm_w[c]).
+// The sums of each out element are those of k_expand, bit for bit. A thread re-reads only the
+// columns it wrote.
+template <bool RROWS>
+__global__ void __launch_bounds__(kExThreads) k_expand_norm(const int* __restrict__ tok_pos, const float* __restrict__ Y,
+                                                        int k, int T, int C, int r, float alpha,
+                                                        const float* __restrict__ R0, const float* __restrict__ qtw,
+                                                        const float* __restrict__ qz, float* __restrict__ q_out,
+                                                        float* __restrict__ out, const float* __restrict__ norm_w,
+                                                        float eps, __nv_bfloat16* __restrict__ normed,
+                                                        float* __restrict__ rstd) {
+  pdl_wait();
+  pdl_launch_next();
+  extern __shared__ float Rs[];                          // [r][kExPitch], one slice at a time
+  __shared__ float Ls[kExTok][kExMaxR];
+  __shared__ int ps[kExTok][32];
+  __shared__ float red[kExThreads / 32][kExTok];
+  __shared__ float rs[kExTok];
+  const int t0 = blockIdx.x * kExTok;
+  const int c = 2 * threadIdx.x;
+  for (int i = threadIdx.x; i < kExTok * k; i += kExThreads) {
+    const int tt = i / k, j = i % k;
+    ps[tt][j] = (t0 + tt < T) ? tok_pos[(int64_t)(t0 + tt) * k + j] : -1;
+  }
+  for (int i = threadIdx.x; i < kExTok * r; i += kExThreads) {
+    const int tt = i / r, rr = i % r;
+    float l = 0.f;
+    if (t0 + tt < T) {
+      for (int j = 0; j < k; j++) {
+        const int pos = tok_pos[(int64_t)(t0 + tt) * k + j];
+        if (pos < 0) break;
+        l = fmaf(qtw[pos], qz[(int64_t)pos * r + rr], l);
+      }
+      if (q_out) q_out[(int64_t)(t0 + tt) * r + rr] = l;
+    }
+    Ls[tt][rr] = l;
+  }
+  float ss[kExTok];
+#pragma unroll
+  for (int tt = 0; tt < kExTok; tt++) ss[tt] = 0.f;
+  for (int c0 = 0; c0 < C; c0 += kExCols) {
+    const int nc = min(kExCols, C - c0);
+    __syncthreads();                                     // Ls / ps ready; the previous slice no longer read
+    ex_stage_r<RROWS>(Rs, R0, r, C, c0, nc);
+    __syncthreads();
+    if (c >= nc) continue;
+    float2 lo[kExTok];
+#pragma unroll
+    for (int tt = 0; tt < kExTok; tt++) lo[tt] = make_float2(0.f, 0.f);
+    for (int rr = 0; rr < r; rr++) {
+      const float2 rv = *reinterpret_cast<const float2*>(Rs + rr * kExPitch + c);
+#pragma unroll
+      for (int tt = 0; tt < kExTok; tt++) {
+        const float l = Ls[tt][rr];
+        lo[tt].x = fmaf(l, rv.x, lo[tt].x); lo[tt].y = fmaf(l, rv.y, lo[tt].y);
+      }
+    }
+#pragma unroll
+    for (int tt = 0; tt < kExTok; tt++) {
+      if (t0 + tt >= T) break;
+      float2 acc = make_float2(0.f, 0.f);
+      for (int j0 = 0; j0 < k; j0 += 8) {
+        float2 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {                    // all requests first
+          const int p = j0 + j < k ? ps[tt][j0 + j] : -1;
+          v[j] = p >= 0 ? *reinterpret_cast<const float2*>(Y + (int64_t)p * C + c0 + c) : make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {                    // then the sum, in slot order
+          acc.x += v[j].x; acc.y += v[j].y;
+        }
+      }
+      float2 o;
+      o.x = acc.x + alpha * lo[tt].x; o.y = acc.y + alpha * lo[tt].y;
+      *reinterpret_cast<float2*>(out + (int64_t)(t0 + tt) * C + c0 + c) = o;
+      ss[tt] = fmaf(o.y, o.y, fmaf(o.x, o.x, ss[tt]));
+    }
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+#pragma unroll
+  for (int tt = 0; tt < kExTok; tt++) {
+    float v = ss[tt];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (lane == 0) red[warp][tt] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < kExTok) {
+    const int tt = threadIdx.x;
+    float tot = red[0][tt];
+    for (int wi = 1; wi < kExThreads / 32; wi++) tot += red[wi][tt];
+    const float rv = rsqrtf(tot / (float)C + eps);
+    rs[tt] = rv;
+    if (t0 + tt < T) rstd[t0 + tt] = rv;
+  }
+  __syncthreads();
+  for (int c0 = 0; c0 < C; c0 += kExCols) {
+    const int nc = min(kExCols, C - c0);
+    if (c >= nc) continue;
+    const float2 wv = *reinterpret_cast<const float2*>(norm_w + c0 + c);
+#pragma unroll
+    for (int tt = 0; tt < kExTok; tt++) {
+      if (t0 + tt >= T) break;
+      const float2 o = *reinterpret_cast<const float2*>(out + (int64_t)(t0 + tt) * C + c0 + c);
+      const float rv = rs[tt];
+      *reinterpret_cast<__nv_bfloat162*>(normed + (int64_t)(t0 + tt) * C + c0 + c) =
+          __floats2bfloat162_rn(o.x * rv * wv.x, o.y * rv * wv.y);
+    }
+  }
+}
+
 // --------------------------------------------------------------- outer-product sums
 // part[seg][rr][c] = sum_{n in seg} Pm(n, rr) * Q[n][c] for the ranks rr = kOuRB blockIdx.z ..
 // + kOuRB - 1 and the 128 columns of blockIdx.x. Pm: [N][r] fp32, or (PGATHER) tw[n] *

@@ -753,10 +753,15 @@ size_t ll_moe_workspace_bytes(const ll_moe_layer* L, int T, int k) {
   return layer_layout(nullptr, L, T, k, nullptr);
 }
 
-int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dtype, const int64_t* idx, const float* w,
-                   float* out, void* ws, size_t ws_bytes, void* stream) {
+// The forward; with norm_w, the final combine also RMS-normalises each token's row (the latent
+// block's routed_expert_norm) into normed (bf16) and rstd.
+static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dtype, const int64_t* idx,
+                       const float* w, float* out, const float* norm_w, float eps, void* normed, float* rstd, void* ws,
+                       size_t ws_bytes, void* stream) {
   LL_TRY(validate(L, T, k, false));
   if (!x || !idx || !w || !out || !ws || (x_dtype != 0 && x_dtype != 1)) return LL_ERR_ARG;
+  if (norm_w && (!normed || !rstd || (reinterpret_cast<uintptr_t>(norm_w) | reinterpret_cast<uintptr_t>(normed)) % 8))
+    return LL_ERR_ARG;
   LL_TRY(check_arch());
   if (ws_bytes < ll_moe_workspace_bytes(L, T, k)) return LL_ERR_WORKSPACE;
   LL_STREAM(stream);
@@ -907,8 +912,28 @@ int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dty
     a.epi.Y = W.Y;
     LL_TRY((gemm_nmax<EPI_F2, 2, 1, false>(W.nmax, pk, sc, act, a, s)));
   }
+  if (norm_w) {
+    if (d % 2 || r > kExMaxR || k > 32) return LL_ERR_ARG;
+    const int smem = r * kExPitch * (int)sizeof(float);
+    LL_TRY(set_smem_attr(reinterpret_cast<const void*>(k_expand_norm<false>), smem));
+    return launch_pdl("k_expand_norm", k_expand_norm<false>, dim3((T + kExTok - 1) / kExTok), dim3(kExThreads), smem,
+                      s, W.tok_pos, W.Y, k, T, d, r, L->lora_scaling, L->B_d, W.tw, W.z, W.q, out, norm_w, eps,
+                      static_cast<__nv_bfloat16*>(normed), rstd);
+  }
   return expand(false, W.tok_pos, W.Y, k, T, d, r, L->lora_scaling, nullptr, L->B_d, nullptr, nullptr, out, s, nullptr,
                 W.tw, W.z, W.q);
+}
+
+int ll_moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x_dtype, const int64_t* idx, const float* w,
+                   float* out, void* ws, size_t ws_bytes, void* stream) {
+  return moe_forward(L, T, k, x, x_dtype, idx, w, out, nullptr, 0.f, nullptr, nullptr, ws, ws_bytes, stream);
+}
+
+int ll_moe_forward_rmsnorm(const ll_moe_layer* L, int T, int k, const void* x, int x_dtype, const int64_t* idx,
+                           const float* w, const float* norm_w, float eps, float* out, void* normed, float* rstd,
+                           void* ws, size_t ws_bytes, void* stream) {
+  if (!norm_w) return LL_ERR_ARG;
+  return moe_forward(L, T, k, x, x_dtype, idx, w, out, norm_w, eps, normed, rstd, ws, ws_bytes, stream);
 }
 
 int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dtype, const int64_t* idx, const float* w,

@@ -11,15 +11,15 @@ lazy_trainer.py:697-736): the normed hidden state is projected down (routed_expe
     computes them on CUDA in the reference, on this library's tcgen05 GEMM (core.dense);
   * the routed experts are a RoutedExpertsLayer at width d_l (this library's grouped MXFP4
     kernels);
-  * the RMSNorm and its gradient are this library's row kernels (ll_rmsnorm_forward /
-    ll_rmsnorm_backward), the norm output written straight to bf16 for the up-projection.
+  * the RMSNorm is fused into the routed experts' final combine (ll_moe_forward_rmsnorm: each
+    token's rows summed, then normalised, written straight to bf16 for the up-projection, and
+    its rsqrt kept); its gradient is this library's row kernel (ll_rmsnorm_backward).
 
 The backward follows the autograd graph of the reference: the up-projection's input gradient,
 the RMSNorm gradient for a frozen norm weight, the routed experts' backward (its grad_h cast to
 h_latent's bf16), the down-projection's input gradient. The projections and the norm weight are
 frozen (LoRA training); the routed experts' LoRA gradients come back as from the layer.
 """
-import ctypes
 from typing import Dict, Tuple
 
 import torch
@@ -52,13 +52,8 @@ class LatentRoutedMoE:
         L.require_cuda(x, idx, w)
         xb = x.reshape(-1, self.down_w.shape[1]).to(torch.bfloat16)
         h_lat = dense.linear(xb, self.down_w).contiguous()                # bf16 [N, d_l]
-        routed = self.layer.forward(h_lat, idx, w)                         # fp32 [N, d_l]
-        N, D = routed.shape
-        normed = torch.empty((N, D), dtype=torch.bfloat16, device=x.device)
-        rstd = torch.empty((N,), dtype=torch.float32, device=x.device)
-        L.check(self.lib.ll_rmsnorm_forward(routed.data_ptr(), self.norm_w.data_ptr(), N, D, ctypes.c_float(self.eps),
-                                            normed.data_ptr(), 1, rstd.data_ptr(), L.stream_ptr()),
-                "ll_rmsnorm_forward")
+        # the routed experts, their combine and the RMSNorm of the fp32 sum in the same final pass
+        routed, normed, rstd = self.layer.forward_rmsnorm(h_lat, idx, w, self.norm_w, self.eps)
         out = dense.linear(normed, self.up_w).contiguous()                 # bf16 [N, d_h]
         self._saved = (h_lat, routed, rstd, idx, w)
         return out

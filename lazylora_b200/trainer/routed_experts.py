@@ -173,6 +173,28 @@ class RoutedExpertsLayer:
         self._ws_key = (x.data_ptr(), idx.data_ptr(), w.data_ptr(), T, k)
         return out
 
+    def forward_rmsnorm(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, norm_w: torch.Tensor, eps: float,
+                        rows_hint: Optional[int] = None):
+        """forward() whose combine also RMS-normalises each token's row (the latent block's norm):
+        (out [T, d] fp32, normed [T, d] bf16, rstd [T] fp32)."""
+        L.require_cuda(x, idx, w, norm_w)
+        self.desc.rows_hint = int(rows_hint) if rows_hint else 0
+        x = x.contiguous()
+        idx = idx.to(torch.int64).contiguous()
+        w = w.to(torch.float32).contiguous()
+        nw = norm_w.to(torch.float32).contiguous()
+        T, k = idx.shape
+        ws = self.workspace(T, k)
+        out = torch.empty((T, self.d), dtype=torch.float32, device=x.device)
+        normed = torch.empty((T, self.d), dtype=torch.bfloat16, device=x.device)
+        rstd = torch.empty((T,), dtype=torch.float32, device=x.device)
+        L.check(self.lib.ll_moe_forward_rmsnorm(ctypes.byref(self.desc), T, k, x.data_ptr(), self._dtype_code(x),
+                                                idx.data_ptr(), w.data_ptr(), nw.data_ptr(), ctypes.c_float(eps),
+                                                out.data_ptr(), normed.data_ptr(), rstd.data_ptr(), ws.data_ptr(),
+                                                ws.numel(), L.stream_ptr()), "ll_moe_forward_rmsnorm")
+        self._ws_key = (x.data_ptr(), idx.data_ptr(), w.data_ptr(), T, k)
+        return out, normed, rstd
+
     def backward(self, x, idx, w, g, forward_done: bool = None, rows_hint: Optional[int] = None):
         """(grad_h [T,d], grad_w [T,k], {dA_g, dB_g, dA_u, dB_u, dA_d, dB_d}), all fp32.
         rows_hint: as given to the forward (used when the forward is recomputed here)."""

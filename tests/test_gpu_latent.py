@@ -90,3 +90,34 @@ def test_rmsnorm_kernels_match_torch():
     assert O.rel_l2(y32.cpu(), y.detach()) < 1e-6
     assert O.rel_l2(ybf.float().cpu(), y.detach().to(torch.bfloat16).float()) < 4e-3
     assert O.rel_l2(gx.cpu(), gx_want) < 1e-5
+
+
+@pytest.mark.parametrize("case", ["tiny", "small"])
+def test_fused_combine_norm_matches_separate_passes(case):
+    """ll_moe_forward_rmsnorm: its fp32 output is ll_moe_forward's bit for bit (the same sums),
+    and its normed rows and rstd are the row kernel's on that output (the squares summed in
+    another fixed order: rstd within 1e-6, the bf16 rows within one rounding)."""
+    import ctypes
+    from lazylora_b200 import _lib as L
+    from lazylora_b200.trainer.routed_experts import RoutedExpertsLayer
+    cfg = CONFIGS[case]
+    inp, _, _, norm_w, _, _, _, _ = _case(256, cfg)
+    layer = RoutedExpertsLayer.from_inputs(inp, cfg.scaling)
+    h = inp["x"].cuda()
+    idx, w = O.route(inp["x"].float(), inp["router_w"], inp["router_b"], cfg.k)
+    idx, w = idx.cuda(), w.cuda()
+    nw = norm_w.cuda()
+    out_a = layer.forward(h, idx, w)
+    out_b, normed, rstd = layer.forward_rmsnorm(h, idx, w, nw, 1e-5)
+    layer.check_status(cfg.T, cfg.k)
+    assert torch.equal(out_a, out_b)
+    lib = L.load()
+    T, D = out_a.shape
+    y = torch.empty(T, D, dtype=torch.bfloat16, device="cuda")
+    r2 = torch.empty(T, device="cuda")
+    L.check(lib.ll_rmsnorm_forward(out_a.data_ptr(), nw.data_ptr(), T, D, ctypes.c_float(1e-5), y.data_ptr(), 1,
+                                   r2.data_ptr(), L.stream_ptr()), "ll_rmsnorm_forward")
+    assert float(((rstd - r2).abs() / r2).max()) < 1e-6
+    want = (out_a * r2[:, None] * nw[None, :])
+    err = (normed.float() - want).abs()
+    assert bool((err <= want.abs() * 2 ** -8 + 1e-6).all())
