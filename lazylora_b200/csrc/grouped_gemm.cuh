@@ -209,8 +209,10 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, N_MAX> tm, const GemmArg
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int n_units = (*args.n_chunks) * args.mtiles;
-  if ((int)blockIdx.x >= n_units || args.K <= 0) return;   // uniform over the CTA: nothing allocated yet
+  if (args.K <= 0) {                        // uniform over the CTA: nothing allocated yet
+    pdl_wait();
+    return;
+  }
 
   const int K = args.K;
   const int n_stage = (K + C::BK - 1) / C::BK;   // packed (TMA) stages per unit
@@ -235,6 +237,14 @@ grouped_mxfp4_gemm(const __grid_constant__ TmaSet<NMAT, N_MAX> tm, const GemmArg
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   DevStatus* st = args.status;
+  // the prologue above reads nothing another kernel writes; the chunk list below does
+  pdl_launch_next();                        // (after the allocation)
+  pdl_wait();
+  const int n_units = (*args.n_chunks) * args.mtiles;
+  if ((int)blockIdx.x >= n_units) {         // uniform per block: no unit for this one
+    if (warp == C::kIssuerWarp0) tmem_dealloc(tmem, C::TMEM_COLS);
+    return;
+  }
 
   if (warp == 0) {
     // ------------------------------------------------ packed weights + scales producer

@@ -158,12 +158,12 @@ int launch_gemm(const CUtensorMap* pk, const CUtensorMap* sc, const CUtensorMap*
   const DeviceInfo di = device_info();
   const bool prof = g_prof_events && g_prof_i + 2 <= g_prof_n;
   if (prof) LL_CUDA(cudaEventRecord(g_prof_events[g_prof_i], stream));
-  kern<<<di.sms, Cfg::kThreads, Cfg::SMEM, stream>>>(tm, a);
-  const int rc = check_launch(EPI == EPI_F1   ? "grouped_mxfp4_gemm F1 gate/up"
-                              : EPI == EPI_F2 ? "grouped_mxfp4_gemm F2 down"
-                              : EPI == EPI_B1 ? "grouped_mxfp4_gemm B1 g.W2"
-                              : EPI == EPI_B2 ? "grouped_mxfp4_gemm B2 dg.W1+du.W3"
-                                              : "grouped_mxfp4_gemm");
+  const int rc = launch_pdl(EPI == EPI_F1   ? "grouped_mxfp4_gemm F1 gate/up"
+                            : EPI == EPI_F2 ? "grouped_mxfp4_gemm F2 down"
+                            : EPI == EPI_B1 ? "grouped_mxfp4_gemm B1 g.W2"
+                            : EPI == EPI_B2 ? "grouped_mxfp4_gemm B2 dg.W1+du.W3"
+                                            : "grouped_mxfp4_gemm",
+                            kern, dim3(di.sms), dim3(Cfg::kThreads), Cfg::SMEM, stream, tm, a);
   if (prof) {
     LL_CUDA(cudaEventRecord(g_prof_events[g_prof_i + 1], stream));
     g_prof_i += 2;

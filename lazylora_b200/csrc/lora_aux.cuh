@@ -602,6 +602,8 @@ __global__ void __launch_bounds__(256) k_outer8(const float* __restrict__ Pm, co
                                                 const float* __restrict__ tw, const void* __restrict__ Q, int N,
                                                 const int* __restrict__ n_dev, int C, int r, int nseg,
                                                 float* __restrict__ part) {
+  pdl_wait();
+  pdl_launch_next();
   extern __shared__ float4 red4[];                    // [8 warps][kOuRB][32 lanes] float4
   __shared__ __align__(16) float ps[8][kOuNB][kOuRB];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;

@@ -236,6 +236,8 @@ __global__ void __launch_bounds__(1024) k_plan_small(const int64_t* __restrict__
 __global__ void k_pair_rows_half(const float* __restrict__ DG, const float* __restrict__ DU, int f,
                                  const int* __restrict__ n_valid, __half* __restrict__ DGh, __half* __restrict__ DUh,
                                  float* __restrict__ inv) {
+  pdl_wait();
+  pdl_launch_next();
   const int p = blockIdx.x;
   if (p >= *n_valid) return;
   __shared__ float red[32];
@@ -263,6 +265,8 @@ __global__ void k_pair_rows_half(const float* __restrict__ DG, const float* __re
 // D{g,u}[t][m] = sum over the token's pairs (ascending expert) of D{G,U}[pos][m]
 __global__ void k_token_sum(const int* __restrict__ tok_pos, const float* __restrict__ DG, const float* __restrict__ DU,
                             int T, int k, int f, float* __restrict__ Dg, float* __restrict__ Du) {
+  pdl_wait();
+  pdl_launch_next();
   const int t = blockIdx.y;
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   if (m >= f) return;
@@ -288,6 +292,8 @@ __global__ void __launch_bounds__(kPTThreads) k_pair_rows_tokens(
     const int* __restrict__ tok_pos, const float* __restrict__ DG, const float* __restrict__ DU, int k, int f,
     __half* __restrict__ DGh, __half* __restrict__ DUh, float* __restrict__ inv, float* __restrict__ Dg,
     float* __restrict__ Du) {
+  pdl_wait();
+  pdl_launch_next();
   const int t = blockIdx.x;
   __shared__ float red[kPTThreads / 32];
   __shared__ float sh;
@@ -351,6 +357,8 @@ __global__ void __launch_bounds__(kPTThreads) k_pair_rows_tokens(
 
 __global__ void k_grad_w(const int* __restrict__ pair_pos, const float* __restrict__ parts, int nparts, int P, int Tk,
                          float* __restrict__ grad_w) {
+  pdl_wait();
+  pdl_launch_next();
   const int q = blockIdx.x * blockDim.x + threadIdx.x;
   if (q >= Tk) return;
   const int pos = pair_pos[q];
@@ -363,6 +371,8 @@ __global__ void k_grad_w(const int* __restrict__ pair_pos, const float* __restri
 // out = s * sum_seg part, stored [r][C] or transposed [C][r]
 __global__ void k_outer_reduce(const float* __restrict__ part, int nseg, int r, int C, float s, bool transposed,
                                float* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_next();
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= (int64_t)r * C) return;
   const int rr = (int)(i / C), c = (int)(i % C);
@@ -694,7 +704,8 @@ int outer(const float* Pm, const int* perm_token, const float* tw, const void* Q
 #define LL_OU(QD, PG)                                                                                \
   do {                                                                                               \
     LL_TRY(set_smem_attr(reinterpret_cast<const void*>(k_outer8<QD, PG>), smem));                   \
-    k_outer8<QD, PG><<<grid, 256, smem, s>>>(Pm, perm_token, tw, Q, N, n_dev, C, r, nseg, part);      \
+    LL_TRY(launch_pdl("k_outer8", k_outer8<QD, PG>, grid, dim3(256), smem, s, Pm, perm_token, tw, Q, N, n_dev, C, \
+                      r, nseg, part));                                                               \
   } while (0)
   if (pg) {
     if (qdt == 0) LL_OU(0, true); else if (qdt == 1) LL_OU(1, true); else LL_OU(2, true);
@@ -702,10 +713,9 @@ int outer(const float* Pm, const int* perm_token, const float* tw, const void* Q
     if (qdt == 0) LL_OU(0, false); else if (qdt == 1) LL_OU(1, false); else LL_OU(2, false);
   }
 #undef LL_OU
-  LL_TRY(check_launch("k_outer8"));
   const int64_t n = (int64_t)r * C;
-  k_outer_reduce<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, nseg, r, C, sc, transposed, out);
-  return check_launch("k_outer_reduce");
+  return launch_pdl("k_outer_reduce", k_outer_reduce, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, part, nseg,
+                    r, C, sc, transposed, out);
 }
 
 }  // namespace ll
@@ -1004,13 +1014,12 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
   const int nv = f / (4 * kPTThreads);
   const bool fused_rows = f % (4 * kPTThreads) == 0 && (nv == 1 || nv == 2 || nv == 4);
   if (fused_rows) {
-    if (nv == 1) k_pair_rows_tokens<1><<<T, kPTThreads, 0, s>>>(W.tok_pos, W.DG, W.DU, k, f, W.DGh, W.DUh, W.rinv, W.Dg, W.Du);
-    else if (nv == 2) k_pair_rows_tokens<2><<<T, kPTThreads, 0, s>>>(W.tok_pos, W.DG, W.DU, k, f, W.DGh, W.DUh, W.rinv, W.Dg, W.Du);
-    else k_pair_rows_tokens<4><<<T, kPTThreads, 0, s>>>(W.tok_pos, W.DG, W.DU, k, f, W.DGh, W.DUh, W.rinv, W.Dg, W.Du);
-    LL_TRY(check_launch("k_pair_rows_tokens"));
+    auto kern = nv == 1 ? k_pair_rows_tokens<1> : nv == 2 ? k_pair_rows_tokens<2> : k_pair_rows_tokens<4>;
+    LL_TRY(launch_pdl("k_pair_rows_tokens", kern, dim3(T), dim3(kPTThreads), 0, s, W.tok_pos, W.DG, W.DU, k, f,
+                      W.DGh, W.DUh, W.rinv, W.Dg, W.Du));
   } else {
-    k_pair_rows_half<<<P, 256, 0, s>>>(W.DG, W.DU, f, n_valid, W.DGh, W.DUh, W.rinv);
-    LL_TRY(check_launch("k_pair_rows_half"));
+    LL_TRY(launch_pdl("k_pair_rows_half", k_pair_rows_half, dim3(P), dim3(256), 0, s, W.DG, W.DU, f, n_valid, W.DGh,
+                      W.DUh, W.rinv));
   }
   // B2: dX = dg . W1 + du . W3
   {
@@ -1035,14 +1044,14 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
     LL_TRY((gemm_nmax<EPI_B2, 2, 2, true>(W.nmax, pk, sc, act, a, s)));
   }
   if (!fused_rows) {
-    k_token_sum<<<dim3((f + 255) / 256, T), 256, 0, s>>>(W.tok_pos, W.DG, W.DU, T, k, f, W.Dg, W.Du);
-    LL_TRY(check_launch("k_token_sum"));
+    LL_TRY(launch_pdl("k_token_sum", k_token_sum, dim3((f + 255) / 256, T), dim3(256), 0, s, W.tok_pos, W.DG, W.DU, T,
+                      k, f, W.Dg, W.Du));
   }
   LL_TRY(skinny(W.Dg, 0, false, T, f, L->B_g, nullptr, r, r, 1.f, W.hg, nullptr, W.skpart, W.skpart_floats, s));
   LL_TRY(skinny(W.Du, 0, false, T, f, L->B_u, nullptr, r, r, 1.f, W.hu, nullptr, W.skpart, W.skpart_floats, s));
   LL_TRY(expand(true, W.tok_pos, W.Y, k, T, d, r, sc_l, W.hg, L->A_g, W.hu, L->A_u, grad_h, s));
-  k_grad_w<<<(P + 255) / 256, 256, 0, s>>>(W.pair_pos, W.gw_part, (f / 128) * 4, P, P, grad_w);
-  LL_TRY(check_launch("k_grad_w"));
+  LL_TRY(launch_pdl("k_grad_w", k_grad_w, dim3((P + 255) / 256), dim3(256), 0, s, W.pair_pos, W.gw_part,
+                    (f / 128) * 4, P, P, grad_w));
   // LoRA gradients
   LL_TRY(outer(W.hg, nullptr, nullptr, x, x_dtype, T, nullptr, d, r, sc_l, false, W.opart, W.nseg_max, dA_g, s));
   LL_TRY(outer(W.xa_g, nullptr, nullptr, W.Dg, 0, T, nullptr, f, r, sc_l, true, W.opart, W.nseg_max, dB_g, s));

@@ -196,6 +196,8 @@ __global__ void k_prepare_beta(const uint8_t* __restrict__ s_a, const uint8_t* _
 template <int SRC>
 __global__ void k_rows_to_half(const void* __restrict__ src, const int* __restrict__ index, int rows, int K,
                                int ld, __half* __restrict__ dst, float* __restrict__ inv) {
+  pdl_wait();
+  pdl_launch_next();
   const int row = blockIdx.x;
   if (row >= rows) return;
   const int sr = index ? index[row] : row;
@@ -237,6 +239,8 @@ template <int SRC>
 __global__ void __launch_bounds__(256) k_rows_to_half_v(const void* __restrict__ src, const int* __restrict__ index,
                                                         int rows, int K, int ld, __half* __restrict__ dst,
                                                         float* __restrict__ inv) {
+  pdl_wait();
+  pdl_launch_next();
   const int row = blockIdx.x;
   if (row >= rows) return;
   const int sr = index ? index[row] : row;
@@ -372,17 +376,9 @@ int launch_rows_to_half(const void* src, int src_dtype, const int* index, int ro
   if (ld < K) return LL_ERR_ARG;
   const bool vec = K % 8 == 0 && ld % 8 == 0 && K <= 8 * 4 * 256 && reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(dst) % 16 == 0;
-  if (vec) {
-    if (src_dtype == 0)
-      k_rows_to_half_v<0><<<rows, 256, 0, s>>>(src, index, rows, K, ld, dst, inv);
-    else
-      k_rows_to_half_v<1><<<rows, 256, 0, s>>>(src, index, rows, K, ld, dst, inv);
-  } else if (src_dtype == 0) {
-    k_rows_to_half<0><<<rows, 256, 0, s>>>(src, index, rows, K, ld, dst, inv);
-  } else {
-    k_rows_to_half<1><<<rows, 256, 0, s>>>(src, index, rows, K, ld, dst, inv);
-  }
-  return check_launch("k_rows_to_half");
+  auto kern = vec ? (src_dtype == 0 ? k_rows_to_half_v<0> : k_rows_to_half_v<1>)
+                  : (src_dtype == 0 ? k_rows_to_half<0> : k_rows_to_half<1>);
+  return launch_pdl("k_rows_to_half", kern, dim3(rows), dim3(256), 0, s, src, index, rows, K, ld, dst, inv);
 }
 
 // The same conversion, one block per source token: the token's row is read and its scale found
@@ -392,6 +388,8 @@ template <int SRC>
 __global__ void __launch_bounds__(256) k_token_rows_to_half(const void* __restrict__ src, const int* __restrict__ tok_pos,
                                                             int T, int k, int K, __half* __restrict__ dst,
                                                             float* __restrict__ inv) {
+  pdl_wait();
+  pdl_launch_next();
   const int t = blockIdx.x;
   if (t >= T) return;
   const int nch = K / 8;
@@ -465,11 +463,8 @@ int launch_token_rows_to_half(const void* src, int src_dtype, const int* perm_to
   const bool vec = K % 8 == 0 && K <= 8 * 4 * 256 && reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(dst) % 16 == 0;
   if (!vec) return launch_rows_to_half(src, src_dtype, perm_token, T * k, K, dst, inv, s);
-  if (src_dtype == 0)
-    k_token_rows_to_half<0><<<T, 256, 0, s>>>(src, tok_pos, T, k, K, dst, inv);
-  else
-    k_token_rows_to_half<1><<<T, 256, 0, s>>>(src, tok_pos, T, k, K, dst, inv);
-  return check_launch("k_rows_to_half");
+  return launch_pdl("k_rows_to_half", src_dtype == 0 ? k_token_rows_to_half<0> : k_token_rows_to_half<1>, dim3(T),
+                    dim3(256), 0, s, src, tok_pos, T, k, K, dst, inv);
 }
 
 
