@@ -879,6 +879,91 @@ def run_latent(args, cfg, rank, local, world, dist):
 
 
 # ------------------------------------------------------------ streaming
+def run_stream_ep(args, cfg, rank, local, world, dist):
+    """configs[4] expert-parallel over `world` GPUs: each rank holds only its block of every
+    layer's experts in pinned host memory (1/world of the layer) and streams it into HBM for
+    every use, inside ExpertParallelLayer (StreamedLocalExperts as the local layer); each rank
+    routes its own cfg.T tokens (weak scaling). An 8-layer fwd + bwd a step; the step time is
+    the max over ranks."""
+    ClockSampler.start(local)
+    from lazylora_b200.core.moe_router import KimiK3MoERouter
+    from lazylora_b200.synthetic import make_layer_device
+    from lazylora_b200.trainer.expert_parallel import ExpertParallelLayer, experts_of_rank
+    from lazylora_b200.trainer.expert_streamer import ExpertStreamer, HostExpertStore, StreamedLocalExperts
+    dev = torch.device("cuda", local)
+    n_layers, D = 8, max(1, args.stream_distinct)
+    first, count = experts_of_rank(cfg.E, world, rank)
+    store = HostExpertStore()
+    inp = None
+    for l in range(D):
+        inp = make_layer_device(cfg if l == 0 else cfg.__class__(**{**cfg.__dict__, "seed": cfg.seed + 100 * l}),
+                                device=dev)
+        store.add_layer(l, {n: inp[n][first:first + count] for n in ("w1p", "w1s", "w3p", "w3s", "w2p", "w2s")})
+        if l + 1 < D:
+            del inp
+            torch.cuda.empty_cache()
+    lora = {n: inp[n] for n in ("A_g", "B_g", "A_u", "B_u", "A_d", "B_d")}
+    gen = torch.Generator(device=dev).manual_seed(cfg.seed + 1000 + rank)      # this rank's tokens
+    x = torch.randn(cfg.T, cfg.d, generator=gen, device=dev).to(torch.bfloat16)
+    g = torch.randn(cfg.T, cfg.d, generator=gen, device=dev).to(torch.bfloat16)
+    Wr, br = inp["router_w"], inp["router_b"]
+    del inp
+    torch.cuda.empty_cache()
+    router = KimiK3MoERouter(hidden_size=cfg.d, num_experts=cfg.E, top_k=cfg.k, device=dev)
+    streamer = ExpertStreamer(store, lora, cfg.scaling, group_experts=min(args.stream_group, count), device=dev)
+    local_ids = list(range(count))
+    eps = [ExpertParallelLayer(StreamedLocalExperts(streamer, l % D, expert_ids=local_ids), cfg.E)
+           for l in range(n_layers)]
+    stream = torch.cuda.current_stream()
+
+    def step():
+        for l in range(n_layers):
+            i, ww = router.forward(x, weight=Wr, bias=br)
+            if l + 1 < n_layers:
+                streamer.prefetch((l + 1) % D, local_ids)
+            eps[l].forward(x, i, ww)
+        for l in reversed(range(n_layers)):
+            if l > 0:
+                streamer.prefetch((l - 1) % D, local_ids)
+            eps[l].backward(g)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    b0 = streamer.bytes_copied
+    with ClockSampler(local) as clk:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            step()
+        b.record(stream)
+        torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / args.steps], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms = float(t.item())
+    bytes_step = (streamer.bytes_copied - b0) / args.steps
+    h2d = bytes_step / (step_ms * 1e-3) / 1e9
+    dist.barrier()
+    if rank != 0:
+        return
+    line = {"metric": "streamed 8-layer MoE fwd+bwd tokens/s (configs[4], weights in pinned host memory, "
+                      "expert parallel)",
+            "value": world * cfg.T / (step_ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+            "dtype": "fp16 operands / fp32 accumulate", "data": "synthetic",
+            "config": {"workload": f"configs[4]: 8 layers, T={cfg.T} per GPU, r={cfg.r}; each of {world} ranks holds "
+                                   f"{count} of {cfg.E} experts per layer in pinned host memory and streams them "
+                                   "host->HBM for the forward and again for the backward; NCCL all-to-all dispatch "
+                                   "+ combine", "d": cfg.d, "f": cfg.f, "E": cfg.E, "k": cfg.k, "T_per_gpu": cfg.T,
+                       "r": cfg.r, "experts_per_rank": count, "distinct_pinned_layers": D,
+                       "group_experts": streamer.group, "parallelism": f"ep{world}"},
+            "h2d_rank0": {"bytes_per_step": bytes_step, "achieved_GBps": h2d, "peak_GBps": args.h2d_peak,
+                          "frac": h2d / args.h2d_peak, "peak_kind": "measured pinned cudaMemcpyAsync on this box"},
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def run_stream(args, cfg, rank, local, world, dist):
     ClockSampler.start(local)
     """configs[4]: an 8-layer fwd + bwd whose expert weights live in pinned host memory and
@@ -1022,7 +1107,10 @@ def main():
         elif args.decode:
             run_decode(args, cfg, rank, local, world, dist)
         elif args.stream:
-            run_stream(args, cfg, rank, local, world, dist)
+            if world > 1:
+                run_stream_ep(args, cfg, rank, local, world, dist)
+            else:
+                run_stream(args, cfg, rank, local, world, dist)
         elif args.latent:
             run_latent(args, cfg, rank, local, world, dist)
         elif args.traces:

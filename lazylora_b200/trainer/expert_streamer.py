@@ -262,3 +262,40 @@ def streamed_backward(streamer: ExpertStreamer, layer_idx: int, x: torch.Tensor,
             for k2 in grads:
                 grads[k2].add_(gr[k2])
     return grad_h, grad_w, grads
+
+
+class StreamedLocalExperts:
+    """One layer's experts held in pinned host memory and streamed into HBM group by group for
+    every forward and backward, with the interface of a resident RoutedExpertsLayer that
+    ExpertParallelLayer takes as its local layer: under expert parallelism each rank's store
+    holds only that rank's block of experts (ids local to the rank), so a rank moves 1/n of the
+    layer's bytes over its PCIe link instead of all of them (configs[4] on n GPUs; the
+    reference streams every expert to its one GPU, expert_streamer.py:315-369).
+
+    expert_ids: the experts streamed for each call, ascending (None: those the call routes to,
+    read back from the routing once, a host synchronisation).
+    """
+
+    accepts_rows_hint = False
+
+    def __init__(self, streamer: ExpertStreamer, layer_idx: int, expert_ids: Optional[Sequence[int]] = None):
+        self.streamer = streamer
+        self.layer_idx = int(layer_idx)
+        self.E = streamer.store.num_experts(layer_idx)
+        self.expert_ids = list(expert_ids) if expert_ids is not None else None
+        self._ids = None
+
+    def forward(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        out, self._ids = streamed_forward(self.streamer, self.layer_idx, x, idx, w, expert_ids=self.expert_ids)
+        return out
+
+    def backward(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, g: torch.Tensor):
+        if self._ids is None:
+            raise RuntimeError("backward before forward")
+        return streamed_backward(self.streamer, self.layer_idx, x, idx, w, g, self._ids)
+
+    def lora_shapes(self) -> Dict[str, tuple]:
+        lo = self.streamer.lora
+        r, d = lo["A_g"].shape
+        f = lo["B_g"].shape[0]
+        return {"dA_g": (r, d), "dB_g": (f, r), "dA_u": (r, d), "dB_u": (f, r), "dA_d": (r, f), "dB_d": (d, r)}

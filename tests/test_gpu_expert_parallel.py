@@ -68,7 +68,20 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, case):
+def _local_layer(local_inp, cfg, streamed):
+    """The rank's block of experts: resident, or (streamed) held in pinned host memory and
+    streamed into HBM three experts at a time for every forward and backward."""
+    from lazylora_b200.trainer.routed_experts import RoutedExpertsLayer
+    if not streamed:
+        return RoutedExpertsLayer.from_inputs(local_inp, cfg.scaling)
+    from lazylora_b200.trainer.expert_streamer import ExpertStreamer, HostExpertStore, StreamedLocalExperts
+    store = HostExpertStore()
+    store.add_layer(0, {n: local_inp[n] for n in ("w1p", "w1s", "w3p", "w3s", "w2p", "w2s")})
+    lora = {n: local_inp[n].cuda() for n in ("A_g", "B_g", "A_u", "B_u", "A_d", "B_d")}
+    return StreamedLocalExperts(ExpertStreamer(store, lora, cfg.scaling, group_experts=3), 0)
+
+
+def _rank_main(rank, world, port, case, streamed=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
@@ -77,13 +90,12 @@ def _rank_main(rank, world, port, case):
                             device_id=torch.device("cuda", rank))
     try:
         from lazylora_b200.trainer.expert_parallel import ExpertParallelLayer
-        from lazylora_b200.trainer.routed_experts import RoutedExpertsLayer
         cfg = CONFIGS[case]
         inp = make_layer(cfg)
         x, g = inp["x"], inp["g"]
         idx, w = O.route(x.float(), inp["router_w"], inp["router_b"], cfg.k)
         local_inp, lo, hi = EPO.split_experts(inp, cfg.E, world, rank)
-        ep = ExpertParallelLayer(RoutedExpertsLayer.from_inputs(local_inp, cfg.scaling), cfg.E)
+        ep = ExpertParallelLayer(_local_layer(local_inp, cfg, streamed), cfg.E)
         bounds = [(cfg.T * r) // world for r in range(world + 1)]
         t0, t1 = bounds[rank], bounds[rank + 1]
         xd = x[t0:t1].cuda()
@@ -94,7 +106,7 @@ def _rank_main(rank, world, port, case):
         got["out"] = ep.forward(xd, idx[t0:t1].cuda(), w[t0:t1].cuda())
         got["grad_h"], got["grad_w"], grads = ep.backward(gd)
         got.update(grads)
-        if ep._ctx["R"]:
+        if ep._ctx["R"] and not streamed:
             ep.local.check_status(ep._ctx["R"], cfg.k)
         # the single-process reference algorithm over all tokens and all experts
         layer = O.Layer.from_inputs(inp, cfg.scaling)
@@ -118,3 +130,18 @@ def _rank_main(rank, world, port, case):
 def test_expert_parallel_two_gpus_matches_oracle(case):
     O.build()
     mp.start_processes(_rank_main, args=(2, _free_port(), case), nprocs=2, start_method="spawn")
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_expert_parallel_two_gpus_streamed_local_experts():
+    """configs[4]'s composition: each rank streams only its own block of experts from pinned
+    host memory (StreamedLocalExperts as the EP layer's local layer), against the oracle."""
+    O.build()
+    mp.start_processes(_rank_main, args=(2, _free_port(), "small", True), nprocs=2, start_method="spawn")
+
+
+def test_expert_parallel_one_rank_streamed_local_experts():
+    """The same composition on one GPU (a one-rank NCCL group): the exchanges are identities,
+    the streamed local experts are the whole layer."""
+    O.build()
+    mp.start_processes(_rank_main, args=(1, _free_port(), "c0", True), nprocs=1, start_method="spawn")
