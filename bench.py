@@ -1073,6 +1073,8 @@ def main():
     ap.add_argument("--zipf-gamma", type=float, default=None, help="override the config's Zipf bias scale")
     ap.add_argument("--experts", type=int, default=None,
                     help="override the config's expert count (profiler captures on a smaller weight stack)")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="override the config's token count (profiler captures of other tile widths)")
     ap.add_argument("--stream", action="store_true", help="configs[4]: experts streamed from pinned host memory")
     ap.add_argument("--latent", action="store_true", help="the latent routed block (use --config c1_latent)")
     ap.add_argument("--traces", action="store_true", help="fwd+bwd steps on the recorded K3 routings (top-16)")
@@ -1092,6 +1094,8 @@ def main():
         cfg = replace(cfg, zipf_gamma=args.zipf_gamma)
     if args.experts is not None:
         cfg = replace(cfg, E=args.experts)
+    if args.tokens is not None:
+        cfg = replace(cfg, T=args.tokens)
     rank, local, world, dist = dist_setup(args)
     if world > 1 and args.config in ("c1", "c2") and not (args.decode or args.stream or args.latent or
                                                           args.traces or args.shared):

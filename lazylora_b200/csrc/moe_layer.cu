@@ -448,6 +448,12 @@ static int choose_nmax(const ll_moe_layer* L, int T, int k) {
   // the narrowest tile that holds nearly every expert's rows in one chunk (a second chunk
   // re-reads the expert's weights): Poisson-like counts exceed 16 rows for ~1% of experts at a
   // mean of 9, 32 rows for ~0.1% at 18, 64 rows for ~1% at 48
+  static const int forced = [] {          // LL_NMAX: a fixed tile width (16, 32, 64 or 128), for tuning
+    const char* e = getenv("LL_NMAX");
+    const int v = e ? atoi(e) : 0;
+    return (v == 16 || v == 32 || v == 64 || v == 128) ? v : 0;
+  }();
+  if (forced) return forced;
   return mean <= 10.0 ? 16 : mean <= 22.0 ? 32 : (mean <= 48.0 ? 64 : 128);
 }
 
