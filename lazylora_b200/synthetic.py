@@ -96,6 +96,39 @@ def zipf_target(E: int, s: float, gen: torch.Generator) -> torch.Tensor:
     return p / p.sum()
 
 
+def fit_zipf_bias(router_w: torch.Tensor, p: torch.Tensor, k: int, tokens: int = 65536, chunk: int = 8192,
+                  iters: int = 1000, lr: float = 0.01, step_max: float = 0.005, seed: int = 7):
+    """A per-expert router bias whose top-k selection frequencies over `tokens` seeded N(0,1)
+    (bf16) tokens approach the target p (iterative: bias_e += clip(lr * (ln p_e - ln f_e),
+    +-step_max); the scores' spread is a few tenths, so steps stay small). An expert
+    is chosen at most once per token, so frequencies above 1/k are out of reach; those targets
+    are capped at 1/k for the iteration. Returns (bias [E] fp32, L1 of the achieved frequencies
+    against the uncapped p). The router arithmetic is the reference's: sigmoid(x Wr^T) + bias,
+    top-k of that (lazy_lora/core/moe_router.py:80-100)."""
+    dev = router_w.device
+    E, d = router_w.shape
+    gx = torch.Generator(device=dev).manual_seed(seed)
+    scores = torch.empty((tokens, E), dtype=torch.float32, device=dev)
+    for t0 in range(0, tokens, chunk):
+        n = min(chunk, tokens - t0)
+        x = torch.randn(n, d, generator=gx, device=dev).to(torch.bfloat16).float()
+        scores[t0:t0 + n] = torch.sigmoid(x @ router_w.float().t())
+    p = p.to(dev).double()
+    target = torch.log(p.clamp(max=1.0 / k))
+    bias = torch.zeros(E, dtype=torch.float64, device=dev)
+
+    def freq(b):
+        idx = torch.topk(scores + b.float(), k, dim=-1).indices
+        return torch.bincount(idx.reshape(-1), minlength=E).double() / (tokens * k)
+
+    for _ in range(iters):
+        f = freq(bias)
+        bias += (lr * (target - torch.log(f + 0.5 / (tokens * k)))).clamp(-step_max, step_max)
+        bias -= bias.max()
+    f = freq(bias)
+    return bias.float(), float((f - p).abs().sum())
+
+
 def fit_zipf_gamma(cfg: LayerConfig, device="cuda", tokens: int = 65536, chunk: int = 8192):
     """The router-bias scale gamma whose top-k selection frequencies over `tokens` seeded
     N(0,1) tokens best match the Zipf target p in L1 (1-D search, log grid then refinement).
