@@ -2,7 +2,8 @@
 KimiK3MoERouter on the B200: same constructor and forward contract as
 lazy_lora/core/moe_router.py:23-135, with the logits, sigmoid, biased top-k selection,
 gather and renormalisation done by the library's router kernels (ll_route_topk_prepared; the
-frozen weight's split into bf16 planes, ll_route_prepare, is kept between calls).
+frozen weight's split into bf16 planes, ll_route_prepare, is kept between calls; up to 8 tokens,
+ll_route_topk on the fp32 weight itself).
 
 Ties in the selection go to the lower expert id. torch's CPU topk leaves the order of equal
 values unspecified, so on inputs with exact ties the order (not the set) may differ.
@@ -58,6 +59,15 @@ class KimiK3MoERouter(torch.nn.Module):
         planes = self._planes[1]
         idx = torch.empty((T, k), dtype=torch.int64, device=xf.device)
         tw = torch.empty((T, k), dtype=torch.float32, device=xf.device)
+        if T <= 8 and weight.dtype == torch.float32 and weight.is_contiguous() and weight.data_ptr() % 16 == 0:
+            # a few tokens: the logits are a matrix-vector product on CUDA cores, which reads the
+            # fp32 weight itself (two thirds of the planes' bytes; the same logits, bit for bit)
+            L.check(lib.ll_route_topk(xf.data_ptr(), 0 if xf.dtype == torch.float32 else 1, weight.data_ptr(),
+                                      L.ptr(b), T, self.hidden_size, E, k, int(self.renormalize),
+                                      float(self.routed_scaling_factor), idx.data_ptr(), tw.data_ptr(), None,
+                                      self._ws.data_ptr(), nbytes, L.stream_ptr()),
+                    "ll_route_topk")
+            return idx, tw
         L.check(lib.ll_route_topk_prepared(xf.data_ptr(), 0 if xf.dtype == torch.float32 else 1, planes.data_ptr(),
                                            L.ptr(b), T, self.hidden_size, E, k, int(self.renormalize),
                                            float(self.routed_scaling_factor), idx.data_ptr(), tw.data_ptr(), None,

@@ -26,6 +26,8 @@
 //
 // Work units are (chunk of <= N_MAX rows of one expert, m-tile) as in grouped_gemm.cuh, with two
 // weight tiles per unit (gate and up for F1; two adjacent 128-row tiles of one stack for F2).
+// With few units (decode) the units' K stages are shared out evenly over the CTAs instead and a
+// unit cut between CTAs is finished from fp32 partials (BsSegs).
 // Warp roles (7 warps): 0 TMA producer (weights, activations, scale blocks of a stage on one
 // mbarrier), 1 MMA issuer (tcgen05.cp of the stage's scales, then the K-steps x 2 tiles of
 // MMAs, one commit releasing the stage), 2..5 epilogue (one TMEM lane quarter each), 6 watcher
@@ -58,6 +60,59 @@ struct BsArgs {
   int prefetch;               // stages the L2 prefetch of weight tiles runs ahead of the loads
   DevStatus* status;
   EpiParams epi;
+  // Balanced split (few units, see BsSegs): partial sums of the units several CTAs share, two
+  // slots per CTA [slot][2 products][N_MAX][128 rows] fp32, and four arrival counters per unit
+  // (one per epilogue warp; zero before the launch, the last arrival sets its counter back to
+  // zero). Off when split_part is null.
+  float* split_part;
+  int* split_cnt;
+  int split_units;            // units the counters cover: the split runs only for n_units <= this
+  int split_ctas;             // CTAs split_part has slots for
+};
+
+// The (unit, K-stage range) pieces a CTA runs. Without the split, CTA b takes whole units b,
+// b + G, b + 2G, ... (G = gridDim.x). With it, the n_units * n_stage stages in unit order are cut
+// into G contiguous ranges of equal length (+-1), CTA b taking stages [b tot / G, (b+1) tot / G):
+// every CTA streams the same number of weight bytes however few units there are. A range is
+// whole units plus at most a partial first and a partial last piece; a unit cut across CTAs
+// b0..b1 (b0 = the owner of its first stage) is finished by whichever of them arrives last,
+// which adds the pieces' fp32 partials in the order b0, b0 + 1, ..., b1.
+struct BsSeg {
+  int u, ks0, ks1;            // unit and its stages [ks0, ks1)
+  int piece;                  // 0: the first piece of this CTA's range, 1: a later one
+};
+struct BsSegs {
+  long long g, end, tot;
+  int ns, G;
+  bool split, first = true;
+  LL_DEV BsSegs(bool sp, int n_units, int n_stage) : ns(n_stage), G((int)gridDim.x), split(sp) {
+    tot = (long long)n_units * n_stage;
+    if (sp) {
+      g = begin_of(blockIdx.x);
+      end = begin_of(blockIdx.x + 1);
+    } else {
+      g = (long long)blockIdx.x * n_stage;
+      end = tot;
+    }
+  }
+  LL_DEV long long begin_of(int b) const { return tot * b / G; }
+  // the CTA whose range holds stage gs: the largest b with begin_of(b) <= gs
+  LL_DEV int owner(long long gs) const { return (int)(((gs + 1) * G - 1) / tot); }
+  LL_DEV bool next(BsSeg& s) {
+    if (g >= end) return false;
+    s.u = (int)(g / ns);
+    const long long u0 = (long long)s.u * ns, u1 = u0 + ns;
+    s.ks0 = (int)(g - u0);
+    s.ks1 = (int)((u1 < end ? u1 : end) - u0);
+    s.piece = first ? 0 : 1;
+    first = false;
+    g = split ? u1 : u1 + (long long)(G - 1) * ns;
+    return true;
+  }
+  // slot of the o-th piece of unit u (o = 0 .. nseg-1, CTAs b0 + o)
+  LL_DEV int slot(int u, int o, int b0) const {
+    return 2 * (b0 + o) + ((o == 0 && begin_of(b0) < (long long)u * ns) ? 1 : 0);
+  }
 };
 
 template <int NMAT, int N_MAX, int KIND>
@@ -167,7 +222,11 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
   pdl_launch_next();                        // (after the allocation: see pdl_launch_next)
   pdl_wait();
   const int n_units = (*args.n_chunks) * args.mtiles;
-  if ((int)blockIdx.x >= n_units) {         // uniform per block: no unit for this one
+  // the balanced split for a few waves of units (at least one unit a CTA: with fewer it measured
+  // slower, the partial sums' round trip costing more than the bytes it evens out)
+  const bool split = args.split_part != nullptr && n_units >= (int)gridDim.x && n_units <= args.split_units &&
+                     (int)gridDim.x <= args.split_ctas;
+  if (!split && (int)blockIdx.x >= n_units) {   // uniform per block: no unit for this one
     if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
     return;
   }
@@ -183,6 +242,7 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
       // weight tiles and scale blocks are prefetched into L2 args.prefetch stages ahead of their
       // loads (off by default: measured slower on configs[1])
       int pu = blockIdx.x, pks = 0;
+      const int prefetch = split ? 0 : args.prefetch;
       auto prefetch_next = [&]() {
         if (pu >= n_units) return;
         const Chunk pc = args.chunks[pu / args.mtiles];
@@ -197,8 +257,11 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
                                 : args.sfa[i] + ((size_t)ptile * n_stage + pks) * kBsSfBlock, kBsSfBlock);
         if (++pks == n_stage) { pks = 0; pu += gridDim.x; }
       };
-      for (int i = 0; i < args.prefetch; i++) prefetch_next();
-      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+      for (int i = 0; i < prefetch; i++) prefetch_next();
+      BsSegs segs(split, n_units, n_stage);
+      BsSeg sg;
+      while (ok && segs.next(sg)) {
+        const int u = sg.u;
         const int ci = u / args.mtiles;
         const Chunk ch = args.chunks[ci];
         const int mt = u % args.mtiles;
@@ -206,7 +269,7 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
         const int tile0 = ch.e * tiles128 + mt * (TILE_ROWS / 128);
         const int npad = (ch.n + 15) & ~15;
         const uint32_t tx = NMAT * C::A_TX + NT * npad * C::ROWB + (NMAT + C::SFB_BLKS) * kBsSfBlock;
-        for (int ks = 0; ks < n_stage && ok; ks++) {
+        for (int ks = sg.ks0; ks < sg.ks1 && ok; ks++) {
           if (!(ok = mbar_wait_sleep(&empty[s], ph ^ 1, abort_flag, st, 21, 256))) break;
           uint8_t* stage = smem + s * C::STAGE;
           mbar_arrive_expect_tx(&full[s], tx);
@@ -228,7 +291,7 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
             bulk_load(sf + NMAT * kBsSfBlock, args.sfb + ((size_t)ci * n_stage + ks) * C::SFB_BLKS * kBsSfBlock,
                       C::SFB_BLKS * kBsSfBlock, &full[s]);
           issued++;
-          if (args.prefetch > 0) prefetch_next();
+          if (prefetch > 0) prefetch_next();
           if (++s == C::S) { s = 0; ph ^= 1; }
         }
       }
@@ -251,13 +314,15 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
       int s = 0, ab = 0;
       uint32_t ev = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-        const Chunk ch = args.chunks[u / args.mtiles];
+      BsSegs segs(split, n_units, n_stage);
+      BsSeg sg;
+      while (ok && segs.next(sg)) {
+        const Chunk ch = args.chunks[sg.u / args.mtiles];
         const int npad = (ch.n + 15) & ~15;
         const uint32_t n_mma = NT * npad;
         if (!(ok = seq_wait(ready_seq, ++ev, abort_flag, st, 23))) break;
         tc_fence_after();
-        for (int ks = 0; ks < n_stage; ks++) {
+        for (int ks = sg.ks0; ks < sg.ks1; ks++) {
           if (!(ok = seq_wait(ready_seq, ++ev, abort_flag, st, 24))) break;
           tc_fence_after();
           uint8_t* stage = smem + s * C::STAGE;
@@ -285,9 +350,10 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
               const uint32_t d = tmem + ab * C::ACC_COLS + i * C::BN;
               const uint32_t sfa = tmem + C::SFA_BASE + (s * NMAT + i) * 4 + (sfid << 30);
               if (C::FP4)
-                mma_mxf4_bs(d, adesc, bdesc0 + kk * 2, idesc, sfa, sfb + (sfid << 30), (ks | kk) ? 1u : 0u);
+                mma_mxf4_bs(d, adesc, bdesc0 + kk * 2, idesc, sfa, sfb + (sfid << 30), (ks != sg.ks0 || kk) ? 1u : 0u);
               else
-                mma_mxf8f6f4_bs(d, adesc, bdesc0 + kk * 2, idesc, sfa, sfb + (sfid << 30), (ks | kk) ? 1u : 0u);
+                mma_mxf8f6f4_bs(d, adesc, bdesc0 + kk * 2, idesc, sfa, sfb + (sfid << 30),
+                                (ks != sg.ks0 || kk) ? 1u : 0u);
             }
           }
           mma_commit(&empty[s]);                 // stage (and its scale slots) free once these finish
@@ -310,10 +376,12 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
     if (lane == 0) {
       int s = 0, ab = 0;
       uint32_t ph = 0, abph = 0, ev = 0;
-      for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      BsSegs segs(split, n_units, n_stage);
+      BsSeg sg;
+      while (segs.next(sg)) {
         mbar_wait(&accempty[ab], abph ^ 1, abort_flag, st, 27);
         seq_publish(ready_seq, ++ev);
-        for (int ks = 0; ks < n_stage; ks++) {
+        for (int ks = sg.ks0; ks < sg.ks1; ks++) {
           mbar_wait(&full[s], ph, abort_flag, st, 28);
           seq_publish(ready_seq, ++ev);
           if (++s == C::S) { s = 0; ph ^= 1; }
@@ -336,12 +404,35 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
     float* __restrict__ Uo = ep.U;
     __half* __restrict__ Ho = ep.H;
     float* __restrict__ Yo = ep.Y;
+    // the per-row output of a finished (token row p, output row m) from its accumulator sums
+    auto finish = [&](int p, int m, float v, float up) {
+      const size_t o = (size_t)p * ep.M + m;
+      if (EPI == EPI_F1) {
+        const int tk = perm ? perm[p] : p;
+        const size_t tmo = (size_t)tk * ep.M + m;
+        const float gate = v + dlt_g[tmo];
+        up += dlt_u[tmo];
+        Go[o] = gate;
+        Uo[o] = up;
+        Ho[o] = __float2half_rn(situ_glu_fwd(gate, up));
+      } else if (EPI == EPI_F2) {
+        Yo[o] = v * tw[p];
+      } else {
+        Yo[o] = v;
+      }
+    };
     int ab = 0;
     uint32_t abph = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+    BsSegs segs(split, n_units, n_stage);
+    BsSeg sg;
+    while (ok && segs.next(sg)) {
+      const int u = sg.u;
       const Chunk ch = args.chunks[u / args.mtiles];
       const int npad = (ch.n + 15) & ~15;
+      // a piece of a split unit: its partial sums go to this CTA's slot
+      const bool whole = sg.ks0 == 0 && sg.ks1 == n_stage;
+      float* part = whole ? nullptr : args.split_part + (size_t)(2 * blockIdx.x + sg.piece) * 2 * N_MAX * 128;
       if (!(ok = mbar_wait_sleep(&accfull[ab], abph, abort_flag, st, 26, 512))) break;
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * C::ACC_COLS;
@@ -379,22 +470,19 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
             float v = __uint_as_float(d[NT - 1][jj]) * sc[NT - 1];
 #pragma unroll
             for (int t = NT - 2; t >= 0; t--) v = fmaf(__uint_as_float(d[t][jj]), sc[t], v);
-            const size_t o = (size_t)p * ep.M + m;
+            float up = 0.f;
             if (EPI == EPI_F1) {
-              float up = __uint_as_float(e[NT - 1][jj]) * sc[NT - 1];
+              up = __uint_as_float(e[NT - 1][jj]) * sc[NT - 1];
 #pragma unroll
               for (int t = NT - 2; t >= 0; t--) up = fmaf(__uint_as_float(e[t][jj]), sc[t], up);
-              const int tk = perm ? perm[p] : p;
-              const size_t tmo = (size_t)tk * ep.M + m;
-              const float gate = v + dlt_g[tmo];
-              up += dlt_u[tmo];
-              Go[o] = gate;
-              Uo[o] = up;
-              Ho[o] = __float2half_rn(situ_glu_fwd(gate, up));
-            } else if (EPI == EPI_F2) {
-              Yo[o] = v * tw[p];
+            }
+            if (whole) {
+              finish(p, m, v, up);
+            } else if (EPI == EPI_F1) {
+              __stcg(part + (size_t)j * 128 + row, v);
+              __stcg(part + (size_t)(N_MAX + j) * 128 + row, up);
             } else {
-              Yo[o] = v;
+              __stcg(part + (size_t)(pm * N_MAX + j) * 128 + row, v);
             }
           }
         }
@@ -403,6 +491,52 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
       __syncwarp();
       if (lane == 0) mbar_arrive(&accempty[ab]);
       if (++ab == C::NACC) { ab = 0; abph ^= 1; }
+      if (!whole) {
+        // count this warp's quarter of the piece in (a counter per unit and quarter: no barrier
+        // across warps); the last of the unit's pieces adds them all, in CTA order, and writes
+        // that quarter's outputs
+        const long long us = (long long)u * n_stage;
+        const int b0 = segs.owner(us), nseg = segs.owner(us + n_stage - 1) - b0 + 1;
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+          int* cnt = args.split_cnt + 4 * u + q;
+          last = atomicAdd(cnt, 1) == nseg - 1;
+          if (last) *cnt = 0;                    // ready for the next launch
+          __threadfence();
+        }
+        if (__shfl_sync(0xffffffffu, last, 0)) {
+          __threadfence();
+#pragma unroll 1
+          for (int pm = 0; pm < (PAIR ? 2 : 1); pm++) {
+            const int m = ((u % args.mtiles) * (PAIR ? 2 : 1) + pm) * 128 + row;
+            if (m >= ep.M) continue;
+#pragma unroll 1
+            for (int j0 = 0; j0 < ch.n; j0 += 16) {
+              // 16 rows' sums at a time, each piece's loads issued together
+              float v[16], up[16];
+#pragma unroll
+              for (int jj = 0; jj < 16; jj++) v[jj] = up[jj] = 0.f;
+#pragma unroll 1
+              for (int o = 0; o < nseg; o++) {
+                const float* pp = args.split_part + (size_t)segs.slot(u, o, b0) * 2 * N_MAX * 128;
+                const float* pv = pp + (size_t)((EPI == EPI_F1 ? 0 : pm) * N_MAX + j0) * 128 + row;
+#pragma unroll
+                for (int jj = 0; jj < 16; jj++) {
+                  if (j0 + jj < ch.n) {
+                    v[jj] += __ldcg(pv + jj * 128);
+                    if (EPI == EPI_F1) up[jj] += __ldcg(pv + (N_MAX + jj) * 128);
+                  }
+                }
+              }
+#pragma unroll
+              for (int jj = 0; jj < 16; jj++)
+                if (j0 + jj < ch.n) finish(ch.p0 + j0 + jj, m, v[jj], up[jj]);
+            }
+          }
+        }
+      }
     }
   }
 

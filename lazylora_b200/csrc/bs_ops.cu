@@ -8,6 +8,8 @@
 #include "host_common.cuh"
 #include "ops.cuh"
 
+#include <cub/block/block_scan.cuh>
+
 namespace ll {
 
 // One thread per (row, 128-K stage): the row's 4 scale bytes of that stage, bytes >= 253 (the
@@ -138,56 +140,16 @@ __global__ void __launch_bounds__(kE3Threads) k_rows_to_e4m3x3(const void* __res
   }
 }
 
-// The BS_FP4 activation terms: per row, four rounds of (per 32-element block: max |r|, scale
-// 2^e with e the smallest exponent bringing that max into [-6, 6], round r / 2^e to E2M1,
-// subtract). Term t of pair row p: packed codes dst[t][p][K/2] (two per byte, even element in
-// the low nibble). A 32-element block is 4 neighbouring threads' 8 values, so the block max is
-// two shuffles, and a row splits over blocks with no reduction: block (x, y) takes source row x,
-// 8-element chunks [256 y, 256 y + 256) (16 stages of 128 K).
-// The E8M0 scale bytes go straight into the MMA's B scale blocks of the row's chunk: block
-// (chunk c, stage ks) of 512 bytes holds, for B row n = t npad + j (term t, chunk row j), the
-// row's 4 scale bytes of the stage at word (n % 32) * 4 + (n % 128) / 32 (the tcgen05.cp layout).
-// The other words are left as they are: they only scale B rows past the chunk's rows (MMA
-// columns the epilogue never reads, as the MMA's columns are independent) or past the MMA's N.
-template <int SRC, bool TOK>
-__global__ void __launch_bounds__(kE3Threads) k_rows_to_e2m1x4(const void* __restrict__ src, int src_rows,
-                                                               const int* __restrict__ tok_pos, int k,
-                                                               const int* __restrict__ n_valid, int K, int64_t P,
-                                                               uint8_t* __restrict__ dst,
-                                                               const Chunk* __restrict__ chunks,
-                                                               const int* __restrict__ chunk_of,
-                                                               uint32_t* __restrict__ sfb) {
-  pdl_wait();
-  pdl_launch_next();
-  const int r = blockIdx.x;
-  if (r >= src_rows) return;
-  if (!TOK && n_valid && r >= *n_valid) return;
-  const int nch = K / 8, n_stage = K / 128;
-  const int ch = blockIdx.y * kE3Threads + threadIdx.x;
+// The four E2M1 term rounds of one thread's 8 source values (8-element chunk ch of the row),
+// each term's packed codes stored to the nd destination pair rows s_p[] (skipping -1) and the
+// stage's scale word to their chunks' B scale blocks (chunk s_c[], row s_jr[] of s_npad[] rows);
+// see k_rows_to_e2m1x4 for the formats.
+LL_DEV void e2m1x4_store(float (&v)[8], int ch, int nch, int K, int64_t P, int nd, const int* s_p, const int* s_c,
+                         const int* s_jr, const int* s_npad, uint8_t* __restrict__ dst, uint32_t* __restrict__ sfb) {
+  const int n_stage = K / 128;
   const int ks = ch / 16;                        // stage of this thread's chunk
   const bool lead = (ch & 15) == 0;              // writes the stage's scale word
   constexpr int WPB = kBsSfBlock / 4;            // words per scale block
-  float v[8];
-#pragma unroll
-  for (int j = 0; j < 8; j++) v[j] = 0.f;
-  if (ch < nch) load8<SRC>(src, r, K, ch, v);
-  // destinations (pair row, chunk, row in the chunk, padded chunk rows), looked up by one thread
-  // each so that their loads overlap
-  __shared__ int s_p[32], s_c[32], s_jr[32], s_npad[32];
-  const int nd = TOK ? k : 1;
-  if ((int)threadIdx.x < nd) {
-    const int j = threadIdx.x;
-    const int p = TOK ? tok_pos[(int64_t)r * k + j] : r;
-    s_p[j] = p;
-    if (p >= 0) {
-      const int c = chunk_of[p];
-      const Chunk cc = chunks[c];
-      s_c[j] = c;
-      s_jr[j] = p - cc.p0;
-      s_npad[j] = (cc.n + 15) & ~15;
-    }
-  }
-  __syncthreads();
 #pragma unroll 1
   for (int t = 0; t < kBsTermsFp4; t++) {
     float mx = 0.f;
@@ -230,6 +192,195 @@ __global__ void __launch_bounds__(kE3Threads) k_rows_to_e2m1x4(const void* __res
       }
     }
   }
+}
+
+// The BS_FP4 activation terms: per row, four rounds of (per 32-element block: max |r|, scale
+// 2^e with e the smallest exponent bringing that max into [-6, 6], round r / 2^e to E2M1,
+// subtract). Term t of pair row p: packed codes dst[t][p][K/2] (two per byte, even element in
+// the low nibble). A 32-element block is 4 neighbouring threads' 8 values, so the block max is
+// two shuffles, and a row splits over blocks with no reduction: block (x, y) takes source row x,
+// 8-element chunks [256 y, 256 y + 256) (16 stages of 128 K).
+// The E8M0 scale bytes go straight into the MMA's B scale blocks of the row's chunk: block
+// (chunk c, stage ks) of 512 bytes holds, for B row n = t npad + j (term t, chunk row j), the
+// row's 4 scale bytes of the stage at word (n % 32) * 4 + (n % 128) / 32 (the tcgen05.cp layout).
+// The other words are left as they are: they only scale B rows past the chunk's rows (MMA
+// columns the epilogue never reads, as the MMA's columns are independent) or past the MMA's N.
+template <int SRC, bool TOK>
+__global__ void __launch_bounds__(kE3Threads) k_rows_to_e2m1x4(const void* __restrict__ src, int src_rows,
+                                                               const int* __restrict__ tok_pos, int k,
+                                                               const int* __restrict__ n_valid, int K, int64_t P,
+                                                               uint8_t* __restrict__ dst,
+                                                               const Chunk* __restrict__ chunks,
+                                                               const int* __restrict__ chunk_of,
+                                                               uint32_t* __restrict__ sfb) {
+  pdl_wait();
+  pdl_launch_next();
+  const int r = blockIdx.x;
+  if (r >= src_rows) return;
+  if (!TOK && n_valid && r >= *n_valid) return;
+  const int nch = K / 8;
+  const int ch = blockIdx.y * kE3Threads + threadIdx.x;
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) v[j] = 0.f;
+  if (ch < nch) load8<SRC>(src, r, K, ch, v);
+  // destinations (pair row, chunk, row in the chunk, padded chunk rows), looked up by one thread
+  // each so that their loads overlap
+  __shared__ int s_p[32], s_c[32], s_jr[32], s_npad[32];
+  const int nd = TOK ? k : 1;
+  if ((int)threadIdx.x < nd) {
+    const int j = threadIdx.x;
+    const int p = TOK ? tok_pos[(int64_t)r * k + j] : r;
+    s_p[j] = p;
+    if (p >= 0) {
+      const int c = chunk_of[p];
+      const Chunk cc = chunks[c];
+      s_c[j] = c;
+      s_jr[j] = p - cc.p0;
+      s_npad[j] = (cc.n + 15) & ~15;
+    }
+  }
+  __syncthreads();
+  e2m1x4_store(v, ch, nch, K, P, nd, s_p, s_c, s_jr, s_npad, dst, sfb);
+}
+
+// The few-token sort and the x terms in one launch (k_plan_small, then k_rows_to_e2m1x4 on the
+// token rows, with the same outputs bit for bit). Every block takes one token row r and 8-element
+// chunks [256 y, 256 y + 256) of it, and works out from idx the sort it needs: the experts'
+// counts (shared-memory histogram of every pair), their row and chunk offsets (two block scans),
+// then for its own token's pairs the position in the sorted order (pairs of one expert keep
+// their order), chunk and row in the chunk. The blocks with y = 0 write their token's entries of
+// the sort (pair_pos, perm_token, perm_slot, tw, chunk_of, tok_pos); block (0, 0) writes the
+// per-expert outputs (offsets, chunks, n_chunks), the -1 of perm_token past the valid pairs, and
+// clears the status word; the n_zero ints at `zero` are cleared by all blocks together. Needs
+// E <= 4 * kE3Threads and k <= 32.
+template <int SRC>
+__global__ void __launch_bounds__(kE3Threads) k_plan_rows_to_e2m1x4(
+    const int64_t* __restrict__ idx, const float* __restrict__ w, int T, int k, int E, int nmax,
+    int* __restrict__ offsets, Chunk* __restrict__ chunks, int* __restrict__ n_chunks, int* __restrict__ perm_token,
+    int* __restrict__ perm_slot, int* __restrict__ pair_pos, float* __restrict__ tw, int* __restrict__ tok_pos,
+    int* __restrict__ chunk_of, DevStatus* __restrict__ st, int* __restrict__ zero, int n_zero,
+    const void* __restrict__ src, int K, int64_t P, uint8_t* __restrict__ dst, uint32_t* __restrict__ sfb) {
+  using Scan = cub::BlockScan<int, kE3Threads>;
+  __shared__ typename Scan::TempStorage tmp;
+  __shared__ int cnt[4 * kE3Threads], rbase[4 * kE3Threads], cbase[4 * kE3Threads];
+  __shared__ int s_p[32], s_c[32], s_jr[32], s_npad[32], s_e[32];
+  extern __shared__ int es[];                    // [T k] expert of each pair, -1 if not routed here
+  pdl_wait();
+  pdl_launch_next();
+  const int r = blockIdx.x, tid = threadIdx.x;
+  const bool first = blockIdx.x == 0 && blockIdx.y == 0;
+  const int np = T * k, nch = K / 8;
+  const int ch = blockIdx.y * kE3Threads + tid;
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) v[j] = 0.f;
+  if (ch < nch) load8<SRC>(src, r, K, ch, v);
+  if (first && tid == 0 && st) *st = DevStatus{0, 0, 0, 0};
+  {
+    const int nb = gridDim.x * gridDim.y, b = blockIdx.y * gridDim.x + blockIdx.x;
+    for (int i = b * kE3Threads + tid; i < n_zero; i += nb * kE3Threads) zero[i] = 0;
+  }
+  for (int e = tid; e < E; e += kE3Threads) cnt[e] = 0;
+  __syncthreads();
+  for (int i = tid; i < np; i += kE3Threads) {
+    const int64_t e = idx[i];
+    const bool ok = e >= 0 && e < E;
+    es[i] = ok ? (int)e : -1;
+    if (ok) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  int c4[4], n4[4], ro[4], co[4], agg_rows, agg_ch;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int e = 4 * tid + j;
+    c4[j] = e < E ? cnt[e] : 0;
+    n4[j] = (c4[j] + nmax - 1) / nmax;
+  }
+  Scan(tmp).ExclusiveSum(c4, ro, agg_rows);
+  __syncthreads();
+  Scan(tmp).ExclusiveSum(n4, co, agg_ch);
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int e = 4 * tid + j;
+    if (e >= E) continue;
+    rbase[e] = ro[j];
+    cbase[e] = co[j];
+    if (first) {
+      offsets[e] = ro[j];
+      for (int i = 0; i < n4[j]; i++) chunks[co[j] + i] = Chunk{e, ro[j] + i * nmax, min(nmax, c4[j] - i * nmax), 0};
+    }
+  }
+  if (first) {
+    if (tid == 0) {
+      offsets[E] = agg_rows;
+      *n_chunks = agg_ch;
+    }
+    for (int p = agg_rows + tid; p < np; p += kE3Threads) perm_token[p] = -1;
+  }
+  __syncthreads();
+  // this token's pairs
+  if (tid < k) {
+    const int i = r * k + tid;
+    const int e = es[i];
+    int p = -1;
+    if (e >= 0) {
+      int rank = 0;
+      for (int j = 0; j < i; j++) rank += es[j] == e;
+      p = rbase[e] + rank;
+      const int cr = rank / nmax;
+      s_c[tid] = cbase[e] + cr;
+      s_jr[tid] = rank - cr * nmax;
+      s_npad[tid] = (min(nmax, cnt[e] - cr * nmax) + 15) & ~15;
+      if (blockIdx.y == 0) {
+        perm_token[p] = r;
+        perm_slot[p] = tid;
+        tw[p] = w[i];
+        chunk_of[p] = s_c[tid];
+      }
+    }
+    s_p[tid] = p;
+    s_e[tid] = e;
+    if (blockIdx.y == 0) pair_pos[i] = p;
+  }
+  __syncthreads();
+  if (blockIdx.y == 0 && tid == 0) {   // the token's pair positions by ascending expert id
+    int ee[32], pp[32];
+    int n = 0;
+    for (int sl = 0; sl < k; sl++) {
+      const int e = s_e[sl];
+      if (e < 0) continue;
+      int j = n++;
+      while (j > 0 && ee[j - 1] > e) { ee[j] = ee[j - 1]; pp[j] = pp[j - 1]; j--; }
+      ee[j] = e;
+      pp[j] = s_p[sl];
+    }
+    for (int sl = 0; sl < k; sl++) tok_pos[(int64_t)r * k + sl] = sl < n ? pp[sl] : -1;
+  }
+  e2m1x4_store(v, ch, nch, K, P, k, s_p, s_c, s_jr, s_npad, dst, sfb);
+}
+
+int launch_plan_rows_to_e2m1x4(const int64_t* idx, const float* w, int T, int k, int E, int nmax, int* offsets,
+                               Chunk* chunks, int* n_chunks, int* perm_token, int* perm_slot, int* pair_pos, float* tw,
+                               int* tok_pos, int* chunk_of, DevStatus* st, int* zero, int n_zero, const void* src,
+                               int src_dtype, int K, int64_t P, uint8_t* dst, uint8_t* sfb, cudaStream_t s) {
+  if (T <= 0) return LL_OK;
+  if (!idx || !w || !src || !dst || !sfb || E <= 0 || E > 4 * kE3Threads || k <= 0 || k > 32 || nmax <= 0 ||
+      nmax > 32 || K <= 0 || K % 128 || src_dtype < 0 || src_dtype > 2 || (int64_t)T * k > 2048)
+    return LL_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(sfb)) % 16)
+    return LL_ERR_ARG;
+  uint32_t* sw = reinterpret_cast<uint32_t*>(sfb);
+  const dim3 grid(T, (K / 8 + kE3Threads - 1) / kE3Threads);
+  const size_t smem = (size_t)T * k * sizeof(int);
+#define LL_PE(SRC)                                                                                               \
+  return launch_pdl("k_plan_rows_to_e2m1x4", k_plan_rows_to_e2m1x4<SRC>, grid, dim3(kE3Threads), smem, s, idx, w, T, \
+                    k, E, nmax, offsets, chunks, n_chunks, perm_token, perm_slot, pair_pos, tw, tok_pos, chunk_of, st, \
+                    zero, n_zero, src, K, P, dst, sw)
+  if (src_dtype == 0) LL_PE(0);
+  if (src_dtype == 1) LL_PE(1);
+  LL_PE(2);
+#undef LL_PE
 }
 
 int launch_rows_to_e2m1x4(const void* src, int src_dtype, int src_rows, const int* tok_pos, int k,

@@ -29,6 +29,9 @@
 namespace ll {
 
 constexpr int kTokBlock = 64;   // tokens per block in the counting sort
+// The block-scaled GEMMs' balanced split: for up to kSplitUnits units (8 per CTA at 148 SMs),
+// with partial slots for up to kSplitCtas CTAs.
+constexpr int kSplitUnits = 1280, kSplitCtas = 160;
 
 // ----------------------------------------------------------------- counting sort
 __global__ void k_count(const int64_t* __restrict__ idx, int T, int k, int E, int* __restrict__ cnt) {
@@ -143,15 +146,16 @@ __global__ void k_scatter(const int64_t* __restrict__ idx, const float* __restri
 
 // The three kernels above in one block, for a batch of at most kTokBlock tokens (nblk == 1),
 // with the same outputs bit for bit (the per-block bases of k_scan are the expert offsets
-// here); also clears perm_token (-1) and the status word, so that a few-token forward starts
-// with no copy or memset.
+// here); also clears perm_token (-1), the status word and n_zero ints at `zero` (the split
+// GEMMs' arrival counters), so that a few-token forward starts with no copy or memset.
 __global__ void __launch_bounds__(1024) k_plan_small(const int64_t* __restrict__ idx, const float* __restrict__ w,
                                                      int T, int k, int E, int nmax, int* __restrict__ offsets,
                                                      Chunk* __restrict__ chunks, int* __restrict__ n_chunks,
                                                      int* __restrict__ perm_token, int* __restrict__ perm_slot,
                                                      int* __restrict__ pair_pos, float* __restrict__ tw,
                                                      int* __restrict__ tok_pos, int* __restrict__ chunk_of,
-                                                     DevStatus* __restrict__ st) {
+                                                     DevStatus* __restrict__ st, int* __restrict__ zero,
+                                                     int n_zero) {
   pdl_wait();
   pdl_launch_next();
   using Scan = cub::BlockScan<int, 1024>;
@@ -168,6 +172,7 @@ __global__ void __launch_bounds__(1024) k_plan_small(const int64_t* __restrict__
   }
   for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
   for (int i = threadIdx.x; i < np; i += blockDim.x) perm_token[i] = -1;
+  for (int i = threadIdx.x; i < n_zero; i += blockDim.x) zero[i] = 0;
   __syncthreads();
   for (int i = threadIdx.x; i < np; i += blockDim.x) {
     const int64_t e = idx[i];
@@ -436,6 +441,11 @@ struct LayerWs {
   size_t skpart_floats;
   int nmax;
   int nseg_max;
+  // the block-scaled GEMMs' balanced split (few tokens only): partial slots, and the F1 then F2
+  // arrival counters (4 per unit each), cleared by k_plan_small
+  float* split_part;
+  int* split_cnt;
+  int split_units;
 };
 
 // Token rows per chunk (the MMA N): the smallest tile that holds most experts' rows in one
@@ -521,6 +531,11 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
     w.skpart_floats = (size_t)4 * 160 * 8192 + (size_t)(rows + 256) * (2 * r + 32);
     w.skpart = c.take<float>(w.skpart_floats);
   }
+  if (T <= kTokBlock && nmax <= 64) {   // the one-block plan clears the counters
+    w.split_units = kSplitUnits;
+    w.split_part = c.take<float>((size_t)2 * kSplitCtas * 2 * nmax * 128);
+    w.split_cnt = c.take<int>((size_t)2 * 4 * kSplitUnits);
+  }
   if (out) *out = w;
   return c.off + 256;
 }
@@ -579,6 +594,24 @@ static int bs_prefetch_stages() {
     return e ? atoi(e) : 0;
   }();
   return v;
+}
+
+// Unit counts up to which F1 / F2 run the balanced split (from one unit a CTA up). Measured on
+// F1 at 352 units (2.4 a CTA, T = 4) 86 -> 78 us; F1 at 1152 units (7.8 a CTA) 211
+// -> 220 us and F2 at 224 / 616 units (16-stage units) 26 -> 28 / 45 -> 47 us, slower; so F1 up
+// to 4 units a CTA and not F2. LL_BS_SPLIT_F1 / LL_BS_SPLIT_F2 override (for tuning; 0 = off;
+// at most kSplitUnits).
+static int bs_split_units(int which) {
+  static const int v[2] = {[] {
+                             const char* e = getenv("LL_BS_SPLIT_F1");
+                             return e ? atoi(e) : -1;
+                           }(),
+                           [] {
+                             const char* e = getenv("LL_BS_SPLIT_F2");
+                             return e ? atoi(e) : 0;
+                           }()};
+  const int u = v[which] >= 0 ? v[which] : 4 * device_info().sms;
+  return std::min(u, kSplitUnits);
 }
 
 // The block-scaled forward GEMM kind for a token-tile width: E2M1 activation terms up to 32
@@ -802,10 +835,21 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
   LL_CUDA(cudaEventRecord(ss->join, ss->s));
   g_launch_stream = s;
 
-  if (nblk == 1) {    // few tokens: the counting sort in one block, no memset
+  // Tiles up to 64 rows: the forward GEMMs run on the block-scaled MMAs (weights not decoded;
+  // E2M1 activation terms up to 32 rows, E4M3 at 64); 128-row tiles (the large-T regime) on the
+  // fp16 dequant path.
+  const int kind = bs_kind(W.nmax);
+  const bool bs = kind >= 0;
+  // few tokens with E2M1 terms: the sort and x's terms in one launch
+  const bool fused_front = nblk == 1 && kind == BS_FP4 && E <= 1024 && k <= 32 && P <= 2048;
+  if (fused_front) {
+    LL_TRY(launch_plan_rows_to_e2m1x4(idx, w, T, k, E, W.nmax, W.offsets, W.chunks, W.n_chunks, W.perm_token,
+                                      W.perm_slot, W.pair_pos, W.tw, W.tok_pos, W.chunk_of, W.st, W.split_cnt,
+                                      W.split_cnt ? 2 * 4 * W.split_units : 0, x, x_dtype, d, P, W.xq, W.xsfb, s));
+  } else if (nblk == 1) {    // few tokens: the counting sort in one block, no memset
     LL_TRY(launch_pdl("k_plan_small", k_plan_small, dim3(1), dim3(1024), (size_t)(E + P) * sizeof(int), s, idx, w, T,
                       k, E, W.nmax, W.offsets, W.chunks, W.n_chunks, W.perm_token, W.perm_slot, W.pair_pos, W.tw,
-                      W.tok_pos, W.chunk_of, W.st));
+                      W.tok_pos, W.chunk_of, W.st, W.split_cnt, W.split_cnt ? 2 * 4 * W.split_units : 0));
   } else {
     LL_TRY(reset_status(W.st, s));
     LL_CUDA(cudaMemsetAsync(W.perm_token, 0xFF, sizeof(int) * P, s));
@@ -815,11 +859,6 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
     LL_TRY(launch_pdl("k_scatter", k_scatter, dim3(nblk), dim3(256), kTokBlock * k * sizeof(int), s, idx, w, T, k, E,
                       W.cnt, W.perm_token, W.perm_slot, W.pair_pos, W.tw, W.tok_pos));
   }
-  // Tiles up to 64 rows: the forward GEMMs run on the block-scaled MMAs (weights not decoded;
-  // E2M1 activation terms up to 32 rows, E4M3 at 64); 128-row tiles (the large-T regime) on the
-  // fp16 dequant path.
-  const int kind = bs_kind(W.nmax);
-  const bool bs = kind >= 0;
   if (!bs) LL_TRY(launch_token_rows_to_half(x, x_dtype, W.perm_token, W.tok_pos, T, k, d, W.xh, W.xinv, s));
   // F1: gate / up (after the side stream's deltas)
   if (bs) {
@@ -832,7 +871,12 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
       LL_TRY(make_fp4_map(&a[1], L->w3p, (int64_t)E * f, d, 128));
     }
     BsArgs a1{};
-    LL_TRY(bs_operand(kind, W, x, x_dtype, T, W.tok_pos, k, nullptr, d, P, W.xq, W.xinv3, W.xsfb, b, a1, s));
+    if (fused_front) {
+      LL_TRY(make_e2m1x4_maps(b, W.nmax / 16, W.xq, P, d));
+      a1.sfb = W.xsfb;
+    } else {
+      LL_TRY(bs_operand(kind, W, x, x_dtype, T, W.tok_pos, k, nullptr, d, P, W.xq, W.xinv3, W.xsfb, b, a1, s));
+    }
     a1.chunks = W.chunks;
     a1.n_chunks = W.n_chunks;
     a1.mtiles = f / 128;
@@ -842,6 +886,10 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
     a1.sfa[1] = L->w3sf;
     a1.prefetch = bs_prefetch_stages();
     a1.status = W.st;
+    a1.split_part = W.split_part;
+    a1.split_cnt = W.split_cnt;
+    a1.split_units = std::min(W.split_units, bs_split_units(0));
+    a1.split_ctas = kSplitCtas;
     a1.epi.perm_token = W.perm_token;
     a1.epi.P = P;
     a1.epi.M = f;
@@ -879,9 +927,21 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
     LL_TRY((gemm_nmax<EPI_F1, 2, 1, false>(W.nmax, pk, sc, act, a, s)));
   }
   const int* n_valid = W.offsets + E;
-  // z = h . A_d^T per pair (h as the fp16 rows the down GEMM reads)
-  LL_TRY(skinny(W.H, 2, true, P, f, L->A_d, nullptr, r, r, 1.f, W.z, nullptr, W.skpart, W.skpart_floats, s));
-  // (q = the routing-weighted sum of z per token is formed by the combine below)
+  // z = h . A_d^T per pair (h as the fp16 rows the down GEMM reads); with few tokens on the side
+  // stream beside the h terms and F2 (which use neither z nor the skinny partials), joined before
+  // the combine. (q = the routing-weighted sum of z per token is formed by the combine below.)
+  const bool z_side = nblk == 1;
+  if (z_side) {
+    LL_CUDA(cudaEventRecord(ss->fork, s));
+    LL_CUDA(cudaStreamWaitEvent(ss->s, ss->fork, 0));
+    g_launch_stream = ss->s;
+  }
+  LL_TRY(skinny(W.H, 2, true, P, f, L->A_d, nullptr, r, r, 1.f, W.z, nullptr, W.skpart, W.skpart_floats,
+                z_side ? ss->s : s));
+  if (z_side) {
+    LL_CUDA(cudaEventRecord(ss->join, ss->s));
+    g_launch_stream = s;
+  }
   // F2: down (paired 128-row tiles of the stack: d a multiple of 256)
   if (bs && d % 256 == 0) {
     CUtensorMap a[2], b[4];
@@ -900,6 +960,10 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
     a2.sfa[0] = a2.sfa[1] = L->w2sf;
     a2.prefetch = bs_prefetch_stages();
     a2.status = W.st;
+    a2.split_part = W.split_part;
+    a2.split_cnt = W.split_cnt ? W.split_cnt + 4 * W.split_units : nullptr;
+    a2.split_units = std::min(W.split_units, bs_split_units(1));
+    a2.split_ctas = kSplitCtas;
     a2.epi.perm_token = W.perm_token;
     a2.epi.tw = W.tw;
     a2.epi.P = P;
@@ -928,6 +992,7 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
     a.epi.Y = W.Y;
     LL_TRY((gemm_nmax<EPI_F2, 2, 1, false>(W.nmax, pk, sc, act, a, s)));
   }
+  if (z_side) LL_CUDA(cudaStreamWaitEvent(s, ss->join, 0));
   if (norm_w) {
     if (d % 2 || r > kExMaxR || k > 32) return LL_ERR_ARG;
     const int smem = r * kExPitch * (int)sizeof(float);

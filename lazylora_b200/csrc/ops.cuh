@@ -51,4 +51,13 @@ int launch_rows_to_e2m1x4(const void* src, int src_dtype, int src_rows, const in
                           const int* n_valid, int K, int64_t P, uint8_t* dst, const Chunk* chunks, const int* chunk_of,
                           int nmax, uint8_t* sfb, cudaStream_t s);
 
+// The few-token sort of the routed pairs (the outputs of k_plan_small: offsets, chunks,
+// n_chunks, perm_token, perm_slot, pair_pos, tw, tok_pos, chunk_of; the status word and n_zero
+// ints at `zero` cleared) and the T token rows of src as launch_rows_to_e2m1x4 writes them to
+// their pair rows, in one launch. E <= 1024, k <= 32, T k <= 2048, nmax <= 32.
+int launch_plan_rows_to_e2m1x4(const int64_t* idx, const float* w, int T, int k, int E, int nmax, int* offsets,
+                               Chunk* chunks, int* n_chunks, int* perm_token, int* perm_slot, int* pair_pos, float* tw,
+                               int* tok_pos, int* chunk_of, DevStatus* st, int* zero, int n_zero, const void* src,
+                               int src_dtype, int K, int64_t P, uint8_t* dst, uint8_t* sfb, cudaStream_t s);
+
 }  // namespace ll

@@ -310,22 +310,23 @@ __global__ void k_sum_partials(const float* __restrict__ part, int nsplit, int64
   logits[i] = acc;
 }
 
-// ------------------------------------------------ few-token logits and selection, one launch
+// ------------------------------------------------------------------ few-token logits
 // For a handful of tokens the router is a matrix-vector product bound by reading W. Block = 8
 // warps = 2 experts x 4 warps; warp q of an expert takes the runs q, q + 4, ... of 32 16-byte
-// chunks of the expert's row (four runs' loads issued together), W read as stored (fp32) or
-// rebuilt from its three bf16 planes (hi + lo + lo2, which is W exactly); per token, the lanes'
-// sums go through a shuffle tree and the 4 warps' sums are added in warp order. With a counter
-// (one token), the last block to finish (the counter in the workspace, zeroed before the launch)
-// then selects the token's top k from the logits (block_select_token); without, the logits are
-// left for k_route_select_block (a block per token, in parallel).
-constexpr int kRgTok = 8, kRgRun = 4;
+// chunks of the expert's row (four runs' loads issued together, two from planes), W read as
+// stored (fp32) or rebuilt from its three bf16 planes (hi + lo + lo2, which is W exactly); per
+// token, the lanes' sums go through a shuffle tree and the 4 warps' sums are added in warp
+// order. At most 64 registers a thread, so that four blocks fit an SM and the 448 blocks of 896
+// experts run as one wave (at three a SM the last four blocks ran as a second wave). The logits
+// are left for k_route_select_block (a block per token): selecting in the last block of this
+// kernel to finish, behind a counter, measured slower (one token: 30.7 us against 28.7 us).
+constexpr int kRgTok = 8;
 template <bool PLANES, int XT>
-__global__ void __launch_bounds__(256) k_router_gemv_select(const void* __restrict__ x, const void* __restrict__ W,
-                                                            const float* __restrict__ bias, int T, int d, int E,
-                                                            int k, int renorm, float rsf, float* __restrict__ logits,
-                                                            unsigned* __restrict__ counter, int64_t* __restrict__ idx,
-                                                            float* __restrict__ w, float* __restrict__ scores_out) {
+__global__ void __launch_bounds__(256, 4) k_router_gemv(const void* __restrict__ x, const void* __restrict__ W, int T,
+                                                       int d, int E, float* __restrict__ logits) {
+  // runs whose loads are issued together: 4 (fp32 W), 2 (three planes: the registers of 4 spill);
+  // a lane adds its chunks in the same order either way
+  constexpr int kRgRun = PLANES ? 2 : 4;
   pdl_wait();
   pdl_launch_next();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -397,7 +398,6 @@ __global__ void __launch_bounds__(256) k_router_gemv_select(const void* __restri
     }
   }
   __shared__ float red[8][kRgTok];
-  __shared__ int s_last;
 #pragma unroll
   for (int t = 0; t < kRgTok; t++) {
     float v = acc[t];
@@ -415,34 +415,6 @@ __global__ void __launch_bounds__(256) k_router_gemv_select(const void* __restri
       for (int qq = 1; qq < 4; qq++) v += red[4 * el + qq][t];
       logits[(int64_t)t * E + ee] = v;
     }
-  }
-  if (!counter) return;                                // the selection is a kernel of its own
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();                                   // this block's logits before its count
-    s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  // the last block: every token's selection, one token at a time by the whole block
-  __shared__ SelShared sh;
-  for (int t = 0; t < T; t++) {
-    float sc[4], ch[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const int ei = 256 * i + 32 * warp + lane;
-      sc[i] = 0.f;
-      ch[i] = -INFINITY;
-      if (ei < E) {
-        const float sg = 1.0f / (1.0f + expf(-__ldcg(logits + (int64_t)t * E + ei)));
-        sc[i] = sg;
-        ch[i] = bias ? sg + bias[ei] : sg;
-        if (scores_out) scores_out[(int64_t)t * E + ei] = sg;
-      }
-    }
-    block_select_token(sc, ch, E, k, renorm, rsf, sh, idx + (int64_t)t * k, w + (int64_t)t * k);
-    __syncthreads();
   }
 }
 
@@ -472,7 +444,7 @@ static RouterPlan router_plan(int T, int d, int E, int x_dtype) {
     p.off_x = take(p.NP == 3 ? (size_t)3 * T * d * 2 : 0);
     p.off_part = take((size_t)p.nsplit * T * E * 4);
     p.off_logits = take((size_t)T * E * 4);
-    p.off_st = take(32);              // the status word, then the few-token path's block counter
+    p.off_st = take(32);              // the status word
     p.bytes = (off + 255) & ~size_t(255);
   }
   return p;
@@ -551,21 +523,15 @@ static int route_topk(const void* x, int x_dtype, const float* router_w, const _
   LL_STREAM(stream);
   g_launch_count = 0;
   if (T <= kRgTok && E <= 1024 && (reinterpret_cast<uintptr_t>(planes ? (const void*)planes : (const void*)router_w) % 16) == 0) {
-    // few tokens: logits on CUDA cores and the selection in the same launch
-    uint8_t* base = static_cast<uint8_t*>(ws);
-    LL_CUDA(cudaMemsetAsync(base + p.off_st, 0, 32, s));
-    unsigned* counter = reinterpret_cast<unsigned*>(base + p.off_st + sizeof(DevStatus));
-    float* logits = reinterpret_cast<float*>(base + p.off_logits);
-    const dim3 grid((E + 1) / 2);
+    // few tokens: logits on CUDA cores, then the selection
+    float* logits = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + p.off_logits);
     const void* wsrc = planes ? static_cast<const void*>(planes) : static_cast<const void*>(router_w);
-    unsigned* cnt = T == 1 ? counter : nullptr;       // one token: selected by the last block
-#define LL_RG(PL, XTv)                                                                                          \
-  LL_TRY(launch_pdl("k_router_gemv_select", k_router_gemv_select<PL, XTv>, grid, dim3(256), 0, s, x, wsrc, bias, T, \
-                    d, E, k, renormalize, routed_scaling_factor, logits, cnt, idx, w, scores_out))
+#define LL_RG(PL, XTv)                                                                                   \
+  LL_TRY(launch_pdl("k_router_gemv", k_router_gemv<PL, XTv>, dim3((E + 1) / 2), dim3(256), 0, s, x, wsrc, T, d, E, \
+                    logits))
     if (planes) { if (x_dtype == 0) LL_RG(true, 0); else LL_RG(true, 1); }
     else { if (x_dtype == 0) LL_RG(false, 0); else LL_RG(false, 1); }
 #undef LL_RG
-    if (T == 1) return LL_OK;
     return launch_select<0>(logits, nullptr, bias, T, E, k, renormalize, routed_scaling_factor, idx, w, scores_out, s,
                             1);
   }

@@ -181,6 +181,37 @@ def test_full_width_token_subset(c1_layer):
     assert n_exp >= 200, n_exp
 
 
+@pytest.mark.parametrize("T", [1, 4, 16])
+def test_full_width_decode_batches(c1_layer, T):
+    """Decode-sized batches of the 896-expert layer (configs[3]'s T = 1, 4, 16: the one-launch
+    sort with the x terms, and the GEMMs' K stages shared out evenly over the CTAs, a unit cut
+    between CTAs finished from fp32 partials) against the oracle, and bitwise repeatable."""
+    cfg, inp, layer, x, idx, w = c1_layer
+    sub = dict(inp, g=inp["g"][:T])
+    tokens = torch.arange(T)
+    _token_subset_vs_oracle(cfg, sub, layer, x[:T].contiguous(), idx[:T].contiguous(), w[:T].contiguous(), tokens)
+    a = layer.forward(x[:T].contiguous(), idx[:T].contiguous(), w[:T].contiguous())
+    b = layer.forward(x[:T].contiguous(), idx[:T].contiguous(), w[:T].contiguous())
+    layer.check_status(T, cfg.k)
+    assert torch.equal(a, b)
+
+
+def test_split_thresholds_raised_subprocess():
+    """The balanced split on every launch it can take (F1 and F2 up to 1280 units, env read once
+    per process, so in a child pytest): the c0 / k3 goldens and the decode batches."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, LL_BS_SPLIT_F1="1280", LL_BS_SPLIT_F2="1280")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-p", "no:cacheprovider",
+                        os.path.join(here, "test_gpu_layer.py"), "-k",
+                        "(goldens and (c0 or k3)) or decode_batches"],
+                       env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert " passed" in r.stdout and "5 passed" in r.stdout, r.stdout[-2000:]
+
+
 def test_configs2_shape_token_subset():
     """configs[2]'s single-GPU shape (T = 8192, about 73 rows per expert: the 128-row token
     tiles, experts split over two chunks): 24 tokens spread over the batch against the oracle."""
