@@ -9,8 +9,9 @@
 // products vanish in the fp32 sums.
 //
 // The activations (the B operand) are a short sum of low-precision terms stacked along N: the B
-// tile of a chunk of n rows is [term][npad rows][K], so one MMA of N = terms * npad computes
-// every term's partial product into adjacent accumulator columns, and the epilogue adds them.
+// tile of a chunk of n rows is [term][npad rows][K] (n padded to 16 rows, or to 4 for tiles of at
+// most 4 rows), so one MMA of N = terms * npad computes every term's partial product into
+// adjacent accumulator columns, and the epilogue adds them.
 // Two kinds:
 //   BS_FP4  kind::mxf4 (K = 64 per MMA): the weights stay packed in shared memory (half the
 //           bytes the tensor core reads per weight element), and the activations are four E2M1
@@ -115,6 +116,16 @@ struct BsSegs {
   }
 };
 
+// Row padding of a chunk's activation rows in the B tile (the MMA N is terms x padded rows):
+// 16 rows, or 4 for the four-row tiles of tiny batches (a chunk of at most 4 rows; MMA N = 16,
+// a quarter of the B bytes a stage of a 16-row tile moves), and the tensor maps per tile height.
+template <int N_MAX>
+struct BsRows {
+  static constexpr int rp = N_MAX < 16 ? 4 : 16;
+  static constexpr int maps = N_MAX / rp;
+  static LL_DEV int pad(int n) { return (n + rp - 1) & ~(rp - 1); }
+};
+
 template <int NMAT, int N_MAX, int KIND>
 struct BsCfg {
   static constexpr int kThreads = 7 * 32;
@@ -131,7 +142,7 @@ struct BsCfg {
   static constexpr int STAGE0 = NMAT * A_TILE + B_TILE + (NMAT + SFB_BLKS) * kBsSfBlock;
   static constexpr int STAGE = (STAGE0 + 1023) / 1024 * 1024;
   static constexpr int S0 = (227 * 1024 - 4096) / STAGE;
-  static constexpr int S = S0 > 10 ? 10 : S0;
+  static constexpr int S = S0 > 12 ? 12 : S0;
   static_assert(S >= 2, "shared memory budget");
   static constexpr int OFF_SFB = S * STAGE;               // BS_FP8: 512 bytes of 0x7f (every B scale 1.0)
   static constexpr int OFF_BAR = OFF_SFB + kBsSfBlock;
@@ -151,14 +162,14 @@ struct BsCfg {
   static constexpr int TMEM_COLS0 = SFB_BASE + SFB_SLOTS * 8;
   static constexpr int TMEM_COLS = TMEM_COLS0 <= 32 ? 32 : TMEM_COLS0 <= 64 ? 64 : TMEM_COLS0 <= 128 ? 128
                                    : TMEM_COLS0 <= 256 ? 256 : 512;
-  static_assert(N_MAX % 16 == 0 && BN <= 256, "MMA N");
+  static_assert((N_MAX % 16 == 0 || (N_MAX == 4 && FP4)) && BN <= 256, "MMA N");
   static_assert(A_TILE % 1024 == 0 && (16 * ROWB) % 1024 == 0, "1024-byte aligned operand tiles and terms");
 };
 
 template <int NMAT, int N_MAX, int KIND>
 struct BsTma {
   CUtensorMap a[NMAT];          // weight codes (BS_FP4 packed, 64-byte swizzle; BS_FP8 unpacked, 128)
-  CUtensorMap b[N_MAX / 16];    // b[c - 1]: [terms][16 c rows][128 K] activation terms
+  CUtensorMap b[BsRows<N_MAX>::maps];   // b[c - 1]: [terms][RP c rows][128 K] activation terms
 };
 
 // UMMA descriptor of a K-major operand tile (rows of ROWB bytes, the swizzle of that width).
@@ -212,7 +223,7 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
   if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
   if (warp == 0 && lane == 0) {
     for (int i = 0; i < NMAT; i++) tma_prefetch_desc(&tm.a[i]);
-    for (int i = 0; i < N_MAX / 16; i++) tma_prefetch_desc(&tm.b[i]);
+    for (int i = 0; i < BsRows<N_MAX>::maps; i++) tma_prefetch_desc(&tm.b[i]);
   }
   tc_fence_before();
   __syncthreads();
@@ -267,7 +278,7 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
         const int mt = u % args.mtiles;
         const int row = ch.e * args.e_rows + mt * TILE_ROWS;
         const int tile0 = ch.e * tiles128 + mt * (TILE_ROWS / 128);
-        const int npad = (ch.n + 15) & ~15;
+        const int npad = BsRows<N_MAX>::pad(ch.n);
         const uint32_t tx = NMAT * C::A_TX + NT * npad * C::ROWB + (NMAT + C::SFB_BLKS) * kBsSfBlock;
         for (int ks = sg.ks0; ks < sg.ks1 && ok; ks++) {
           if (!(ok = mbar_wait_sleep(&empty[s], ph ^ 1, abort_flag, st, 21, 256))) break;
@@ -279,7 +290,8 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
 #pragma unroll
             for (int i = 0; i < NMAT; i++) tma_load_2d(stage + i * C::A_TILE, &tm.a[i], &full[s], ks * AX, row);
           }
-          tma_load_3d(stage + NMAT * C::A_TILE, &tm.b[npad / 16 - 1], &full[s], ks * C::ROWB, ch.p0, 0);
+          tma_load_3d(stage + NMAT * C::A_TILE, &tm.b[npad / BsRows<N_MAX>::rp - 1], &full[s], ks * C::ROWB, ch.p0,
+                      0);
           uint8_t* sf = stage + NMAT * C::A_TILE + C::B_TILE;
 #pragma unroll
           for (int i = 0; i < NMAT; i++) {
@@ -318,7 +330,7 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
       BsSeg sg;
       while (ok && segs.next(sg)) {
         const Chunk ch = args.chunks[sg.u / args.mtiles];
-        const int npad = (ch.n + 15) & ~15;
+        const int npad = BsRows<N_MAX>::pad(ch.n);
         const uint32_t n_mma = NT * npad;
         if (!(ok = seq_wait(ready_seq, ++ev, abort_flag, st, 23))) break;
         tc_fence_after();
@@ -429,7 +441,7 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
     while (ok && segs.next(sg)) {
       const int u = sg.u;
       const Chunk ch = args.chunks[u / args.mtiles];
-      const int npad = (ch.n + 15) & ~15;
+      const int npad = BsRows<N_MAX>::pad(ch.n);
       // a piece of a split unit: its partial sums go to this CTA's slot
       const bool whole = sg.ks0 == 0 && sg.ks1 == n_stage;
       float* part = whole ? nullptr : args.split_part + (size_t)(2 * blockIdx.x + sg.piece) * 2 * N_MAX * 128;
@@ -445,21 +457,38 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
         for (int j0 = 0; j0 < npad; j0 += 16) {
           // the terms' partial products of 16 tokens (and of the up projection for F1)
           uint32_t d[NT][16], e[EPI == EPI_F1 ? NT : 1][16];
+          if (BsRows<N_MAX>::rp == 4) {
+            // four rows a term: one 16-column load holds every term's columns (term t at 4 t)
+            uint32_t rd[16], re[16];
+            tmem_ld16_u(c0, rd);
+            if (EPI == EPI_F1) tmem_ld16_u(c0 + C::BN, re);
+            tmem_ld_wait();
+            tmem_regs_ready(rd);
+            if (EPI == EPI_F1) tmem_regs_ready(re);
 #pragma unroll
-          for (int t = 0; t < NT; t++) tmem_ld16_u(c0 + t * npad + j0, d[t]);
-          if (EPI == EPI_F1) {                   // the up projection: tile 1's accumulator
+            for (int t = 0; t < NT; t++)
 #pragma unroll
-            for (int t = 0; t < NT; t++) tmem_ld16_u(c0 + C::BN + t * npad + j0, e[t]);
+              for (int jj = 0; jj < 4; jj++) {
+                d[t][jj] = rd[4 * t + jj];
+                if (EPI == EPI_F1) e[t][jj] = re[4 * t + jj];
+              }
+          } else {
+#pragma unroll
+            for (int t = 0; t < NT; t++) tmem_ld16_u(c0 + t * npad + j0, d[t]);
+            if (EPI == EPI_F1) {                 // the up projection: tile 1's accumulator
+#pragma unroll
+              for (int t = 0; t < NT; t++) tmem_ld16_u(c0 + C::BN + t * npad + j0, e[t]);
+            }
+            tmem_ld_wait();
+#pragma unroll
+            for (int t = 0; t < NT; t++) tmem_regs_ready(d[t]);
+            if (EPI == EPI_F1) {
+#pragma unroll
+              for (int t = 0; t < NT; t++) tmem_regs_ready(e[t]);
+            }
           }
-          tmem_ld_wait();
 #pragma unroll
-          for (int t = 0; t < NT; t++) tmem_regs_ready(d[t]);
-          if (EPI == EPI_F1) {
-#pragma unroll
-            for (int t = 0; t < NT; t++) tmem_regs_ready(e[t]);
-          }
-#pragma unroll
-          for (int jj = 0; jj < 16; jj++) {
+          for (int jj = 0; jj < (BsRows<N_MAX>::rp == 4 ? 4 : 16); jj++) {
             const int j = j0 + jj;
             if (j >= ch.n || !mvalid) continue;
             const int p = ch.p0 + j;

@@ -201,8 +201,9 @@ LL_DEV void e2m1x4_store(float (&v)[8], int ch, int nch, int K, int64_t P, int n
 // two shuffles, and a row splits over blocks with no reduction: block (x, y) takes source row x,
 // 8-element chunks [256 y, 256 y + 256) (16 stages of 128 K).
 // The E8M0 scale bytes go straight into the MMA's B scale blocks of the row's chunk: block
-// (chunk c, stage ks) of 512 bytes holds, for B row n = t npad + j (term t, chunk row j), the
-// row's 4 scale bytes of the stage at word (n % 32) * 4 + (n % 128) / 32 (the tcgen05.cp layout).
+// (chunk c, stage ks) of 512 bytes holds, for B row n = t npad + j (term t, chunk row j; npad =
+// the chunk's rows padded to rp = 16, or to 4 for four-row tiles), the row's 4 scale bytes of the
+// stage at word (n % 32) * 4 + (n % 128) / 32 (the tcgen05.cp layout).
 // The other words are left as they are: they only scale B rows past the chunk's rows (MMA
 // columns the epilogue never reads, as the MMA's columns are independent) or past the MMA's N.
 template <int SRC, bool TOK>
@@ -212,7 +213,7 @@ __global__ void __launch_bounds__(kE3Threads) k_rows_to_e2m1x4(const void* __res
                                                                uint8_t* __restrict__ dst,
                                                                const Chunk* __restrict__ chunks,
                                                                const int* __restrict__ chunk_of,
-                                                               uint32_t* __restrict__ sfb) {
+                                                               uint32_t* __restrict__ sfb, int rp) {
   pdl_wait();
   pdl_launch_next();
   const int r = blockIdx.x;
@@ -237,7 +238,7 @@ __global__ void __launch_bounds__(kE3Threads) k_rows_to_e2m1x4(const void* __res
       const Chunk cc = chunks[c];
       s_c[j] = c;
       s_jr[j] = p - cc.p0;
-      s_npad[j] = (cc.n + 15) & ~15;
+      s_npad[j] = (cc.n + rp - 1) & ~(rp - 1);
     }
   }
   __syncthreads();
@@ -331,7 +332,8 @@ __global__ void __launch_bounds__(kE3Threads) k_plan_rows_to_e2m1x4(
       const int cr = rank / nmax;
       s_c[tid] = cbase[e] + cr;
       s_jr[tid] = rank - cr * nmax;
-      s_npad[tid] = (min(nmax, cnt[e] - cr * nmax) + 15) & ~15;
+      const int rp = nmax < 16 ? 4 : 16;
+      s_npad[tid] = (min(nmax, cnt[e] - cr * nmax) + rp - 1) & ~(rp - 1);
       if (blockIdx.y == 0) {
         perm_token[p] = r;
         perm_slot[p] = tid;
@@ -397,7 +399,7 @@ int launch_rows_to_e2m1x4(const void* src, int src_dtype, int src_rows, const in
 #define LL_E2(SRC, TOKV)                                                                                      \
   LL_TRY(launch_pdl("k_rows_to_e2m1x4", k_rows_to_e2m1x4<SRC, TOKV>,                                        \
                     dim3(src_rows, (K / 8 + kE3Threads - 1) / kE3Threads), dim3(kE3Threads), 0, s, src, src_rows, \
-                    tok_pos, k, n_valid, K, P, dst, chunks, chunk_of, sw))
+                    tok_pos, k, n_valid, K, P, dst, chunks, chunk_of, sw, nmax < 16 ? 4 : 16))
   if (tok) {
     if (src_dtype == 0) LL_E2(0, true); else if (src_dtype == 1) LL_E2(1, true); else LL_E2(2, true);
   } else {

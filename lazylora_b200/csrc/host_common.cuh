@@ -196,15 +196,15 @@ inline int make_e4m3x3_maps(CUtensorMap* maps, int n, const uint8_t* base, int64
   return LL_OK;
 }
 
-// Packed E2M1 activation terms [4][rows][K/2] bytes (BS_FP4): a box is [4 terms][16 c rows][64
-// bytes = 128 K], 64-byte swizzle.
-inline int make_e2m1x4_maps(CUtensorMap* maps, int n, const uint8_t* base, int64_t rows, int K) {
+// Packed E2M1 activation terms [4][rows][K/2] bytes (BS_FP4): a box is [4 terms][rp c rows][64
+// bytes = 128 K] (rp = 16, or 4 for four-row tiles), 64-byte swizzle.
+inline int make_e2m1x4_maps(CUtensorMap* maps, int n, const uint8_t* base, int64_t rows, int K, int rp = 16) {
   constexpr int NT = BsTerms<BS_FP4>::value;
-  if (K % 128 || n < 1 || n > 4) return LL_ERR_ARG;
+  if (K % 128 || n < 1 || n > 4 || (rp != 4 && rp != 16)) return LL_ERR_ARG;
   const uint64_t dims[3] = {(uint64_t)K / 2, (uint64_t)rows, (uint64_t)NT};
   const uint64_t strides[2] = {(uint64_t)K / 2, (uint64_t)rows * K / 2};
   for (int c = 1; c <= n; c++) {
-    const uint32_t box[3] = {64, (uint32_t)(16 * c), (uint32_t)NT};
+    const uint32_t box[3] = {64, (uint32_t)(rp * c), (uint32_t)NT};
     LL_TRY(make_map_nd(&maps[c - 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, base, 3, dims, strides, box,
                        CU_TENSOR_MAP_SWIZZLE_64B));
   }
@@ -224,7 +224,7 @@ int launch_bs_gemm(const CUtensorMap* a, const CUtensorMap* b, const BsArgs& arg
   using Cfg = BsCfg<NMAT, N_MAX, KIND>;
   BsTma<NMAT, N_MAX, KIND> tm;
   for (int i = 0; i < NMAT; i++) tm.a[i] = a[i];
-  for (int i = 0; i < N_MAX / 16; i++) tm.b[i] = b[i];
+  for (int i = 0; i < BsRows<N_MAX>::maps; i++) tm.b[i] = b[i];
   auto kern = grouped_mxfp4_bs_gemm<EPI, NMAT, N_MAX, KIND>;
   LL_TRY(set_smem_attr(reinterpret_cast<const void*>(kern), Cfg::SMEM));
   const DeviceInfo di = device_info();

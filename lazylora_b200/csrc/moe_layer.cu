@@ -464,6 +464,8 @@ static int choose_nmax(const ll_moe_layer* L, int T, int k) {
     return (v == 16 || v == 32 || v == 64 || v == 128) ? v : 0;
   }();
   if (forced) return forced;
+  // a token takes an expert at most once: up to 4 tokens, no expert has more than 4 rows
+  if (T <= 4) return 4;
   return mean <= 10.0 ? 16 : mean <= 22.0 ? 32 : (mean <= 48.0 ? 64 : 128);
 }
 
@@ -614,6 +616,10 @@ static int bs_split_units(int which) {
   return std::min(u, kSplitUnits);
 }
 
+// The token-tile width of the fp16 dequant GEMMs: the layer's, at least 16 (four-row chunks run
+// in 16-row tiles there).
+static int dq_nmax(const LayerWs& W) { return W.nmax < 16 ? 16 : W.nmax; }
+
 // The block-scaled forward GEMM kind for a token-tile width: E2M1 activation terms up to 32
 // rows, E4M3 terms at 64 rows, none (fp16 dequant path) at 128.
 static int bs_kind(int nmax) { return nmax <= 32 ? BS_FP4 : nmax <= 64 ? BS_FP8 : -1; }
@@ -622,7 +628,9 @@ template <int EPI>
 static int bs_launch(int kind, int nmax, const CUtensorMap* a, const CUtensorMap* b, const BsArgs& args,
                      cudaStream_t s) {
   if (kind == BS_FP4)
-    return nmax == 16 ? launch_bs_gemm<EPI, 2, 16, BS_FP4>(a, b, args, s) : launch_bs_gemm<EPI, 2, 32, BS_FP4>(a, b, args, s);
+    return nmax == 4    ? launch_bs_gemm<EPI, 2, 4, BS_FP4>(a, b, args, s)
+           : nmax == 16 ? launch_bs_gemm<EPI, 2, 16, BS_FP4>(a, b, args, s)
+                        : launch_bs_gemm<EPI, 2, 32, BS_FP4>(a, b, args, s);
   return launch_bs_gemm<EPI, 2, 64, BS_FP8>(a, b, args, s);
 }
 
@@ -635,7 +643,7 @@ static int bs_operand(int kind, const LayerWs& W, const void* src, int src_dtype
   if (kind == BS_FP4) {
     LL_TRY(launch_rows_to_e2m1x4(src, src_dtype, src_rows, tok_pos, k, n_valid, K, P, q, W.chunks, W.chunk_of,
                                  W.nmax, sfb, s));
-    LL_TRY(make_e2m1x4_maps(maps, W.nmax / 16, q, P, K));
+    LL_TRY(make_e2m1x4_maps(maps, W.nmax < 16 ? 1 : W.nmax / 16, q, P, K, W.nmax < 16 ? 4 : 16));
     a.sfb = sfb;
   } else {
     LL_TRY(launch_rows_to_e4m3x3(src, src_dtype, src_rows, tok_pos, k, n_valid, K, P, q, inv3, s));
@@ -872,7 +880,7 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
     }
     BsArgs a1{};
     if (fused_front) {
-      LL_TRY(make_e2m1x4_maps(b, W.nmax / 16, W.xq, P, d));
+      LL_TRY(make_e2m1x4_maps(b, W.nmax < 16 ? 1 : W.nmax / 16, W.xq, P, d, W.nmax < 16 ? 4 : 16));
       a1.sfb = W.xsfb;
     } else {
       LL_TRY(bs_operand(kind, W, x, x_dtype, T, W.tok_pos, k, nullptr, d, P, W.xq, W.xinv3, W.xsfb, b, a1, s));
@@ -904,7 +912,7 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
     CUtensorMap pk[2], sc[2], act[8];
     LL_TRY(make_rowscale_maps(&pk[0], &sc[0], L->w1p, L->w1s, (int64_t)E * f, d, L->s13_stride));
     LL_TRY(make_rowscale_maps(&pk[1], &sc[1], L->w3p, L->w3s, (int64_t)E * f, d, L->s13_stride));
-    LL_TRY(make_act_maps(act, W.nmax / 16, W.xh, P, d));
+    LL_TRY(make_act_maps(act, dq_nmax(W) / 16, W.xh, P, d));
     GemmArgs a{};
     a.chunks = W.chunks;
     a.n_chunks = W.n_chunks;
@@ -924,7 +932,7 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
     a.epi.U = W.U;
     a.epi.H = W.H;
     LL_CUDA(cudaStreamWaitEvent(s, ss->join, 0));
-    LL_TRY((gemm_nmax<EPI_F1, 2, 1, false>(W.nmax, pk, sc, act, a, s)));
+    LL_TRY((gemm_nmax<EPI_F1, 2, 1, false>(dq_nmax(W), pk, sc, act, a, s)));
   }
   const int* n_valid = W.offsets + E;
   // z = h . A_d^T per pair (h as the fp16 rows the down GEMM reads); with few tokens on the side
@@ -975,7 +983,7 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
     LL_TRY(make_rowscale_maps(&pk[0], &sc[0], L->w2p, L->w2s, (int64_t)E * d, f, L->s2_stride, 256));
     pk[1] = pk[0];
     sc[1] = sc[0];
-    LL_TRY(make_act_maps(act, W.nmax / 16, W.H, P, f));
+    LL_TRY(make_act_maps(act, dq_nmax(W) / 16, W.H, P, f));
     GemmArgs a{};
     a.chunks = W.chunks;
     a.n_chunks = W.n_chunks;
@@ -990,7 +998,7 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
     a.epi.P = P;
     a.epi.M = d;
     a.epi.Y = W.Y;
-    LL_TRY((gemm_nmax<EPI_F2, 2, 1, false>(W.nmax, pk, sc, act, a, s)));
+    LL_TRY((gemm_nmax<EPI_F2, 2, 1, false>(dq_nmax(W), pk, sc, act, a, s)));
   }
   if (z_side) LL_CUDA(cudaStreamWaitEvent(s, ss->join, 0));
   if (norm_w) {
@@ -1049,7 +1057,7 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
                               pair ? 256 : 128));
     pk[1] = pk[0];
     sc[1] = sc[0];
-    LL_TRY(make_act_maps(act, W.nmax / 16, W.gh, P, d));
+    LL_TRY(make_act_maps(act, dq_nmax(W) / 16, W.gh, P, d));
     GemmArgs a{};
     a.chunks = W.chunks;
     a.n_chunks = W.n_chunks;
@@ -1074,9 +1082,9 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
     a.epi.gw_part = W.gw_part;
     if (!pair)
       LL_TRY((launch_gemm<EPI_B1, 1, 1, true, 128>(pk, sc, act, a, s)));
-    else if (W.nmax == 16)
+    else if (dq_nmax(W) == 16)
       LL_TRY((launch_gemm<EPI_B1, 2, 1, true, 16>(pk, sc, act, a, s)));
-    else if (W.nmax == 32)
+    else if (dq_nmax(W) == 32)
       LL_TRY((launch_gemm<EPI_B1, 2, 1, true, 32>(pk, sc, act, a, s)));
     else
       LL_TRY((launch_gemm<EPI_B1, 2, 1, true, 64>(pk, sc, act, a, s)));
@@ -1097,7 +1105,7 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
     CUtensorMap pk[2], sc[2], act[8];
     LL_TRY(make_colscale_maps(&pk[0], &sc[0], L->w1t, reinterpret_cast<const __half*>(L->s1t), (int64_t)E * d, f));
     LL_TRY(make_colscale_maps(&pk[1], &sc[1], L->w3t, reinterpret_cast<const __half*>(L->s3t), (int64_t)E * d, f));
-    LL_TRY(make_act_maps(act, W.nmax / 16, W.DGh, P, f, 2, (int64_t)(W.DUh - W.DGh)));
+    LL_TRY(make_act_maps(act, dq_nmax(W) / 16, W.DGh, P, f, 2, (int64_t)(W.DUh - W.DGh)));
     GemmArgs a{};
     a.chunks = W.chunks;
     a.n_chunks = W.n_chunks;
@@ -1112,7 +1120,7 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
     a.epi.P = P;
     a.epi.M = d;
     a.epi.Y = W.Y;
-    LL_TRY((gemm_nmax<EPI_B2, 2, 2, true>(W.nmax, pk, sc, act, a, s)));
+    LL_TRY((gemm_nmax<EPI_B2, 2, 2, true>(dq_nmax(W), pk, sc, act, a, s)));
   }
   if (!fused_rows) {
     LL_TRY(launch_pdl("k_token_sum", k_token_sum, dim3((f + 255) / 256, T), dim3(256), 0, s, W.tok_pos, W.DG, W.DU, T,

@@ -111,6 +111,26 @@ def test_edge_cases_vs_oracle():
         assert O.rel_l2(got[key].cpu(), want[key]) <= TOL, key
 
 
+@pytest.mark.parametrize("T", [1, 2, 3, 4, 5])
+def test_few_tokens_vs_oracle(T):
+    """Up to four tokens the forward GEMMs use four-row activation tiles (MMA N = 16) and the
+    backward's fp16 GEMMs 16-row tiles; five tokens are back on 16-row tiles. Forward and
+    backward against the oracle."""
+    from lazylora_b200.trainer.routed_experts import RoutedExpertsLayer
+    cfg = dataclasses.replace(CONFIGS["small"], T=T)
+    inp = make_layer(cfg)
+    layer = RoutedExpertsLayer.from_inputs(inp, cfg.scaling)
+    gen = torch.Generator().manual_seed(40 + T)
+    idx = torch.stack([torch.randperm(cfg.E, generator=gen)[:cfg.k] for _ in range(T)])
+    w = torch.softmax(torch.randn(T, cfg.k, generator=gen), -1)
+    x = inp["x"][:T]
+    g = inp["g"][:T]
+    want = _oracle(dict(inp, x=x), idx, w, g.float(), cfg.scaling)
+    got = _run(layer, x.cuda(), idx.cuda(), w.cuda(), g.cuda())
+    for key in KEYS:
+        assert O.rel_l2(got[key].cpu(), want[key]) <= TOL, (T, key)
+
+
 def test_expert_over_tile_width():
     """An expert with more rows than N_MAX (128) is split into chunks; results unchanged."""
     from lazylora_b200.trainer.routed_experts import RoutedExpertsLayer
