@@ -18,7 +18,7 @@
 // mbarrier). Accumulators double-buffered (2 x BN columns), so a tile's epilogue overlaps the
 // next tile's main loop. Tiles are ordered M-fastest, so the CTAs working at the same time share
 // B tiles (the weight slices) through L2; A (the activations) stays in L2. Every wait is
-// bounded (common.cuh). No cluster, no multicast.
+// bounded (common.cuh). No cluster; every TMA load fills only the issuing CTA's shared memory.
 #include <algorithm>
 #include <cmath>
 
@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(kDnThreads, 1) k_dense_gemm(const __grid_const
 // The same GEMM with tiles of 256 rows on a CTA pair (a cluster of 2): tcgen05.mma.cta_group::2
 // with M = 256 reads A's rows from both CTAs' shared memory (rows 0..127 from CTA 0, 128..255
 // from CTA 1, at the same offset) and B's N/2-row halves likewise, and writes each CTA's 128
-// accumulator rows to its own tensor memory. Each CTA loads only its own halves (no multicast):
+// accumulator rows to its own tensor memory. Each CTA loads only its own halves (one destination):
 // per CTA a stage is A 16 KB + B BN/2 x 128 B, so a ring of 6 stages fits and each byte brought
 // from L2 feeds twice the MMA work of the single-CTA kernel. CTA 0 issues the MMAs; its stage
 // barrier expects both CTAs' bytes (CTA 1's TMA completes on CTA 0's barrier), and each commit
