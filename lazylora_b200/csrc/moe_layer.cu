@@ -32,6 +32,9 @@ constexpr int kTokBlock = 64;   // tokens per block in the counting sort
 // The block-scaled GEMMs' balanced split: for up to kSplitUnits units (8 per CTA at 148 SMs),
 // with partial slots for up to kSplitCtas CTAs.
 constexpr int kSplitUnits = 1280, kSplitCtas = 160;
+// Above this many tokens the LoRA projections x . [A_g; A_u]^T and g . B_d run on the tensor
+// cores (project_tc) when x / g are bf16; below, on CUDA cores (skinny).
+constexpr int kProjTcMin = 128;
 
 // ----------------------------------------------------------------- counting sort
 __global__ void k_count(const int64_t* __restrict__ idx, int T, int k, int E, int* __restrict__ cnt) {
@@ -446,6 +449,9 @@ struct LayerWs {
   float* split_part;
   int* split_cnt;
   int split_units;
+  // the tensor-core LoRA projections x . [A_g; A_u]^T and g . B_d (more than 128 tokens)
+  void* proj_ws;
+  size_t proj_bytes;
 };
 
 // Token rows per chunk (the MMA N): the smallest tile that holds most experts' rows in one
@@ -532,6 +538,10 @@ static size_t layer_layout(void* base, const ll_moe_layer* L, int T, int k, Laye
     const int64_t rows = P > T ? P : T;
     w.skpart_floats = (size_t)4 * 160 * 8192 + (size_t)(rows + 256) * (2 * r + 32);
     w.skpart = c.take<float>(w.skpart_floats);
+  }
+  if (T > kProjTcMin) {
+    w.proj_bytes = project_tc_bytes(T, d, 2 * r);
+    w.proj_ws = c.take<uint8_t>(w.proj_bytes);
   }
   if (T <= kTokBlock && nmax <= 64) {   // the one-block plan clears the counters
     w.split_units = kSplitUnits;
@@ -833,11 +843,15 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
   // the operand conversion, joined before F1.
   SideStream* ss = nullptr;
   LL_TRY(side_stream(&ss));
+  if (nblk > 1) LL_TRY(reset_status(W.st, s));   // before the fork: the side branch may report to it
   LL_CUDA(cudaEventRecord(ss->fork, s));
   LL_CUDA(cudaStreamWaitEvent(ss->s, ss->fork, 0));
   g_launch_stream = ss->s;
-  LL_TRY(skinny(x, x_dtype, true, T, d, L->A_g, L->A_u, r, 2 * r, 1.f, W.xa_g, W.xa_u, W.skpart, W.skpart_floats,
-                ss->s));
+  if (W.proj_ws && x_dtype == 1)
+    LL_TRY(project_tc(x, T, d, L->A_g, L->A_u, false, r, W.xa_g, W.xa_u, W.proj_ws, W.proj_bytes, W.st, ss->s));
+  else
+    LL_TRY(skinny(x, x_dtype, true, T, d, L->A_g, L->A_u, r, 2 * r, 1.f, W.xa_g, W.xa_u, W.skpart, W.skpart_floats,
+                  ss->s));
   LL_TRY(expand(false, nullptr, nullptr, k, T, f, r, L->lora_scaling, W.xa_g, L->B_g, W.xa_u, L->B_u, W.dlt_g, ss->s,
                 W.dlt_u));
   LL_CUDA(cudaEventRecord(ss->join, ss->s));
@@ -859,7 +873,6 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
                       k, E, W.nmax, W.offsets, W.chunks, W.n_chunks, W.perm_token, W.perm_slot, W.pair_pos, W.tw,
                       W.tok_pos, W.chunk_of, W.st, W.split_cnt, W.split_cnt ? 2 * 4 * W.split_units : 0));
   } else {
-    LL_TRY(reset_status(W.st, s));
     LL_CUDA(cudaMemsetAsync(W.perm_token, 0xFF, sizeof(int) * P, s));
     LL_TRY(launch_pdl("k_count", k_count, dim3(nblk), dim3(256), E * sizeof(int), s, idx, T, k, E, W.cnt));
     LL_TRY(launch_pdl("k_scan", k_scan, dim3(1), dim3(1024), 0, s, W.cnt, nblk, E, W.nmax, W.offsets, W.chunks,
@@ -1044,7 +1057,10 @@ int ll_moe_backward(const ll_moe_layer* L, int T, int k, const void* x, int x_dt
   g_launch_count = 0;
 
   LL_TRY(launch_token_rows_to_half(g, g_dtype, W.perm_token, W.tok_pos, T, k, d, W.gh, W.ginv, s));
-  LL_TRY(skinny(g, g_dtype, false, T, d, L->B_d, nullptr, r, r, 1.f, W.gB, nullptr, W.skpart, W.skpart_floats, s));
+  if (W.proj_ws && g_dtype == 1)
+    LL_TRY(project_tc(g, T, d, L->B_d, nullptr, true, r, W.gB, nullptr, W.proj_ws, W.proj_bytes, W.st, s));
+  else
+    LL_TRY(skinny(g, g_dtype, false, T, d, L->B_d, nullptr, r, r, 1.f, W.gB, nullptr, W.skpart, W.skpart_floats, s));
   // the down adapter's term of dL/dh, once per token: (g B_d) A_d [T][f]
   LL_TRY(expand(true, nullptr, nullptr, k, T, f, r, 1.f, W.gB, L->A_d, nullptr, nullptr, W.lora_d, s));
   // B1: v = g . W2 (+ LoRA down), SiTU-GLU backward

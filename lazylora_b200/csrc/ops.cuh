@@ -60,4 +60,13 @@ int launch_plan_rows_to_e2m1x4(const int64_t* idx, const float* w, int T, int k,
                                int* tok_pos, int* chunk_of, DevStatus* st, int* zero, int n_zero, const void* src,
                                int src_dtype, int K, int64_t P, uint8_t* dst, uint8_t* sfb, cudaStream_t s);
 
+// C0 [T][r] (and C1) = x [T][d] (bf16) . W0^T (W1^T) for LoRA projection matrices W [r][d], or
+// x . W for W [d][r] when `transposed`, on the tensor cores: W split into three bf16 planes
+// (exact), the router's tcgen05 logits kernel split over K to fill the SMs, the splits' fp32
+// partials added in order. Workspace project_tc_bytes(T, d, rows = r or 2r); bounded waits
+// report to st.
+size_t project_tc_bytes(int T, int d, int E);
+int project_tc(const void* x, int T, int d, const float* W0, const float* W1, bool transposed, int r, float* out0,
+               float* out1, void* ws, size_t ws_bytes, DevStatus* st, cudaStream_t s);
+
 }  // namespace ll

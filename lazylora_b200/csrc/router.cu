@@ -2,6 +2,8 @@
 //   logits = x . Wr^T (fp32), scores = sigmoid(logits), choice = scores + bias,
 //   top-k of choice (descending; ties: lower expert id), weights = scores at those ids,
 //   renormalised by (sum + 1e-20) when asked and k > 1, times the routed scaling factor.
+#include <algorithm>
+
 #include "host_common.cuh"
 #include "ops.cuh"
 #include "router_tc.cuh"
@@ -463,7 +465,7 @@ static int launch_router_mma(const RouterMaps& maps, float* part, int T, int E, 
 // planes: the router weight split into its three bf16 planes (hi, lo, lo2; [3][E][d]), or null
 // to split W into the workspace on this call.
 static int router_logits_tc(const void* x, int x_dtype, const float* W, const __nv_bfloat16* planes, int T, int d,
-                            int E, void* ws, const RouterPlan& p, cudaStream_t s) {
+                            int E, void* ws, const RouterPlan& p, cudaStream_t s, DevStatus* status = nullptr) {
   uint8_t* base = static_cast<uint8_t*>(ws);
   const int64_t nw = (int64_t)E * d;
   const __nv_bfloat16* wp = planes;
@@ -489,8 +491,11 @@ static int router_logits_tc(const void* x, int x_dtype, const float* W, const __
     LL_TRY(make_map_2d(&maps.b[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xp[i], (uint64_t)d, (uint64_t)T,
                        (uint64_t)d * 2, 64, p.BN, CU_TENSOR_MAP_SWIZZLE_128B));
   if (p.NP == 1) maps.b[1] = maps.b[2] = maps.b[0];
-  DevStatus* st = reinterpret_cast<DevStatus*>(base + p.off_st);
-  LL_TRY(reset_status(st, s));
+  DevStatus* st = status;
+  if (!st) {   // its own status word (the caller's, when given, is reset by the caller)
+    st = reinterpret_cast<DevStatus*>(base + p.off_st);
+    LL_TRY(reset_status(st, s));
+  }
   float* part = reinterpret_cast<float*>(base + p.off_part);
 #define LL_RT(NPv, BNv) \
   if (p.NP == NPv && p.BN == BNv) return launch_router_mma<NPv, BNv>(maps, part, T, E, p, st, s);
@@ -498,6 +503,44 @@ static int router_logits_tc(const void* x, int x_dtype, const float* W, const __
   LL_RT(3, 16) LL_RT(3, 32) LL_RT(3, 64) LL_RT(3, 128)
 #undef LL_RT
   return LL_ERR_ARG;
+}
+
+// out0 [T][r] (and out1 [T][r]) = the columns 0..r-1 (r..2r-1) of the sum of the nsplit
+// partials [nsplit][T][E], added in split order.
+__global__ void k_sum_split_cols(const float* __restrict__ part, int nsplit, int T, int E, int r,
+                                 float* __restrict__ out0, float* __restrict__ out1) {
+  pdl_wait();
+  pdl_launch_next();
+  const int64_t n = (int64_t)T * E;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float acc = part[i];
+#pragma unroll 8
+  for (int sp = 1; sp < nsplit; sp++) acc += part[(int64_t)sp * n + i];
+  const int t = (int)(i / E), e = (int)(i % E);
+  if (e < r) out0[(int64_t)t * r + e] = acc;
+  else out1[(int64_t)t * r + (e - r)] = acc;
+}
+
+size_t project_tc_bytes(int T, int d, int E) { return router_plan(T, d, E, 1).bytes; }
+
+int project_tc(const void* x, int T, int d, const float* W0, const float* W1, bool transposed, int r, float* out0,
+               float* out1, void* ws, size_t ws_bytes, DevStatus* st, cudaStream_t s) {
+  const int E = W1 ? 2 * r : r;
+  if (T <= 0 || d <= 0 || r <= 0 || d % 64 || !x || !W0 || !out0 || (W1 && !out1) || !ws) return LL_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(ws) % 256) return LL_ERR_ARG;
+  const RouterPlan p = router_plan(T, d, E, 1);
+  if (ws_bytes < p.bytes) return LL_ERR_WORKSPACE;
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  __nv_bfloat16* planes = reinterpret_cast<__nv_bfloat16*>(base + p.off_w);
+  k_split_lora_planes<<<(unsigned)std::min<int64_t>(((int64_t)E * d + 255) / 256, 148 * 4), 256, 0, s>>>(
+      W0, W1, transposed, r, d, planes);
+  LL_TRY(check_launch("k_split_lora_planes"));
+  LL_TRY(router_logits_tc(x, 1, nullptr, planes, T, d, E, ws, p, s, st));
+  const float* part = reinterpret_cast<const float*>(base + p.off_part);
+  const int64_t n = (int64_t)T * E;
+  return launch_pdl("k_sum_split_cols", k_sum_split_cols, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, part,
+                    p.nsplit, T, E, r, out0, out1);
 }
 
 }  // namespace ll

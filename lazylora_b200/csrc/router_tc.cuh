@@ -162,18 +162,34 @@ k_router_mma(const __grid_constant__ RouterMaps maps, float* __restrict__ part, 
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
-// W fp32 -> three bf16 planes whose sum is W exactly (round-to-nearest at each step).
+// An fp32 value as three bf16 planes whose sum is the value exactly (round-to-nearest at each step).
+LL_DEV void split_bf16x3(float v, __nv_bfloat16& h, __nv_bfloat16& l, __nv_bfloat16& l2) {
+  h = __float2bfloat16_rn(v);
+  const float r1 = v - __bfloat162float(h);
+  l = __float2bfloat16_rn(r1);
+  l2 = __float2bfloat16_rn(r1 - __bfloat162float(l));
+}
+
+// W fp32 -> three bf16 planes whose sum is W exactly.
 __global__ void k_split_bf16x3(const float* __restrict__ w, __nv_bfloat16* __restrict__ hi,
                                __nv_bfloat16* __restrict__ lo, __nv_bfloat16* __restrict__ lo2, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    split_bf16x3(w[i], hi[i], lo[i], lo2[i]);
+}
+
+// The planes [3][E][d] of a LoRA projection matrix for the logits kernel: rows 0..r-1 from W0,
+// rows r..2r-1 from W1 (when given); W0 / W1 stored [r][d], or [d][r] when `transposed` (the
+// matrix read as its transpose).
+__global__ void k_split_lora_planes(const float* __restrict__ W0, const float* __restrict__ W1, bool transposed,
+                                    int r, int d, __nv_bfloat16* __restrict__ planes) {
+  const int E = W1 ? 2 * r : r;
+  const int64_t n = (int64_t)E * d;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const float v = w[i];
-    const __nv_bfloat16 h = __float2bfloat16_rn(v);
-    const float r1 = v - __bfloat162float(h);
-    const __nv_bfloat16 l = __float2bfloat16_rn(r1);
-    const float r2 = r1 - __bfloat162float(l);
-    hi[i] = h;
-    lo[i] = l;
-    lo2[i] = __float2bfloat16_rn(r2);
+    const int e = (int)(i / d), c = (int)(i % d);
+    const float* W = e < r ? W0 : W1;
+    const int j = e < r ? e : e - r;
+    split_bf16x3(transposed ? W[(int64_t)c * r + j] : W[(int64_t)j * d + c], planes[i], planes[n + i],
+                 planes[2 * n + i]);
   }
 }
 
