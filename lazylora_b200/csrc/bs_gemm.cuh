@@ -416,7 +416,8 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
     float* __restrict__ Uo = ep.U;
     __half* __restrict__ Ho = ep.H;
     float* __restrict__ Yo = ep.Y;
-    // the per-row output of a finished (token row p, output row m) from its accumulator sums
+    // the per-row output of a finished (token row p, output row m) from its accumulator sums, for
+    // the units finished from split partials (the whole-unit path below has the same lines inline)
     auto finish = [&](int p, int m, float v, float up) {
       const size_t o = (size_t)p * ep.M + m;
       if (EPI == EPI_F1) {
@@ -505,8 +506,21 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
 #pragma unroll
               for (int t = NT - 2; t >= 0; t--) up = fmaf(__uint_as_float(e[t][jj]), sc[t], up);
             }
-            if (whole) {
-              finish(p, m, v, up);
+            if (whole) {                         // (inline: the pointers keep their __restrict__)
+              const size_t o = (size_t)p * ep.M + m;
+              if (EPI == EPI_F1) {
+                const int tk = perm ? perm[p] : p;
+                const size_t tmo = (size_t)tk * ep.M + m;
+                const float gate = v + dlt_g[tmo];
+                up += dlt_u[tmo];
+                Go[o] = gate;
+                Uo[o] = up;
+                Ho[o] = __float2half_rn(situ_glu_fwd(gate, up));
+              } else if (EPI == EPI_F2) {
+                Yo[o] = v * tw[p];
+              } else {
+                Yo[o] = v;
+              }
             } else if (EPI == EPI_F1) {
               __stcg(part + (size_t)j * 128 + row, v);
               __stcg(part + (size_t)(N_MAX + j) * 128 + row, up);
