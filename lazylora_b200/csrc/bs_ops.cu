@@ -346,20 +346,23 @@ __global__ void __launch_bounds__(kE3Threads) k_plan_rows_to_e2m1x4(
     if (blockIdx.y == 0) pair_pos[i] = p;
   }
   __syncthreads();
-  if (blockIdx.y == 0 && tid == 0) {   // the token's pair positions by ascending expert id
-    int ee[32], pp[32];
-    int n = 0;
-    for (int sl = 0; sl < k; sl++) {
-      const int e = s_e[sl];
-      if (e < 0) continue;
-      int j = n++;
-      while (j > 0 && ee[j - 1] > e) { ee[j] = ee[j - 1]; pp[j] = pp[j - 1]; j--; }
-      ee[j] = e;
-      pp[j] = s_p[sl];
-    }
-    for (int sl = 0; sl < k; sl++) tok_pos[(int64_t)r * k + sl] = sl < n ? pp[sl] : -1;
-  }
   e2m1x4_store(v, ch, nch, K, P, k, s_p, s_c, s_jr, s_npad, dst, sfb);
+  if (blockIdx.y == 0 && tid < 32) {
+    // the token's pair positions by ascending expert id (equal ids in slot order), then -1 for
+    // the slots routed elsewhere: lane l's place is the number of valid slots ahead of it
+    const int lane = tid;
+    const int el = lane < k ? s_e[lane] : -1;
+    const int n = __popc(__ballot_sync(0xffffffffu, el >= 0));
+    int rank = 0;
+    for (int i = 0; i < k; i++) {
+      const int ei = __shfl_sync(0xffffffffu, el, i);
+      rank += ei >= 0 && (ei < el || (ei == el && i < lane));
+    }
+    if (lane < k) {
+      if (el >= 0) tok_pos[(int64_t)r * k + rank] = s_p[lane];
+      if (lane >= n) tok_pos[(int64_t)r * k + lane] = -1;
+    }
+  }
 }
 
 int launch_plan_rows_to_e2m1x4(const int64_t* idx, const float* w, int T, int k, int E, int nmax, int* offsets,

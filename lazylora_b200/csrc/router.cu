@@ -223,11 +223,19 @@ __global__ void __launch_bounds__(kSelWarps * 32) k_route_select_block(
     int renorm, float rsf, int64_t* __restrict__ idx, float* __restrict__ w, float* __restrict__ scores_out,
     int nsplit) {
   static_assert(PL == 4, "four experts a thread");
+  const int wp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // the bias was written before the router's first kernel, which had passed its own wait before
+  // this launch could start: its loads go before the wait and overlap it
+  float bv[PL];
+#pragma unroll
+  for (int i = 0; i < PL; i++) {
+    const int e = 256 * i + 32 * wp + lane;
+    bv[i] = (MODE == 0 && bias && e < E) ? bias[e] : 0.f;
+  }
   pdl_wait();
   pdl_launch_next();
   const int t = blockIdx.x;
   if (t >= T) return;
-  const int wp = threadIdx.x / 32, lane = threadIdx.x % 32;
   __shared__ SelShared sh;
   float sc[PL], ch[PL];
 #pragma unroll
@@ -273,7 +281,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) k_route_select_block(
     if (MODE == 0) {
       const float sg = 1.0f / (1.0f + expf(-l));
       sc[i] = sg;
-      ch[i] = bias ? sg + bias[e] : sg;
+      ch[i] = bias ? sg + bv[i] : sg;
       if (scores_out) scores_out[(int64_t)t * E + e] = sg;
     } else {
       sc[i] = a[(int64_t)t * E + e];
