@@ -348,8 +348,6 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
                                                    const float* __restrict__ R1, float* __restrict__ out,
                                                    float* __restrict__ out1, const float* __restrict__ qtw,
                                                    const float* __restrict__ qz, float* __restrict__ q_out) {
-  pdl_wait();
-  pdl_launch_next();
   // gridDim.z == 2 (one product, TWO false): blocks z = 1 compute out1 = alpha L1 R1 instead
   if (!TWO && blockIdx.z == 1) {
     L0 = L1;
@@ -362,6 +360,12 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
   const int c0 = blockIdx.x * kExCols, t0 = blockIdx.y * kExTok;
   const int nc = min(kExCols, C - c0);
   const int c = 2 * threadIdx.x;
+  // The first R is a LoRA weight (every caller passes the layer's adapters), written before the
+  // kernels this launch follows had passed their own waits: its slice is staged before the wait,
+  // overlapping the predecessor.
+  ex_stage_r<RROWS>(Rs, R0, r, C, c0, nc);
+  pdl_wait();
+  pdl_launch_next();
   if (HASY)
     for (int i = threadIdx.x; i < kExTok * k; i += kExThreads) {
       const int tt = i / k, j = i % k;
@@ -371,10 +375,11 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
 #pragma unroll
   for (int tt = 0; tt < kExTok; tt++) lo[tt] = make_float2(0.f, 0.f);
   for (int w = 0; w < (TWO ? 2 : 1); w++) {
-    const float* R = w == 0 ? R0 : R1;
     const float* Lm = w == 0 ? L0 : L1;
-    __syncthreads();                                     // the previous R is no longer read
-    ex_stage_r<RROWS>(Rs, R, r, C, c0, nc);
+    if (w > 0) {
+      __syncthreads();                                   // the previous R is no longer read
+      ex_stage_r<RROWS>(Rs, R1, r, C, c0, nc);
+    }
     for (int i = threadIdx.x; i < kExTok * r; i += kExThreads) {
       const int tt = i / r, rr = i % r;
       float l = 0.f;
