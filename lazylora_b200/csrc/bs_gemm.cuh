@@ -69,6 +69,7 @@ struct BsArgs {
   int* split_cnt;
   int split_units;            // units the counters cover: the split runs only for n_units <= this
   int split_ctas;             // CTAs split_part has slots for
+  int chunks_cap;             // entries the chunk list has room for (0: unknown)
 };
 
 // The (unit, K-stage range) pieces a CTA runs. Without the split, CTA b takes whole units b,
@@ -233,6 +234,11 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
   pdl_launch_next();                        // (after the allocation: see pdl_launch_next)
   pdl_wait();
   const int n_units = (*args.n_chunks) * args.mtiles;
+  // the chunk of this CTA's first unit without the split (unit blockIdx.x), loaded beside the
+  // count instead of after it (inside the chunk list's capacity; used only if that unit exists)
+  const int c_first_i = (int)blockIdx.x / args.mtiles;
+  Chunk c_first{};
+  if (warp == 0 && lane == 0 && c_first_i < args.chunks_cap) c_first = args.chunks[c_first_i];
   // the balanced split for a few waves of units (at least one unit a CTA: with fewer it measured
   // slower, the partial sums' round trip costing more than the bytes it evens out)
   const bool split = args.split_part != nullptr && n_units >= (int)gridDim.x && n_units <= args.split_units &&
@@ -274,7 +280,7 @@ grouped_mxfp4_bs_gemm(const __grid_constant__ BsTma<NMAT, N_MAX, KIND> tm, const
       while (ok && segs.next(sg)) {
         const int u = sg.u;
         const int ci = u / args.mtiles;
-        const Chunk ch = args.chunks[ci];
+        const Chunk ch = (!split && u == (int)blockIdx.x && ci < args.chunks_cap) ? c_first : args.chunks[ci];
         const int mt = u % args.mtiles;
         const int row = ch.e * args.e_rows + mt * TILE_ROWS;
         const int tile0 = ch.e * tiles128 + mt * (TILE_ROWS / 128);

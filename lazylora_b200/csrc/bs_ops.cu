@@ -140,17 +140,12 @@ __global__ void __launch_bounds__(kE3Threads) k_rows_to_e4m3x3(const void* __res
   }
 }
 
-// The four E2M1 term rounds of one thread's 8 source values (8-element chunk ch of the row),
-// each term's packed codes stored to the nd destination pair rows s_p[] (skipping -1) and the
-// stage's scale word to their chunks' B scale blocks (chunk s_c[], row s_jr[] of s_npad[] rows);
-// see k_rows_to_e2m1x4 for the formats.
-LL_DEV void e2m1x4_store(float (&v)[8], int ch, int nch, int K, int64_t P, int nd, const int* s_p, const int* s_c,
-                         const int* s_jr, const int* s_npad, uint8_t* __restrict__ dst, uint32_t* __restrict__ sfb) {
-  const int n_stage = K / 128;
-  const int ks = ch / 16;                        // stage of this thread's chunk
-  const bool lead = (ch & 15) == 0;              // writes the stage's scale word
-  constexpr int WPB = kBsSfBlock / 4;            // words per scale block
-#pragma unroll 1
+// The four E2M1 term rounds of one thread's 8 source values (8-element chunk ch of the row):
+// term t's packed codes word[t] and its stage's four scale bytes sw[t] (the blocks of this
+// thread and the threads + 4, 8, 12; meaningful in the stage's lead thread). Every lane of the
+// warp takes part (shuffles). See k_rows_to_e2m1x4 for the formats.
+LL_DEV void e2m1x4_terms(float (&v)[8], uint32_t (&word)[kBsTermsFp4], uint32_t (&sw)[kBsTermsFp4]) {
+#pragma unroll
   for (int t = 0; t < kBsTermsFp4; t++) {
     float mx = 0.f;
 #pragma unroll
@@ -167,11 +162,11 @@ LL_DEV void e2m1x4_store(float (&v)[8], int ch, int nch, int K, int64_t P, int n
     }
     const uint32_t sbyte = (uint32_t)(e + 127);
     const float inv = ldexpf(1.f, -e), scl = ldexpf(1.f, e);
-    uint32_t word = 0;
+    uint32_t wd = 0;
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       const uint32_t b = f32x2_to_e2m1x2(v[2 * j] * inv, v[2 * j + 1] * inv);
-      word |= b << (8 * j);
+      wd |= b << (8 * j);
       const uint32_t h = e2m1x2_to_half2(b);
       const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&h));
       v[2 * j] -= d.x * scl;                     // the residual the next term takes
@@ -181,17 +176,40 @@ LL_DEV void e2m1x4_store(float (&v)[8], int ch, int nch, int K, int64_t P, int n
     const uint32_t s1 = __shfl_down_sync(0xffffffffu, sbyte, 4);
     const uint32_t s2 = __shfl_down_sync(0xffffffffu, sbyte, 8);
     const uint32_t s3 = __shfl_down_sync(0xffffffffu, sbyte, 12);
-    const uint32_t sw = sbyte | (s1 << 8) | (s2 << 16) | (s3 << 24);
-    for (int j = 0; j < nd; j++) {
-      const int p = s_p[j];
-      if (p < 0) continue;
-      if (ch < nch) reinterpret_cast<uint32_t*>(dst + ((int64_t)t * P + p) * (K / 2))[ch] = word;
-      if (lead && ch < nch) {
+    word[t] = wd;
+    sw[t] = sbyte | (s1 << 8) | (s2 << 16) | (s3 << 24);
+  }
+}
+
+// The terms of e2m1x4_terms stored to the nd destination pair rows s_p[] (skipping -1), and the
+// stage's scale word to their chunks' B scale blocks (chunk s_c[], row s_jr[] of s_npad[] rows).
+LL_DEV void e2m1x4_put(const uint32_t (&word)[kBsTermsFp4], const uint32_t (&sw)[kBsTermsFp4], int ch, int nch,
+                       int K, int64_t P, int nd, const int* s_p, const int* s_c, const int* s_jr, const int* s_npad,
+                       uint8_t* __restrict__ dst, uint32_t* __restrict__ sfb) {
+  if (ch >= nch) return;
+  const int n_stage = K / 128;
+  const int ks = ch / 16;                        // stage of this thread's chunk
+  const bool lead = (ch & 15) == 0;              // writes the stage's scale word
+  constexpr int WPB = kBsSfBlock / 4;            // words per scale block
+  for (int j = 0; j < nd; j++) {
+    const int p = s_p[j];
+    if (p < 0) continue;
+#pragma unroll
+    for (int t = 0; t < kBsTermsFp4; t++) {
+      reinterpret_cast<uint32_t*>(dst + ((int64_t)t * P + p) * (K / 2))[ch] = word[t];
+      if (lead) {
         const int n = t * s_npad[j] + s_jr[j];
-        sfb[((int64_t)s_c[j] * n_stage + ks) * WPB + (n % 32) * 4 + (n % 128) / 32] = sw;
+        sfb[((int64_t)s_c[j] * n_stage + ks) * WPB + (n % 32) * 4 + (n % 128) / 32] = sw[t];
       }
     }
   }
+}
+
+LL_DEV void e2m1x4_store(float (&v)[8], int ch, int nch, int K, int64_t P, int nd, const int* s_p, const int* s_c,
+                         const int* s_jr, const int* s_npad, uint8_t* __restrict__ dst, uint32_t* __restrict__ sfb) {
+  uint32_t word[kBsTermsFp4], sw[kBsTermsFp4];
+  e2m1x4_terms(v, word, sw);
+  e2m1x4_put(word, sw, ch, nch, K, P, nd, s_p, s_c, s_jr, s_npad, dst, sfb);
 }
 
 // The BS_FP4 activation terms: per row, four rounds of (per 32-element block: max |r|, scale
@@ -290,6 +308,9 @@ __global__ void __launch_bounds__(kE3Threads) k_plan_rows_to_e2m1x4(
     es[i] = ok ? (int)e : -1;
     if (ok) atomicAdd(&cnt[e], 1);
   }
+  // x's terms (they depend on x alone), while the idx loads above are answered
+  uint32_t word[kBsTermsFp4], swd[kBsTermsFp4];
+  e2m1x4_terms(v, word, swd);
   __syncthreads();
   int c4[4], n4[4], ro[4], co[4], agg_rows, agg_ch;
 #pragma unroll
@@ -346,7 +367,7 @@ __global__ void __launch_bounds__(kE3Threads) k_plan_rows_to_e2m1x4(
     if (blockIdx.y == 0) pair_pos[i] = p;
   }
   __syncthreads();
-  e2m1x4_store(v, ch, nch, K, P, k, s_p, s_c, s_jr, s_npad, dst, sfb);
+  e2m1x4_put(word, swd, ch, nch, K, P, k, s_p, s_c, s_jr, s_npad, dst, sfb);
   if (blockIdx.y == 0 && tid < 32) {
     // the token's pair positions by ascending expert id (equal ids in slot order), then -1 for
     // the slots routed elsewhere: lane l's place is the number of valid slots ahead of it

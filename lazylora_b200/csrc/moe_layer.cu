@@ -900,6 +900,7 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
     }
     a1.chunks = W.chunks;
     a1.n_chunks = W.n_chunks;
+    a1.chunks_cap = W.max_chunks;
     a1.mtiles = f / 128;
     a1.K = d;
     a1.e_rows = f;
@@ -975,6 +976,7 @@ static int moe_forward(const ll_moe_layer* L, int T, int k, const void* x, int x
     LL_TRY(bs_operand(kind, W, W.H, 2, P, nullptr, 0, n_valid, f, P, W.hq, W.hinv3, W.hsfb, b, a2, s));
     a2.chunks = W.chunks;
     a2.n_chunks = W.n_chunks;
+    a2.chunks_cap = W.max_chunks;
     a2.mtiles = d / 256;
     a2.K = f;
     a2.e_rows = d;
