@@ -281,6 +281,31 @@ constexpr int kExMaxR = 64;
 
 // The block's R slice into shared memory ([r][kExPitch]; columns >= nc zero), in batches of 8
 // 16-byte loads a thread, so one batch's latency is paid once instead of once per element.
+// q = the sum over a token's pair positions tp[0..k) (ascending expert; the first -1 ends the
+// list) of tw[pos] * z[pos][rr], added in that order; eight positions' loads are issued together
+// (one chain of two load latencies per eight pairs instead of two per pair).
+LL_DEV float token_q(const int* __restrict__ tp, int k, const float* __restrict__ tw, const float* __restrict__ z,
+                     int r, int rr) {
+  float l = 0.f;
+  for (int j0 = 0; j0 < k; j0 += 8) {
+    int pos[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) pos[u] = j0 + u < k ? tp[j0 + u] : -1;
+    float a[8], b[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      a[u] = pos[u] >= 0 ? tw[pos[u]] : 0.f;
+      b[u] = pos[u] >= 0 ? z[(int64_t)pos[u] * r + rr] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      if (pos[u] < 0) return l;
+      l = fmaf(a[u], b[u], l);
+    }
+  }
+  return l;
+}
+
 template <bool RROWS>
 LL_DEV void ex_stage_r(float* Rs, const float* __restrict__ R, int r, int C, int c0, int nc) {
   const int tid = threadIdx.x;
@@ -386,11 +411,7 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
       if (t0 + tt < T) {
         if (qz) {
           // L0 = q: q[t][rr] = sum over the token's pairs (ascending expert) of tw * z, as k_q
-          for (int j = 0; j < k; j++) {
-            const int pos = tok_pos[(int64_t)(t0 + tt) * k + j];
-            if (pos < 0) break;
-            l = fmaf(qtw[pos], qz[(int64_t)pos * r + rr], l);
-          }
+          l = token_q(tok_pos + (int64_t)(t0 + tt) * k, k, qtw, qz, r, rr);
           if (q_out && blockIdx.x == 0) q_out[(int64_t)(t0 + tt) * r + rr] = l;
         } else {
           l = Lm[(int64_t)(t0 + tt) * r + rr];
@@ -469,11 +490,7 @@ __global__ void __launch_bounds__(kExThreads) k_expand_norm(const int* __restric
     const int tt = i / r, rr = i % r;
     float l = 0.f;
     if (t0 + tt < T) {
-      for (int j = 0; j < k; j++) {
-        const int pos = tok_pos[(int64_t)(t0 + tt) * k + j];
-        if (pos < 0) break;
-        l = fmaf(qtw[pos], qz[(int64_t)pos * r + rr], l);
-      }
+      l = token_q(tok_pos + (int64_t)(t0 + tt) * k, k, qtw, qz, r, rr);
       if (q_out) q_out[(int64_t)(t0 + tt) * r + rr] = l;
     }
     Ls[tt][rr] = l;
