@@ -410,7 +410,7 @@ __global__ void __launch_bounds__(kExThreads) k_expand(const int* __restrict__ t
       float l = 0.f;
       if (t0 + tt < T) {
         if (qz) {
-          // L0 = q: q[t][rr] = sum over the token's pairs (ascending expert) of tw * z, as k_q
+          // L0 = q: q[t][rr] = sum over the token's pairs (ascending expert) of tw * z
           l = token_q(tok_pos + (int64_t)(t0 + tt) * k, k, qtw, qz, r, rr);
           if (q_out && blockIdx.x == 0) q_out[(int64_t)(t0 + tt) * r + rr] = l;
         } else {
